@@ -1,0 +1,106 @@
+"""Model and pool configuration for the B200 decode backend.
+
+The field names follow the reference's ``ModelConfig``
+(engine/backend/kv_cache_pool.py:36-60) so that a ``b200`` backend can be
+constructed from the same manifest values.  Two groups are added that the
+reference keeps inside its TensorRT plan: the code-predictor architecture
+(scripts/export/utils.py:852-1042) and the paged-KV pool geometry, which has
+no counterpart in the slot-contiguous reference pool.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field, asdict
+
+
+@dataclass
+class TalkerConfig:
+    """Qwen3 talker (scripts/export/talker_unified_modules.py:231-320)."""
+
+    num_layers: int = 28
+    hidden_size: int = 2048
+    num_heads: int = 16
+    kv_heads: int = 8
+    head_dim: int = 128
+    intermediate_size: int = 6144
+    codec_vocab_size: int = 3072
+    rope_theta: float = 1.0e6
+    rms_eps: float = 1.0e-6
+    codec_eos_id: int = 2150
+    logits_topk: int = 50
+
+    @property
+    def q_size(self) -> int:
+        return self.num_heads * self.head_dim
+
+    @property
+    def kv_size(self) -> int:
+        return self.kv_heads * self.head_dim
+
+    @property
+    def kv_bytes_per_token(self) -> int:
+        """K+V bytes of one token over all layers, bf16."""
+        return self.num_layers * 2 * self.kv_heads * self.head_dim * 2
+
+
+@dataclass
+class CodePredictorConfig:
+    """15-stage residual codebook predictor (scripts/export/utils.py:852-1042)."""
+
+    num_layers: int = 5
+    hidden_size: int = 1024
+    num_heads: int = 16
+    kv_heads: int = 8
+    head_dim: int = 64
+    intermediate_size: int = 3072
+    vocab_size: int = 2048
+    num_stages: int = 15
+    talker_hidden_size: int = 2048
+    rope_theta: float = 1.0e6
+    rms_eps: float = 1.0e-6
+    logits_topk: int = 50
+
+    @property
+    def max_seq(self) -> int:
+        # positions 0..num_stages: [h_last, emb(tok0), emb_1(t1), ...]
+        return self.num_stages + 1
+
+
+@dataclass
+class PagedPoolConfig:
+    """Geometry of the paged talker KV pool (no counterpart in the reference)."""
+
+    block_size: int = 16
+    num_blocks: int = 8192
+    max_slots: int = 64
+    max_seq_len: int = 1024
+
+    @property
+    def max_blocks_per_seq(self) -> int:
+        return (self.max_seq_len + self.block_size - 1) // self.block_size
+
+
+@dataclass
+class EngineConfig:
+    talker: TalkerConfig = field(default_factory=TalkerConfig)
+    cp: CodePredictorConfig = field(default_factory=CodePredictorConfig)
+    pool: PagedPoolConfig = field(default_factory=PagedPoolConfig)
+
+    def to_dict(self) -> dict:
+        return asdict(self)
+
+
+def tiny_engine_config(num_layers: int = 2) -> EngineConfig:
+    """A small configuration with the talker's vocab and head layout intact.
+
+    Used by the CPU tests and the golden-vector fixtures: the vocab (3072,
+    suppress range [2048, 3072), EOS 2150) and the GQA ratio are kept because
+    the sampling head and the attention kernels depend on them.
+    """
+    return EngineConfig(
+        talker=TalkerConfig(num_layers=num_layers, hidden_size=256, num_heads=4, kv_heads=2,
+                            head_dim=64, intermediate_size=512),
+        cp=CodePredictorConfig(num_layers=2, hidden_size=128, num_heads=4, kv_heads=2, head_dim=32,
+                               intermediate_size=256, talker_hidden_size=256),
+        pool=PagedPoolConfig(block_size=16, num_blocks=64, max_slots=8, max_seq_len=256),
+    )

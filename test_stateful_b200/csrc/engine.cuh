@@ -1,0 +1,428 @@
+// The decode-step engine: the launch sequence of one TalkerUnifiedFusedONNX
+// forward (talker_unified_modules.py:357-401) over the paged pool, built once
+// (tensor maps, buffers, per-stage row tables) and replayed every step.
+//
+// Step for n_rows streams x n_new tokens (decode: n_new = 1):
+//   sched append (+ COW copies) -> 28 x [RMSNorm, QKV GEMM (+q/k norm, RoPE,
+//   KV store), paged attention, O GEMM (+residual), RMSNorm, gate/up GEMM
+//   (+SwiGLU), down GEMM (+residual)] -> final norm of the last token ->
+//   codec head -> sampling -> code predictor: stage 0 over [h_last, emb(tok0)]
+//   then 14 single-token stages with a per-step KV cache (one 16-token block
+//   per stream) -> codec embedding sum + text embedding -> next input.
+//
+// The code predictor keeps K/V across its 15 stages instead of recomputing the
+// whole sequence each stage as CodePredictorUnrolled does (utils.py:1003-1042);
+// attention is causal and positions restart at 0 every frame, so each
+// stage's last hidden state is the same function of the same inputs.
+#pragma once
+
+#include <vector>
+
+#include "attention.cuh"
+#include "common.cuh"
+#include "gemm_tc.cuh"
+#include "sampling.cuh"
+#include "sched.cuh"
+#include "small_ops.cuh"
+
+namespace qtts {
+
+struct LayerGemms {
+    GemmPlan qkv, o, gu, down;
+};
+
+struct DevBuf {
+    void* p = nullptr;
+    ~DevBuf() {
+        if (p) cudaFree(p);
+    }
+};
+
+}  // namespace qtts
+
+struct qtts_engine {
+    qtts_model_desc d;
+    int rmax;        // token rows per call (talker)
+    int bmax;        // streams per call
+    int qkv_rows, cp_qkv_rows;
+    int max_splits, cp_max_splits;
+    // talker activations
+    float* x = nullptr;              // [rmax][H] fp32 residual stream
+    __nv_bfloat16* xn = nullptr;     // [rmax][max(H, I)] GEMM input (normed x / SwiGLU act)
+    __nv_bfloat16* qbuf = nullptr;   // [rmax][Hq*D]
+    __nv_bfloat16* attn = nullptr;   // [rmax][Hq*D]
+    __nv_bfloat16* act = nullptr;    // [rmax][I]
+    __nv_bfloat16* hid = nullptr;    // [bmax][H] final-normed last token
+    float* ws_o = nullptr;
+    float* ws_ml = nullptr;
+    int32_t *mapping = nullptr, *row_ctx = nullptr, *row_pos = nullptr, *row_slot = nullptr;
+    int32_t *cow_src = nullptr, *cow_dst = nullptr;
+    // code predictor
+    __nv_bfloat16* cp_in = nullptr;  // [2*bmax][H]
+    float* cx = nullptr;             // [2*bmax][cpH]
+    __nv_bfloat16* cxn = nullptr;    // [2*bmax][max(cpH, cpI)]
+    __nv_bfloat16* cq = nullptr;
+    __nv_bfloat16* cattn = nullptr;
+    __nv_bfloat16* cact = nullptr;
+    __nv_bfloat16* chid = nullptr;   // [bmax][cpH]
+    float* clogits = nullptr;        // [bmax][cp_vocab]
+    __nv_bfloat16* cp_kv = nullptr;  // [bmax][cpL][2][cpHkv][16][cpD]
+    float* cws_o = nullptr;
+    float* cws_ml = nullptr;
+    int32_t* cp_meta = nullptr;      // per stage: mapping, pos, ctx, slot  [stages][4][2*bmax]
+    int32_t* cp_table = nullptr;     // identity block table [bmax]
+    std::vector<void*> allocs;
+    // plans (built for rmax / 2*bmax rows; M is set per call)
+    std::vector<qtts::LayerGemms> tg;
+    qtts::GemmPlan head;
+    std::vector<qtts::LayerGemms> cg;
+    qtts::GemmPlan cp_proj_pair, cp_proj_one;
+    std::vector<qtts::GemmPlan> cp_heads;
+};
+
+namespace qtts {
+
+template <class T>
+inline int dev_alloc(qtts_engine* e, T** p, size_t count) {
+    void* ptr = nullptr;
+    QTTS_CHECK_CUDA(cudaMalloc(&ptr, count * sizeof(T) + 256));
+    e->allocs.push_back(ptr);
+    *p = reinterpret_cast<T*>(ptr);
+    return QTTS_OK;
+}
+
+#define QTTS_TRY(x)               \
+    do {                          \
+        int _rc = (x);            \
+        if (_rc != QTTS_OK) return _rc; \
+    } while (0)
+
+inline const __nv_bfloat16* bf(const void* p, size_t off) { return reinterpret_cast<const __nv_bfloat16*>(p) + off; }
+
+inline int engine_build(qtts_engine* e) {
+    const qtts_model_desc& d = e->d;
+    const int H = d.hidden, D = d.head_dim, Hq = d.heads, Hkv = d.kv_heads, I = d.inter;
+    e->bmax = d.max_batch;
+    e->rmax = d.max_batch > d.max_prefill_rows ? d.max_batch : d.max_prefill_rows;
+    e->qkv_rows = (Hq + 2 * Hkv) * D;
+    const int max_ctx = d.pool.max_blocks_per_seq * d.pool.block_size;
+    e->max_splits = attn_max_splits(max_ctx);
+    const int rmax = e->rmax, bmax = e->bmax;
+    const int wide = H > I ? H : I;
+    QTTS_TRY(dev_alloc(e, &e->x, (size_t)rmax * H));
+    QTTS_TRY(dev_alloc(e, &e->xn, (size_t)rmax * wide));
+    QTTS_TRY(dev_alloc(e, &e->qbuf, (size_t)rmax * Hq * D));
+    QTTS_TRY(dev_alloc(e, &e->attn, (size_t)rmax * Hq * D));
+    QTTS_TRY(dev_alloc(e, &e->act, (size_t)rmax * I));
+    QTTS_TRY(dev_alloc(e, &e->hid, (size_t)bmax * H));
+    QTTS_TRY(dev_alloc(e, &e->ws_o, (size_t)rmax * Hq * e->max_splits * D));
+    QTTS_TRY(dev_alloc(e, &e->ws_ml, (size_t)rmax * Hq * e->max_splits * 2));
+    QTTS_TRY(dev_alloc(e, &e->mapping, (size_t)rmax));
+    QTTS_TRY(dev_alloc(e, &e->row_ctx, (size_t)rmax));
+    QTTS_TRY(dev_alloc(e, &e->row_pos, (size_t)rmax));
+    QTTS_TRY(dev_alloc(e, &e->row_slot, (size_t)rmax));
+    QTTS_TRY(dev_alloc(e, &e->cow_src, (size_t)rmax));
+    QTTS_TRY(dev_alloc(e, &e->cow_dst, (size_t)rmax));
+
+    // ---- talker GEMM plans
+    e->tg.resize(d.layers);
+    for (int l = 0; l < d.layers; ++l) {
+        LayerGemms& g = e->tg[l];
+        qtts_qkv_epilogue q = {};
+        q.num_heads = Hq;
+        q.kv_heads = Hkv;
+        q.head_dim = D;
+        q.q_norm_w = bf(d.w_q_norm, (size_t)l * D);
+        q.k_norm_w = bf(d.w_k_norm, (size_t)l * D);
+        q.rms_eps = d.rms_eps;
+        q.rope_cos = d.rope_cos;
+        q.rope_sin = d.rope_sin;
+        q.max_pos = d.max_pos;
+        q.row_pos = e->row_pos;
+        q.slot_mapping = e->mapping;
+        q.kv_pool = d.kv_pool;
+        q.layer = l;
+        q.num_layers = d.layers;
+        q.block_size = d.pool.block_size;
+        QTTS_TRY(gemm_plan(&g.qkv, e->xn, rmax, H, bf(d.w_qkv, (size_t)l * e->qkv_rows * H), e->qkv_rows,
+                           QTTS_EPI_QKV_ROPE, e->qbuf, nullptr, &q));
+        QTTS_TRY(gemm_plan(&g.o, e->attn, rmax, Hq * D, bf(d.w_o, (size_t)l * H * Hq * D), H, QTTS_EPI_RESIDUAL,
+                           e->x, nullptr, nullptr));
+        QTTS_TRY(gemm_plan(&g.gu, e->xn, rmax, H, bf(d.w_gate_up, (size_t)l * 2 * I * H), 2 * I, QTTS_EPI_SWIGLU,
+                           e->act, nullptr, nullptr));
+        QTTS_TRY(gemm_plan(&g.down, e->act, rmax, I, bf(d.w_down, (size_t)l * H * I), H, QTTS_EPI_RESIDUAL, e->x,
+                           nullptr, nullptr));
+    }
+    QTTS_TRY(dev_alloc(e, &e->cp_table, (size_t)bmax));
+    // ---- code predictor
+    const int cH = d.cp_hidden, cD = d.cp_head_dim, cHq = d.cp_heads, cHkv = d.cp_kv_heads, cI = d.cp_inter;
+    const int S = d.cp_stages;
+    e->cp_qkv_rows = (cHq + 2 * cHkv) * cD;
+    e->cp_max_splits = 1;
+    const int crows = 2 * bmax;
+    const int cwide = cH > cI ? cH : cI;
+    QTTS_TRY(dev_alloc(e, &e->cp_in, (size_t)crows * H));
+    QTTS_TRY(dev_alloc(e, &e->cx, (size_t)crows * cH));
+    QTTS_TRY(dev_alloc(e, &e->cxn, (size_t)crows * cwide));
+    QTTS_TRY(dev_alloc(e, &e->cq, (size_t)crows * cHq * cD));
+    QTTS_TRY(dev_alloc(e, &e->cattn, (size_t)crows * cHq * cD));
+    QTTS_TRY(dev_alloc(e, &e->cact, (size_t)crows * cI));
+    QTTS_TRY(dev_alloc(e, &e->chid, (size_t)bmax * cH));
+    QTTS_TRY(dev_alloc(e, &e->clogits, (size_t)bmax * d.cp_vocab));
+    QTTS_TRY(dev_alloc(e, &e->cp_kv, (size_t)bmax * d.cp_layers * 2 * cHkv * 16 * cD));
+    QTTS_TRY(dev_alloc(e, &e->cws_o, (size_t)crows * cHq * cD));
+    QTTS_TRY(dev_alloc(e, &e->cws_ml, (size_t)crows * cHq * 2));
+    QTTS_TRY(dev_alloc(e, &e->cp_meta, (size_t)S * 4 * crows));
+    // every stage's rows: stage 0 has rows 2b+p (p = 0: talker hidden, 1: emb(tok0)),
+    // stage s >= 1 has one row per stream at position s+1.
+    {
+        std::vector<int32_t> meta((size_t)S * 4 * crows, 0), table(bmax);
+        for (int b = 0; b < bmax; ++b) table[b] = b;
+        for (int s = 0; s < S; ++s) {
+            int32_t* m = meta.data() + (size_t)s * 4 * crows;
+            if (s == 0) {
+                for (int b = 0; b < bmax; ++b)
+                    for (int p = 0; p < 2; ++p) {
+                        const int r = 2 * b + p;
+                        m[r] = b * 16 + p;
+                        m[crows + r] = p;
+                        m[2 * crows + r] = p + 1;
+                        m[3 * crows + r] = b;
+                    }
+            } else {
+                for (int b = 0; b < bmax; ++b) {
+                    m[b] = b * 16 + s + 1;
+                    m[crows + b] = s + 1;
+                    m[2 * crows + b] = s + 2;
+                    m[3 * crows + b] = b;
+                }
+            }
+        }
+        QTTS_CHECK_CUDA(cudaMemcpy(e->cp_meta, meta.data(), meta.size() * 4, cudaMemcpyHostToDevice));
+        QTTS_CHECK_CUDA(cudaMemcpy(e->cp_table, table.data(), table.size() * 4, cudaMemcpyHostToDevice));
+    }
+    e->cg.resize(d.cp_layers);
+    for (int l = 0; l < d.cp_layers; ++l) {
+        LayerGemms& g = e->cg[l];
+        qtts_qkv_epilogue q = {};
+        q.num_heads = cHq;
+        q.kv_heads = cHkv;
+        q.head_dim = cD;
+        q.q_norm_w = bf(d.cp_w_q_norm, (size_t)l * cD);
+        q.k_norm_w = bf(d.cp_w_k_norm, (size_t)l * cD);
+        q.rms_eps = d.cp_rms_eps;
+        q.rope_cos = d.cp_rope_cos;
+        q.rope_sin = d.cp_rope_sin;
+        q.max_pos = S + 1;
+        q.row_pos = nullptr;       // set per stage
+        q.slot_mapping = nullptr;  // set per stage
+        q.kv_pool = e->cp_kv;
+        q.layer = l;
+        q.num_layers = d.cp_layers;
+        q.block_size = 16;
+        QTTS_TRY(gemm_plan(&g.qkv, e->cxn, crows, cH, bf(d.cp_w_qkv, (size_t)l * e->cp_qkv_rows * cH),
+                           e->cp_qkv_rows, QTTS_EPI_QKV_ROPE, e->cq, nullptr, &q, bmax));
+        QTTS_TRY(gemm_plan(&g.o, e->cattn, crows, cHq * cD, bf(d.cp_w_o, (size_t)l * cH * cHq * cD), cH,
+                           QTTS_EPI_RESIDUAL, e->cx, nullptr, nullptr, bmax));
+        QTTS_TRY(gemm_plan(&g.gu, e->cxn, crows, cH, bf(d.cp_w_gate_up, (size_t)l * 2 * cI * cH), 2 * cI,
+                           QTTS_EPI_SWIGLU, e->cact, nullptr, nullptr, bmax));
+        QTTS_TRY(gemm_plan(&g.down, e->cact, crows, cI, bf(d.cp_w_down, (size_t)l * cH * cI), cH, QTTS_EPI_RESIDUAL,
+                           e->cx, nullptr, nullptr, bmax));
+    }
+    QTTS_TRY(gemm_plan(&e->cp_proj_pair, e->cp_in, crows, H, d.cp_w_proj, cH, QTTS_EPI_F32, e->cx, d.cp_b_proj,
+                       nullptr, bmax));
+    e->cp_heads.resize(S);
+    for (int s = 0; s < S; ++s)
+        QTTS_TRY(gemm_plan(&e->cp_heads[s], e->chid, bmax, cH, bf(d.cp_w_lm_head, (size_t)s * d.cp_vocab * cH),
+                           d.cp_vocab, QTTS_EPI_F32, e->clogits, nullptr, nullptr));
+    QTTS_TRY(gemm_plan(&e->head, e->hid, bmax, H, d.w_codec_head, d.vocab, QTTS_EPI_F32, nullptr, nullptr, nullptr));
+    return QTTS_OK;
+}
+
+inline int run_plan(const GemmPlan& g, int M, cudaStream_t st, void* out = nullptr) {
+    return gemm_run(g, M, st, out);
+}
+
+inline int engine_step(qtts_engine* e, const qtts_step_io& io, cudaStream_t st) {
+    const qtts_model_desc& d = e->d;
+    const int H = d.hidden, D = d.head_dim, Hq = d.heads, Hkv = d.kv_heads, I = d.inter;
+    const int nr = io.n_rows, nn = io.n_new, R = nr * nn;
+    if (nr <= 0 || nn <= 0 || nr > e->bmax || R > e->rmax) {
+        set_error("engine_step: n_rows=%d n_new=%d outside max_batch=%d / max rows=%d", nr, nn, e->bmax, e->rmax);
+        return QTTS_ERR_INVALID;
+    }
+    if (!io.slots || !io.x_in || !io.status) {
+        set_error("engine_step: slots, x_in and status are required");
+        return QTTS_ERR_INVALID;
+    }
+    if (io.sample && (!io.token_counts || !io.full_codec_out || !io.next_x_out || !io.logits_out)) {
+        set_error("engine_step: sampling needs token_counts, logits_out, full_codec_out and next_x_out");
+        return QTTS_ERR_INVALID;
+    }
+    const SchedView sv = view_of(&d.pool);
+    // ---- scheduler: reserve KV positions, copy shared blocks
+    sched_append_kernel<<<1, kSchedThreads, 0, st>>>(sv, io.slots, nr, nn, e->mapping, e->row_ctx, e->row_pos,
+                                                     e->cow_src, e->cow_dst, io.status);
+    QTTS_LAUNCH_CHECK();
+    const size_t block_elems = (size_t)d.layers * 2 * Hkv * d.pool.block_size * D;
+    kv_copy_blocks_kernel<<<dim3(64, nr), 256, 0, st>>>(reinterpret_cast<uint4*>(d.kv_pool), block_elems / 8,
+                                                        e->cow_src, e->cow_dst, d.pool.num_blocks);
+    QTTS_LAUNCH_CHECK();
+    expand_rows_kernel<<<ceil_div(R, 256), 256, 0, st>>>(io.slots, nr, nn, e->row_slot);
+    QTTS_LAUNCH_CHECK();
+    const int32_t* smap = io.slot_indexed ? io.slots : nullptr;
+    load_x_kernel<<<ceil_div(R * H, 1024), 256, 0, st>>>(io.x_in, e->x, R, H, (io.slot_indexed && nn == 1) ? smap : nullptr);
+    QTTS_LAUNCH_CHECK();
+
+    AttnParams ap = {};
+    ap.q = e->qbuf;
+    ap.kv = reinterpret_cast<const __nv_bfloat16*>(d.kv_pool);
+    ap.num_heads = Hq;
+    ap.kv_heads = Hkv;
+    ap.num_layers = d.layers;
+    ap.block_size = d.pool.block_size;
+    ap.num_blocks = d.pool.num_blocks;
+    ap.block_table = d.pool.block_table;
+    ap.mbps = d.pool.max_blocks_per_seq;
+    ap.row_slot = e->row_slot;
+    ap.row_ctx = e->row_ctx;
+    ap.max_splits = e->max_splits;
+    ap.scale_log2 = 1.4426950408889634f / sqrtf((float)D);
+    ap.ws_o = e->ws_o;
+    ap.ws_ml = e->ws_ml;
+    ap.out = e->attn;
+    ap.R = R;
+
+    // ---- talker layers
+    for (int l = 0; l < d.layers; ++l) {
+        const LayerGemms& g = e->tg[l];
+        QTTS_TRY(launch_rmsnorm(e->x, R, H, H, bf(d.w_in_norm, (size_t)l * H), d.rms_eps, e->xn, st));
+        QTTS_TRY(run_plan(g.qkv, R, st));
+        ap.layer = l;
+        QTTS_TRY(launch_attention(ap, D, st));
+        QTTS_TRY(run_plan(g.o, R, st));
+        QTTS_TRY(launch_rmsnorm(e->x, R, H, H, bf(d.w_post_norm, (size_t)l * H), d.rms_eps, e->xn, st));
+        QTTS_TRY(run_plan(g.gu, R, st));
+        QTTS_TRY(run_plan(g.down, R, st));
+    }
+    // ---- final norm of each stream's last new token, codec head
+    QTTS_TRY(launch_rmsnorm(e->x + (size_t)(nn - 1) * H, nr, H, nn * H, d.w_final_norm, d.rms_eps, e->hid, st));
+    if (io.hidden_out)
+        QTTS_CHECK_CUDA(cudaMemcpyAsync(io.hidden_out, e->hid, (size_t)nr * H * 2, cudaMemcpyDeviceToDevice, st));
+    if (io.logits_out) QTTS_TRY(run_plan(e->head, nr, st, io.logits_out));
+    if (!io.sample) return QTTS_OK;
+
+    // ---- talker sampling head
+    const int G = 1 + d.cp_stages;
+    SampleParams sp = {};
+    sp.logits = io.logits_out;
+    sp.R = nr;
+    sp.V = d.vocab;
+    sp.ld = d.vocab;
+    sp.topk = d.topk;
+    sp.gumbel = io.gumbel;
+    sp.gumbel_ld = d.topk;
+    sp.seed = io.noise_seed;
+    sp.noise_key = io.noise_key;
+    sp.noise_step = io.noise_step;
+    sp.step = io.noise_step ? 0 : io.step * 16;
+    sp.temperature = io.temperature;
+    sp.penalty = io.penalty;
+    sp.counts = io.token_counts;
+    sp.counts_row = smap;
+    sp.eos_id = d.eos_id;
+    sp.tok_out = io.full_codec_out;
+    sp.tok_ld = G;
+    QTTS_TRY(launch_sample(sp, st));
+
+    // ---- code predictor
+    const int cH = d.cp_hidden, cD = d.cp_head_dim, cHq = d.cp_heads, cHkv = d.cp_kv_heads;
+    const int crows = 2 * e->bmax;
+    AttnParams cap = {};
+    cap.q = e->cq;
+    cap.kv = e->cp_kv;
+    cap.num_heads = cHq;
+    cap.kv_heads = cHkv;
+    cap.num_layers = d.cp_layers;
+    cap.block_size = 16;
+    cap.num_blocks = e->bmax;
+    cap.block_table = e->cp_table;
+    cap.mbps = 1;
+    cap.max_splits = 1;
+    cap.scale_log2 = 1.4426950408889634f / sqrtf((float)cD);
+    cap.ws_o = e->cws_o;
+    cap.ws_ml = e->cws_ml;
+    cap.out = e->cattn;
+
+    // the tokens the next stage consumes: sampled, or forced by a parity test
+    const int64_t* codes_in = io.force_codes ? io.force_codes : io.full_codec_out;
+    for (int s = 0; s < d.cp_stages; ++s) {
+        const int rows = s == 0 ? 2 * nr : nr;
+        const int32_t* m = e->cp_meta + (size_t)s * 4 * crows;
+        if (s == 0) {
+            cp_stage0_rows_kernel<<<nr, 128, 0, st>>>(e->hid, bf(d.w_codec_emb, 0), d.vocab, H, codes_in, G,
+                                                      e->cp_in);
+        } else {
+            gather_rows_kernel<<<nr, 128, 0, st>>>(bf(d.cp_w_codec_emb, (size_t)(s - 1) * d.cp_vocab * H),
+                                                   d.cp_vocab, H, codes_in + s, G, e->cp_in, H);
+        }
+        QTTS_LAUNCH_CHECK();
+        QTTS_TRY(run_plan(e->cp_proj_pair, rows, st));
+        cap.row_slot = m + 3 * crows;
+        cap.row_ctx = m + 2 * crows;
+        cap.R = rows;
+        for (int l = 0; l < d.cp_layers; ++l) {
+            const LayerGemms& g = e->cg[l];
+            QTTS_TRY(launch_rmsnorm(e->cx, rows, cH, cH, bf(d.cp_w_in_norm, (size_t)l * cH), d.cp_rms_eps, e->cxn, st));
+            GemmPlan q = g.qkv;
+            q.p.qkv.row_pos = m + crows;
+            q.p.qkv.slot_mapping = m;
+            QTTS_TRY(run_plan(q, rows, st));
+            cap.layer = l;
+            QTTS_TRY(launch_attention(cap, cD, st));
+            QTTS_TRY(run_plan(g.o, rows, st));
+            QTTS_TRY(launch_rmsnorm(e->cx, rows, cH, cH, bf(d.cp_w_post_norm, (size_t)l * cH), d.cp_rms_eps, e->cxn,
+                                    st));
+            QTTS_TRY(run_plan(g.gu, rows, st));
+            QTTS_TRY(run_plan(g.down, rows, st));
+        }
+        // last position of each stream: row 2b+1 at stage 0, row b afterwards
+        const float* last = s == 0 ? e->cx + cH : e->cx;
+        const int ld = s == 0 ? 2 * cH : cH;
+        QTTS_TRY(launch_rmsnorm(last, nr, cH, ld, d.cp_w_final_norm, d.cp_rms_eps, e->chid, st));
+        QTTS_TRY(run_plan(e->cp_heads[s], nr, st));
+        SampleParams cs = {};
+        cs.logits = e->clogits;
+        cs.R = nr;
+        cs.V = d.cp_vocab;
+        cs.ld = d.cp_vocab;
+        cs.topk = d.topk < d.cp_vocab ? d.topk : d.cp_vocab;
+        cs.gumbel = io.cp_gumbel ? io.cp_gumbel + (size_t)s * d.topk : nullptr;
+        cs.gumbel_ld = d.cp_stages * d.topk;
+        cs.seed = io.noise_seed;
+        cs.noise_key = io.noise_key;
+        cs.noise_step = io.noise_step;
+        cs.step = (io.noise_step ? 0 : io.step * 16) + 1 + s;
+        cs.temperature = io.temperature;
+        cs.penalty = nullptr;
+        cs.counts = nullptr;
+        cs.counts_row = smap;  // per-stream temperature / noise state
+        cs.eos_id = -1;
+        cs.tok_out = io.full_codec_out + 1 + s;
+        cs.tok_ld = G;
+        QTTS_TRY(launch_sample(cs, st));
+        if (io.cp_logits_out)
+            QTTS_CHECK_CUDA(cudaMemcpy2DAsync(io.cp_logits_out + (size_t)s * d.cp_vocab,
+                                              (size_t)d.cp_stages * d.cp_vocab * sizeof(float), e->clogits,
+                                              (size_t)d.cp_vocab * sizeof(float), (size_t)d.cp_vocab * sizeof(float),
+                                              nr, cudaMemcpyDeviceToDevice, st));
+    }
+    // ---- codec embedding sum -> next input
+    codec_sum_kernel<<<nr, 256, G * sizeof(int64_t), st>>>(io.full_codec_out, G, bf(d.w_codec_emb, 0), d.vocab,
+                                                           bf(d.cp_w_codec_emb, 0), d.cp_vocab, H, io.text_add,
+                                                           io.codec_sum_out, io.next_x_out, smap, io.noise_step);
+    QTTS_LAUNCH_CHECK();
+    return QTTS_OK;
+}
+
+}  // namespace qtts

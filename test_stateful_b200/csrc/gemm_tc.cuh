@@ -1,0 +1,422 @@
+// tcgen05 bf16 GEMM for weight-streaming projections: Y[M,N] = X[M,K] · W[N,K]^T.
+//
+// Decode runs the projections at M = 64 tokens, where the work is reading the
+// weights once from HBM.  The kernel therefore puts the WEIGHT rows on the
+// UMMA M side (128 rows per tile, TMEM lanes) and the tokens on the N side
+// (BN columns of the TMEM accumulator), so one 128 x BN x 16 UMMA consumes a
+// 4 KB slice of weights.  Split-K spreads the K range of one 128-row weight
+// tile over the CTAs of a thread-block cluster (1 x splits x 1); the fp32
+// partial tiles are reduced through distributed shared memory — each CTA
+// reduces a slice of BN/splits tokens across the cluster — so there is no
+// global workspace and no atomics, and the result is deterministic.
+//
+// Roles in a 128-thread CTA: warp 0 lane 0 issues TMA loads into a STAGES-deep
+// ring (full/empty mbarriers), warp 1 lane 0 issues UMMAs and commits, warp 2
+// owns the TMEM allocation; all four warps run the epilogue (warp w reads TMEM
+// lanes 32w..32w+31).
+//
+// Epilogues (fused, applied by the reducing CTA to its token slice):
+//   BF16 / F32 store (+bias), RESIDUAL (fp32 residual += Y, the "residual +"
+//   of talker_unified_modules.py:222, 227), SWIGLU (silu(gate)*up of
+//   Qwen3MLP; weight rows interleaved 64 gate / 64 up per tile), QKV_ROPE
+//   (per-head q_norm/k_norm RMSNorm, RoPE, q to a buffer, k/v stored into the
+//   paged KV pool through the slot mapping — talker_unified_modules.py:173-190).
+#pragma once
+
+#include "common.cuh"
+
+namespace qtts {
+
+struct GemmParams {
+    int M, N, K;
+    int kblocks;   // K / 64
+    int splits;    // cluster size along grid.y
+    int epilogue;
+    void* out;
+    const __nv_bfloat16* bias;
+    qtts_qkv_epilogue qkv;
+};
+
+template <int BN, int STAGES>
+struct GemmLayout {
+    static constexpr int A_BYTES = 128 * 64 * 2;  // weight tile 128 rows x 64 k
+    static constexpr int B_BYTES = BN * 64 * 2;   // token tile BN rows x 64 k
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int PIPE_BYTES = STAGES * STAGE_BYTES;
+    static constexpr int PART_BYTES = BN * 128 * 4;  // fp32 partial, [BN tokens][128 rows]
+    static constexpr int BODY = PIPE_BYTES > PART_BYTES ? PIPE_BYTES : PART_BYTES;
+    static constexpr int SCRATCH_BYTES = 2 * 128 * 4;  // epilogue reduction scratch
+    static constexpr int BAR_BYTES = 256;
+    static constexpr int SMEM = 1024 + BODY + SCRATCH_BYTES + BAR_BYTES;
+    static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "stage buffers must keep 1024-B alignment");
+};
+
+// ---------------------------------------------------------------------------
+// epilogue helpers: operate on the reduced slice R[m][128] (fp32, shared)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
+
+template <int BN>
+__device__ void gemm_epilogue(const GemmParams& p, float* R, int m0, int per, int tile_n, int tile_m,
+                              float* scratch) {
+    const int t = threadIdx.x;  // row within the 128-row weight tile
+    const int n_g = tile_n * 128 + t;
+    switch (p.epilogue) {
+        case QTTS_EPI_BF16:
+        case QTTS_EPI_F32:
+        case QTTS_EPI_RESIDUAL: {
+            const float b = p.bias ? __bfloat162float(p.bias[n_g]) : 0.0f;
+            for (int i = 0; i < per; ++i) {
+                const int m_g = tile_m * BN + m0 + i;
+                if (m_g >= p.M) break;
+                const float v = R[(m0 + i) * 128 + t] + b;
+                const size_t o = (size_t)m_g * p.N + n_g;
+                if (p.epilogue == QTTS_EPI_BF16)
+                    reinterpret_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16(v);
+                else if (p.epilogue == QTTS_EPI_F32)
+                    reinterpret_cast<float*>(p.out)[o] = v;
+                else
+                    reinterpret_cast<float*>(p.out)[o] += v;
+            }
+            break;
+        }
+        case QTTS_EPI_SWIGLU: {
+            if (t < 64) {
+                const int half_n = p.N >> 1;
+                for (int i = 0; i < per; ++i) {
+                    const int m_g = tile_m * BN + m0 + i;
+                    if (m_g >= p.M) break;
+                    const float g = R[(m0 + i) * 128 + t];
+                    const float u = R[(m0 + i) * 128 + 64 + t];
+                    reinterpret_cast<__nv_bfloat16*>(p.out)[(size_t)m_g * half_n + tile_n * 64 + t] =
+                        __float2bfloat16(silu(g) * u);
+                }
+            }
+            break;
+        }
+        case QTTS_EPI_QKV_ROPE: {
+            const qtts_qkv_epilogue& e = p.qkv;
+            const int D = e.head_dim;
+            const int q_rows = e.num_heads * D;
+            const int k_rows = e.kv_heads * D;
+            const int d = n_g % D;
+            const int warp = t >> 5;
+            const int region = n_g < q_rows ? 0 : (n_g < q_rows + k_rows ? 1 : 2);
+            const __nv_bfloat16* nw = region == 0 ? (const __nv_bfloat16*)e.q_norm_w
+                                                  : (const __nv_bfloat16*)e.k_norm_w;
+            for (int i = 0; i < per; ++i) {
+                const int m_g = tile_m * BN + m0 + i;
+                if (m_g >= p.M) break;  // uniform across the CTA
+                float v = R[(m0 + i) * 128 + t];
+                // per-head sum of squares (a head spans D/32 warps of this tile)
+                float ss = warp_sum(v * v);
+                if ((t & 31) == 0) scratch[warp] = ss;
+                __syncthreads();
+                if (region < 2) {
+                    const int wpd = D >> 5;
+                    const int w0 = (warp / wpd) * wpd;
+                    float tot = 0.f;
+                    for (int w = 0; w < wpd; ++w) tot += scratch[w0 + w];
+                    v = v * rsqrtf(tot / (float)D + e.rms_eps) * __bfloat162float(nw[d]);
+                }
+                scratch[8 + t] = v;
+                __syncthreads();
+                int pos = e.row_pos[m_g];
+                pos = pos < 0 ? 0 : (pos >= e.max_pos ? e.max_pos - 1 : pos);  // table bounds
+                if (region < 2) {
+                    const int half = D >> 1;
+                    const int dd = d < half ? d : d - half;
+                    const float c = e.rope_cos[(size_t)pos * half + dd];
+                    const float s = e.rope_sin[(size_t)pos * half + dd];
+                    const float partner = scratch[8 + (d < half ? t + half : t - half)];
+                    v = d < half ? v * c - partner * s : v * c + partner * s;
+                }
+                if (region == 0) {
+                    reinterpret_cast<__nv_bfloat16*>(p.out)[(size_t)m_g * q_rows + n_g] = __float2bfloat16(v);
+                } else {
+                    const int slot = e.slot_mapping[m_g];
+                    if (slot >= 0) {
+                        const int blk = slot / e.block_size, off = slot % e.block_size;
+                        const int g = (n_g - q_rows - (region == 2 ? k_rows : 0)) / D;
+                        const size_t idx =
+                            ((((size_t)blk * e.num_layers + e.layer) * 2 + (region - 1)) * e.kv_heads + g) *
+                                e.block_size +
+                            off;
+                        reinterpret_cast<__nv_bfloat16*>(e.kv_pool)[idx * D + d] = __float2bfloat16(v);
+                    }
+                }
+                __syncthreads();
+            }
+            break;
+        }
+        default:
+            break;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// the kernel
+// ---------------------------------------------------------------------------
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(128) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW,
+                                                      const __grid_constant__ CUtensorMap tmX,
+                                                      const GemmParams p) {
+    using L = GemmLayout<BN, STAGES>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    float* scratch = reinterpret_cast<float*>(smem + L::BODY);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::BODY + L::SCRATCH_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* accum = empty + STAGES;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+    int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0] error, [1] loads issued, [2] loads consumed
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tile_n = blockIdx.x, tile_m = blockIdx.z;
+    const int split = (int)cluster_ctarank();  // cluster is (1, splits, 1): rank == blockIdx.y
+    const int per_split = p.kblocks / p.splits, rem = p.kblocks % p.splits;
+    const int kb0 = split * per_split + min(split, rem);
+    const int nkb = per_split + (split < rem ? 1 : 0);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(accum, 1);
+        flags[0] = 0;
+        flags[1] = 0;
+        flags[2] = 0;
+        fence_mbar_init();
+        tma_prefetch_desc(&tmW);
+        tma_prefetch_desc(&tmX);
+    }
+    if (warp == 2) {
+        tmem_alloc(tmem_slot, BN);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0 && lane == 0) {
+        // ---------------- TMA producer ----------------
+        int issued = 0;
+        for (int i = 0; i < nkb; ++i) {
+            const int s = i % STAGES;
+            const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
+            if (i >= STAGES && !mbar_wait(&empty[s], ph ^ 1u, DEV_ERR_GEMM_PRODUCER)) {
+                flags[0] = 1;
+                break;
+            }
+            uint8_t* a = smem + s * L::STAGE_BYTES;
+            uint8_t* b = a + L::A_BYTES;
+            mbar_arrive_expect_tx(&full[s], L::STAGE_BYTES);
+            tma_load_2d(a, &tmW, &full[s], (kb0 + i) * 64, tile_n * 128);
+            tma_load_2d(b, &tmX, &full[s], (kb0 + i) * 64, tile_m * BN);
+            ++issued;
+        }
+        flags[1] = issued;
+    } else if (warp == 1 && lane == 0) {
+        // ---------------- UMMA issuer ----------------
+        const uint32_t idesc = make_idesc_bf16(128, BN);
+        int consumed = 0;
+        for (int i = 0; i < nkb; ++i) {
+            const int s = i % STAGES;
+            const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
+            if (!mbar_wait(&full[s], ph, DEV_ERR_GEMM_MMA)) {
+                flags[0] = 1;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t a = smem_u32(smem + s * L::STAGE_BYTES);
+            const uint64_t da = make_sw128_desc(a);
+            const uint64_t db = make_sw128_desc(a + L::A_BYTES);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)  // 4 x UMMA_K(16) = 64; +32 B per step inside the swizzle atom
+                umma_bf16(tmem, da + 2 * kk, db + 2 * kk, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+            umma_commit(&empty[s]);
+            ++consumed;
+        }
+        flags[2] = consumed;
+        umma_commit(accum);
+    }
+    __syncwarp();
+
+    // ---------------- epilogue: TMEM -> shared partial ----------------
+    const bool ok = mbar_wait(accum, 0, DEV_ERR_GEMM_EPILOGUE);
+    tc_fence_after();
+    __syncthreads();
+    if (threadIdx.x == 0 && (flags[0] || !ok)) {
+        // drain: wait (bounded) for loads issued but never consumed before reusing their buffers
+        for (int i = flags[2]; i < flags[1]; ++i)
+            mbar_wait(&full[i % STAGES], (uint32_t)(i / STAGES) & 1u, DEV_ERR_DRAIN);
+    }
+    __syncthreads();
+    float* P = reinterpret_cast<float*>(smem);
+    const bool good = ok && flags[0] == 0;
+    {
+        const int row = warp * 32 + lane;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+            float v[16];
+            tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c, v);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) P[(c + j) * 128 + row] = good ? v[j] : 0.0f;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 2) tmem_dealloc(tmem, BN);
+
+    // ---------------- split-K reduction across the cluster ----------------
+    const int per = BN / p.splits;
+    const int m0 = split * per;
+    if (p.splits > 1) {
+        cluster_sync();  // every CTA's partial is in its shared memory
+        const uint32_t base = smem_u32(P);
+        for (int i = 0; i < per; ++i) {
+            const int idx = (m0 + i) * 128 + threadIdx.x;
+            float acc = 0.f;
+            for (int r = 0; r < p.splits; ++r)  // fixed order: deterministic
+                acc += ld_dsmem_f32(map_to_rank(base + idx * 4, (uint32_t)r));
+            P[idx] = acc;
+        }
+        __syncthreads();
+    }
+    gemm_epilogue<BN>(p, P, m0, per, tile_n, tile_m, scratch);
+    if (p.splits > 1) cluster_sync();  // peers finished reading this CTA's shared memory
+}
+
+// ---------------------------------------------------------------------------
+// host side: tensor maps and launch
+// ---------------------------------------------------------------------------
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+inline PFN_encodeTiled get_encode_fn() {
+    static PFN_encodeTiled fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_encodeTiled>(p);
+    }
+    return fn;
+}
+
+// 2-D bf16 row-major [rows, cols] map with a (64 x box_rows) box and 128-B swizzle.
+inline int make_map_bf16(CUtensorMap* map, const void* ptr, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+    PFN_encodeTiled enc = get_encode_fn();
+    if (!enc) {
+        set_error("cuTensorMapEncodeTiled unavailable");
+        return QTTS_ERR_CUDA;
+    }
+    if ((reinterpret_cast<uintptr_t>(ptr) & 15) != 0 || (cols * 2) % 16 != 0) {
+        set_error("tensor map needs a 16-byte aligned base and row pitch");
+        return QTTS_ERR_INVALID;
+    }
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {cols * 2};
+    cuuint32_t box[2] = {64, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("cuTensorMapEncodeTiled failed (%d)", (int)r);
+        return QTTS_ERR_CUDA;
+    }
+    return QTTS_OK;
+}
+
+constexpr int kGemmStages = 4;
+
+inline int pick_bn(int M) { return M <= 64 ? 64 : 128; }
+
+inline int pick_splits(int N, int M, int K, int BN) {
+    const int tiles = (N / 128) * ceil_div(M, BN);
+    const int kb = K / 64;
+    const int target = 2 * num_sms();
+    int s = 1;
+    while (s * 2 <= 8 && tiles * s * 2 <= target + target / 5 && kb / (s * 2) >= 2 && BN % (s * 2) == 0) s *= 2;
+    return s;
+}
+
+template <int BN>
+inline int launch_gemm_bn(const CUtensorMap& mw, const CUtensorMap& mx, const GemmParams& p, cudaStream_t st) {
+    using L = GemmLayout<BN, kGemmStages>;
+    auto kern = gemm_tc_kernel<BN, kGemmStages>;
+    static bool attr_done = false;
+    if (!attr_done) {
+        QTTS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM));
+        attr_done = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.N / 128, p.splits, ceil_div(p.M, BN));
+    cfg.blockDim = dim3(128, 1, 1);
+    cfg.dynamicSmemBytes = L::SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = p.splits;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    QTTS_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, mw, mx, p));
+    return QTTS_OK;
+}
+
+// Prepared GEMM: tensor maps built once (two token-tile heights), reused every step.
+struct GemmPlan {
+    CUtensorMap mw, mx64, mx128;
+    GemmParams p;
+};
+
+inline int gemm_plan(GemmPlan* g, const void* X, int rows, int K, const void* W, int N, int epilogue, void* out,
+                     const void* bias, const qtts_qkv_epilogue* qkv, int unused = -1) {
+    (void)unused;
+    if (N % 128 != 0 || K % 64 != 0 || rows <= 0) {
+        set_error("gemm: need N %% 128 == 0, K %% 64 == 0, rows > 0 (N=%d K=%d rows=%d)", N, K, rows);
+        return QTTS_ERR_UNSUPPORTED;
+    }
+    if (epilogue == QTTS_EPI_QKV_ROPE && (!qkv || qkv->head_dim % 32 != 0 || 128 % qkv->head_dim != 0)) {
+        set_error("gemm: QKV epilogue needs head_dim in {32, 64, 128}");
+        return QTTS_ERR_UNSUPPORTED;
+    }
+    int rc = make_map_bf16(&g->mw, W, (uint64_t)N, (uint64_t)K, 128);
+    if (rc) return rc;
+    rc = make_map_bf16(&g->mx64, X, (uint64_t)rows, (uint64_t)K, 64);
+    if (rc) return rc;
+    rc = make_map_bf16(&g->mx128, X, (uint64_t)rows, (uint64_t)K, 128);
+    if (rc) return rc;
+    GemmParams& p = g->p;
+    memset(&p, 0, sizeof(p));
+    p.M = rows;
+    p.N = N;
+    p.K = K;
+    p.kblocks = K / 64;
+    p.splits = 1;
+    p.epilogue = epilogue;
+    p.out = out;
+    p.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+    if (qkv) p.qkv = *qkv;
+    return QTTS_OK;
+}
+
+// Launch on the first M rows of the plan's X buffer.
+inline int gemm_run(GemmPlan g, int M, cudaStream_t st, void* out = nullptr) {
+    if (M <= 0) return QTTS_OK;
+    const int bn = pick_bn(M);
+    g.p.M = M;
+    g.p.splits = pick_splits(g.p.N, M, g.p.K, bn);
+    if (out) g.p.out = out;
+    if (bn == 64) return launch_gemm_bn<64>(g.mw, g.mx64, g.p, st);
+    return launch_gemm_bn<128>(g.mw, g.mx128, g.p, st);
+}
+
+}  // namespace qtts

@@ -1,0 +1,230 @@
+// On-device sampling head: suppress / repetition penalty / top-k / temperature /
+// Gumbel-max / counts update, one CTA per row.
+//
+// Talker (talker_unified_modules.py:373-388): ids [V-1024, V) except EOS are
+// set to -1e9; where token_counts > 0 a logit g becomes g/penalty if g > 0
+// else g*penalty; the top-k values (descending) are divided by the
+// temperature, the j-th gets gumbel[j] added, the argmax picks the token and
+// token_counts[token] += 1.  Code predictor (utils.py:986-1001): the same
+// without suppress, penalty and counts.
+//
+// Top-k: a 4-pass 8-bit radix select on order-preserving integer keys finds
+// the k-th largest key; the candidates (>= that key) are sorted by
+// (value desc, index asc) in one warp, which fixes the rank each Gumbel
+// sample is added to.  Noise, when not supplied, is Philox4x32-10
+// (Salmon et al., SC'11) keyed by (seed, per-stream key, step, rank) and
+// mapped to -log(-log(u)) with u clamped to [1e-8, 1] as
+// engine/backend/executor.py:1238-1251 does.
+#pragma once
+
+#include "common.cuh"
+
+namespace qtts {
+
+struct SampleParams {
+    const float* logits;
+    int R, V, ld, topk;
+    const float* gumbel;
+    int gumbel_ld;
+    uint64_t seed;
+    const int64_t* noise_key;   // per counts-row key (NULL: row index)
+    const int32_t* noise_step;  // per counts-row frame counter (NULL: 0); counter = 16*frame + step
+    int step;
+    const float* temperature;
+    const float* penalty;
+    int64_t* counts;
+    const int32_t* counts_row;  // counts row of batch row r (NULL: r)
+    int eos_id;
+    int64_t* tok_out;
+    int tok_ld;
+};
+
+__device__ __forceinline__ uint32_t float_key(float f) {
+    const uint32_t b = __float_as_uint(f);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+// Philox4x32 with 10 rounds; constants from the published algorithm.
+__device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint2 k) {
+    const uint32_t M0 = 0xD2511F53u, M1 = 0xCD9E8D57u, W0 = 0x9E3779B9u, W1 = 0xBB67AE85u;
+#pragma unroll
+    for (int i = 0; i < 10; ++i) {
+        const uint32_t hi0 = __umulhi(M0, c.x), lo0 = M0 * c.x;
+        const uint32_t hi1 = __umulhi(M1, c.z), lo1 = M1 * c.z;
+        c = make_uint4(hi1 ^ c.y ^ k.x, lo1, hi0 ^ c.w ^ k.y, lo0);
+        k.x += W0;
+        k.y += W1;
+    }
+    return c;
+}
+
+__device__ __forceinline__ float gumbel_noise(uint64_t seed, uint64_t key, int step, int j) {
+    const uint4 ctr = make_uint4((uint32_t)j, (uint32_t)step, (uint32_t)key, (uint32_t)(key >> 32));
+    const uint4 r = philox4x32_10(ctr, make_uint2((uint32_t)seed, (uint32_t)(seed >> 32)));
+    float u = ((float)r.x + 0.5f) * 2.3283064365386963e-10f;  // (0, 1)
+    u = fminf(fmaxf(u, 1e-8f), 1.0f);
+    return -logf(-logf(u));
+}
+
+constexpr int kSampleThreads = 256;
+constexpr int kSampleMaxPer = 16;   // V <= 4096
+constexpr int kSampleCand = 128;    // candidate buffer (>= topk, room for ties)
+
+__global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SampleParams p) {
+    __shared__ uint32_t hist[256];
+    __shared__ uint32_t s_prefix, s_need;
+    __shared__ int s_ncand;
+    __shared__ float c_val[kSampleCand];
+    __shared__ int c_idx[kSampleCand];
+
+    const int r = blockIdx.x, tid = threadIdx.x;
+    const float* lg = p.logits + (size_t)r * p.ld;
+    const int crow = p.counts_row ? p.counts_row[r] : r;  // per-stream state row (slot)
+    const float pen = p.penalty ? p.penalty[crow] : 1.0f;
+    const float temp = p.temperature ? p.temperature[crow] : 1.0f;
+    int64_t* cnt_rw = p.counts ? p.counts + (size_t)crow * p.V : nullptr;
+    const int64_t* cnt = cnt_rw;
+
+    float val[kSampleMaxPer];
+    uint32_t key[kSampleMaxPer];
+#pragma unroll
+    for (int i = 0; i < kSampleMaxPer; ++i) {
+        const int idx = tid + i * kSampleThreads;
+        float g = -INFINITY;
+        if (idx < p.V) {
+            g = lg[idx];
+            if (cnt) {
+                if (idx >= p.V - 1024 && idx != p.eos_id) g = -1e9f;
+                if (cnt[idx] > 0) g = g > 0.f ? g / pen : g * pen;
+            }
+        }
+        val[i] = g;
+        key[i] = idx < p.V ? float_key(g) : 0u;  // padding sorts below every real value
+    }
+
+    // radix select of the topk-th largest key
+    uint32_t prefix = 0, mask = 0;
+    uint32_t need = (uint32_t)p.topk;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        for (int i = tid; i < 256; i += kSampleThreads) hist[i] = 0;
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < kSampleMaxPer; ++i) {
+            const int idx = tid + i * kSampleThreads;
+            if (idx < p.V && (key[i] & mask) == prefix) atomicAdd(&hist[(key[i] >> shift) & 255u], 1u);
+        }
+        __syncthreads();
+        if (tid == 0) {
+            uint32_t above = 0;
+            int b = 255;
+            for (; b > 0; --b) {
+                if (above + hist[b] >= need) break;
+                above += hist[b];
+            }
+            s_prefix = prefix | ((uint32_t)b << shift);
+            s_need = need - above;
+        }
+        __syncthreads();
+        prefix = s_prefix;
+        need = s_need;
+        mask |= 255u << shift;
+        __syncthreads();
+    }
+    // gather candidates: all keys > prefix, and ties (== prefix) while room remains
+    if (tid == 0) s_ncand = 0;
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < kSampleMaxPer; ++i) {
+        const int idx = tid + i * kSampleThreads;
+        if (idx < p.V && key[i] >= prefix) {
+            const int slot = atomicAdd(&s_ncand, 1);
+            if (slot < kSampleCand) {
+                c_val[slot] = val[i];
+                c_idx[slot] = idx;
+            }
+        }
+    }
+    __syncthreads();
+    if (tid < 32) {
+        const int n = min(s_ncand, kSampleCand);
+        // bitonic sort of 128 entries by (value desc, index asc) in one warp, 4 per lane
+        float v[4];
+        int ix[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int e = tid * 4 + j;
+            v[j] = e < n ? c_val[e] : -INFINITY;
+            ix[j] = e < n ? c_idx[e] : 0x7fffffff;
+        }
+        // write back to shared and sort there (simple, 128 elements)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            c_val[tid * 4 + j] = v[j];
+            c_idx[tid * 4 + j] = ix[j];
+        }
+        __syncwarp();
+        for (int k = 2; k <= kSampleCand; k <<= 1) {
+            for (int jj = k >> 1; jj > 0; jj >>= 1) {
+                for (int e = tid; e < kSampleCand; e += 32) {
+                    const int o = e ^ jj;
+                    if (o > e) {
+                        const bool up = (e & k) == 0;  // "up" = descending order block
+                        const float va = c_val[e], vb = c_val[o];
+                        const int ia = c_idx[e], ib = c_idx[o];
+                        const bool a_first = (va > vb) || (va == vb && ia < ib);
+                        if (up != a_first) {
+                            c_val[e] = vb;
+                            c_val[o] = va;
+                            c_idx[e] = ib;
+                            c_idx[o] = ia;
+                        }
+                    }
+                }
+                __syncwarp();
+            }
+        }
+        // Gumbel-max over the first topk ranks
+        float best = -INFINITY;
+        int best_j = 0x7fffffff;
+        for (int j = tid; j < p.topk; j += 32) {
+            float gn;
+            if (p.gumbel)
+                gn = p.gumbel[(size_t)r * p.gumbel_ld + j];
+            else
+                gn = gumbel_noise(p.seed, p.noise_key ? (uint64_t)p.noise_key[crow] : (uint64_t)crow,
+                                  (p.noise_step ? p.noise_step[crow] * 16 : 0) + p.step, j);
+            const float sc = c_val[j] / temp + gn;
+            if (sc > best || (sc == best && j < best_j)) {
+                best = sc;
+                best_j = j;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+            const int oj = __shfl_xor_sync(0xffffffffu, best_j, o);
+            if (ob > best || (ob == best && oj < best_j)) {
+                best = ob;
+                best_j = oj;
+            }
+        }
+        if (tid == 0) {
+            const int tok = c_idx[best_j];
+            p.tok_out[(size_t)r * p.tok_ld] = tok;
+            if (cnt_rw) cnt_rw[tok] += 1;
+        }
+    }
+}
+
+inline int launch_sample(const SampleParams& p, cudaStream_t st) {
+    if (p.R <= 0) return QTTS_OK;
+    if (p.V > kSampleThreads * kSampleMaxPer || p.topk < 1 || p.topk > 64 || p.topk > p.V) {
+        set_error("sample: need V <= %d and 1 <= topk <= min(64, V)", kSampleThreads * kSampleMaxPer);
+        return QTTS_ERR_UNSUPPORTED;
+    }
+    sample_kernel<<<p.R, kSampleThreads, 0, st>>>(p);
+    QTTS_LAUNCH_CHECK();
+    return QTTS_OK;
+}
+
+}  // namespace qtts

@@ -1,0 +1,195 @@
+// Bandwidth-bound helper kernels on the decode path: RMSNorm, embedding
+// gathers, the codec embedding sum, KV block copy / scatter / gather, and the
+// row bookkeeping of the code predictor.
+#pragma once
+
+#include "common.cuh"
+
+namespace qtts {
+
+// ---------------------------------------------------------------------------
+// RMSNorm (Qwen3RMSNorm): y = w * x * rsqrt(mean(x^2) + eps), fp32 in, bf16 out
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const float* __restrict__ x, int H, int ld,
+                                                      const __nv_bfloat16* __restrict__ w, float eps,
+                                                      __nv_bfloat16* __restrict__ y) {
+    __shared__ float red[8];
+    const int r = blockIdx.x;
+    const float* xr = x + (size_t)r * ld;
+    float ss = 0.f;
+    for (int i = threadIdx.x * 4; i < H; i += 1024) {
+        const float4 v = *reinterpret_cast<const float4*>(xr + i);
+        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) tot += red[i];
+    const float inv = rsqrtf(tot / (float)H + eps);
+    __nv_bfloat16* yr = y + (size_t)r * H;
+    for (int i = threadIdx.x * 4; i < H; i += 1024) {
+        const float4 v = *reinterpret_cast<const float4*>(xr + i);
+        const __nv_bfloat162 w01 = *reinterpret_cast<const __nv_bfloat162*>(w + i);
+        const __nv_bfloat162 w23 = *reinterpret_cast<const __nv_bfloat162*>(w + i + 2);
+        __nv_bfloat162 o01 = __floats2bfloat162_rn(v.x * inv * __low2float(w01), v.y * inv * __high2float(w01));
+        __nv_bfloat162 o23 = __floats2bfloat162_rn(v.z * inv * __low2float(w23), v.w * inv * __high2float(w23));
+        uint2 pack;
+        pack.x = *reinterpret_cast<uint32_t*>(&o01);
+        pack.y = *reinterpret_cast<uint32_t*>(&o23);
+        *reinterpret_cast<uint2*>(yr + i) = pack;
+    }
+}
+
+inline int launch_rmsnorm(const float* x, int M, int H, int ld, const void* w, float eps, void* y, cudaStream_t st) {
+    if (M <= 0) return QTTS_OK;
+    if (H % 4 != 0 || ld % 4 != 0) {
+        set_error("rmsnorm: H and ld must be multiples of 4");
+        return QTTS_ERR_UNSUPPORTED;
+    }
+    rmsnorm_kernel<<<M, 256, 0, st>>>(x, H, ld, reinterpret_cast<const __nv_bfloat16*>(w), eps,
+                                      reinterpret_cast<__nv_bfloat16*>(y));
+    QTTS_LAUNCH_CHECK();
+    return QTTS_OK;
+}
+
+// ---------------------------------------------------------------------------
+// row gathers
+// ---------------------------------------------------------------------------
+// out[r * out_ld + c] = table[ids[r * id_ld] * H + c]   (bf16 rows)
+__global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ table, int V, int H,
+                                   const int64_t* __restrict__ ids, int id_ld, __nv_bfloat16* __restrict__ out,
+                                   int out_ld) {
+    const int r = blockIdx.x;
+    int64_t id = ids[(size_t)r * id_ld];
+    if (id < 0 || id >= V) id = 0;  // stay in bounds; callers pass sampled (valid) ids
+    const uint4* src = reinterpret_cast<const uint4*>(table + (size_t)id * H);
+    uint4* dst = reinterpret_cast<uint4*>(out + (size_t)r * out_ld);
+    for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = src[i];
+}
+
+// Stage-0 input of the code predictor: rows [2b] = hidden[b], [2b+1] = codec_emb[tok0[b]]
+// (CodePredictorUnrolled.forward, utils.py:1019-1020).
+__global__ void cp_stage0_rows_kernel(const __nv_bfloat16* __restrict__ hidden, const __nv_bfloat16* __restrict__ emb,
+                                      int V, int H, const int64_t* __restrict__ tok, int tok_ld,
+                                      __nv_bfloat16* __restrict__ out) {
+    const int b = blockIdx.x;
+    int64_t id = tok[(size_t)b * tok_ld];
+    if (id < 0 || id >= V) id = 0;
+    const uint4* h = reinterpret_cast<const uint4*>(hidden + (size_t)b * H);
+    const uint4* e = reinterpret_cast<const uint4*>(emb + (size_t)id * H);
+    uint4* o0 = reinterpret_cast<uint4*>(out + (size_t)(2 * b) * H);
+    uint4* o1 = reinterpret_cast<uint4*>(out + (size_t)(2 * b + 1) * H);
+    for (int i = threadIdx.x; i < H / 8; i += blockDim.x) {
+        o0[i] = h[i];
+        o1[i] = e[i];
+    }
+}
+
+// ---------------------------------------------------------------------------
+// codec embedding sum + next input embedding
+// ---------------------------------------------------------------------------
+__global__ void codec_sum_kernel(const int64_t* __restrict__ codes, int G, const __nv_bfloat16* __restrict__ t0,
+                                 int V0, const __nv_bfloat16* __restrict__ tc, int Vc, int H,
+                                 const float* __restrict__ text_add, float* __restrict__ csum,
+                                 float* __restrict__ next_x, const int32_t* __restrict__ row_map,
+                                 int32_t* __restrict__ noise_step) {
+    const int r = blockIdx.x;
+    const size_t orow = row_map ? (size_t)row_map[r] : (size_t)r;  // output / text row
+    if (noise_step && threadIdx.x == 0) noise_step[orow] += 1;     // this stream sampled one more frame
+    extern __shared__ int64_t ids[];
+    for (int g = threadIdx.x; g < G; g += blockDim.x) {
+        int64_t c = codes[(size_t)r * G + g];
+        const int64_t lim = g == 0 ? V0 : Vc;
+        ids[g] = (c < 0 || c >= lim) ? -1 : c;  // CP tables are zero beyond Vc (codec_embedding_sum.py:46-49)
+    }
+    __syncthreads();
+    for (int h = threadIdx.x * 2; h < H; h += blockDim.x * 2) {
+        float a = 0.f, b = 0.f;
+        for (int g = 0; g < G; ++g) {
+            const int64_t id = ids[g];
+            if (id < 0) continue;
+            const __nv_bfloat16* row = g == 0 ? t0 + (size_t)id * H : tc + ((size_t)(g - 1) * Vc + id) * H;
+            const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(row + h);
+            a += __low2float(v);
+            b += __high2float(v);
+        }
+        if (csum) {
+            csum[orow * H + h] = a;
+            csum[orow * H + h + 1] = b;
+        }
+        if (text_add) {
+            a += text_add[orow * H + h];
+            b += text_add[orow * H + h + 1];
+        }
+        // the engine feeds next_embed to the graph in the model dtype (executor.py:1095-1097)
+        next_x[orow * H + h] = bf16_round(a);
+        next_x[orow * H + h + 1] = bf16_round(b);
+    }
+}
+
+// x[r] = bf16round(x_in[row_map ? row_map[r] : r]) (the executor casts input_embeds to bf16)
+__global__ void load_x_kernel(const float* __restrict__ x_in, float* __restrict__ x, int rows, int H,
+                              const int32_t* __restrict__ row_map) {
+    const size_t n = (size_t)rows * H;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t r = i / H, c = i % H;
+        const size_t src = row_map ? (size_t)row_map[r] : r;
+        x[i] = bf16_round(x_in[src * H + c]);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// KV pool: block copy (copy-on-write), row scatter / gather
+// ---------------------------------------------------------------------------
+__global__ void kv_copy_blocks_kernel(uint4* __restrict__ pool, size_t block_vec, const int32_t* __restrict__ src,
+                                      const int32_t* __restrict__ dst, int num_blocks) {
+    const int i = blockIdx.y;
+    const int s = src[i], d = dst[i];
+    if (s < 0 || d < 0 || s >= num_blocks || d >= num_blocks) return;
+    const uint4* a = pool + (size_t)s * block_vec;
+    uint4* b = pool + (size_t)d * block_vec;
+    for (size_t k = (size_t)blockIdx.x * blockDim.x + threadIdx.x; k < block_vec; k += (size_t)gridDim.x * blockDim.x)
+        b[k] = a[k];
+}
+
+// rows [n][L2][Hkv][D] -> pool[(blk, l2, g, off, d)]
+__global__ void kv_scatter_kernel(__nv_bfloat16* __restrict__ pool, int L2, int Hkv, int D, int bs, int num_blocks,
+                                  const __nv_bfloat16* __restrict__ rows, const int32_t* __restrict__ mapping) {
+    const int i = blockIdx.x;
+    const int m = mapping[i];
+    if (m < 0) return;
+    const int blk = m / bs, off = m % bs;
+    if (blk >= num_blocks) return;
+    const int per = L2 * Hkv * D;
+    for (int e = threadIdx.x; e < per; e += blockDim.x) {
+        const int d = e % D, g = (e / D) % Hkv, l2 = e / (D * Hkv);
+        pool[((((size_t)blk * L2 + l2) * Hkv + g) * bs + off) * D + d] = rows[(size_t)i * per + e];
+    }
+}
+
+// out [L2][Hkv][n][D] from the slot's block table
+__global__ void kv_gather_kernel(const __nv_bfloat16* __restrict__ pool, int L2, int Hkv, int D, int bs,
+                                 int num_blocks, const int32_t* __restrict__ table_row, int n,
+                                 __nv_bfloat16* __restrict__ out) {
+    const int t = blockIdx.x;
+    int blk = table_row[t / bs];
+    const int off = t % bs;
+    const bool ok = blk >= 0 && blk < num_blocks;
+    const int per = L2 * Hkv * D;
+    for (int e = threadIdx.x; e < per; e += blockDim.x) {
+        const int d = e % D, g = (e / D) % Hkv, l2 = e / (D * Hkv);
+        const __nv_bfloat16 v =
+            ok ? pool[((((size_t)blk * L2 + l2) * Hkv + g) * bs + off) * D + d] : __float2bfloat16(0.f);
+        out[(((size_t)l2 * Hkv + g) * n + t) * D + d] = v;
+    }
+}
+
+// row -> slot map for n_rows x n_new rows: row i*n_new+j belongs to slots[i]
+__global__ void expand_rows_kernel(const int32_t* __restrict__ slots, int n_rows, int n_new, int32_t* __restrict__ out) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n_rows * n_new; i += gridDim.x * blockDim.x)
+        out[i] = slots[i / n_new];
+}
+
+}  // namespace qtts

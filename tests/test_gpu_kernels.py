@@ -1,0 +1,270 @@
+"""Kernel parity on the B200: each entry point of libqtts_b200.so against the
+CPU oracle (integer/index work: bit-exact) or an fp32 torch statement of the
+same op (floating point: tolerance in each test)."""
+
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+from oracle import model as M  # noqa: E402
+from oracle.paged_state import PagedState, OK  # noqa: E402
+from test_stateful_b200 import _lib, ops  # noqa: E402
+from test_stateful_b200.config import EngineConfig, PagedPoolConfig, TalkerConfig  # noqa: E402
+from test_stateful_b200.runtime.model import PagedPoolTensors, rope_tables  # noqa: E402
+
+DEV = "cuda"
+
+
+def _gen(seed):
+    return torch.Generator(device="cpu").manual_seed(seed)
+
+
+def _rand(shape, seed, scale=1.0, dtype=torch.bfloat16):
+    return (torch.randn(shape, generator=_gen(seed)) * scale).to(dtype).to(DEV)
+
+
+# --------------------------------------------------------------------- GEMM
+GEMM_SHAPES = [(64, 4096, 2048), (64, 2048, 6144), (37, 1024, 2048), (128, 2048, 1024), (200, 512, 256),
+               (1, 3072, 2048), (17, 128, 64)]
+
+
+@pytest.mark.parametrize("M_,N,K", GEMM_SHAPES)
+def test_gemm_f32_matches_fp32_matmul(M_, N, K):
+    x = _rand((M_, K), 1)
+    w = _rand((N, K), 2, 0.05)
+    y = ops.gemm(x, w, _lib.EPI_F32)
+    ref = x.float() @ w.float().T
+    torch.testing.assert_close(y, ref, rtol=1e-3, atol=1e-3)  # fp32 accumulation of exact bf16 products
+
+
+def test_gemm_bf16_bias_and_residual():
+    x = _rand((64, 1024), 3)
+    w = _rand((2048, 1024), 4, 0.05)
+    b = _rand((2048,), 5, 0.1)
+    y = ops.gemm(x, w, _lib.EPI_BF16, bias=b)
+    ref = x.float() @ w.float().T + b.float()
+    torch.testing.assert_close(y.float(), ref, rtol=1e-2, atol=1e-2)  # bf16 output rounding
+    r0 = torch.randn(64, 2048, generator=_gen(6)).to(DEV)
+    r = r0.clone()
+    ops.gemm(x, w, _lib.EPI_RESIDUAL, out=r)
+    torch.testing.assert_close(r, r0 + x.float() @ w.float().T, rtol=1e-3, atol=1e-3)
+
+
+def test_gemm_swiglu_interleaved():
+    from test_stateful_b200.runtime.model import _interleave_gate_up
+    H, I = 1024, 3072
+    x = _rand((64, H), 7)
+    g = _rand((I, H), 8, 0.05)
+    u = _rand((I, H), 9, 0.05)
+    w = _interleave_gate_up(g, u)
+    y = ops.gemm(x, w, _lib.EPI_SWIGLU)
+    gf, uf = x.float() @ g.float().T, x.float() @ u.float().T
+    ref = torch.nn.functional.silu(gf) * uf
+    torch.testing.assert_close(y.float(), ref, rtol=2e-2, atol=2e-3)
+
+
+@pytest.mark.parametrize("D,Hq,Hkv,H", [(128, 16, 8, 2048), (64, 16, 8, 1024)])
+def test_gemm_qkv_rope_epilogue(D, Hq, Hkv, H):
+    Mr = 64
+    L, layer, nb = 3, 1, 32
+    x = _rand((Mr, H), 10)
+    w = _rand(((Hq + 2 * Hkv) * D, H), 11, 0.05)
+    qn = (1 + 0.1 * torch.randn(D, generator=_gen(12))).to(torch.bfloat16).to(DEV)
+    kn = (1 + 0.1 * torch.randn(D, generator=_gen(13))).to(torch.bfloat16).to(DEV)
+    cos, sin = rope_tables(D, 1e6, 1024, DEV)
+    pos = torch.randint(0, 1000, (Mr,), generator=_gen(14)).to(torch.int32).to(DEV)
+    perm = torch.randperm(nb * 16, generator=_gen(15))[:Mr].to(torch.int32)
+    mapping = perm.clone()
+    mapping[5] = -1
+    mapping = mapping.to(DEV)
+    pool = torch.zeros(nb, L, 2, Hkv, 16, D, device=DEV, dtype=torch.bfloat16)
+    q_out = torch.empty(Mr, Hq * D, device=DEV, dtype=torch.bfloat16)
+    e = _lib.QkvEpilogue(Hq, Hkv, D, qn.data_ptr(), kn.data_ptr(), 1e-6, cos.data_ptr(), sin.data_ptr(), 1024,
+                         pos.data_ptr(), mapping.data_ptr(), pool.data_ptr(), layer, L, 16)
+    ops.gemm(x, w, _lib.EPI_QKV_ROPE, out=q_out, qkv=e)
+    torch.cuda.synchronize()
+    y = (x.float() @ w.float().T).cpu()
+    q = y[:, :Hq * D].view(Mr, Hq, D)
+    k = y[:, Hq * D:(Hq + Hkv) * D].view(Mr, Hkv, D)
+    v = y[:, (Hq + Hkv) * D:].view(Mr, Hkv, D)
+    q = M.rms_norm(q, qn.float().cpu(), 1e-6)
+    k = M.rms_norm(k, kn.float().cpu(), 1e-6)
+    c, s = M.rope_cos_sin(pos.long().cpu().unsqueeze(1), D, 1e6)   # [M,1,D]
+    q = q * c + M.rotate_half(q) * s
+    k = k * c + M.rotate_half(k) * s
+    torch.testing.assert_close(q_out.float().cpu().view(Mr, Hq, D), q, rtol=2e-2, atol=2e-2)
+    pc = pool.float().cpu()
+    for m in range(Mr):
+        sm = int(mapping[m])
+        if sm < 0:
+            continue
+        blk, off = sm // 16, sm % 16
+        torch.testing.assert_close(pc[blk, layer, 0, :, off], k[m], rtol=2e-2, atol=2e-2)
+        torch.testing.assert_close(pc[blk, layer, 1, :, off], v[m], rtol=2e-2, atol=2e-2)
+    # row 5 had no slot: its position must be untouched (zeros) everywhere
+    assert int((pool[:, layer].float().abs().sum(dim=(1, 2, 4)) > 0).sum()) == Mr - 1
+
+
+# --------------------------------------------------------------------- attention
+@pytest.mark.parametrize("D", [128, 64])
+def test_paged_attention_ragged(D):
+    Hkv, Hq, L, layer, nb, mbps = 8, 16, 2, 1, 300, 80
+    ctxs = [1, 15, 16, 17, 100, 255, 256, 257, 700, 1024, 1280]
+    R = len(ctxs)
+    g = _gen(20)
+    kv = (torch.randn(nb, L, 2, Hkv, 16, D, generator=g)).to(torch.bfloat16).to(DEV)
+    table = torch.full((R, mbps), -1, dtype=torch.int32)
+    perm = torch.randperm(nb, generator=g)
+    i = 0
+    for r, c in enumerate(ctxs):
+        n = -(-c // 16)
+        table[r, :n] = perm[i:i + n] if i + n <= nb else torch.randint(0, nb, (n,), generator=g)
+        i = (i + n) % (nb - 100)
+    q = torch.randn(R, Hq, D, generator=g).to(torch.bfloat16).to(DEV)
+    row_slot = torch.arange(R, dtype=torch.int32, device=DEV)
+    row_ctx = torch.tensor(ctxs, dtype=torch.int32, device=DEV)
+    out = ops.paged_attention(q, kv, layer, table.to(DEV), row_slot, row_ctx, max_ctx=mbps * 16)
+    kvc, qc = kv.float().cpu(), q.float().cpu()
+    for r, c in enumerate(ctxs):
+        blocks = table[r, : -(-c // 16)].long()
+        K = kvc[blocks, layer, 0].permute(1, 0, 2, 3).reshape(Hkv, -1, D)[:, :c]
+        V = kvc[blocks, layer, 1].permute(1, 0, 2, 3).reshape(Hkv, -1, D)[:, :c]
+        K = K.repeat_interleave(2, 0)
+        V = V.repeat_interleave(2, 0)
+        p = torch.softmax((qc[r].unsqueeze(1) @ K.transpose(1, 2)).squeeze(1) / D ** 0.5, dim=-1)
+        ref = (p.unsqueeze(1) @ V).squeeze(1).reshape(-1)
+        torch.testing.assert_close(out[r].float().cpu(), ref, rtol=2e-2, atol=1e-2)
+
+
+# --------------------------------------------------------------------- scheduler
+def _pool(num_blocks=16, max_slots=6, mbps=8):
+    cfg = EngineConfig(talker=TalkerConfig(num_layers=1, kv_heads=1, head_dim=8),
+                       pool=PagedPoolConfig(block_size=16, num_blocks=num_blocks, max_slots=max_slots,
+                                            max_seq_len=mbps * 16))
+    return PagedPoolTensors(cfg, DEV)
+
+
+def _assert_state_equal(pool, st: PagedState):
+    torch.cuda.synchronize()
+    top = int(pool.free_top.item())
+    assert top == st.free_top
+    assert np.array_equal(pool.free_stack[:top].cpu().numpy(), st.free_stack_array())
+    assert np.array_equal(pool.refcount.cpu().numpy(), st.refcount)
+    assert np.array_equal(pool.block_table.cpu().numpy(), st.table)
+    assert np.array_equal(pool.seq_len.cpu().numpy(), st.seq_len)
+
+
+def test_sched_matches_oracle_bit_exact():
+    pool = _pool()
+    pool.init()
+    sch = ops.Sched(pool)
+    st = PagedState(16, 16, 6, 8)
+    rng = np.random.default_rng(0)
+
+    def append(slots, n):
+        s_dev = torch.tensor(slots, dtype=torch.int32, device=DEV)
+        m, ctx, pos, cs, cd = sch.append(s_dev, n)
+        status, m_ref, cow = st.append(slots, n)
+        torch.cuda.synchronize()
+        assert int(sch.status.item()) == status
+        assert np.array_equal(m.cpu().numpy().astype(np.int64), m_ref)
+        got = [(int(a), int(b)) for a, b in zip(cs.cpu(), cd.cpu()) if a >= 0]
+        assert got == cow
+        _assert_state_equal(pool, st)
+        return status
+
+    assert append([0], 37) == OK
+    assert append([1], 5) == OK
+    entry_dev = sch.make_entry(0, 21)
+    entry = st.make_entry(0, 21)
+    torch.cuda.synchronize()
+    assert entry_dev.cpu().tolist() == entry
+    _assert_state_equal(pool, st)
+    for slot in (2, 3):
+        sch.share_prefix(slot, entry_dev, 21)
+        assert st.share_prefix(slot, entry, 21) == OK
+        _assert_state_equal(pool, st)
+    # shared partial block: slots 2, 3 copy; slot 0 is past it
+    for _ in range(20):
+        batch = list(rng.permutation([0, 1, 2, 3]))
+        assert append(batch, 1) == OK
+    sch.release(1)
+    st.release(1)
+    _assert_state_equal(pool, st)
+    sch.drop_blocks(entry_dev)
+    st.drop_entry(entry)
+    _assert_state_equal(pool, st)
+    assert append([4, 1], 16) == OK
+    # capacity error: all-or-nothing
+    assert append([0, 4], 200) == -3
+    # exhaustion error: all-or-nothing
+    assert append([5], 8 * 16) == -4
+
+
+# --------------------------------------------------------------------- sampling
+def test_sample_talker_head_matches_oracle():
+    R, V = 64, 3072
+    g = _gen(30)
+    logits = torch.randn(R, V, generator=g)
+    counts = (torch.rand(R, V, generator=g) < 0.05).long() * torch.randint(1, 4, (R, V), generator=g)
+    gum = M.gumbel_from_uniform(torch.rand(R, 50, generator=g))
+    temp = torch.full((R, 1), 0.9)
+    pen = torch.full((R, 1), 1.05)
+    tok_ref, counts_ref = M.talker_sample(logits, counts, gum, temp, pen, eos_id=2150)
+    c_dev = counts.to(DEV)
+    tok = ops.sample(logits.to(DEV), 50, gumbel=gum.to(DEV), temperature=temp.to(DEV).view(-1),
+                     penalty=pen.to(DEV).view(-1), counts=c_dev, eos_id=2150)
+    assert torch.equal(tok.cpu(), tok_ref)
+    assert torch.equal(c_dev.cpu(), counts_ref)
+
+
+def test_sample_greedy_and_cp_select():
+    R, V = 64, 2048
+    g = _gen(31)
+    logits = torch.randn(R, V, generator=g)
+    gum = M.gumbel_from_uniform(torch.rand(R, 15, 50, generator=g))
+    temp = torch.full((R, 1), 0.9)
+    for s in (0, 7, 14):
+        ref = M.topk_select(logits, temp, gum[:, s], 50)
+        tok = ops.sample(logits.to(DEV), 50, gumbel=gum[:, s].contiguous().to(DEV), temperature=temp.view(-1).to(DEV))
+        assert torch.equal(tok.cpu(), ref)
+    zeros = torch.zeros(R, 50)
+    tok = ops.sample(logits.to(DEV), 50, gumbel=zeros.to(DEV))
+    assert torch.equal(tok.cpu(), logits.argmax(-1))
+
+
+def test_sample_philox_noise_is_deterministic_and_keyed():
+    R, V = 8, 2048
+    logits = torch.zeros(R, V, device=DEV)
+    key = torch.arange(R, dtype=torch.int64, device=DEV) * 7 + 3
+    a = ops.sample(logits, 50, seed=123, noise_key=key, step=5)
+    b = ops.sample(logits, 50, seed=123, noise_key=key, step=5)
+    c = ops.sample(logits, 50, seed=123, noise_key=key, step=6)
+    assert torch.equal(a, b)
+    assert not torch.equal(a, c)
+    assert int(a.min()) >= 0 and int(a.max()) < V
+
+
+# --------------------------------------------------------------------- small ops
+def test_rmsnorm_and_codec_sum():
+    H = 2048
+    x = torch.randn(64, H, generator=_gen(40)).to(DEV)
+    w = (1 + 0.1 * torch.randn(H, generator=_gen(41))).to(torch.bfloat16).to(DEV)
+    y = ops.rmsnorm(x, w, 1e-6)
+    torch.testing.assert_close(y.float(), M.rms_norm(x, w.float(), 1e-6), rtol=1e-2, atol=1e-2)
+    t0 = _rand((3072, H), 42, 0.02)
+    tc = _rand((15, 2048, H), 43, 0.02)
+    codes = torch.cat([torch.randint(0, 3072, (64, 1), generator=_gen(44)),
+                       torch.randint(0, 2048, (64, 15), generator=_gen(45))], 1).to(DEV)
+    text = torch.randn(64, H, generator=_gen(46)).to(DEV) * 0.02
+    cs, nx = ops.codec_sum(codes, t0, tc, text)
+    W = {"talker.codec_embedding.weight": t0.float().cpu()}
+    for s in range(15):
+        W[f"cp.codec_embedding.{s}.weight"] = tc[s].float().cpu()
+    ref = M.codec_sum(M.stacked_codec_table(W, 15), codes.cpu())
+    torch.testing.assert_close(cs.cpu(), ref, rtol=1e-4, atol=1e-5)
+    torch.testing.assert_close(nx.cpu(), (ref + text.cpu()).to(torch.bfloat16).float(), rtol=0, atol=0)
