@@ -85,7 +85,8 @@ int qtts_sched_append(const qtts_paged_state* st, const int32_t* slots, int n_ro
                       int32_t* cow_src, int32_t* cow_dst, int32_t* status, qtts_stream_t stream);
 
 /* Copy whole KV blocks for the (cow_src[i], cow_dst[i]) pairs with src >= 0.
- * kv_pool layout: [num_blocks][layers][2][kv_heads][block_size][head_dim] bf16. */
+ * kv_pool layout: [num_blocks][layers][2][kv_heads][block_size][head_dim] fp16 (same bytes as the
+ * reference's bf16 cache, 3 more mantissa bits; K is RMS-normalised, V bounded). */
 int qtts_kv_copy_blocks(void* kv_pool, size_t block_elems, int num_blocks, const int32_t* cow_src,
                         const int32_t* cow_dst, int n, qtts_stream_t stream);
 
@@ -104,10 +105,10 @@ int qtts_sched_drop_blocks(const qtts_paged_state* st, const int32_t* blocks, in
 int qtts_sched_release(const qtts_paged_state* st, int slot, qtts_stream_t stream);
 
 /* Write per-token K/V rows into the pool through slot_mapping (-1 skipped).
- * kv_rows: [n][layers*2][kv_heads][head_dim] bf16 (KVCachePool.scatter_prefill_kv layout). */
+ * kv_rows: [n][layers*2][kv_heads][head_dim] fp16 (KVCachePool.scatter_prefill_kv layout). */
 int qtts_kv_scatter(void* kv_pool, const qtts_paged_state* st, int layers, int kv_heads, int head_dim,
                     const void* kv_rows, const int32_t* slot_mapping, int n, qtts_stream_t stream);
-/* Logical KV of one slot: out [layers*2][kv_heads][n_tokens][head_dim] bf16
+/* Logical KV of one slot: out [layers*2][kv_heads][n_tokens][head_dim] fp16
  * (KVCachePool.gather_talker_kv, kv_cache_pool.py:410-420). */
 int qtts_kv_gather(const void* kv_pool, const qtts_paged_state* st, int layers, int kv_heads,
                    int head_dim, int slot, int n_tokens, void* out, qtts_stream_t stream);
@@ -133,23 +134,29 @@ typedef struct qtts_qkv_epilogue {
     int32_t max_pos;
     const int32_t* row_pos;      /* [M] RoPE position of each row */
     const int32_t* slot_mapping; /* [M] block*block_size+offset, -1 = do not store */
-    void* kv_pool;               /* [num_blocks][layers][2][kv_heads][block_size][head_dim] bf16 */
+    void* kv_pool;               /* [num_blocks][layers][2][kv_heads][block_size][head_dim] fp16 */
     int32_t layer, num_layers, block_size;
 } qtts_qkv_epilogue;
 
 /* X: [M,K] bf16 row-major, W: [N,K] bf16 row-major.  N % 128 == 0, K % 64 == 0.
- * out/resid per epilogue; bias may be NULL (bf16 [N]).  Uses a split-K cluster
- * reduction through distributed shared memory (no global workspace). */
-int qtts_gemm(const void* X, int M, int K, const void* W, int N, int epilogue, void* out,
-              const void* bias, const qtts_qkv_epilogue* qkv, qtts_stream_t stream);
+ * X_lo (optional, same shape): bf16 residual of the activation, X ~ X + X_lo; the kernel
+ * accumulates W·X + W·X_lo in one pass over the weights.  out/resid per epilogue
+ * (QKV_ROPE: q out is fp32 [M][num_heads*head_dim]); out_lo (optional, SwiGLU) receives
+ * the bf16 residual of the output.  bias may be NULL (bf16 [N]).  Split-K runs as a
+ * thread-block cluster reduced through distributed shared memory (no global workspace). */
+int qtts_gemm(const void* X, const void* X_lo, int M, int K, const void* W, int N, int epilogue,
+              void* out, void* out_lo, const void* bias, const qtts_qkv_epilogue* qkv,
+              qtts_stream_t stream);
 
-/* RMSNorm rows of fp32 x [M,H] (row stride ld) -> bf16 y [M,H]  (Qwen3RMSNorm). */
-int qtts_rmsnorm(const float* x, int M, int H, int ld, const void* w, float eps, void* y,
+/* RMSNorm rows of fp32 x [M,H] (row stride ld) -> bf16 y [M,H]  (Qwen3RMSNorm);
+ * y_lo (optional) receives bf16(y_exact - y), the lo half of a GEMM operand. */
+int qtts_rmsnorm(const float* x, int M, int H, int ld, const void* w, float eps, void* y, void* y_lo,
                  qtts_stream_t stream);
 
 /* Paged GQA attention for R query rows (decode: one row per stream; chunked prefill:
- * one row per new token).  q: [R][num_heads][head_dim] bf16, row_slot[R] selects the
- * block table row, row_ctx[R] keys visible to the row.  out: [R][num_heads*head_dim] bf16.
+ * one row per new token).  q: [R][num_heads][head_dim] fp32, row_slot[R] selects the
+ * block table row, row_ctx[R] keys visible to the row.  out: [R][num_heads*head_dim] bf16,
+ * out_lo (optional): its bf16 residual (lo half of the next GEMM's operand).
  * Scratch: partial results for the split-KV reduction, allocated by the caller:
  * ws_o [R*num_heads*max_splits*head_dim] fp32, ws_ml [R*num_heads*max_splits*2] fp32,
  * with max_splits = ceil(max_ctx / (16*QTTS_ATTN_SPLIT_BLOCKS)).
@@ -159,7 +166,7 @@ int qtts_paged_attention(const void* q, int R, int num_heads, int kv_heads, int 
                          const void* kv_pool, int layer, int num_layers, int block_size, int num_blocks,
                          const int32_t* block_table, int max_blocks_per_seq,
                          const int32_t* row_slot, const int32_t* row_ctx, int max_ctx,
-                         float* ws_o, float* ws_ml, void* out, qtts_stream_t stream);
+                         float* ws_o, float* ws_ml, void* out, void* out_lo, qtts_stream_t stream);
 
 /* Top-k / temperature / Gumbel-max sampling of fp32 logits [R][V] (row stride ld).
  * Talker head (talker_unified_modules.py:373-388) when counts != NULL: suppress
@@ -279,9 +286,10 @@ typedef struct qtts_step_io {
      * (engine/backend/debug_dump.py:112-175), they exist to compare intermediate tensors. */
     const int64_t* force_codes;
     float* cp_logits_out;
+    int32_t launches;   /* out (host): kernels this call enqueued */
 } qtts_step_io;
 
-int qtts_engine_step(qtts_engine* e, const qtts_step_io* io, qtts_stream_t stream);
+int qtts_engine_step(qtts_engine* e, qtts_step_io* io, qtts_stream_t stream);
 
 #ifdef __cplusplus
 }

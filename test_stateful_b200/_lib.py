@@ -71,7 +71,7 @@ class StepIO(C.Structure):
                 ("cp_gumbel", P), ("noise_seed", C.c_uint64), ("noise_key", P), ("noise_step", P), ("step", I32),
                 ("temperature", P), ("penalty", P), ("sample", I32), ("text_add", P), ("hidden_out", P),
                 ("logits_out", P), ("full_codec_out", P), ("codec_sum_out", P), ("next_x_out", P), ("status", P),
-                ("force_codes", P), ("cp_logits_out", P)]
+                ("force_codes", P), ("cp_logits_out", P), ("launches", I32)]
 
 
 # every symbol the header declares, in header order
@@ -110,10 +110,10 @@ def load() -> C.CDLL:
         "qtts_sched_release": ([C.POINTER(PagedState), C.c_int, P], C.c_int),
         "qtts_kv_scatter": ([P, C.POINTER(PagedState), C.c_int, C.c_int, C.c_int, P, P, C.c_int, P], C.c_int),
         "qtts_kv_gather": ([P, C.POINTER(PagedState), C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, P, P], C.c_int),
-        "qtts_gemm": ([P, C.c_int, C.c_int, P, C.c_int, C.c_int, P, P, C.POINTER(QkvEpilogue), P], C.c_int),
-        "qtts_rmsnorm": ([P, C.c_int, C.c_int, C.c_int, P, C.c_float, P, P], C.c_int),
+        "qtts_gemm": ([P, P, C.c_int, C.c_int, P, C.c_int, C.c_int, P, P, P, C.POINTER(QkvEpilogue), P], C.c_int),
+        "qtts_rmsnorm": ([P, C.c_int, C.c_int, C.c_int, P, C.c_float, P, P, P], C.c_int),
         "qtts_paged_attention": ([P, C.c_int, C.c_int, C.c_int, C.c_int, P, C.c_int, C.c_int, C.c_int, C.c_int,
-                                  P, C.c_int, P, P, C.c_int, P, P, P, P], C.c_int),
+                                  P, C.c_int, P, P, C.c_int, P, P, P, P, P], C.c_int),
         "qtts_sample": ([P, C.c_int, C.c_int, C.c_int, C.c_int, P, C.c_int, C.c_uint64, P, C.c_int, P, P, P,
                          C.c_int, P, C.c_int, P], C.c_int),
         "qtts_codec_sum": ([P, C.c_int, C.c_int, P, C.c_int, P, C.c_int, C.c_int, P, P, P, P], C.c_int),

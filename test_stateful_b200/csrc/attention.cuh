@@ -26,8 +26,8 @@
 namespace qtts {
 
 struct AttnParams {
-    const __nv_bfloat16* q;
-    const __nv_bfloat16* kv;
+    const float* q;  // [R][num_heads][D] fp32
+    const kv_t* kv;
     int num_heads, kv_heads;
     int layer, num_layers, block_size, num_blocks;
     const int32_t* block_table;
@@ -39,6 +39,7 @@ struct AttnParams {
     float* ws_o;
     float* ws_ml;
     __nv_bfloat16* out;
+    __nv_bfloat16* out_lo;  // bf16 residual of the output (hi/lo GEMM operand), or NULL
     int R;
 };
 
@@ -53,21 +54,21 @@ struct AttnLayout {
 };
 
 template <int D>
-__device__ __forceinline__ void load_row(const __nv_bfloat16* base, int lane, float (&v)[D / 32]) {
+__device__ __forceinline__ void load_row(const kv_t* base, int lane, float (&v)[D / 32]) {
     if constexpr (D == 128) {
         const uint2 raw = *reinterpret_cast<const uint2*>(base + lane * 4);
-        const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
-        const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
-        v[0] = __low2float(a);
-        v[1] = __high2float(a);
-        v[2] = __low2float(b);
-        v[3] = __high2float(b);
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+        v[0] = a.x;
+        v[1] = a.y;
+        v[2] = b.x;
+        v[3] = b.y;
     } else if constexpr (D == 64) {
-        const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(base + lane * 2);
-        v[0] = __low2float(a);
-        v[1] = __high2float(a);
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(base + lane * 2));
+        v[0] = a.x;
+        v[1] = a.y;
     } else {
-        v[0] = __bfloat162float(base[lane]);
+        v[0] = __half2float(base[lane]);
     }
 }
 
@@ -91,13 +92,11 @@ __global__ void __launch_bounds__(128) paged_attn_kernel(const AttnParams p) {
     // q for the two heads of this kv group, pre-scaled into the log2 domain
     float q0[DPL], q1[DPL];
     {
-        const __nv_bfloat16* qb = p.q + ((size_t)r * p.num_heads + g * 2) * D;
-        load_row<D>(qb, lane, q0);
-        load_row<D>(qb + D, lane, q1);
+        const float* qb = p.q + ((size_t)r * p.num_heads + g * 2) * D;
 #pragma unroll
         for (int j = 0; j < DPL; ++j) {
-            q0[j] *= p.scale_log2;
-            q1[j] *= p.scale_log2;
+            q0[j] = qb[lane * DPL + j] * p.scale_log2;
+            q1[j] = qb[D + lane * DPL + j] * p.scale_log2;
         }
     }
 
@@ -118,9 +117,9 @@ __global__ void __launch_bounds__(128) paged_attn_kernel(const AttnParams p) {
             record_error(DEV_ERR_ATTN_WAIT);
             blk = 0;  // stay in bounds; the error word reports the bad table entry
         }
-        const __nv_bfloat16* kp =
+        const kv_t* kp =
             p.kv + ((((size_t)blk * p.num_layers + p.layer) * 2 + 0) * p.kv_heads + g) * head_stride;
-        const __nv_bfloat16* vp = kp + (size_t)p.kv_heads * head_stride;
+        const kv_t* vp = kp + (size_t)p.kv_heads * head_stride;
         uint8_t* dst = wbuf + s * L::STAGE;
         mbar_arrive_expect_tx(&wbar[s], L::STAGE);
         bulk_load(dst, kp, L::CHUNK, &wbar[s]);
@@ -147,8 +146,8 @@ __global__ void __launch_bounds__(128) paged_attn_kernel(const AttnParams p) {
             failed = true;
             break;
         }
-        const __nv_bfloat16* Kb = reinterpret_cast<const __nv_bfloat16*>(wbuf + s * L::STAGE);
-        const __nv_bfloat16* Vb = Kb + 16 * D;
+        const kv_t* Kb = reinterpret_cast<const kv_t*>(wbuf + s * L::STAGE);
+        const kv_t* Vb = Kb + 16 * D;
         const int jb = b_start + warp + 4 * i;
 
         // ---- scores: partials for 32 (head, token) pairs, then reduce-scatter
@@ -284,7 +283,10 @@ __global__ void attn_combine_kernel(const AttnParams p) {
         acc += p.ws_o[(hrow * p.max_splits + s) * D + d] * f;
         lsum += p.ws_ml[(hrow * p.max_splits + s) * 2 + 1] * f;
     }
-    p.out[hrow * D + d] = __float2bfloat16(lsum > 0.f ? acc / lsum : 0.f);
+    const float o = lsum > 0.f ? acc / lsum : 0.f;
+    const __nv_bfloat16 hi = __float2bfloat16(o);
+    p.out[hrow * D + d] = hi;
+    if (p.out_lo) p.out_lo[hrow * D + d] = __float2bfloat16(o - __bfloat162float(hi));
 }
 
 inline int attn_max_splits(int max_ctx) {
@@ -305,6 +307,7 @@ inline int launch_attention_d(const AttnParams& p, cudaStream_t st) {
     QTTS_LAUNCH_CHECK();
     attn_combine_kernel<D><<<dim3(p.R, p.num_heads), D, 0, st>>>(p);
     QTTS_LAUNCH_CHECK();
+    g_launch_count += 2;
     return QTTS_OK;
 }
 

@@ -5,6 +5,7 @@
 
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -269,6 +270,13 @@ __device__ __forceinline__ float4 ld_dsmem_f32x4(uint32_t addr) {
 // ----------------------------------------------------------------------------
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16(x)); }
 
+// KV cache element: fp16.  Same two bytes as the reference's bf16 cache, three
+// more mantissa bits; K is RMS-normalised per head and V is a bounded linear
+// map of a normalised input, so values sit far inside fp16 range (stores
+// saturate at +-65504 all the same).
+using kv_t = __half;
+__device__ __forceinline__ kv_t to_kv(float x) { return __float2half_rn(fminf(fmaxf(x, -65504.f), 65504.f)); }
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -282,6 +290,9 @@ __device__ __forceinline__ float warp_max(float v) {
 }
 
 inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
+
+// kernels enqueued by this host thread (the engine reports it per step)
+inline thread_local int g_launch_count = 0;
 
 inline int num_sms() {
     static int n = 0;

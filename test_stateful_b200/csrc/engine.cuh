@@ -47,26 +47,27 @@ struct qtts_engine {
     int qkv_rows, cp_qkv_rows;
     int max_splits, cp_max_splits;
     // talker activations
+    // GEMM operands are hi/lo bf16 pairs (x_lo = bf16(x - x_hi)), see gemm_tc.cuh
     float* x = nullptr;              // [rmax][H] fp32 residual stream
-    __nv_bfloat16* xn = nullptr;     // [rmax][max(H, I)] GEMM input (normed x / SwiGLU act)
-    __nv_bfloat16* qbuf = nullptr;   // [rmax][Hq*D]
-    __nv_bfloat16* attn = nullptr;   // [rmax][Hq*D]
-    __nv_bfloat16* act = nullptr;    // [rmax][I]
-    __nv_bfloat16* hid = nullptr;    // [bmax][H] final-normed last token
+    __nv_bfloat16 *xn = nullptr, *xn_lo = nullptr;      // [rmax][H] normed x
+    float* qbuf = nullptr;                              // [rmax][Hq*D] fp32 q after norm + RoPE
+    __nv_bfloat16 *attn = nullptr, *attn_lo = nullptr;  // [rmax][Hq*D]
+    __nv_bfloat16 *act = nullptr, *act_lo = nullptr;    // [rmax][I] SwiGLU output
+    __nv_bfloat16 *hid = nullptr, *hid_lo = nullptr;    // [bmax][H] final-normed last token
     float* ws_o = nullptr;
     float* ws_ml = nullptr;
     int32_t *mapping = nullptr, *row_ctx = nullptr, *row_pos = nullptr, *row_slot = nullptr;
     int32_t *cow_src = nullptr, *cow_dst = nullptr;
     // code predictor
-    __nv_bfloat16* cp_in = nullptr;  // [2*bmax][H]
-    float* cx = nullptr;             // [2*bmax][cpH]
-    __nv_bfloat16* cxn = nullptr;    // [2*bmax][max(cpH, cpI)]
-    __nv_bfloat16* cq = nullptr;
-    __nv_bfloat16* cattn = nullptr;
-    __nv_bfloat16* cact = nullptr;
-    __nv_bfloat16* chid = nullptr;   // [bmax][cpH]
+    __nv_bfloat16 *cp_in = nullptr, *cp_in_lo = nullptr;  // [2*bmax][H]
+    float* cx = nullptr;                                  // [2*bmax][cpH]
+    __nv_bfloat16 *cxn = nullptr, *cxn_lo = nullptr;      // [2*bmax][cpH]
+    float* cq = nullptr;
+    __nv_bfloat16 *cattn = nullptr, *cattn_lo = nullptr;
+    __nv_bfloat16 *cact = nullptr, *cact_lo = nullptr;
+    __nv_bfloat16 *chid = nullptr, *chid_lo = nullptr;    // [bmax][cpH]
     float* clogits = nullptr;        // [bmax][cp_vocab]
-    __nv_bfloat16* cp_kv = nullptr;  // [bmax][cpL][2][cpHkv][16][cpD]
+    qtts::kv_t* cp_kv = nullptr;           // [bmax][cpL][2][cpHkv][16][cpD]
     float* cws_o = nullptr;
     float* cws_ml = nullptr;
     int32_t* cp_meta = nullptr;      // per stage: mapping, pos, ctx, slot  [stages][4][2*bmax]
@@ -108,13 +109,16 @@ inline int engine_build(qtts_engine* e) {
     const int max_ctx = d.pool.max_blocks_per_seq * d.pool.block_size;
     e->max_splits = attn_max_splits(max_ctx);
     const int rmax = e->rmax, bmax = e->bmax;
-    const int wide = H > I ? H : I;
     QTTS_TRY(dev_alloc(e, &e->x, (size_t)rmax * H));
-    QTTS_TRY(dev_alloc(e, &e->xn, (size_t)rmax * wide));
+    QTTS_TRY(dev_alloc(e, &e->xn, (size_t)rmax * H));
+    QTTS_TRY(dev_alloc(e, &e->xn_lo, (size_t)rmax * H));
     QTTS_TRY(dev_alloc(e, &e->qbuf, (size_t)rmax * Hq * D));
     QTTS_TRY(dev_alloc(e, &e->attn, (size_t)rmax * Hq * D));
+    QTTS_TRY(dev_alloc(e, &e->attn_lo, (size_t)rmax * Hq * D));
     QTTS_TRY(dev_alloc(e, &e->act, (size_t)rmax * I));
+    QTTS_TRY(dev_alloc(e, &e->act_lo, (size_t)rmax * I));
     QTTS_TRY(dev_alloc(e, &e->hid, (size_t)bmax * H));
+    QTTS_TRY(dev_alloc(e, &e->hid_lo, (size_t)bmax * H));
     QTTS_TRY(dev_alloc(e, &e->ws_o, (size_t)rmax * Hq * e->max_splits * D));
     QTTS_TRY(dev_alloc(e, &e->ws_ml, (size_t)rmax * Hq * e->max_splits * 2));
     QTTS_TRY(dev_alloc(e, &e->mapping, (size_t)rmax));
@@ -145,13 +149,13 @@ inline int engine_build(qtts_engine* e) {
         q.num_layers = d.layers;
         q.block_size = d.pool.block_size;
         QTTS_TRY(gemm_plan(&g.qkv, e->xn, rmax, H, bf(d.w_qkv, (size_t)l * e->qkv_rows * H), e->qkv_rows,
-                           QTTS_EPI_QKV_ROPE, e->qbuf, nullptr, &q));
+                           QTTS_EPI_QKV_ROPE, e->qbuf, nullptr, &q, e->xn_lo));
         QTTS_TRY(gemm_plan(&g.o, e->attn, rmax, Hq * D, bf(d.w_o, (size_t)l * H * Hq * D), H, QTTS_EPI_RESIDUAL,
-                           e->x, nullptr, nullptr));
+                           e->x, nullptr, nullptr, e->attn_lo));
         QTTS_TRY(gemm_plan(&g.gu, e->xn, rmax, H, bf(d.w_gate_up, (size_t)l * 2 * I * H), 2 * I, QTTS_EPI_SWIGLU,
-                           e->act, nullptr, nullptr));
+                           e->act, nullptr, nullptr, e->xn_lo, e->act_lo));
         QTTS_TRY(gemm_plan(&g.down, e->act, rmax, I, bf(d.w_down, (size_t)l * H * I), H, QTTS_EPI_RESIDUAL, e->x,
-                           nullptr, nullptr));
+                           nullptr, nullptr, e->act_lo));
     }
     QTTS_TRY(dev_alloc(e, &e->cp_table, (size_t)bmax));
     // ---- code predictor
@@ -160,14 +164,18 @@ inline int engine_build(qtts_engine* e) {
     e->cp_qkv_rows = (cHq + 2 * cHkv) * cD;
     e->cp_max_splits = 1;
     const int crows = 2 * bmax;
-    const int cwide = cH > cI ? cH : cI;
     QTTS_TRY(dev_alloc(e, &e->cp_in, (size_t)crows * H));
+    QTTS_TRY(dev_alloc(e, &e->cp_in_lo, (size_t)crows * H));
     QTTS_TRY(dev_alloc(e, &e->cx, (size_t)crows * cH));
-    QTTS_TRY(dev_alloc(e, &e->cxn, (size_t)crows * cwide));
+    QTTS_TRY(dev_alloc(e, &e->cxn, (size_t)crows * cH));
+    QTTS_TRY(dev_alloc(e, &e->cxn_lo, (size_t)crows * cH));
     QTTS_TRY(dev_alloc(e, &e->cq, (size_t)crows * cHq * cD));
     QTTS_TRY(dev_alloc(e, &e->cattn, (size_t)crows * cHq * cD));
+    QTTS_TRY(dev_alloc(e, &e->cattn_lo, (size_t)crows * cHq * cD));
     QTTS_TRY(dev_alloc(e, &e->cact, (size_t)crows * cI));
+    QTTS_TRY(dev_alloc(e, &e->cact_lo, (size_t)crows * cI));
     QTTS_TRY(dev_alloc(e, &e->chid, (size_t)bmax * cH));
+    QTTS_TRY(dev_alloc(e, &e->chid_lo, (size_t)bmax * cH));
     QTTS_TRY(dev_alloc(e, &e->clogits, (size_t)bmax * d.cp_vocab));
     QTTS_TRY(dev_alloc(e, &e->cp_kv, (size_t)bmax * d.cp_layers * 2 * cHkv * 16 * cD));
     QTTS_TRY(dev_alloc(e, &e->cws_o, (size_t)crows * cHq * cD));
@@ -221,21 +229,25 @@ inline int engine_build(qtts_engine* e) {
         q.num_layers = d.cp_layers;
         q.block_size = 16;
         QTTS_TRY(gemm_plan(&g.qkv, e->cxn, crows, cH, bf(d.cp_w_qkv, (size_t)l * e->cp_qkv_rows * cH),
-                           e->cp_qkv_rows, QTTS_EPI_QKV_ROPE, e->cq, nullptr, &q, bmax));
+                           e->cp_qkv_rows, QTTS_EPI_QKV_ROPE, e->cq, nullptr, &q, e->cxn_lo));
         QTTS_TRY(gemm_plan(&g.o, e->cattn, crows, cHq * cD, bf(d.cp_w_o, (size_t)l * cH * cHq * cD), cH,
-                           QTTS_EPI_RESIDUAL, e->cx, nullptr, nullptr, bmax));
+                           QTTS_EPI_RESIDUAL, e->cx, nullptr, nullptr, e->cattn_lo));
         QTTS_TRY(gemm_plan(&g.gu, e->cxn, crows, cH, bf(d.cp_w_gate_up, (size_t)l * 2 * cI * cH), 2 * cI,
-                           QTTS_EPI_SWIGLU, e->cact, nullptr, nullptr, bmax));
+                           QTTS_EPI_SWIGLU, e->cact, nullptr, nullptr, e->cxn_lo, e->cact_lo));
         QTTS_TRY(gemm_plan(&g.down, e->cact, crows, cI, bf(d.cp_w_down, (size_t)l * cH * cI), cH, QTTS_EPI_RESIDUAL,
-                           e->cx, nullptr, nullptr, bmax));
+                           e->cx, nullptr, nullptr, e->cact_lo));
     }
+    // stage 0 projects [talker hidden (hi/lo), codec embedding]; later stages only embeddings (exact in bf16)
     QTTS_TRY(gemm_plan(&e->cp_proj_pair, e->cp_in, crows, H, d.cp_w_proj, cH, QTTS_EPI_F32, e->cx, d.cp_b_proj,
-                       nullptr, bmax));
+                       nullptr, e->cp_in_lo));
+    QTTS_TRY(gemm_plan(&e->cp_proj_one, e->cp_in, crows, H, d.cp_w_proj, cH, QTTS_EPI_F32, e->cx, d.cp_b_proj,
+                       nullptr));
     e->cp_heads.resize(S);
     for (int s = 0; s < S; ++s)
         QTTS_TRY(gemm_plan(&e->cp_heads[s], e->chid, bmax, cH, bf(d.cp_w_lm_head, (size_t)s * d.cp_vocab * cH),
-                           d.cp_vocab, QTTS_EPI_F32, e->clogits, nullptr, nullptr));
-    QTTS_TRY(gemm_plan(&e->head, e->hid, bmax, H, d.w_codec_head, d.vocab, QTTS_EPI_F32, nullptr, nullptr, nullptr));
+                           d.cp_vocab, QTTS_EPI_F32, e->clogits, nullptr, nullptr, e->chid_lo));
+    QTTS_TRY(gemm_plan(&e->head, e->hid, bmax, H, d.w_codec_head, d.vocab, QTTS_EPI_F32, nullptr, nullptr, nullptr,
+                       e->hid_lo));
     return QTTS_OK;
 }
 
@@ -243,7 +255,7 @@ inline int run_plan(const GemmPlan& g, int M, cudaStream_t st, void* out = nullp
     return gemm_run(g, M, st, out);
 }
 
-inline int engine_step(qtts_engine* e, const qtts_step_io& io, cudaStream_t st) {
+inline int engine_step_impl(qtts_engine* e, const qtts_step_io& io, cudaStream_t st) {
     const qtts_model_desc& d = e->d;
     const int H = d.hidden, D = d.head_dim, Hq = d.heads, Hkv = d.kv_heads, I = d.inter;
     const int nr = io.n_rows, nn = io.n_new, R = nr * nn;
@@ -264,19 +276,23 @@ inline int engine_step(qtts_engine* e, const qtts_step_io& io, cudaStream_t st) 
     sched_append_kernel<<<1, kSchedThreads, 0, st>>>(sv, io.slots, nr, nn, e->mapping, e->row_ctx, e->row_pos,
                                                      e->cow_src, e->cow_dst, io.status);
     QTTS_LAUNCH_CHECK();
+    ++g_launch_count;
     const size_t block_elems = (size_t)d.layers * 2 * Hkv * d.pool.block_size * D;
     kv_copy_blocks_kernel<<<dim3(64, nr), 256, 0, st>>>(reinterpret_cast<uint4*>(d.kv_pool), block_elems / 8,
                                                         e->cow_src, e->cow_dst, d.pool.num_blocks);
     QTTS_LAUNCH_CHECK();
+    ++g_launch_count;
     expand_rows_kernel<<<ceil_div(R, 256), 256, 0, st>>>(io.slots, nr, nn, e->row_slot);
     QTTS_LAUNCH_CHECK();
+    ++g_launch_count;
     const int32_t* smap = io.slot_indexed ? io.slots : nullptr;
     load_x_kernel<<<ceil_div(R * H, 1024), 256, 0, st>>>(io.x_in, e->x, R, H, (io.slot_indexed && nn == 1) ? smap : nullptr);
     QTTS_LAUNCH_CHECK();
+    ++g_launch_count;
 
     AttnParams ap = {};
     ap.q = e->qbuf;
-    ap.kv = reinterpret_cast<const __nv_bfloat16*>(d.kv_pool);
+    ap.kv = reinterpret_cast<const kv_t*>(d.kv_pool);
     ap.num_heads = Hq;
     ap.kv_heads = Hkv;
     ap.num_layers = d.layers;
@@ -291,22 +307,24 @@ inline int engine_step(qtts_engine* e, const qtts_step_io& io, cudaStream_t st) 
     ap.ws_o = e->ws_o;
     ap.ws_ml = e->ws_ml;
     ap.out = e->attn;
+    ap.out_lo = e->attn_lo;
     ap.R = R;
 
     // ---- talker layers
     for (int l = 0; l < d.layers; ++l) {
         const LayerGemms& g = e->tg[l];
-        QTTS_TRY(launch_rmsnorm(e->x, R, H, H, bf(d.w_in_norm, (size_t)l * H), d.rms_eps, e->xn, st));
+        QTTS_TRY(launch_rmsnorm(e->x, R, H, H, bf(d.w_in_norm, (size_t)l * H), d.rms_eps, e->xn, st, e->xn_lo));
         QTTS_TRY(run_plan(g.qkv, R, st));
         ap.layer = l;
         QTTS_TRY(launch_attention(ap, D, st));
         QTTS_TRY(run_plan(g.o, R, st));
-        QTTS_TRY(launch_rmsnorm(e->x, R, H, H, bf(d.w_post_norm, (size_t)l * H), d.rms_eps, e->xn, st));
+        QTTS_TRY(launch_rmsnorm(e->x, R, H, H, bf(d.w_post_norm, (size_t)l * H), d.rms_eps, e->xn, st, e->xn_lo));
         QTTS_TRY(run_plan(g.gu, R, st));
         QTTS_TRY(run_plan(g.down, R, st));
     }
     // ---- final norm of each stream's last new token, codec head
-    QTTS_TRY(launch_rmsnorm(e->x + (size_t)(nn - 1) * H, nr, H, nn * H, d.w_final_norm, d.rms_eps, e->hid, st));
+    QTTS_TRY(launch_rmsnorm(e->x + (size_t)(nn - 1) * H, nr, H, nn * H, d.w_final_norm, d.rms_eps, e->hid, st,
+                            e->hid_lo));
     if (io.hidden_out)
         QTTS_CHECK_CUDA(cudaMemcpyAsync(io.hidden_out, e->hid, (size_t)nr * H * 2, cudaMemcpyDeviceToDevice, st));
     if (io.logits_out) QTTS_TRY(run_plan(e->head, nr, st, io.logits_out));
@@ -353,6 +371,7 @@ inline int engine_step(qtts_engine* e, const qtts_step_io& io, cudaStream_t st) 
     cap.ws_o = e->cws_o;
     cap.ws_ml = e->cws_ml;
     cap.out = e->cattn;
+    cap.out_lo = e->cattn_lo;
 
     // the tokens the next stage consumes: sampled, or forced by a parity test
     const int64_t* codes_in = io.force_codes ? io.force_codes : io.full_codec_out;
@@ -360,20 +379,22 @@ inline int engine_step(qtts_engine* e, const qtts_step_io& io, cudaStream_t st) 
         const int rows = s == 0 ? 2 * nr : nr;
         const int32_t* m = e->cp_meta + (size_t)s * 4 * crows;
         if (s == 0) {
-            cp_stage0_rows_kernel<<<nr, 128, 0, st>>>(e->hid, bf(d.w_codec_emb, 0), d.vocab, H, codes_in, G,
-                                                      e->cp_in);
+            cp_stage0_rows_kernel<<<nr, 128, 0, st>>>(e->hid, e->hid_lo, bf(d.w_codec_emb, 0), d.vocab, H, codes_in,
+                                                      G, e->cp_in, e->cp_in_lo);
         } else {
             gather_rows_kernel<<<nr, 128, 0, st>>>(bf(d.cp_w_codec_emb, (size_t)(s - 1) * d.cp_vocab * H),
                                                    d.cp_vocab, H, codes_in + s, G, e->cp_in, H);
         }
         QTTS_LAUNCH_CHECK();
-        QTTS_TRY(run_plan(e->cp_proj_pair, rows, st));
+        ++g_launch_count;
+        QTTS_TRY(run_plan(s == 0 ? e->cp_proj_pair : e->cp_proj_one, rows, st));
         cap.row_slot = m + 3 * crows;
         cap.row_ctx = m + 2 * crows;
         cap.R = rows;
         for (int l = 0; l < d.cp_layers; ++l) {
             const LayerGemms& g = e->cg[l];
-            QTTS_TRY(launch_rmsnorm(e->cx, rows, cH, cH, bf(d.cp_w_in_norm, (size_t)l * cH), d.cp_rms_eps, e->cxn, st));
+            QTTS_TRY(launch_rmsnorm(e->cx, rows, cH, cH, bf(d.cp_w_in_norm, (size_t)l * cH), d.cp_rms_eps, e->cxn, st,
+                                    e->cxn_lo));
             GemmPlan q = g.qkv;
             q.p.qkv.row_pos = m + crows;
             q.p.qkv.slot_mapping = m;
@@ -382,14 +403,14 @@ inline int engine_step(qtts_engine* e, const qtts_step_io& io, cudaStream_t st) 
             QTTS_TRY(launch_attention(cap, cD, st));
             QTTS_TRY(run_plan(g.o, rows, st));
             QTTS_TRY(launch_rmsnorm(e->cx, rows, cH, cH, bf(d.cp_w_post_norm, (size_t)l * cH), d.cp_rms_eps, e->cxn,
-                                    st));
+                                    st, e->cxn_lo));
             QTTS_TRY(run_plan(g.gu, rows, st));
             QTTS_TRY(run_plan(g.down, rows, st));
         }
         // last position of each stream: row 2b+1 at stage 0, row b afterwards
         const float* last = s == 0 ? e->cx + cH : e->cx;
         const int ld = s == 0 ? 2 * cH : cH;
-        QTTS_TRY(launch_rmsnorm(last, nr, cH, ld, d.cp_w_final_norm, d.cp_rms_eps, e->chid, st));
+        QTTS_TRY(launch_rmsnorm(last, nr, cH, ld, d.cp_w_final_norm, d.cp_rms_eps, e->chid, st, e->chid_lo));
         QTTS_TRY(run_plan(e->cp_heads[s], nr, st));
         SampleParams cs = {};
         cs.logits = e->clogits;
@@ -422,7 +443,15 @@ inline int engine_step(qtts_engine* e, const qtts_step_io& io, cudaStream_t st) 
                                                            bf(d.cp_w_codec_emb, 0), d.cp_vocab, H, io.text_add,
                                                            io.codec_sum_out, io.next_x_out, smap, io.noise_step);
     QTTS_LAUNCH_CHECK();
+    ++g_launch_count;
     return QTTS_OK;
+}
+
+inline int engine_step(qtts_engine* e, qtts_step_io& io, cudaStream_t st) {
+    g_launch_count = 0;
+    const int rc = engine_step_impl(e, io, st);
+    io.launches = g_launch_count;
+    return rc;
 }
 
 }  // namespace qtts

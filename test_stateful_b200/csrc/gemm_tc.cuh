@@ -10,6 +10,12 @@
 // reduces a slice of BN/splits tokens across the cluster — so there is no
 // global workspace and no atomics, and the result is deterministic.
 //
+// Activation precision: at decode the MMA pipe is idle (the kernel waits on
+// weight bytes), so an activation operand can be carried as a bf16 pair
+// hi + lo (hi = bf16(x), lo = bf16(x - hi)); the UMMA issuer then runs two
+// MMAs per k-slice on the same weight tile and TMEM accumulates W·hi + W·lo,
+// recovering ~16 mantissa bits of the fp32 activation for no extra HBM bytes.
+//
 // Roles in a 128-thread CTA: warp 0 lane 0 issues TMA loads into a STAGES-deep
 // ring (full/empty mbarriers), warp 1 lane 0 issues UMMAs and commits, warp 2
 // owns the TMEM allocation; all four warps run the epilogue (warp w reads TMEM
@@ -33,15 +39,16 @@ struct GemmParams {
     int splits;    // cluster size along grid.y
     int epilogue;
     void* out;
+    void* out_lo;  // SwiGLU: bf16 residual part of the output (hi/lo pair), or NULL
     const __nv_bfloat16* bias;
     qtts_qkv_epilogue qkv;
 };
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool SPLIT>
 struct GemmLayout {
     static constexpr int A_BYTES = 128 * 64 * 2;  // weight tile 128 rows x 64 k
-    static constexpr int B_BYTES = BN * 64 * 2;   // token tile BN rows x 64 k
-    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int B_BYTES = BN * 64 * 2;   // token tile BN rows x 64 k (hi, then lo when SPLIT)
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES * (SPLIT ? 2 : 1);
     static constexpr int PIPE_BYTES = STAGES * STAGE_BYTES;
     static constexpr int PART_BYTES = BN * 128 * 4;  // fp32 partial, [BN tokens][128 rows]
     static constexpr int BODY = PIPE_BYTES > PART_BYTES ? PIPE_BYTES : PART_BYTES;
@@ -88,8 +95,12 @@ __device__ void gemm_epilogue(const GemmParams& p, float* R, int m0, int per, in
                     if (m_g >= p.M) break;
                     const float g = R[(m0 + i) * 128 + t];
                     const float u = R[(m0 + i) * 128 + 64 + t];
-                    reinterpret_cast<__nv_bfloat16*>(p.out)[(size_t)m_g * half_n + tile_n * 64 + t] =
-                        __float2bfloat16(silu(g) * u);
+                    const float a = silu(g) * u;
+                    const size_t o = (size_t)m_g * half_n + tile_n * 64 + t;
+                    const __nv_bfloat16 hi = __float2bfloat16(a);
+                    reinterpret_cast<__nv_bfloat16*>(p.out)[o] = hi;
+                    if (p.out_lo)
+                        reinterpret_cast<__nv_bfloat16*>(p.out_lo)[o] = __float2bfloat16(a - __bfloat162float(hi));
                 }
             }
             break;
@@ -132,7 +143,7 @@ __device__ void gemm_epilogue(const GemmParams& p, float* R, int m0, int per, in
                     v = d < half ? v * c - partner * s : v * c + partner * s;
                 }
                 if (region == 0) {
-                    reinterpret_cast<__nv_bfloat16*>(p.out)[(size_t)m_g * q_rows + n_g] = __float2bfloat16(v);
+                    reinterpret_cast<float*>(p.out)[(size_t)m_g * q_rows + n_g] = v;  // q stays fp32
                 } else {
                     const int slot = e.slot_mapping[m_g];
                     if (slot >= 0) {
@@ -142,7 +153,7 @@ __device__ void gemm_epilogue(const GemmParams& p, float* R, int m0, int per, in
                             ((((size_t)blk * e.num_layers + e.layer) * 2 + (region - 1)) * e.kv_heads + g) *
                                 e.block_size +
                             off;
-                        reinterpret_cast<__nv_bfloat16*>(e.kv_pool)[idx * D + d] = __float2bfloat16(v);
+                        reinterpret_cast<kv_t*>(e.kv_pool)[idx * D + d] = to_kv(v);
                     }
                 }
                 __syncthreads();
@@ -157,11 +168,12 @@ __device__ void gemm_epilogue(const GemmParams& p, float* R, int m0, int per, in
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool SPLIT>
 __global__ void __launch_bounds__(128) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW,
                                                       const __grid_constant__ CUtensorMap tmX,
+                                                      const __grid_constant__ CUtensorMap tmXlo,
                                                       const GemmParams p) {
-    using L = GemmLayout<BN, STAGES>;
+    using L = GemmLayout<BN, STAGES, SPLIT>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     float* scratch = reinterpret_cast<float*>(smem + L::BODY);
@@ -190,6 +202,7 @@ __global__ void __launch_bounds__(128) gemm_tc_kernel(const __grid_constant__ CU
         fence_mbar_init();
         tma_prefetch_desc(&tmW);
         tma_prefetch_desc(&tmX);
+        if (SPLIT) tma_prefetch_desc(&tmXlo);
     }
     if (warp == 2) {
         tmem_alloc(tmem_slot, BN);
@@ -215,6 +228,7 @@ __global__ void __launch_bounds__(128) gemm_tc_kernel(const __grid_constant__ CU
             mbar_arrive_expect_tx(&full[s], L::STAGE_BYTES);
             tma_load_2d(a, &tmW, &full[s], (kb0 + i) * 64, tile_n * 128);
             tma_load_2d(b, &tmX, &full[s], (kb0 + i) * 64, tile_m * BN);
+            if (SPLIT) tma_load_2d(b + L::B_BYTES, &tmXlo, &full[s], (kb0 + i) * 64, tile_m * BN);
             ++issued;
         }
         flags[1] = issued;
@@ -233,9 +247,12 @@ __global__ void __launch_bounds__(128) gemm_tc_kernel(const __grid_constant__ CU
             const uint32_t a = smem_u32(smem + s * L::STAGE_BYTES);
             const uint64_t da = make_sw128_desc(a);
             const uint64_t db = make_sw128_desc(a + L::A_BYTES);
+            const uint64_t dl = make_sw128_desc(a + L::A_BYTES + L::B_BYTES);
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk)  // 4 x UMMA_K(16) = 64; +32 B per step inside the swizzle atom
+            for (int kk = 0; kk < 4; ++kk) {  // 4 x UMMA_K(16) = 64; +32 B per step inside the swizzle atom
                 umma_bf16(tmem, da + 2 * kk, db + 2 * kk, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+                if (SPLIT) umma_bf16(tmem, da + 2 * kk, dl + 2 * kk, idesc, 1u);
+            }
             umma_commit(&empty[s]);
             ++consumed;
         }
@@ -333,8 +350,6 @@ inline int make_map_bf16(CUtensorMap* map, const void* ptr, uint64_t rows, uint6
     return QTTS_OK;
 }
 
-constexpr int kGemmStages = 4;
-
 inline int pick_bn(int M) { return M <= 64 ? 64 : 128; }
 
 inline int pick_splits(int N, int M, int K, int BN) {
@@ -346,10 +361,11 @@ inline int pick_splits(int N, int M, int K, int BN) {
     return s;
 }
 
-template <int BN>
-inline int launch_gemm_bn(const CUtensorMap& mw, const CUtensorMap& mx, const GemmParams& p, cudaStream_t st) {
-    using L = GemmLayout<BN, kGemmStages>;
-    auto kern = gemm_tc_kernel<BN, kGemmStages>;
+template <int BN, int STAGES, bool SPLIT>
+inline int launch_gemm_t(const CUtensorMap& mw, const CUtensorMap& mx, const CUtensorMap& mxlo, const GemmParams& p,
+                         cudaStream_t st) {
+    using L = GemmLayout<BN, STAGES, SPLIT>;
+    auto kern = gemm_tc_kernel<BN, STAGES, SPLIT>;
     static bool attr_done = false;
     if (!attr_done) {
         QTTS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM));
@@ -367,19 +383,21 @@ inline int launch_gemm_bn(const CUtensorMap& mw, const CUtensorMap& mx, const Ge
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    QTTS_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, mw, mx, p));
+    QTTS_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, mw, mx, mxlo, p));
+    ++g_launch_count;
     return QTTS_OK;
 }
 
-// Prepared GEMM: tensor maps built once (two token-tile heights), reused every step.
+// Prepared GEMM: tensor maps built once (two token-tile heights, optional lo operand), reused every step.
 struct GemmPlan {
-    CUtensorMap mw, mx64, mx128;
+    CUtensorMap mw, mx64, mx128, mlo64, mlo128;
     GemmParams p;
+    bool split;
 };
 
 inline int gemm_plan(GemmPlan* g, const void* X, int rows, int K, const void* W, int N, int epilogue, void* out,
-                     const void* bias, const qtts_qkv_epilogue* qkv, int unused = -1) {
-    (void)unused;
+                     const void* bias, const qtts_qkv_epilogue* qkv, const void* X_lo = nullptr,
+                     void* out_lo = nullptr) {
     if (N % 128 != 0 || K % 64 != 0 || rows <= 0) {
         set_error("gemm: need N %% 128 == 0, K %% 64 == 0, rows > 0 (N=%d K=%d rows=%d)", N, K, rows);
         return QTTS_ERR_UNSUPPORTED;
@@ -394,6 +412,16 @@ inline int gemm_plan(GemmPlan* g, const void* X, int rows, int K, const void* W,
     if (rc) return rc;
     rc = make_map_bf16(&g->mx128, X, (uint64_t)rows, (uint64_t)K, 128);
     if (rc) return rc;
+    g->split = X_lo != nullptr;
+    if (g->split) {
+        rc = make_map_bf16(&g->mlo64, X_lo, (uint64_t)rows, (uint64_t)K, 64);
+        if (rc) return rc;
+        rc = make_map_bf16(&g->mlo128, X_lo, (uint64_t)rows, (uint64_t)K, 128);
+        if (rc) return rc;
+    } else {
+        g->mlo64 = g->mx64;
+        g->mlo128 = g->mx128;
+    }
     GemmParams& p = g->p;
     memset(&p, 0, sizeof(p));
     p.M = rows;
@@ -403,20 +431,25 @@ inline int gemm_plan(GemmPlan* g, const void* X, int rows, int K, const void* W,
     p.splits = 1;
     p.epilogue = epilogue;
     p.out = out;
+    p.out_lo = out_lo;
     p.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
     if (qkv) p.qkv = *qkv;
     return QTTS_OK;
 }
 
-// Launch on the first M rows of the plan's X buffer.
+// Launch on the first M rows of the plan's X buffer(s).
 inline int gemm_run(GemmPlan g, int M, cudaStream_t st, void* out = nullptr) {
     if (M <= 0) return QTTS_OK;
     const int bn = pick_bn(M);
     g.p.M = M;
     g.p.splits = pick_splits(g.p.N, M, g.p.K, bn);
     if (out) g.p.out = out;
-    if (bn == 64) return launch_gemm_bn<64>(g.mw, g.mx64, g.p, st);
-    return launch_gemm_bn<128>(g.mw, g.mx128, g.p, st);
+    if (g.split) {
+        if (bn == 64) return launch_gemm_t<64, 3, true>(g.mw, g.mx64, g.mlo64, g.p, st);
+        return launch_gemm_t<128, 3, true>(g.mw, g.mx128, g.mlo128, g.p, st);
+    }
+    if (bn == 64) return launch_gemm_t<64, 4, false>(g.mw, g.mx64, g.mx64, g.p, st);
+    return launch_gemm_t<128, 4, false>(g.mw, g.mx128, g.mx128, g.p, st);
 }
 
 }  // namespace qtts

@@ -121,8 +121,8 @@ int qtts_kv_scatter(void* kv_pool, const qtts_paged_state* st, int layers, int k
     QTTS_REQUIRE(kv_pool && state_ok(st) && kv_rows && slot_mapping && n >= 0, "kv_scatter: bad arguments");
     if (n == 0) return QTTS_OK;
     kv_scatter_kernel<<<n, 256, 0, (cudaStream_t)stream>>>(
-        reinterpret_cast<__nv_bfloat16*>(kv_pool), 2 * layers, kv_heads, head_dim, st->block_size, st->num_blocks,
-        reinterpret_cast<const __nv_bfloat16*>(kv_rows), slot_mapping);
+        reinterpret_cast<kv_t*>(kv_pool), 2 * layers, kv_heads, head_dim, st->block_size, st->num_blocks,
+        reinterpret_cast<const kv_t*>(kv_rows), slot_mapping);
     QTTS_LAUNCH_CHECK();
     return QTTS_OK;
 }
@@ -134,34 +134,35 @@ int qtts_kv_gather(const void* kv_pool, const qtts_paged_state* st, int layers, 
                  "kv_gather: bad arguments");
     if (n_tokens == 0) return QTTS_OK;
     kv_gather_kernel<<<n_tokens, 256, 0, (cudaStream_t)stream>>>(
-        reinterpret_cast<const __nv_bfloat16*>(kv_pool), 2 * layers, kv_heads, head_dim, st->block_size,
+        reinterpret_cast<const kv_t*>(kv_pool), 2 * layers, kv_heads, head_dim, st->block_size,
         st->num_blocks, st->block_table + (size_t)slot * st->max_blocks_per_seq, n_tokens,
-        reinterpret_cast<__nv_bfloat16*>(out));
+        reinterpret_cast<kv_t*>(out));
     QTTS_LAUNCH_CHECK();
     return QTTS_OK;
 }
 
 // ---------------------------------------------------------------- kernels
-int qtts_gemm(const void* X, int M, int K, const void* W, int N, int epilogue, void* out, const void* bias,
-              const qtts_qkv_epilogue* qkv, qtts_stream_t stream) {
+int qtts_gemm(const void* X, const void* X_lo, int M, int K, const void* W, int N, int epilogue, void* out,
+              void* out_lo, const void* bias, const qtts_qkv_epilogue* qkv, qtts_stream_t stream) {
     QTTS_REQUIRE(X && W && out && M > 0, "gemm: null pointer or M <= 0");
     QTTS_REQUIRE(epilogue >= QTTS_EPI_BF16 && epilogue <= QTTS_EPI_QKV_ROPE, "gemm: unknown epilogue %d", epilogue);
     QTTS_REQUIRE(epilogue != QTTS_EPI_SWIGLU || N % 256 == 0 || N == 128, "gemm: SwiGLU needs N %% 128 == 0");
     GemmPlan g;
-    int rc = gemm_plan(&g, X, M, K, W, N, epilogue, out, bias, qkv);
+    int rc = gemm_plan(&g, X, M, K, W, N, epilogue, out, bias, qkv, X_lo, out_lo);
     if (rc) return rc;
     return gemm_run(g, M, (cudaStream_t)stream);
 }
 
-int qtts_rmsnorm(const float* x, int M, int H, int ld, const void* w, float eps, void* y, qtts_stream_t stream) {
+int qtts_rmsnorm(const float* x, int M, int H, int ld, const void* w, float eps, void* y, void* y_lo,
+                 qtts_stream_t stream) {
     QTTS_REQUIRE(x && w && y && M >= 0 && H > 0 && ld >= H, "rmsnorm: bad arguments");
-    return launch_rmsnorm(x, M, H, ld, w, eps, y, (cudaStream_t)stream);
+    return launch_rmsnorm(x, M, H, ld, w, eps, y, (cudaStream_t)stream, y_lo);
 }
 
 int qtts_paged_attention(const void* q, int R, int num_heads, int kv_heads, int head_dim, const void* kv_pool,
                          int layer, int num_layers, int block_size, int num_blocks, const int32_t* block_table,
                          int max_blocks_per_seq, const int32_t* row_slot, const int32_t* row_ctx, int max_ctx,
-                         float* ws_o, float* ws_ml, void* out, qtts_stream_t stream) {
+                         float* ws_o, float* ws_ml, void* out, void* out_lo, qtts_stream_t stream) {
     QTTS_REQUIRE(q && kv_pool && block_table && row_slot && row_ctx && ws_o && ws_ml && out && R >= 0,
                  "paged_attention: null pointer");
     QTTS_REQUIRE(block_size == 16, "paged_attention: block_size must be 16");
@@ -169,8 +170,8 @@ int qtts_paged_attention(const void* q, int R, int num_heads, int kv_heads, int 
     QTTS_REQUIRE(layer >= 0 && layer < num_layers && max_ctx > 0 && max_ctx <= max_blocks_per_seq * block_size,
                  "paged_attention: layer / max_ctx out of range");
     AttnParams p = {};
-    p.q = reinterpret_cast<const __nv_bfloat16*>(q);
-    p.kv = reinterpret_cast<const __nv_bfloat16*>(kv_pool);
+    p.q = reinterpret_cast<const float*>(q);
+    p.kv = reinterpret_cast<const kv_t*>(kv_pool);
     p.num_heads = num_heads;
     p.kv_heads = kv_heads;
     p.layer = layer;
@@ -186,6 +187,7 @@ int qtts_paged_attention(const void* q, int R, int num_heads, int kv_heads, int 
     p.ws_o = ws_o;
     p.ws_ml = ws_ml;
     p.out = reinterpret_cast<__nv_bfloat16*>(out);
+    p.out_lo = reinterpret_cast<__nv_bfloat16*>(out_lo);
     p.R = R;
     return launch_attention(p, head_dim, (cudaStream_t)stream);
 }
@@ -243,7 +245,7 @@ int qtts_engine_destroy(qtts_engine* e) {
     return QTTS_OK;
 }
 
-int qtts_engine_step(qtts_engine* e, const qtts_step_io* io, qtts_stream_t stream) {
+int qtts_engine_step(qtts_engine* e, qtts_step_io* io, qtts_stream_t stream) {
     QTTS_REQUIRE(e && io, "engine_step: null argument");
     return engine_step(e, *io, (cudaStream_t)stream);
 }

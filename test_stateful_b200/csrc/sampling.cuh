@@ -130,19 +130,46 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
         mask |= 255u << shift;
         __syncthreads();
     }
-    // gather candidates: all keys > prefix, and ties (== prefix) while room remains
+    // gather candidates: every key > prefix (fewer than topk; their order is fixed by the sort
+    // below), then the lowest-index keys == prefix until topk are taken, in index order, so the
+    // selection is deterministic when values tie
     if (tid == 0) s_ncand = 0;
     __syncthreads();
 #pragma unroll
     for (int i = 0; i < kSampleMaxPer; ++i) {
         const int idx = tid + i * kSampleThreads;
-        if (idx < p.V && key[i] >= prefix) {
+        if (idx < p.V && key[i] > prefix) {
             const int slot = atomicAdd(&s_ncand, 1);
-            if (slot < kSampleCand) {
-                c_val[slot] = val[i];
-                c_idx[slot] = idx;
-            }
+            c_val[slot] = val[i];
+            c_idx[slot] = idx;
         }
+    }
+    __syncthreads();
+    {
+        __shared__ int s_wcnt[kSampleThreads / 32];
+        const int lane = tid & 31, wid = tid >> 5;
+        int base = s_ncand;
+#pragma unroll 1
+        for (int i = 0; i < kSampleMaxPer && base < p.topk; ++i) {
+            const int idx = tid + i * kSampleThreads;  // indices of round i are consecutive across threads
+            const bool tie = idx < p.V && key[i] == prefix;
+            const unsigned b = __ballot_sync(0xffffffffu, tie);
+            if (lane == 0) s_wcnt[wid] = __popc(b);
+            __syncthreads();
+            int off = 0, total = 0;
+            for (int w = 0; w < kSampleThreads / 32; ++w) {
+                off += w < wid ? s_wcnt[w] : 0;
+                total += s_wcnt[w];
+            }
+            const int pos = base + off + __popc(b & ((1u << lane) - 1u));
+            if (tie && pos < p.topk) {
+                c_val[pos] = val[i];
+                c_idx[pos] = idx;
+            }
+            base += total;
+            __syncthreads();
+        }
+        if (tid == 0) s_ncand = min(base, p.topk);
     }
     __syncthreads();
     if (tid < 32) {
@@ -224,6 +251,7 @@ inline int launch_sample(const SampleParams& p, cudaStream_t st) {
     }
     sample_kernel<<<p.R, kSampleThreads, 0, st>>>(p);
     QTTS_LAUNCH_CHECK();
+    ++g_launch_count;
     return QTTS_OK;
 }
 

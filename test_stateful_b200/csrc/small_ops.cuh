@@ -8,11 +8,29 @@
 namespace qtts {
 
 // ---------------------------------------------------------------------------
-// RMSNorm (Qwen3RMSNorm): y = w * x * rsqrt(mean(x^2) + eps), fp32 in, bf16 out
+// RMSNorm (Qwen3RMSNorm): y = w * x * rsqrt(mean(x^2) + eps), fp32 in, bf16 out.
+// With y_lo, the bf16 residual y - bf16(y) is stored too (the hi/lo operand of
+// the tcgen05 GEMM).
 // ---------------------------------------------------------------------------
+__device__ __forceinline__ void store_hilo4(__nv_bfloat16* hi, __nv_bfloat16* lo, float a, float b, float c, float d) {
+    __nv_bfloat162 h01 = __floats2bfloat162_rn(a, b);
+    __nv_bfloat162 h23 = __floats2bfloat162_rn(c, d);
+    uint2 pack;
+    pack.x = *reinterpret_cast<uint32_t*>(&h01);
+    pack.y = *reinterpret_cast<uint32_t*>(&h23);
+    *reinterpret_cast<uint2*>(hi) = pack;
+    if (lo) {
+        __nv_bfloat162 l01 = __floats2bfloat162_rn(a - __low2float(h01), b - __high2float(h01));
+        __nv_bfloat162 l23 = __floats2bfloat162_rn(c - __low2float(h23), d - __high2float(h23));
+        pack.x = *reinterpret_cast<uint32_t*>(&l01);
+        pack.y = *reinterpret_cast<uint32_t*>(&l23);
+        *reinterpret_cast<uint2*>(lo) = pack;
+    }
+}
+
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const float* __restrict__ x, int H, int ld,
                                                       const __nv_bfloat16* __restrict__ w, float eps,
-                                                      __nv_bfloat16* __restrict__ y) {
+                                                      __nv_bfloat16* __restrict__ y, __nv_bfloat16* __restrict__ y_lo) {
     __shared__ float red[8];
     const int r = blockIdx.x;
     const float* xr = x + (size_t)r * ld;
@@ -29,28 +47,27 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float* __restrict__ 
     for (int i = 0; i < 8; ++i) tot += red[i];
     const float inv = rsqrtf(tot / (float)H + eps);
     __nv_bfloat16* yr = y + (size_t)r * H;
+    __nv_bfloat16* yl = y_lo ? y_lo + (size_t)r * H : nullptr;
     for (int i = threadIdx.x * 4; i < H; i += 1024) {
         const float4 v = *reinterpret_cast<const float4*>(xr + i);
         const __nv_bfloat162 w01 = *reinterpret_cast<const __nv_bfloat162*>(w + i);
         const __nv_bfloat162 w23 = *reinterpret_cast<const __nv_bfloat162*>(w + i + 2);
-        __nv_bfloat162 o01 = __floats2bfloat162_rn(v.x * inv * __low2float(w01), v.y * inv * __high2float(w01));
-        __nv_bfloat162 o23 = __floats2bfloat162_rn(v.z * inv * __low2float(w23), v.w * inv * __high2float(w23));
-        uint2 pack;
-        pack.x = *reinterpret_cast<uint32_t*>(&o01);
-        pack.y = *reinterpret_cast<uint32_t*>(&o23);
-        *reinterpret_cast<uint2*>(yr + i) = pack;
+        store_hilo4(yr + i, yl ? yl + i : nullptr, v.x * inv * __low2float(w01), v.y * inv * __high2float(w01),
+                    v.z * inv * __low2float(w23), v.w * inv * __high2float(w23));
     }
 }
 
-inline int launch_rmsnorm(const float* x, int M, int H, int ld, const void* w, float eps, void* y, cudaStream_t st) {
+inline int launch_rmsnorm(const float* x, int M, int H, int ld, const void* w, float eps, void* y, cudaStream_t st,
+                          void* y_lo = nullptr) {
     if (M <= 0) return QTTS_OK;
     if (H % 4 != 0 || ld % 4 != 0) {
         set_error("rmsnorm: H and ld must be multiples of 4");
         return QTTS_ERR_UNSUPPORTED;
     }
     rmsnorm_kernel<<<M, 256, 0, st>>>(x, H, ld, reinterpret_cast<const __nv_bfloat16*>(w), eps,
-                                      reinterpret_cast<__nv_bfloat16*>(y));
+                                      reinterpret_cast<__nv_bfloat16*>(y), reinterpret_cast<__nv_bfloat16*>(y_lo));
     QTTS_LAUNCH_CHECK();
+    ++g_launch_count;
     return QTTS_OK;
 }
 
@@ -70,20 +87,28 @@ __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ table, int 
 }
 
 // Stage-0 input of the code predictor: rows [2b] = hidden[b], [2b+1] = codec_emb[tok0[b]]
-// (CodePredictorUnrolled.forward, utils.py:1019-1020).
-__global__ void cp_stage0_rows_kernel(const __nv_bfloat16* __restrict__ hidden, const __nv_bfloat16* __restrict__ emb,
-                                      int V, int H, const int64_t* __restrict__ tok, int tok_ld,
-                                      __nv_bfloat16* __restrict__ out) {
+// (CodePredictorUnrolled.forward, utils.py:1019-1020), as a hi/lo operand pair
+// (the embedding is exact in bf16, its lo row is zero).
+__global__ void cp_stage0_rows_kernel(const __nv_bfloat16* __restrict__ hidden, const __nv_bfloat16* __restrict__ hidden_lo,
+                                      const __nv_bfloat16* __restrict__ emb, int V, int H,
+                                      const int64_t* __restrict__ tok, int tok_ld, __nv_bfloat16* __restrict__ out,
+                                      __nv_bfloat16* __restrict__ out_lo) {
     const int b = blockIdx.x;
     int64_t id = tok[(size_t)b * tok_ld];
     if (id < 0 || id >= V) id = 0;
     const uint4* h = reinterpret_cast<const uint4*>(hidden + (size_t)b * H);
+    const uint4* hl = reinterpret_cast<const uint4*>(hidden_lo + (size_t)b * H);
     const uint4* e = reinterpret_cast<const uint4*>(emb + (size_t)id * H);
     uint4* o0 = reinterpret_cast<uint4*>(out + (size_t)(2 * b) * H);
     uint4* o1 = reinterpret_cast<uint4*>(out + (size_t)(2 * b + 1) * H);
+    uint4* l0 = reinterpret_cast<uint4*>(out_lo + (size_t)(2 * b) * H);
+    uint4* l1 = reinterpret_cast<uint4*>(out_lo + (size_t)(2 * b + 1) * H);
+    const uint4 z = make_uint4(0, 0, 0, 0);
     for (int i = threadIdx.x; i < H / 8; i += blockDim.x) {
         o0[i] = h[i];
         o1[i] = e[i];
+        l0[i] = hl[i];
+        l1[i] = z;
     }
 }
 
@@ -123,20 +148,19 @@ __global__ void codec_sum_kernel(const int64_t* __restrict__ codes, int G, const
             a += text_add[orow * H + h];
             b += text_add[orow * H + h + 1];
         }
-        // the engine feeds next_embed to the graph in the model dtype (executor.py:1095-1097)
-        next_x[orow * H + h] = bf16_round(a);
-        next_x[orow * H + h + 1] = bf16_round(b);
+        next_x[orow * H + h] = a;
+        next_x[orow * H + h + 1] = b;
     }
 }
 
-// x[r] = bf16round(x_in[row_map ? row_map[r] : r]) (the executor casts input_embeds to bf16)
+// x[r] = x_in[row_map ? row_map[r] : r]  (the residual stream starts in fp32)
 __global__ void load_x_kernel(const float* __restrict__ x_in, float* __restrict__ x, int rows, int H,
                               const int32_t* __restrict__ row_map) {
     const size_t n = (size_t)rows * H;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
         const size_t r = i / H, c = i % H;
         const size_t src = row_map ? (size_t)row_map[r] : r;
-        x[i] = bf16_round(x_in[src * H + c]);
+        x[i] = x_in[src * H + c];
     }
 }
 
@@ -154,9 +178,9 @@ __global__ void kv_copy_blocks_kernel(uint4* __restrict__ pool, size_t block_vec
         b[k] = a[k];
 }
 
-// rows [n][L2][Hkv][D] -> pool[(blk, l2, g, off, d)]
-__global__ void kv_scatter_kernel(__nv_bfloat16* __restrict__ pool, int L2, int Hkv, int D, int bs, int num_blocks,
-                                  const __nv_bfloat16* __restrict__ rows, const int32_t* __restrict__ mapping) {
+// rows [n][L2][Hkv][D] -> pool[(blk, l2, g, off, d)]   (KV element type kv_t)
+__global__ void kv_scatter_kernel(kv_t* __restrict__ pool, int L2, int Hkv, int D, int bs, int num_blocks,
+                                  const kv_t* __restrict__ rows, const int32_t* __restrict__ mapping) {
     const int i = blockIdx.x;
     const int m = mapping[i];
     if (m < 0) return;
@@ -170,9 +194,9 @@ __global__ void kv_scatter_kernel(__nv_bfloat16* __restrict__ pool, int L2, int 
 }
 
 // out [L2][Hkv][n][D] from the slot's block table
-__global__ void kv_gather_kernel(const __nv_bfloat16* __restrict__ pool, int L2, int Hkv, int D, int bs,
+__global__ void kv_gather_kernel(const kv_t* __restrict__ pool, int L2, int Hkv, int D, int bs,
                                  int num_blocks, const int32_t* __restrict__ table_row, int n,
-                                 __nv_bfloat16* __restrict__ out) {
+                                 kv_t* __restrict__ out) {
     const int t = blockIdx.x;
     int blk = table_row[t / bs];
     const int off = t % bs;
@@ -180,8 +204,7 @@ __global__ void kv_gather_kernel(const __nv_bfloat16* __restrict__ pool, int L2,
     const int per = L2 * Hkv * D;
     for (int e = threadIdx.x; e < per; e += blockDim.x) {
         const int d = e % D, g = (e / D) % Hkv, l2 = e / (D * Hkv);
-        const __nv_bfloat16 v =
-            ok ? pool[((((size_t)blk * L2 + l2) * Hkv + g) * bs + off) * D + d] : __float2bfloat16(0.f);
+        const kv_t v = ok ? pool[((((size_t)blk * L2 + l2) * Hkv + g) * bs + off) * D + d] : __float2half(0.f);
         out[(((size_t)l2 * Hkv + g) * n + t) * D + d] = v;
     }
 }

@@ -21,10 +21,17 @@ def _need_cuda(*ts):
             raise ValueError("libqtts_b200 kernels take CUDA tensors only")
 
 
+def split_hilo(x: torch.Tensor):
+    """fp32 activation -> (hi, lo) bf16 pair with hi + lo ~ x."""
+    hi = x.to(torch.bfloat16)
+    return hi, (x - hi.float()).to(torch.bfloat16)
+
+
 def gemm(x: torch.Tensor, w: torch.Tensor, epilogue: int = _lib.EPI_F32, out: Optional[torch.Tensor] = None,
-         bias: Optional[torch.Tensor] = None, qkv: Optional[_lib.QkvEpilogue] = None) -> torch.Tensor:
-    """``x [M,K] bf16 · w [N,K]^T`` with a fused epilogue (see ``_lib.EPI_*``)."""
-    _need_cuda(x, w, out, bias)
+         bias: Optional[torch.Tensor] = None, qkv: Optional[_lib.QkvEpilogue] = None,
+         x_lo: Optional[torch.Tensor] = None, out_lo: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``(x [+ x_lo]) [M,K] bf16 · w [N,K]^T`` with a fused epilogue (see ``_lib.EPI_*``)."""
+    _need_cuda(x, w, out, bias, x_lo, out_lo)
     M, K = x.shape
     N = w.shape[0]
     if out is None:
@@ -36,14 +43,15 @@ def gemm(x: torch.Tensor, w: torch.Tensor, epilogue: int = _lib.EPI_F32, out: Op
             out = torch.empty(M, N // 2, device=x.device, dtype=torch.bfloat16)
         else:
             raise ValueError("this epilogue needs an explicit out tensor")
-    rc = _lib.load().qtts_gemm(x.data_ptr(), M, K, w.data_ptr(), N, epilogue, out.data_ptr(),
-                               _lib.ptr(bias), C.byref(qkv) if qkv is not None else None, _lib.stream_ptr())
+    rc = _lib.load().qtts_gemm(x.data_ptr(), _lib.ptr(x_lo), M, K, w.data_ptr(), N, epilogue, out.data_ptr(),
+                               _lib.ptr(out_lo), _lib.ptr(bias), C.byref(qkv) if qkv is not None else None,
+                               _lib.stream_ptr())
     _lib.check(rc, "gemm")
     return out
 
 
 def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, rows: Optional[int] = None, ld: Optional[int] = None,
-            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+            out: Optional[torch.Tensor] = None, out_lo: Optional[torch.Tensor] = None) -> torch.Tensor:
     _need_cuda(x, w)
     H = w.shape[0]
     M = rows if rows is not None else x.numel() // H
@@ -51,15 +59,15 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, rows: Optional[int] = 
     if out is None:
         out = torch.empty(M, H, device=x.device, dtype=torch.bfloat16)
     _lib.check(_lib.load().qtts_rmsnorm(x.data_ptr(), M, H, ld, w.data_ptr(), eps, out.data_ptr(),
-                                        _lib.stream_ptr()), "rmsnorm")
+                                        _lib.ptr(out_lo), _lib.stream_ptr()), "rmsnorm")
     return out
 
 
 def paged_attention(q: torch.Tensor, kv_pool: torch.Tensor, layer: int, block_table: torch.Tensor,
                     row_slot: torch.Tensor, row_ctx: torch.Tensor, max_ctx: int,
                     out: Optional[torch.Tensor] = None, ws_o: Optional[torch.Tensor] = None,
-                    ws_ml: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """``q [R, Hq, D]`` bf16 over ``kv_pool [blocks, L, 2, Hkv, 16, D]`` bf16."""
+                    ws_ml: Optional[torch.Tensor] = None, out_lo: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``q [R, Hq, D]`` fp32 over ``kv_pool [blocks, L, 2, Hkv, 16, D]`` bf16."""
     _need_cuda(q, kv_pool, block_table, row_slot, row_ctx)
     R, Hq, D = q.shape
     nb, L, _, Hkv, bs, _ = kv_pool.shape
@@ -74,7 +82,7 @@ def paged_attention(q: torch.Tensor, kv_pool: torch.Tensor, layer: int, block_ta
     rc = _lib.load().qtts_paged_attention(q.data_ptr(), R, Hq, Hkv, D, kv_pool.data_ptr(), layer, L, bs, nb,
                                           block_table.data_ptr(), block_table.shape[-1], row_slot.data_ptr(),
                                           row_ctx.data_ptr(), max_ctx, ws_o.data_ptr(), ws_ml.data_ptr(),
-                                          out.data_ptr(), _lib.stream_ptr())
+                                          out.data_ptr(), _lib.ptr(out_lo), _lib.stream_ptr())
     _lib.check(rc, "paged_attention")
     return out
 
@@ -171,7 +179,7 @@ class Sched:
     def gather(self, slot: int, n: int) -> torch.Tensor:
         kv = self.pool.kv
         L, Hkv, D = kv.shape[1], kv.shape[3], kv.shape[5]
-        out = torch.empty(2 * L, Hkv, n, D, device=kv.device, dtype=torch.bfloat16)
+        out = torch.empty(2 * L, Hkv, n, D, device=kv.device, dtype=torch.float16)
         rc = self.lib.qtts_kv_gather(kv.data_ptr(), C.byref(self.pool.state), L, Hkv, D, slot, n, out.data_ptr(),
                                      _lib.stream_ptr())
         _lib.check(rc, "kv_gather")

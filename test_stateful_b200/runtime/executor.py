@@ -1,0 +1,361 @@
+"""``B200Executor``: the reference ``Executor`` surface over libqtts_b200.so.
+
+Reference: engine/backend/executor.py:487-1612 (``Executor``), 357-480
+(``GPUFuture`` / ``StepOutput``).  The engine loop calls the same methods
+(``load``, ``prefill``, ``prefill_prefix_only``, ``prefill_from_prefix``,
+``launch_decode_step`` -> ``GPUFuture.wait`` -> ``StepOutput``, ``warmup``,
+``shutdown``; properties ``kv_pool``, ``max_batch_size``, ``max_seq_len``).
+
+What changes underneath:
+
+* KV is paged and written by the step itself, so ``StepOutput.batch_talker_kv``
+  is ``None`` and the engine loop's delta scatter
+  (engine/backend/engine_loop.py:2086-2092) has nothing to do.
+* Per-slot decode state lives on the device, indexed by slot id: token counts,
+  the next input embedding (``codec_sum + text`` computed by the step), the
+  text embedding to add next, temperature / penalty and the Philox noise
+  key / counter.  The reference keeps these as per-slot torch tensors and
+  rebuilds batch inputs every step (executor.py:1259-1469).
+* A decode step for a given batch size is captured once in a CUDA graph and
+  replayed; the host only writes the slot list.
+
+Code2wav is not part of this backend yet: ``audio_chunks`` entries are
+``None`` (the reference returns them as ``None`` too when its plan has no
+``wav`` output, executor.py:424-435).
+"""
+
+from __future__ import annotations
+
+import hashlib
+import logging
+from dataclasses import dataclass, field
+from typing import Any, Dict, List, Optional
+
+import torch
+
+from .. import _lib
+from ..config import EngineConfig, PagedPoolConfig
+from ..weights import make_cp_weights, make_talker_weights
+from .model import DeviceModel
+from .pool import PagedKVCachePool, PagedPrefixKVCache, SlotState
+
+logger = logging.getLogger(__name__)
+
+_MAX_SEED = (1 << 63) - 1
+
+
+def stable_sampling_seed(base_seed: int, *parts: object) -> int:
+    """Deterministic per-(session, segment) seed (executor.py:45-52)."""
+    h = hashlib.blake2b(digest_size=16)
+    h.update(str(int(base_seed)).encode("utf-8"))
+    for part in parts:
+        h.update(b"\0")
+        h.update(str(part).encode("utf-8"))
+    return int.from_bytes(h.digest()[:8], "little") & _MAX_SEED
+
+
+@dataclass
+class StepOutput:
+    """Results of one decode step (executor.py:455-480)."""
+
+    slots: List[SlotState]
+    eos_flags: List[bool]
+    audio_chunks: List[Optional[bytes]]
+    batch_talker_kv: Optional[torch.Tensor] = None
+    batch_c2w_kv: Optional[torch.Tensor] = None
+    original_past_lens: List[int] = field(default_factory=list)
+    padded_past_len: int = 0
+    split_c2w_conv: List[list] = field(default_factory=list)
+    split_c2w_transconv: List[list] = field(default_factory=list)
+    codec_sum: Optional[torch.Tensor] = None
+    full_codec: Optional[torch.Tensor] = None
+    updated_tc: Optional[torch.Tensor] = None
+    used_pingpong: bool = False
+    step_input_embeds: Optional[torch.Tensor] = None
+
+
+@dataclass
+class GPUFuture:
+    """Handle to an in-flight decode step (executor.py:357-452)."""
+
+    _executor: Any = None
+    _event: Any = None
+    _slots: List[SlotState] = field(default_factory=list)
+    _original_past_lens: List[int] = field(default_factory=list)
+    _codes_host: Optional[torch.Tensor] = None
+    _codes_dev: Optional[torch.Tensor] = None
+    _codec_sum: Optional[torch.Tensor] = None
+    _status_host: Optional[torch.Tensor] = None
+
+    def wait(self) -> StepOutput:
+        if self._event is not None:
+            self._event.synchronize()
+        n = len(self._slots)
+        if self._status_host is not None and int(self._status_host[0]) != 0:
+            st = int(self._status_host[0])
+            _lib.check(st, "decode step scheduler")
+        codes = self._codes_host[:n].clone() if self._codes_host is not None else None
+        eos_id = self._executor._config.talker.codec_eos_id if self._executor else 2150
+        eos = (codes[:, 0] == eos_id).tolist() if codes is not None else [False] * n
+        return StepOutput(slots=self._slots, eos_flags=eos, audio_chunks=[None] * n,
+                          original_past_lens=self._original_past_lens, codec_sum=self._codec_sum,
+                          full_codec=codes, split_c2w_conv=[[] for _ in range(n)],
+                          split_c2w_transconv=[[] for _ in range(n)])
+
+
+class B200Executor:
+    """Drop-in for ``engine.backend.executor.Executor`` on a B200."""
+
+    def __init__(self, *, engine_dir: str = "", weights_dir: str = "", device_id: int = 0,
+                 max_batch_size: int = 64, max_seq_len: int = 1024, model_config: Optional[EngineConfig] = None,
+                 do_sample: bool = False, temperature: float = 0.9, repetition_penalty: float = 1.05,
+                 random_seed: int = 0, num_blocks: int = 8192, weights: Optional[Dict[str, torch.Tensor]] = None,
+                 weight_seed: int = 1, max_prefill_rows: int = 512, use_cuda_graphs: bool = True):
+        if not torch.cuda.is_available():
+            raise RuntimeError("B200Executor needs a CUDA device (no CPU path)")
+        self._device = torch.device("cuda", device_id)
+        self._config = model_config or EngineConfig()
+        self._config.pool = PagedPoolConfig(block_size=16, num_blocks=num_blocks, max_slots=max_batch_size,
+                                            max_seq_len=max_seq_len)
+        self._max_batch = max_batch_size
+        self._max_seq_len = max_seq_len
+        self._max_input_len = max_prefill_rows
+        self._do_sample = do_sample
+        self._temperature = temperature
+        self._repetition_penalty = repetition_penalty
+        self._random_seed = int(random_seed)
+        self._weights = weights
+        self._weight_seed = weight_seed
+        self._use_graphs = use_cuda_graphs
+        self._stream = torch.cuda.Stream(device=self._device)
+        self._model: Optional[DeviceModel] = None
+        self._kv_pool: Optional[PagedKVCachePool] = None
+        self._graphs: Dict[int, Any] = {}
+        self._embedding_weights = None
+
+    # -- properties the engine loop reads ---------------------------------
+    @property
+    def kv_pool(self) -> PagedKVCachePool:
+        return self._kv_pool
+
+    @property
+    def max_batch_size(self) -> int:
+        return self._max_batch
+
+    @property
+    def max_seq_len(self) -> int:
+        return self._max_seq_len
+
+    @property
+    def model(self) -> DeviceModel:
+        return self._model
+
+    # -- lifecycle --------------------------------------------------------
+    def load(self) -> None:
+        cfg = self._config
+        W = self._weights
+        if W is None:
+            W = make_talker_weights(cfg.talker, self._weight_seed, device=self._device)
+            W.update(make_cp_weights(cfg.cp, self._weight_seed, device=self._device))
+        with torch.cuda.device(self._device):
+            self._model = DeviceModel(cfg, W, self._device, max_batch=self._max_batch,
+                                      max_prefill_rows=self._max_input_len)
+        self._weights = None
+        self._alloc_state()
+        self._kv_pool = PagedKVCachePool(self._model, self._max_batch)
+        self._kv_pool.counts_reset_hook = self._reset_slot_state
+        logger.info("B200Executor loaded (slots=%d, blocks=%d)", self._max_batch, cfg.pool.num_blocks)
+
+    def make_prefix_cache(self, max_entries: int = 16, max_prefix_len: int = 512) -> PagedPrefixKVCache:
+        return PagedPrefixKVCache(self._kv_pool, max_entries=max_entries, max_prefix_len=max_prefix_len)
+
+    def set_embedding_weights(self, weights) -> None:
+        self._embedding_weights = weights
+
+    def shutdown(self) -> None:
+        self._graphs.clear()
+        if self._model is not None:
+            self._model.close()
+        self._model = None
+        self._kv_pool = None
+
+    # -- per-slot device state --------------------------------------------
+    def _alloc_state(self) -> None:
+        t, c = self._config.talker, self._config.cp
+        S, B, dev = self._max_batch, self._max_batch, self._device
+        f32, i32, i64 = torch.float32, torch.int32, torch.int64
+        self.counts = torch.zeros(S, t.codec_vocab_size, dtype=i64, device=dev)
+        self.next_x = torch.zeros(S, t.hidden_size, dtype=f32, device=dev)
+        self.text_add = torch.zeros(S, t.hidden_size, dtype=f32, device=dev)
+        self.codec_sum = torch.zeros(S, t.hidden_size, dtype=f32, device=dev)
+        self.temperature = torch.ones(S, dtype=f32, device=dev)
+        self.penalty = torch.full((S,), self._repetition_penalty, dtype=f32, device=dev)
+        self.noise_key = torch.zeros(S, dtype=i64, device=dev)
+        self.noise_step = torch.zeros(S, dtype=i32, device=dev)
+        self.zero_gumbel = torch.zeros(B, t.logits_topk, dtype=f32, device=dev)
+        self.zero_cp_gumbel = torch.zeros(B, c.num_stages, t.logits_topk, dtype=f32, device=dev)
+        self.slots_dev = torch.zeros(B, dtype=i32, device=dev)
+        self.slots_host = torch.zeros(B, dtype=i32).pin_memory()
+        self.hidden = torch.zeros(B, t.hidden_size, dtype=torch.bfloat16, device=dev)
+        self.logits = torch.zeros(B, t.codec_vocab_size, dtype=f32, device=dev)
+        self.codes = torch.zeros(B, 1 + c.num_stages, dtype=i64, device=dev)
+        self.codes_host = torch.zeros(B, 1 + c.num_stages, dtype=i64).pin_memory()
+        self.status = torch.zeros(1, dtype=i32, device=dev)
+        self.status_host = torch.zeros(1, dtype=i32).pin_memory()
+
+    def _reset_slot_state(self, slot_id: int) -> None:
+        self.counts[slot_id].zero_()
+
+    def _configure_sampling(self, slot: SlotState) -> None:
+        """Per-slot sampling parameters (executor.py:1212-1227, 1335-1350)."""
+        sid = slot.slot_id
+        identity = slot.session_id if slot.session_id is not None else f"slot:{sid}"
+        seed = stable_sampling_seed(self._random_seed, identity, slot.segment_idx)
+        slot.sampling_seed = seed
+        self.noise_key[sid] = seed
+        self.noise_step[sid] = 0
+        self.temperature[sid] = self._temperature if self._do_sample else 1.0
+        self.penalty[sid] = self._repetition_penalty
+
+    def _io(self, n_rows: int, n_new: int, x_in: torch.Tensor, sample: int) -> _lib.StepIO:
+        io = _lib.StepIO()
+        io.slots = self.slots_dev.data_ptr()
+        io.n_rows = n_rows
+        io.n_new = n_new
+        io.slot_indexed = 1
+        io.x_in = x_in.data_ptr()
+        io.token_counts = self.counts.data_ptr()
+        if self._do_sample:
+            io.noise_seed = self._random_seed & _MAX_SEED
+            io.noise_key = self.noise_key.data_ptr()
+            io.noise_step = self.noise_step.data_ptr()
+        else:
+            io.gumbel = self.zero_gumbel.data_ptr()
+            io.cp_gumbel = self.zero_cp_gumbel.data_ptr()
+        io.temperature = self.temperature.data_ptr()
+        io.penalty = self.penalty.data_ptr()
+        io.sample = sample
+        io.text_add = self.text_add.data_ptr()
+        io.hidden_out = self.hidden.data_ptr()
+        io.logits_out = self.logits.data_ptr()
+        io.full_codec_out = self.codes.data_ptr()
+        io.codec_sum_out = self.codec_sum.data_ptr()
+        io.next_x_out = self.next_x.data_ptr()
+        io.status = self.status.data_ptr()
+        return io
+
+    def set_text_embedding(self, slot: SlotState, emb: Optional[torch.Tensor]) -> None:
+        """Text embedding added to the codec sum to form the slot's next input
+        (engine_loop.py:2170-2203: trailing[text_idx] or tts_pad)."""
+        if emb is None:
+            self.text_add[slot.slot_id].zero_()
+        else:
+            self.text_add[slot.slot_id].copy_(emb.reshape(-1).to(self._device, torch.float32), non_blocking=True)
+
+    # -- prefill ----------------------------------------------------------
+    def _validate_prefill_len(self, seq: int, stage: str) -> None:
+        if seq > self._max_input_len:
+            raise ValueError(f"{stage} input length {seq} exceeds max_input_len={self._max_input_len}; "
+                             "split the request into shorter segments")
+
+    def _prefill_call(self, slot: SlotState, embeds: torch.Tensor, sample: int) -> None:
+        seq = int(embeds.shape[-2]) if embeds.dim() == 3 else int(embeds.shape[0])
+        x = embeds.reshape(seq, -1).to(self._device, torch.float32).contiguous()
+        with torch.cuda.stream(self._stream):
+            self.slots_dev[:1].fill_(slot.slot_id)
+            self._model.step(self._io(1, seq, x, sample), self._stream)
+            self.status_host.copy_(self.status, non_blocking=True)
+        self._stream.synchronize()
+        _lib.check(int(self.status_host[0]), "prefill scheduler")
+        slot.past_len += seq
+
+    def prefill(self, slot: SlotState, prefill_embeds: torch.Tensor):
+        """executor.py:759-877: KV for the prompt plus the first frame's codes."""
+        seq = int(prefill_embeds.shape[1])
+        self._validate_prefill_len(seq, "prefill")
+        self._kv_pool.init_kv_tensors(slot)
+        self._configure_sampling(slot)
+        self._prefill_call(slot, prefill_embeds, sample=1)
+        slot.position_offset = 0
+        slot.frame_idx += 1
+        slot.next_embed = self.next_x[slot.slot_id]
+        codes = self.codes[:1].cpu()
+        return None, bool(int(codes[0, 0]) == self._config.talker.codec_eos_id)
+
+    def prefill_prefix_only(self, slot: SlotState, prefill_embeds: torch.Tensor) -> None:
+        """executor.py:879-950: KV for a cacheable prefix, no sampling."""
+        seq = int(prefill_embeds.shape[1])
+        self._validate_prefill_len(seq, "prefill_prefix_only")
+        self._kv_pool.init_kv_tensors(slot)
+        self._prefill_call(slot, prefill_embeds, sample=0)
+        slot.position_offset = 0
+
+    def prefill_from_prefix(self, slot: SlotState, request_prefill_embeds: torch.Tensor):
+        """executor.py:952-1081: append a suffix on top of the slot's (shared) KV."""
+        seq = int(request_prefill_embeds.shape[1])
+        self._validate_prefill_len(seq, "prefill_from_prefix")
+        self._configure_sampling(slot)
+        self._prefill_call(slot, request_prefill_embeds, sample=1)
+        slot.frame_idx += 1
+        slot.next_embed = self.next_x[slot.slot_id]
+        codes = self.codes[:1].cpu()
+        return None, bool(int(codes[0, 0]) == self._config.talker.codec_eos_id)
+
+    # -- decode -----------------------------------------------------------
+    def _capture(self, n: int):
+        io = self._io(n, 1, self.next_x, sample=1)
+        # warm the kernels (attributes, tensor-map prefetch) before capture
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=self._stream):
+            self._model.step(io, self._stream)
+        return g, io
+
+    def launch_decode_step(self, slots: List[SlotState]) -> GPUFuture:
+        """executor.py:1087-1183 — enqueue one decode step and return at once."""
+        n = len(slots)
+        if n == 0 or n > self._max_batch:
+            raise ValueError(f"batch of {n} slots outside [1, {self._max_batch}]")
+        cap = self._max_seq_len
+        for s in slots:
+            if s.past_len + 1 > cap:
+                raise ValueError(f"slot {s.slot_id} is at max_seq_len={cap}")
+        original = [s.past_len for s in slots]
+        for i, s in enumerate(slots):
+            self.slots_host[i] = s.slot_id
+        with torch.cuda.stream(self._stream):
+            self.slots_dev[:n].copy_(self.slots_host[:n], non_blocking=True)
+            if self._use_graphs:
+                if n not in self._graphs:
+                    self._model.step(self._io(n, 1, self.next_x, sample=1), self._stream)  # eager warm-up step
+                    self._stream.synchronize()
+                    self._graphs[n] = None  # the warm-up already advanced this batch
+                else:
+                    if self._graphs[n] is None:
+                        self._graphs[n] = self._capture(n)
+                    self._graphs[n][0].replay()
+            else:
+                self._model.step(self._io(n, 1, self.next_x, sample=1), self._stream)
+            self.codes_host[:n].copy_(self.codes[:n], non_blocking=True)
+            self.status_host.copy_(self.status, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(self._stream)
+        for s in slots:
+            s.past_len += 1
+            s.frame_idx += 1
+            s.touch()
+        return GPUFuture(_executor=self, _event=ev, _slots=list(slots), _original_past_lens=original,
+                         _codes_host=self.codes_host, _codes_dev=self.codes, _codec_sum=self.codec_sum,
+                         _status_host=self.status_host)
+
+    def warmup(self, n_rounds: int = 3) -> None:
+        """executor.py:1541-1605: a throw-away slot through prefill and decode."""
+        slot = self._kv_pool.allocate("__warmup__")
+        if slot is None:
+            return
+        try:
+            dummy = torch.randn(1, 4, self._config.talker.hidden_size, device=self._device) * 0.02
+            self.prefill(slot, dummy)
+            for _ in range(n_rounds):
+                self.launch_decode_step([slot]).wait()
+        finally:
+            self._kv_pool.release(slot.slot_id)

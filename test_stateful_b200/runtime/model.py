@@ -11,7 +11,7 @@ and are packed once into the layouts the kernels stream:
   both halves of a feature in one 128-row tile (Qwen3MLP);
 * ``w_o``, ``w_down``, norms          — stacked per layer.
 
-The paged KV pool is ``[num_blocks][L][2][Hkv][16][D]`` bf16: one block of one
+The paged KV pool is ``[num_blocks][L][2][Hkv][16][D]`` fp16: one block of one
 (layer, k|v, head) is a contiguous 4 KB chunk, the unit the attention kernel
 copies into shared memory; a whole block (all layers) is one contiguous
 region, the unit of a copy-on-write.
@@ -57,7 +57,7 @@ class PagedPoolTensors:
         self.seq_len = torch.empty(p.max_slots, **i32)
         self.position_offset = torch.empty(p.max_slots, **i32)
         self.kv = torch.empty(p.num_blocks, t.num_layers, 2, t.kv_heads, p.block_size, t.head_dim,
-                              device=device, dtype=torch.bfloat16)
+                              device=device, dtype=torch.float16)
         self.block_elems = t.num_layers * 2 * t.kv_heads * p.block_size * t.head_dim
         self.state = _lib.PagedState(
             self.free_stack.data_ptr(), self.free_top.data_ptr(), self.refcount.data_ptr(),

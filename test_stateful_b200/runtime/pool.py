@@ -180,7 +180,7 @@ class PagedKVCachePool:
         """``[B, L*2, H, max_past_len, D]`` zero-padded (kv_cache_pool.py:410-420)."""
         t = self._cfg.talker
         out = torch.zeros(len(slot_ids), 2 * t.num_layers, t.kv_heads, max_past_len, t.head_dim,
-                          device=self._pool.kv.device, dtype=torch.bfloat16)
+                          device=self._pool.kv.device, dtype=torch.float16)
         for i, sid in enumerate(slot_ids):
             n = min(int(self._pool.seq_len[sid].item()), max_past_len)
             if n > 0:
@@ -212,7 +212,7 @@ class PagedKVCachePool:
         slots = torch.tensor([slot_id], dtype=torch.int32, device=self._pool.kv.device)
         mapping, _, _, cs, cd = self._sched.append(slots, n)
         self._sched.copy_blocks(cs, cd)
-        self._sched.scatter(rows.to(torch.bfloat16).contiguous(), mapping)
+        self._sched.scatter(rows.to(torch.float16).contiguous(), mapping)
         st = int(self._sched.status.item())
         if st != 0:
             raise ValueError(f"KV append failed with status {st}")

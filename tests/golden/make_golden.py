@@ -365,13 +365,33 @@ def make_pool_ops(ref_mods, out):
     np.savez_compressed(out, **payload)
 
 
+def make_seeds(out):
+    """Per-(session, segment) sampling seeds from engine/backend/executor.py:45-52."""
+    from engine.backend import executor as ref_executor
+    base, sess, seg, seed = [], [], [], []
+    for b in (0, 1, 1234567):
+        for s in ("s0", "session-42", "slot:3"):
+            for g in (-1, 0, 7):
+                base.append(b)
+                sess.append(s)
+                seg.append(g)
+                seed.append(ref_executor._stable_sampling_seed(b, s, g))
+    np.savez_compressed(out, base=np.asarray(base, np.int64), session=np.asarray(sess),
+                        segment=np.asarray(seg, np.int64), seed=np.asarray(seed, np.uint64))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, type=Path)
     ap.add_argument("--skip-full", action="store_true")
+    ap.add_argument("--only", default=None)
     args = ap.parse_args()
     torch.set_num_threads(max(1, torch.get_num_threads()))
     ref_mods = import_reference(args.reference.resolve())
+    if args.only == "seeds":
+        make_seeds(HERE / "seeds.npz")
+        return
+    make_seeds(HERE / "seeds.npz")
     t0 = time.time()
     make_fused_tiny(ref_mods, HERE / "fused_tiny.npz")
     make_pool_ops(ref_mods, HERE / "pool_ops.npz")
