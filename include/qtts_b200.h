@@ -168,6 +168,20 @@ int qtts_paged_attention(const void* q, int R, int num_heads, int kv_heads, int 
                          const int32_t* row_slot, const int32_t* row_ctx, int max_ctx,
                          float* ws_o, float* ws_ml, void* out, void* out_lo, qtts_stream_t stream);
 
+/* Same computation as qtts_paged_attention, for callers that cannot allocate device memory
+ * when they run attention (a plugin host that owns every allocation and passes only the
+ * call's tensors, or a latency-bound thread that must not call cudaMalloc).  No counterpart
+ * in the reference.  The split-KV partials live in a static device array of the library
+ * (4 MiB, held on every GPU that loads it), so nothing is allocated; shapes with
+ * num_rows * num_heads * max_splits * head_dim > 1048576 are rejected with QTTS_ERR_INVALID.
+ * The first call on a device looks up the array's address; make that call before any stream
+ * capture.  Calls share the array: two calls that overlap on the GPU race. */
+int qtts_paged_attention_noalloc(const void* q, int R, int num_heads, int kv_heads, int head_dim,
+                                 const void* kv_pool, int layer, int num_layers, int block_size,
+                                 int num_blocks, const int32_t* block_table, int max_blocks_per_seq,
+                                 const int32_t* row_slot, const int32_t* row_ctx, int max_ctx,
+                                 void* out, void* out_lo, qtts_stream_t stream);
+
 /* Top-k / temperature / Gumbel-max sampling of fp32 logits [R][V] (row stride ld).
  * Talker head (talker_unified_modules.py:373-388) when counts != NULL: suppress
  * [V-1024,V) except eos_id, repetition penalty on counts>0, counts[tok] += 1.

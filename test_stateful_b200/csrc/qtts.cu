@@ -4,6 +4,7 @@
 // the caller's stream and returns a status code; nothing here allocates per
 // call except qtts_engine_create.
 #include <cstdarg>
+#include <mutex>
 #include <new>
 
 #include "common.cuh"
@@ -251,3 +252,79 @@ int qtts_engine_step(qtts_engine* e, qtts_step_io* io, qtts_stream_t stream) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Paged attention without caller scratch.
+//
+// qtts_paged_attention needs two scratch buffers for its split-KV partial
+// results, which the caller allocates.  Some callers cannot allocate device
+// memory at the point where they run attention: a host that owns every device
+// allocation itself and hands plugins only the tensors of the call (a
+// TensorRT-style plugin or a fixed-arena serving runtime), or a latency-bound
+// thread that must not call cudaMalloc because it can synchronise the device.
+// For them this variant keeps the partials in the static device array below,
+// which every GPU that loads the library holds until the process exits.
+//
+// Limit: R * num_heads * max_splits * head_dim <= kNoAllocMaxPartials
+// (4 MiB of fp32, e.g. 64 rows x 16 heads x 8 splits (2048 keys) x 128),
+// with max_splits = ceil(ceil(max_ctx / 16) / QTTS_ATTN_SPLIT_BLOCKS).
+// Nothing in the array needs to start at zero: each call writes every partial
+// it later reads.  All calls share the one array, so two calls that overlap
+// on the GPU (different streams, no ordering between them) race on it.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kNoAllocMaxPartials = size_t(1) << 20;               // o partials, floats
+constexpr size_t kNoAllocMaxStats = kNoAllocMaxPartials / 64;         // (max, sum) pairs, floats
+static __device__ __align__(256) float g_noalloc_attn_scratch[kNoAllocMaxPartials + kNoAllocMaxStats];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[kMaxDevices] = {nullptr};
+
+// Device address of the static array on the current device, looked up once per device.
+int noalloc_scratch(float** out) {
+    int dev = 0;
+    QTTS_CHECK_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) {
+        set_error("paged_attention_noalloc: device index %d out of range", dev);
+        return QTTS_ERR_INVALID;
+    }
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void* p = nullptr;
+        const cudaError_t rc = cudaGetSymbolAddress(&p, g_noalloc_attn_scratch);
+        if (rc != cudaSuccess || !p) {
+            set_error("paged_attention_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(rc));
+            return QTTS_ERR_CUDA;
+        }
+        g_noalloc_ptr[dev] = static_cast<float*>(p);
+    }
+    *out = g_noalloc_ptr[dev];
+    return QTTS_OK;
+}
+
+}  // namespace
+
+extern "C" int qtts_paged_attention_noalloc(const void* q, int R, int num_heads, int kv_heads, int head_dim,
+                                            const void* kv_pool, int layer, int num_layers, int block_size,
+                                            int num_blocks, const int32_t* block_table, int max_blocks_per_seq,
+                                            const int32_t* row_slot, const int32_t* row_ctx, int max_ctx, void* out,
+                                            void* out_lo, qtts_stream_t stream) {
+    QTTS_REQUIRE(R >= 0 && num_heads > 0 && head_dim > 0 && max_ctx > 0, "paged_attention_noalloc: bad shape");
+    const size_t splits = (size_t)attn_max_splits(max_ctx);
+    const size_t need_o = (size_t)R * num_heads * splits * head_dim;
+    const size_t need_ml = (size_t)R * num_heads * splits * 2;
+    if (need_o > kNoAllocMaxPartials || need_ml > kNoAllocMaxStats) {
+        set_error("paged_attention_noalloc: %zu rows x heads x splits x head_dim partials exceed the static scratch "
+                  "of %zu floats; use fewer rows or qtts_paged_attention with caller scratch",
+                  need_o, kNoAllocMaxPartials);
+        return QTTS_ERR_INVALID;
+    }
+    float* scratch = nullptr;
+    const int rc = noalloc_scratch(&scratch);
+    if (rc != QTTS_OK) return rc;
+    return qtts_paged_attention(q, R, num_heads, kv_heads, head_dim, kv_pool, layer, num_layers, block_size,
+                                num_blocks, block_table, max_blocks_per_seq, row_slot, row_ctx, max_ctx, scratch,
+                                scratch + kNoAllocMaxPartials, out, out_lo, stream);
+}
