@@ -52,6 +52,9 @@ def parse():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=64)
+    ap.add_argument("--profile", action="store_true",
+                    help="timed region only, inside an NVTX range 'timed' (for ncu --nvtx-include timed/); "
+                         "no CPU baseline, e2e or roofline pass")
     return ap.parse_args()
 
 
@@ -295,12 +298,14 @@ def run_b200(rank, world, local):
         torch.distributed.barrier()
     torch.cuda.synchronize(dev)
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(ARGS.steps + 1)]
+    torch.cuda.nvtx.range_push("timed")
     with torch.cuda.stream(stream):
         evs[0].record(stream)
         for k in range(ARGS.steps):
             g.replay()
             evs[k + 1].record(stream)
     torch.cuda.synchronize(dev)
+    torch.cuda.nvtx.range_pop()
     if world > 1:
         torch.distributed.barrier()
     clk = clocks.stop()
@@ -315,6 +320,13 @@ def run_b200(rank, world, local):
         total_ms = float(t.item())
     frames = n * ARGS.steps * world
     value = frames / (total_ms / 1e3)
+    if ARGS.profile:
+        if rank == 0:
+            print(json.dumps({"profile_run": True, "value": round(value, 1), "unit": UNIT,
+                              "ms_per_step": round(total_ms / ARGS.steps, 4), "kernels_per_step": launches}))
+        ex._graphs.clear()
+        ex.shutdown()
+        return
 
     # ---- e2e through the executor call with host buffers
     t_host = pad.float().cpu().expand(n, -1).contiguous().pin_memory()

@@ -82,11 +82,22 @@ __global__ void __launch_bounds__(128) paged_attn_kernel(const AttnParams p) {
 
     const int r = blockIdx.x, g = blockIdx.y, sp = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    griddep_wait();
+    griddep_launch();
     const int ctx = p.row_ctx[r];
     const int nbt = (ctx + 15) >> 4;
     const int b_start = sp * QTTS_ATTN_SPLIT_BLOCKS;
     const int b_end = min(nbt, b_start + QTTS_ATTN_SPLIT_BLOCKS);
-    if (b_start >= b_end) return;  // uniform for the CTA
+    if (b_start >= b_end) {  // uniform for the CTA
+        if (nbt == 0 && sp == 0) {  // a row with no keys (only after a scheduler error): zero output
+            for (int i = threadIdx.x; i < 2 * D; i += blockDim.x) {
+                const size_t o = ((size_t)r * p.num_heads + g * 2) * D + i;
+                p.out[o] = __float2bfloat16(0.f);
+                if (p.out_lo) p.out_lo[o] = __float2bfloat16(0.f);
+            }
+        }
+        return;
+    }
     const int slot = p.row_slot[r];
 
     // q for the two heads of this kv group, pre-scaled into the log2 domain
@@ -258,6 +269,14 @@ __global__ void __launch_bounds__(128) paged_attn_kernel(const AttnParams p) {
             lsum += red[(w * 2 + h) * RS + D + 1] * f;
         }
         const size_t hrow = (size_t)r * p.num_heads + g * 2 + h;
+        if (nbt <= QTTS_ATTN_SPLIT_BLOCKS) {
+            // the row has a single split: finish here, the combine kernel skips it
+            const float o = lsum > 0.f ? acc / lsum : 0.f;
+            const __nv_bfloat16 hi = __float2bfloat16(o);
+            p.out[hrow * D + d] = hi;
+            if (p.out_lo) p.out_lo[hrow * D + d] = __float2bfloat16(o - __bfloat162float(hi));
+            continue;
+        }
         p.ws_o[(hrow * p.max_splits + sp) * D + d] = acc;
         if (d == 0) {
             p.ws_ml[(hrow * p.max_splits + sp) * 2 + 0] = M;
@@ -270,9 +289,12 @@ __global__ void __launch_bounds__(128) paged_attn_kernel(const AttnParams p) {
 template <int D>
 __global__ void attn_combine_kernel(const AttnParams p) {
     const int r = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+    griddep_wait();
+    griddep_launch();
     const int ctx = p.row_ctx[r];
     const int nbt = (ctx + 15) >> 4;
     const int ns = min(p.max_splits, (nbt + QTTS_ATTN_SPLIT_BLOCKS - 1) / QTTS_ATTN_SPLIT_BLOCKS);
+    if (ns <= 1) return;  // single-split (and empty) rows were finished by paged_attn_kernel
     const size_t hrow = (size_t)r * p.num_heads + h;
     float M = -INFINITY;
     for (int s = 0; s < ns; ++s) M = fmaxf(M, p.ws_ml[(hrow * p.max_splits + s) * 2]);
@@ -303,11 +325,9 @@ inline int launch_attention_d(const AttnParams& p, cudaStream_t st) {
         QTTS_CHECK_CUDA(cudaFuncSetAttribute(paged_attn_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM));
         attr = true;
     }
-    paged_attn_kernel<D><<<dim3(p.R, p.kv_heads, p.max_splits), 128, L::SMEM, st>>>(p);
-    QTTS_LAUNCH_CHECK();
-    attn_combine_kernel<D><<<dim3(p.R, p.num_heads), D, 0, st>>>(p);
-    QTTS_LAUNCH_CHECK();
-    g_launch_count += 2;
+    QTTS_LAUNCH(paged_attn_kernel<D>, dim3(p.R, p.kv_heads, p.max_splits), dim3(128), L::SMEM, st, p);
+    if (p.max_splits > 1)  // otherwise every row finished inside paged_attn_kernel
+        QTTS_LAUNCH(attn_combine_kernel<D>, dim3(p.R, p.num_heads), dim3(D), 0, st, p);
     return QTTS_OK;
 }
 

@@ -256,12 +256,13 @@ __device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
     return v;
 }
 
+// No memory clobber: callers read data published by a cluster barrier, and the
+// compiler may keep several of these loads in flight before their first use.
 __device__ __forceinline__ float4 ld_dsmem_f32x4(uint32_t addr) {
     float4 v;
     asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
                  : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                 : "r"(addr)
-                 : "memory");
+                 : "r"(addr));
     return v;
 }
 
@@ -293,6 +294,63 @@ inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
 
 // kernels enqueued by this host thread (the engine reports it per step)
 inline thread_local int g_launch_count = 0;
+
+// ----------------------------------------------------------------------------
+// programmatic dependent launch: a kernel launched with the attribute may
+// start while its predecessor drains; it must call griddep_wait() before it
+// touches anything the predecessor writes, and calls griddep_launch() to let
+// its own successor start early.  Without a programmatic predecessor both are
+// no-ops.  QTTS_PDL=0 in the environment turns the attribute off.
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+inline bool pdl_enabled() {
+    static const bool on = [] {
+        const char* v = getenv("QTTS_PDL");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
+
+// Launch with the programmatic-serialization attribute (and an optional cluster shape).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              dim3 cluster, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    int n = 0;
+    if (pdl_enabled()) {
+        attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[n].val.programmaticStreamSerializationAllowed = 1;
+        ++n;
+    }
+    if (cluster.x * cluster.y * cluster.z > 1) {
+        attr[n].id = cudaLaunchAttributeClusterDimension;
+        attr[n].val.clusterDim.x = cluster.x;
+        attr[n].val.clusterDim.y = cluster.y;
+        attr[n].val.clusterDim.z = cluster.z;
+        ++n;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = n;
+    ++g_launch_count;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+#define QTTS_LAUNCH(kernel, grid, block, smem, st, ...)                                                 \
+    do {                                                                                                \
+        cudaError_t _e = ::qtts::launch_pdl(kernel, grid, block, smem, st, dim3(1, 1, 1), __VA_ARGS__); \
+        if (_e != cudaSuccess) {                                                                        \
+            ::qtts::set_error("launch of %s failed: %s (%s:%d)", #kernel, cudaGetErrorString(_e),       \
+                              __FILE__, __LINE__);                                                      \
+            return QTTS_ERR_CUDA;                                                                       \
+        }                                                                                               \
+    } while (0)
 
 inline int num_sms() {
     static int n = 0;

@@ -273,22 +273,15 @@ inline int engine_step_impl(qtts_engine* e, const qtts_step_io& io, cudaStream_t
     }
     const SchedView sv = view_of(&d.pool);
     // ---- scheduler: reserve KV positions, copy shared blocks
-    sched_append_kernel<<<1, kSchedThreads, 0, st>>>(sv, io.slots, nr, nn, e->mapping, e->row_ctx, e->row_pos,
-                                                     e->cow_src, e->cow_dst, io.status);
-    QTTS_LAUNCH_CHECK();
-    ++g_launch_count;
+    QTTS_LAUNCH(sched_append_kernel, dim3(1), dim3(kSchedThreads), 0, st, sv, io.slots, nr, nn, e->mapping,
+                e->row_ctx, e->row_pos, e->cow_src, e->cow_dst, io.status);
     const size_t block_elems = (size_t)d.layers * 2 * Hkv * d.pool.block_size * D;
-    kv_copy_blocks_kernel<<<dim3(64, nr), 256, 0, st>>>(reinterpret_cast<uint4*>(d.kv_pool), block_elems / 8,
-                                                        e->cow_src, e->cow_dst, d.pool.num_blocks);
-    QTTS_LAUNCH_CHECK();
-    ++g_launch_count;
-    expand_rows_kernel<<<ceil_div(R, 256), 256, 0, st>>>(io.slots, nr, nn, e->row_slot);
-    QTTS_LAUNCH_CHECK();
-    ++g_launch_count;
+    QTTS_LAUNCH(kv_copy_blocks_kernel, dim3(64, nr), dim3(256), 0, st, reinterpret_cast<uint4*>(d.kv_pool),
+                block_elems / 8, (const int32_t*)e->cow_src, (const int32_t*)e->cow_dst, d.pool.num_blocks);
+    QTTS_LAUNCH(expand_rows_kernel, dim3(ceil_div(R, 256)), dim3(256), 0, st, io.slots, nr, nn, e->row_slot);
     const int32_t* smap = io.slot_indexed ? io.slots : nullptr;
-    load_x_kernel<<<ceil_div(R * H, 1024), 256, 0, st>>>(io.x_in, e->x, R, H, (io.slot_indexed && nn == 1) ? smap : nullptr);
-    QTTS_LAUNCH_CHECK();
-    ++g_launch_count;
+    QTTS_LAUNCH(load_x_kernel, dim3(ceil_div(R * H, 1024)), dim3(256), 0, st, io.x_in, e->x, R, H,
+                (io.slot_indexed && nn == 1) ? smap : (const int32_t*)nullptr);
 
     AttnParams ap = {};
     ap.q = e->qbuf;
@@ -379,14 +372,14 @@ inline int engine_step_impl(qtts_engine* e, const qtts_step_io& io, cudaStream_t
         const int rows = s == 0 ? 2 * nr : nr;
         const int32_t* m = e->cp_meta + (size_t)s * 4 * crows;
         if (s == 0) {
-            cp_stage0_rows_kernel<<<nr, 128, 0, st>>>(e->hid, e->hid_lo, bf(d.w_codec_emb, 0), d.vocab, H, codes_in,
-                                                      G, e->cp_in, e->cp_in_lo);
+            QTTS_LAUNCH(cp_stage0_rows_kernel, dim3(nr), dim3(128), 0, st, (const __nv_bfloat16*)e->hid,
+                        (const __nv_bfloat16*)e->hid_lo, bf(d.w_codec_emb, 0), d.vocab, H, codes_in, G, e->cp_in,
+                        e->cp_in_lo);
         } else {
-            gather_rows_kernel<<<nr, 128, 0, st>>>(bf(d.cp_w_codec_emb, (size_t)(s - 1) * d.cp_vocab * H),
-                                                   d.cp_vocab, H, codes_in + s, G, e->cp_in, H);
+            QTTS_LAUNCH(gather_rows_kernel, dim3(nr), dim3(128), 0, st,
+                        bf(d.cp_w_codec_emb, (size_t)(s - 1) * d.cp_vocab * H), d.cp_vocab, H, codes_in + s, G,
+                        e->cp_in, H);
         }
-        QTTS_LAUNCH_CHECK();
-        ++g_launch_count;
         QTTS_TRY(run_plan(s == 0 ? e->cp_proj_pair : e->cp_proj_one, rows, st));
         cap.row_slot = m + 3 * crows;
         cap.row_ctx = m + 2 * crows;
@@ -439,11 +432,9 @@ inline int engine_step_impl(qtts_engine* e, const qtts_step_io& io, cudaStream_t
                                               nr, cudaMemcpyDeviceToDevice, st));
     }
     // ---- codec embedding sum -> next input
-    codec_sum_kernel<<<nr, 256, G * sizeof(int64_t), st>>>(io.full_codec_out, G, bf(d.w_codec_emb, 0), d.vocab,
-                                                           bf(d.cp_w_codec_emb, 0), d.cp_vocab, H, io.text_add,
-                                                           io.codec_sum_out, io.next_x_out, smap, io.noise_step);
-    QTTS_LAUNCH_CHECK();
-    ++g_launch_count;
+    QTTS_LAUNCH(codec_sum_kernel, dim3(nr), dim3(256), G * sizeof(int64_t), st, (const int64_t*)io.full_codec_out,
+                G, bf(d.w_codec_emb, 0), d.vocab, bf(d.cp_w_codec_emb, 0), d.cp_vocab, H, io.text_add,
+                io.codec_sum_out, io.next_x_out, smap, io.noise_step);
     return QTTS_OK;
 }
 

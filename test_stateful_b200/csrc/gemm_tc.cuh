@@ -203,7 +203,15 @@ __global__ void __launch_bounds__(128) gemm_tc_kernel(const __grid_constant__ CU
         tma_prefetch_desc(&tmW);
         tma_prefetch_desc(&tmX);
         if (SPLIT) tma_prefetch_desc(&tmXlo);
+        // The weights do not depend on the previous kernel: start streaming the
+        // first stages before waiting for it (programmatic dependent launch).
+        for (int i = 0; i < nkb && i < STAGES; ++i) {
+            mbar_arrive_expect_tx(&full[i], L::STAGE_BYTES);
+            tma_load_2d(smem + i * L::STAGE_BYTES, &tmW, &full[i], (kb0 + i) * 64, tile_n * 128);
+        }
     }
+    griddep_wait();  // activations, outputs and the KV pool belong to earlier kernels
+    griddep_launch();
     if (warp == 2) {
         tmem_alloc(tmem_slot, BN);
         tmem_relinquish();
@@ -225,8 +233,10 @@ __global__ void __launch_bounds__(128) gemm_tc_kernel(const __grid_constant__ CU
             }
             uint8_t* a = smem + s * L::STAGE_BYTES;
             uint8_t* b = a + L::A_BYTES;
-            mbar_arrive_expect_tx(&full[s], L::STAGE_BYTES);
-            tma_load_2d(a, &tmW, &full[s], (kb0 + i) * 64, tile_n * 128);
+            if (i >= STAGES) {  // the first stages' weight tiles are already in flight
+                mbar_arrive_expect_tx(&full[s], L::STAGE_BYTES);
+                tma_load_2d(a, &tmW, &full[s], (kb0 + i) * 64, tile_n * 128);
+            }
             tma_load_2d(b, &tmX, &full[s], (kb0 + i) * 64, tile_m * BN);
             if (SPLIT) tma_load_2d(b + L::B_BYTES, &tmXlo, &full[s], (kb0 + i) * 64, tile_m * BN);
             ++issued;
@@ -292,13 +302,25 @@ __global__ void __launch_bounds__(128) gemm_tc_kernel(const __grid_constant__ CU
     const int m0 = split * per;
     if (p.splits > 1) {
         cluster_sync();  // every CTA's partial is in its shared memory
-        const uint32_t base = smem_u32(P);
-        for (int i = 0; i < per; ++i) {
-            const int idx = (m0 + i) * 128 + threadIdx.x;
-            float acc = 0.f;
-            for (int r = 0; r < p.splits; ++r)  // fixed order: deterministic
-                acc += ld_dsmem_f32(map_to_rank(base + idx * 4, (uint32_t)r));
-            P[idx] = acc;
+        // this CTA's token slice, as float4 chunks: all splits' loads are issued
+        // before any is consumed, so the remote-shared-memory latency is paid once
+        const uint32_t base = smem_u32(P + m0 * 128);
+        for (int e = threadIdx.x; e < per * 32; e += 128) {
+            float4 v[8];
+#pragma unroll
+            for (int r = 0; r < 8; ++r)
+                if (r < p.splits) v[r] = ld_dsmem_f32x4(map_to_rank(base + (uint32_t)e * 16u, (uint32_t)r));
+            float4 acc = v[0];
+#pragma unroll
+            for (int r = 1; r < 8; ++r) {  // fixed order: deterministic
+                if (r < p.splits) {
+                    acc.x += v[r].x;
+                    acc.y += v[r].y;
+                    acc.z += v[r].z;
+                    acc.w += v[r].w;
+                }
+            }
+            *reinterpret_cast<float4*>(P + m0 * 128 + e * 4) = acc;
         }
         __syncthreads();
     }
@@ -371,20 +393,8 @@ inline int launch_gemm_t(const CUtensorMap& mw, const CUtensorMap& mx, const CUt
         QTTS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM));
         attr_done = true;
     }
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(p.N / 128, p.splits, ceil_div(p.M, BN));
-    cfg.blockDim = dim3(128, 1, 1);
-    cfg.dynamicSmemBytes = L::SMEM;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = p.splits;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    QTTS_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, mw, mx, mxlo, p));
-    ++g_launch_count;
+    QTTS_CHECK_CUDA(launch_pdl(kern, dim3(p.N / 128, p.splits, ceil_div(p.M, BN)), dim3(128, 1, 1), L::SMEM, st,
+                               dim3(1, p.splits, 1), mw, mx, mxlo, p));
     return QTTS_OK;
 }
 

@@ -78,6 +78,8 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
     __shared__ int c_idx[kSampleCand];
 
     const int r = blockIdx.x, tid = threadIdx.x;
+    griddep_wait();
+    griddep_launch();
     const float* lg = p.logits + (size_t)r * p.ld;
     const int crow = p.counts_row ? p.counts_row[r] : r;  // per-stream state row (slot)
     const float pen = p.penalty ? p.penalty[crow] : 1.0f;
@@ -114,15 +116,36 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
             if (idx < p.V && (key[i] & mask) == prefix) atomicAdd(&hist[(key[i] >> shift) & 255u], 1u);
         }
         __syncthreads();
-        if (tid == 0) {
-            uint32_t above = 0;
-            int b = 255;
-            for (; b > 0; --b) {
-                if (above + hist[b] >= need) break;
-                above += hist[b];
+        if (tid < 32) {
+            // warp scan from the top bin down: lane l owns bins 255-8l .. 248-8l
+            const int lane = tid;
+            uint32_t c[8], tot = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                c[j] = hist[255 - 8 * lane - j];
+                tot += c[j];
             }
-            s_prefix = prefix | ((uint32_t)b << shift);
-            s_need = need - above;
+            uint32_t incl = tot;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t nb = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += nb;
+            }
+            const uint32_t excl = incl - tot;
+            const unsigned hit = __ballot_sync(0xffffffffu, excl < need && need <= incl);
+            const int src = hit ? __ffs(hit) - 1 : 31;
+            if (lane == src) {
+                uint32_t above = excl;
+                int b = 255 - 8 * lane;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    b = 255 - 8 * lane - j;
+                    if (above + c[j] >= need || b == 0) break;
+                    above += c[j];
+                }
+                s_prefix = prefix | ((uint32_t)b << shift);
+                s_need = need - above;
+            }
         }
         __syncthreads();
         prefix = s_prefix;
@@ -249,9 +272,7 @@ inline int launch_sample(const SampleParams& p, cudaStream_t st) {
         set_error("sample: need V <= %d and 1 <= topk <= min(64, V)", kSampleThreads * kSampleMaxPer);
         return QTTS_ERR_UNSUPPORTED;
     }
-    sample_kernel<<<p.R, kSampleThreads, 0, st>>>(p);
-    QTTS_LAUNCH_CHECK();
-    ++g_launch_count;
+    QTTS_LAUNCH(sample_kernel, dim3(p.R), dim3(kSampleThreads), 0, st, p);
     return QTTS_OK;
 }
 

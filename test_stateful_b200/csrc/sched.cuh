@@ -68,6 +68,8 @@ __global__ void __launch_bounds__(kSchedThreads) sched_append_kernel(SchedView v
     __shared__ int s_scan[kSchedThreads];
     __shared__ int s_err;
     const int i = threadIdx.x;
+    griddep_wait();
+    griddep_launch();
     const bool active = i < n_rows;
     int slot = 0, pos = 0, bi0 = 0, blk0 = -1, need = 0;
     bool cow = false, bad = false;

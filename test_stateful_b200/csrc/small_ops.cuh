@@ -33,6 +33,8 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float* __restrict__ 
                                                       __nv_bfloat16* __restrict__ y, __nv_bfloat16* __restrict__ y_lo) {
     __shared__ float red[8];
     const int r = blockIdx.x;
+    griddep_wait();
+    griddep_launch();
     const float* xr = x + (size_t)r * ld;
     float ss = 0.f;
     for (int i = threadIdx.x * 4; i < H; i += 1024) {
@@ -64,10 +66,8 @@ inline int launch_rmsnorm(const float* x, int M, int H, int ld, const void* w, f
         set_error("rmsnorm: H and ld must be multiples of 4");
         return QTTS_ERR_UNSUPPORTED;
     }
-    rmsnorm_kernel<<<M, 256, 0, st>>>(x, H, ld, reinterpret_cast<const __nv_bfloat16*>(w), eps,
-                                      reinterpret_cast<__nv_bfloat16*>(y), reinterpret_cast<__nv_bfloat16*>(y_lo));
-    QTTS_LAUNCH_CHECK();
-    ++g_launch_count;
+    QTTS_LAUNCH(rmsnorm_kernel, dim3(M), dim3(256), 0, st, x, H, ld, reinterpret_cast<const __nv_bfloat16*>(w), eps,
+                reinterpret_cast<__nv_bfloat16*>(y), reinterpret_cast<__nv_bfloat16*>(y_lo));
     return QTTS_OK;
 }
 
@@ -79,6 +79,8 @@ __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ table, int 
                                    const int64_t* __restrict__ ids, int id_ld, __nv_bfloat16* __restrict__ out,
                                    int out_ld) {
     const int r = blockIdx.x;
+    griddep_wait();
+    griddep_launch();
     int64_t id = ids[(size_t)r * id_ld];
     if (id < 0 || id >= V) id = 0;  // stay in bounds; callers pass sampled (valid) ids
     const uint4* src = reinterpret_cast<const uint4*>(table + (size_t)id * H);
@@ -94,6 +96,8 @@ __global__ void cp_stage0_rows_kernel(const __nv_bfloat16* __restrict__ hidden, 
                                       const int64_t* __restrict__ tok, int tok_ld, __nv_bfloat16* __restrict__ out,
                                       __nv_bfloat16* __restrict__ out_lo) {
     const int b = blockIdx.x;
+    griddep_wait();
+    griddep_launch();
     int64_t id = tok[(size_t)b * tok_ld];
     if (id < 0 || id >= V) id = 0;
     const uint4* h = reinterpret_cast<const uint4*>(hidden + (size_t)b * H);
@@ -121,6 +125,8 @@ __global__ void codec_sum_kernel(const int64_t* __restrict__ codes, int G, const
                                  float* __restrict__ next_x, const int32_t* __restrict__ row_map,
                                  int32_t* __restrict__ noise_step) {
     const int r = blockIdx.x;
+    griddep_wait();
+    griddep_launch();
     const size_t orow = row_map ? (size_t)row_map[r] : (size_t)r;  // output / text row
     if (noise_step && threadIdx.x == 0) noise_step[orow] += 1;     // this stream sampled one more frame
     extern __shared__ int64_t ids[];
@@ -156,6 +162,8 @@ __global__ void codec_sum_kernel(const int64_t* __restrict__ codes, int G, const
 // x[r] = x_in[row_map ? row_map[r] : r]  (the residual stream starts in fp32)
 __global__ void load_x_kernel(const float* __restrict__ x_in, float* __restrict__ x, int rows, int H,
                               const int32_t* __restrict__ row_map) {
+    griddep_wait();
+    griddep_launch();
     const size_t n = (size_t)rows * H;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
         const size_t r = i / H, c = i % H;
@@ -170,6 +178,8 @@ __global__ void load_x_kernel(const float* __restrict__ x_in, float* __restrict_
 __global__ void kv_copy_blocks_kernel(uint4* __restrict__ pool, size_t block_vec, const int32_t* __restrict__ src,
                                       const int32_t* __restrict__ dst, int num_blocks) {
     const int i = blockIdx.y;
+    griddep_wait();
+    griddep_launch();
     const int s = src[i], d = dst[i];
     if (s < 0 || d < 0 || s >= num_blocks || d >= num_blocks) return;
     const uint4* a = pool + (size_t)s * block_vec;
@@ -211,6 +221,8 @@ __global__ void kv_gather_kernel(const kv_t* __restrict__ pool, int L2, int Hkv,
 
 // row -> slot map for n_rows x n_new rows: row i*n_new+j belongs to slots[i]
 __global__ void expand_rows_kernel(const int32_t* __restrict__ slots, int n_rows, int n_new, int32_t* __restrict__ out) {
+    griddep_wait();
+    griddep_launch();
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n_rows * n_new; i += gridDim.x * blockDim.x)
         out[i] = slots[i / n_new];
 }
