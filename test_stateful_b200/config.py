@@ -67,6 +67,63 @@ class CodePredictorConfig:
 
 
 @dataclass
+class Code2WavConfig:
+    """Streaming code2wav decoder (scripts/export/code2wav_streaming.py:595-856).
+
+    Fixed by the reference: 16 codebooks of 2048 entries (1 semantic + 15
+    acoustic, codes clamped to 2047 — export_09_talker_code2wav_fused.py:146),
+    codebook_dim 512, latent 1024, hidden 1024, 8 layers, 16 kv heads x 64,
+    window 72, decoder_dim 1536, upsampling (2, 2) then strides (8, 5, 4, 3),
+    residual dilations (1, 3, 9) (code2wav_streaming.py:159-193,
+    docs/code2wav_state_size.md, tests/unit/test_conv1d_subpixel.py:98-104).
+    Not fixed by any reference file (the qwen_tts decoder is absent), chosen
+    here: RVQ vector width 256, SwiGLU MLP 3072, ConvNeXt expansion 4 with
+    GELU, RMSNorm eps 1e-5, LayerNorm eps 1e-6, RoPE theta 10000.
+    """
+
+    num_codebooks: int = 16
+    codebook_size: int = 2048
+    vq_dim: int = 256
+    codebook_dim: int = 512
+    latent_dim: int = 1024
+    hidden_size: int = 1024
+    num_layers: int = 8
+    num_heads: int = 16
+    kv_heads: int = 16
+    head_dim: int = 64
+    intermediate_size: int = 3072
+    window: int = 72
+    rms_eps: float = 1.0e-5
+    rope_theta: float = 10000.0
+    decoder_dim: int = 1536
+    upsample_ratios: tuple = (2, 2)
+    upsample_rates: tuple = (8, 5, 4, 3)
+    dilations: tuple = (1, 3, 9)
+    convnext_mult: int = 4
+    ln_eps: float = 1.0e-6
+
+    @property
+    def samples_per_frame(self) -> int:
+        n = 1
+        for r in tuple(self.upsample_ratios) + tuple(self.upsample_rates):
+            n *= r
+        return n
+
+    def block_dims(self):
+        """(in, out, stride) of the four decoder blocks."""
+        out = []
+        for b, s in enumerate(self.upsample_rates):
+            out.append((self.decoder_dim // (2 ** b), self.decoder_dim // (2 ** (b + 1)), s))
+        return out
+
+
+def tiny_code2wav_config() -> Code2WavConfig:
+    """Narrow channels, same strides/kernels/window: the fixture configuration."""
+    return Code2WavConfig(vq_dim=16, codebook_dim=32, latent_dim=64, hidden_size=64, num_layers=2, num_heads=4,
+                          kv_heads=4, head_dim=16, intermediate_size=128, decoder_dim=96, convnext_mult=2)
+
+
+@dataclass
 class PagedPoolConfig:
     """Geometry of the paged talker KV pool (no counterpart in the reference)."""
 

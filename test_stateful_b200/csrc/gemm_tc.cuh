@@ -374,12 +374,34 @@ inline int make_map_bf16(CUtensorMap* map, const void* ptr, uint64_t rows, uint6
 
 inline int pick_bn(int M) { return M <= 64 ? 64 : 128; }
 
+// Tuning knobs read once from the environment (defaults are the measured best):
+// QTTS_GEMM_STAGES (pipeline depth of the hi/lo kernel at BN = 64) and
+// QTTS_GEMM_MAX_SPLITS (largest split-K cluster), QTTS_GEMM_CTAS_PER_SM (split-K target).
+inline int env_int(const char* name, int dflt) {
+    const char* v = getenv(name);
+    return (v && *v) ? atoi(v) : dflt;
+}
+inline int gemm_stages() {
+    static const int s = env_int("QTTS_GEMM_STAGES", 3);
+    return s;
+}
+inline int gemm_max_splits() {
+    static const int s = env_int("QTTS_GEMM_MAX_SPLITS", 8);
+    return s;
+}
+inline int gemm_ctas_per_sm() {
+    static const int s = env_int("QTTS_GEMM_CTAS_PER_SM", 2);
+    return s;
+}
+
 inline int pick_splits(int N, int M, int K, int BN) {
     const int tiles = (N / 128) * ceil_div(M, BN);
     const int kb = K / 64;
-    const int target = 2 * num_sms();
+    const int target = gemm_ctas_per_sm() * num_sms();
     int s = 1;
-    while (s * 2 <= 8 && tiles * s * 2 <= target + target / 5 && kb / (s * 2) >= 2 && BN % (s * 2) == 0) s *= 2;
+    while (s * 2 <= gemm_max_splits() && tiles * s * 2 <= target + target / 5 && kb / (s * 2) >= 2 &&
+           BN % (s * 2) == 0)
+        s *= 2;
     return s;
 }
 
@@ -455,7 +477,13 @@ inline int gemm_run(GemmPlan g, int M, cudaStream_t st, void* out = nullptr) {
     g.p.splits = pick_splits(g.p.N, M, g.p.K, bn);
     if (out) g.p.out = out;
     if (g.split) {
-        if (bn == 64) return launch_gemm_t<64, 3, true>(g.mw, g.mx64, g.mlo64, g.p, st);
+        if (bn == 64) {
+            switch (gemm_stages()) {
+                case 4: return launch_gemm_t<64, 4, true>(g.mw, g.mx64, g.mlo64, g.p, st);
+                case 6: return launch_gemm_t<64, 6, true>(g.mw, g.mx64, g.mlo64, g.p, st);
+                default: return launch_gemm_t<64, 3, true>(g.mw, g.mx64, g.mlo64, g.p, st);
+            }
+        }
         return launch_gemm_t<128, 3, true>(g.mw, g.mx128, g.mlo128, g.p, st);
     }
     if (bn == 64) return launch_gemm_t<64, 4, false>(g.mw, g.mx64, g.mx64, g.p, st);

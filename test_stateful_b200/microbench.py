@@ -1,0 +1,103 @@
+"""Single-kernel timing on small cases that still exceed L2 (126 MB).
+
+    python -m test_stateful_b200.microbench attention [--rows 64] [--ctx-mean 520] [--launches 50]
+    python -m test_stateful_b200.microbench gemm [--n 12288] [--k 2048] [--m 64] [--launches 50]
+
+Prints one JSON line with the mean launch time (CUDA events) and the
+achieved bandwidth over the kernel's algorithmic bytes:
+* attention: K+V bytes of every visible key of one layer (fp16) + q/out;
+* gemm: the weight bytes (bf16) + activation hi/lo operands + fp32 output.
+Inputs cycle through enough copies that every launch reads from HBM.  The
+same command is the small case for an ``ncu --set full`` capture.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from . import _lib, ops
+
+
+def bench_attention(rows: int, ctx_mean: int, launches: int, layers: int = 4, seed: int = 0):
+    dev = "cuda"
+    g = torch.Generator().manual_seed(seed)
+    lo, hi = max(1, ctx_mean // 2), ctx_mean * 3 // 2
+    ctx = torch.randint(lo, hi + 1, (rows,), generator=g)
+    nblk = [-(-int(c) // 16) for c in ctx]
+    mbps = max(nblk)
+    total = sum(nblk)
+    kv = torch.randn(total, layers, 2, 8, 16, 128, generator=g).to(torch.float16).to(dev)
+    table = torch.full((rows, mbps), -1, dtype=torch.int32)
+    perm = torch.randperm(total, generator=g)
+    off = 0
+    for r, n in enumerate(nblk):
+        table[r, :n] = perm[off:off + n].to(torch.int32)
+        off += n
+    table = table.to(dev)
+    q = torch.randn(rows, 16, 128, generator=g).to(dev)
+    row_slot = torch.arange(rows, dtype=torch.int32, device=dev)
+    row_ctx = ctx.to(torch.int32).to(dev)
+    out = torch.empty(rows, 16 * 128, device=dev, dtype=torch.bfloat16)
+    out_lo = torch.empty_like(out)
+    max_ctx = mbps * 16
+    for i in range(3):
+        ops.paged_attention(q, kv, i % layers, table, row_slot, row_ctx, max_ctx, out=out, out_lo=out_lo)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(launches):
+        ops.paged_attention(q, kv, i % layers, table, row_slot, row_ctx, max_ctx, out=out, out_lo=out_lo)
+    e1.record()
+    torch.cuda.synchronize()
+    sec = e0.elapsed_time(e1) / 1e3 / launches
+    algo = int(ctx.sum()) * 2 * 8 * 128 * 2 + rows * 16 * 128 * (4 + 4)
+    return {"kernel": "paged_attn_kernel<128>", "rows": rows, "ctx_sum": int(ctx.sum()), "launch_us": sec * 1e6,
+            "algorithmic_bytes": algo, "achieved_gbs": algo / sec / 1e9}
+
+
+def bench_gemm(n: int, k: int, m: int, launches: int, seed: int = 0):
+    dev = "cuda"
+    g = torch.Generator(device=dev).manual_seed(seed)
+    copies = max(2, -(-300_000_000 // (n * k * 2)))  # > 2x L2 of distinct weights
+    ws = [torch.randn(n, k, generator=g, device=dev).mul_(0.02).to(torch.bfloat16) for _ in range(copies)]
+    x = torch.randn(m, k, generator=g, device=dev)
+    hi, lo = ops.split_hilo(x)
+    out = torch.empty(m, n, device=dev)
+    for i in range(3):
+        ops.gemm(hi, ws[i % copies], _lib.EPI_F32, out=out, x_lo=lo)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(launches):
+        ops.gemm(hi, ws[i % copies], _lib.EPI_F32, out=out, x_lo=lo)
+    e1.record()
+    torch.cuda.synchronize()
+    sec = e0.elapsed_time(e1) / 1e3 / launches
+    algo = n * k * 2 + m * k * 4 + m * n * 4
+    return {"kernel": "gemm_tc_kernel<64,3,split>", "n": n, "k": k, "m": m, "launch_us": sec * 1e6,
+            "algorithmic_bytes": algo, "achieved_gbs": algo / sec / 1e9,
+            "tflops": 2 * 2 * m * n * k / sec / 1e12}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("what", choices=["attention", "gemm"])
+    ap.add_argument("--rows", type=int, default=64)
+    ap.add_argument("--ctx-mean", type=int, default=520)
+    ap.add_argument("--n", type=int, default=12288)
+    ap.add_argument("--k", type=int, default=2048)
+    ap.add_argument("--m", type=int, default=64)
+    ap.add_argument("--launches", type=int, default=50)
+    a = ap.parse_args()
+    if a.what == "attention":
+        r = bench_attention(a.rows, a.ctx_mean, a.launches)
+    else:
+        r = bench_gemm(a.n, a.k, a.m, a.launches)
+    print(json.dumps(r))
+
+
+if __name__ == "__main__":
+    main()

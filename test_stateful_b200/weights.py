@@ -79,11 +79,101 @@ def cp_param_specs(cfg: CodePredictorConfig) -> Iterator[Tuple[str, tuple, str]]
         yield f"cp.lm_head.{s}.weight", (cfg.vocab_size, H), "linear"
 
 
-def _make(name: str, shape: tuple, kind: str, seed: int, device, dtype) -> torch.Tensor:
+def code2wav_param_specs(cfg) -> Iterator[Tuple[str, tuple, object]]:
+    """Decoder tensors, named after the module paths code2wav_streaming.py reads
+    (``decoder.quantizer.rvq_first``, ``decoder.pre_conv``, ``decoder.pre_transformer``,
+    ``decoder.upsample[i]``, ``decoder.decoder[j]``).  Conv weights use the
+    torch layouts (Conv1d ``[out, in, k]``, ConvTranspose1d ``[in, out, k]``) and
+    a 1/sqrt(fan-in) scale so the signal stays O(1) through the stack; the last
+    conv is scaled down so the waveform sits inside the [-1, 1] clamp."""
+    V, d, cd, L, H = cfg.codebook_size, cfg.vq_dim, cfg.codebook_dim, cfg.latent_dim, cfg.hidden_size
+    hd, I = cfg.head_dim, cfg.intermediate_size
+
+    def conv(out_c, in_c, k, gain=1.0):
+        return ("normal", gain / (in_c * k) ** 0.5, 0.0)
+
+    def small(std):
+        return ("normal", std, 0.0)
+
+    yield "c2w.rvq_first.codebook.0", (V, d), small(1.0)
+    for i in range(cfg.num_codebooks - 1):
+        yield f"c2w.rvq_rest.codebook.{i}", (V, d), small(1.0)
+    for part in ("rvq_first", "rvq_rest"):
+        yield f"c2w.{part}.output_proj.weight", (cd, d, 1), conv(cd, d, 1)
+        yield f"c2w.{part}.output_proj.bias", (cd,), small(0.02)
+    yield "c2w.pre_conv.weight", (L, cd, 3), conv(L, cd, 3)
+    yield "c2w.pre_conv.bias", (L,), small(0.02)
+    p = "c2w.pre_transformer."
+    yield p + "input_proj.weight", (H, L), conv(H, L, 1)
+    yield p + "input_proj.bias", (H,), small(0.02)
+    for i in range(cfg.num_layers):
+        q = f"{p}layers.{i}."
+        yield q + "input_layernorm.weight", (H,), "norm"
+        yield q + "self_attn.q_proj.weight", (cfg.num_heads * hd, H), conv(0, H, 1)
+        yield q + "self_attn.k_proj.weight", (cfg.kv_heads * hd, H), conv(0, H, 1)
+        yield q + "self_attn.v_proj.weight", (cfg.kv_heads * hd, H), conv(0, H, 1)
+        yield q + "self_attn.o_proj.weight", (H, cfg.num_heads * hd), conv(0, cfg.num_heads * hd, 1)
+        yield q + "self_attn.q_norm.weight", (hd,), "norm"
+        yield q + "self_attn.k_norm.weight", (hd,), "norm"
+        yield q + "self_attn_layer_scale.scale", (H,), ("normal", 0.02, 0.1)
+        yield q + "post_attention_layernorm.weight", (H,), "norm"
+        yield q + "mlp.gate_proj.weight", (I, H), conv(0, H, 1)
+        yield q + "mlp.up_proj.weight", (I, H), conv(0, H, 1)
+        yield q + "mlp.down_proj.weight", (H, I), conv(0, I, 1)
+        yield q + "mlp_layer_scale.scale", (H,), ("normal", 0.02, 0.1)
+    yield p + "norm.weight", (H,), "norm"
+    yield p + "output_proj.weight", (L, H), conv(L, H, 1)
+    yield p + "output_proj.bias", (L,), small(0.02)
+    for i, _ in enumerate(cfg.upsample_ratios):
+        u = f"c2w.upsample.{i}."
+        yield u + "transconv.weight", (L, L, 2), conv(L, L, 1)
+        yield u + "transconv.bias", (L,), small(0.02)
+        yield u + "convnext.dwconv.weight", (L, 1, 7), conv(L, 1, 7)
+        yield u + "convnext.dwconv.bias", (L,), small(0.02)
+        yield u + "convnext.norm.weight", (L,), "norm"
+        yield u + "convnext.norm.bias", (L,), small(0.02)
+        yield u + "convnext.pwconv1.weight", (cfg.convnext_mult * L, L), conv(0, L, 1)
+        yield u + "convnext.pwconv1.bias", (cfg.convnext_mult * L,), small(0.02)
+        yield u + "convnext.pwconv2.weight", (L, cfg.convnext_mult * L), conv(0, cfg.convnext_mult * L, 1)
+        yield u + "convnext.pwconv2.bias", (L,), small(0.02)
+        yield u + "convnext.gamma", (L,), ("normal", 0.02, 0.1)
+    D0 = cfg.decoder_dim
+    yield "c2w.decoder.0.weight", (D0, L, 7), conv(D0, L, 7)
+    yield "c2w.decoder.0.bias", (D0,), small(0.02)
+    for b, (cin, cout, s) in enumerate(cfg.block_dims()):
+        k = f"c2w.decoder.{1 + b}."
+        yield k + "snake.alpha", (cin,), small(0.1)
+        yield k + "snake.beta", (cin,), small(0.1)
+        yield k + "transconv.weight", (cin, cout, 2 * s), conv(cout, cin, 2)
+        yield k + "transconv.bias", (cout,), small(0.02)
+        for j, _ in enumerate(cfg.dilations):
+            r = f"{k}res.{j}."
+            yield r + "act1.alpha", (cout,), small(0.1)
+            yield r + "act1.beta", (cout,), small(0.1)
+            yield r + "conv1.weight", (cout, cout, 7), conv(cout, cout, 7, 0.5)
+            yield r + "conv1.bias", (cout,), small(0.02)
+            yield r + "act2.alpha", (cout,), small(0.1)
+            yield r + "act2.beta", (cout,), small(0.1)
+            yield r + "conv2.weight", (cout, cout, 1), conv(cout, cout, 1, 0.5)
+            yield r + "conv2.bias", (cout,), small(0.02)
+    last = cfg.block_dims()[-1][1]
+    yield "c2w.decoder.5.alpha", (last,), small(0.1)
+    yield "c2w.decoder.5.beta", (last,), small(0.1)
+    yield "c2w.decoder.6.weight", (1, last, 7), conv(1, last, 7, 0.1)
+    yield "c2w.decoder.6.bias", (1,), small(0.01)
+
+
+def make_code2wav_weights(cfg, seed: int, device="cpu", dtype=torch.bfloat16):
+    return make_weights(code2wav_param_specs(cfg), seed, device, dtype)
+
+
+def _make(name: str, shape: tuple, kind, seed: int, device, dtype) -> torch.Tensor:
     gen = torch.Generator(device=device)
     gen.manual_seed(_tensor_seed(seed, name))
     t = torch.randn(shape, generator=gen, device=device, dtype=torch.float32)
-    if kind == "linear":
+    if isinstance(kind, tuple):  # ("normal", std, mean)
+        t.mul_(kind[1]).add_(kind[2])
+    elif kind == "linear":
         t.mul_(LINEAR_STD)
     elif kind == "embed":
         t.mul_(EMBED_STD)

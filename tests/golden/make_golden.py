@@ -365,6 +365,256 @@ def make_pool_ops(ref_mods, out):
     np.savez_compressed(out, **payload)
 
 
+# ----------------------------------------------------------------------------
+# code2wav: stand-in decoder tree for scripts/export/code2wav_streaming.py
+# ----------------------------------------------------------------------------
+
+class SnakeBeta(nn.Module):
+    """The wrapper patches every module of this class NAME (code2wav_streaming.py:562-592)."""
+
+    def __init__(self, alpha, beta):
+        super().__init__()
+        self.alpha = nn.Parameter(alpha.clone())
+        self.beta = nn.Parameter(beta.clone())
+
+    def forward(self, x):
+        a = torch.exp(self.alpha.view(1, -1, 1))
+        s = torch.sin(x * a)
+        return x + s * s * torch.exp(-self.beta.view(1, -1, 1))
+
+
+class _CausalConv(nn.Module):
+    """``.conv`` and a left ``.padding`` are what streaming_causal_conv reads."""
+
+    def __init__(self, w, b, dilation=1, groups=1):
+        super().__init__()
+        cout, cin_g, k = w.shape
+        self.conv = nn.Conv1d(cin_g * groups, cout, k, dilation=dilation, groups=groups)
+        self.conv.weight.data.copy_(w)
+        self.conv.bias.data.copy_(b)
+        self.padding = (k - 1) * dilation
+
+    def forward(self, x):
+        return self.conv(nn.functional.pad(x, (self.padding, 0)))
+
+
+class _CausalTransConv(nn.Module):
+    def __init__(self, w, b, stride):
+        super().__init__()
+        cin, cout, k = w.shape
+        self.conv = nn.ConvTranspose1d(cin, cout, k, stride=stride)
+        self.conv.weight.data.copy_(w)
+        self.conv.bias.data.copy_(b)
+        self.right_pad = k - stride
+
+    def forward(self, x):
+        y = self.conv(x)
+        return y[..., :-self.right_pad] if self.right_pad > 0 else y
+
+
+class _Scale(nn.Module):
+    def __init__(self, s):
+        super().__init__()
+        self.scale = nn.Parameter(s.clone())
+
+    def forward(self, x):
+        return self.scale * x
+
+
+class _Codebook(nn.Module):
+    """embedding = embedding_sum / cluster_usage.clamp(min=epsilon) (code2wav_streaming.py:227-229)."""
+
+    def __init__(self, table):
+        super().__init__()
+        self.register_buffer("embedding_sum", table * 2.0)
+        self.register_buffer("cluster_usage", torch.full((table.shape[0],), 2.0))
+        self.epsilon = 1e-5
+
+    def decode(self, codes):
+        emb = self.embedding_sum / self.cluster_usage.clamp(min=self.epsilon).unsqueeze(1)
+        return nn.functional.embedding(codes, emb).transpose(1, 2)
+
+
+def _linear(W, name, bias=False):
+    w = W[name + ".weight"]
+    m = nn.Linear(w.shape[1], w.shape[0], bias=bias)
+    m.weight.data.copy_(w.reshape(w.shape[0], w.shape[1]))
+    if bias:
+        m.bias.data.copy_(W[name + ".bias"])
+    return m
+
+
+def build_code2wav_standin(c, W):
+    """A module tree with exactly the attributes Code2WavStreamingWrapper reads
+    (quantizer.rvq_*.{n_q, vq.layers[i]._codebook, output_proj}, pre_conv,
+    pre_transformer.{input_proj, rotary_emb, layers, norm, output_proj},
+    upsample[i] = (transconv, convnext), decoder[0..6], config)."""
+    import types
+    from transformers.models.qwen3.modeling_qwen3 import Qwen3RMSNorm
+
+    def rvq(part, tables):
+        r = nn.Module()
+        r.n_q = len(tables)
+        r.vq = nn.Module()
+        r.vq.layers = nn.ModuleList()
+        for t in tables:
+            layer = nn.Module()
+            layer._codebook = _Codebook(t)
+            r.vq.layers.append(layer)
+        w = W[f"c2w.{part}.output_proj.weight"]
+        r.output_proj = nn.Conv1d(w.shape[1], w.shape[0], 1)
+        r.output_proj.weight.data.copy_(w)
+        r.output_proj.bias.data.copy_(W[f"c2w.{part}.output_proj.bias"])
+        return r
+
+    dec = nn.Module()
+    dec.config = types.SimpleNamespace(
+        codebook_dim=c.codebook_dim, latent_dim=c.latent_dim, decoder_dim=c.decoder_dim,
+        num_key_value_heads=c.kv_heads, num_attention_heads=c.num_heads, head_dim=c.head_dim,
+        hidden_size=c.hidden_size, num_hidden_layers=c.num_layers, _attn_implementation="eager")
+    q = nn.Module()
+    q.n_q_semantic, q.n_q_acoustic = 1, c.num_codebooks - 1
+    q.rvq_first = rvq("rvq_first", [W["c2w.rvq_first.codebook.0"]])
+    q.rvq_rest = rvq("rvq_rest", [W[f"c2w.rvq_rest.codebook.{i}"] for i in range(c.num_codebooks - 1)])
+    dec.quantizer = q
+    dec.pre_conv = _CausalConv(W["c2w.pre_conv.weight"], W["c2w.pre_conv.bias"])
+
+    p = "c2w.pre_transformer."
+    pt = nn.Module()
+    pt.input_proj = _linear(W, p + "input_proj", bias=True)
+    pt.rotary_emb = nn.Module()
+    pt.rotary_emb.register_buffer(
+        "inv_freq", 1.0 / (c.rope_theta ** (torch.arange(0, c.head_dim, 2, dtype=torch.int64).float() / c.head_dim)))
+    pt.rotary_emb.attention_scaling = 1.0
+    pt.layers = nn.ModuleList()
+    for i in range(c.num_layers):
+        lp = f"{p}layers.{i}."
+        layer = nn.Module()
+        layer.input_layernorm = Qwen3RMSNorm(c.hidden_size, eps=c.rms_eps)
+        layer.input_layernorm.weight.data.copy_(W[lp + "input_layernorm.weight"])
+        layer.post_attention_layernorm = Qwen3RMSNorm(c.hidden_size, eps=c.rms_eps)
+        layer.post_attention_layernorm.weight.data.copy_(W[lp + "post_attention_layernorm.weight"])
+        a = nn.Module()
+        for n in ("q_proj", "k_proj", "v_proj", "o_proj"):
+            setattr(a, n, _linear(W, lp + "self_attn." + n))
+        a.q_norm = Qwen3RMSNorm(c.head_dim, eps=c.rms_eps)
+        a.q_norm.weight.data.copy_(W[lp + "self_attn.q_norm.weight"])
+        a.k_norm = Qwen3RMSNorm(c.head_dim, eps=c.rms_eps)
+        a.k_norm.weight.data.copy_(W[lp + "self_attn.k_norm.weight"])
+        a.head_dim, a.layer_idx = c.head_dim, i
+        a.num_key_value_groups = c.num_heads // c.kv_heads
+        a.scaling = c.head_dim ** -0.5
+        layer.self_attn = a
+        layer.self_attn_layer_scale = _Scale(W[lp + "self_attn_layer_scale.scale"])
+        layer.mlp_layer_scale = _Scale(W[lp + "mlp_layer_scale.scale"])
+        mlp = nn.Module()
+        for n in ("gate_proj", "up_proj", "down_proj"):
+            setattr(mlp, n, _linear(W, lp + "mlp." + n))
+        mlp.forward = types.MethodType(
+            lambda self, x: self.down_proj(nn.functional.silu(self.gate_proj(x)) * self.up_proj(x)), mlp)
+        layer.mlp = mlp
+        pt.layers.append(layer)
+    pt.norm = Qwen3RMSNorm(c.hidden_size, eps=c.rms_eps)
+    pt.norm.weight.data.copy_(W[p + "norm.weight"])
+    pt.output_proj = _linear(W, p + "output_proj", bias=True)
+    dec.pre_transformer = pt
+
+    dec.upsample = nn.ModuleList()
+    for i, s in enumerate(c.upsample_ratios):
+        u = f"c2w.upsample.{i}."
+        tconv = _CausalTransConv(W[u + "transconv.weight"], W[u + "transconv.bias"], s)
+        cn = nn.Module()
+        cn.dwconv = _CausalConv(W[u + "convnext.dwconv.weight"], W[u + "convnext.dwconv.bias"],
+                                groups=c.latent_dim)
+        cn.norm = nn.LayerNorm(c.latent_dim, eps=c.ln_eps)
+        cn.norm.weight.data.copy_(W[u + "convnext.norm.weight"])
+        cn.norm.bias.data.copy_(W[u + "convnext.norm.bias"])
+        cn.pwconv1 = _linear(W, u + "convnext.pwconv1", bias=True)
+        cn.act = nn.GELU()
+        cn.pwconv2 = _linear(W, u + "convnext.pwconv2", bias=True)
+        cn.gamma = nn.Parameter(W[u + "convnext.gamma"].clone())
+        dec.upsample.append(nn.ModuleList([tconv, cn]))
+
+    d = nn.ModuleList([_CausalConv(W["c2w.decoder.0.weight"], W["c2w.decoder.0.bias"])])
+    for b, (cin, cout, s) in enumerate(c.block_dims()):
+        k = f"c2w.decoder.{1 + b}."
+        blk = nn.Module()
+        mods = [SnakeBeta(W[k + "snake.alpha"], W[k + "snake.beta"]),
+                _CausalTransConv(W[k + "transconv.weight"], W[k + "transconv.bias"], s)]
+        for j, dil in enumerate(c.dilations):
+            r = f"{k}res.{j}."
+            ru = nn.Module()
+            ru.act1 = SnakeBeta(W[r + "act1.alpha"], W[r + "act1.beta"])
+            ru.conv1 = _CausalConv(W[r + "conv1.weight"], W[r + "conv1.bias"], dilation=dil)
+            ru.act2 = SnakeBeta(W[r + "act2.alpha"], W[r + "act2.beta"])
+            ru.conv2 = _CausalConv(W[r + "conv2.weight"], W[r + "conv2.bias"])
+            mods.append(ru)
+        blk.block = nn.ModuleList(mods)
+        d.append(blk)
+    d.append(SnakeBeta(W["c2w.decoder.5.alpha"], W["c2w.decoder.5.beta"]))
+    d.append(_CausalConv(W["c2w.decoder.6.weight"], W["c2w.decoder.6.bias"]))
+    dec.decoder = d
+    return dec.eval()
+
+
+def make_code2wav(ref: Path, out, seed=5, steps=78, starts=(0, 9)):
+    """Batched T=1 streaming decode the way the fused step drives the wrapper:
+    per-slot delta KV appended and trimmed to window-1 frames (executor.py:68-79),
+    left-padded past KV with a -inf bias on the padding (executor.py:1374-1441),
+    cache_position = each slot's frame index (executor.py:1298-1301)."""
+    sys.path.insert(0, str(ref / "scripts" / "export"))
+    import code2wav_streaming as c2ws
+    from test_stateful_b200.config import tiny_code2wav_config
+    c = tiny_code2wav_config()
+    W = wmod.to_fp32(wmod.make_code2wav_weights(c, seed))
+    dec = build_code2wav_standin(c, W)
+    wrap = c2ws.Code2WavStreamingWrapper(dec, window_size=c.window, emit_delta_kv=True).eval()
+    shapes = c2ws.get_initial_state_shapes(dec, batch_size=1)
+    conv_shapes = [s for n, s in shapes if n.startswith("conv_state")]
+    trans_shapes = [s for n, s in shapes if n.startswith("transconv")]
+    n_slots = len(starts)
+    g = torch.Generator().manual_seed(seed)
+    codes = torch.randint(0, c.codebook_size, (steps, n_slots, c.num_codebooks), generator=g)
+    kv = [None] * n_slots                      # [1, 2L, H, S, hd] past per slot
+    conv = [[torch.zeros(s) for s in conv_shapes] for _ in range(n_slots)]
+    trans = [[torch.zeros(s) for s in trans_shapes] for _ in range(n_slots)]
+    frame = [0] * n_slots
+    wav = np.zeros((steps, n_slots, c.samples_per_frame), np.float32)
+    active = np.zeros((steps, n_slots), bool)
+    max_past = c.window - 1
+    L2 = 2 * c.num_layers
+    with torch.no_grad():
+        for t in range(steps):
+            act = [i for i in range(n_slots) if t >= starts[i]]
+            lens = [0 if kv[i] is None else min(kv[i].shape[3], max_past) for i in act]
+            P = max(1, max(lens))
+            bias = torch.zeros(len(act), 1, 1, P + 1)
+            past = []
+            for bi, (i, sl) in enumerate(zip(act, lens)):
+                bias[bi, :, :, :P - sl] = float("-inf")
+                k = kv[i] if kv[i] is not None else torch.zeros(1, L2, c.kv_heads, 0, c.head_dim)
+                past.append(nn.functional.pad(k[:, :, :, -max_past:], (0, 0, P - sl, 0)))
+            past = torch.cat(past, 0)
+            states = [past[:, j] for j in range(L2)]
+            states += [torch.cat([conv[i][j] for i in act], 0) for j in range(len(conv_shapes))]
+            states += [torch.cat([trans[i][j] for i in act], 0) for j in range(len(trans_shapes))]
+            cpos = torch.tensor([[float(frame[i])] for i in act])
+            outs = wrap(codes[t, act].unsqueeze(-1), cpos, bias, *states)
+            delta = torch.stack(outs[1:1 + L2], dim=1)
+            nc = outs[1 + L2:1 + L2 + len(conv_shapes)]
+            nt = outs[1 + L2 + len(conv_shapes):]
+            for bi, i in enumerate(act):
+                wav[t, i] = outs[0][bi].numpy()
+                active[t, i] = True
+                d = delta[bi:bi + 1]
+                kv[i] = d if kv[i] is None else torch.cat([kv[i], d], 3)[:, :, :, -max_past:]
+                conv[i] = [x[bi:bi + 1].clone() for x in nc]
+                trans[i] = [x[bi:bi + 1].clone() for x in nt]
+                frame[i] += 1
+    np.savez_compressed(out, codes=codes.numpy().astype(np.int32), active=active, wav=wav,
+                        seed=np.int64(seed), starts=np.asarray(starts, np.int32))
+
+
 def make_seeds(out):
     """Per-(session, segment) sampling seeds from engine/backend/executor.py:45-52."""
     from engine.backend import executor as ref_executor
@@ -391,6 +641,10 @@ def main():
     if args.only == "seeds":
         make_seeds(HERE / "seeds.npz")
         return
+    if args.only == "code2wav":
+        make_code2wav(args.reference.resolve(), HERE / "code2wav_tiny.npz")
+        return
+    make_code2wav(args.reference.resolve(), HERE / "code2wav_tiny.npz")
     make_seeds(HERE / "seeds.npz")
     t0 = time.time()
     make_fused_tiny(ref_mods, HERE / "fused_tiny.npz")

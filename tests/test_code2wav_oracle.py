@@ -1,0 +1,67 @@
+"""Pin the code2wav oracle against the reference's own streaming wrapper.
+
+``tests/golden/code2wav_tiny.npz`` was written by ``make_golden.py`` running
+``Code2WavStreamingWrapper`` (scripts/export/code2wav_streaming.py:595-856)
+batched at T=1 the way the fused step drives it: two slots that start 9
+steps apart (ragged past lengths, -inf bias on the left padding), 78 steps so
+the first slot's KV window (72) wraps, per-slot conv/transconv state carried
+between steps.
+"""
+
+import os
+
+import numpy as np
+import torch
+
+from oracle import code2wav as C
+from test_stateful_b200 import weights as wmod
+from test_stateful_b200.config import Code2WavConfig, tiny_code2wav_config
+
+from .conftest import GOLDEN
+
+
+def test_code2wav_oracle_matches_reference_stream():
+    z = np.load(os.path.join(GOLDEN, "code2wav_tiny.npz"))
+    cfg = tiny_code2wav_config()
+    W = wmod.to_fp32(wmod.make_code2wav_weights(cfg, int(z["seed"])))
+    codes, active, wav = z["codes"], z["active"], z["wav"]
+    assert wav.shape[-1] == cfg.samples_per_frame == 1920
+    for s in range(codes.shape[1]):
+        st = C.Code2WavState(cfg)
+        n = 0
+        for t in range(codes.shape[0]):
+            if not active[t, s]:
+                continue
+            w = C.decode_chunk(W, cfg, torch.from_numpy(codes[t, s]).view(-1, 1), st).numpy()
+            np.testing.assert_allclose(w, wav[t, s], rtol=0, atol=2e-5)
+            n += 1
+        assert n == int(active[:, s].sum())
+        if n > cfg.window:
+            assert st.kv[0][0].shape[2] == cfg.window - 1  # the window wrapped
+
+
+def test_code2wav_chunk_equals_frames():
+    """A T-frame chunk through the oracle equals T single-frame steps (the
+    chunked cfg4 path and the T=1 fused path produce the same waveform)."""
+    cfg = tiny_code2wav_config()
+    W = wmod.to_fp32(wmod.make_code2wav_weights(cfg, 3))
+    g = torch.Generator().manual_seed(0)
+    codes = torch.randint(0, cfg.codebook_size, (cfg.num_codebooks, 6), generator=g)
+    a, b = C.Code2WavState(cfg), C.Code2WavState(cfg)
+    chunk = C.decode_chunk(W, cfg, codes, a)
+    frames = torch.cat([C.decode_chunk(W, cfg, codes[:, t:t + 1], b) for t in range(6)])
+    torch.testing.assert_close(chunk, frames, rtol=0, atol=2e-5)
+
+
+def test_code2wav_state_shapes_match_reference_layout():
+    """17 conv + 4 transconv states with the shapes of get_initial_state_shapes
+    (code2wav_streaming.py:159-193) at the full configuration."""
+    cfg = Code2WavConfig()
+    st = C.Code2WavState(cfg)
+    conv = [tuple(t.shape[1:]) for t in st.conv]
+    assert conv[:4] == [(512, 2), (1024, 6), (1024, 6), (1024, 6)]
+    assert conv[4:7] == [(768, 6), (768, 18), (768, 54)]
+    assert conv[13:16] == [(96, 6), (96, 18), (96, 54)]
+    assert conv[16] == (96, 6)
+    assert [tuple(t.shape[1:]) for t in st.trans] == [(768, 8), (384, 5), (192, 4), (96, 3)]
+    assert cfg.samples_per_frame == 1920
