@@ -305,6 +305,92 @@ typedef struct qtts_step_io {
 
 int qtts_engine_step(qtts_engine* e, qtts_step_io* io, qtts_stream_t stream);
 
+/* ---------------------------------------------------------------------------
+ * Streaming code2wav decoder.  Replaces Code2WavStreamingWrapper.forward
+ * (scripts/export/code2wav_streaming.py:708-810) as the fused graph runs it
+ * at T = 1 frame per step (export_09_talker_code2wav_fused.py:145-160): codes
+ * clamped to [0, codebook_size) -> RVQ tables -> causal pre_conv (k3) -> window
+ * transformer -> 2 x [transposed conv x2 + ConvNeXt] -> conv k7 -> 4 x
+ * [SnakeBeta, transposed conv (2s, s), 3 residual units k7 d1/3/9] -> SnakeBeta
+ * -> conv k7 -> clamp(-1, 1).  The streaming state (window KV, conv left
+ * contexts, transposed-conv overlaps, frame counter) lives on the device,
+ * indexed by pool slot; the transposed-conv overlap is kept as the previous
+ * input frame, from which the reference's bias-free overlap tail
+ * (code2wav_streaming.py:118-124) is recomputed inside the GEMM.
+ *
+ * Weights are packed by the host (test_stateful_b200/runtime/code2wav.py):
+ * bf16 unless noted; GEMM weights [N_pad][K_pad] zero-padded to N % 128 == 0
+ * and K % 64 == 0; a conv [out][in][k] becomes [out][k*in] (tap-major); a
+ * transposed conv (stride s, kernel 2s) becomes rows (phase p, out channel)
+ * over [x(i-1) | x(i)] with taps w[:, :, p+s] and w[:, :, p]. */
+typedef struct qtts_c2w_desc {
+    int32_t num_codebooks, codebook_size, codebook_dim, latent, hidden, layers, heads, head_dim, inter;
+    int32_t window, decoder_dim, convnext_dim, max_slots, max_frames;
+    int32_t up_ratio[2];
+    int32_t rates[4];
+    int32_t dilations[3];
+    float rms_eps, ln_eps;
+    const float* rvq_tables;      /* fp32 [num_codebooks][codebook_size][codebook_dim]: codebook rows
+                                     through output_proj, both biases folded into tables 0 and 1 */
+    const void* w_pre_conv;       /* [latent][pad64(3*codebook_dim)] */
+    const void* b_pre_conv;       /* [latent] */
+    const void* w_in_proj;        /* [hidden][latent] */
+    const void* b_in_proj;
+    const void* w_in_norm;        /* [layers][hidden] */
+    const void* w_qkv;            /* [layers][3*heads*head_dim][hidden] */
+    const void* w_q_norm;         /* [layers][head_dim] */
+    const void* w_k_norm;
+    const void* w_o;              /* [layers][hidden][heads*head_dim] */
+    const void* attn_scale;       /* [layers][hidden] layer scale */
+    const void* w_post_norm;
+    const void* w_gate_up;        /* [layers][2*inter][hidden], 64-row interleave gate/up */
+    const void* w_down;           /* [layers][hidden][inter] */
+    const void* mlp_scale;        /* [layers][hidden] */
+    const void* w_final_norm;     /* [hidden] */
+    const void* w_out_proj;       /* [latent][hidden] */
+    const void* b_out_proj;
+    const float* rope_cos;        /* [max_frames][head_dim/2] (theta of the decoder) */
+    const float* rope_sin;
+    const void* up_w[2];          /* [2*latent][latent] (phase-major rows) */
+    const void* up_b[2];          /* [2*latent] */
+    const float* dw_w[2];         /* fp32 [latent][7] depthwise */
+    const float* dw_b[2];
+    const float* ln_w[2];         /* fp32 [latent] */
+    const float* ln_b[2];
+    const void* pw1_w[2];         /* [convnext_dim][latent] */
+    const void* pw1_b[2];
+    const void* pw2_w[2];         /* [latent][convnext_dim] */
+    const void* pw2_b[2];
+    const void* gamma[2];         /* [latent] */
+    const void* w_conv0;          /* [decoder_dim][7*latent] */
+    const void* b_conv0;
+    const float* blk_snake[4];    /* fp32 [2][cin]: exp(alpha), exp(-beta) */
+    const void* blk_tw[4];        /* [pad128(s*cout)][pad64(2*cin)] */
+    const void* blk_tb[4];        /* [pad128(s*cout)] */
+    const float* res_act1[4][3];  /* fp32 [2][cout] */
+    const float* res_act2[4][3];
+    const void* res_w1[4][3];     /* [pad128(cout)][pad64(7*cout)] */
+    const void* res_b1[4][3];     /* [pad128(cout)] */
+    const void* res_w2[4][3];     /* [pad128(cout)][pad128(cout)] */
+    const void* res_b2[4][3];
+    const float* final_snake;     /* fp32 [2][cout of block 3] */
+    const float* final_w;         /* fp32 [7][cout of block 3] (tap-major) */
+    float final_b;
+} qtts_c2w_desc;
+
+typedef struct qtts_c2w qtts_c2w;
+
+int qtts_c2w_create(const qtts_c2w_desc* desc, qtts_c2w** out);
+int qtts_c2w_destroy(qtts_c2w* c);
+/* Zero the streaming state of n slots (device int32 [n]): a new stream starts at frame 0. */
+int qtts_c2w_reset(qtts_c2w* c, const int32_t* slots, int n, qtts_stream_t stream);
+/* One frame for each of n rows: codes int64 (device) [n][codes_ld] (first num_codebooks used),
+ * slots int32 (device) [n] (distinct), wav fp32 (device) [n][samples_per_frame]. */
+int qtts_c2w_step(qtts_c2w* c, const int64_t* codes, int codes_ld, const int32_t* slots, int n, float* wav,
+                  qtts_stream_t stream);
+/* Kernels the last qtts_c2w_step enqueued (host counter). */
+int qtts_c2w_launches(const qtts_c2w* c);
+
 #ifdef __cplusplus
 }
 #endif

@@ -74,6 +74,25 @@ class StepIO(C.Structure):
                 ("force_codes", P), ("cp_logits_out", P), ("launches", I32)]
 
 
+class C2wDesc(C.Structure):
+    _fields_ = [
+        ("num_codebooks", I32), ("codebook_size", I32), ("codebook_dim", I32), ("latent", I32), ("hidden", I32),
+        ("layers", I32), ("heads", I32), ("head_dim", I32), ("inter", I32),
+        ("window", I32), ("decoder_dim", I32), ("convnext_dim", I32), ("max_slots", I32), ("max_frames", I32),
+        ("up_ratio", I32 * 2), ("rates", I32 * 4), ("dilations", I32 * 3), ("rms_eps", F32), ("ln_eps", F32),
+        ("rvq_tables", P), ("w_pre_conv", P), ("b_pre_conv", P), ("w_in_proj", P), ("b_in_proj", P),
+        ("w_in_norm", P), ("w_qkv", P), ("w_q_norm", P), ("w_k_norm", P), ("w_o", P), ("attn_scale", P),
+        ("w_post_norm", P), ("w_gate_up", P), ("w_down", P), ("mlp_scale", P), ("w_final_norm", P),
+        ("w_out_proj", P), ("b_out_proj", P), ("rope_cos", P), ("rope_sin", P),
+        ("up_w", P * 2), ("up_b", P * 2), ("dw_w", P * 2), ("dw_b", P * 2), ("ln_w", P * 2), ("ln_b", P * 2),
+        ("pw1_w", P * 2), ("pw1_b", P * 2), ("pw2_w", P * 2), ("pw2_b", P * 2), ("gamma", P * 2),
+        ("w_conv0", P), ("b_conv0", P), ("blk_snake", P * 4), ("blk_tw", P * 4), ("blk_tb", P * 4),
+        ("res_act1", (P * 3) * 4), ("res_act2", (P * 3) * 4), ("res_w1", (P * 3) * 4), ("res_b1", (P * 3) * 4),
+        ("res_w2", (P * 3) * 4), ("res_b2", (P * 3) * 4),
+        ("final_snake", P), ("final_w", P), ("final_b", F32),
+    ]
+
+
 # every symbol the header declares, in header order
 EXPORTS = [
     "qtts_version", "qtts_last_error", "qtts_device_error",
@@ -82,6 +101,7 @@ EXPORTS = [
     "qtts_gemm", "qtts_rmsnorm", "qtts_paged_attention", "qtts_paged_attention_noalloc", "qtts_sample",
     "qtts_codec_sum",
     "qtts_engine_create", "qtts_engine_destroy", "qtts_engine_step",
+    "qtts_c2w_create", "qtts_c2w_destroy", "qtts_c2w_reset", "qtts_c2w_step", "qtts_c2w_launches",
 ]
 
 _lib = None
@@ -123,6 +143,11 @@ def load() -> C.CDLL:
         "qtts_engine_create": ([C.POINTER(ModelDesc), C.POINTER(P)], C.c_int),
         "qtts_engine_destroy": ([P], C.c_int),
         "qtts_engine_step": ([P, C.POINTER(StepIO), P], C.c_int),
+        "qtts_c2w_create": ([C.POINTER(C2wDesc), C.POINTER(P)], C.c_int),
+        "qtts_c2w_destroy": ([P], C.c_int),
+        "qtts_c2w_reset": ([P, P, C.c_int, P], C.c_int),
+        "qtts_c2w_step": ([P, P, C.c_int, P, C.c_int, P, P], C.c_int),
+        "qtts_c2w_launches": ([P], C.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)

@@ -118,9 +118,11 @@ class Code2WavConfig:
 
 
 def tiny_code2wav_config() -> Code2WavConfig:
-    """Narrow channels, same strides/kernels/window: the fixture configuration."""
-    return Code2WavConfig(vq_dim=16, codebook_dim=32, latent_dim=64, hidden_size=64, num_layers=2, num_heads=4,
-                          kv_heads=4, head_dim=16, intermediate_size=128, decoder_dim=96, convnext_mult=2)
+    """Narrow channels, same strides/kernels/window: the fixture configuration.
+    Widths stay multiples of the GEMM tiles where the full model's are
+    (projections of 128, head_dim 32, decoder channels multiples of 8)."""
+    return Code2WavConfig(vq_dim=16, codebook_dim=64, latent_dim=128, hidden_size=128, num_layers=2, num_heads=4,
+                          kv_heads=4, head_dim=32, intermediate_size=256, decoder_dim=128, convnext_mult=2)
 
 
 @dataclass

@@ -61,6 +61,7 @@ enum DeviceErr : int {
     DEV_ERR_GEMM_EPILOGUE = 3,
     DEV_ERR_ATTN_WAIT = 4,
     DEV_ERR_DRAIN = 5,
+    DEV_ERR_BAD_SLOT = 6,  // a code2wav row named a slot outside the decoder's range
 };
 
 // Wall-clock limit of every device-side wait (ns).  A correct kernel waits

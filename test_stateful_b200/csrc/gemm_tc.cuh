@@ -16,22 +16,59 @@
 // MMAs per k-slice on the same weight tile and TMEM accumulates W·hi + W·lo,
 // recovering ~16 mantissa bits of the fp32 activation for no extra HBM bytes.
 //
-// Roles in a 128-thread CTA: warp 0 lane 0 issues TMA loads into a STAGES-deep
-// ring (full/empty mbarriers), warp 1 lane 0 issues UMMAs and commits, warp 2
-// owns the TMEM allocation; all four warps run the epilogue (warp w reads TMEM
-// lanes 32w..32w+31).
+// Roles in a 128- (or 256-) thread CTA: warp 0 lane 0 issues TMA loads into a
+// STAGES-deep ring (full/empty mbarriers), warp 1 lane 0 issues UMMAs and
+// commits, warp 2 owns the TMEM allocation; all warps run the epilogue (warp w
+// reads TMEM lanes 32(w%4)..32(w%4)+31; with 256 threads warps w and w+4 split
+// the token columns).  The 256-thread form serves the wide-row convolution
+// GEMMs of the code2wav decoder, whose epilogues carry most of the work.
 //
 // Epilogues (fused, applied by the reducing CTA to its token slice):
 //   BF16 / F32 store (+bias), RESIDUAL (fp32 residual += Y, the "residual +"
 //   of talker_unified_modules.py:222, 227), SWIGLU (silu(gate)*up of
 //   Qwen3MLP; weight rows interleaved 64 gate / 64 up per tile), QKV_ROPE
 //   (per-head q_norm/k_norm RMSNorm, RoPE, q to a buffer, k/v stored into the
-//   paged KV pool through the slot mapping — talker_unified_modules.py:173-190).
+//   paged KV pool through the slot mapping — talker_unified_modules.py:173-190),
+//   CONV (code2wav: bias, layer scale, residual, SnakeBeta/GELU, strided and
+//   slot-indexed stores; see ConvEpi).
 #pragma once
 
 #include "common.cuh"
 
 namespace qtts {
+
+// Element (stream, time, channel) of an activation buffer.  Streams are
+// indexed by their slot (per-stream state that persists across steps) or by
+// the row of this call; time t sits at row ctx + t of the stream's
+// seq_rows-row segment, so the ctx rows before it hold the left context of a
+// causal convolution.
+struct ActView {
+    void* ptr;  // null: not used
+    int by_slot, seq_rows, ctx, ld;
+};
+
+__host__ __device__ __forceinline__ size_t view_index(const ActView& v, int r, int slot, int t, int c) {
+    return ((size_t)(v.by_slot ? slot : r) * v.seq_rows + v.ctx + t) * v.ld + c;
+}
+
+enum ConvAct : int { ACT_NONE = 0, ACT_SNAKE = 1, ACT_GELU = 2 };
+
+// Epilogue of the code2wav GEMMs.  GEMM row m is (stream r = m / T_rows,
+// step i = m % T_rows); column n is (phase n / C_o, channel n % C_o), so a
+// transposed convolution written as a GEMM (phases = stride) lands at time
+// t = i * phases + phase.  With y = acc + bias[n]:
+//   v = (res ? res[r,t,c] : 0) + (scale ? scale[c] : 1) * y
+//   out32[r,t,c] = v ;  out16[r,t,c] = bf16(act(v))
+// Columns n >= n_valid are tile padding and are not stored.
+struct ConvEpi {
+    int T_rows, phases, C_o, n_valid, act;
+    const int32_t* row_slot;
+    const __nv_bfloat16* scale;  // per channel, or null
+    const float* act_p;          // SnakeBeta: [2][C_o] = exp(alpha), exp(-beta)
+    ActView res, out32, out16;
+};
+
+constexpr int kEpiConv = 16;  // internal epilogue id (not part of the C ABI)
 
 struct GemmParams {
     int M, N, K;
@@ -42,6 +79,7 @@ struct GemmParams {
     void* out_lo;  // SwiGLU: bf16 residual part of the output (hi/lo pair), or NULL
     const __nv_bfloat16* bias;
     qtts_qkv_epilogue qkv;
+    ConvEpi conv;
 };
 
 template <int BN, int STAGES, bool SPLIT>
@@ -52,7 +90,7 @@ struct GemmLayout {
     static constexpr int PIPE_BYTES = STAGES * STAGE_BYTES;
     static constexpr int PART_BYTES = BN * 128 * 4;  // fp32 partial, [BN tokens][128 rows]
     static constexpr int BODY = PIPE_BYTES > PART_BYTES ? PIPE_BYTES : PART_BYTES;
-    static constexpr int SCRATCH_BYTES = 2 * 128 * 4;  // epilogue reduction scratch
+    static constexpr int SCRATCH_BYTES = 4 * 128 * 4;  // epilogue scratch (norm sums / token metadata)
     static constexpr int BAR_BYTES = 256;
     static constexpr int SMEM = 1024 + BODY + SCRATCH_BYTES + BAR_BYTES;
     static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "stage buffers must keep 1024-B alignment");
@@ -63,17 +101,21 @@ struct GemmLayout {
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
 
-template <int BN>
+// NT threads: thread (row = tid % 128, group = tid / 128) handles weight row
+// `row` of the tile for tokens group, group + NT/128, ...
+template <int BN, int NT>
 __device__ void gemm_epilogue(const GemmParams& p, float* R, int m0, int per, int tile_n, int tile_m,
                               float* scratch) {
-    const int t = threadIdx.x;  // row within the 128-row weight tile
+    constexpr int NG = NT / 128;
+    const int t = threadIdx.x & 127;  // row within the 128-row weight tile
+    const int grp = threadIdx.x >> 7;
     const int n_g = tile_n * 128 + t;
     switch (p.epilogue) {
         case QTTS_EPI_BF16:
         case QTTS_EPI_F32:
         case QTTS_EPI_RESIDUAL: {
             const float b = p.bias ? __bfloat162float(p.bias[n_g]) : 0.0f;
-            for (int i = 0; i < per; ++i) {
+            for (int i = grp; i < per; i += NG) {
                 const int m_g = tile_m * BN + m0 + i;
                 if (m_g >= p.M) break;
                 const float v = R[(m0 + i) * 128 + t] + b;
@@ -90,7 +132,7 @@ __device__ void gemm_epilogue(const GemmParams& p, float* R, int m0, int per, in
         case QTTS_EPI_SWIGLU: {
             if (t < 64) {
                 const int half_n = p.N >> 1;
-                for (int i = 0; i < per; ++i) {
+                for (int i = grp; i < per; i += NG) {
                     const int m_g = tile_m * BN + m0 + i;
                     if (m_g >= p.M) break;
                     const float g = R[(m0 + i) * 128 + t];
@@ -106,57 +148,155 @@ __device__ void gemm_epilogue(const GemmParams& p, float* R, int m0, int per, in
             break;
         }
         case QTTS_EPI_QKV_ROPE: {
-            const qtts_qkv_epilogue& e = p.qkv;
-            const int D = e.head_dim;
-            const int q_rows = e.num_heads * D;
-            const int k_rows = e.kv_heads * D;
-            const int d = n_g % D;
-            const int warp = t >> 5;
-            const int region = n_g < q_rows ? 0 : (n_g < q_rows + k_rows ? 1 : 2);
-            const __nv_bfloat16* nw = region == 0 ? (const __nv_bfloat16*)e.q_norm_w
-                                                  : (const __nv_bfloat16*)e.k_norm_w;
-            for (int i = 0; i < per; ++i) {
+            if constexpr (NT == 128) {  // the plans never pair this epilogue with wider CTAs
+                const qtts_qkv_epilogue& e = p.qkv;
+                const int D = e.head_dim;
+                const int q_rows = e.num_heads * D;
+                const int k_rows = e.kv_heads * D;
+                const int d = n_g % D;
+                const int warp = t >> 5;
+                const int region = n_g < q_rows ? 0 : (n_g < q_rows + k_rows ? 1 : 2);
+                const __nv_bfloat16* nw = region == 0 ? (const __nv_bfloat16*)e.q_norm_w
+                                                      : (const __nv_bfloat16*)e.k_norm_w;
+                for (int i = 0; i < per; ++i) {
+                    const int m_g = tile_m * BN + m0 + i;
+                    if (m_g >= p.M) break;  // uniform across the CTA
+                    float v = R[(m0 + i) * 128 + t];
+                    // per-head sum of squares (a head spans D/32 warps of this tile)
+                    float ss = warp_sum(v * v);
+                    if ((t & 31) == 0) scratch[warp] = ss;
+                    __syncthreads();
+                    if (region < 2) {
+                        const int wpd = D >> 5;
+                        const int w0 = (warp / wpd) * wpd;
+                        float tot = 0.f;
+                        for (int w = 0; w < wpd; ++w) tot += scratch[w0 + w];
+                        v = v * rsqrtf(tot / (float)D + e.rms_eps) * __bfloat162float(nw[d]);
+                    }
+                    scratch[8 + t] = v;
+                    __syncthreads();
+                    int pos = e.row_pos[m_g];
+                    pos = pos < 0 ? 0 : (pos >= e.max_pos ? e.max_pos - 1 : pos);  // table bounds
+                    if (region < 2) {
+                        const int half = D >> 1;
+                        const int dd = d < half ? d : d - half;
+                        const float c = e.rope_cos[(size_t)pos * half + dd];
+                        const float s = e.rope_sin[(size_t)pos * half + dd];
+                        const float partner = scratch[8 + (d < half ? t + half : t - half)];
+                        v = d < half ? v * c - partner * s : v * c + partner * s;
+                    }
+                    if (region == 0) {
+                        reinterpret_cast<float*>(p.out)[(size_t)m_g * q_rows + n_g] = v;  // q stays fp32
+                    } else {
+                        const int slot = e.slot_mapping[m_g];
+                        if (slot >= 0) {
+                            const int blk = slot / e.block_size, off = slot % e.block_size;
+                            const int g = (n_g - q_rows - (region == 2 ? k_rows : 0)) / D;
+                            const size_t idx =
+                                ((((size_t)blk * e.num_layers + e.layer) * 2 + (region - 1)) * e.kv_heads + g) *
+                                    e.block_size +
+                                off;
+                            reinterpret_cast<kv_t*>(e.kv_pool)[idx * D + d] = to_kv(v);
+                        }
+                    }
+                    __syncthreads();
+                }
+            }
+            break;
+        }
+        case kEpiConv: {
+            // Vectorised: thread = (channel quad cg, token lane tl).  Each token's
+            // row index in the three views is computed once into shared memory,
+            // and the residual loads of 8 tokens are issued before their stores.
+            const ConvEpi& e = p.conv;
+            int* tok_ok = reinterpret_cast<int*>(scratch);
+            int* row_res = tok_ok + 128;
+            int* row_o32 = row_res + 128;
+            int* row_o16 = row_o32 + 128;
+            for (int i = threadIdx.x; i < per; i += NT) {
                 const int m_g = tile_m * BN + m0 + i;
-                if (m_g >= p.M) break;  // uniform across the CTA
-                float v = R[(m0 + i) * 128 + t];
-                // per-head sum of squares (a head spans D/32 warps of this tile)
-                float ss = warp_sum(v * v);
-                if ((t & 31) == 0) scratch[warp] = ss;
-                __syncthreads();
-                if (region < 2) {
-                    const int wpd = D >> 5;
-                    const int w0 = (warp / wpd) * wpd;
-                    float tot = 0.f;
-                    for (int w = 0; w < wpd; ++w) tot += scratch[w0 + w];
-                    v = v * rsqrtf(tot / (float)D + e.rms_eps) * __bfloat162float(nw[d]);
-                }
-                scratch[8 + t] = v;
-                __syncthreads();
-                int pos = e.row_pos[m_g];
-                pos = pos < 0 ? 0 : (pos >= e.max_pos ? e.max_pos - 1 : pos);  // table bounds
-                if (region < 2) {
-                    const int half = D >> 1;
-                    const int dd = d < half ? d : d - half;
-                    const float c = e.rope_cos[(size_t)pos * half + dd];
-                    const float s = e.rope_sin[(size_t)pos * half + dd];
-                    const float partner = scratch[8 + (d < half ? t + half : t - half)];
-                    v = d < half ? v * c - partner * s : v * c + partner * s;
-                }
-                if (region == 0) {
-                    reinterpret_cast<float*>(p.out)[(size_t)m_g * q_rows + n_g] = v;  // q stays fp32
-                } else {
-                    const int slot = e.slot_mapping[m_g];
-                    if (slot >= 0) {
-                        const int blk = slot / e.block_size, off = slot % e.block_size;
-                        const int g = (n_g - q_rows - (region == 2 ? k_rows : 0)) / D;
-                        const size_t idx =
-                            ((((size_t)blk * e.num_layers + e.layer) * 2 + (region - 1)) * e.kv_heads + g) *
-                                e.block_size +
-                            off;
-                        reinterpret_cast<kv_t*>(e.kv_pool)[idx * D + d] = to_kv(v);
+                const bool ok = m_g < p.M;
+                const int r = ok ? m_g / e.T_rows : 0;
+                const int t0 = ok ? (m_g - r * e.T_rows) * e.phases : 0;
+                const int sl = (ok && e.row_slot) ? e.row_slot[r] : r;
+                tok_ok[i] = ok;
+                row_res[i] = (e.res.by_slot ? sl : r) * e.res.seq_rows + e.res.ctx + t0;
+                row_o32[i] = (e.out32.by_slot ? sl : r) * e.out32.seq_rows + e.out32.ctx + t0;
+                row_o16[i] = (e.out16.by_slot ? sl : r) * e.out16.seq_rows + e.out16.ctx + t0;
+            }
+            __syncthreads();
+            constexpr int NTL = NT / 32;  // token lanes
+            const int cg = threadIdx.x & 31, tl = threadIdx.x >> 5;
+            const int n0 = tile_n * 128 + cg * 4;
+            if (n0 >= e.n_valid) break;  // n_valid and C_o are multiples of 4
+            const int ph = n0 / e.C_o, c0 = n0 - ph * e.C_o;
+            float b4[4], s4[4], pa[4], pb[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                b4[k] = p.bias ? __bfloat162float(p.bias[n0 + k]) : 0.0f;
+                s4[k] = e.scale ? __bfloat162float(e.scale[c0 + k]) : 1.0f;
+                pa[k] = e.act == ACT_SNAKE ? e.act_p[c0 + k] : 0.f;
+                pb[k] = e.act == ACT_SNAKE ? e.act_p[e.C_o + c0 + k] : 0.f;
+            }
+            const float* res = reinterpret_cast<const float*>(e.res.ptr);
+            float* o32 = reinterpret_cast<float*>(e.out32.ptr);
+            __nv_bfloat16* o16 = reinterpret_cast<__nv_bfloat16*>(e.out16.ptr);
+            constexpr int B = 8;
+            for (int i0 = tl; i0 < per; i0 += NTL * B) {
+                float4 v[B];
+                bool ok[B];
+#pragma unroll
+                for (int u = 0; u < B; ++u) {
+                    const int i = i0 + NTL * u;
+                    ok[u] = i < per && tok_ok[i];
+                    v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (ok[u]) {
+                        const float4 a = *reinterpret_cast<const float4*>(R + (m0 + i) * 128 + cg * 4);
+                        v[u] = make_float4(s4[0] * (a.x + b4[0]), s4[1] * (a.y + b4[1]), s4[2] * (a.z + b4[2]),
+                                           s4[3] * (a.w + b4[3]));
                     }
                 }
-                __syncthreads();
+                if (res) {
+                    float4 rv[B];
+#pragma unroll
+                    for (int u = 0; u < B; ++u) {
+                        const int i = i0 + NTL * u;
+                        rv[u] = ok[u] ? *reinterpret_cast<const float4*>(
+                                            res + (size_t)(row_res[i] + ph) * e.res.ld + c0)
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+#pragma unroll
+                    for (int u = 0; u < B; ++u) {
+                        v[u].x += rv[u].x;
+                        v[u].y += rv[u].y;
+                        v[u].z += rv[u].z;
+                        v[u].w += rv[u].w;
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < B; ++u) {
+                    if (!ok[u]) continue;
+                    const int i = i0 + NTL * u;
+                    if (o32) *reinterpret_cast<float4*>(o32 + (size_t)(row_o32[i] + ph) * e.out32.ld + c0) = v[u];
+                    if (o16) {
+                        float a[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            if (e.act == ACT_SNAKE) {
+                                const float sn = __sinf(a[k] * pa[k]);
+                                a[k] = a[k] + sn * sn * pb[k];
+                            } else if (e.act == ACT_GELU) {
+                                a[k] = 0.5f * a[k] * (1.0f + erff(a[k] * 0.70710678118654752f));
+                            }
+                        }
+                        const __nv_bfloat162 h01 = __floats2bfloat162_rn(a[0], a[1]);
+                        const __nv_bfloat162 h23 = __floats2bfloat162_rn(a[2], a[3]);
+                        uint2 pack;
+                        pack.x = *reinterpret_cast<const uint32_t*>(&h01);
+                        pack.y = *reinterpret_cast<const uint32_t*>(&h23);
+                        *reinterpret_cast<uint2*>(o16 + (size_t)(row_o16[i] + ph) * e.out16.ld + c0) = pack;
+                    }
+                }
             }
             break;
         }
@@ -168,11 +308,12 @@ __device__ void gemm_epilogue(const GemmParams& p, float* R, int m0, int per, in
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-template <int BN, int STAGES, bool SPLIT>
-__global__ void __launch_bounds__(128) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW,
-                                                      const __grid_constant__ CUtensorMap tmX,
-                                                      const __grid_constant__ CUtensorMap tmXlo,
-                                                      const GemmParams p) {
+template <int BN, int STAGES, bool SPLIT, int NT>
+__global__ void __launch_bounds__(NT) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW,
+                                                     const __grid_constant__ CUtensorMap tmX,
+                                                     const __grid_constant__ CUtensorMap tmXlo,
+                                                     const GemmParams p) {
+    static_assert(NT == 128 || NT == 256, "128 or 256 threads");
     using L = GemmLayout<BN, STAGES, SPLIT>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -284,11 +425,15 @@ __global__ void __launch_bounds__(128) gemm_tc_kernel(const __grid_constant__ CU
     float* P = reinterpret_cast<float*>(smem);
     const bool good = ok && flags[0] == 0;
     {
-        const int row = warp * 32 + lane;
+        // warp w reads TMEM lane quarter w % 4; with 256 threads warps w and w + 4
+        // take one half of the columns each
+        const int quarter = warp & 3, half = warp >> 2;
+        constexpr int COLS = BN / (NT / 128);
+        const int row = quarter * 32 + lane;
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 16) {
+        for (int c = half * COLS; c < (half + 1) * COLS; c += 16) {
             float v[16];
-            tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c, v);
+            tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c, v);
 #pragma unroll
             for (int j = 0; j < 16; ++j) P[(c + j) * 128 + row] = good ? v[j] : 0.0f;
         }
@@ -305,7 +450,7 @@ __global__ void __launch_bounds__(128) gemm_tc_kernel(const __grid_constant__ CU
         // this CTA's token slice, as float4 chunks: all splits' loads are issued
         // before any is consumed, so the remote-shared-memory latency is paid once
         const uint32_t base = smem_u32(P + m0 * 128);
-        for (int e = threadIdx.x; e < per * 32; e += 128) {
+        for (int e = threadIdx.x; e < per * 32; e += NT) {
             float4 v[8];
 #pragma unroll
             for (int r = 0; r < 8; ++r)
@@ -324,7 +469,7 @@ __global__ void __launch_bounds__(128) gemm_tc_kernel(const __grid_constant__ CU
         }
         __syncthreads();
     }
-    gemm_epilogue<BN>(p, P, m0, per, tile_n, tile_m, scratch);
+    gemm_epilogue<BN, NT>(p, P, m0, per, tile_n, tile_m, scratch);
     if (p.splits > 1) cluster_sync();  // peers finished reading this CTA's shared memory
 }
 
@@ -405,17 +550,17 @@ inline int pick_splits(int N, int M, int K, int BN) {
     return s;
 }
 
-template <int BN, int STAGES, bool SPLIT>
+template <int BN, int STAGES, bool SPLIT, int NT = 128>
 inline int launch_gemm_t(const CUtensorMap& mw, const CUtensorMap& mx, const CUtensorMap& mxlo, const GemmParams& p,
                          cudaStream_t st) {
     using L = GemmLayout<BN, STAGES, SPLIT>;
-    auto kern = gemm_tc_kernel<BN, STAGES, SPLIT>;
+    auto kern = gemm_tc_kernel<BN, STAGES, SPLIT, NT>;
     static bool attr_done = false;
     if (!attr_done) {
         QTTS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM));
         attr_done = true;
     }
-    QTTS_CHECK_CUDA(launch_pdl(kern, dim3(p.N / 128, p.splits, ceil_div(p.M, BN)), dim3(128, 1, 1), L::SMEM, st,
+    QTTS_CHECK_CUDA(launch_pdl(kern, dim3(p.N / 128, p.splits, ceil_div(p.M, BN)), dim3(NT, 1, 1), L::SMEM, st,
                                dim3(1, p.splits, 1), mw, mx, mxlo, p));
     return QTTS_OK;
 }
@@ -487,7 +632,10 @@ inline int gemm_run(GemmPlan g, int M, cudaStream_t st, void* out = nullptr) {
         return launch_gemm_t<128, 3, true>(g.mw, g.mx128, g.mlo128, g.p, st);
     }
     if (bn == 64) return launch_gemm_t<64, 4, false>(g.mw, g.mx64, g.mx64, g.p, st);
-    return launch_gemm_t<128, 4, false>(g.mw, g.mx128, g.mx128, g.p, st);
+    // wide-row (convolution) GEMMs: 3 x 32 KB stages keep two CTAs per SM, so one
+    // CTA's epilogue overlaps the other's main loop, and 8 warps share the epilogue
+    if (g.p.epilogue == QTTS_EPI_QKV_ROPE) return launch_gemm_t<128, 3, false, 128>(g.mw, g.mx128, g.mx128, g.p, st);
+    return launch_gemm_t<128, 3, false, 256>(g.mw, g.mx128, g.mx128, g.p, st);
 }
 
 }  // namespace qtts

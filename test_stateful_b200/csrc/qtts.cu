@@ -2,12 +2,13 @@
 // decode backend and the extern "C" entry points declared in
 // include/qtts_b200.h.  Each entry point validates its arguments, launches on
 // the caller's stream and returns a status code; nothing here allocates per
-// call except qtts_engine_create.
+// call except qtts_engine_create and qtts_c2w_create.
 #include <cstdarg>
 #include <mutex>
 #include <new>
 
 #include "common.cuh"
+#include "code2wav.cuh"
 #include "engine.cuh"
 
 namespace qtts {
@@ -250,6 +251,49 @@ int qtts_engine_step(qtts_engine* e, qtts_step_io* io, qtts_stream_t stream) {
     QTTS_REQUIRE(e && io, "engine_step: null argument");
     return engine_step(e, *io, (cudaStream_t)stream);
 }
+
+// ---------------------------------------------------------------- code2wav
+int qtts_c2w_create(const qtts_c2w_desc* desc, qtts_c2w** out) {
+    QTTS_REQUIRE(desc && out, "c2w_create: null argument");
+    QTTS_REQUIRE(desc->rvq_tables && desc->w_pre_conv && desc->w_qkv && desc->w_conv0 && desc->final_w &&
+                     desc->rope_cos && desc->rope_sin,
+                 "c2w_create: weights incomplete");
+    qtts_c2w* c = new (std::nothrow) qtts_c2w();
+    if (!c) {
+        set_error("c2w_create: out of host memory");
+        return QTTS_ERR_INVALID;
+    }
+    c->d = *desc;
+    const int rc = c2w_build(c);
+    if (rc != QTTS_OK) {
+        for (void* p : c->allocs) cudaFree(p);
+        delete c;
+        return rc;
+    }
+    *out = c;
+    return QTTS_OK;
+}
+
+int qtts_c2w_destroy(qtts_c2w* c) {
+    if (!c) return QTTS_OK;
+    for (void* p : c->allocs) cudaFree(p);
+    delete c;
+    return QTTS_OK;
+}
+
+int qtts_c2w_reset(qtts_c2w* c, const int32_t* slots, int n, qtts_stream_t stream) {
+    QTTS_REQUIRE(c && (n == 0 || slots), "c2w_reset: null argument");
+    QTTS_REQUIRE(n >= 0 && n <= c->S, "c2w_reset: n=%d outside [0, %d]", n, c->S);
+    return c2w_reset(c, slots, n, (cudaStream_t)stream);
+}
+
+int qtts_c2w_step(qtts_c2w* c, const int64_t* codes, int codes_ld, const int32_t* slots, int n, float* wav,
+                  qtts_stream_t stream) {
+    QTTS_REQUIRE(c, "c2w_step: null decoder");
+    return c2w_step(c, codes, codes_ld, slots, n, wav, (cudaStream_t)stream);
+}
+
+int qtts_c2w_launches(const qtts_c2w* c) { return c ? c->launches : 0; }
 
 }  // extern "C"
 

@@ -18,7 +18,7 @@ HEADER = os.path.join(ROOT, "include", "qtts_b200.h")
 
 def _declared():
     text = open(HEADER).read()
-    return sorted(set(re.findall(r"^int (qtts_[a-z_]+)\(", text, flags=re.M)))
+    return sorted(set(re.findall(r"^int (qtts_[a-z0-9_]+)\(", text, flags=re.M)))
 
 
 def test_library_exports_every_declared_symbol():
@@ -28,7 +28,7 @@ def test_library_exports_every_declared_symbol():
     for name in declared:
         assert hasattr(lib, name), name
     out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)], capture_output=True, text=True).stdout
-    exported = sorted(set(re.findall(r" T (qtts_[a-z_]+)$", out, flags=re.M)))
+    exported = sorted(set(re.findall(r" T (qtts_[a-z0-9_]+)$", out, flags=re.M)))
     assert exported == declared
 
 
@@ -43,6 +43,8 @@ int main(void) {
          sizeof(qtts_step_io));
   printf("%zu %zu %zu %zu\n", offsetof(qtts_model_desc, pool), offsetof(qtts_model_desc, max_prefill_rows),
          offsetof(qtts_step_io, noise_seed), offsetof(qtts_step_io, launches));
+  printf("%zu %zu %zu %zu %zu\n", sizeof(qtts_c2w_desc), offsetof(qtts_c2w_desc, rvq_tables),
+         offsetof(qtts_c2w_desc, up_w), offsetof(qtts_c2w_desc, res_b2), offsetof(qtts_c2w_desc, final_b));
   return 0;
 }
 """
@@ -58,6 +60,9 @@ int main(void) {
                      C.sizeof(_lib.StepIO)]
     assert offs == [_lib.ModelDesc.pool.offset, _lib.ModelDesc.max_prefill_rows.offset,
                     _lib.StepIO.noise_seed.offset, _lib.StepIO.launches.offset]
+    c2w = [int(v) for v in lines[2].split()]
+    D = _lib.C2wDesc
+    assert c2w == [C.sizeof(D), D.rvq_tables.offset, D.up_w.offset, D.res_b2.offset, D.final_b.offset]
 
 
 def test_invalid_arguments_return_status_codes():

@@ -1,0 +1,107 @@
+"""Streaming code2wav on the B200 against the reference wrapper's fixture and
+the CPU oracle.  Bar: waveform SNR >= 30 dB per stream (bf16 weights and
+activations on the device, fp32 in the reference/oracle)."""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+from oracle import code2wav as OC  # noqa: E402
+from test_stateful_b200 import _lib, weights as wmod  # noqa: E402
+from test_stateful_b200.config import Code2WavConfig, tiny_code2wav_config  # noqa: E402
+from test_stateful_b200.runtime.code2wav import DeviceCode2Wav  # noqa: E402
+
+from .conftest import GOLDEN  # noqa: E402
+
+DEV = "cuda"
+SNR_DB = 30.0
+
+
+def snr_db(ref: np.ndarray, out: np.ndarray) -> float:
+    noise = float(((out.astype(np.float64) - ref) ** 2).sum())
+    return 10 * np.log10(float((ref.astype(np.float64) ** 2).sum()) / max(noise, 1e-30))
+
+
+def test_code2wav_matches_reference_stream_fixture():
+    """Replay the reference's 2-slot, 78-step batched stream (slots start 9
+    steps apart; slot 0 wraps the 72-frame window) on device slots 3 and 1."""
+    z = np.load(os.path.join(GOLDEN, "code2wav_tiny.npz"))
+    cfg = tiny_code2wav_config()
+    W = wmod.make_code2wav_weights(cfg, int(z["seed"]))
+    dec = DeviceCode2Wav(cfg, W, DEV, max_slots=4, max_frames=256)
+    codes, active, ref = z["codes"], z["active"], z["wav"]
+    dev_slot = [3, 1]
+    out = np.zeros_like(ref)
+    started = [False, False]
+    for t in range(codes.shape[0]):
+        act = [i for i in range(2) if active[t, i]]
+        new = [i for i in act if not started[i]]
+        if new:
+            dec.reset(torch.tensor([dev_slot[i] for i in new], dtype=torch.int32, device=DEV))
+            for i in new:
+                started[i] = True
+        slots = torch.tensor([dev_slot[i] for i in act], dtype=torch.int32, device=DEV)
+        cds = torch.from_numpy(codes[t, act]).long().to(DEV)
+        wav = torch.empty(len(act), cfg.samples_per_frame, device=DEV)
+        dec.step(cds, slots, wav)
+        out[t, act] = wav.cpu().numpy()
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    for i in range(2):
+        m = active[:, i]
+        s = snr_db(ref[m, i], out[m, i])
+        assert s >= SNR_DB, (i, s)
+    dec.close()
+
+
+def test_code2wav_full_config_matches_oracle():
+    """Full decoder widths (latent 1024, 8 layers, 1536 -> 96 channels), 3
+    streams x 6 frames with a stream joining late, against the fp32 oracle."""
+    cfg = Code2WavConfig()
+    W = wmod.make_code2wav_weights(cfg, 11)
+    Wf = wmod.to_fp32(W)
+    dec = DeviceCode2Wav(cfg, W, DEV, max_slots=8, max_frames=64)
+    g = torch.Generator().manual_seed(3)
+    steps, starts, slots_of = 6, [0, 0, 2], [5, 0, 2]
+    codes = torch.randint(0, 2200, (steps, 3, 16), generator=g)  # ids >= 2048 exercise the clamp
+    states = [OC.Code2WavState(cfg) for _ in range(3)]
+    ref = np.zeros((steps, 3, cfg.samples_per_frame), np.float32)
+    out = np.zeros_like(ref)
+    for t in range(steps):
+        act = [i for i in range(3) if t >= starts[i]]
+        new = [i for i in act if t == starts[i]]
+        dec.reset(torch.tensor([slots_of[i] for i in new], dtype=torch.int32, device=DEV))
+        wav = torch.empty(len(act), cfg.samples_per_frame, device=DEV)
+        dec.step(codes[t, act].to(DEV), torch.tensor([slots_of[i] for i in act], dtype=torch.int32, device=DEV), wav)
+        out[t, act] = wav.cpu().numpy()
+        for i in act:
+            ref[t, i] = OC.decode_chunk(Wf, cfg, codes[t, i].view(-1, 1), states[i]).numpy()
+    assert _lib.device_error() == 0
+    for i in range(3):
+        s = snr_db(ref[starts[i]:, i], out[starts[i]:, i])
+        assert s >= SNR_DB, (i, s)
+    assert dec.last_launches > 0
+    dec.close()
+
+
+def test_code2wav_reset_replays_identically():
+    cfg = tiny_code2wav_config()
+    dec = DeviceCode2Wav(cfg, wmod.make_code2wav_weights(cfg, 2), DEV, max_slots=2, max_frames=64)
+    g = torch.Generator().manual_seed(9)
+    codes = torch.randint(0, 2048, (5, 1, 16), generator=g).to(DEV)
+    slot = torch.tensor([1], dtype=torch.int32, device=DEV)
+    runs = []
+    for _ in range(2):
+        dec.reset(slot)
+        w = []
+        for t in range(5):
+            wav = torch.empty(1, cfg.samples_per_frame, device=DEV)
+            dec.step(codes[t], slot, wav)
+            w.append(wav)
+        runs.append(torch.cat(w))
+    torch.testing.assert_close(runs[0], runs[1], rtol=0, atol=0)
+    dec.close()
