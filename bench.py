@@ -10,11 +10,13 @@ predictor (5 layers, hidden 1024), 16-token KV blocks in an 8192-block pool,
 top-k 50 / temperature 0.9 sampling with in-kernel Philox noise.
 
 One step = one decode step for all 64 streams (talker + sampling + code
-predictor + codec sum), i.e. 64 codec frames.  ``value`` replays the captured
-decode step with everything resident on the device; ``e2e`` goes through the
-public executor call (``B200Executor.launch_decode_step`` -> ``GPUFuture.wait``)
-with the per-step text embeddings copied from pinned host memory and the codec
-frames copied back every step.
+predictor + codec sum + streaming code2wav), i.e. 64 codec frames and 64 x 1920
+waveform samples — the unit of work of the reference's fused
+talker+code2wav plan.  ``value`` replays the captured decode step with
+everything resident on the device; ``e2e`` goes through the public executor
+call (``B200Executor.launch_decode_step`` -> ``GPUFuture.wait``) with the
+per-step text embeddings copied from pinned host memory and the codec frames
+and audio chunks copied back every step.
 
 ``--impl reference`` times the CPU oracle (a restatement of the reference's
 PyTorch modules, fp32) on the host cores.  Under torchrun each rank is an
@@ -341,7 +343,7 @@ def run_b200(rank, world, local):
             staged.copy_(t_host, non_blocking=True)
             ex.text_add.index_copy_(0, idx, staged)
         out = ex.launch_decode_step(slots).wait()
-        _ = out.full_codec
+        _ = out.full_codec, out.audio_chunks
     torch.cuda.synchronize(dev)
     e2e_sec = time.perf_counter() - t0
     if world > 1:
@@ -350,7 +352,7 @@ def run_b200(rank, world, local):
         e2e_sec = float(t.item())
     e2e_value = n * ARGS.e2e_steps * world / e2e_sec
     h2d = t_host.numel() * 4 + n * 4
-    d2h = n * (1 + ex._config.cp.num_stages) * 8 + 4
+    d2h = n * (1 + ex._config.cp.num_stages) * 8 + 4 + n * ex._config.c2w.samples_per_frame * 4
 
     peaks = load_peaks()
     roof = attention_roofline(ex, slots, peaks)
@@ -368,8 +370,8 @@ def run_b200(rank, world, local):
                                    "8192 x 16-token KV blocks, top-k 50 / T 0.9 Philox sampling",
                        "streams_per_gpu": n, "parallelism": f"replicas x{world} (request-sharded, no collective)",
                        "l2": "inputs larger than L2 (KV ~4 GB + weights ~3 GB read per step)",
-                       "step": "talker 28 layers + sampling + 15-stage code predictor + codec sum; "
-                               "code2wav not included yet",
+                       "step": "talker 28 layers + sampling + 15-stage code predictor + codec sum + "
+                               "streaming code2wav (1920 samples/stream)",
                        "ctx_mean_end": round(sum(ctx_now) / len(ctx_now), 1)},
             "gpu_launches": launches * ARGS.steps,
             "roofline": roof,

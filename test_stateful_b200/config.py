@@ -144,6 +144,7 @@ class EngineConfig:
     talker: TalkerConfig = field(default_factory=TalkerConfig)
     cp: CodePredictorConfig = field(default_factory=CodePredictorConfig)
     pool: PagedPoolConfig = field(default_factory=PagedPoolConfig)
+    c2w: Code2WavConfig = field(default_factory=Code2WavConfig)
 
     def to_dict(self) -> dict:
         return asdict(self)
@@ -162,4 +163,5 @@ def tiny_engine_config(num_layers: int = 2) -> EngineConfig:
         cp=CodePredictorConfig(num_layers=2, hidden_size=128, num_heads=4, kv_heads=2, head_dim=32,
                                intermediate_size=256, talker_hidden_size=256),
         pool=PagedPoolConfig(block_size=16, num_blocks=64, max_slots=8, max_seq_len=256),
+        c2w=tiny_code2wav_config(),
     )

@@ -18,10 +18,13 @@ What changes underneath:
   rebuilds batch inputs every step (executor.py:1259-1469).
 * A decode step for a given batch size is captured once in a CUDA graph and
   replayed; the host only writes the slot list.
-
-Code2wav is not part of this backend yet: ``audio_chunks`` entries are
-``None`` (the reference returns them as ``None`` too when its plan has no
-``wav`` output, executor.py:424-435).
+* Code2wav runs in the same step (and graph) as the talker, one frame per
+  stream, like the fused plan (export_09_talker_code2wav_fused.py:145-160):
+  ``audio_chunks`` carries each stream's 1920 fp32 samples as bytes
+  (executor.py:424-435).  Its streaming state is device-resident per slot
+  (``runtime/code2wav.py``), so ``make_zero_conv_states`` /
+  ``make_zero_transconv_states`` return empty lists and a stream's decoder
+  state is zeroed by the prefill that starts it.
 """
 
 from __future__ import annotations
@@ -35,7 +38,8 @@ import torch
 
 from .. import _lib
 from ..config import EngineConfig, PagedPoolConfig
-from ..weights import make_cp_weights, make_talker_weights
+from ..weights import make_code2wav_weights, make_cp_weights, make_talker_weights
+from .code2wav import DeviceCode2Wav
 from .model import DeviceModel
 from .pool import PagedKVCachePool, PagedPrefixKVCache, SlotState
 
@@ -86,6 +90,7 @@ class GPUFuture:
     _codes_dev: Optional[torch.Tensor] = None
     _codec_sum: Optional[torch.Tensor] = None
     _status_host: Optional[torch.Tensor] = None
+    _wav_host: Optional[torch.Tensor] = None
 
     def wait(self) -> StepOutput:
         if self._event is not None:
@@ -97,7 +102,11 @@ class GPUFuture:
         codes = self._codes_host[:n].clone() if self._codes_host is not None else None
         eos_id = self._executor._config.talker.codec_eos_id if self._executor else 2150
         eos = (codes[:, 0] == eos_id).tolist() if codes is not None else [False] * n
-        return StepOutput(slots=self._slots, eos_flags=eos, audio_chunks=[None] * n,
+        if self._wav_host is not None:
+            audio = [self._wav_host[i].numpy().tobytes() for i in range(n)]
+        else:
+            audio = [None] * n
+        return StepOutput(slots=self._slots, eos_flags=eos, audio_chunks=audio,
                           original_past_lens=self._original_past_lens, codec_sum=self._codec_sum,
                           full_codec=codes, split_c2w_conv=[[] for _ in range(n)],
                           split_c2w_transconv=[[] for _ in range(n)])
@@ -110,7 +119,8 @@ class B200Executor:
                  max_batch_size: int = 64, max_seq_len: int = 1024, model_config: Optional[EngineConfig] = None,
                  do_sample: bool = False, temperature: float = 0.9, repetition_penalty: float = 1.05,
                  random_seed: int = 0, num_blocks: int = 8192, weights: Optional[Dict[str, torch.Tensor]] = None,
-                 weight_seed: int = 1, max_prefill_rows: int = 512, use_cuda_graphs: bool = True):
+                 weight_seed: int = 1, max_prefill_rows: int = 512, use_cuda_graphs: bool = True,
+                 enable_code2wav: bool = True, c2w_weights: Optional[Dict[str, torch.Tensor]] = None):
         if not torch.cuda.is_available():
             raise RuntimeError("B200Executor needs a CUDA device (no CPU path)")
         self._device = torch.device("cuda", device_id)
@@ -127,6 +137,9 @@ class B200Executor:
         self._weights = weights
         self._weight_seed = weight_seed
         self._use_graphs = use_cuda_graphs
+        self._enable_c2w = enable_code2wav
+        self._c2w_weights = c2w_weights
+        self._c2w: Optional[DeviceCode2Wav] = None
         self._stream = torch.cuda.Stream(device=self._device)
         self._model: Optional[DeviceModel] = None
         self._kv_pool: Optional[PagedKVCachePool] = None
@@ -160,7 +173,15 @@ class B200Executor:
         with torch.cuda.device(self._device):
             self._model = DeviceModel(cfg, W, self._device, max_batch=self._max_batch,
                                       max_prefill_rows=self._max_input_len)
+            if self._enable_c2w:
+                Wc = self._c2w_weights
+                if Wc is None:
+                    Wc = make_code2wav_weights(cfg.c2w, self._weight_seed, device=self._device)
+                # one frame per decode step plus the prefill frame
+                self._c2w = DeviceCode2Wav(cfg.c2w, Wc, self._device, max_slots=self._max_batch,
+                                           max_frames=self._max_seq_len + 1)
         self._weights = None
+        self._c2w_weights = None
         self._alloc_state()
         self._kv_pool = PagedKVCachePool(self._model, self._max_batch)
         self._kv_pool.counts_reset_hook = self._reset_slot_state
@@ -174,10 +195,31 @@ class B200Executor:
 
     def shutdown(self) -> None:
         self._graphs.clear()
+        if self._c2w is not None:
+            self._c2w.close()
+        self._c2w = None
         if self._model is not None:
             self._model.close()
         self._model = None
         self._kv_pool = None
+
+    # -- code2wav state (device-resident per slot) -------------------------
+    def make_zero_conv_states(self) -> list:
+        """executor.py:701-706.  The conv states live on the device, per slot."""
+        return []
+
+    def make_zero_transconv_states(self) -> list:
+        """executor.py:708-713.  The transposed-conv states live on the device, per slot."""
+        return []
+
+    def apply_c2w_warm_state(self, slot: SlotState, c2w_kv, conv_states, transconv_states, frame_idx: int) -> bool:
+        """executor.py:715-757.  A warm state in the reference's tensor layout is
+        not installed (this backend keeps the decoder state on the device in
+        its own layout); like the reference on a mismatched state, the call
+        returns False and the stream starts from zero state."""
+        if c2w_kv is not None:
+            logger.warning("Code2Wav warm state not applied on the b200 backend (slot=%d)", slot.slot_id)
+        return False
 
     # -- per-slot device state --------------------------------------------
     def _alloc_state(self) -> None:
@@ -202,6 +244,9 @@ class B200Executor:
         self.codes_host = torch.zeros(B, 1 + c.num_stages, dtype=i64).pin_memory()
         self.status = torch.zeros(1, dtype=i32, device=dev)
         self.status_host = torch.zeros(1, dtype=i32).pin_memory()
+        spf = self._config.c2w.samples_per_frame
+        self.wav = torch.zeros(B, spf, dtype=f32, device=dev) if self._enable_c2w else None
+        self.wav_host = torch.zeros(B, spf, dtype=f32).pin_memory() if self._enable_c2w else None
 
     def _reset_slot_state(self, slot_id: int) -> None:
         self.counts[slot_id].zero_()
@@ -269,8 +314,20 @@ class B200Executor:
         _lib.check(int(self.status_host[0]), "prefill scheduler")
         slot.past_len += seq
 
+    def _first_frame_audio(self) -> Optional[bytes]:
+        """Code2wav of the frame a prefill sampled, from zero decoder state
+        (the fused prefill runs code2wav on it: executor.py:859-877)."""
+        if self._c2w is None:
+            return None
+        with torch.cuda.stream(self._stream):
+            self._c2w.reset(self.slots_dev[:1], stream=self._stream)
+            self._c2w.step(self.codes, self.slots_dev, self.wav, n=1, stream=self._stream)
+            self.wav_host[:1].copy_(self.wav[:1], non_blocking=True)
+        self._stream.synchronize()
+        return self.wav_host[0].numpy().tobytes()
+
     def prefill(self, slot: SlotState, prefill_embeds: torch.Tensor):
-        """executor.py:759-877: KV for the prompt plus the first frame's codes."""
+        """executor.py:759-877: KV for the prompt plus the first frame's codes and audio."""
         seq = int(prefill_embeds.shape[1])
         self._validate_prefill_len(seq, "prefill")
         self._kv_pool.init_kv_tensors(slot)
@@ -279,8 +336,9 @@ class B200Executor:
         slot.position_offset = 0
         slot.frame_idx += 1
         slot.next_embed = self.next_x[slot.slot_id]
+        audio = self._first_frame_audio()
         codes = self.codes[:1].cpu()
-        return None, bool(int(codes[0, 0]) == self._config.talker.codec_eos_id)
+        return audio, bool(int(codes[0, 0]) == self._config.talker.codec_eos_id)
 
     def prefill_prefix_only(self, slot: SlotState, prefill_embeds: torch.Tensor) -> None:
         """executor.py:879-950: KV for a cacheable prefix, no sampling."""
@@ -298,16 +356,23 @@ class B200Executor:
         self._prefill_call(slot, request_prefill_embeds, sample=1)
         slot.frame_idx += 1
         slot.next_embed = self.next_x[slot.slot_id]
+        audio = self._first_frame_audio()
         codes = self.codes[:1].cpu()
-        return None, bool(int(codes[0, 0]) == self._config.talker.codec_eos_id)
+        return audio, bool(int(codes[0, 0]) == self._config.talker.codec_eos_id)
 
     # -- decode -----------------------------------------------------------
+    def _step_body(self, io: _lib.StepIO, n: int) -> None:
+        """One fused decode step: talker + sampling + code predictor + codec sum, then code2wav."""
+        self._model.step(io, self._stream)
+        if self._c2w is not None:
+            self._c2w.step(self.codes, self.slots_dev, self.wav, n=n, stream=self._stream)
+            io.launches += self._c2w.last_launches
+
     def _capture(self, n: int):
         io = self._io(n, 1, self.next_x, sample=1)
-        # warm the kernels (attributes, tensor-map prefetch) before capture
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=self._stream):
-            self._model.step(io, self._stream)
+            self._step_body(io, n)
         return g, io
 
     def launch_decode_step(self, slots: List[SlotState]) -> GPUFuture:
@@ -326,7 +391,7 @@ class B200Executor:
             self.slots_dev[:n].copy_(self.slots_host[:n], non_blocking=True)
             if self._use_graphs:
                 if n not in self._graphs:
-                    self._model.step(self._io(n, 1, self.next_x, sample=1), self._stream)  # eager warm-up step
+                    self._step_body(self._io(n, 1, self.next_x, sample=1), n)  # eager warm-up step
                     self._stream.synchronize()
                     self._graphs[n] = None  # the warm-up already advanced this batch
                 else:
@@ -334,8 +399,10 @@ class B200Executor:
                         self._graphs[n] = self._capture(n)
                     self._graphs[n][0].replay()
             else:
-                self._model.step(self._io(n, 1, self.next_x, sample=1), self._stream)
+                self._step_body(self._io(n, 1, self.next_x, sample=1), n)
             self.codes_host[:n].copy_(self.codes[:n], non_blocking=True)
+            if self._c2w is not None:
+                self.wav_host[:n].copy_(self.wav[:n], non_blocking=True)
             self.status_host.copy_(self.status, non_blocking=True)
             ev = torch.cuda.Event()
             ev.record(self._stream)
@@ -345,7 +412,7 @@ class B200Executor:
             s.touch()
         return GPUFuture(_executor=self, _event=ev, _slots=list(slots), _original_past_lens=original,
                          _codes_host=self.codes_host, _codes_dev=self.codes, _codec_sum=self.codec_sum,
-                         _status_host=self.status_host)
+                         _status_host=self.status_host, _wav_host=self.wav_host)
 
     def warmup(self, n_rounds: int = 3) -> None:
         """executor.py:1541-1605: a throw-away slot through prefill and decode."""

@@ -4,7 +4,9 @@ There is no network and no checkpoint, so every run (tests, fixtures, bench)
 uses random-init weights of the reference architecture.  Each tensor gets its
 own generator seeded from ``(seed, name)`` through a stable hash, so any subset
 of the model (for example the first four layers) holds the same values as the
-full model, on any machine with this torch build.
+full model, on any machine with this torch build.  The values depend on the
+generator's device: tensors made with ``device="cuda"`` (fast, used by the
+benchmark) differ from the CPU ones the oracle and the parity tests use.
 
 Names follow the module paths the reference reads:
 ``talker.layers.{i}.self_attn.q_proj.weight`` etc. mirror
