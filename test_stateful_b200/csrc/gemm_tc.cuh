@@ -90,7 +90,8 @@ struct GemmLayout {
     static constexpr int PIPE_BYTES = STAGES * STAGE_BYTES;
     static constexpr int PART_BYTES = BN * 128 * 4;  // fp32 partial, [BN tokens][128 rows]
     static constexpr int BODY = PIPE_BYTES > PART_BYTES ? PIPE_BYTES : PART_BYTES;
-    static constexpr int SCRATCH_BYTES = 4 * 128 * 4;  // epilogue scratch (norm sums / token metadata)
+    static constexpr int SCRATCH_BYTES = 4 * 128 * 4;  // epilogue scratch: [0,136) norm sums / RoPE exchange,
+                                                        // [256,512) token metadata
     static constexpr int BAR_BYTES = 256;
     static constexpr int SMEM = 1024 + BODY + SCRATCH_BYTES + BAR_BYTES;
     static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "stage buffers must keep 1024-B alignment");
@@ -114,18 +115,37 @@ __device__ void gemm_epilogue(const GemmParams& p, float* R, int m0, int per, in
         case QTTS_EPI_BF16:
         case QTTS_EPI_F32:
         case QTTS_EPI_RESIDUAL: {
+            // tokens in batches of 8 so the residual loads of a batch are in flight together
             const float b = p.bias ? __bfloat162float(p.bias[n_g]) : 0.0f;
-            for (int i = grp; i < per; i += NG) {
-                const int m_g = tile_m * BN + m0 + i;
-                if (m_g >= p.M) break;
-                const float v = R[(m0 + i) * 128 + t] + b;
-                const size_t o = (size_t)m_g * p.N + n_g;
-                if (p.epilogue == QTTS_EPI_BF16)
-                    reinterpret_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16(v);
-                else if (p.epilogue == QTTS_EPI_F32)
-                    reinterpret_cast<float*>(p.out)[o] = v;
-                else
-                    reinterpret_cast<float*>(p.out)[o] += v;
+            constexpr int B = 8;
+            for (int i0 = grp; i0 < per; i0 += NG * B) {
+                float v[B];
+                size_t o[B];
+                bool ok[B];
+#pragma unroll
+                for (int u = 0; u < B; ++u) {
+                    const int i = i0 + NG * u;
+                    const int m_g = tile_m * BN + m0 + i;
+                    ok[u] = i < per && m_g < p.M;
+                    v[u] = ok[u] ? R[(m0 + i) * 128 + t] + b : 0.f;
+                    o[u] = ok[u] ? (size_t)m_g * p.N + n_g : 0;
+                }
+                if (p.epilogue == QTTS_EPI_RESIDUAL) {
+                    float old[B];
+#pragma unroll
+                    for (int u = 0; u < B; ++u) old[u] = ok[u] ? reinterpret_cast<const float*>(p.out)[o[u]] : 0.f;
+#pragma unroll
+                    for (int u = 0; u < B; ++u)
+                        if (ok[u]) reinterpret_cast<float*>(p.out)[o[u]] = old[u] + v[u];
+                } else if (p.epilogue == QTTS_EPI_F32) {
+#pragma unroll
+                    for (int u = 0; u < B; ++u)
+                        if (ok[u]) reinterpret_cast<float*>(p.out)[o[u]] = v[u];
+                } else {
+#pragma unroll
+                    for (int u = 0; u < B; ++u)
+                        if (ok[u]) reinterpret_cast<__nv_bfloat16*>(p.out)[o[u]] = __float2bfloat16(v[u]);
+                }
             }
             break;
         }
@@ -158,9 +178,28 @@ __device__ void gemm_epilogue(const GemmParams& p, float* R, int m0, int per, in
                 const int region = n_g < q_rows ? 0 : (n_g < q_rows + k_rows ? 1 : 2);
                 const __nv_bfloat16* nw = region == 0 ? (const __nv_bfloat16*)e.q_norm_w
                                                       : (const __nv_bfloat16*)e.k_norm_w;
+                const float wn = region < 2 ? __bfloat162float(nw[d]) : 0.f;
+                const int half = D >> 1;
+                const int dd = d < half ? d : d - half;
+                const int partner_t = d < half ? t + half : t - half;
+                // token metadata first (positions and slots of all tokens in flight together)
+                int* tok_pos = reinterpret_cast<int*>(scratch) + 256;
+                int* tok_slot = tok_pos + 128;
+                for (int i = t; i < per; i += 128) {
+                    const int m_g = tile_m * BN + m0 + i;
+                    int pos = m_g < p.M ? e.row_pos[m_g] : 0;
+                    tok_pos[i] = pos < 0 ? 0 : (pos >= e.max_pos ? e.max_pos - 1 : pos);  // table bounds
+                    tok_slot[i] = m_g < p.M ? e.slot_mapping[m_g] : -1;
+                }
+                __syncthreads();
                 for (int i = 0; i < per; ++i) {
                     const int m_g = tile_m * BN + m0 + i;
                     if (m_g >= p.M) break;  // uniform across the CTA
+                    float c = 1.f, sn = 0.f;
+                    if (region < 2) {  // issued before the reductions below
+                        c = e.rope_cos[(size_t)tok_pos[i] * half + dd];
+                        sn = e.rope_sin[(size_t)tok_pos[i] * half + dd];
+                    }
                     float v = R[(m0 + i) * 128 + t];
                     // per-head sum of squares (a head spans D/32 warps of this tile)
                     float ss = warp_sum(v * v);
@@ -171,24 +210,18 @@ __device__ void gemm_epilogue(const GemmParams& p, float* R, int m0, int per, in
                         const int w0 = (warp / wpd) * wpd;
                         float tot = 0.f;
                         for (int w = 0; w < wpd; ++w) tot += scratch[w0 + w];
-                        v = v * rsqrtf(tot / (float)D + e.rms_eps) * __bfloat162float(nw[d]);
+                        v = v * rsqrtf(tot / (float)D + e.rms_eps) * wn;
                     }
                     scratch[8 + t] = v;
                     __syncthreads();
-                    int pos = e.row_pos[m_g];
-                    pos = pos < 0 ? 0 : (pos >= e.max_pos ? e.max_pos - 1 : pos);  // table bounds
                     if (region < 2) {
-                        const int half = D >> 1;
-                        const int dd = d < half ? d : d - half;
-                        const float c = e.rope_cos[(size_t)pos * half + dd];
-                        const float s = e.rope_sin[(size_t)pos * half + dd];
-                        const float partner = scratch[8 + (d < half ? t + half : t - half)];
-                        v = d < half ? v * c - partner * s : v * c + partner * s;
+                        const float partner = scratch[8 + partner_t];
+                        v = d < half ? v * c - partner * sn : v * c + partner * sn;
                     }
                     if (region == 0) {
                         reinterpret_cast<float*>(p.out)[(size_t)m_g * q_rows + n_g] = v;  // q stays fp32
                     } else {
-                        const int slot = e.slot_mapping[m_g];
+                        const int slot = tok_slot[i];
                         if (slot >= 0) {
                             const int blk = slot / e.block_size, off = slot % e.block_size;
                             const int g = (n_g - q_rows - (region == 2 ? k_rows : 0)) / D;
