@@ -70,12 +70,20 @@ def bench_gemm(n: int, k: int, m: int, launches: int, seed: int = 0):
     for i in range(3):
         ops.gemm(hi, ws[i % copies], _lib.EPI_F32, out=out, x_lo=lo)
     torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for i in range(launches):
-        ops.gemm(hi, ws[i % copies], _lib.EPI_F32, out=out, x_lo=lo)
-    e1.record()
-    torch.cuda.synchronize()
+    # captured in a CUDA graph: the per-call host path (tensor-map encoding) is not timed
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            for i in range(launches):
+                ops.gemm(hi, ws[i % copies], _lib.EPI_F32, out=out, x_lo=lo)
+        graph.replay()
+        s.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        graph.replay()
+        e1.record(s)
+        s.synchronize()
     sec = e0.elapsed_time(e1) / 1e3 / launches
     algo = n * k * 2 + m * k * 4 + m * n * 4
     return {"kernel": "gemm_tc_kernel<64,3,split>", "n": n, "k": k, "m": m, "launch_us": sec * 1e6,
