@@ -176,32 +176,42 @@ def attention_roofline(ex, slots, peaks):
     max_ctx = ex._config.pool.max_blocks_per_seq * 16
     out = torch.empty(n, t.num_heads * t.head_dim, device=dev, dtype=torch.bfloat16)
     nb = -(-max_ctx // 16)
-    splits = max(1, -(-nb // 16))
+    splits = max(1, -(-nb // 1))  # scratch for any split size
     ws_o = torch.empty(n * t.num_heads * splits * t.head_dim, device=dev)
     ws_ml = torch.empty(n * t.num_heads * splits * 2, device=dev)
     table = m.pool.block_table
-    s = torch.cuda.current_stream()
+
+    split = int(os.environ.get("QTTS_ATTN_SPLIT", "16"))  # the engine's split size
 
     def run(layer):
-        ops.paged_attention(q, m.pool.kv, layer, table, row_slot, ctx, max_ctx, out=out, ws_o=ws_o, ws_ml=ws_ml)
+        ops.paged_attention(q, m.pool.kv, layer, table, row_slot, ctx, max_ctx, out=out, ws_o=ws_o, ws_ml=ws_ml,
+                            split_blocks=split)
 
     for layer in range(3):
         run(layer)
     torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # all layers of the pool, twice, captured in a CUDA graph and replayed on one stream
     reps = 2 * t.num_layers
-    e0.record(s)
-    for i in range(reps):
-        run(i % t.num_layers)
-    e1.record(s)
-    torch.cuda.synchronize()
+    gs = torch.cuda.Stream()
+    with torch.cuda.stream(gs):
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=gs):
+            for i in range(reps):
+                run(i % t.num_layers)
+        graph.replay()
+        gs.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(gs)
+        graph.replay()
+        e1.record(gs)
+        gs.synchronize()
     sec = e0.elapsed_time(e1) / 1e3 / reps
     kv_bytes = int(ctx.sum()) * 2 * t.kv_heads * t.head_dim * 2      # K+V of one layer
     qo_bytes = n * t.num_heads * t.head_dim * (4 + 2)
     algo = kv_bytes + qo_bytes
     gbs = algo / sec / 1e9
     peak = peaks.get("hbm_gbs")
-    return {"kernel": "paged_attn_kernel<128> + attn_combine_kernel<128>", "bound": "hbm", "achieved": round(gbs, 1),
+    return {"kernel": "paged_attn_tc_kernel + attn_combine_kernel", "bound": "hbm", "achieved": round(gbs, 1),
             "peak": peak, "unit": "GB/s", "frac": round(gbs / peak, 3) if peak else None, "traffic": None,
             "algorithmic_bytes_per_launch": algo, "launch_us": round(sec * 1e6, 2),
             "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)"}

@@ -159,13 +159,15 @@ int qtts_rmsnorm(const float* x, int M, int H, int ld, const void* w, float eps,
  * out_lo (optional): its bf16 residual (lo half of the next GEMM's operand).
  * Scratch: partial results for the split-KV reduction, allocated by the caller:
  * ws_o [R*num_heads*max_splits*head_dim] fp32, ws_ml [R*num_heads*max_splits*2] fp32,
- * with max_splits = ceil(max_ctx / (16*QTTS_ATTN_SPLIT_BLOCKS)).
+ * with max_splits = ceil(max_ctx / (16*split_blocks)); split_blocks = KV blocks per split
+ * (0 = QTTS_ATTN_SPLIT_BLOCKS; fewer blocks per split shorten each warp's chain of copies
+ * at the cost of more partials).
  * (talker_unified_modules.py:159-201 with the padded bias of batch_helper.py:48-66.) */
 #define QTTS_ATTN_SPLIT_BLOCKS 16
 int qtts_paged_attention(const void* q, int R, int num_heads, int kv_heads, int head_dim,
                          const void* kv_pool, int layer, int num_layers, int block_size, int num_blocks,
                          const int32_t* block_table, int max_blocks_per_seq,
-                         const int32_t* row_slot, const int32_t* row_ctx, int max_ctx,
+                         const int32_t* row_slot, const int32_t* row_ctx, int max_ctx, int split_blocks,
                          float* ws_o, float* ws_ml, void* out, void* out_lo, qtts_stream_t stream);
 
 /* Same computation as qtts_paged_attention, for callers that cannot allocate device memory

@@ -134,7 +134,7 @@ def load() -> C.CDLL:
         "qtts_gemm": ([P, P, C.c_int, C.c_int, P, C.c_int, C.c_int, P, P, P, C.POINTER(QkvEpilogue), P], C.c_int),
         "qtts_rmsnorm": ([P, C.c_int, C.c_int, C.c_int, P, C.c_float, P, P, P], C.c_int),
         "qtts_paged_attention": ([P, C.c_int, C.c_int, C.c_int, C.c_int, P, C.c_int, C.c_int, C.c_int, C.c_int,
-                                  P, C.c_int, P, P, C.c_int, P, P, P, P, P], C.c_int),
+                                  P, C.c_int, P, P, C.c_int, C.c_int, P, P, P, P, P], C.c_int),
         "qtts_paged_attention_noalloc": ([P, C.c_int, C.c_int, C.c_int, C.c_int, P, C.c_int, C.c_int, C.c_int,
                                           C.c_int, P, C.c_int, P, P, C.c_int, P, P, P], C.c_int),
         "qtts_sample": ([P, C.c_int, C.c_int, C.c_int, C.c_int, P, C.c_int, C.c_uint64, P, C.c_int, P, P, P,

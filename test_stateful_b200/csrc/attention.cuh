@@ -1,6 +1,6 @@
 // Paged GQA attention over the block pool (decode and chunked prefill rows).
 //
-// One CTA per (query row, kv head, split of QTTS_ATTN_SPLIT_BLOCKS blocks).
+// One CTA per (query row, kv head, split of split_blocks KV blocks).
 // Each of the 4 warps owns every 4th KV block of the split and streams it
 // through its own STAGES-deep ring in shared memory: lane 0 issues two bulk
 // copies (K chunk and V chunk of one block, head, layer: block_size x D bf16,
@@ -35,6 +35,7 @@ struct AttnParams {
     const int32_t* row_slot;
     const int32_t* row_ctx;
     int max_splits;
+    int split_blocks;  // KV blocks per split (QTTS_ATTN_SPLIT_BLOCKS unless a caller sizes its scratch for another)
     float scale_log2;  // log2(e) / sqrt(D)
     float* ws_o;
     float* ws_ml;
@@ -43,14 +44,23 @@ struct AttnParams {
     int R;
 };
 
-constexpr int kAttnStages = 3;
+// Ring depth per warp (QTTS_ATTN_STAGES, default below): 3 stages x 8 KB x 4
+// warps hold 2 CTAs per SM; 2 stages hold 3.
+inline int attn_stages() {
+    static const int s = [] {
+        const char* v = getenv("QTTS_ATTN_STAGES");
+        const int x = (v && *v) ? atoi(v) : 2;
+        return (x == 2 || x == 3 || x == 4) ? x : 2;
+    }();
+    return s;
+}
 
-template <int D>
+template <int D, int STAGES>
 struct AttnLayout {
     static constexpr int CHUNK = 16 * D * 2;  // one block's K (or V) for one head, bytes
     static constexpr int STAGE = 2 * CHUNK;
-    static constexpr int WARP_BYTES = kAttnStages * STAGE;
-    static constexpr int SMEM = 128 + 4 * WARP_BYTES + 4 * kAttnStages * 8;
+    static constexpr int WARP_BYTES = STAGES * STAGE;
+    static constexpr int SMEM = 128 + 4 * WARP_BYTES + 4 * STAGES * 8;
 };
 
 template <int D>
@@ -72,9 +82,9 @@ __device__ __forceinline__ void load_row(const kv_t* base, int lane, float (&v)[
     }
 }
 
-template <int D>
+template <int D, int kAttnStages>
 __global__ void __launch_bounds__(128) paged_attn_kernel(const AttnParams p) {
-    using L = AttnLayout<D>;
+    using L = AttnLayout<D, kAttnStages>;
     constexpr int DPL = D / 32;  // dims per lane
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
@@ -86,8 +96,8 @@ __global__ void __launch_bounds__(128) paged_attn_kernel(const AttnParams p) {
     griddep_launch();
     const int ctx = p.row_ctx[r];
     const int nbt = (ctx + 15) >> 4;
-    const int b_start = sp * QTTS_ATTN_SPLIT_BLOCKS;
-    const int b_end = min(nbt, b_start + QTTS_ATTN_SPLIT_BLOCKS);
+    const int b_start = sp * p.split_blocks;
+    const int b_end = min(nbt, b_start + p.split_blocks);
     if (b_start >= b_end) {  // uniform for the CTA
         if (nbt == 0 && sp == 0) {  // a row with no keys (only after a scheduler error): zero output
             for (int i = threadIdx.x; i < 2 * D; i += blockDim.x) {
@@ -269,7 +279,7 @@ __global__ void __launch_bounds__(128) paged_attn_kernel(const AttnParams p) {
             lsum += red[(w * 2 + h) * RS + D + 1] * f;
         }
         const size_t hrow = (size_t)r * p.num_heads + g * 2 + h;
-        if (nbt <= QTTS_ATTN_SPLIT_BLOCKS) {
+        if (nbt <= p.split_blocks) {
             // the row has a single split: finish here, the combine kernel skips it
             const float o = lsum > 0.f ? acc / lsum : 0.f;
             const __nv_bfloat16 hi = __float2bfloat16(o);
@@ -285,6 +295,331 @@ __global__ void __launch_bounds__(128) paged_attn_kernel(const AttnParams p) {
     }
 }
 
+// ---------------------------------------------------------------------------
+// head_dim 128: one warp per (split, row, kv head) work item, each with its own
+// ring of whole blocks and no cross-warp merge, so a CTA is four independent
+// streams and a layer's items fit in about one wave; the per-block math runs on
+// the tensor pipe (warp-level mma.sync, m16n8k16, fp16 inputs, fp32
+// accumulators).
+//
+// The K and V chunks of a block come in by TMA as two 16 x 64 boxes each with
+// the 128-B swizzle, so the ldmatrix row reads below hit eight different
+// bank groups.  Per 16-token block and warp:
+//   S^T[16 tok][8] = K[16][128] · Q^T[128][8]   (8 k-steps; Q^T columns 0, 1 =
+//                     the two q heads, carried as an fp16 hi/lo pair so the
+//                     scores keep ~fp32 accuracy; columns 2..7 zero)
+//   online softmax on the 32 real scores (lanes 4k hold tokens k, k+8)
+//   O^T[128][8] += V^T[128][16] · P^T[16][8]    (8 m-tiles; P as fp16 hi/lo)
+// ~130 instructions per block instead of ~900 for the same math on FMAs.
+// ---------------------------------------------------------------------------
+constexpr int kTcBox = 16 * 128;         // one 16-token x 64-dim fp16 box, bytes
+constexpr int kTcStage = 4 * kTcBox;     // K dims 0-63, K 64-127, V 0-63, V 64-127
+
+template <int S>
+struct AttnTcLayout {
+    static constexpr int WARP_BYTES = S * kTcStage;
+    static constexpr int SMEM = 1024 + 4 * WARP_BYTES + 4 * S * 8;
+};
+
+// byte address (shared window) of the 16-B chunk holding (row, dim..dim+7) of a
+// [16 rows][128 dims] tile stored as two swizzled 16 x 64 boxes
+__device__ __forceinline__ uint32_t tc_sw128(uint32_t tile, int row, int dim) {
+    return tile + (uint32_t)((dim >> 6) * kTcBox + row * 128 + ((((dim & 63) >> 3) ^ (row & 7)) << 4));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// (hi, lo) fp16 pairs of two floats: hi = fp16(x), lo = fp16(x - hi)
+__device__ __forceinline__ void split_h2(float a, float b, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(a, b);
+    const float2 hf = __half22float2(h);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = pack_h2(a - hf.x, b - hf.y);
+}
+
+template <int S>
+__global__ void __launch_bounds__(128) paged_attn_tc_kernel(const __grid_constant__ CUtensorMap tmKV,
+                                                            const AttnParams p) {
+    constexpr int D = 128;
+    using L = AttnTcLayout<S>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 4 * L::WARP_BYTES);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int gq = lane >> 2, qq = lane & 3;  // mma fragment coordinates
+    griddep_wait();
+    griddep_launch();
+    // work item of this warp: (split, row, kv head), heads fastest, so the four warps
+    // of a CTA share a row and have the same amount of work
+    const int item = blockIdx.x * 4 + warp;
+    if (item >= p.R * p.kv_heads * p.max_splits) return;  // warp-uniform
+    const int g = item % p.kv_heads;
+    const int r = (item / p.kv_heads) % p.R;
+    const int sp = item / (p.kv_heads * p.R);
+    const int ctx = p.row_ctx[r];
+    const int nbt = (ctx + 15) >> 4;
+    const int b_start = sp * p.split_blocks;
+    const int b_end = min(nbt, b_start + p.split_blocks);
+    const size_t hrow0 = (size_t)r * p.num_heads + g * 2;
+    if (b_start >= b_end) {
+        if (nbt == 0 && sp == 0) {  // a row with no keys (only after a scheduler error): zero output
+            for (int i = lane; i < 2 * D; i += 32) {
+                p.out[hrow0 * D + i] = __float2bfloat16(0.f);
+                if (p.out_lo) p.out_lo[hrow0 * D + i] = __float2bfloat16(0.f);
+            }
+        }
+        return;
+    }
+    const int slot = p.row_slot[r];
+
+    // Q^T fragments (B operand): lane (gq, qq) holds head gq's dims 16s + 2qq (+1) and +8 (+9)
+    uint32_t qh[8][2], ql[8][2];
+    {
+        const float* qb = p.q + (hrow0 + (gq < 2 ? gq : 0)) * D;
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+            const int d0 = 16 * s + 2 * qq;
+            float v[4] = {0.f, 0.f, 0.f, 0.f};
+            if (gq < 2) {
+                v[0] = qb[d0] * p.scale_log2;
+                v[1] = qb[d0 + 1] * p.scale_log2;
+                v[2] = qb[d0 + 8] * p.scale_log2;
+                v[3] = qb[d0 + 9] * p.scale_log2;
+            }
+            split_h2(v[0], v[1], qh[s][0], ql[s][0]);
+            split_h2(v[2], v[3], qh[s][1], ql[s][1]);
+        }
+    }
+
+    uint8_t* wbuf = smem + warp * L::WARP_BYTES;
+    uint64_t* wbar = bars + warp * S;
+    if (lane == 0) {
+        for (int s = 0; s < S; ++s) mbar_init(&wbar[s], 1);
+        tma_prefetch_desc(&tmKV);
+        fence_mbar_init();
+    }
+    __syncwarp();
+
+    const int n_mine = b_end - b_start;
+    auto issue = [&](int i) {
+        const int jb = b_start + i;
+        const int s = i % S;
+        int blk = jb < p.mbps ? p.block_table[(size_t)slot * p.mbps + jb] : -1;
+        if (blk < 0 || blk >= p.num_blocks) {
+            record_error(DEV_ERR_ATTN_WAIT);
+            blk = 0;  // stay in bounds; the error word reports the bad table entry
+        }
+        const int krow = (((blk * p.num_layers + p.layer) * 2 + 0) * p.kv_heads + g) * 16;
+        const int vrow = krow + p.kv_heads * 16;
+        uint8_t* dst = wbuf + s * kTcStage;
+        mbar_arrive_expect_tx(&wbar[s], kTcStage);
+        tma_load_2d(dst, &tmKV, &wbar[s], 0, krow);
+        tma_load_2d(dst + kTcBox, &tmKV, &wbar[s], 64, krow);
+        tma_load_2d(dst + 2 * kTcBox, &tmKV, &wbar[s], 0, vrow);
+        tma_load_2d(dst + 3 * kTcBox, &tmKV, &wbar[s], 64, vrow);
+    };
+
+    int issued = 0;
+    if (lane == 0) {
+        for (int i = 0; i < n_mine && i < S; ++i) issue(i);
+        issued = min(n_mine, S);
+    }
+    issued = __shfl_sync(0xffffffffu, issued, 0);
+
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    float o[8][4];
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+
+    // ldmatrix row addresses: lane supplies row (lane & 7) of matrix (lane >> 3)
+    const int mi = lane >> 3, rr = lane & 7;
+    const int k_tok = (mi & 1) * 8 + rr, k_dim = (mi >> 1) * 8;  // K as the A operand (rows = tokens)
+    const int v_tok = (mi >> 1) * 8 + rr, v_dim = (mi & 1) * 8;  // V^T as the A operand (transposed load)
+
+    int done = 0;
+    bool failed = false;
+    for (int i = 0; i < n_mine; ++i) {
+        const int s = i % S;
+        if (!mbar_wait(&wbar[s], (uint32_t)(i / S) & 1u, DEV_ERR_ATTN_WAIT)) {
+            failed = true;
+            break;
+        }
+        const uint32_t kb = smem_u32(wbuf + s * kTcStage);
+        const uint32_t vb = kb + 2 * kTcBox;
+        const int jb = b_start + i;
+
+        // ---- S^T = K Q^T
+        float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+            uint32_t a[4];
+            ldsm_x4(tc_sw128(kb, k_tok, 16 * ks + k_dim), a);
+            mma_16816(sc, a, qh[ks][0], qh[ks][1]);
+            mma_16816(sc, a, ql[ks][0], ql[ks][1]);
+        }
+        // lanes with qq == 0: sc[0] = (tok gq, head 0), sc[1] = (tok gq, head 1), sc[2], sc[3] = tok gq + 8
+        const int tA = jb * 16 + gq, tB = tA + 8;
+        const float s00 = tA < ctx ? sc[0] : -INFINITY, s01 = tA < ctx ? sc[1] : -INFINITY;
+        const float s10 = tB < ctx ? sc[2] : -INFINITY, s11 = tB < ctx ? sc[3] : -INFINITY;
+        float bm0 = fmaxf(s00, s10), bm1 = fmaxf(s01, s11);
+#pragma unroll
+        for (int off = 4; off <= 16; off <<= 1) {
+            bm0 = fmaxf(bm0, __shfl_xor_sync(0xffffffffu, bm0, off));
+            bm1 = fmaxf(bm1, __shfl_xor_sync(0xffffffffu, bm1, off));
+        }
+        // every processed block has at least one visible key, so bm0/bm1 are finite
+        const float mn0 = fmaxf(m0, bm0), mn1 = fmaxf(m1, bm1);
+        float a0 = m0 == -INFINITY ? 0.f : exp2f(m0 - mn0);
+        float a1 = m1 == -INFINITY ? 0.f : exp2f(m1 - mn1);
+        const float p00 = s00 == -INFINITY ? 0.f : exp2f(s00 - mn0);
+        const float p01 = s01 == -INFINITY ? 0.f : exp2f(s01 - mn1);
+        const float p10 = s10 == -INFINITY ? 0.f : exp2f(s10 - mn0);
+        const float p11 = s11 == -INFINITY ? 0.f : exp2f(s11 - mn1);
+        float ps0 = p00 + p10, ps1 = p01 + p11;
+#pragma unroll
+        for (int off = 4; off <= 16; off <<= 1) {
+            ps0 += __shfl_xor_sync(0xffffffffu, ps0, off);
+            ps1 += __shfl_xor_sync(0xffffffffu, ps1, off);
+        }
+        l0 = l0 * a0 + ps0;
+        l1 = l1 * a1 + ps1;
+        m0 = mn0;
+        m1 = mn1;
+        if (qq != 0) a0 = a1 = 0.f;  // these lanes' O^T columns are padding heads (kept at zero)
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+            o[mt][0] *= a0;
+            o[mt][1] *= a1;
+            o[mt][2] *= a0;
+            o[mt][3] *= a1;
+        }
+        // ---- P^T fragments: lane (gq = head, qq) needs P[gq][2qq], [2qq+1], [2qq+8], [2qq+9];
+        // P[h][k] sits in lane 4k (k < 8) or 4(k-8) (k >= 8)
+        const int src1 = 8 * qq, src2 = 8 * qq + 4;
+        const float x0 = __shfl_sync(0xffffffffu, p00, src1), x1 = __shfl_sync(0xffffffffu, p01, src1);
+        const float y0 = __shfl_sync(0xffffffffu, p00, src2), y1 = __shfl_sync(0xffffffffu, p01, src2);
+        const float z0 = __shfl_sync(0xffffffffu, p10, src1), z1 = __shfl_sync(0xffffffffu, p11, src1);
+        const float w0 = __shfl_sync(0xffffffffu, p10, src2), w1 = __shfl_sync(0xffffffffu, p11, src2);
+        float pa = 0.f, pb = 0.f, pc = 0.f, pd = 0.f;
+        if (gq == 0) {
+            pa = x0; pb = y0; pc = z0; pd = w0;
+        } else if (gq == 1) {
+            pa = x1; pb = y1; pc = z1; pd = w1;
+        }
+        uint32_t bh0, bl0, bh1, bl1;
+        split_h2(pa, pb, bh0, bl0);
+        split_h2(pc, pd, bh1, bl1);
+        // ---- O^T += V^T P^T
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+            uint32_t a[4];
+            ldsm_x4_t(tc_sw128(vb, v_tok, 16 * mt + v_dim), a);
+            mma_16816(o[mt], a, bh0, bh1);
+            mma_16816(o[mt], a, bl0, bl1);
+        }
+        ++done;
+        __syncwarp();
+        if (lane == 0 && i + S < n_mine) {
+            fence_proxy_async_smem();
+            issue(i + S);
+            ++issued;
+        }
+        issued = __shfl_sync(0xffffffffu, issued, 0);
+    }
+    if (failed && lane == 0) {
+        for (int i = done; i < issued; ++i) mbar_wait(&wbar[i % S], (uint32_t)(i / S) & 1u, DEV_ERR_DRAIN);
+    }
+
+    // ---- finish: lanes with qq == 0 hold O^T[dims 16mt + gq (+8)][heads 0, 1]
+    if (nbt <= p.split_blocks) {  // a single split: final output
+        if (qq == 0) {
+            const float i0 = l0 > 0.f ? 1.f / l0 : 0.f, i1 = l1 > 0.f ? 1.f / l1 : 0.f;
+#pragma unroll
+            for (int mt = 0; mt < 8; ++mt) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int h = e & 1, d = 16 * mt + gq + (e >> 1) * 8;
+                    const float ov = o[mt][e] * (h ? i1 : i0);
+                    const __nv_bfloat16 hi = __float2bfloat16(ov);
+                    p.out[(hrow0 + h) * D + d] = hi;
+                    if (p.out_lo) p.out_lo[(hrow0 + h) * D + d] = __float2bfloat16(ov - __bfloat162float(hi));
+                }
+            }
+        }
+        return;
+    }
+    if (qq == 0) {
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int h = e & 1, d = 16 * mt + gq + (e >> 1) * 8;
+                p.ws_o[((hrow0 + h) * p.max_splits + sp) * D + d] = o[mt][e];
+            }
+        }
+    }
+    if (lane == 0) {
+        p.ws_ml[((hrow0 + 0) * p.max_splits + sp) * 2 + 0] = m0;
+        p.ws_ml[((hrow0 + 0) * p.max_splits + sp) * 2 + 1] = l0;
+        p.ws_ml[((hrow0 + 1) * p.max_splits + sp) * 2 + 0] = m1;
+        p.ws_ml[((hrow0 + 1) * p.max_splits + sp) * 2 + 1] = l1;
+    }
+}
+
+// fp16 KV pool as a 2-D tensor [blocks*layers*2*kv_heads*16 rows][128] with 16 x 64 swizzled boxes
+inline int make_kv_map(CUtensorMap* map, const AttnParams& p) {
+    const uint64_t rows = (uint64_t)p.num_blocks * p.num_layers * 2 * p.kv_heads * 16;
+    if (rows >= (1ull << 31)) {
+        set_error("paged attention: pool too large for 32-bit tensor-map rows");
+        return QTTS_ERR_UNSUPPORTED;
+    }
+    PFN_encodeTiled enc = get_encode_fn();
+    if (!enc) {
+        set_error("cuTensorMapEncodeTiled unavailable");
+        return QTTS_ERR_CUDA;
+    }
+    if ((reinterpret_cast<uintptr_t>(p.kv) & 15) != 0) {
+        set_error("paged attention: KV pool must be 16-byte aligned");
+        return QTTS_ERR_INVALID;
+    }
+    cuuint64_t dims[2] = {128, rows};
+    cuuint64_t strides[1] = {256};
+    cuuint32_t box[2] = {64, 16};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult rc = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<kv_t*>(p.kv), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (rc != CUDA_SUCCESS) {
+        set_error("cuTensorMapEncodeTiled (KV pool) failed (%d)", (int)rc);
+        return QTTS_ERR_CUDA;
+    }
+    return QTTS_OK;
+}
+
 // Fold split partials: out = Σ_s o_s 2^(m_s - M) / Σ_s l_s 2^(m_s - M), bf16.
 template <int D>
 __global__ void attn_combine_kernel(const AttnParams p) {
@@ -293,7 +628,7 @@ __global__ void attn_combine_kernel(const AttnParams p) {
     griddep_launch();
     const int ctx = p.row_ctx[r];
     const int nbt = (ctx + 15) >> 4;
-    const int ns = min(p.max_splits, (nbt + QTTS_ATTN_SPLIT_BLOCKS - 1) / QTTS_ATTN_SPLIT_BLOCKS);
+    const int ns = min(p.max_splits, (nbt + p.split_blocks - 1) / p.split_blocks);
     if (ns <= 1) return;  // single-split (and empty) rows were finished by paged_attn_kernel
     const size_t hrow = (size_t)r * p.num_heads + h;
     float M = -INFINITY;
@@ -311,21 +646,76 @@ __global__ void attn_combine_kernel(const AttnParams p) {
     if (p.out_lo) p.out_lo[hrow * D + d] = __float2bfloat16(o - __bfloat162float(hi));
 }
 
-inline int attn_max_splits(int max_ctx) {
+// KV blocks per split in the engine's decode step (QTTS_ATTN_SPLIT to override)
+inline int attn_engine_split() {
+    static const int s = [] {
+        const char* v = getenv("QTTS_ATTN_SPLIT");
+        const int x = (v && *v) ? atoi(v) : QTTS_ATTN_SPLIT_BLOCKS;
+        return (x >= 1 && x <= 64) ? x : QTTS_ATTN_SPLIT_BLOCKS;
+    }();
+    return s;
+}
+
+inline int attn_max_splits(int max_ctx, int split_blocks = QTTS_ATTN_SPLIT_BLOCKS) {
     const int nb = (max_ctx + 15) / 16;
-    const int s = (nb + QTTS_ATTN_SPLIT_BLOCKS - 1) / QTTS_ATTN_SPLIT_BLOCKS;
+    const int s = (nb + split_blocks - 1) / split_blocks;
     return s > 1 ? s : 1;
+}
+
+template <int D, int S>
+inline int launch_attention_s(const AttnParams& p, cudaStream_t st) {
+    using L = AttnLayout<D, S>;
+    auto kern = paged_attn_kernel<D, S>;
+    static bool attr = false;
+    if (!attr) {
+        QTTS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM));
+        attr = true;
+    }
+    QTTS_LAUNCH(kern, dim3(p.R, p.kv_heads, p.max_splits), dim3(128), L::SMEM, st, p);
+    return QTTS_OK;
+}
+
+template <int S>
+inline int launch_attention_tc(const AttnParams& p, cudaStream_t st) {
+    using L = AttnTcLayout<S>;
+    CUtensorMap map;
+    const int rc = make_kv_map(&map, p);
+    if (rc) return rc;
+    auto kern = paged_attn_tc_kernel<S>;
+    static bool attr = false;
+    if (!attr) {
+        QTTS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM));
+        attr = true;
+    }
+    const int items = p.R * p.kv_heads * p.max_splits;  // one (split, row, kv head) per warp
+    QTTS_LAUNCH(kern, dim3(ceil_div(items, 4)), dim3(128), L::SMEM, st, map, p);
+    return QTTS_OK;
+}
+
+// head_dim 128 runs on the tensor pipe unless QTTS_ATTN_TC=0
+inline bool attn_use_tc() {
+    static const bool on = [] {
+        const char* v = getenv("QTTS_ATTN_TC");
+        return !(v && *v == '0');
+    }();
+    return on;
 }
 
 template <int D>
 inline int launch_attention_d(const AttnParams& p, cudaStream_t st) {
-    using L = AttnLayout<D>;
-    static bool attr = false;
-    if (!attr) {
-        QTTS_CHECK_CUDA(cudaFuncSetAttribute(paged_attn_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM));
-        attr = true;
+    int rc;
+    if (D == 128 && attn_use_tc()) {
+        rc = attn_stages() == 3 ? launch_attention_tc<3>(p, st) : launch_attention_tc<2>(p, st);
+        if (rc) return rc;
+        if (p.max_splits > 1) QTTS_LAUNCH(attn_combine_kernel<D>, dim3(p.R, p.num_heads), dim3(D), 0, st, p);
+        return QTTS_OK;
     }
-    QTTS_LAUNCH(paged_attn_kernel<D>, dim3(p.R, p.kv_heads, p.max_splits), dim3(128), L::SMEM, st, p);
+    switch (attn_stages()) {
+        case 3: rc = launch_attention_s<D, 3>(p, st); break;
+        case 4: rc = launch_attention_s<D, 4>(p, st); break;
+        default: rc = launch_attention_s<D, 2>(p, st); break;
+    }
+    if (rc) return rc;
     if (p.max_splits > 1)  // otherwise every row finished inside paged_attn_kernel
         QTTS_LAUNCH(attn_combine_kernel<D>, dim3(p.R, p.num_heads), dim3(D), 0, st, p);
     return QTTS_OK;

@@ -46,6 +46,7 @@ struct qtts_engine {
     int bmax;        // streams per call
     int qkv_rows, cp_qkv_rows;
     int max_splits, cp_max_splits;
+    int attn_split;  // KV blocks per attention split (talker)
     // talker activations
     // GEMM operands are hi/lo bf16 pairs (x_lo = bf16(x - x_hi)), see gemm_tc.cuh
     float* x = nullptr;              // [rmax][H] fp32 residual stream
@@ -107,7 +108,8 @@ inline int engine_build(qtts_engine* e) {
     e->rmax = d.max_batch > d.max_prefill_rows ? d.max_batch : d.max_prefill_rows;
     e->qkv_rows = (Hq + 2 * Hkv) * D;
     const int max_ctx = d.pool.max_blocks_per_seq * d.pool.block_size;
-    e->max_splits = attn_max_splits(max_ctx);
+    e->attn_split = attn_engine_split();
+    e->max_splits = attn_max_splits(max_ctx, e->attn_split);
     const int rmax = e->rmax, bmax = e->bmax;
     QTTS_TRY(dev_alloc(e, &e->x, (size_t)rmax * H));
     QTTS_TRY(dev_alloc(e, &e->xn, (size_t)rmax * H));
@@ -296,6 +298,7 @@ inline int engine_step_impl(qtts_engine* e, const qtts_step_io& io, cudaStream_t
     ap.row_slot = e->row_slot;
     ap.row_ctx = e->row_ctx;
     ap.max_splits = e->max_splits;
+    ap.split_blocks = e->attn_split;
     ap.scale_log2 = 1.4426950408889634f / sqrtf((float)D);
     ap.ws_o = e->ws_o;
     ap.ws_ml = e->ws_ml;
@@ -360,6 +363,7 @@ inline int engine_step_impl(qtts_engine* e, const qtts_step_io& io, cudaStream_t
     cap.block_table = e->cp_table;
     cap.mbps = 1;
     cap.max_splits = 1;
+    cap.split_blocks = QTTS_ATTN_SPLIT_BLOCKS;
     cap.scale_log2 = 1.4426950408889634f / sqrtf((float)cD);
     cap.ws_o = e->cws_o;
     cap.ws_ml = e->cws_ml;

@@ -164,7 +164,8 @@ int qtts_rmsnorm(const float* x, int M, int H, int ld, const void* w, float eps,
 int qtts_paged_attention(const void* q, int R, int num_heads, int kv_heads, int head_dim, const void* kv_pool,
                          int layer, int num_layers, int block_size, int num_blocks, const int32_t* block_table,
                          int max_blocks_per_seq, const int32_t* row_slot, const int32_t* row_ctx, int max_ctx,
-                         float* ws_o, float* ws_ml, void* out, void* out_lo, qtts_stream_t stream) {
+                         int split_blocks, float* ws_o, float* ws_ml, void* out, void* out_lo,
+                         qtts_stream_t stream) {
     QTTS_REQUIRE(q && kv_pool && block_table && row_slot && row_ctx && ws_o && ws_ml && out && R >= 0,
                  "paged_attention: null pointer");
     QTTS_REQUIRE(block_size == 16, "paged_attention: block_size must be 16");
@@ -184,7 +185,9 @@ int qtts_paged_attention(const void* q, int R, int num_heads, int kv_heads, int 
     p.mbps = max_blocks_per_seq;
     p.row_slot = row_slot;
     p.row_ctx = row_ctx;
-    p.max_splits = attn_max_splits(max_ctx);
+    QTTS_REQUIRE(split_blocks >= 0 && split_blocks <= 1024, "paged_attention: split_blocks out of range");
+    p.split_blocks = split_blocks > 0 ? split_blocks : QTTS_ATTN_SPLIT_BLOCKS;
+    p.max_splits = attn_max_splits(max_ctx, p.split_blocks);
     p.scale_log2 = 1.4426950408889634f / sqrtf((float)head_dim);
     p.ws_o = ws_o;
     p.ws_ml = ws_ml;
@@ -369,6 +372,6 @@ extern "C" int qtts_paged_attention_noalloc(const void* q, int R, int num_heads,
     const int rc = noalloc_scratch(&scratch);
     if (rc != QTTS_OK) return rc;
     return qtts_paged_attention(q, R, num_heads, kv_heads, head_dim, kv_pool, layer, num_layers, block_size,
-                                num_blocks, block_table, max_blocks_per_seq, row_slot, row_ctx, max_ctx, scratch,
+                                num_blocks, block_table, max_blocks_per_seq, row_slot, row_ctx, max_ctx, 0, scratch,
                                 scratch + kNoAllocMaxPartials, out, out_lo, stream);
 }

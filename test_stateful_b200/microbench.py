@@ -22,7 +22,7 @@ import torch
 from . import _lib, ops
 
 
-def bench_attention(rows: int, ctx_mean: int, launches: int, layers: int = 4, seed: int = 0):
+def bench_attention(rows: int, ctx_mean: int, launches: int, layers: int = 4, seed: int = 0, split: int = 0):
     dev = "cuda"
     g = torch.Generator().manual_seed(seed)
     lo, hi = max(1, ctx_mean // 2), ctx_mean * 3 // 2
@@ -45,17 +45,27 @@ def bench_attention(rows: int, ctx_mean: int, launches: int, layers: int = 4, se
     out_lo = torch.empty_like(out)
     max_ctx = mbps * 16
     for i in range(3):
-        ops.paged_attention(q, kv, i % layers, table, row_slot, row_ctx, max_ctx, out=out, out_lo=out_lo)
+        ops.paged_attention(q, kv, i % layers, table, row_slot, row_ctx, max_ctx, out=out, out_lo=out_lo,
+                                    split_blocks=split)
     torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for i in range(launches):
-        ops.paged_attention(q, kv, i % layers, table, row_slot, row_ctx, max_ctx, out=out, out_lo=out_lo)
-    e1.record()
-    torch.cuda.synchronize()
+    # captured in a CUDA graph: the per-call host path is not timed
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            for i in range(launches):
+                ops.paged_attention(q, kv, i % layers, table, row_slot, row_ctx, max_ctx, out=out, out_lo=out_lo,
+                                    split_blocks=split)
+        graph.replay()
+        s.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        graph.replay()
+        e1.record(s)
+        s.synchronize()
     sec = e0.elapsed_time(e1) / 1e3 / launches
     algo = int(ctx.sum()) * 2 * 8 * 128 * 2 + rows * 16 * 128 * (4 + 4)
-    return {"kernel": "paged_attn_kernel<128>", "rows": rows, "ctx_sum": int(ctx.sum()), "launch_us": sec * 1e6,
+    return {"kernel": "paged_attn_tc_kernel", "split_blocks": split or 16, "rows": rows, "ctx_sum": int(ctx.sum()), "launch_us": sec * 1e6,
             "algorithmic_bytes": algo, "achieved_gbs": algo / sec / 1e9}
 
 
@@ -140,9 +150,10 @@ def main():
     ap.add_argument("--k", type=int, default=2048)
     ap.add_argument("--m", type=int, default=64)
     ap.add_argument("--launches", type=int, default=50)
+    ap.add_argument("--split", type=int, default=0, help="attention: KV blocks per split (0: library default)")
     a = ap.parse_args()
     if a.what == "attention":
-        r = bench_attention(a.rows, a.ctx_mean, a.launches)
+        r = bench_attention(a.rows, a.ctx_mean, a.launches, split=a.split)
     elif a.what == "code2wav":
         r = bench_code2wav(a.rows, a.launches)
     else:

@@ -66,13 +66,15 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, rows: Optional[int] = 
 def paged_attention(q: torch.Tensor, kv_pool: torch.Tensor, layer: int, block_table: torch.Tensor,
                     row_slot: torch.Tensor, row_ctx: torch.Tensor, max_ctx: int,
                     out: Optional[torch.Tensor] = None, ws_o: Optional[torch.Tensor] = None,
-                    ws_ml: Optional[torch.Tensor] = None, out_lo: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """``q [R, Hq, D]`` fp32 over ``kv_pool [blocks, L, 2, Hkv, 16, D]`` bf16."""
+                    ws_ml: Optional[torch.Tensor] = None, out_lo: Optional[torch.Tensor] = None,
+                    split_blocks: int = 0) -> torch.Tensor:
+    """``q [R, Hq, D]`` fp32 over ``kv_pool [blocks, L, 2, Hkv, 16, D]`` fp16; ``split_blocks``
+    KV blocks per split (0: the library default)."""
     _need_cuda(q, kv_pool, block_table, row_slot, row_ctx)
     R, Hq, D = q.shape
     nb, L, _, Hkv, bs, _ = kv_pool.shape
     n_blocks = -(-max_ctx // bs)
-    splits = max(1, -(-n_blocks // _lib.ATTN_SPLIT_BLOCKS))
+    splits = max(1, -(-n_blocks // (split_blocks or _lib.ATTN_SPLIT_BLOCKS)))
     if out is None:
         out = torch.empty(R, Hq * D, device=q.device, dtype=torch.bfloat16)
     if ws_o is None:
@@ -81,7 +83,7 @@ def paged_attention(q: torch.Tensor, kv_pool: torch.Tensor, layer: int, block_ta
         ws_ml = torch.empty(R * Hq * splits * 2, device=q.device, dtype=torch.float32)
     rc = _lib.load().qtts_paged_attention(q.data_ptr(), R, Hq, Hkv, D, kv_pool.data_ptr(), layer, L, bs, nb,
                                           block_table.data_ptr(), block_table.shape[-1], row_slot.data_ptr(),
-                                          row_ctx.data_ptr(), max_ctx, ws_o.data_ptr(), ws_ml.data_ptr(),
+                                          row_ctx.data_ptr(), max_ctx, split_blocks, ws_o.data_ptr(), ws_ml.data_ptr(),
                                           out.data_ptr(), _lib.ptr(out_lo), _lib.stream_ptr())
     _lib.check(rc, "paged_attention")
     return out

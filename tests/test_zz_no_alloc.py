@@ -38,7 +38,7 @@ def _with_caller_scratch(kv, table, q, ctx, rows, layer, max_ctx):
     out = torch.empty(R, HQ * d, device=DEV, dtype=torch.bfloat16)
     out_lo = torch.empty_like(out)
     rc = _lib.load().qtts_paged_attention(q.data_ptr(), R, HQ, HKV, d, kv.data_ptr(), layer, L, BS, NB,
-                                          table.data_ptr(), MBPS, rows.data_ptr(), ctx.data_ptr(), max_ctx,
+                                          table.data_ptr(), MBPS, rows.data_ptr(), ctx.data_ptr(), max_ctx, 0,
                                           ws_o.data_ptr(), ws_ml.data_ptr(), out.data_ptr(), out_lo.data_ptr(),
                                           _lib.stream_ptr())
     _lib.check(rc, "paged_attention")
