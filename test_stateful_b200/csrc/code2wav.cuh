@@ -15,9 +15,13 @@
 // [x(i-1) | x(i)] from a ctx = 1 buffer: the previous input frame replaces the
 // reference's bias-free overlap tail, which equals W[:, :, s:] x(i-1).
 //
-// Convolutions run as tcgen05 GEMMs (gemm_tc.cuh) over an im2col gather of
-// the history rows; the fused epilogue adds bias, scales/residual-adds,
-// applies the NEXT activation and scatters into the next history buffer.
+// Convolutions run as tcgen05 GEMMs (gemm_tc.cuh).  Where a stream's step has
+// a multiple of 128 rows (the residual convolutions of blocks 2-3 and block 3's
+// transposed conv), the GEMM reads its operand tiles by TMA straight from the
+// history buffer (implicit convolution: tap j is a row offset of j*dilation;
+// those buffers pad channels to a multiple of 64); the short ones go through an
+// im2col gather.  The fused epilogue adds bias, scales/residual-adds, applies
+// the NEXT activation and scatters into the next history buffer.
 // Decoder transformer: RMSNorm kernel + QKV GEMM whose epilogue does q/k norm,
 // RoPE at the stream's frame index and stores K/V into a per-slot ring of
 // `window` frames (the sliding-window cache, code2wav_streaming.py:29-66 with
@@ -346,6 +350,10 @@ struct qtts_c2w {
     int S;                     // max streams per step (= max slots)
     int T_up[2], T_in[4], T_blk[4], cin[4], cout[4];
     int K_pc, K_c0, K_tc[4], K_c1[4], N_c[4], N_tc[4];
+    // implicit convolution (the GEMM reads the history buffer directly, no im2col) where the
+    // rows per stream are a multiple of 128; those history buffers pad channels to 64
+    bool impl_tc[4], impl_c1[4];
+    int cinpad[4], cpad[4];
     int32_t *frame = nullptr, *row_slot = nullptr, *row_pos = nullptr, *row_kv = nullptr, *row_nkeys = nullptr;
     qtts::kv_t* ring = nullptr;
     __nv_bfloat16 *H_pc = nullptr, *Xa = nullptr, *Xb = nullptr;
@@ -444,9 +452,13 @@ inline int c2w_build(qtts_c2w* c) {
             set_error("c2w: decoder channels must stay multiples of 8");
             return QTTS_ERR_UNSUPPORTED;
         }
-        c->K_tc[b] = pad64(2 * c->cin[b]);
+        c->impl_tc[b] = c->T_in[b] % 128 == 0;
+        c->impl_c1[b] = c->T_blk[b] % 128 == 0;
+        c->cinpad[b] = c->impl_tc[b] ? pad64(c->cin[b]) : c->cin[b];
+        c->cpad[b] = c->impl_c1[b] ? pad64(c->cout[b]) : c->cout[b];
+        c->K_tc[b] = c->impl_tc[b] ? 2 * c->cinpad[b] : pad64(2 * c->cin[b]);
         c->N_tc[b] = pad128(d.rates[b] * c->cout[b]);
-        c->K_c1[b] = pad64(7 * c->cout[b]);
+        c->K_c1[b] = c->impl_c1[b] ? 7 * c->cpad[b] : pad64(7 * c->cout[b]);
         c->N_c[b] = pad128(c->cout[b]);
     }
     if (c->cout[3] > kFinalMaxC) {
@@ -466,8 +478,8 @@ inline int c2w_build(qtts_c2w* c) {
     size_t xa = (size_t)S * c->K_pc;
     xa = std::max(xa, (size_t)S * 4 * c->K_c0);
     for (int b = 0; b < 4; ++b) {
-        xa = std::max(xa, (size_t)S * c->T_in[b] * c->K_tc[b]);
-        xa = std::max(xa, (size_t)S * c->T_blk[b] * c->K_c1[b]);
+        if (!c->impl_tc[b]) xa = std::max(xa, (size_t)S * c->T_in[b] * c->K_tc[b]);
+        if (!c->impl_c1[b]) xa = std::max(xa, (size_t)S * c->T_blk[b] * c->K_c1[b]);
     }
     QTTS_TRY(c2w_alloc(c, &c->Xa, xa));
     QTTS_TRY(c2w_alloc(c, &c->Xb, (size_t)S * LAT));
@@ -487,10 +499,10 @@ inline int c2w_build(qtts_c2w* c) {
     QTTS_TRY(c2w_alloc(c, &c->H_c0, (size_t)S1 * (6 + 4) * LAT));
     for (int b = 0; b < 4; ++b) {
         const int Tb = c->T_blk[b], co = c->cout[b];
-        QTTS_TRY(c2w_alloc(c, &c->H_tc[b], (size_t)S1 * (1 + c->T_in[b]) * c->cin[b]));
+        QTTS_TRY(c2w_alloc(c, &c->H_tc[b], (size_t)S1 * (1 + c->T_in[b]) * c->cinpad[b]));
         QTTS_TRY(c2w_alloc(c, &c->h[b], (size_t)S * Tb * co));
         for (int j = 0; j < 3; ++j)
-            QTTS_TRY(c2w_alloc(c, &c->H_res[b][j], (size_t)S1 * (6 * d.dilations[j] + Tb) * co));
+            QTTS_TRY(c2w_alloc(c, &c->H_res[b][j], (size_t)S1 * (6 * d.dilations[j] + Tb) * c->cpad[b]));
         QTTS_TRY(c2w_alloc(c, &c->X2[b], (size_t)S * Tb * c->N_c[b]));
     }
     QTTS_TRY(c2w_alloc(c, &c->H_fin, (size_t)S1 * (6 + c->T_blk[3]) * c->cout[3]));
@@ -502,9 +514,9 @@ inline int c2w_build(qtts_c2w* c) {
     add_roll(c, c->H_dw[1], 6, c->T_up[1], LAT * 4);
     add_roll(c, c->H_c0, 6, 4, LAT * 2);
     for (int b = 0; b < 4; ++b)
-        for (int j = 0; j < 3; ++j) add_roll(c, c->H_res[b][j], 6 * d.dilations[j], c->T_blk[b], c->cout[b] * 2);
+        for (int j = 0; j < 3; ++j) add_roll(c, c->H_res[b][j], 6 * d.dilations[j], c->T_blk[b], c->cpad[b] * 2);
     add_roll(c, c->H_fin, 6, c->T_blk[3], c->cout[3] * 2);
-    for (int b = 0; b < 4; ++b) add_roll(c, c->H_tc[b], 1, c->T_in[b], c->cin[b] * 2);
+    for (int b = 0; b < 4; ++b) add_roll(c, c->H_tc[b], 1, c->T_in[b], c->cinpad[b] * 2);
     for (int i = 0; i < c->roll.n; ++i)
         if (c->roll.job[i].row_bytes % 16 != 0 || c->roll.job[i].row_bytes > kRollChunks * kRollChunk) {
             set_error("c2w: state rows must be multiples of 16 bytes, at most %d", kRollChunks * kRollChunk);
@@ -570,7 +582,7 @@ inline int c2w_build(qtts_c2w* c) {
         ConvEpi e = conv_epi(c, 4, 1, D0, D0);
         e.act = ACT_SNAKE;
         e.act_p = d.blk_snake[0];
-        e.out16 = view_slot(c->H_tc[0], 1, 4, D0);
+        e.out16 = view_slot(c->H_tc[0], 1, 4, c->cinpad[0]);
         QTTS_TRY(conv_plan(&c->conv0, c->Xa, S * 4, c->K_c0, d.w_conv0, pad128(D0), d.b_conv0, e));
     }
     for (int b = 0; b < 4; ++b) {
@@ -579,25 +591,36 @@ inline int c2w_build(qtts_c2w* c) {
         et.out32 = view_rows(c->h[b], Tb, co);
         et.act = ACT_SNAKE;
         et.act_p = d.res_act1[b][0];
-        et.out16 = view_slot(c->H_res[b][0], 6 * d.dilations[0], Tb, co);
-        QTTS_TRY(conv_plan(&c->blk_t[b], c->Xa, S * c->T_in[b], c->K_tc[b], d.blk_tw[b], c->N_tc[b], d.blk_tb[b], et));
+        et.out16 = view_slot(c->H_res[b][0], 6 * d.dilations[0], Tb, c->cpad[b]);
+        if (c->impl_tc[b])
+            QTTS_TRY(gemm_plan_implicit(&c->blk_t[b], c->H_tc[b], S1 * (1 + c->T_in[b]), c->cinpad[b], 2, 1,
+                                        c->T_in[b], 1 + c->T_in[b], S * c->T_in[b], d.blk_tw[b], c->N_tc[b],
+                                        d.blk_tb[b], et));
+        else
+            QTTS_TRY(conv_plan(&c->blk_t[b], c->Xa, S * c->T_in[b], c->K_tc[b], d.blk_tw[b], c->N_tc[b],
+                               d.blk_tb[b], et));
         for (int j = 0; j < 3; ++j) {
             ConvEpi e1 = conv_epi(c, Tb, 1, co, co);
             e1.act = ACT_SNAKE;
             e1.act_p = d.res_act2[b][j];
             e1.out16 = view_rows(c->X2[b], Tb, c->N_c[b]);
-            QTTS_TRY(conv_plan(&c->c1[b][j], c->Xa, S * Tb, c->K_c1[b], d.res_w1[b][j], c->N_c[b], d.res_b1[b][j],
-                               e1));
+            const int dil = d.dilations[j];
+            if (c->impl_c1[b])
+                QTTS_TRY(gemm_plan_implicit(&c->c1[b][j], c->H_res[b][j], S1 * (6 * dil + Tb), c->cpad[b], 7, dil,
+                                            Tb, 6 * dil + Tb, S * Tb, d.res_w1[b][j], c->N_c[b], d.res_b1[b][j], e1));
+            else
+                QTTS_TRY(conv_plan(&c->c1[b][j], c->Xa, S * Tb, c->K_c1[b], d.res_w1[b][j], c->N_c[b],
+                                   d.res_b1[b][j], e1));
             ConvEpi e2 = conv_epi(c, Tb, 1, co, co);
             e2.res = view_rows(c->h[b], Tb, co);
             e2.out32 = e2.res;
             e2.act = ACT_SNAKE;
             if (j < 2) {
                 e2.act_p = d.res_act1[b][j + 1];
-                e2.out16 = view_slot(c->H_res[b][j + 1], 6 * d.dilations[j + 1], Tb, co);
+                e2.out16 = view_slot(c->H_res[b][j + 1], 6 * d.dilations[j + 1], Tb, c->cpad[b]);
             } else if (b < 3) {
                 e2.act_p = d.blk_snake[b + 1];
-                e2.out16 = view_slot(c->H_tc[b + 1], 1, Tb, co);
+                e2.out16 = view_slot(c->H_tc[b + 1], 1, Tb, c->cinpad[b + 1]);
             } else {
                 e2.act_p = d.final_snake;
                 e2.out16 = view_slot(c->H_fin, 6, Tb, co);
@@ -619,6 +642,7 @@ inline int c2w_im2col(const qtts_c2w* c, const __nv_bfloat16* H, int ctx, int T,
 
 inline int run_conv(GemmPlan g, int M, const int32_t* slots, cudaStream_t st) {
     g.p.conv.row_slot = slots;
+    g.p.ix.row_slot = slots;  // implicit convolutions read the history rows of each row's slot
     return gemm_run(g, M, st);
 }
 
@@ -670,11 +694,13 @@ inline int c2w_step_impl(qtts_c2w* c, const int64_t* codes, int codes_ld, const 
     QTTS_TRY(run_conv(c->conv0, n * 4, slots, st));
     for (int b = 0; b < 4; ++b) {
         const int Tb = c->T_blk[b], co = c->cout[b];
-        QTTS_TRY(c2w_im2col(c, c->H_tc[b], 1, c->T_in[b], c->cin[b], 2, 1, c->K_tc[b], slots, n, st));
+        if (!c->impl_tc[b])
+            QTTS_TRY(c2w_im2col(c, c->H_tc[b], 1, c->T_in[b], c->cin[b], 2, 1, c->K_tc[b], slots, n, st));
         QTTS_TRY(run_conv(c->blk_t[b], n * c->T_in[b], slots, st));
         for (int j = 0; j < 3; ++j) {
             const int dil = d.dilations[j];
-            QTTS_TRY(c2w_im2col(c, c->H_res[b][j], 6 * dil, Tb, co, 7, dil, c->K_c1[b], slots, n, st));
+            if (!c->impl_c1[b])
+                QTTS_TRY(c2w_im2col(c, c->H_res[b][j], 6 * dil, Tb, co, 7, dil, c->K_c1[b], slots, n, st));
             QTTS_TRY(run_conv(c->c1[b][j], n * Tb, slots, st));
             QTTS_TRY(run_conv(c->c2[b][j], n * Tb, slots, st));
         }

@@ -70,6 +70,20 @@ struct ConvEpi {
 
 constexpr int kEpiConv = 16;  // internal epilogue id (not part of the C ABI)
 
+// Implicit convolution operand: instead of a dense [M][K] X, row tile (stream r,
+// steps t0..t0+BN) at k-block kb = (tap, channel block cb) is the box
+// H[slot(r)][t0 + tap*dil ..][cb*64 ..] of a slot-indexed history buffer whose
+// segments hold ctx = (taps-1)*dil context rows before the T current rows.
+// Needs T % BN == 0 (a row tile never spans two streams).
+struct ImplicitX {
+    int on;
+    int T;         // rows per stream
+    int seq_rows;  // rows per slot segment of the history buffer
+    int dil;       // tap stride in rows
+    int cblocks;   // 64-channel blocks per tap (channels padded to a multiple of 64)
+    const int32_t* row_slot;
+};
+
 struct GemmParams {
     int M, N, K;
     int kblocks;   // K / 64
@@ -80,6 +94,7 @@ struct GemmParams {
     const __nv_bfloat16* bias;
     qtts_qkv_epilogue qkv;
     ConvEpi conv;
+    ImplicitX ix;
 };
 
 template <int BN, int STAGES, bool SPLIT>
@@ -398,6 +413,11 @@ __global__ void __launch_bounds__(NT) gemm_tc_kernel(const __grid_constant__ CUt
     if (warp == 0 && lane == 0) {
         // ---------------- TMA producer ----------------
         int issued = 0;
+        int x_row0 = 0;  // implicit convolution: first history row of this row tile
+        if (p.ix.on) {
+            const int m0g = tile_m * BN, r = m0g / p.ix.T;
+            x_row0 = p.ix.row_slot[r] * p.ix.seq_rows + (m0g - r * p.ix.T);
+        }
         for (int i = 0; i < nkb; ++i) {
             const int s = i % STAGES;
             const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
@@ -411,8 +431,13 @@ __global__ void __launch_bounds__(NT) gemm_tc_kernel(const __grid_constant__ CUt
                 mbar_arrive_expect_tx(&full[s], L::STAGE_BYTES);
                 tma_load_2d(a, &tmW, &full[s], (kb0 + i) * 64, tile_n * 128);
             }
-            tma_load_2d(b, &tmX, &full[s], (kb0 + i) * 64, tile_m * BN);
-            if (SPLIT) tma_load_2d(b + L::B_BYTES, &tmXlo, &full[s], (kb0 + i) * 64, tile_m * BN);
+            if (p.ix.on) {
+                const int kb = kb0 + i, tap = kb / p.ix.cblocks, cb = kb - tap * p.ix.cblocks;
+                tma_load_2d(b, &tmX, &full[s], cb * 64, x_row0 + tap * p.ix.dil);
+            } else {
+                tma_load_2d(b, &tmX, &full[s], (kb0 + i) * 64, tile_m * BN);
+                if (SPLIT) tma_load_2d(b + L::B_BYTES, &tmXlo, &full[s], (kb0 + i) * 64, tile_m * BN);
+            }
             ++issued;
         }
         flags[1] = issued;
@@ -631,10 +656,49 @@ inline int gemm_plan(GemmPlan* g, const void* X, int rows, int K, const void* W,
     return QTTS_OK;
 }
 
+// Implicit-convolution plan: X is a slot-indexed history buffer H [(slots) * seq_rows][cpad]
+// (bf16, cpad % 64 == 0), K = taps * cpad, rows per stream T % 128 == 0.
+inline int gemm_plan_implicit(GemmPlan* g, const void* H, int total_rows, int cpad, int taps, int dil, int T,
+                              int seq_rows, int max_rows, const void* W, int N, const void* bias, const ConvEpi& e) {
+    if (cpad % 64 != 0 || T % 128 != 0 || N % 128 != 0) {
+        set_error("implicit conv: need channels %% 64 == 0, T %% 128 == 0, N %% 128 == 0");
+        return QTTS_ERR_UNSUPPORTED;
+    }
+    const int K = taps * cpad;
+    int rc = make_map_bf16(&g->mw, W, (uint64_t)N, (uint64_t)K, 128);
+    if (rc) return rc;
+    rc = make_map_bf16(&g->mx128, H, (uint64_t)total_rows, (uint64_t)cpad, 128);
+    if (rc) return rc;
+    g->mx64 = g->mx128;
+    g->mlo64 = g->mx128;
+    g->mlo128 = g->mx128;
+    g->split = false;
+    GemmParams& p = g->p;
+    memset(&p, 0, sizeof(p));
+    p.M = max_rows;
+    p.N = N;
+    p.K = K;
+    p.kblocks = K / 64;
+    p.splits = 1;
+    p.epilogue = kEpiConv;
+    p.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+    p.conv = e;
+    p.ix.on = 1;
+    p.ix.T = T;
+    p.ix.seq_rows = seq_rows;
+    p.ix.dil = dil;
+    p.ix.cblocks = cpad / 64;
+    return QTTS_OK;
+}
+
 // Launch on the first M rows of the plan's X buffer(s).
 inline int gemm_run(GemmPlan g, int M, cudaStream_t st, void* out = nullptr) {
     if (M <= 0) return QTTS_OK;
     const int bn = pick_bn(M);
+    if (g.p.ix.on && (bn != 128 || M % g.p.ix.T != 0)) {
+        set_error("implicit conv: rows must be whole streams of T >= 128 steps (M=%d T=%d)", M, g.p.ix.T);
+        return QTTS_ERR_INVALID;
+    }
     g.p.M = M;
     g.p.splits = pick_splits(g.p.N, M, g.p.K, bn);
     if (out) g.p.out = out;

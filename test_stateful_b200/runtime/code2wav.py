@@ -12,7 +12,10 @@ Packing (all one-time, at load):
   once, so a frame is a sum of 16 table rows (code2wav_streaming.py:681-706);
   the two projection biases are folded into tables 0 and 1.  fp32.
 * Conv ``[out][in][k]`` -> GEMM weight ``[out][k*in]`` (tap-major, matching
-  the im2col column order), zero-padded to N % 128 and K % 64.
+  the im2col column order), zero-padded to N % 128 and K % 64.  Where the
+  device reads the operand straight from a history buffer (implicit
+  convolution: rows per stream a multiple of 128), each tap's channels are
+  padded to 64 first, as the buffer's rows are.
 * Transposed conv ``[in][out][2s]`` (stride s) -> rows (phase p, out) over
   ``[x(i-1) | x(i)]``: ``W'[p*out+o] = [w[:, o, p+s] | w[:, o, p]]``; the
   upsampling transposed convs (kernel = stride = 2) -> ``W'[p*out+o] = w[:, o, p]``.
@@ -64,11 +67,22 @@ def pack_code2wav(cfg: Code2WavConfig, W: Dict[str, torch.Tensor], device) -> Di
         tabs.append(t)
     P["rvq_tables"] = fp(torch.stack(tabs))
 
-    def conv_w(name, n_pad=None, k_pad=None):
+    def conv_w(name, n_pad=None, k_pad=None, in_pad=None):
+        """[out, in, k] -> [out, k * in_pad] (tap-major, each tap's channels padded to in_pad)."""
         w = f32[name]  # [out, in, k]
         o, i, k = w.shape
-        m = w.permute(0, 2, 1).reshape(o, k * i)
-        return bf(_pad_to(m, n_pad or _p128(o), k_pad or _p64(k * i)))
+        ip = in_pad or i
+        m = torch.zeros(o, k, ip)
+        m[:, :, :i] = w.permute(0, 2, 1)
+        m = m.reshape(o, k * ip)
+        return bf(_pad_to(m, n_pad or _p128(o), k_pad or _p64(k * ip)))
+
+    # implicit-convolution blocks (rows per stream a multiple of 128) pad each tap's channels to 64
+    T, t_in, t_blk = 4, [], []
+    for r_ in cfg.upsample_rates:
+        t_in.append(T)
+        T *= r_
+        t_blk.append(T)
 
     def vec(name, n_pad=None):
         v = f32[name]
@@ -122,8 +136,15 @@ def pack_code2wav(cfg: Code2WavConfig, W: Dict[str, torch.Tensor], device) -> Di
         k = f"c2w.decoder.{1 + b}."
         P[f"blk_snake{b}"] = snake(k + "snake.alpha", k + "snake.beta")
         w = f32[k + "transconv.weight"]  # [cin, cout, 2s]
-        rows = [torch.cat([w[:, :, ph + s].t(), w[:, :, ph].t()], dim=1) for ph in range(s)]
-        P[f"blk_tw{b}"] = bf(_pad_to(torch.cat(rows), _p128(s * cout), _p64(2 * cin)))
+        cinp = _p64(cin) if t_in[b] % 128 == 0 else cin
+        rows = []
+        for ph in range(s):
+            r2 = torch.zeros(cout, 2, cinp)
+            r2[:, 0, :cin] = w[:, :, ph + s].t()  # tap x(i-1)
+            r2[:, 1, :cin] = w[:, :, ph].t()      # tap x(i)
+            rows.append(r2.reshape(cout, 2 * cinp))
+        P[f"blk_tw{b}"] = bf(_pad_to(torch.cat(rows), _p128(s * cout), _p64(2 * cinp)))
+        coutp = _p64(cout) if t_blk[b] % 128 == 0 else cout
         bias = torch.zeros(_p128(s * cout))
         bias[:s * cout] = f32[k + "transconv.bias"].repeat(s)
         P[f"blk_tb{b}"] = bf(bias)
@@ -131,7 +152,7 @@ def pack_code2wav(cfg: Code2WavConfig, W: Dict[str, torch.Tensor], device) -> Di
             r = f"{k}res.{j}."
             P[f"res_act1_{b}_{j}"] = snake(r + "act1.alpha", r + "act1.beta")
             P[f"res_act2_{b}_{j}"] = snake(r + "act2.alpha", r + "act2.beta")
-            P[f"res_w1_{b}_{j}"] = conv_w(r + "conv1.weight")
+            P[f"res_w1_{b}_{j}"] = conv_w(r + "conv1.weight", in_pad=coutp)
             P[f"res_b1_{b}_{j}"] = vec(r + "conv1.bias", _p128(cout))
             P[f"res_w2_{b}_{j}"] = conv_w(r + "conv2.weight", _p128(cout), _p128(cout))
             P[f"res_b2_{b}_{j}"] = vec(r + "conv2.bias", _p128(cout))
