@@ -656,6 +656,93 @@ inline int attn_engine_split() {
     return s;
 }
 
+// ---------------------------------------------------------------------------
+// Short rows (at most one 16-token block of keys, e.g. the code predictor's
+// per-frame cache): one warp per query head, keys read straight from the pool
+// (lane l scores key l), softmax with warp reductions, P·V with one broadcast
+// per key.  No staging ring: the whole row is 2-4 KB per head.
+// ---------------------------------------------------------------------------
+template <int D>
+__global__ void __launch_bounds__(128) short_attn_kernel(const AttnParams p) {
+    static_assert(D % 32 == 0 && D <= 128, "head_dim 32, 64 or 128");
+    constexpr int PER = D / 32;
+    __shared__ float qs[4][D];
+    const int r = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int h = blockIdx.y * 4 + warp;
+    griddep_wait();
+    griddep_launch();
+    if (h >= p.num_heads) return;
+    const int g = h / (p.num_heads / p.kv_heads);
+    const int n = min(p.row_ctx[r], 16);
+    const size_t orow = ((size_t)r * p.num_heads + h) * D;
+    if (n <= 0) {
+        for (int d = lane; d < D; d += 32) {
+            p.out[orow + d] = __float2bfloat16(0.f);
+            if (p.out_lo) p.out_lo[orow + d] = __float2bfloat16(0.f);
+        }
+        return;
+    }
+    int blk = p.block_table[(size_t)p.row_slot[r] * p.mbps];
+    if (blk < 0 || blk >= p.num_blocks) {
+        record_error(DEV_ERR_ATTN_WAIT);
+        blk = 0;
+    }
+    for (int d = lane; d < D; d += 32) qs[warp][d] = p.q[orow + d] * p.scale_log2;
+    __syncwarp();
+    const size_t head = (size_t)16 * D;
+    const kv_t* K = p.kv + ((((size_t)blk * p.num_layers + p.layer) * 2 + 0) * p.kv_heads + g) * head;
+    const kv_t* V = K + (size_t)p.kv_heads * head;
+    float sc = -INFINITY;
+    if (lane < n) {
+        const kv_t* kr = K + (size_t)lane * D;
+        float acc = 0.f;
+#pragma unroll
+        for (int d = 0; d < D; d += 8) {
+            const uint4 u = *reinterpret_cast<const uint4*>(kr + d);
+            const __half2* hp = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float2 f = __half22float2(hp[e]);
+                acc += f.x * qs[warp][d + 2 * e] + f.y * qs[warp][d + 2 * e + 1];
+            }
+        }
+        sc = acc;
+    }
+    const float mx = warp_max(sc);
+    const float pr = lane < n ? exp2f(sc - mx) : 0.f;
+    const float inv = 1.0f / warp_sum(pr);
+    float o[PER];
+#pragma unroll
+    for (int e = 0; e < PER; ++e) o[e] = 0.f;
+    for (int k = 0; k < n; ++k) {
+        const float pk = __shfl_sync(0xffffffffu, pr, k);
+        const kv_t* vr = V + (size_t)k * D + lane * PER;
+#pragma unroll
+        for (int e = 0; e < PER; ++e) o[e] += pk * __half2float(vr[e]);
+    }
+#pragma unroll
+    for (int e = 0; e < PER; ++e) {
+        const float v = o[e] * inv;
+        const __nv_bfloat16 hi = __float2bfloat16(v);
+        p.out[orow + lane * PER + e] = hi;
+        if (p.out_lo) p.out_lo[orow + lane * PER + e] = __float2bfloat16(v - __bfloat162float(hi));
+    }
+}
+
+// rows whose keys fit one 16-token block (p.mbps == 1)
+inline int launch_short_attention(const AttnParams& p, int head_dim, cudaStream_t st) {
+    if (p.R <= 0) return QTTS_OK;
+    const dim3 grid(p.R, ceil_div(p.num_heads, 4));
+    switch (head_dim) {
+        case 128: QTTS_LAUNCH(short_attn_kernel<128>, grid, dim3(128), 0, st, p); return QTTS_OK;
+        case 64: QTTS_LAUNCH(short_attn_kernel<64>, grid, dim3(128), 0, st, p); return QTTS_OK;
+        case 32: QTTS_LAUNCH(short_attn_kernel<32>, grid, dim3(128), 0, st, p); return QTTS_OK;
+        default:
+            set_error("short attention: head_dim %d not supported (32, 64 or 128)", head_dim);
+            return QTTS_ERR_UNSUPPORTED;
+    }
+}
+
 inline int attn_max_splits(int max_ctx, int split_blocks = QTTS_ATTN_SPLIT_BLOCKS) {
     const int nb = (max_ctx + 15) / 16;
     const int s = (nb + split_blocks - 1) / split_blocks;

@@ -397,7 +397,7 @@ inline int engine_step_impl(qtts_engine* e, const qtts_step_io& io, cudaStream_t
             q.p.qkv.slot_mapping = m;
             QTTS_TRY(run_plan(q, rows, st));
             cap.layer = l;
-            QTTS_TRY(launch_attention(cap, cD, st));
+            QTTS_TRY(launch_short_attention(cap, cD, st));  // <= 16 keys per row
             QTTS_TRY(run_plan(g.o, rows, st));
             QTTS_TRY(launch_rmsnorm(e->cx, rows, cH, cH, bf(d.cp_w_post_norm, (size_t)l * cH), d.cp_rms_eps, e->cxn,
                                     st, e->cxn_lo));

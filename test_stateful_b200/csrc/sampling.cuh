@@ -112,8 +112,16 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
         __syncthreads();
 #pragma unroll
         for (int i = 0; i < kSampleMaxPer; ++i) {
+            // warp-aggregated: logits of similar size share the high key bits, so lanes
+            // hitting the same bin add once through their lowest lane
             const int idx = tid + i * kSampleThreads;
-            if (idx < p.V && (key[i] & mask) == prefix) atomicAdd(&hist[(key[i] >> shift) & 255u], 1u);
+            const bool act = idx < p.V && (key[i] & mask) == prefix;
+            const uint32_t am = __ballot_sync(0xffffffffu, act);
+            if (act) {
+                const uint32_t bin = (key[i] >> shift) & 255u;
+                const uint32_t peers = __match_any_sync(am, bin);
+                if ((int)(threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&hist[bin], (uint32_t)__popc(peers));
+            }
         }
         __syncthreads();
         if (tid < 32) {

@@ -5,6 +5,10 @@ Run once, in a checkout that has the reference tree next to it:
 
     python tests/golden/make_golden.py --reference <path to the reference checkout>
 
+and, for the oracle-extended 512-step greedy horizon (no reference needed):
+
+    python tests/golden/make_golden.py --only cfg1_long
+
 It imports, from the reference tree:
 
 * ``scripts/export/talker_unified_modules.py``: ``TalkerUnifiedONNX``,
@@ -615,6 +619,33 @@ def make_code2wav(ref: Path, out, seed=5, steps=78, starts=(0, 9)):
                         seed=np.int64(seed), starts=np.asarray(starts, np.int32))
 
 
+def make_cfg1_long(out, steps=512):
+    """BASELINE configs[0] streams (seed 0, prompts {37, 64, 91, 128}, greedy) for ``steps``
+    decode steps, run by the ORACLE (oracle/engine.py): the reference's own modules pin the
+    oracle over the first 32 steps (cfg1_full_greedy.npz); this fixture extends the horizon to
+    the 512-step agreement bar.  Stores the greedy codes and every 64th step's logits (fp16)."""
+    from oracle.engine import run_trajectory as oracle_trajectory
+    cfg = EngineConfig()
+    seed, lengths = 0, [37, 64, 91, 128]
+    t, c = cfg.talker, cfg.cp
+    W = fp32_weights(cfg, seed)
+    table = workload.text_table(t.hidden_size, seed)
+    pad = workload.tts_pad_embed(t.hidden_size, seed)
+    ids = workload.prompt_ids(lengths, seed)
+    B = len(lengths)
+    g = np.zeros((steps + 1, B, 50), np.float32)
+    cg = np.zeros((steps + 1, B, c.num_stages, 50), np.float32)
+    t0 = time.time()
+    codes, step_logits = oracle_trajectory(W, t, c, [table[i] for i in ids], steps, pad, g, cg, 1.0, 1.05)
+    every = 64
+    keep = np.arange(0, steps + 1, every)
+    np.savez_compressed(out, codes=codes.astype(np.int16), logit_steps=keep.astype(np.int32),
+                        step_logits=step_logits[keep].astype(np.float16), lengths=np.asarray(lengths, np.int64),
+                        seed=np.int64(seed), steps=np.int64(steps), do_sample=np.int64(0),
+                        temperature=np.float32(1.0), penalty=np.float32(1.05))
+    print(f"cfg1_long: {steps} steps in {time.time() - t0:.0f}s", flush=True)
+
+
 def make_seeds(out):
     """Per-(session, segment) sampling seeds from engine/backend/executor.py:45-52."""
     from engine.backend import executor as ref_executor
@@ -632,11 +663,16 @@ def make_seeds(out):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", required=True, type=Path)
+    ap.add_argument("--reference", type=Path, default=None)
     ap.add_argument("--skip-full", action="store_true")
     ap.add_argument("--only", default=None)
     args = ap.parse_args()
     torch.set_num_threads(max(1, torch.get_num_threads()))
+    if args.only == "cfg1_long":  # oracle-only
+        make_cfg1_long(HERE / "cfg1_long_greedy.npz")
+        return
+    if args.reference is None:
+        ap.error("--reference is required")
     ref_mods = import_reference(args.reference.resolve())
     if args.only == "seeds":
         make_seeds(HERE / "seeds.npz")

@@ -139,8 +139,16 @@ def _replay_reference(name, cfg, check_tokens):
     sampled = bool(int(z["do_sample"]))
     r = Runner(cfg, W, max_batch=B, temperature=float(z["temperature"]), penalty=float(z["penalty"]))
     r.text[:B] = pad.to(DEV)
-    codes_ref = torch.from_numpy(z["codes"])
+    codes_ref = torch.from_numpy(z["codes"].astype(np.int64))
     talk, cp = Tally(), Tally()
+    # logits compared at every step, or at the steps a long-horizon fixture keeps
+    logit_row = {int(s_): j for j, s_ in enumerate(z["logit_steps"])} if "logit_steps" in z.files else None
+
+    def ref_logits(step, i):
+        if logit_row is None:
+            return torch.from_numpy(z["step_logits"][step, i])
+        j = logit_row.get(step)
+        return None if j is None else torch.from_numpy(z["step_logits"][j, i].astype(np.float32))
 
     def noise(step, rows):
         if not sampled:
@@ -151,7 +159,8 @@ def _replay_reference(name, cfg, check_tokens):
     for i in range(B):
         g, cg = noise(0, [i])
         out = r.prefill(i, text[ids[i]], g, cg, force=codes_ref[i:i + 1, 0])
-        talk.logits(out["logits"][0], torch.from_numpy(z["step_logits"][0, i]))
+        if ref_logits(0, i) is not None:
+            talk.logits(out["logits"][0], ref_logits(0, i))
         if check_tokens:
             talk.tokens(out["codes"][0, :1], codes_ref[i, 0, :1])
             cp.tokens(out["codes"][0, 1:], codes_ref[i, 0, 1:])
@@ -161,14 +170,13 @@ def _replay_reference(name, cfg, check_tokens):
         r.next_x[:B] = nx.to(DEV)
         # repetition-penalty state = the reference's tok0 history (frames 0 .. step-1)
         hist = torch.zeros(B, t.codec_vocab_size, dtype=torch.int64)
-        for i in range(B):
-            for s2 in range(step):
-                hist[i, int(codes_ref[i, s2, 0])] += 1
+        hist.scatter_add_(1, codes_ref[:, :step, 0], torch.ones(B, step, dtype=torch.int64))
         r.counts[:B] = hist.to(DEV)
         g, cg = noise(step, list(range(B)))
         out = r.decode(list(range(B)), g, cg, force=codes_ref[:, step])
         for i in range(B):
-            talk.logits(out["logits"][i], torch.from_numpy(z["step_logits"][step, i]))
+            if ref_logits(step, i) is not None:
+                talk.logits(out["logits"][i], ref_logits(step, i))
         if check_tokens:
             talk.tokens(out["codes"][:, :1], codes_ref[:, step, :1])
             cp.tokens(out["codes"][:, 1:], codes_ref[:, step, 1:])
@@ -187,6 +195,22 @@ def test_reference_greedy_trajectory_tiny():
 def test_reference_sampled_trajectory_tiny_logits():
     talk, _ = _replay_reference("traj_tiny_sampled.npz", tiny_engine_config(num_layers=2), check_tokens=False)
     assert talk.worst <= LOGIT_TOL
+
+
+def test_cfg1_full_model_512_step_greedy_agreement():
+    """The agreement bar over its full 512-step horizon: cfg1's streams decoded for 512
+    greedy steps by the oracle (itself pinned to the reference over the first 32 steps),
+    replayed teacher-forced on the device."""
+    path = os.path.join(GOLDEN, "cfg1_long_greedy.npz")
+    if not os.path.exists(path):
+        pytest.skip("cfg1 long-horizon fixture not generated")
+    cfg = EngineConfig()
+    cfg.pool = PagedPoolConfig(block_size=16, num_blocks=256, max_slots=4, max_seq_len=768)
+    talk, cp = _replay_reference("cfg1_long_greedy.npz", cfg, check_tokens=True)
+    print(f"cfg1 512 steps: talker logit rel err {talk.worst:.4f}, tok0 agreement {talk.rate:.4f} "
+          f"({talk.agree}/{talk.total}), cp agreement {cp.rate:.4f} ({cp.agree}/{cp.total})")
+    assert talk.worst <= LOGIT_TOL
+    assert (talk.agree + cp.agree) / (talk.total + cp.total) >= GREEDY_AGREEMENT
 
 
 def test_cfg1_full_model_greedy_against_reference():
