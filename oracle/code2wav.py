@@ -77,7 +77,8 @@ class Code2WavState:
 
 
 def decode_chunk(W: Dict[str, Tensor], cfg, codes: Tensor, st: Code2WavState) -> Tensor:
-    """One stream, ``codes [16, T]`` -> wav ``[T * 1920]``; updates ``st``.
+    """One stream, ``codes [16, T]`` -> wav ``[T * 1920]``; updates ``st``.  A chunk of T
+    frames sees at most window - T past frames plus the chunk's own frames causally.
 
     code2wav_streaming.py:708-810 with the quantizer table path (681-706), the
     transformer layer (367-391) and attention (323-364)."""
@@ -96,6 +97,10 @@ def decode_chunk(W: Dict[str, Tensor], cfg, codes: Tensor, st: Code2WavState) ->
     pos = torch.arange(st.frame, st.frame + T).unsqueeze(0)
     cos, sin = rope_cos_sin(pos, cfg.head_dim, cfg.rope_theta)
     cos, sin = cos.unsqueeze(1), sin.unsqueeze(1)
+    # past + chunk keys must fit the window: the caller keeps at most window - T past frames
+    # (executor.py:1374-1380 with FUSED_CHUNK_T = T)
+    st.kv = [(k[:, :, -(cfg.window - T):] if T < cfg.window else k[:, :, :0],
+              v[:, :, -(cfg.window - T):] if T < cfg.window else v[:, :, :0]) for k, v in st.kv]
     P = st.kv[0][0].shape[2]
     cols = torch.arange(P + T)
     rows = torch.arange(T).unsqueeze(1) + P
@@ -122,7 +127,7 @@ def decode_chunk(W: Dict[str, Tensor], cfg, codes: Tensor, st: Code2WavState) ->
         m = F.linear(F.silu(F.linear(n, W[q_ + "mlp.gate_proj.weight"].float()))
                      * F.linear(n, W[q_ + "mlp.up_proj.weight"].float()), W[q_ + "mlp.down_proj.weight"].float())
         x = x + W[q_ + "mlp_layer_scale.scale"].float() * m
-        keep = cfg.window - 1  # the executor keeps window - chunk past frames (T = 1)
+        keep = cfg.window - 1  # at most window - 1 past frames are ever visible (T >= 1)
         st.kv[i] = (fk[:, :, -keep:], fv[:, :, -keep:])
     x = rms_norm(x, W[p + "norm.weight"], cfg.rms_eps)
     h = F.linear(x, W[p + "output_proj.weight"].float(), W[p + "output_proj.bias"].float()).transpose(1, 2)

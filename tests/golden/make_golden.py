@@ -646,6 +646,65 @@ def make_cfg1_long(out, steps=512):
     print(f"cfg1_long: {steps} steps in {time.time() - t0:.0f}s", flush=True)
 
 
+def make_code2wav_chunked(ref: Path, out, seed=6, chunks=(25, 25, 25, 7), start1=1):
+    """Multi-frame chunks through the reference wrapper (BASELINE cfg4): per call T frames per
+    slot, past KV capped at window - T frames (the executor's max_past = window - chunk_T,
+    executor.py:1374-1380), bias = -inf on each slot's left padding plus the causal mask inside
+    the chunk, delta KV appended.  Slot 1 joins at call ``start1`` (ragged pasts)."""
+    sys.path.insert(0, str(ref / "scripts" / "export"))
+    import code2wav_streaming as c2ws
+    from test_stateful_b200.config import tiny_code2wav_config
+    c = tiny_code2wav_config()
+    W = wmod.to_fp32(wmod.make_code2wav_weights(c, seed))
+    dec = build_code2wav_standin(c, W)
+    wrap = c2ws.Code2WavStreamingWrapper(dec, window_size=c.window, emit_delta_kv=True).eval()
+    shapes = c2ws.get_initial_state_shapes(dec, batch_size=1)
+    conv_shapes = [s for n, s in shapes if n.startswith("conv_state")]
+    trans_shapes = [s for n, s in shapes if n.startswith("transconv")]
+    L2 = 2 * c.num_layers
+    g = torch.Generator().manual_seed(seed)
+    total = sum(chunks)
+    codes = torch.randint(0, c.codebook_size, (2, c.num_codebooks, total), generator=g)
+    kv = [None, None]
+    conv = [[torch.zeros(s) for s in conv_shapes] for _ in range(2)]
+    trans = [[torch.zeros(s) for s in trans_shapes] for _ in range(2)]
+    frame = [0, 0]
+    wav = [[], []]
+    with torch.no_grad():
+        for call, T in enumerate(chunks):
+            act = [0] + ([1] if call >= start1 else [])
+            max_past = c.window - T
+            lens = [0 if kv[i] is None else min(kv[i].shape[3], max_past) for i in act]
+            P = max(1, max(lens))
+            bias = torch.zeros(len(act), 1, T, P + T)
+            bias[:, :, :, P:] = torch.triu(torch.full((T, T), float("-inf")), diagonal=1)
+            past = []
+            for bi, (i, sl) in enumerate(zip(act, lens)):
+                bias[bi, :, :, :P - sl] = float("-inf")
+                k = kv[i] if kv[i] is not None else torch.zeros(1, L2, c.kv_heads, 0, c.head_dim)
+                past.append(nn.functional.pad(k[:, :, :, k.shape[3] - sl:], (0, 0, P - sl, 0)))
+            past = torch.cat(past, 0)
+            states = [past[:, j] for j in range(L2)]
+            states += [torch.cat([conv[i][j] for i in act], 0) for j in range(len(conv_shapes))]
+            states += [torch.cat([trans[i][j] for i in act], 0) for j in range(len(trans_shapes))]
+            cpos = torch.stack([torch.arange(frame[i], frame[i] + T, dtype=torch.float32) for i in act])
+            cds = torch.stack([codes[i, :, frame[i]:frame[i] + T] for i in act])
+            outs = wrap(cds, cpos, bias, *states)
+            delta = torch.stack(outs[1:1 + L2], dim=1)
+            nc = outs[1 + L2:1 + L2 + len(conv_shapes)]
+            nt = outs[1 + L2 + len(conv_shapes):]
+            for bi, i in enumerate(act):
+                wav[i].append(outs[0][bi].numpy())
+                d = delta[bi:bi + 1]
+                kv[i] = d if kv[i] is None else torch.cat([kv[i], d], 3)[:, :, :, -(c.window - 1):]
+                conv[i] = [x[bi:bi + 1].clone() for x in nc]
+                trans[i] = [x[bi:bi + 1].clone() for x in nt]
+                frame[i] += T
+    np.savez_compressed(out, codes=codes.numpy().astype(np.int32), chunks=np.asarray(chunks, np.int32),
+                        start1=np.int32(start1), seed=np.int64(seed),
+                        wav0=np.concatenate(wav[0]).astype(np.float16), wav1=np.concatenate(wav[1]).astype(np.float16))
+
+
 def make_seeds(out):
     """Per-(session, segment) sampling seeds from engine/backend/executor.py:45-52."""
     from engine.backend import executor as ref_executor
@@ -679,8 +738,10 @@ def main():
         return
     if args.only == "code2wav":
         make_code2wav(args.reference.resolve(), HERE / "code2wav_tiny.npz")
+        make_code2wav_chunked(args.reference.resolve(), HERE / "code2wav_chunked_tiny.npz")
         return
     make_code2wav(args.reference.resolve(), HERE / "code2wav_tiny.npz")
+    make_code2wav_chunked(args.reference.resolve(), HERE / "code2wav_chunked_tiny.npz")
     make_seeds(HERE / "seeds.npz")
     t0 = time.time()
     make_fused_tiny(ref_mods, HERE / "fused_tiny.npz")

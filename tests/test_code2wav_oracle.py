@@ -65,3 +65,24 @@ def test_code2wav_state_shapes_match_reference_layout():
     assert conv[16] == (96, 6)
     assert [tuple(t.shape[1:]) for t in st.trans] == [(768, 8), (384, 5), (192, 4), (96, 3)]
     assert cfg.samples_per_frame == 1920
+
+
+def test_code2wav_oracle_matches_reference_chunked_stream():
+    """BASELINE cfg4 semantics: chunks of T frames (here 25, 25, 25, 7) with carried state;
+    each chunk sees at most window - T past frames plus its own frames causally.  Fixture
+    from the reference wrapper, two slots with ragged pasts (wav stored as fp16)."""
+    z = np.load(os.path.join(GOLDEN, "code2wav_chunked_tiny.npz"))
+    cfg = tiny_code2wav_config()
+    W = wmod.to_fp32(wmod.make_code2wav_weights(cfg, int(z["seed"])))
+    codes, chunks, start1 = z["codes"], z["chunks"].tolist(), int(z["start1"])
+    for s_, ref in ((0, z["wav0"]), (1, z["wav1"])):
+        st = C.Code2WavState(cfg)
+        f, out = 0, []
+        for call, T in enumerate(chunks):
+            if s_ == 1 and call < start1:
+                continue
+            out.append(C.decode_chunk(W, cfg, torch.from_numpy(codes[s_, :, f:f + T]).long(), st).numpy())
+            f += T
+        got = np.concatenate(out)
+        assert got.shape == ref.shape
+        np.testing.assert_allclose(got, ref.astype(np.float32), rtol=0, atol=1.5e-3)
