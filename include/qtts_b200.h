@@ -328,6 +328,7 @@ int qtts_engine_step(qtts_engine* e, qtts_step_io* io, qtts_stream_t stream);
 typedef struct qtts_c2w_desc {
     int32_t num_codebooks, codebook_size, codebook_dim, latent, hidden, layers, heads, head_dim, inter;
     int32_t window, decoder_dim, convnext_dim, max_slots, max_frames;
+    int32_t max_chunk;            /* frames per stream per qtts_c2w_step call, at most (0 = 1) */
     int32_t up_ratio[2];
     int32_t rates[4];
     int32_t dilations[3];
@@ -388,10 +389,14 @@ int qtts_c2w_create(const qtts_c2w_desc* desc, qtts_c2w** out);
 int qtts_c2w_destroy(qtts_c2w* c);
 /* Zero the streaming state of n slots (device int32 [n]): a new stream starts at frame 0. */
 int qtts_c2w_reset(qtts_c2w* c, const int32_t* slots, int n, qtts_stream_t stream);
-/* One frame for each of n rows: codes int64 (device) [n][codes_ld] (first num_codebooks used),
- * slots int32 (device) [n] (distinct), wav fp32 (device) [n][samples_per_frame]. */
-int qtts_c2w_step(qtts_c2w* c, const int64_t* codes, int codes_ld, const int32_t* slots, int n, float* wav,
-                  qtts_stream_t stream);
+/* `frames` consecutive frames (1 <= frames <= max_chunk) for each of n streams:
+ * codes int64 (device) [n][frames][codes_ld] (first num_codebooks used), slots int32 (device) [n]
+ * (distinct), wav fp32 (device) [n][frames * samples_per_frame].  A chunk of F frames sees at
+ * most window - F past frames plus its own frames causally (the reference caller's crop of the
+ * window cache to window - chunk, engine/backend/executor.py:1374-1380); frames = 1 is the
+ * fused step's streaming decode (export_09_talker_code2wav_fused.py:145-160). */
+int qtts_c2w_step(qtts_c2w* c, const int64_t* codes, int codes_ld, int frames, const int32_t* slots, int n,
+                  float* wav, qtts_stream_t stream);
 /* Kernels the last qtts_c2w_step enqueued (host counter). */
 int qtts_c2w_launches(const qtts_c2w* c);
 

@@ -79,6 +79,7 @@ class C2wDesc(C.Structure):
         ("num_codebooks", I32), ("codebook_size", I32), ("codebook_dim", I32), ("latent", I32), ("hidden", I32),
         ("layers", I32), ("heads", I32), ("head_dim", I32), ("inter", I32),
         ("window", I32), ("decoder_dim", I32), ("convnext_dim", I32), ("max_slots", I32), ("max_frames", I32),
+        ("max_chunk", I32),
         ("up_ratio", I32 * 2), ("rates", I32 * 4), ("dilations", I32 * 3), ("rms_eps", F32), ("ln_eps", F32),
         ("rvq_tables", P), ("w_pre_conv", P), ("b_pre_conv", P), ("w_in_proj", P), ("b_in_proj", P),
         ("w_in_norm", P), ("w_qkv", P), ("w_q_norm", P), ("w_k_norm", P), ("w_o", P), ("attn_scale", P),
@@ -146,7 +147,7 @@ def load() -> C.CDLL:
         "qtts_c2w_create": ([C.POINTER(C2wDesc), C.POINTER(P)], C.c_int),
         "qtts_c2w_destroy": ([P], C.c_int),
         "qtts_c2w_reset": ([P, P, C.c_int, P], C.c_int),
-        "qtts_c2w_step": ([P, P, C.c_int, P, C.c_int, P, P], C.c_int),
+        "qtts_c2w_step": ([P, P, C.c_int, C.c_int, P, C.c_int, P, P], C.c_int),
         "qtts_c2w_launches": ([P], C.c_int),
     }
     for name, (args, res) in sig.items():

@@ -46,14 +46,15 @@ inline int pad128(int x) { return (x + 127) / 128 * 128; }
 // with the output projections folded into the tables by the host.  Writes the
 // pre_conv input row, and the per-row frame bookkeeping of this step.
 // ---------------------------------------------------------------------------
+// One CTA per (stream s, frame t of the chunk): row rr = s * F + t.
 __global__ void __launch_bounds__(256) c2w_rvq_kernel(const float* __restrict__ tables, int G, int V, int CD,
-                                                      const int64_t* __restrict__ codes, int codes_ld,
+                                                      const int64_t* __restrict__ codes, int codes_ld, int F,
                                                       const int32_t* __restrict__ slots, int max_slots,
-                                                      int32_t* __restrict__ frame, int window, int max_frames,
+                                                      const int32_t* __restrict__ frame, int window, int max_frames,
                                                       int32_t* __restrict__ row_slot, int32_t* __restrict__ row_pos,
                                                       int32_t* __restrict__ row_kv, int32_t* __restrict__ row_nkeys,
-                                                      ActView dst) {
-    const int r = blockIdx.x;
+                                                      int32_t* __restrict__ row_lo, ActView dst) {
+    const int rr = blockIdx.x, r = rr / F, t = rr - r * F;
     griddep_wait();
     griddep_launch();
     // every later kernel of the step indexes state through row_slot: a slot
@@ -65,7 +66,7 @@ __global__ void __launch_bounds__(256) c2w_rvq_kernel(const float* __restrict__ 
     }
     __shared__ int idx[32];
     if (threadIdx.x < G) {
-        long long c = codes[(size_t)r * codes_ld + threadIdx.x];
+        long long c = codes[(size_t)rr * codes_ld + threadIdx.x];
         c = c < 0 ? 0 : (c >= V ? V - 1 : c);  // export_09_talker_code2wav_fused.py:146
         idx[threadIdx.x] = (int)c;
     }
@@ -73,15 +74,19 @@ __global__ void __launch_bounds__(256) c2w_rvq_kernel(const float* __restrict__ 
     for (int c = threadIdx.x; c < CD; c += blockDim.x) {
         float acc = 0.f;
         for (int g = 0; g < G; ++g) acc += tables[((size_t)g * V + idx[g]) * CD + c];
-        reinterpret_cast<__nv_bfloat16*>(dst.ptr)[view_index(dst, r, slot, 0, c)] = __float2bfloat16(acc);
+        reinterpret_cast<__nv_bfloat16*>(dst.ptr)[view_index(dst, r, slot, t, c)] = __float2bfloat16(acc);
     }
     if (threadIdx.x == 0) {
-        const int f = frame[slot];
-        row_slot[r] = slot;
-        row_pos[r] = f < max_frames ? f : max_frames - 1;
-        row_kv[r] = slot * window + f % window;
-        row_nkeys[r] = f + 1 < window ? f + 1 : window;
-        frame[slot] = f + 1;
+        // frame t of the chunk sees min(f0, window - F) past frames and the chunk's frames up to t
+        // (the executor's max_past = window - chunk, executor.py:1374-1380); the ring holds frame
+        // f at position f % window, and the chunk's writes never land on a frame it still reads
+        const int f0 = frame[slot], f = f0 + t;
+        const int nk = min(f0, window - F) + t + 1;
+        if (t == 0) row_slot[r] = slot;
+        row_pos[rr] = f < max_frames ? f : max_frames - 1;
+        row_kv[rr] = slot * window + f % window;
+        row_nkeys[rr] = nk;
+        row_lo[rr] = (f + 1 - nk) % window;
     }
 }
 
@@ -114,9 +119,10 @@ __global__ void __launch_bounds__(256) c2w_im2col_kernel(const __nv_bfloat16* __
 // ---------------------------------------------------------------------------
 template <int D>
 __global__ void __launch_bounds__(128) c2w_attn_kernel(const float* __restrict__ q, const kv_t* __restrict__ ring,
-                                                       int heads, int layers, int layer, int window,
+                                                       int heads, int layers, int layer, int window, int F,
                                                        const int32_t* __restrict__ slots,
-                                                       const int32_t* __restrict__ nkeys, float scale,
+                                                       const int32_t* __restrict__ nkeys,
+                                                       const int32_t* __restrict__ lo, float scale,
                                                        __nv_bfloat16* __restrict__ out,
                                                        __nv_bfloat16* __restrict__ out_lo) {
     static_assert(D == 32 || D == 64, "head_dim 32 or 64");
@@ -127,8 +133,8 @@ __global__ void __launch_bounds__(128) c2w_attn_kernel(const float* __restrict__
     griddep_wait();
     griddep_launch();
     if (h >= heads) return;
-    const int slot = slots[r];
-    const int n = nkeys[r];
+    const int slot = slots[r / F];  // row r = (stream, frame of the chunk)
+    const int n = nkeys[r], k0 = lo[r];
     for (int d = lane; d < D; d += 32) qs[warp][d] = q[((size_t)r * heads + h) * D + d];
     __syncwarp();
     const size_t kbase = ((((size_t)slot * layers + layer) * 2 + 0) * heads + h) * window * D;
@@ -140,7 +146,7 @@ __global__ void __launch_bounds__(128) c2w_attn_kernel(const float* __restrict__
         const int k = c * 32 + lane;
         s[c] = -INFINITY;
         if (k < n) {
-            const kv_t* kr = ring + kbase + (size_t)k * D;
+            const kv_t* kr = ring + kbase + (size_t)((k0 + k) % window) * D;
             float acc = 0.f;
 #pragma unroll
             for (int d = 0; d < D; d += 8) {
@@ -173,7 +179,7 @@ __global__ void __launch_bounds__(128) c2w_attn_kernel(const float* __restrict__
             const int k = c * 32 + j;
             if (k >= n) break;  // uniform across the warp
             const float pk = __shfl_sync(0xffffffffu, s[c], j);
-            const kv_t* vr = ring + vbase + (size_t)k * D;
+            const kv_t* vr = ring + vbase + (size_t)((k0 + k) % window) * D;
 #pragma unroll
             for (int e = 0; e < PER; ++e) o[e] += pk * __half2float(vr[lane * PER + e]);
         }
@@ -285,7 +291,7 @@ __global__ void __launch_bounds__(kFinalChunk) c2w_final_conv_kernel(const __nv_
 // ---------------------------------------------------------------------------
 struct RollJob {
     uint8_t* ptr;
-    int seq_rows, ctx, T, row_bytes;
+    int seq_rows, ctx, T, row_bytes;  // T: rows per frame (a call of F frames uses F * T)
 };
 constexpr int kMaxRollJobs = 24;
 constexpr int kRollChunk = 512;  // bytes of a row per CTA
@@ -297,22 +303,26 @@ struct RollTable {
     int n;
 };
 
-// rows [T, T + ctx) -> [0, ctx) of each active slot; the CTA stages its column
-// chunk of all ctx rows before writing, so T < ctx (overlapping ranges) is safe.
+// rows [T, T + ctx) -> [0, ctx) of each active slot (T = F * rows per frame); the
+// CTA stages its column chunk of all ctx rows before writing, so T < ctx
+// (overlapping ranges) is safe.  Also advances each slot's frame counter by F.
 __global__ void __launch_bounds__(128) c2w_roll_kernel(const __grid_constant__ RollTable tab,
-                                                       const int32_t* __restrict__ slots) {
+                                                       const int32_t* __restrict__ slots, int F,
+                                                       int32_t* __restrict__ frame) {
     __shared__ uint4 buf[kRollMaxCtx * (kRollChunk / 16)];
     griddep_wait();
     griddep_launch();
+    if (blockIdx.y == 0 && blockIdx.z == 0 && threadIdx.x == 0) frame[slots[blockIdx.x]] += F;
     if ((int)blockIdx.y >= tab.n) return;
     const RollJob& j = tab.job[blockIdx.y];
+    const int T = j.T * F;
     const int off = blockIdx.z * kRollChunk;
     if (off >= j.row_bytes || j.ctx <= 0 || j.ctx > kRollMaxCtx) return;
     const int vec = min(kRollChunk, j.row_bytes - off) / 16;
     uint8_t* seg = j.ptr + (size_t)slots[blockIdx.x] * j.seq_rows * j.row_bytes + off;
     for (int i = threadIdx.x; i < j.ctx * vec; i += blockDim.x) {
         const int q = i / vec, e = i - q * vec;
-        buf[q * (kRollChunk / 16) + e] = *reinterpret_cast<const uint4*>(seg + (size_t)(j.T + q) * j.row_bytes + e * 16);
+        buf[q * (kRollChunk / 16) + e] = *reinterpret_cast<const uint4*>(seg + (size_t)(T + q) * j.row_bytes + e * 16);
     }
     __syncthreads();
     for (int i = threadIdx.x; i < j.ctx * vec; i += blockDim.x) {
@@ -348,13 +358,15 @@ __global__ void __launch_bounds__(128) c2w_reset_kernel(const __grid_constant__ 
 struct qtts_c2w {
     qtts_c2w_desc d;
     int S;                     // max streams per step (= max slots)
-    int T_up[2], T_in[4], T_blk[4], cin[4], cout[4];
+    int Fm;                    // max frames per stream per call (chunk)
+    int T_up[2], T_in[4], T_blk[4], cin[4], cout[4];  // rows per stream per FRAME
     int K_pc, K_c0, K_tc[4], K_c1[4], N_c[4], N_tc[4];
     // implicit convolution (the GEMM reads the history buffer directly, no im2col) where the
     // rows per stream are a multiple of 128; those history buffers pad channels to 64
     bool impl_tc[4], impl_c1[4];
     int cinpad[4], cpad[4];
-    int32_t *frame = nullptr, *row_slot = nullptr, *row_pos = nullptr, *row_kv = nullptr, *row_nkeys = nullptr;
+    int32_t *frame = nullptr, *row_slot = nullptr, *row_pos = nullptr, *row_kv = nullptr, *row_nkeys = nullptr,
+            *row_lo = nullptr;
     qtts::kv_t* ring = nullptr;
     __nv_bfloat16 *H_pc = nullptr, *Xa = nullptr, *Xb = nullptr;
     float *x = nullptr, *qbuf = nullptr;
@@ -409,10 +421,11 @@ inline int conv_plan(GemmPlan* g, const void* X, int rows, int K, const void* W,
     return QTTS_OK;
 }
 
-inline void add_roll(qtts_c2w* c, void* p, int ctx, int T, int row_bytes) {
+// history buffer segment: ctx rows + Fm frames of T rows; a call of F frames rolls rows [F*T, F*T + ctx)
+inline void add_roll(qtts_c2w* c, void* p, int ctx, int T, int Fm, int row_bytes) {
     RollJob& j = c->roll.job[c->roll.n++];
     j.ptr = reinterpret_cast<uint8_t*>(p);
-    j.seq_rows = ctx + T;
+    j.seq_rows = ctx + Fm * T;
     j.ctx = ctx;
     j.T = T;
     j.row_bytes = row_bytes;
@@ -437,8 +450,15 @@ inline int c2w_build(qtts_c2w* c) {
             set_error("c2w: dilation %d outside [1, %d]", d.dilations[j], kRollMaxCtx / 6);
             return QTTS_ERR_UNSUPPORTED;
         }
+    const int Fm = d.max_chunk > 0 ? d.max_chunk : 1;
+    if (Fm > W) {
+        set_error("c2w: max_chunk %d above the window %d", Fm, W);
+        return QTTS_ERR_UNSUPPORTED;
+    }
     c->S = S;
+    c->Fm = Fm;
     const int S1 = S + 1;  // slot-indexed state has a spare slot for rejected slot ids
+    const int SF = S * Fm;  // rows of a call at one row per frame
     c->T_up[0] = 2;
     c->T_up[1] = 4;
     int T = 4;
@@ -470,63 +490,66 @@ inline int c2w_build(qtts_c2w* c) {
 
     QTTS_TRY(c2w_alloc(c, &c->frame, S1));
     QTTS_TRY(c2w_alloc(c, &c->row_slot, S));
-    QTTS_TRY(c2w_alloc(c, &c->row_pos, S));
-    QTTS_TRY(c2w_alloc(c, &c->row_kv, S));
-    QTTS_TRY(c2w_alloc(c, &c->row_nkeys, S));
+    QTTS_TRY(c2w_alloc(c, &c->row_pos, SF));
+    QTTS_TRY(c2w_alloc(c, &c->row_kv, SF));
+    QTTS_TRY(c2w_alloc(c, &c->row_nkeys, SF));
+    QTTS_TRY(c2w_alloc(c, &c->row_lo, SF));
     QTTS_TRY(c2w_alloc(c, &c->ring, (size_t)S1 * L * 2 * NH * W * HD));
-    QTTS_TRY(c2w_alloc(c, &c->H_pc, (size_t)S1 * 3 * CD));
-    size_t xa = (size_t)S * c->K_pc;
-    xa = std::max(xa, (size_t)S * 4 * c->K_c0);
+    QTTS_TRY(c2w_alloc(c, &c->H_pc, (size_t)S1 * (2 + Fm) * CD));
+    size_t xa = (size_t)SF * c->K_pc;
+    xa = std::max(xa, (size_t)SF * 4 * c->K_c0);
     for (int b = 0; b < 4; ++b) {
-        if (!c->impl_tc[b]) xa = std::max(xa, (size_t)S * c->T_in[b] * c->K_tc[b]);
-        if (!c->impl_c1[b]) xa = std::max(xa, (size_t)S * c->T_blk[b] * c->K_c1[b]);
+        if (!c->impl_tc[b]) xa = std::max(xa, (size_t)SF * c->T_in[b] * c->K_tc[b]);
+        if (!c->impl_c1[b]) xa = std::max(xa, (size_t)SF * c->T_blk[b] * c->K_c1[b]);
     }
     QTTS_TRY(c2w_alloc(c, &c->Xa, xa));
-    QTTS_TRY(c2w_alloc(c, &c->Xb, (size_t)S * LAT));
-    QTTS_TRY(c2w_alloc(c, &c->x, (size_t)S * HID));
-    QTTS_TRY(c2w_alloc(c, &c->xn, (size_t)S * HID));
-    QTTS_TRY(c2w_alloc(c, &c->xn_lo, (size_t)S * HID));
-    QTTS_TRY(c2w_alloc(c, &c->qbuf, (size_t)S * NH * HD));
-    QTTS_TRY(c2w_alloc(c, &c->attn, (size_t)S * NH * HD));
-    QTTS_TRY(c2w_alloc(c, &c->attn_lo, (size_t)S * NH * HD));
-    QTTS_TRY(c2w_alloc(c, &c->act, (size_t)S * I));
-    QTTS_TRY(c2w_alloc(c, &c->act_lo, (size_t)S * I));
-    QTTS_TRY(c2w_alloc(c, &c->U0, (size_t)S * LAT));
-    QTTS_TRY(c2w_alloc(c, &c->U1, (size_t)S * 2 * LAT));
-    QTTS_TRY(c2w_alloc(c, &c->Xln, (size_t)S * 4 * LAT));
-    QTTS_TRY(c2w_alloc(c, &c->Xg, (size_t)S * 4 * CN));
-    for (int i = 0; i < 2; ++i) QTTS_TRY(c2w_alloc(c, &c->H_dw[i], (size_t)S1 * (6 + c->T_up[i]) * LAT));
-    QTTS_TRY(c2w_alloc(c, &c->H_c0, (size_t)S1 * (6 + 4) * LAT));
+    QTTS_TRY(c2w_alloc(c, &c->Xb, (size_t)SF * LAT));
+    QTTS_TRY(c2w_alloc(c, &c->x, (size_t)SF * HID));
+    QTTS_TRY(c2w_alloc(c, &c->xn, (size_t)SF * HID));
+    QTTS_TRY(c2w_alloc(c, &c->xn_lo, (size_t)SF * HID));
+    QTTS_TRY(c2w_alloc(c, &c->qbuf, (size_t)SF * NH * HD));
+    QTTS_TRY(c2w_alloc(c, &c->attn, (size_t)SF * NH * HD));
+    QTTS_TRY(c2w_alloc(c, &c->attn_lo, (size_t)SF * NH * HD));
+    QTTS_TRY(c2w_alloc(c, &c->act, (size_t)SF * I));
+    QTTS_TRY(c2w_alloc(c, &c->act_lo, (size_t)SF * I));
+    QTTS_TRY(c2w_alloc(c, &c->U0, (size_t)SF * LAT));
+    QTTS_TRY(c2w_alloc(c, &c->U1, (size_t)SF * 2 * LAT));
+    QTTS_TRY(c2w_alloc(c, &c->Xln, (size_t)SF * 4 * LAT));
+    QTTS_TRY(c2w_alloc(c, &c->Xg, (size_t)SF * 4 * CN));
+    for (int i = 0; i < 2; ++i) QTTS_TRY(c2w_alloc(c, &c->H_dw[i], (size_t)S1 * (6 + Fm * c->T_up[i]) * LAT));
+    QTTS_TRY(c2w_alloc(c, &c->H_c0, (size_t)S1 * (6 + Fm * 4) * LAT));
     for (int b = 0; b < 4; ++b) {
         const int Tb = c->T_blk[b], co = c->cout[b];
-        QTTS_TRY(c2w_alloc(c, &c->H_tc[b], (size_t)S1 * (1 + c->T_in[b]) * c->cinpad[b]));
-        QTTS_TRY(c2w_alloc(c, &c->h[b], (size_t)S * Tb * co));
+        QTTS_TRY(c2w_alloc(c, &c->H_tc[b], (size_t)S1 * (1 + Fm * c->T_in[b]) * c->cinpad[b]));
+        QTTS_TRY(c2w_alloc(c, &c->h[b], (size_t)SF * Tb * co));
         for (int j = 0; j < 3; ++j)
-            QTTS_TRY(c2w_alloc(c, &c->H_res[b][j], (size_t)S1 * (6 * d.dilations[j] + Tb) * c->cpad[b]));
-        QTTS_TRY(c2w_alloc(c, &c->X2[b], (size_t)S * Tb * c->N_c[b]));
+            QTTS_TRY(c2w_alloc(c, &c->H_res[b][j], (size_t)S1 * (6 * d.dilations[j] + Fm * Tb) * c->cpad[b]));
+        QTTS_TRY(c2w_alloc(c, &c->X2[b], (size_t)SF * Tb * c->N_c[b]));
     }
-    QTTS_TRY(c2w_alloc(c, &c->H_fin, (size_t)S1 * (6 + c->T_blk[3]) * c->cout[3]));
+    QTTS_TRY(c2w_alloc(c, &c->H_fin, (size_t)S1 * (6 + Fm * c->T_blk[3]) * c->cout[3]));
 
-    // the 21 streaming states, in the reference's order (conv 0..16, transconv 0..3)
+    // the 21 streaming states, in the reference's order (conv 0..16, transconv 0..3);
+    // segments hold ctx + Fm * (rows per frame) rows
     c->roll.n = 0;
-    add_roll(c, c->H_pc, 2, 1, CD * 2);
-    add_roll(c, c->H_dw[0], 6, c->T_up[0], LAT * 4);
-    add_roll(c, c->H_dw[1], 6, c->T_up[1], LAT * 4);
-    add_roll(c, c->H_c0, 6, 4, LAT * 2);
+    add_roll(c, c->H_pc, 2, 1, Fm, CD * 2);
+    add_roll(c, c->H_dw[0], 6, c->T_up[0], Fm, LAT * 4);
+    add_roll(c, c->H_dw[1], 6, c->T_up[1], Fm, LAT * 4);
+    add_roll(c, c->H_c0, 6, 4, Fm, LAT * 2);
     for (int b = 0; b < 4; ++b)
-        for (int j = 0; j < 3; ++j) add_roll(c, c->H_res[b][j], 6 * d.dilations[j], c->T_blk[b], c->cpad[b] * 2);
-    add_roll(c, c->H_fin, 6, c->T_blk[3], c->cout[3] * 2);
-    for (int b = 0; b < 4; ++b) add_roll(c, c->H_tc[b], 1, c->T_in[b], c->cinpad[b] * 2);
+        for (int j = 0; j < 3; ++j)
+            add_roll(c, c->H_res[b][j], 6 * d.dilations[j], c->T_blk[b], Fm, c->cpad[b] * 2);
+    add_roll(c, c->H_fin, 6, c->T_blk[3], Fm, c->cout[3] * 2);
+    for (int b = 0; b < 4; ++b) add_roll(c, c->H_tc[b], 1, c->T_in[b], Fm, c->cinpad[b] * 2);
     for (int i = 0; i < c->roll.n; ++i)
         if (c->roll.job[i].row_bytes % 16 != 0 || c->roll.job[i].row_bytes > kRollChunks * kRollChunk) {
             set_error("c2w: state rows must be multiples of 16 bytes, at most %d", kRollChunks * kRollChunk);
             return QTTS_ERR_UNSUPPORTED;
         }
 
-    // ---- front + transformer
-    QTTS_TRY(gemm_plan(&c->pre_conv, c->Xa, S, c->K_pc, d.w_pre_conv, LAT, QTTS_EPI_BF16, c->Xb, d.b_pre_conv,
+    // ---- front + transformer (one row per frame; plans sized for Fm frames per stream)
+    QTTS_TRY(gemm_plan(&c->pre_conv, c->Xa, SF, c->K_pc, d.w_pre_conv, LAT, QTTS_EPI_BF16, c->Xb, d.b_pre_conv,
                        nullptr));
-    QTTS_TRY(gemm_plan(&c->in_proj, c->Xb, S, LAT, d.w_in_proj, HID, QTTS_EPI_F32, c->x, d.b_in_proj, nullptr));
+    QTTS_TRY(gemm_plan(&c->in_proj, c->Xb, SF, LAT, d.w_in_proj, HID, QTTS_EPI_F32, c->x, d.b_in_proj, nullptr));
     c->layer.resize(L);
     for (int l = 0; l < L; ++l) {
         LayerGemms& g = c->layer[l];
@@ -546,44 +569,44 @@ inline int c2w_build(qtts_c2w* c) {
         q.layer = l;
         q.num_layers = L;
         q.block_size = W;
-        QTTS_TRY(gemm_plan(&g.qkv, c->xn, S, HID, bf(d.w_qkv, (size_t)l * 3 * HID * HID), 3 * HID, QTTS_EPI_QKV_ROPE,
-                           c->qbuf, nullptr, &q, c->xn_lo));
+        QTTS_TRY(gemm_plan(&g.qkv, c->xn, SF, HID, bf(d.w_qkv, (size_t)l * 3 * HID * HID), 3 * HID,
+                           QTTS_EPI_QKV_ROPE, c->qbuf, nullptr, &q, c->xn_lo));
         ConvEpi eo = conv_epi(c, 1, 1, HID, HID);
         eo.scale = bf(d.attn_scale, (size_t)l * HID);
         eo.res = view_rows(c->x, 1, HID);
         eo.out32 = eo.res;
-        QTTS_TRY(conv_plan(&g.o, c->attn, S, HID, bf(d.w_o, (size_t)l * HID * HID), HID, nullptr, eo, c->attn_lo));
-        QTTS_TRY(gemm_plan(&g.gu, c->xn, S, HID, bf(d.w_gate_up, (size_t)l * 2 * I * HID), 2 * I, QTTS_EPI_SWIGLU,
+        QTTS_TRY(conv_plan(&g.o, c->attn, SF, HID, bf(d.w_o, (size_t)l * HID * HID), HID, nullptr, eo, c->attn_lo));
+        QTTS_TRY(gemm_plan(&g.gu, c->xn, SF, HID, bf(d.w_gate_up, (size_t)l * 2 * I * HID), 2 * I, QTTS_EPI_SWIGLU,
                            c->act, nullptr, nullptr, c->xn_lo, c->act_lo));
         ConvEpi ed = eo;
         ed.scale = bf(d.mlp_scale, (size_t)l * HID);
-        QTTS_TRY(conv_plan(&g.down, c->act, S, I, bf(d.w_down, (size_t)l * HID * I), HID, nullptr, ed, c->act_lo));
+        QTTS_TRY(conv_plan(&g.down, c->act, SF, I, bf(d.w_down, (size_t)l * HID * I), HID, nullptr, ed, c->act_lo));
     }
-    QTTS_TRY(gemm_plan(&c->out_proj, c->xn, S, HID, d.w_out_proj, LAT, QTTS_EPI_BF16, c->U0, d.b_out_proj, nullptr,
+    QTTS_TRY(gemm_plan(&c->out_proj, c->xn, SF, HID, d.w_out_proj, LAT, QTTS_EPI_BF16, c->U0, d.b_out_proj, nullptr,
                        c->xn_lo));
     // ---- upsampling: transposed conv (k = s = 2) + ConvNeXt
     for (int i = 0; i < 2; ++i) {
         const int Tin = i == 0 ? 1 : 2, To = c->T_up[i];
         ConvEpi et = conv_epi(c, Tin, 2, LAT, 2 * LAT);
-        et.out32 = view_slot(c->H_dw[i], 6, To, LAT);
-        QTTS_TRY(conv_plan(&c->up_t[i], i == 0 ? c->U0 : c->U1, S * Tin, LAT, d.up_w[i], 2 * LAT, d.up_b[i], et));
+        et.out32 = view_slot(c->H_dw[i], 6, Fm * To, LAT);
+        QTTS_TRY(conv_plan(&c->up_t[i], i == 0 ? c->U0 : c->U1, SF * Tin, LAT, d.up_w[i], 2 * LAT, d.up_b[i], et));
         ConvEpi e1 = conv_epi(c, 1, 1, CN, CN);
         e1.act = ACT_GELU;
         e1.out16 = view_rows(c->Xg, 1, CN);
-        QTTS_TRY(conv_plan(&c->pw1[i], c->Xln, S * To, LAT, d.pw1_w[i], CN, d.pw1_b[i], e1));
+        QTTS_TRY(conv_plan(&c->pw1[i], c->Xln, SF * To, LAT, d.pw1_w[i], CN, d.pw1_b[i], e1));
         ConvEpi e2 = conv_epi(c, To, 1, LAT, LAT);
         e2.scale = reinterpret_cast<const __nv_bfloat16*>(d.gamma[i]);
-        e2.res = view_slot(c->H_dw[i], 6, To, LAT);
-        e2.out16 = i == 0 ? view_rows(c->U1, 2, LAT) : view_slot(c->H_c0, 6, 4, LAT);
-        QTTS_TRY(conv_plan(&c->pw2[i], c->Xg, S * To, CN, d.pw2_w[i], LAT, d.pw2_b[i], e2));
+        e2.res = view_slot(c->H_dw[i], 6, Fm * To, LAT);
+        e2.out16 = i == 0 ? view_rows(c->U1, 2, LAT) : view_slot(c->H_c0, 6, Fm * 4, LAT);
+        QTTS_TRY(conv_plan(&c->pw2[i], c->Xg, SF * To, CN, d.pw2_w[i], LAT, d.pw2_b[i], e2));
     }
     // ---- decoder conv k7 (latent -> decoder_dim), then SnakeBeta of block 0 into its transconv input
     {
         ConvEpi e = conv_epi(c, 4, 1, D0, D0);
         e.act = ACT_SNAKE;
         e.act_p = d.blk_snake[0];
-        e.out16 = view_slot(c->H_tc[0], 1, 4, c->cinpad[0]);
-        QTTS_TRY(conv_plan(&c->conv0, c->Xa, S * 4, c->K_c0, d.w_conv0, pad128(D0), d.b_conv0, e));
+        e.out16 = view_slot(c->H_tc[0], 1, Fm * 4, c->cinpad[0]);
+        QTTS_TRY(conv_plan(&c->conv0, c->Xa, SF * 4, c->K_c0, d.w_conv0, pad128(D0), d.b_conv0, e));
     }
     for (int b = 0; b < 4; ++b) {
         const int Tb = c->T_blk[b], co = c->cout[b], s = d.rates[b];
@@ -591,13 +614,13 @@ inline int c2w_build(qtts_c2w* c) {
         et.out32 = view_rows(c->h[b], Tb, co);
         et.act = ACT_SNAKE;
         et.act_p = d.res_act1[b][0];
-        et.out16 = view_slot(c->H_res[b][0], 6 * d.dilations[0], Tb, c->cpad[b]);
+        et.out16 = view_slot(c->H_res[b][0], 6 * d.dilations[0], Fm * Tb, c->cpad[b]);
         if (c->impl_tc[b])
-            QTTS_TRY(gemm_plan_implicit(&c->blk_t[b], c->H_tc[b], S1 * (1 + c->T_in[b]), c->cinpad[b], 2, 1,
-                                        c->T_in[b], 1 + c->T_in[b], S * c->T_in[b], d.blk_tw[b], c->N_tc[b],
+            QTTS_TRY(gemm_plan_implicit(&c->blk_t[b], c->H_tc[b], S1 * (1 + Fm * c->T_in[b]), c->cinpad[b], 2, 1,
+                                        c->T_in[b], 1 + Fm * c->T_in[b], SF * c->T_in[b], d.blk_tw[b], c->N_tc[b],
                                         d.blk_tb[b], et));
         else
-            QTTS_TRY(conv_plan(&c->blk_t[b], c->Xa, S * c->T_in[b], c->K_tc[b], d.blk_tw[b], c->N_tc[b],
+            QTTS_TRY(conv_plan(&c->blk_t[b], c->Xa, SF * c->T_in[b], c->K_tc[b], d.blk_tw[b], c->N_tc[b],
                                d.blk_tb[b], et));
         for (int j = 0; j < 3; ++j) {
             ConvEpi e1 = conv_epi(c, Tb, 1, co, co);
@@ -606,10 +629,11 @@ inline int c2w_build(qtts_c2w* c) {
             e1.out16 = view_rows(c->X2[b], Tb, c->N_c[b]);
             const int dil = d.dilations[j];
             if (c->impl_c1[b])
-                QTTS_TRY(gemm_plan_implicit(&c->c1[b][j], c->H_res[b][j], S1 * (6 * dil + Tb), c->cpad[b], 7, dil,
-                                            Tb, 6 * dil + Tb, S * Tb, d.res_w1[b][j], c->N_c[b], d.res_b1[b][j], e1));
+                QTTS_TRY(gemm_plan_implicit(&c->c1[b][j], c->H_res[b][j], S1 * (6 * dil + Fm * Tb), c->cpad[b], 7,
+                                            dil, Tb, 6 * dil + Fm * Tb, SF * Tb, d.res_w1[b][j], c->N_c[b],
+                                            d.res_b1[b][j], e1));
             else
-                QTTS_TRY(conv_plan(&c->c1[b][j], c->Xa, S * Tb, c->K_c1[b], d.res_w1[b][j], c->N_c[b],
+                QTTS_TRY(conv_plan(&c->c1[b][j], c->Xa, SF * Tb, c->K_c1[b], d.res_w1[b][j], c->N_c[b],
                                    d.res_b1[b][j], e1));
             ConvEpi e2 = conv_epi(c, Tb, 1, co, co);
             e2.res = view_rows(c->h[b], Tb, co);
@@ -617,105 +641,121 @@ inline int c2w_build(qtts_c2w* c) {
             e2.act = ACT_SNAKE;
             if (j < 2) {
                 e2.act_p = d.res_act1[b][j + 1];
-                e2.out16 = view_slot(c->H_res[b][j + 1], 6 * d.dilations[j + 1], Tb, c->cpad[b]);
+                e2.out16 = view_slot(c->H_res[b][j + 1], 6 * d.dilations[j + 1], Fm * Tb, c->cpad[b]);
             } else if (b < 3) {
                 e2.act_p = d.blk_snake[b + 1];
-                e2.out16 = view_slot(c->H_tc[b + 1], 1, Tb, c->cinpad[b + 1]);
+                e2.out16 = view_slot(c->H_tc[b + 1], 1, Fm * Tb, c->cinpad[b + 1]);
             } else {
                 e2.act_p = d.final_snake;
-                e2.out16 = view_slot(c->H_fin, 6, Tb, co);
+                e2.out16 = view_slot(c->H_fin, 6, Fm * Tb, co);
             }
-            QTTS_TRY(conv_plan(&c->c2[b][j], c->X2[b], S * Tb, c->N_c[b], d.res_w2[b][j], c->N_c[b], d.res_b2[b][j],
-                               e2));
+            QTTS_TRY(conv_plan(&c->c2[b][j], c->X2[b], SF * Tb, c->N_c[b], d.res_w2[b][j], c->N_c[b],
+                               d.res_b2[b][j], e2));
         }
     }
     return QTTS_OK;
 }
 
-inline int c2w_im2col(const qtts_c2w* c, const __nv_bfloat16* H, int ctx, int T, int C, int taps, int dil, int K,
-                      const int32_t* slots, int n, cudaStream_t st) {
+inline int c2w_im2col(const qtts_c2w* c, const __nv_bfloat16* H, int ctx, int seq_rows, int T, int C, int taps,
+                      int dil, int K, const int32_t* slots, int n, cudaStream_t st) {
     const size_t total = (size_t)n * T * (K / 8);
     const int blocks = (int)std::min<size_t>((total + 255) / 256, (size_t)num_sms() * 8);
-    QTTS_LAUNCH(c2w_im2col_kernel, dim3(blocks), dim3(256), 0, st, H, ctx + T, C, taps, dil, T, slots, n, c->Xa, K);
+    QTTS_LAUNCH(c2w_im2col_kernel, dim3(blocks), dim3(256), 0, st, H, seq_rows, C, taps, dil, T, slots, n, c->Xa, K);
     return QTTS_OK;
 }
 
-inline int run_conv(GemmPlan g, int M, const int32_t* slots, cudaStream_t st) {
+// A plan built for one frame's rows per stream, run on F frames: rows per stream and the
+// stride of the per-call (not slot-indexed) buffers scale by F; history buffers keep their
+// segment size (ctx + Fm * rows per frame).
+inline int run_conv(GemmPlan g, int M, const int32_t* slots, cudaStream_t st, int F) {
     g.p.conv.row_slot = slots;
+    g.p.conv.T_rows *= F;
+    for (ActView* v : {&g.p.conv.res, &g.p.conv.out32, &g.p.conv.out16})
+        if (!v->by_slot) v->seq_rows *= F;
     g.p.ix.row_slot = slots;  // implicit convolutions read the history rows of each row's slot
+    g.p.ix.T *= F;
     return gemm_run(g, M, st);
 }
 
-inline int c2w_step_impl(qtts_c2w* c, const int64_t* codes, int codes_ld, const int32_t* slots_in, int n,
+inline int c2w_step_impl(qtts_c2w* c, const int64_t* codes, int codes_ld, int F, const int32_t* slots_in, int n,
                          float* wav, cudaStream_t st) {
     const qtts_c2w_desc& d = c->d;
     if (n <= 0 || n > c->S || !codes || !slots_in || !wav || codes_ld < d.num_codebooks) {
         set_error("c2w_step: n=%d outside (0, %d] or missing pointers", n, c->S);
         return QTTS_ERR_INVALID;
     }
+    if (F < 1 || F > c->Fm) {
+        set_error("c2w_step: %d frames outside [1, %d] (max_chunk)", F, c->Fm);
+        return QTTS_ERR_INVALID;
+    }
+    const int Fm = c->Fm, nF = n * F;
     const int LAT = d.latent, HID = d.hidden, NH = d.heads, HD = d.head_dim, CD = d.codebook_dim, L = d.layers;
-    QTTS_LAUNCH(c2w_rvq_kernel, dim3(n), dim3(256), 0, st, d.rvq_tables, d.num_codebooks, d.codebook_size, CD, codes,
-                codes_ld, slots_in, c->S, c->frame, d.window, d.max_frames, c->row_slot, c->row_pos, c->row_kv,
-                c->row_nkeys, view_slot(c->H_pc, 2, 1, CD));
-    const int32_t* slots = c->row_slot;  // validated slot of each row
-    QTTS_TRY(c2w_im2col(c, c->H_pc, 2, 1, CD, 3, 1, c->K_pc, slots, n, st));
-    QTTS_TRY(gemm_run(c->pre_conv, n, st));
-    QTTS_TRY(gemm_run(c->in_proj, n, st));
+    QTTS_LAUNCH(c2w_rvq_kernel, dim3(nF), dim3(256), 0, st, d.rvq_tables, d.num_codebooks, d.codebook_size, CD, codes,
+                codes_ld, F, slots_in, c->S, (const int32_t*)c->frame, d.window, d.max_frames, c->row_slot,
+                c->row_pos, c->row_kv, c->row_nkeys, c->row_lo, view_slot(c->H_pc, 2, Fm, CD));
+    const int32_t* slots = c->row_slot;  // validated slot of each stream
+    QTTS_TRY(c2w_im2col(c, c->H_pc, 2, 2 + Fm, F, CD, 3, 1, c->K_pc, slots, n, st));
+    QTTS_TRY(gemm_run(c->pre_conv, nF, st));
+    QTTS_TRY(gemm_run(c->in_proj, nF, st));
     for (int l = 0; l < L; ++l) {
         const LayerGemms& g = c->layer[l];
-        QTTS_TRY(launch_rmsnorm(c->x, n, HID, HID, bf(d.w_in_norm, (size_t)l * HID), d.rms_eps, c->xn, st, c->xn_lo));
-        QTTS_TRY(gemm_run(g.qkv, n, st));
+        QTTS_TRY(launch_rmsnorm(c->x, nF, HID, HID, bf(d.w_in_norm, (size_t)l * HID), d.rms_eps, c->xn, st,
+                                c->xn_lo));
+        QTTS_TRY(gemm_run(g.qkv, nF, st));
         const float scale = 1.0f / sqrtf((float)HD);
         if (HD == 64)
-            QTTS_LAUNCH(c2w_attn_kernel<64>, dim3(n, ceil_div(NH, 4)), dim3(128), 0, st, (const float*)c->qbuf,
-                        (const kv_t*)c->ring, NH, L, l, d.window, slots, (const int32_t*)c->row_nkeys, scale, c->attn,
-                        c->attn_lo);
+            QTTS_LAUNCH(c2w_attn_kernel<64>, dim3(nF, ceil_div(NH, 4)), dim3(128), 0, st, (const float*)c->qbuf,
+                        (const kv_t*)c->ring, NH, L, l, d.window, F, slots, (const int32_t*)c->row_nkeys,
+                        (const int32_t*)c->row_lo, scale, c->attn, c->attn_lo);
         else
-            QTTS_LAUNCH(c2w_attn_kernel<32>, dim3(n, ceil_div(NH, 4)), dim3(128), 0, st, (const float*)c->qbuf,
-                        (const kv_t*)c->ring, NH, L, l, d.window, slots, (const int32_t*)c->row_nkeys, scale, c->attn,
-                        c->attn_lo);
-        QTTS_TRY(run_conv(g.o, n, slots, st));
-        QTTS_TRY(launch_rmsnorm(c->x, n, HID, HID, bf(d.w_post_norm, (size_t)l * HID), d.rms_eps, c->xn, st,
+            QTTS_LAUNCH(c2w_attn_kernel<32>, dim3(nF, ceil_div(NH, 4)), dim3(128), 0, st, (const float*)c->qbuf,
+                        (const kv_t*)c->ring, NH, L, l, d.window, F, slots, (const int32_t*)c->row_nkeys,
+                        (const int32_t*)c->row_lo, scale, c->attn, c->attn_lo);
+        QTTS_TRY(run_conv(g.o, nF, slots, st, F));
+        QTTS_TRY(launch_rmsnorm(c->x, nF, HID, HID, bf(d.w_post_norm, (size_t)l * HID), d.rms_eps, c->xn, st,
                                 c->xn_lo));
-        QTTS_TRY(gemm_run(g.gu, n, st));
-        QTTS_TRY(run_conv(g.down, n, slots, st));
+        QTTS_TRY(gemm_run(g.gu, nF, st));
+        QTTS_TRY(run_conv(g.down, nF, slots, st, F));
     }
-    QTTS_TRY(launch_rmsnorm(c->x, n, HID, HID, d.w_final_norm, d.rms_eps, c->xn, st, c->xn_lo));
-    QTTS_TRY(gemm_run(c->out_proj, n, st));
+    QTTS_TRY(launch_rmsnorm(c->x, nF, HID, HID, d.w_final_norm, d.rms_eps, c->xn, st, c->xn_lo));
+    QTTS_TRY(gemm_run(c->out_proj, nF, st));
     for (int i = 0; i < 2; ++i) {
         const int Tin = i == 0 ? 1 : 2, To = c->T_up[i];
-        QTTS_TRY(run_conv(c->up_t[i], n * Tin, slots, st));
-        QTTS_LAUNCH(c2w_dwconv_ln_kernel, dim3(n * To), dim3(256), 0, st, (const float*)c->H_dw[i], 6 + To, LAT, To,
-                    slots, d.dw_w[i], d.dw_b[i], d.ln_w[i], d.ln_b[i], d.ln_eps, c->Xln);
-        QTTS_TRY(run_conv(c->pw1[i], n * To, slots, st));
-        QTTS_TRY(run_conv(c->pw2[i], n * To, slots, st));
+        QTTS_TRY(run_conv(c->up_t[i], nF * Tin, slots, st, F));
+        QTTS_LAUNCH(c2w_dwconv_ln_kernel, dim3(nF * To), dim3(256), 0, st, (const float*)c->H_dw[i], 6 + Fm * To,
+                    LAT, F * To, slots, d.dw_w[i], d.dw_b[i], d.ln_w[i], d.ln_b[i], d.ln_eps, c->Xln);
+        QTTS_TRY(run_conv(c->pw1[i], nF * To, slots, st, F));
+        QTTS_TRY(run_conv(c->pw2[i], nF * To, slots, st, F));
     }
-    QTTS_TRY(c2w_im2col(c, c->H_c0, 6, 4, LAT, 7, 1, c->K_c0, slots, n, st));
-    QTTS_TRY(run_conv(c->conv0, n * 4, slots, st));
+    QTTS_TRY(c2w_im2col(c, c->H_c0, 6, 6 + Fm * 4, F * 4, LAT, 7, 1, c->K_c0, slots, n, st));
+    QTTS_TRY(run_conv(c->conv0, nF * 4, slots, st, F));
     for (int b = 0; b < 4; ++b) {
         const int Tb = c->T_blk[b], co = c->cout[b];
         if (!c->impl_tc[b])
-            QTTS_TRY(c2w_im2col(c, c->H_tc[b], 1, c->T_in[b], c->cin[b], 2, 1, c->K_tc[b], slots, n, st));
-        QTTS_TRY(run_conv(c->blk_t[b], n * c->T_in[b], slots, st));
+            QTTS_TRY(c2w_im2col(c, c->H_tc[b], 1, 1 + Fm * c->T_in[b], F * c->T_in[b], c->cin[b], 2, 1, c->K_tc[b],
+                                slots, n, st));
+        QTTS_TRY(run_conv(c->blk_t[b], nF * c->T_in[b], slots, st, F));
         for (int j = 0; j < 3; ++j) {
             const int dil = d.dilations[j];
             if (!c->impl_c1[b])
-                QTTS_TRY(c2w_im2col(c, c->H_res[b][j], 6 * dil, Tb, co, 7, dil, c->K_c1[b], slots, n, st));
-            QTTS_TRY(run_conv(c->c1[b][j], n * Tb, slots, st));
-            QTTS_TRY(run_conv(c->c2[b][j], n * Tb, slots, st));
+                QTTS_TRY(c2w_im2col(c, c->H_res[b][j], 6 * dil, 6 * dil + Fm * Tb, F * Tb, co, 7, dil, c->K_c1[b],
+                                    slots, n, st));
+            QTTS_TRY(run_conv(c->c1[b][j], nF * Tb, slots, st, F));
+            QTTS_TRY(run_conv(c->c2[b][j], nF * Tb, slots, st, F));
         }
     }
-    QTTS_LAUNCH(c2w_final_conv_kernel, dim3(ceil_div(c->T_blk[3], kFinalChunk), n), dim3(kFinalChunk), 0, st,
-                (const __nv_bfloat16*)c->H_fin, 6 + c->T_blk[3], c->cout[3], c->T_blk[3], slots, d.final_w,
-                d.final_b, wav);
-    QTTS_LAUNCH(c2w_roll_kernel, dim3(n, c->roll.n, kRollChunks), dim3(128), 0, st, c->roll, slots);
+    const int T3 = F * c->T_blk[3];
+    QTTS_LAUNCH(c2w_final_conv_kernel, dim3(ceil_div(T3, kFinalChunk), n), dim3(kFinalChunk), 0, st,
+                (const __nv_bfloat16*)c->H_fin, 6 + Fm * c->T_blk[3], c->cout[3], T3, slots, d.final_w, d.final_b,
+                wav);
+    QTTS_LAUNCH(c2w_roll_kernel, dim3(n, c->roll.n, kRollChunks), dim3(128), 0, st, c->roll, slots, F, c->frame);
     return QTTS_OK;
 }
 
-inline int c2w_step(qtts_c2w* c, const int64_t* codes, int codes_ld, const int32_t* slots, int n, float* wav,
+inline int c2w_step(qtts_c2w* c, const int64_t* codes, int codes_ld, int F, const int32_t* slots, int n, float* wav,
                     cudaStream_t st) {
     const int before = g_launch_count;
-    const int rc = c2w_step_impl(c, codes, codes_ld, slots, n, wav, st);
+    const int rc = c2w_step_impl(c, codes, codes_ld, F, slots, n, wav, st);
     c->launches = g_launch_count - before;
     return rc;
 }

@@ -290,10 +290,10 @@ int qtts_c2w_reset(qtts_c2w* c, const int32_t* slots, int n, qtts_stream_t strea
     return c2w_reset(c, slots, n, (cudaStream_t)stream);
 }
 
-int qtts_c2w_step(qtts_c2w* c, const int64_t* codes, int codes_ld, const int32_t* slots, int n, float* wav,
+int qtts_c2w_step(qtts_c2w* c, const int64_t* codes, int codes_ld, int frames, const int32_t* slots, int n, float* wav,
                   qtts_stream_t stream) {
     QTTS_REQUIRE(c, "c2w_step: null decoder");
-    return c2w_step(c, codes, codes_ld, slots, n, wav, (cudaStream_t)stream);
+    return c2w_step(c, codes, codes_ld, frames, slots, n, wav, (cudaStream_t)stream);
 }
 
 int qtts_c2w_launches(const qtts_c2w* c) { return c ? c->launches : 0; }

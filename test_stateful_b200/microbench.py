@@ -2,7 +2,7 @@
 
     python -m test_stateful_b200.microbench attention [--rows 64] [--ctx-mean 520] [--launches 50]
     python -m test_stateful_b200.microbench gemm [--n 12288] [--k 2048] [--m 64] [--launches 50]
-    python -m test_stateful_b200.microbench code2wav [--rows 64] [--launches 50]
+    python -m test_stateful_b200.microbench code2wav [--rows 64] [--launches 50] [--chunk 25]
 
 Prints one JSON line with the mean launch time (CUDA events) and the
 achieved bandwidth over the kernel's algorithmic bytes:
@@ -101,28 +101,29 @@ def bench_gemm(n: int, k: int, m: int, launches: int, seed: int = 0):
             "tflops": 2 * 2 * m * n * k / sec / 1e12}
 
 
-def bench_code2wav(rows: int, launches: int, seed: int = 0):
-    """One streaming code2wav step (full decoder widths) for `rows` streams,
-    captured in a CUDA graph and replayed; frames/s = rows / step time."""
+def bench_code2wav(rows: int, launches: int, seed: int = 0, chunk: int = 1):
+    """One code2wav call (full decoder widths) for `rows` streams x `chunk` frames,
+    captured in a CUDA graph and replayed; frames/s = rows * chunk / call time."""
     from . import weights as wmod
     from .config import Code2WavConfig
     from .runtime.code2wav import DeviceCode2Wav
     dev = "cuda"
     cfg = Code2WavConfig()
-    dec = DeviceCode2Wav(cfg, wmod.make_code2wav_weights(cfg, seed), dev, max_slots=rows, max_frames=1024)
+    dec = DeviceCode2Wav(cfg, wmod.make_code2wav_weights(cfg, seed), dev, max_slots=rows, max_frames=4096,
+                         max_chunk=chunk)
     slots = torch.arange(rows, dtype=torch.int32, device=dev)
     dec.reset(slots)
     g = torch.Generator(device=dev).manual_seed(seed)
-    codes = torch.randint(0, cfg.codebook_size, (rows, 16), generator=g, device=dev)
-    wav = torch.empty(rows, cfg.samples_per_frame, device=dev)
+    codes = torch.randint(0, cfg.codebook_size, (rows, chunk, 16), generator=g, device=dev)
+    wav = torch.empty(rows, chunk * cfg.samples_per_frame, device=dev)
     s = torch.cuda.Stream()
     with torch.cuda.stream(s):
         for _ in range(3):
-            dec.step(codes, slots, wav, stream=s)
+            dec.step(codes, slots, wav, stream=s, frames=chunk)
         s.synchronize()
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=s):
-            dec.step(codes, slots, wav, stream=s)
+            dec.step(codes, slots, wav, stream=s, frames=chunk)
         for _ in range(3):
             graph.replay()
         s.synchronize()
@@ -133,8 +134,9 @@ def bench_code2wav(rows: int, launches: int, seed: int = 0):
         e1.record(s)
         s.synchronize()
     sec = e0.elapsed_time(e1) / 1e3 / launches
-    flops = 5.1e9 * rows
-    out = {"kernel": "code2wav step", "rows": rows, "step_us": sec * 1e6, "frames_per_s": rows / sec,
+    flops = 5.1e9 * rows * chunk
+    out = {"kernel": "code2wav step", "rows": rows, "chunk": chunk, "step_us": sec * 1e6,
+           "frames_per_s": rows * chunk / sec,
            "kernels_per_step": dec.last_launches, "approx_tflops": flops / sec / 1e12,
            "wav_absmean": float(wav.abs().mean())}
     dec.close()
@@ -151,11 +153,12 @@ def main():
     ap.add_argument("--m", type=int, default=64)
     ap.add_argument("--launches", type=int, default=50)
     ap.add_argument("--split", type=int, default=0, help="attention: KV blocks per split (0: library default)")
+    ap.add_argument("--chunk", type=int, default=1, help="code2wav: frames per stream per call")
     a = ap.parse_args()
     if a.what == "attention":
         r = bench_attention(a.rows, a.ctx_mean, a.launches, split=a.split)
     elif a.what == "code2wav":
-        r = bench_code2wav(a.rows, a.launches)
+        r = bench_code2wav(a.rows, a.launches, chunk=a.chunk)
     else:
         r = bench_gemm(a.n, a.k, a.m, a.launches)
     print(json.dumps(r))

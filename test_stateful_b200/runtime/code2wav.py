@@ -166,7 +166,7 @@ class DeviceCode2Wav:
     """Packed weights + native decoder state for ``max_slots`` streams on one GPU."""
 
     def __init__(self, cfg: Code2WavConfig, weights: Dict[str, torch.Tensor], device, max_slots: int,
-                 max_frames: int = 4096):
+                 max_frames: int = 4096, max_chunk: int = 1):
         self.cfg = cfg
         self.device = torch.device(device)
         self.max_slots = max_slots
@@ -180,7 +180,8 @@ class DeviceCode2Wav:
         d.heads, d.head_dim, d.inter = cfg.num_heads, cfg.head_dim, cfg.intermediate_size
         d.window, d.decoder_dim = cfg.window, cfg.decoder_dim
         d.convnext_dim = cfg.convnext_mult * cfg.latent_dim
-        d.max_slots, d.max_frames = max_slots, max_frames
+        d.max_slots, d.max_frames, d.max_chunk = max_slots, max_frames, max_chunk
+        self.max_chunk = max_chunk
         d.up_ratio[:] = list(cfg.upsample_ratios)
         d.rates[:] = list(cfg.upsample_rates)
         d.dilations[:] = list(cfg.dilations)
@@ -215,12 +216,17 @@ class DeviceCode2Wav:
         _lib.check(lib.qtts_c2w_reset(self.handle, _lib.ptr(slots), int(slots.numel()), _lib.stream_ptr(stream)),
                    "c2w_reset")
 
-    def step(self, codes: torch.Tensor, slots: torch.Tensor, wav: torch.Tensor, n: int = None, stream=None) -> None:
-        """One frame per row: ``codes`` int64 [n][>=16] (device), ``slots`` int32 [n], ``wav`` fp32 [n][1920]."""
+    def step(self, codes: torch.Tensor, slots: torch.Tensor, wav: torch.Tensor, n: int = None, stream=None,
+             frames: int = 1) -> None:
+        """``frames`` frames per stream: ``codes`` int64 [n][>=16] (frames = 1) or [n][frames][16]
+        (device, contiguous), ``slots`` int32 [n], ``wav`` fp32 [n][frames * 1920]."""
         n = int(slots.numel()) if n is None else n
         assert codes.dtype == torch.int64 and slots.dtype == torch.int32 and wav.dtype == torch.float32
+        ld = int(codes.stride(-2)) if codes.dim() == 3 else int(codes.stride(0))
+        if codes.dim() == 3:
+            assert codes.is_contiguous() and codes.shape[1] == frames
         lib = _lib.load()
-        _lib.check(lib.qtts_c2w_step(self.handle, _lib.ptr(codes), int(codes.stride(0)), _lib.ptr(slots), n,
+        _lib.check(lib.qtts_c2w_step(self.handle, _lib.ptr(codes), ld, frames, _lib.ptr(slots), n,
                                      _lib.ptr(wav), _lib.stream_ptr(stream)), "c2w_step")
         self.last_launches = lib.qtts_c2w_launches(self.handle)
 

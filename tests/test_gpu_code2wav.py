@@ -105,3 +105,33 @@ def test_code2wav_reset_replays_identically():
         runs.append(torch.cat(w))
     torch.testing.assert_close(runs[0], runs[1], rtol=0, atol=0)
     dec.close()
+
+
+def test_code2wav_chunked_matches_reference_fixture():
+    """BASELINE cfg4: chunks of 25, 25, 25 and 7 frames per call with carried state, two slots
+    with ragged pasts (slot 1 joins one call later), against the reference wrapper's output."""
+    z = np.load(os.path.join(GOLDEN, "code2wav_chunked_tiny.npz"))
+    cfg = tiny_code2wav_config()
+    dec = DeviceCode2Wav(cfg, wmod.make_code2wav_weights(cfg, int(z["seed"])), DEV, max_slots=3, max_frames=256,
+                         max_chunk=25)
+    codes, chunks, start1 = torch.from_numpy(z["codes"]).long(), z["chunks"].tolist(), int(z["start1"])
+    dev_slot = [2, 0]
+    out = [[], []]
+    f = [0, 0]
+    for call, T in enumerate(chunks):
+        act = [0] + ([1] if call >= start1 else [])
+        new = [i for i in act if f[i] == 0]
+        dec.reset(torch.tensor([dev_slot[i] for i in new], dtype=torch.int32, device=DEV))
+        cds = torch.stack([codes[i, :, f[i]:f[i] + T].t() for i in act]).contiguous().to(DEV)  # [n][T][16]
+        wav = torch.empty(len(act), T * cfg.samples_per_frame, device=DEV)
+        dec.step(cds, torch.tensor([dev_slot[i] for i in act], dtype=torch.int32, device=DEV), wav, frames=T)
+        for k, i in enumerate(act):
+            out[i].append(wav[k].cpu().numpy())
+            f[i] += T
+    assert _lib.device_error() == 0
+    for i, ref in ((0, z["wav0"]), (1, z["wav1"])):
+        got = np.concatenate(out[i])
+        assert got.shape == ref.shape
+        s = snr_db(ref.astype(np.float32), got)
+        assert s >= SNR_DB, (i, s)
+    dec.close()
