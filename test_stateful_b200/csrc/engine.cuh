@@ -50,7 +50,8 @@ struct qtts_engine {
     // talker activations
     // GEMM operands are hi/lo bf16 pairs (x_lo = bf16(x - x_hi)), see gemm_tc.cuh
     float* x = nullptr;              // [rmax][H] fp32 residual stream
-    __nv_bfloat16 *xn = nullptr, *xn_lo = nullptr;      // [rmax][H] normed x
+    __nv_bfloat16 *xn = nullptr, *xn_lo = nullptr;      // [rmax][H] normed x (layer 0) or x∘γ (folded norms)
+    float* ss = nullptr;                                // [rmax][H/128] folded-norm partial sums of x²
     float* qbuf = nullptr;                              // [rmax][Hq*D] fp32 q after norm + RoPE
     __nv_bfloat16 *attn = nullptr, *attn_lo = nullptr;  // [rmax][Hq*D]
     __nv_bfloat16 *act = nullptr, *act_lo = nullptr;    // [rmax][I] SwiGLU output
@@ -62,7 +63,8 @@ struct qtts_engine {
     // code predictor
     __nv_bfloat16 *cp_in = nullptr, *cp_in_lo = nullptr;  // [2*bmax][H]
     float* cx = nullptr;                                  // [2*bmax][cpH]
-    __nv_bfloat16 *cxn = nullptr, *cxn_lo = nullptr;      // [2*bmax][cpH]
+    __nv_bfloat16 *cxn = nullptr, *cxn_lo = nullptr;      // [2*bmax][cpH] x∘γ of the folded norms
+    float* css = nullptr;                                 // [2*bmax][cpH/128]
     float* cq = nullptr;
     __nv_bfloat16 *cattn = nullptr, *cattn_lo = nullptr;
     __nv_bfloat16 *cact = nullptr, *cact_lo = nullptr;
@@ -101,6 +103,22 @@ inline int dev_alloc(qtts_engine* e, T** p, size_t count) {
 
 inline const __nv_bfloat16* bf(const void* p, size_t off) { return reinterpret_cast<const __nv_bfloat16*>(p) + off; }
 
+// Fold an RMSNorm between two GEMMs: `prod` (F32 / RESIDUAL epilogue writing x) also
+// emits x∘γ as the hi/lo operand and the per-tile sums of x²; `cons` reads them.
+inline void fold_norm_out(GemmPlan& prod, const __nv_bfloat16* gamma, __nv_bfloat16* hi, __nv_bfloat16* lo,
+                          float* ss) {
+    prod.p.nout.gamma = gamma;
+    prod.p.nout.hi = hi;
+    prod.p.nout.lo = lo;
+    prod.p.nout.ss = ss;
+}
+inline void fold_norm_in(GemmPlan& cons, const float* ss, int hidden, float eps) {
+    cons.p.nin.ss = ss;
+    cons.p.nin.parts = hidden / 128;
+    cons.p.nin.K = hidden;
+    cons.p.nin.eps = eps;
+}
+
 inline int engine_build(qtts_engine* e) {
     const qtts_model_desc& d = e->d;
     const int H = d.hidden, D = d.head_dim, Hq = d.heads, Hkv = d.kv_heads, I = d.inter;
@@ -114,6 +132,7 @@ inline int engine_build(qtts_engine* e) {
     QTTS_TRY(dev_alloc(e, &e->x, (size_t)rmax * H));
     QTTS_TRY(dev_alloc(e, &e->xn, (size_t)rmax * H));
     QTTS_TRY(dev_alloc(e, &e->xn_lo, (size_t)rmax * H));
+    QTTS_TRY(dev_alloc(e, &e->ss, (size_t)rmax * (H / 128)));
     QTTS_TRY(dev_alloc(e, &e->qbuf, (size_t)rmax * Hq * D));
     QTTS_TRY(dev_alloc(e, &e->attn, (size_t)rmax * Hq * D));
     QTTS_TRY(dev_alloc(e, &e->attn_lo, (size_t)rmax * Hq * D));
@@ -158,6 +177,12 @@ inline int engine_build(qtts_engine* e) {
                            e->act, nullptr, nullptr, e->xn_lo, e->act_lo));
         QTTS_TRY(gemm_plan(&g.down, e->act, rmax, I, bf(d.w_down, (size_t)l * H * I), H, QTTS_EPI_RESIDUAL, e->x,
                            nullptr, nullptr, e->act_lo));
+        // post-attention norm folded into o-proj -> gate/up; the next layer's input
+        // norm into down -> next qkv (layer 0's input norm stays a kernel)
+        fold_norm_out(g.o, bf(d.w_post_norm, (size_t)l * H), e->xn, e->xn_lo, e->ss);
+        fold_norm_in(g.gu, e->ss, H, d.rms_eps);
+        if (l > 0) fold_norm_in(g.qkv, e->ss, H, d.rms_eps);
+        if (l + 1 < d.layers) fold_norm_out(g.down, bf(d.w_in_norm, (size_t)(l + 1) * H), e->xn, e->xn_lo, e->ss);
     }
     QTTS_TRY(dev_alloc(e, &e->cp_table, (size_t)bmax));
     // ---- code predictor
@@ -171,6 +196,7 @@ inline int engine_build(qtts_engine* e) {
     QTTS_TRY(dev_alloc(e, &e->cx, (size_t)crows * cH));
     QTTS_TRY(dev_alloc(e, &e->cxn, (size_t)crows * cH));
     QTTS_TRY(dev_alloc(e, &e->cxn_lo, (size_t)crows * cH));
+    QTTS_TRY(dev_alloc(e, &e->css, (size_t)crows * (cH / 128)));
     QTTS_TRY(dev_alloc(e, &e->cq, (size_t)crows * cHq * cD));
     QTTS_TRY(dev_alloc(e, &e->cattn, (size_t)crows * cHq * cD));
     QTTS_TRY(dev_alloc(e, &e->cattn_lo, (size_t)crows * cHq * cD));
@@ -238,12 +264,20 @@ inline int engine_build(qtts_engine* e) {
                            QTTS_EPI_SWIGLU, e->cact, nullptr, nullptr, e->cxn_lo, e->cact_lo));
         QTTS_TRY(gemm_plan(&g.down, e->cact, crows, cI, bf(d.cp_w_down, (size_t)l * cH * cI), cH, QTTS_EPI_RESIDUAL,
                            e->cx, nullptr, nullptr, e->cact_lo));
+        fold_norm_out(g.o, bf(d.cp_w_post_norm, (size_t)l * cH), e->cxn, e->cxn_lo, e->css);
+        fold_norm_in(g.gu, e->css, cH, d.cp_rms_eps);
+        fold_norm_in(g.qkv, e->css, cH, d.cp_rms_eps);
+        if (l + 1 < d.cp_layers)
+            fold_norm_out(g.down, bf(d.cp_w_in_norm, (size_t)(l + 1) * cH), e->cxn, e->cxn_lo, e->css);
     }
     // stage 0 projects [talker hidden (hi/lo), codec embedding]; later stages only embeddings (exact in bf16)
     QTTS_TRY(gemm_plan(&e->cp_proj_pair, e->cp_in, crows, H, d.cp_w_proj, cH, QTTS_EPI_F32, e->cx, d.cp_b_proj,
                        nullptr, e->cp_in_lo));
     QTTS_TRY(gemm_plan(&e->cp_proj_one, e->cp_in, crows, H, d.cp_w_proj, cH, QTTS_EPI_F32, e->cx, d.cp_b_proj,
                        nullptr));
+    // the first layer's input norm folded into the projection
+    fold_norm_out(e->cp_proj_pair, bf(d.cp_w_in_norm, 0), e->cxn, e->cxn_lo, e->css);
+    fold_norm_out(e->cp_proj_one, bf(d.cp_w_in_norm, 0), e->cxn, e->cxn_lo, e->css);
     e->cp_heads.resize(S);
     for (int s = 0; s < S; ++s)
         QTTS_TRY(gemm_plan(&e->cp_heads[s], e->chid, bmax, cH, bf(d.cp_w_lm_head, (size_t)s * d.cp_vocab * cH),
@@ -309,12 +343,12 @@ inline int engine_step_impl(qtts_engine* e, const qtts_step_io& io, cudaStream_t
     // ---- talker layers
     for (int l = 0; l < d.layers; ++l) {
         const LayerGemms& g = e->tg[l];
-        QTTS_TRY(launch_rmsnorm(e->x, R, H, H, bf(d.w_in_norm, (size_t)l * H), d.rms_eps, e->xn, st, e->xn_lo));
+        if (l == 0)  // later input norms are folded into the previous layer's down projection
+            QTTS_TRY(launch_rmsnorm(e->x, R, H, H, bf(d.w_in_norm, 0), d.rms_eps, e->xn, st, e->xn_lo));
         QTTS_TRY(run_plan(g.qkv, R, st));
         ap.layer = l;
         QTTS_TRY(launch_attention(ap, D, st));
-        QTTS_TRY(run_plan(g.o, R, st));
-        QTTS_TRY(launch_rmsnorm(e->x, R, H, H, bf(d.w_post_norm, (size_t)l * H), d.rms_eps, e->xn, st, e->xn_lo));
+        QTTS_TRY(run_plan(g.o, R, st));  // + post-attention norm (folded)
         QTTS_TRY(run_plan(g.gu, R, st));
         QTTS_TRY(run_plan(g.down, R, st));
     }
@@ -390,17 +424,13 @@ inline int engine_step_impl(qtts_engine* e, const qtts_step_io& io, cudaStream_t
         cap.R = rows;
         for (int l = 0; l < d.cp_layers; ++l) {
             const LayerGemms& g = e->cg[l];
-            QTTS_TRY(launch_rmsnorm(e->cx, rows, cH, cH, bf(d.cp_w_in_norm, (size_t)l * cH), d.cp_rms_eps, e->cxn, st,
-                                    e->cxn_lo));
-            GemmPlan q = g.qkv;
+            GemmPlan q = g.qkv;  // input norm folded into the projection / previous down GEMM
             q.p.qkv.row_pos = m + crows;
             q.p.qkv.slot_mapping = m;
             QTTS_TRY(run_plan(q, rows, st));
             cap.layer = l;
             QTTS_TRY(launch_short_attention(cap, cD, st));  // <= 16 keys per row
-            QTTS_TRY(run_plan(g.o, rows, st));
-            QTTS_TRY(launch_rmsnorm(e->cx, rows, cH, cH, bf(d.cp_w_post_norm, (size_t)l * cH), d.cp_rms_eps, e->cxn,
-                                    st, e->cxn_lo));
+            QTTS_TRY(run_plan(g.o, rows, st));  // + post-attention norm (folded)
             QTTS_TRY(run_plan(g.gu, rows, st));
             QTTS_TRY(run_plan(g.down, rows, st));
         }

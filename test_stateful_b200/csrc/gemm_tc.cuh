@@ -84,6 +84,26 @@ struct ImplicitX {
     const int32_t* row_slot;
 };
 
+// RMSNorm folded into the GEMMs around it.  RMSNorm(x)·W^T = inv_rms(x) · ((x∘γ)·W^T)
+// with inv_rms(x) = 1/sqrt(mean(x²) + eps) a per-token scalar, so
+//  - the PRODUCER of x (an F32 or RESIDUAL epilogue) also writes the bf16 hi/lo
+//    pair of x∘γ (the next GEMM's operand) and, per token, the sum of x² over its
+//    128 columns into ss[token][tile_n];
+//  - the CONSUMER (QKV or SwiGLU epilogue) sums the partials of each token in a
+//    fixed order and scales its accumulators by inv_rms before anything else.
+struct NormOut {
+    const __nv_bfloat16* gamma;  // null: off
+    __nv_bfloat16* hi;
+    __nv_bfloat16* lo;
+    float* ss;  // [M][N / 128]
+};
+struct NormIn {
+    const float* ss;  // null: off; [M][parts]
+    int parts;
+    int K;
+    float eps;
+};
+
 struct GemmParams {
     int M, N, K;
     int kblocks;   // K / 64
@@ -95,6 +115,8 @@ struct GemmParams {
     qtts_qkv_epilogue qkv;
     ConvEpi conv;
     ImplicitX ix;
+    NormOut nout;
+    NormIn nin;
 };
 
 template <int BN, int STAGES, bool SPLIT>
@@ -105,8 +127,9 @@ struct GemmLayout {
     static constexpr int PIPE_BYTES = STAGES * STAGE_BYTES;
     static constexpr int PART_BYTES = BN * 128 * 4;  // fp32 partial, [BN tokens][128 rows]
     static constexpr int BODY = PIPE_BYTES > PART_BYTES ? PIPE_BYTES : PART_BYTES;
-    static constexpr int SCRATCH_BYTES = 4 * 128 * 4;  // epilogue scratch: [0,136) norm sums / RoPE exchange,
-                                                        // [256,512) token metadata
+    static constexpr int SCRATCH_BYTES = 5 * 128 * 4;  // epilogue scratch: [0,136) norm sums / RoPE exchange,
+                                                        // [256,512) token metadata, [0,512) norm-out sums,
+                                                        // [512,640) per-token inv_rms of the norm-in
     static constexpr int BAR_BYTES = 256;
     static constexpr int SMEM = 1024 + BODY + SCRATCH_BYTES + BAR_BYTES;
     static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "stage buffers must keep 1024-B alignment");
@@ -121,17 +144,23 @@ __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x));
 // `row` of the tile for tokens group, group + NT/128, ...
 template <int BN, int NT>
 __device__ void gemm_epilogue(const GemmParams& p, float* R, int m0, int per, int tile_n, int tile_m,
-                              float* scratch) {
+                              float* scratch, const float* pre_old = nullptr) {
     constexpr int NG = NT / 128;
     const int t = threadIdx.x & 127;  // row within the 128-row weight tile
     const int grp = threadIdx.x >> 7;
     const int n_g = tile_n * 128 + t;
+    if (p.nin.ss) {  // folded RMSNorm of the operand: scale each token's row by its inv_rms
+        const float* inv = scratch + 512;
+        for (int e = threadIdx.x; e < per * 128; e += NT) R[(m0 + (e >> 7)) * 128 + (e & 127)] *= inv[e >> 7];
+        __syncthreads();
+    }
     switch (p.epilogue) {
         case QTTS_EPI_BF16:
         case QTTS_EPI_F32:
         case QTTS_EPI_RESIDUAL: {
             // tokens in batches of 8 so the residual loads of a batch are in flight together
             const float b = p.bias ? __bfloat162float(p.bias[n_g]) : 0.0f;
+            const float gam = p.nout.gamma ? __bfloat162float(p.nout.gamma[n_g]) : 0.0f;
             constexpr int B = 8;
             for (int i0 = grp; i0 < per; i0 += NG * B) {
                 float v[B];
@@ -148,10 +177,13 @@ __device__ void gemm_epilogue(const GemmParams& p, float* R, int m0, int per, in
                 if (p.epilogue == QTTS_EPI_RESIDUAL) {
                     float old[B];
 #pragma unroll
-                    for (int u = 0; u < B; ++u) old[u] = ok[u] ? reinterpret_cast<const float*>(p.out)[o[u]] : 0.f;
-#pragma unroll
                     for (int u = 0; u < B; ++u)
-                        if (ok[u]) reinterpret_cast<float*>(p.out)[o[u]] = old[u] + v[u];
+                        old[u] = pre_old ? pre_old[u] : (ok[u] ? reinterpret_cast<const float*>(p.out)[o[u]] : 0.f);
+#pragma unroll
+                    for (int u = 0; u < B; ++u) {
+                        v[u] += old[u];
+                        if (ok[u]) reinterpret_cast<float*>(p.out)[o[u]] = v[u];
+                    }
                 } else if (p.epilogue == QTTS_EPI_F32) {
 #pragma unroll
                     for (int u = 0; u < B; ++u)
@@ -160,6 +192,31 @@ __device__ void gemm_epilogue(const GemmParams& p, float* R, int m0, int per, in
 #pragma unroll
                     for (int u = 0; u < B; ++u)
                         if (ok[u]) reinterpret_cast<__nv_bfloat16*>(p.out)[o[u]] = __float2bfloat16(v[u]);
+                }
+                if (p.nout.gamma) {
+                    // the next GEMM's operand x∘γ as a bf16 pair, and each token's sum of
+                    // squares over this tile's 128 columns (warp sums, combined below)
+#pragma unroll
+                    for (int u = 0; u < B; ++u) {
+                        const float xg = v[u] * gam;
+                        const __nv_bfloat16 hi = __float2bfloat16(xg);
+                        if (ok[u]) {
+                            p.nout.hi[o[u]] = hi;
+                            p.nout.lo[o[u]] = __float2bfloat16(xg - __bfloat162float(hi));
+                        }
+                        const float sq = warp_sum(ok[u] ? v[u] * v[u] : 0.f);
+                        const int i = i0 + NG * u;
+                        if ((t & 31) == 0 && i < per) scratch[(t >> 5) * 128 + i] = sq;
+                    }
+                }
+            }
+            if (p.nout.gamma) {
+                __syncthreads();
+                for (int i = threadIdx.x; i < per; i += NT) {
+                    const int m_g = tile_m * BN + m0 + i;
+                    if (m_g < p.M)  // fixed order over the four warps of the 128 columns
+                        p.nout.ss[(size_t)m_g * (p.N >> 7) + tile_n] =
+                            ((scratch[i] + scratch[128 + i]) + scratch[256 + i]) + scratch[384 + i];
                 }
             }
             break;
@@ -503,32 +560,311 @@ __global__ void __launch_bounds__(NT) gemm_tc_kernel(const __grid_constant__ CUt
     // ---------------- split-K reduction across the cluster ----------------
     const int per = BN / p.splits;
     const int m0 = split * per;
+    if (p.splits > 1) cluster_arrive();  // this CTA's partial is in its shared memory
+    // Loads the epilogue needs are issued between arriving at the cluster barrier
+    // and waiting on it, so they overlap the barrier and the reduction: the old
+    // residual (when the token slice is one batch) and the norm-in partial sums.
+    if (p.nin.ss) {
+        for (int i = threadIdx.x; i < per; i += NT) {
+            const int m_g = tile_m * BN + m0 + i;
+            float tot = 0.f;
+            if (m_g < p.M) {
+                const float* q = p.nin.ss + (size_t)m_g * p.nin.parts;
+                for (int j = 0; j < p.nin.parts; ++j) tot += q[j];  // fixed order: deterministic
+            }
+            scratch[512 + i] = rsqrtf(tot / (float)p.nin.K + p.nin.eps);
+        }
+    }
+    float pre_old[8];
+    const bool prefetch = p.epilogue == QTTS_EPI_RESIDUAL && per <= 8 * (NT / 128);
+    if (prefetch) {
+        const int t = threadIdx.x & 127, grp = threadIdx.x >> 7;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = grp + (NT / 128) * u;
+            const int m_g = tile_m * BN + m0 + i;
+            pre_old[u] = (i < per && m_g < p.M)
+                             ? reinterpret_cast<const float*>(p.out)[(size_t)m_g * p.N + tile_n * 128 + t]
+                             : 0.f;
+        }
+    }
     if (p.splits > 1) {
-        cluster_sync();  // every CTA's partial is in its shared memory
-        // this CTA's token slice, as float4 chunks: all splits' loads are issued
-        // before any is consumed, so the remote-shared-memory latency is paid once
+        cluster_wait();  // every CTA's partial is in its shared memory
+        // this CTA's token slice, as float4 chunks: the loads of two chunks from
+        // every split are issued before any is consumed, so the remote-shared-memory
+        // latency is paid once per 16 loads
         const uint32_t base = smem_u32(P + m0 * 128);
-        for (int e = threadIdx.x; e < per * 32; e += NT) {
-            float4 v[8];
+        for (int e = threadIdx.x; e < per * 32; e += 2 * NT) {
+            const int e2 = e + NT;
+            const bool two = e2 < per * 32;
+            float4 v[2][8];
 #pragma unroll
-            for (int r = 0; r < 8; ++r)
-                if (r < p.splits) v[r] = ld_dsmem_f32x4(map_to_rank(base + (uint32_t)e * 16u, (uint32_t)r));
-            float4 acc = v[0];
-#pragma unroll
-            for (int r = 1; r < 8; ++r) {  // fixed order: deterministic
+            for (int r = 0; r < 8; ++r) {
                 if (r < p.splits) {
-                    acc.x += v[r].x;
-                    acc.y += v[r].y;
-                    acc.z += v[r].z;
-                    acc.w += v[r].w;
+                    v[0][r] = ld_dsmem_f32x4(map_to_rank(base + (uint32_t)e * 16u, (uint32_t)r));
+                    if (two) v[1][r] = ld_dsmem_f32x4(map_to_rank(base + (uint32_t)e2 * 16u, (uint32_t)r));
                 }
             }
-            *reinterpret_cast<float4*>(P + m0 * 128 + e * 4) = acc;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                if (h == 1 && !two) break;
+                float4 acc = v[h][0];
+#pragma unroll
+                for (int r = 1; r < 8; ++r) {  // fixed order: deterministic
+                    if (r < p.splits) {
+                        acc.x += v[h][r].x;
+                        acc.y += v[h][r].y;
+                        acc.z += v[h][r].z;
+                        acc.w += v[h][r].w;
+                    }
+                }
+                *reinterpret_cast<float4*>(P + m0 * 128 + (h ? e2 : e) * 4) = acc;
+            }
         }
+        cluster_arrive();  // done reading the peers' shared memory
+        __syncthreads();
+    } else if (p.nin.ss) {
         __syncthreads();
     }
-    gemm_epilogue<BN, NT>(p, P, m0, per, tile_n, tile_m, scratch);
-    if (p.splits > 1) cluster_sync();  // peers finished reading this CTA's shared memory
+    gemm_epilogue<BN, NT>(p, P, m0, per, tile_n, tile_m, scratch, prefetch ? pre_old : nullptr);
+    if (p.splits > 1) cluster_wait();  // no CTA leaves while a peer may still read its shared memory
+}
+
+// ---------------------------------------------------------------------------
+// Persistent form for wide-row convolution GEMMs (conv epilogue, no split-K):
+// one CTA per SM walks the (row tile, weight tile) list.  Warp 0 lane 0 streams
+// weight and activation tiles through a 4-deep ring across tile borders, warp 1
+// lane 0 issues the UMMAs into one of two 128-column TMEM accumulators, and
+// warps 4-11 run the conv epilogue straight from TMEM (TMEM lane = output
+// channel, so a warp's loads and stores of one token are 32 consecutive
+// channels): the epilogue of tile i overlaps the loads and MMAs of tile i + 1.
+// ---------------------------------------------------------------------------
+constexpr int kPersistStages = 4;
+constexpr int kPersistThreads = 384;  // 4 control warps + 8 epilogue warps
+constexpr int kPersistEpiThreads = 256;
+
+struct PersistLayout {
+    static constexpr int A_BYTES = 128 * 64 * 2;
+    static constexpr int B_BYTES = 128 * 64 * 2;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int RING = kPersistStages * STAGE_BYTES;
+    static constexpr int META = 4 * 128 * 4;  // per token: valid flag, rows in the three views
+    static constexpr int BAR_BYTES = 256;
+    static constexpr int SMEM = 1024 + RING + META + BAR_BYTES;
+};
+
+// Named barrier 1 among the epilogue warps; returns whether any of them passed a non-zero flag.
+__device__ __forceinline__ int epi_sync_or(int flag) {
+    int r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.s32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, 1, %2, p;\n\t"
+        "selp.s32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"(flag), "n"(kPersistEpiThreads)
+        : "memory");
+    return r;
+}
+
+__global__ void __launch_bounds__(kPersistThreads, 1)
+    gemm_conv_persist_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+                             const GemmParams p) {
+    using L = PersistLayout;
+    constexpr int BN = 128, S = kPersistStages;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    int* meta = reinterpret_cast<int*>(smem + L::RING);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::RING + L::META);
+    uint64_t* empty = full + S;
+    uint64_t* tfull = empty + S;   // [2] accumulator ready
+    uint64_t* tempty = tfull + 2;  // [2] accumulator read out by the epilogue
+    uint64_t* done = tempty + 2;   // every UMMA of this CTA has completed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0] error, [1] loads issued, [2] loads consumed
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_tiles_n = p.N / 128, n_tiles = n_tiles_n * ((p.M + BN - 1) / BN);
+    const int nkb = p.kblocks;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&tfull[i], 1);
+            mbar_init(&tempty[i], 1);
+        }
+        mbar_init(done, 1);
+        flags[0] = flags[1] = flags[2] = 0;
+        fence_mbar_init();
+        tma_prefetch_desc(&tmW);
+        tma_prefetch_desc(&tmX);
+    }
+    griddep_wait();  // activations and outputs belong to earlier kernels
+    griddep_launch();
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, 2 * BN);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0 && lane == 0) {
+        // ---------------- producer: every k-block of every tile of this CTA ----------------
+        int it = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+            const int tile_m = tile / n_tiles_n, tile_n = tile - tile_m * n_tiles_n;
+            int x_row0 = tile_m * BN;
+            if (p.ix.on) {
+                const int r = x_row0 / p.ix.T;
+                x_row0 = p.ix.row_slot[r] * p.ix.seq_rows + (x_row0 - r * p.ix.T);
+            }
+            for (int kb = 0; kb < nkb; ++kb, ++it) {
+                const int s = it % S;
+                if (it >= S && !mbar_wait(&empty[s], ((uint32_t)(it / S) & 1u) ^ 1u, DEV_ERR_GEMM_PRODUCER)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t* a = smem + s * L::STAGE_BYTES;
+                mbar_arrive_expect_tx(&full[s], L::STAGE_BYTES);
+                tma_load_2d(a, &tmW, &full[s], kb * 64, tile_n * 128);
+                if (p.ix.on) {
+                    const int tap = kb / p.ix.cblocks, cb = kb - tap * p.ix.cblocks;
+                    tma_load_2d(a + L::A_BYTES, &tmX, &full[s], cb * 64, x_row0 + tap * p.ix.dil);
+                } else {
+                    tma_load_2d(a + L::A_BYTES, &tmX, &full[s], kb * 64, x_row0);
+                }
+            }
+        }
+        flags[1] = it;
+        if (!ok) atomicExch(&flags[0], 1);
+    } else if (warp == 1 && lane == 0) {
+        // ---------------- UMMA issuer ----------------
+        const uint32_t idesc = make_idesc_bf16(128, BN);
+        int it = 0, j = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++j) {
+            const int buf = j & 1;
+            if (j >= 2 && !mbar_wait(&tempty[buf], ((uint32_t)(j >> 1) & 1u) ^ 1u, DEV_ERR_GEMM_MMA)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t acc = tmem + (uint32_t)(buf * BN);
+            for (int kb = 0; kb < nkb; ++kb, ++it) {
+                const int s = it % S;
+                if (!mbar_wait(&full[s], (uint32_t)(it / S) & 1u, DEV_ERR_GEMM_MMA)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a = smem_u32(smem + s * L::STAGE_BYTES);
+                const uint64_t da = make_sw128_desc(a);
+                const uint64_t db = make_sw128_desc(a + L::A_BYTES);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    umma_bf16(acc, da + 2 * kk, db + 2 * kk, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                umma_commit(&empty[s]);
+            }
+            umma_commit(&tfull[buf]);  // also after a failed wait, so the epilogue is not left waiting
+        }
+        flags[2] = it;
+        if (!ok) atomicExch(&flags[0], 1);
+        umma_commit(done);
+    } else if (warp >= 4) {
+        // ---------------- epilogue: thread = (TMEM lane = channel, half of the token columns) ----------------
+        const ConvEpi& e = p.conv;
+        const int t = threadIdx.x - 128;        // 0..255
+        const int quarter = warp & 3;           // TMEM lanes 32*quarter .. +31
+        const int half = (warp - 4) >> 2;       // token columns 64*half .. +63
+        int* tok_ok = meta;
+        int* row_res = meta + 128;
+        int* row_o32 = meta + 256;
+        int* row_o16 = meta + 384;
+        const float* res = reinterpret_cast<const float*>(e.res.ptr);
+        float* o32 = reinterpret_cast<float*>(e.out32.ptr);
+        __nv_bfloat16* o16 = reinterpret_cast<__nv_bfloat16*>(e.out16.ptr);
+        int j = 0;
+        for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++j) {
+            const int buf = j & 1;
+            const int tile_m = tile / n_tiles_n, tile_n = tile - tile_m * n_tiles_n;
+            if (t < 128) {  // the token rows of this tile in the three views
+                const int m_g = tile_m * BN + t;
+                const bool okm = m_g < p.M;
+                const int r = okm ? m_g / e.T_rows : 0;
+                const int t0 = okm ? (m_g - r * e.T_rows) * e.phases : 0;
+                const int sl = (okm && e.row_slot) ? e.row_slot[r] : r;
+                tok_ok[t] = okm;
+                row_res[t] = (e.res.by_slot ? sl : r) * e.res.seq_rows + e.res.ctx + t0;
+                row_o32[t] = (e.out32.by_slot ? sl : r) * e.out32.seq_rows + e.out32.ctx + t0;
+                row_o16[t] = (e.out16.by_slot ? sl : r) * e.out16.seq_rows + e.out16.ctx + t0;
+            }
+            const bool got = mbar_wait(&tfull[buf], (uint32_t)(j >> 1) & 1u, DEV_ERR_GEMM_EPILOGUE);
+            tc_fence_after();
+            // uniform decision: every epilogue warp leaves together or none does
+            if (epi_sync_or(!got || flags[0] != 0)) break;
+            const int n_g = tile_n * 128 + quarter * 32 + lane;
+            const bool colok = n_g < e.n_valid;
+            const int ph = colok ? n_g / e.C_o : 0, c = colok ? n_g - ph * e.C_o : 0;
+            const float b = (colok && p.bias) ? __bfloat162float(p.bias[n_g]) : 0.f;
+            const float sc = (colok && e.scale) ? __bfloat162float(e.scale[c]) : 1.f;
+            const float pa = (colok && e.act == ACT_SNAKE) ? e.act_p[c] : 0.f;
+            const float pb = (colok && e.act == ACT_SNAKE) ? e.act_p[e.C_o + c] : 0.f;
+#pragma unroll 1
+            for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 32) {
+                float v[32];
+                tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * BN + c0),
+                          *reinterpret_cast<float(*)[16]>(v));
+                tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * BN + c0 + 16),
+                          *reinterpret_cast<float(*)[16]>(v + 16));
+                if (!colok) continue;
+                if (res) {
+                    float rv[32];
+#pragma unroll
+                    for (int u = 0; u < 32; ++u)
+                        rv[u] = tok_ok[c0 + u] ? res[(size_t)(row_res[c0 + u] + ph) * e.res.ld + c] : 0.f;
+#pragma unroll
+                    for (int u = 0; u < 32; ++u) v[u] = rv[u] + sc * (v[u] + b);
+                } else {
+#pragma unroll
+                    for (int u = 0; u < 32; ++u) v[u] = sc * (v[u] + b);
+                }
+#pragma unroll
+                for (int u = 0; u < 32; ++u) {
+                    const int i = c0 + u;
+                    if (!tok_ok[i]) continue;
+                    float a = v[u];
+                    if (o32) o32[(size_t)(row_o32[i] + ph) * e.out32.ld + c] = a;
+                    if (o16) {
+                        if (e.act == ACT_SNAKE) {
+                            const float sn = __sinf(a * pa);
+                            a = a + sn * sn * pb;
+                        } else if (e.act == ACT_GELU) {
+                            a = 0.5f * a * (1.0f + erff(a * 0.70710678118654752f));
+                        }
+                        o16[(size_t)(row_o16[i] + ph) * e.out16.ld + c] = __float2bfloat16(a);
+                    }
+                }
+            }
+            tc_fence_before();
+            epi_sync_or(0);  // every epilogue thread is done with this accumulator and the token rows
+            if (t == 0) mbar_arrive(&tempty[buf]);
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 32) mbar_wait(done, 0, DEV_ERR_DRAIN);  // no UMMA still writes TMEM
+    if (threadIdx.x == 0 && flags[0]) {
+        // loads issued but never consumed must land before the CTA's shared memory is released
+        for (int i = flags[2]; i < flags[1]; ++i) mbar_wait(&full[i % S], (uint32_t)(i / S) & 1u, DEV_ERR_DRAIN);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem, 2 * BN);
 }
 
 // ---------------------------------------------------------------------------
@@ -560,6 +896,18 @@ inline int make_map_bf16(CUtensorMap* map, const void* ptr, uint64_t rows, uint6
 }
 
 inline int pick_bn(int M) { return M <= 64 ? 64 : 128; }
+
+// Persistent conv GEMMs for wide rows: opt-in (QTTS_GEMM_PERSIST=1).  At the decoder's
+// sizes they measured slower than the two-CTAs-per-SM form (2.43 vs 1.64 ms per
+// 64-stream step): eight epilogue warps per SM issue 4x the memory instructions
+// of the smem-staged float4 epilogue, and a 4-stage ring holds less in flight.
+inline bool gemm_persist_enabled() {
+    static const bool on = [] {
+        const char* v = getenv("QTTS_GEMM_PERSIST");
+        return v && *v == '1';
+    }();
+    return on;
+}
 
 // Tuning knobs read once from the environment (defaults are the measured best):
 // QTTS_GEMM_STAGES (pipeline depth of the hi/lo kernel at BN = 64) and
@@ -691,6 +1039,28 @@ inline int gemm_plan_implicit(GemmPlan* g, const void* H, int total_rows, int cp
     return QTTS_OK;
 }
 
+// Worth it once every SM gets two or more tiles (QTTS_GEMM_PERSIST_MIN_TILES overrides the threshold).
+inline bool gemm_persist_ok(const GemmPlan& g, int M) {
+    static const int min_tiles = env_int("QTTS_GEMM_PERSIST_MIN_TILES", 2 * num_sms());
+    const int tiles = (g.p.N / 128) * ceil_div(M, 128);
+    return !g.split && g.p.epilogue == kEpiConv && tiles >= min_tiles;
+}
+
+inline int launch_gemm_persist(const GemmPlan& g, const GemmParams& p, cudaStream_t st) {
+    using L = PersistLayout;
+    static bool attr = false;
+    if (!attr) {
+        QTTS_CHECK_CUDA(
+            cudaFuncSetAttribute(gemm_conv_persist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM));
+        attr = true;
+    }
+    const int tiles = (p.N / 128) * ceil_div(p.M, 128);
+    const int grid = tiles < num_sms() ? tiles : num_sms();
+    QTTS_CHECK_CUDA(launch_pdl(gemm_conv_persist_kernel, dim3(grid), dim3(kPersistThreads), L::SMEM, st,
+                               dim3(1, 1, 1), g.mw, g.mx128, p));
+    return QTTS_OK;
+}
+
 // Launch on the first M rows of the plan's X buffer(s).
 inline int gemm_run(GemmPlan g, int M, cudaStream_t st, void* out = nullptr) {
     if (M <= 0) return QTTS_OK;
@@ -713,6 +1083,10 @@ inline int gemm_run(GemmPlan g, int M, cudaStream_t st, void* out = nullptr) {
         return launch_gemm_t<128, 3, true>(g.mw, g.mx128, g.mlo128, g.p, st);
     }
     if (bn == 64) return launch_gemm_t<64, 4, false>(g.mw, g.mx64, g.mx64, g.p, st);
+    if (gemm_persist_enabled() && gemm_persist_ok(g, M)) {
+        g.p.splits = 1;
+        return launch_gemm_persist(g, g.p, st);
+    }
     // wide-row (convolution) GEMMs: 3 x 32 KB stages keep two CTAs per SM, so one
     // CTA's epilogue overlaps the other's main loop, and 8 warps share the epilogue
     if (g.p.epilogue == QTTS_EPI_QKV_ROPE) return launch_gemm_t<128, 3, false, 128>(g.mw, g.mx128, g.mx128, g.p, st);

@@ -118,7 +118,11 @@ def bench_code2wav(rows: int, launches: int, seed: int = 0, chunk: int = 1):
     wav = torch.empty(rows, chunk * cfg.samples_per_frame, device=dev)
     s = torch.cuda.Stream()
     with torch.cuda.stream(s):
-        for _ in range(3):
+        dec.step(codes, slots, wav, stream=s, frames=chunk)
+        s.synchronize()
+        first = wav.double()
+        first_sum, first_abs = float(first.sum()), float(first.abs().sum())
+        for _ in range(2):
             dec.step(codes, slots, wav, stream=s, frames=chunk)
         s.synchronize()
         graph = torch.cuda.CUDAGraph()
@@ -138,7 +142,7 @@ def bench_code2wav(rows: int, launches: int, seed: int = 0, chunk: int = 1):
     out = {"kernel": "code2wav step", "rows": rows, "chunk": chunk, "step_us": sec * 1e6,
            "frames_per_s": rows * chunk / sec,
            "kernels_per_step": dec.last_launches, "approx_tflops": flops / sec / 1e12,
-           "wav_absmean": float(wav.abs().mean())}
+           "wav_absmean": float(wav.abs().mean()), "first_call_sum": first_sum, "first_call_abs_sum": first_abs}
     dec.close()
     return out
 

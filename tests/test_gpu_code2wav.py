@@ -135,3 +135,17 @@ def test_code2wav_chunked_matches_reference_fixture():
         s = snr_db(ref.astype(np.float32), got)
         assert s >= SNR_DB, (i, s)
     dec.close()
+
+
+@pytest.mark.skipif(os.environ.get("QTTS_GEMM_PERSIST_MIN_TILES") is not None, reason="already the forced run")
+def test_code2wav_parity_with_persistent_conv_gemm():
+    """The persistent conv GEMM only serves launches with >= 2 tiles per SM, which
+    the parity cases above are too small to reach; rerun them in a child process
+    with the threshold at one tile so every conv GEMM takes the persistent kernel."""
+    import subprocess
+    import sys
+
+    env = dict(os.environ, QTTS_GEMM_PERSIST="1", QTTS_GEMM_PERSIST_MIN_TILES="1")
+    r = subprocess.run([sys.executable, "-m", "pytest", "-x", "-q", "-m", "gpu", "-p", "no:cacheprovider",
+                        os.path.abspath(__file__)], env=env, capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
