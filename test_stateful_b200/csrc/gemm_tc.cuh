@@ -149,7 +149,10 @@ __device__ void gemm_epilogue(const GemmParams& p, float* R, int m0, int per, in
     const int t = threadIdx.x & 127;  // row within the 128-row weight tile
     const int grp = threadIdx.x >> 7;
     const int n_g = tile_n * 128 + t;
-    if (p.nin.ss) {  // folded RMSNorm of the operand: scale each token's row by its inv_rms
+    // folded RMSNorm of the operand: each token's row is scaled by its inv_rms
+    // (scratch[512 + i]); the QKV and SwiGLU epilogues apply it as they read R
+    const bool nin_inline = p.epilogue == QTTS_EPI_SWIGLU || p.epilogue == QTTS_EPI_QKV_ROPE;
+    if (p.nin.ss && !nin_inline) {
         const float* inv = scratch + 512;
         for (int e = threadIdx.x; e < per * 128; e += NT) R[(m0 + (e >> 7)) * 128 + (e & 127)] *= inv[e >> 7];
         __syncthreads();
@@ -196,6 +199,7 @@ __device__ void gemm_epilogue(const GemmParams& p, float* R, int m0, int per, in
                 if (p.nout.gamma) {
                     // the next GEMM's operand x∘γ as a bf16 pair, and each token's sum of
                     // squares over this tile's 128 columns (warp sums, combined below)
+                    float sq[B];
 #pragma unroll
                     for (int u = 0; u < B; ++u) {
                         const float xg = v[u] * gam;
@@ -204,9 +208,18 @@ __device__ void gemm_epilogue(const GemmParams& p, float* R, int m0, int per, in
                             p.nout.hi[o[u]] = hi;
                             p.nout.lo[o[u]] = __float2bfloat16(xg - __bfloat162float(hi));
                         }
-                        const float sq = warp_sum(ok[u] ? v[u] * v[u] : 0.f);
-                        const int i = i0 + NG * u;
-                        if ((t & 31) == 0 && i < per) scratch[(t >> 5) * 128 + i] = sq;
+                        sq[u] = ok[u] ? v[u] * v[u] : 0.f;
+                    }
+#pragma unroll
+                    for (int off = 16; off > 0; off >>= 1)  // the B reductions interleaved
+#pragma unroll
+                        for (int u = 0; u < B; ++u) sq[u] += __shfl_xor_sync(0xffffffffu, sq[u], off);
+                    if ((t & 31) == 0) {
+#pragma unroll
+                        for (int u = 0; u < B; ++u) {
+                            const int i = i0 + NG * u;
+                            if (i < per) scratch[(t >> 5) * 128 + i] = sq[u];
+                        }
                     }
                 }
             }
@@ -222,15 +235,29 @@ __device__ void gemm_epilogue(const GemmParams& p, float* R, int m0, int per, in
             break;
         }
         case QTTS_EPI_SWIGLU: {
-            if (t < 64) {
-                const int half_n = p.N >> 1;
-                for (int i = grp; i < per; i += NG) {
+            // thread = (pair column c of the tile's 64 gate/up pairs, token lane); batches of
+            // 8 tokens with every load of a batch issued before the math
+            constexpr int TL = NT / 64, B = 8;
+            const int c = threadIdx.x & 63, tl = threadIdx.x >> 6;
+            const int half_n = p.N >> 1;
+            const float* inv = scratch + 512;
+            for (int i0 = tl; i0 < per; i0 += TL * B) {
+                float g[B], u[B];
+#pragma unroll
+                for (int k = 0; k < B; ++k) {
+                    const int i = i0 + TL * k;
+                    const bool ok = i < per;
+                    const float sc = (ok && p.nin.ss) ? inv[i] : 1.f;
+                    g[k] = ok ? R[(m0 + i) * 128 + c] * sc : 0.f;
+                    u[k] = ok ? R[(m0 + i) * 128 + 64 + c] * sc : 0.f;
+                }
+#pragma unroll
+                for (int k = 0; k < B; ++k) {
+                    const int i = i0 + TL * k;
                     const int m_g = tile_m * BN + m0 + i;
-                    if (m_g >= p.M) break;
-                    const float g = R[(m0 + i) * 128 + t];
-                    const float u = R[(m0 + i) * 128 + 64 + t];
-                    const float a = silu(g) * u;
-                    const size_t o = (size_t)m_g * half_n + tile_n * 64 + t;
+                    if (i >= per || m_g >= p.M) continue;
+                    const float a = __fdividef(g[k], 1.0f + __expf(-g[k])) * u[k];
+                    const size_t o = (size_t)m_g * half_n + tile_n * 64 + c;
                     const __nv_bfloat16 hi = __float2bfloat16(a);
                     reinterpret_cast<__nv_bfloat16*>(p.out)[o] = hi;
                     if (p.out_lo)
@@ -246,7 +273,7 @@ __device__ void gemm_epilogue(const GemmParams& p, float* R, int m0, int per, in
                 const int q_rows = e.num_heads * D;
                 const int k_rows = e.kv_heads * D;
                 const int d = n_g % D;
-                const int warp = t >> 5;
+                const int warp = t >> 5, lane = t & 31;
                 const int region = n_g < q_rows ? 0 : (n_g < q_rows + k_rows ? 1 : 2);
                 const __nv_bfloat16* nw = region == 0 ? (const __nv_bfloat16*)e.q_norm_w
                                                       : (const __nv_bfloat16*)e.k_norm_w;
@@ -254,57 +281,73 @@ __device__ void gemm_epilogue(const GemmParams& p, float* R, int m0, int per, in
                 const int half = D >> 1;
                 const int dd = d < half ? d : d - half;
                 const int partner_t = d < half ? t + half : t - half;
-                // token metadata first (positions and slots of all tokens in flight together)
-                int* tok_pos = reinterpret_cast<int*>(scratch) + 256;
-                int* tok_slot = tok_pos + 128;
-                for (int i = t; i < per; i += 128) {
-                    const int m_g = tile_m * BN + m0 + i;
-                    int pos = m_g < p.M ? e.row_pos[m_g] : 0;
-                    tok_pos[i] = pos < 0 ? 0 : (pos >= e.max_pos ? e.max_pos - 1 : pos);  // table bounds
-                    tok_slot[i] = m_g < p.M ? e.slot_mapping[m_g] : -1;
-                }
-                __syncthreads();
-                for (int i = 0; i < per; ++i) {
-                    const int m_g = tile_m * BN + m0 + i;
-                    if (m_g >= p.M) break;  // uniform across the CTA
-                    float c = 1.f, sn = 0.f;
-                    if (region < 2) {  // issued before the reductions below
-                        c = e.rope_cos[(size_t)tok_pos[i] * half + dd];
-                        sn = e.rope_sin[(size_t)tok_pos[i] * half + dd];
+                const int wpd = D >> 5, w0 = (warp / wpd) * wpd;  // the warps of this thread's head
+                const float* inv = scratch + 512;
+                float* red = scratch;  // [4 warps][8 tokens] per-head sums of squares
+                // per-token position and KV row base, written by the kernel before the reduction
+                const int* tok_pos = reinterpret_cast<const int*>(scratch) + 256;
+                const int* tok_kv = tok_pos + 128;
+                const int kv_col = region == 0 ? 0
+                                                : (((region - 1) * e.kv_heads) + (n_g - q_rows - (region == 2 ? k_rows : 0)) / D) *
+                                                      e.block_size;
+                const float inv_d = 1.0f / (float)D;  // D is a power of two: exact
+                // 8 tokens at a time: RoPE table loads, head norms and stores of the 8 overlap;
+                // two barriers per 8 tokens (norm sums, RoPE partner exchange through R)
+                for (int c0 = 0; c0 < per; c0 += 8) {
+                    float v[8], cs[8], sn[8], sq[8];
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        const int i = c0 + k;
+                        const bool ok = i < per && tile_m * BN + m0 + i < p.M;
+                        cs[k] = 1.f;
+                        sn[k] = 0.f;
+                        if (region < 2 && ok) {
+                            cs[k] = e.rope_cos[(size_t)tok_pos[i] * half + dd];
+                            sn[k] = e.rope_sin[(size_t)tok_pos[i] * half + dd];
+                        }
+                        v[k] = ok ? R[(m0 + i) * 128 + t] * (p.nin.ss ? inv[i] : 1.f) : 0.f;
+                        sq[k] = v[k] * v[k];
                     }
-                    float v = R[(m0 + i) * 128 + t];
-                    // per-head sum of squares (a head spans D/32 warps of this tile)
-                    float ss = warp_sum(v * v);
-                    if ((t & 31) == 0) scratch[warp] = ss;
+#pragma unroll
+                    for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) sq[k] += __shfl_xor_sync(0xffffffffu, sq[k], off);
+                    if (lane == 0) {
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) red[warp * 8 + k] = sq[k];
+                    }
                     __syncthreads();
                     if (region < 2) {
-                        const int wpd = D >> 5;
-                        const int w0 = (warp / wpd) * wpd;
-                        float tot = 0.f;
-                        for (int w = 0; w < wpd; ++w) tot += scratch[w0 + w];
-                        v = v * rsqrtf(tot / (float)D + e.rms_eps) * wn;
-                    }
-                    scratch[8 + t] = v;
-                    __syncthreads();
-                    if (region < 2) {
-                        const float partner = scratch[8 + partner_t];
-                        v = d < half ? v * c - partner * sn : v * c + partner * sn;
-                    }
-                    if (region == 0) {
-                        reinterpret_cast<float*>(p.out)[(size_t)m_g * q_rows + n_g] = v;  // q stays fp32
-                    } else {
-                        const int slot = tok_slot[i];
-                        if (slot >= 0) {
-                            const int blk = slot / e.block_size, off = slot % e.block_size;
-                            const int g = (n_g - q_rows - (region == 2 ? k_rows : 0)) / D;
-                            const size_t idx =
-                                ((((size_t)blk * e.num_layers + e.layer) * 2 + (region - 1)) * e.kv_heads + g) *
-                                    e.block_size +
-                                off;
-                            reinterpret_cast<kv_t*>(e.kv_pool)[idx * D + d] = to_kv(v);
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) {
+                            float tot = 0.f;
+#pragma unroll
+                            for (int w = 0; w < 4; ++w)  // head_dim <= 128: at most 4 warps per head
+                                if (w < wpd) tot += red[(w0 + w) * 8 + k];
+                            v[k] = v[k] * rsqrtf(tot * inv_d + e.rms_eps) * wn;
                         }
                     }
+                    // each thread rewrites only its own elements of R, read by its RoPE partner
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)
+                        if (c0 + k < per) R[(m0 + c0 + k) * 128 + t] = v[k];
                     __syncthreads();
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        const int i = c0 + k;
+                        const int m_g = tile_m * BN + m0 + i;
+                        if (i >= per || m_g >= p.M) continue;
+                        float val = v[k];
+                        if (region < 2) {
+                            const float partner = R[(m0 + i) * 128 + partner_t];
+                            val = d < half ? val * cs[k] - partner * sn[k] : val * cs[k] + partner * sn[k];
+                        }
+                        if (region == 0) {
+                            reinterpret_cast<float*>(p.out)[(size_t)m_g * q_rows + n_g] = val;  // q stays fp32
+                        } else if (tok_kv[i] >= 0) {
+                            reinterpret_cast<kv_t*>(e.kv_pool)[(size_t)(tok_kv[i] + kv_col) * D + d] = to_kv(val);
+                        }
+                    }
                 }
             }
             break;
@@ -575,6 +618,22 @@ __global__ void __launch_bounds__(NT) gemm_tc_kernel(const __grid_constant__ CUt
             scratch[512 + i] = rsqrtf(tot / (float)p.nin.K + p.nin.eps);
         }
     }
+    if (p.epilogue == QTTS_EPI_QKV_ROPE) {
+        // token metadata of the QKV epilogue: clamped RoPE position, and the KV-pool row of
+        // (block, layer, k, head 0, offset) for the token's slot (-1: not stored)
+        const qtts_qkv_epilogue& e = p.qkv;
+        int* tok_pos = reinterpret_cast<int*>(scratch) + 256;
+        int* tok_kv = tok_pos + 128;
+        for (int i = threadIdx.x; i < per; i += NT) {
+            const int m_g = tile_m * BN + m0 + i;
+            const int pos = m_g < p.M ? e.row_pos[m_g] : 0;
+            const int slot = m_g < p.M ? e.slot_mapping[m_g] : -1;
+            tok_pos[i] = pos < 0 ? 0 : (pos >= e.max_pos ? e.max_pos - 1 : pos);  // table bounds
+            tok_kv[i] = slot < 0 ? -1
+                                 : ((slot / e.block_size) * e.num_layers + e.layer) * 2 * e.kv_heads * e.block_size +
+                                       slot % e.block_size;
+        }
+    }
     float pre_old[8];
     const bool prefetch = p.epilogue == QTTS_EPI_RESIDUAL && per <= 8 * (NT / 128);
     if (prefetch) {
@@ -623,7 +682,7 @@ __global__ void __launch_bounds__(NT) gemm_tc_kernel(const __grid_constant__ CUt
         }
         cluster_arrive();  // done reading the peers' shared memory
         __syncthreads();
-    } else if (p.nin.ss) {
+    } else if (p.nin.ss || p.epilogue == QTTS_EPI_QKV_ROPE) {
         __syncthreads();
     }
     gemm_epilogue<BN, NT>(p, P, m0, per, tile_n, tile_m, scratch, prefetch ? pre_old : nullptr);
