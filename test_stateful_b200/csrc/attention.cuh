@@ -42,6 +42,8 @@ struct AttnParams {
     __nv_bfloat16* out;
     __nv_bfloat16* out_lo;  // bf16 residual of the output (hi/lo GEMM operand), or NULL
     int R;
+    int static_meta;  // row_slot / row_ctx / block_table are not written by earlier kernels of the
+                      // stream, so a kernel may read them before waiting on its predecessor
 };
 
 // Ring depth per warp (QTTS_ATTN_STAGES, default below): 3 stages x 8 KB x 4
@@ -669,11 +671,21 @@ __global__ void __launch_bounds__(128) short_attn_kernel(const AttnParams p) {
     __shared__ float qs[4][D];
     const int r = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int h = blockIdx.y * 4 + warp;
+    const bool head_ok = h < p.num_heads;
+    // row metadata (static for the code predictor's stages: read before the wait)
+    int n = 0, blk = 0;
+    if (p.static_meta && head_ok) {
+        n = min(p.row_ctx[r], 16);
+        blk = p.block_table[(size_t)p.row_slot[r] * p.mbps];
+    }
     griddep_wait();
     griddep_launch();
-    if (h >= p.num_heads) return;
+    if (!head_ok) return;
+    if (!p.static_meta) {
+        n = min(p.row_ctx[r], 16);
+        blk = p.block_table[(size_t)p.row_slot[r] * p.mbps];
+    }
     const int g = h / (p.num_heads / p.kv_heads);
-    const int n = min(p.row_ctx[r], 16);
     const size_t orow = ((size_t)r * p.num_heads + h) * D;
     if (n <= 0) {
         for (int d = lane; d < D; d += 32) {
@@ -682,31 +694,41 @@ __global__ void __launch_bounds__(128) short_attn_kernel(const AttnParams p) {
         }
         return;
     }
-    int blk = p.block_table[(size_t)p.row_slot[r] * p.mbps];
     if (blk < 0 || blk >= p.num_blocks) {
         record_error(DEV_ERR_ATTN_WAIT);
         blk = 0;
     }
-    for (int d = lane; d < D; d += 32) qs[warp][d] = p.q[orow + d] * p.scale_log2;
-    __syncwarp();
     const size_t head = (size_t)16 * D;
     const kv_t* K = p.kv + ((((size_t)blk * p.num_layers + p.layer) * 2 + 0) * p.kv_heads + g) * head;
     const kv_t* V = K + (size_t)p.kv_heads * head;
+    // every load of the kernel in flight together: this lane's key row, q, and the V
+    // elements this lane accumulates for all 16 keys
+    uint4 kraw[D / 8];
+    if (lane < n) {
+#pragma unroll
+        for (int j = 0; j < D / 8; ++j) kraw[j] = *reinterpret_cast<const uint4*>(K + (size_t)lane * D + j * 8);
+    }
+    float vv[16][PER];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+#pragma unroll
+        for (int e = 0; e < PER; ++e) vv[k][e] = k < n ? __half2float(V[(size_t)k * D + lane * PER + e]) : 0.f;
+    }
+    for (int d = lane; d < D; d += 32) qs[warp][d] = p.q[orow + d] * p.scale_log2;
+    __syncwarp();
     float sc = -INFINITY;
     if (lane < n) {
-        const kv_t* kr = K + (size_t)lane * D;
-        float acc = 0.f;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};  // independent chains
 #pragma unroll
-        for (int d = 0; d < D; d += 8) {
-            const uint4 u = *reinterpret_cast<const uint4*>(kr + d);
-            const __half2* hp = reinterpret_cast<const __half2*>(&u);
+        for (int j = 0; j < D / 8; ++j) {
+            const __half2* hp = reinterpret_cast<const __half2*>(&kraw[j]);
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 const float2 f = __half22float2(hp[e]);
-                acc += f.x * qs[warp][d + 2 * e] + f.y * qs[warp][d + 2 * e + 1];
+                acc[e] += f.x * qs[warp][j * 8 + 2 * e] + f.y * qs[warp][j * 8 + 2 * e + 1];
             }
         }
-        sc = acc;
+        sc = (acc[0] + acc[1]) + (acc[2] + acc[3]);
     }
     const float mx = warp_max(sc);
     const float pr = lane < n ? exp2f(sc - mx) : 0.f;
@@ -714,11 +736,11 @@ __global__ void __launch_bounds__(128) short_attn_kernel(const AttnParams p) {
     float o[PER];
 #pragma unroll
     for (int e = 0; e < PER; ++e) o[e] = 0.f;
-    for (int k = 0; k < n; ++k) {
-        const float pk = __shfl_sync(0xffffffffu, pr, k);
-        const kv_t* vr = V + (size_t)k * D + lane * PER;
 #pragma unroll
-        for (int e = 0; e < PER; ++e) o[e] += pk * __half2float(vr[e]);
+    for (int k = 0; k < 16; ++k) {
+        const float pk = __shfl_sync(0xffffffffu, pr, k);  // 0 beyond n
+#pragma unroll
+        for (int e = 0; e < PER; ++e) o[e] += pk * vv[k][e];
     }
 #pragma unroll
     for (int e = 0; e < PER; ++e) {

@@ -403,6 +403,7 @@ inline int engine_step_impl(qtts_engine* e, const qtts_step_io& io, cudaStream_t
     cap.ws_ml = e->cws_ml;
     cap.out = e->cattn;
     cap.out_lo = e->cattn_lo;
+    cap.static_meta = 1;  // cp_meta and cp_table are written once, at build time
 
     // the tokens the next stage consumes: sampled, or forced by a parity test
     const int64_t* codes_in = io.force_codes ? io.force_codes : io.full_codec_out;
