@@ -273,6 +273,12 @@ __device__ __forceinline__ float4 ld_dsmem_f32x4(uint32_t addr) {
     return v;
 }
 
+// Store to (possibly another CTA's) shared memory in the cluster.
+__device__ __forceinline__ void st_dsmem_f32x4(uint32_t addr, float a, float b, float c, float d) {
+    asm volatile("st.shared::cluster.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+                 : "memory");
+}
+
 // ----------------------------------------------------------------------------
 // numerics
 // ----------------------------------------------------------------------------

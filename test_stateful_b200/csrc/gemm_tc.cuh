@@ -119,14 +119,18 @@ struct GemmParams {
     NormIn nin;
 };
 
-template <int BN, int STAGES, bool SPLIT>
+template <int BN, int STAGES, bool SPLIT, bool PUSH = false>
 struct GemmLayout {
     static constexpr int A_BYTES = 128 * 64 * 2;  // weight tile 128 rows x 64 k
     static constexpr int B_BYTES = BN * 64 * 2;   // token tile BN rows x 64 k (hi, then lo when SPLIT)
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES * (SPLIT ? 2 : 1);
     static constexpr int PIPE_BYTES = STAGES * STAGE_BYTES;
     static constexpr int PART_BYTES = BN * 128 * 4;  // fp32 partial, [BN tokens][128 rows]
-    static constexpr int BODY = PIPE_BYTES > PART_BYTES ? PIPE_BYTES : PART_BYTES;
+    static constexpr int RING = PIPE_BYTES > PART_BYTES ? PIPE_BYTES : PART_BYTES;
+    // push reduction: the partials the cluster's CTAs send this one, [split][128 rows][BN/splits tokens];
+    // not aliased with the ring, which peers may still be reading from TMA when they push
+    static constexpr int RECV_BYTES = PUSH ? BN * 128 * 4 : 0;
+    static constexpr int BODY = RING + RECV_BYTES;
     static constexpr int SCRATCH_BYTES = 5 * 128 * 4;  // epilogue scratch: [0,136) norm sums / RoPE exchange,
                                                         // [256,512) token metadata, [0,512) norm-out sums,
                                                         // [512,640) per-token inv_rms of the norm-in
@@ -456,13 +460,14 @@ __device__ void gemm_epilogue(const GemmParams& p, float* R, int m0, int per, in
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-template <int BN, int STAGES, bool SPLIT, int NT>
+template <int BN, int STAGES, bool SPLIT, int NT, bool PUSH = false>
 __global__ void __launch_bounds__(NT) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW,
                                                      const __grid_constant__ CUtensorMap tmX,
                                                      const __grid_constant__ CUtensorMap tmXlo,
                                                      const GemmParams p) {
     static_assert(NT == 128 || NT == 256, "128 or 256 threads");
-    using L = GemmLayout<BN, STAGES, SPLIT>;
+    static_assert(!PUSH || (NT == 128 && BN == 64), "push reduction: BN 64, 128 threads");
+    using L = GemmLayout<BN, STAGES, SPLIT, PUSH>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     float* scratch = reinterpret_cast<float*>(smem + L::BODY);
@@ -582,18 +587,36 @@ __global__ void __launch_bounds__(NT) gemm_tc_kernel(const __grid_constant__ CUt
     __syncthreads();
     float* P = reinterpret_cast<float*>(smem);
     const bool good = ok && flags[0] == 0;
+    const int per = BN / p.splits;
+    const int m0 = split * per;
+    const bool push = PUSH && p.splits > 1;
     {
         // warp w reads TMEM lane quarter w % 4; with 256 threads warps w and w + 4
         // take one half of the columns each
         const int quarter = warp & 3, half = warp >> 2;
         constexpr int COLS = BN / (NT / 128);
         const int row = quarter * 32 + lane;
+        // push: each 4-token group goes straight from registers to the receive buffer of
+        // the CTA that owns those tokens, at [this split][row][token in its slice]
+        const uint32_t recv_s = smem_u32(smem + L::RING) + (uint32_t)((split * 128 + row) * per) * 4u;
 #pragma unroll 1
         for (int c = half * COLS; c < (half + 1) * COLS; c += 16) {
             float v[16];
             tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c, v);
+            if (push) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) P[(c + j) * 128 + row] = good ? v[j] : 0.0f;
+                for (int q = 0; q < 4; ++q) {
+                    const int tok = c + 4 * q, dst = tok / per, i0 = tok - dst * per;
+                    const uint32_t a = map_to_rank(recv_s + (uint32_t)i0 * 4u, (uint32_t)dst);
+                    if (good)
+                        st_dsmem_f32x4(a, v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                    else
+                        st_dsmem_f32x4(a, 0.f, 0.f, 0.f, 0.f);
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) P[(c + j) * 128 + row] = good ? v[j] : 0.0f;
+            }
         }
     }
     tc_fence_before();
@@ -601,9 +624,9 @@ __global__ void __launch_bounds__(NT) gemm_tc_kernel(const __grid_constant__ CUt
     if (warp == 2) tmem_dealloc(tmem, BN);
 
     // ---------------- split-K reduction across the cluster ----------------
-    const int per = BN / p.splits;
-    const int m0 = split * per;
-    if (p.splits > 1) cluster_arrive();  // this CTA's partial is in its shared memory
+    // pull: arrive = this CTA's partial is in its shared memory; push: arrive = this
+    // CTA's stores into its peers' receive buffers are done
+    if (p.splits > 1) cluster_arrive();
     // Loads the epilogue needs are issued between arriving at the cluster barrier
     // and waiting on it, so they overlap the barrier and the reduction: the old
     // residual (when the token slice is one batch) and the norm-in partial sums.
@@ -647,7 +670,26 @@ __global__ void __launch_bounds__(NT) gemm_tc_kernel(const __grid_constant__ CUt
                              : 0.f;
         }
     }
-    if (p.splits > 1) {
+    if (push) {
+        cluster_wait();  // every peer's partial of this CTA's token slice has landed here
+        const float* recv = reinterpret_cast<const float*>(smem + L::RING);
+        const int t = threadIdx.x;  // weight row
+        for (int i0 = 0; i0 < per; i0 += 4) {
+            float4 acc = *reinterpret_cast<const float4*>(recv + (size_t)t * per + i0);
+            for (int r = 1; r < p.splits; ++r) {  // fixed order: deterministic
+                const float4 b = *reinterpret_cast<const float4*>(recv + ((size_t)r * 128 + t) * per + i0);
+                acc.x += b.x;
+                acc.y += b.y;
+                acc.z += b.z;
+                acc.w += b.w;
+            }
+            P[(m0 + i0) * 128 + t] = acc.x;
+            P[(m0 + i0 + 1) * 128 + t] = acc.y;
+            P[(m0 + i0 + 2) * 128 + t] = acc.z;
+            P[(m0 + i0 + 3) * 128 + t] = acc.w;
+        }
+        __syncthreads();
+    } else if (p.splits > 1) {
         cluster_wait();  // every CTA's partial is in its shared memory
         // this CTA's token slice, as float4 chunks: the loads of two chunks from
         // every split are issued before any is consumed, so the remote-shared-memory
@@ -686,7 +728,7 @@ __global__ void __launch_bounds__(NT) gemm_tc_kernel(const __grid_constant__ CUt
         __syncthreads();
     }
     gemm_epilogue<BN, NT>(p, P, m0, per, tile_n, tile_m, scratch, prefetch ? pre_old : nullptr);
-    if (p.splits > 1) cluster_wait();  // no CTA leaves while a peer may still read its shared memory
+    if (p.splits > 1 && !push) cluster_wait();  // no CTA leaves while a peer may still read its shared memory
 }
 
 // ---------------------------------------------------------------------------
@@ -968,6 +1010,14 @@ inline bool gemm_persist_enabled() {
     return on;
 }
 
+inline bool gemm_push_enabled() {
+    static const bool on = [] {
+        const char* v = getenv("QTTS_GEMM_PUSH");
+        return v && *v == '1';
+    }();
+    return on;
+}
+
 // Tuning knobs read once from the environment (defaults are the measured best):
 // QTTS_GEMM_STAGES (pipeline depth of the hi/lo kernel at BN = 64) and
 // QTTS_GEMM_MAX_SPLITS (largest split-K cluster), QTTS_GEMM_CTAS_PER_SM (split-K target).
@@ -999,11 +1049,11 @@ inline int pick_splits(int N, int M, int K, int BN) {
     return s;
 }
 
-template <int BN, int STAGES, bool SPLIT, int NT = 128>
+template <int BN, int STAGES, bool SPLIT, int NT = 128, bool PUSH = false>
 inline int launch_gemm_t(const CUtensorMap& mw, const CUtensorMap& mx, const CUtensorMap& mxlo, const GemmParams& p,
                          cudaStream_t st) {
-    using L = GemmLayout<BN, STAGES, SPLIT>;
-    auto kern = gemm_tc_kernel<BN, STAGES, SPLIT, NT>;
+    using L = GemmLayout<BN, STAGES, SPLIT, PUSH>;
+    auto kern = gemm_tc_kernel<BN, STAGES, SPLIT, NT, PUSH>;
     static bool attr_done = false;
     if (!attr_done) {
         QTTS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM));
@@ -1131,6 +1181,18 @@ inline int gemm_run(GemmPlan g, int M, cudaStream_t st, void* out = nullptr) {
     g.p.M = M;
     g.p.splits = pick_splits(g.p.N, M, g.p.K, bn);
     if (out) g.p.out = out;
+    // Opt-in (QTTS_GEMM_PUSH=1): split-K launches that fit one CTA per SM reduce by
+    // pushing partials from registers into the owner's receive buffer (5-stage ring +
+    // 32 KB receive buffer).  Measured slower in the decode step (9.28 vs 7.65 ms): the
+    // 196 KB footprint keeps the next kernel's CTAs off the SM until this one exits, so
+    // programmatic dependent launch no longer overlaps their weight prefetch, and the
+    // remote stores cost about what the pull's remote loads do.
+    const bool push = bn == 64 && g.p.splits > 1 && gemm_push_enabled() &&
+                      (g.p.N / 128) * g.p.splits * ceil_div(M, bn) <= num_sms();
+    if (push) {
+        if (g.split) return launch_gemm_t<64, 5, true, 128, true>(g.mw, g.mx64, g.mlo64, g.p, st);
+        return launch_gemm_t<64, 5, false, 128, true>(g.mw, g.mx64, g.mx64, g.p, st);
+    }
     if (g.split) {
         if (bn == 64) {
             switch (gemm_stages()) {

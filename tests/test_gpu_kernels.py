@@ -3,6 +3,7 @@ CPU oracle (integer/index work: bit-exact) or an fp32 torch statement of the
 same op (floating point: tolerance in each test)."""
 
 import ctypes as C
+import os
 
 import numpy as np
 import pytest
@@ -300,3 +301,16 @@ def test_rmsnorm_and_codec_sum():
     ref = M.codec_sum(M.stacked_codec_table(W, 15), codes.cpu())
     torch.testing.assert_close(cs.cpu(), ref, rtol=1e-4, atol=1e-5)
     torch.testing.assert_close(nx.cpu(), ref + text.cpu(), rtol=1e-6, atol=1e-7)  # next input stays fp32
+
+
+@pytest.mark.skipif(os.environ.get("QTTS_GEMM_PUSH") is not None, reason="already the forced run")
+def test_gemm_push_reduction_variant():
+    """The push form of the split-K reduction is opt-in (QTTS_GEMM_PUSH=1, read once per
+    process); rerun the GEMM tests in a child process with it on."""
+    import subprocess
+    import sys
+
+    env = dict(os.environ, QTTS_GEMM_PUSH="1")
+    r = subprocess.run([sys.executable, "-m", "pytest", "-x", "-q", "-m", "gpu", "-p", "no:cacheprovider", "-k", "gemm",
+                        os.path.abspath(__file__)], env=env, capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
