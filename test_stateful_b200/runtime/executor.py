@@ -140,11 +140,20 @@ class B200Executor:
         self._enable_c2w = enable_code2wav
         self._c2w_weights = c2w_weights
         self._c2w: Optional[DeviceCode2Wav] = None
-        self._stream = torch.cuda.Stream(device=self._device)
+        # Two streams: talker + code predictor (latency-bound kernel chain, high priority)
+        # and code2wav (low priority).  Code2wav of step t only needs step t's codes, so it
+        # runs while step t + 1's talker and code predictor run.
+        self._stream = torch.cuda.Stream(device=self._device, priority=-1)
+        self._c2w_stream = torch.cuda.Stream(device=self._device, priority=0)
         self._model: Optional[DeviceModel] = None
         self._kv_pool: Optional[PagedKVCachePool] = None
         self._graphs: Dict[int, Any] = {}
         self._embedding_weights = None
+        # decode steps alternate between two sets of step buffers (parity); the events of
+        # the last step of each parity guard their reuse two steps later
+        self._parity = 0
+        self._done_a: List[Any] = [None, None]
+        self._done_b: List[Any] = [None, None]
 
     # -- properties the engine loop reads ---------------------------------
     @property
@@ -236,17 +245,23 @@ class B200Executor:
         self.noise_step = torch.zeros(S, dtype=i32, device=dev)
         self.zero_gumbel = torch.zeros(B, t.logits_topk, dtype=f32, device=dev)
         self.zero_cp_gumbel = torch.zeros(B, c.num_stages, t.logits_topk, dtype=f32, device=dev)
-        self.slots_dev = torch.zeros(B, dtype=i32, device=dev)
-        self.slots_host = torch.zeros(B, dtype=i32).pin_memory()
+        # step buffers by parity: [0], [1] alternate between decode steps, [2] serves prefill
+        self.slots_buf = torch.zeros(3, B, dtype=i32, device=dev)
+        self.slots_host_buf = torch.zeros(3, B, dtype=i32).pin_memory()
+        self.slots_dev = self.slots_buf[2]
+        self.slots_host = self.slots_host_buf[2]
         self.hidden = torch.zeros(B, t.hidden_size, dtype=torch.bfloat16, device=dev)
         self.logits = torch.zeros(B, t.codec_vocab_size, dtype=f32, device=dev)
-        self.codes = torch.zeros(B, 1 + c.num_stages, dtype=i64, device=dev)
-        self.codes_host = torch.zeros(B, 1 + c.num_stages, dtype=i64).pin_memory()
+        self.codes_buf = torch.zeros(3, B, 1 + c.num_stages, dtype=i64, device=dev)
+        self.codes_host_buf = torch.zeros(3, B, 1 + c.num_stages, dtype=i64).pin_memory()
+        self.codes = self.codes_buf[2]  # the last prefill's frame
         self.status = torch.zeros(1, dtype=i32, device=dev)
-        self.status_host = torch.zeros(1, dtype=i32).pin_memory()
+        self.status_host_buf = torch.zeros(3, 1, dtype=i32).pin_memory()
+        self.status_host = self.status_host_buf[2]
         spf = self._config.c2w.samples_per_frame
         self.wav = torch.zeros(B, spf, dtype=f32, device=dev) if self._enable_c2w else None
-        self.wav_host = torch.zeros(B, spf, dtype=f32).pin_memory() if self._enable_c2w else None
+        self.wav_host_buf = torch.zeros(3, B, spf, dtype=f32).pin_memory() if self._enable_c2w else None
+        self.wav_host = self.wav_host_buf[2] if self._enable_c2w else None
 
     def _reset_slot_state(self, slot_id: int) -> None:
         self.counts[slot_id].zero_()
@@ -262,9 +277,9 @@ class B200Executor:
         self.temperature[sid] = self._temperature if self._do_sample else 1.0
         self.penalty[sid] = self._repetition_penalty
 
-    def _io(self, n_rows: int, n_new: int, x_in: torch.Tensor, sample: int) -> _lib.StepIO:
+    def _io(self, n_rows: int, n_new: int, x_in: torch.Tensor, sample: int, parity: int = 2) -> _lib.StepIO:
         io = _lib.StepIO()
-        io.slots = self.slots_dev.data_ptr()
+        io.slots = self.slots_buf[parity].data_ptr()
         io.n_rows = n_rows
         io.n_new = n_new
         io.slot_indexed = 1
@@ -283,7 +298,7 @@ class B200Executor:
         io.text_add = self.text_add.data_ptr()
         io.hidden_out = self.hidden.data_ptr()
         io.logits_out = self.logits.data_ptr()
-        io.full_codec_out = self.codes.data_ptr()
+        io.full_codec_out = self.codes_buf[parity].data_ptr()
         io.codec_sum_out = self.codec_sum.data_ptr()
         io.next_x_out = self.next_x.data_ptr()
         io.status = self.status.data_ptr()
@@ -319,11 +334,13 @@ class B200Executor:
         (the fused prefill runs code2wav on it: executor.py:859-877)."""
         if self._c2w is None:
             return None
-        with torch.cuda.stream(self._stream):
-            self._c2w.reset(self.slots_dev[:1], stream=self._stream)
-            self._c2w.step(self.codes, self.slots_dev, self.wav, n=1, stream=self._stream)
+        cs = self._c2w_stream  # every code2wav call runs on this stream, in order
+        cs.wait_stream(self._stream)
+        with torch.cuda.stream(cs):
+            self._c2w.reset(self.slots_dev[:1], stream=cs)
+            self._c2w.step(self.codes, self.slots_dev, self.wav, n=1, stream=cs)
             self.wav_host[:1].copy_(self.wav[:1], non_blocking=True)
-        self._stream.synchronize()
+        cs.synchronize()
         return self.wav_host[0].numpy().tobytes()
 
     def prefill(self, slot: SlotState, prefill_embeds: torch.Tensor):
@@ -361,19 +378,87 @@ class B200Executor:
         return audio, bool(int(codes[0, 0]) == self._config.talker.codec_eos_id)
 
     # -- decode -----------------------------------------------------------
-    def _step_body(self, io: _lib.StepIO, n: int) -> None:
-        """One fused decode step: talker + sampling + code predictor + codec sum, then code2wav."""
+    def _step_a(self, io: _lib.StepIO) -> None:
+        """Talker + sampling + code predictor + codec sum (stream A)."""
         self._model.step(io, self._stream)
-        if self._c2w is not None:
-            self._c2w.step(self.codes, self.slots_dev, self.wav, n=n, stream=self._stream)
-            io.launches += self._c2w.last_launches
+
+    def _step_b(self, n: int, parity: int) -> None:
+        """Code2wav of the step's frame (stream B)."""
+        self._c2w.step(self.codes_buf[parity], self.slots_buf[parity], self.wav, n=n, stream=self._c2w_stream)
 
     def _capture(self, n: int):
-        io = self._io(n, 1, self.next_x, sample=1)
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=self._stream):
-            self._step_body(io, n)
-        return g, io
+        """CUDA graphs of both parities: (graph A, graph B or None) per parity, and the launch count."""
+        graphs = []
+        launches = 0
+        for par in (0, 1):
+            io = self._io(n, 1, self.next_x, sample=1, parity=par)
+            ga = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(ga, stream=self._stream):
+                self._step_a(io)
+            gb = None
+            if self._c2w is not None:
+                gb = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gb, stream=self._c2w_stream):
+                    self._step_b(n, par)
+                io.launches += self._c2w.last_launches
+            graphs.append((ga, gb))
+            launches = io.launches
+        return graphs, launches
+
+    def _enqueue_step(self, n: int, upload: bool, graphs=None):
+        """Enqueue one decode step of the first n slots of the next parity's slot buffer.
+        Returns (parity, event after stream A's part, event after the whole step)."""
+        par = self._parity
+        self._parity ^= 1
+        a, b = self._stream, self._c2w_stream
+        with torch.cuda.stream(a):
+            if self._done_b[par] is not None:  # code2wav of step t - 2 has read this parity's buffers
+                a.wait_event(self._done_b[par])
+            if upload:
+                self.slots_buf[par][:n].copy_(self.slots_host_buf[par][:n], non_blocking=True)
+            if graphs is not None:
+                graphs[par][0].replay()
+            else:
+                self._step_a(self._io(n, 1, self.next_x, sample=1, parity=par))
+            self.codes_host_buf[par][:n].copy_(self.codes_buf[par][:n], non_blocking=True)
+            self.status_host_buf[par].copy_(self.status, non_blocking=True)
+            ev_a = torch.cuda.Event()
+            ev_a.record(a)
+        ev_b = ev_a
+        if self._c2w is not None:
+            b.wait_event(ev_a)
+            with torch.cuda.stream(b):
+                if graphs is not None:
+                    graphs[par][1].replay()
+                else:
+                    self._step_b(n, par)
+                self.wav_host_buf[par][:n].copy_(self.wav[:n], non_blocking=True)
+                ev_b = torch.cuda.Event()
+                ev_b.record(b)
+        self._done_a[par] = ev_a
+        self._done_b[par] = ev_b
+        return par, ev_a, ev_b
+
+    def prepare_replay(self, slots: List[SlotState]):
+        """Upload `slots` to both parities' slot buffers and capture the batch's graphs (for
+        timing loops that replay the same batch); returns the launches per step."""
+        n = len(slots)
+        for par in (0, 1):
+            for i, s in enumerate(slots):
+                self.slots_host_buf[par][i] = s.slot_id
+            self.slots_buf[par][:n].copy_(self.slots_host_buf[par][:n])
+        torch.cuda.synchronize(self._device)
+        g = self._graphs.get(n)
+        if g is None:
+            g = self._capture(n)
+            self._graphs[n] = g
+        return g[1]
+
+    def replay_step(self, n: int):
+        """One decode step of the batch `prepare_replay` set up; returns (event after
+        stream A's part, event after the whole step).  The host does not wait."""
+        _, ev_a, ev_b = self._enqueue_step(n, upload=False, graphs=self._graphs[n][0])
+        return ev_a, ev_b
 
     def launch_decode_step(self, slots: List[SlotState]) -> GPUFuture:
         """executor.py:1087-1183 — enqueue one decode step and return at once."""
@@ -385,34 +470,29 @@ class B200Executor:
             if s.past_len + 1 > cap:
                 raise ValueError(f"slot {s.slot_id} is at max_seq_len={cap}")
         original = [s.past_len for s in slots]
+        par = self._parity
+        if self._done_a[par] is not None:  # the staging copy of step t - 2 has been consumed
+            self._done_a[par].synchronize()
         for i, s in enumerate(slots):
-            self.slots_host[i] = s.slot_id
-        with torch.cuda.stream(self._stream):
-            self.slots_dev[:n].copy_(self.slots_host[:n], non_blocking=True)
-            if self._use_graphs:
-                if n not in self._graphs:
-                    self._step_body(self._io(n, 1, self.next_x, sample=1), n)  # eager warm-up step
-                    self._stream.synchronize()
-                    self._graphs[n] = None  # the warm-up already advanced this batch
-                else:
-                    if self._graphs[n] is None:
-                        self._graphs[n] = self._capture(n)
-                    self._graphs[n][0].replay()
-            else:
-                self._step_body(self._io(n, 1, self.next_x, sample=1), n)
-            self.codes_host[:n].copy_(self.codes[:n], non_blocking=True)
-            if self._c2w is not None:
-                self.wav_host[:n].copy_(self.wav[:n], non_blocking=True)
-            self.status_host.copy_(self.status, non_blocking=True)
-            ev = torch.cuda.Event()
-            ev.record(self._stream)
+            self.slots_host_buf[par][i] = s.slot_id
+        graphs = None
+        if self._use_graphs:
+            if n not in self._graphs:
+                self._graphs[n] = None  # first step of this batch size runs eagerly
+            elif self._graphs[n] is None:
+                torch.cuda.synchronize(self._device)
+                self._graphs[n] = self._capture(n)
+            if self._graphs[n] is not None:
+                graphs = self._graphs[n][0]
+        par, ev_a, ev_b = self._enqueue_step(n, upload=True, graphs=graphs)
         for s in slots:
             s.past_len += 1
             s.frame_idx += 1
             s.touch()
-        return GPUFuture(_executor=self, _event=ev, _slots=list(slots), _original_past_lens=original,
-                         _codes_host=self.codes_host, _codes_dev=self.codes, _codec_sum=self.codec_sum,
-                         _status_host=self.status_host, _wav_host=self.wav_host)
+        return GPUFuture(_executor=self, _event=ev_b, _slots=list(slots), _original_past_lens=original,
+                         _codes_host=self.codes_host_buf[par], _codes_dev=self.codes_buf[par],
+                         _codec_sum=self.codec_sum, _status_host=self.status_host_buf[par],
+                         _wav_host=self.wav_host_buf[par] if self._c2w is not None else None)
 
     def warmup(self, n_rounds: int = 3) -> None:
         """executor.py:1541-1605: a throw-away slot through prefill and decode."""
