@@ -226,9 +226,10 @@ def load_peaks():
 
 
 # ----------------------------------------------------------------------------- CPU baseline
-def cpu_oracle_rate(n_streams=4, ctx=256, steps=2):
+def cpu_oracle_rate(n_streams=4, ctx=256, steps=40, warmup=1):
     """The oracle (fp32, all host threads) on a bounded sample of the workload:
-    ``steps`` decode steps of ``n_streams`` streams at context ``ctx``."""
+    ``warmup`` untimed then ``steps`` timed decode steps of ``n_streams`` streams starting
+    at context ``ctx`` (about 10 s of CPU work at the default)."""
     from oracle.engine import OracleEngine
     from oracle import model as M
     from test_stateful_b200 import weights as wmod
@@ -248,8 +249,10 @@ def cpu_oracle_rate(n_streams=4, ctx=256, steps=2):
     counts = torch.zeros(n_streams, t.codec_vocab_size, dtype=torch.long)
     temp = torch.full((n_streams, 1), 0.9)
     pen = torch.full((n_streams, 1), 1.05)
-    t0 = time.perf_counter()
-    for _ in range(steps):
+    t0 = None
+    for k in range(warmup + steps):
+        if k == warmup:
+            t0 = time.perf_counter()
         gum = M.gumbel_from_uniform(torch.rand(n_streams, 50, generator=g))
         cgum = M.gumbel_from_uniform(torch.rand(n_streams, c.num_stages, 50, generator=g))
         r = eng.decode(list(range(n_streams)), x, counts, gum, cgum, temp, pen)
@@ -267,7 +270,8 @@ def cpu_oracle_rate(n_streams=4, ctx=256, steps=2):
 def run_reference(rank, world):
     if rank != 0:
         return
-    base = cpu_oracle_rate()
+    # the arm's own --steps / --warmup, each step a 4-stream sample of the 64-stream step
+    base = cpu_oracle_rate(steps=max(1, ARGS.steps), warmup=ARGS.warmup)
     line = {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": UNIT, "n_gpus": world,
             "steps": ARGS.steps, "warmup": ARGS.warmup, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
