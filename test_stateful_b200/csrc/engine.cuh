@@ -80,7 +80,8 @@ struct qtts_engine {
     std::vector<qtts::LayerGemms> tg;
     qtts::GemmPlan head;
     std::vector<qtts::LayerGemms> cg;
-    qtts::GemmPlan cp_proj_pair, cp_proj_one;
+    qtts::GemmPlan cp_proj_pair;
+    float* cp_tab = nullptr;  // [cp_stages - 1][cp_vocab][cH]: stage embeddings through the projection
     std::vector<qtts::GemmPlan> cp_heads;
 };
 
@@ -273,11 +274,19 @@ inline int engine_build(qtts_engine* e) {
     // stage 0 projects [talker hidden (hi/lo), codec embedding]; later stages only embeddings (exact in bf16)
     QTTS_TRY(gemm_plan(&e->cp_proj_pair, e->cp_in, crows, H, d.cp_w_proj, cH, QTTS_EPI_F32, e->cx, d.cp_b_proj,
                        nullptr, e->cp_in_lo));
-    QTTS_TRY(gemm_plan(&e->cp_proj_one, e->cp_in, crows, H, d.cp_w_proj, cH, QTTS_EPI_F32, e->cx, d.cp_b_proj,
-                       nullptr));
+    {
+        // stages 1..S-1 feed a codec embedding row through the (linear) projection: do it once
+        // for every row of their embedding tables
+        const int rows = (S - 1) * d.cp_vocab;
+        QTTS_TRY(dev_alloc(e, &e->cp_tab, (size_t)rows * cH));
+        GemmPlan tab;
+        QTTS_TRY(gemm_plan(&tab, d.cp_w_codec_emb, rows, H, d.cp_w_proj, cH, QTTS_EPI_F32, e->cp_tab, d.cp_b_proj,
+                           nullptr));
+        QTTS_TRY(gemm_run(tab, rows, 0));
+        QTTS_CHECK_CUDA(cudaStreamSynchronize(0));
+    }
     // the first layer's input norm folded into the projection
     fold_norm_out(e->cp_proj_pair, bf(d.cp_w_in_norm, 0), e->cxn, e->cxn_lo, e->css);
-    fold_norm_out(e->cp_proj_one, bf(d.cp_w_in_norm, 0), e->cxn, e->cxn_lo, e->css);
     e->cp_heads.resize(S);
     for (int s = 0; s < S; ++s)
         QTTS_TRY(gemm_plan(&e->cp_heads[s], e->chid, bmax, cH, bf(d.cp_w_lm_head, (size_t)s * d.cp_vocab * cH),
@@ -414,12 +423,12 @@ inline int engine_step_impl(qtts_engine* e, const qtts_step_io& io, cudaStream_t
             QTTS_LAUNCH(cp_stage0_rows_kernel, dim3(nr), dim3(128), 0, st, (const __nv_bfloat16*)e->hid,
                         (const __nv_bfloat16*)e->hid_lo, bf(d.w_codec_emb, 0), d.vocab, H, codes_in, G, e->cp_in,
                         e->cp_in_lo);
+            QTTS_TRY(run_plan(e->cp_proj_pair, rows, st));
         } else {
-            QTTS_LAUNCH(gather_rows_kernel, dim3(nr), dim3(128), 0, st,
-                        bf(d.cp_w_codec_emb, (size_t)(s - 1) * d.cp_vocab * H), d.cp_vocab, H, codes_in + s, G,
-                        e->cp_in, H);
+            QTTS_LAUNCH(cp_embed_rows_kernel, dim3(nr), dim3(256), 0, st,
+                        (const float*)e->cp_tab + (size_t)(s - 1) * d.cp_vocab * cH, d.cp_vocab, cH, codes_in + s, G,
+                        bf(d.cp_w_in_norm, 0), e->cx, e->cxn, e->cxn_lo, e->css);
         }
-        QTTS_TRY(run_plan(s == 0 ? e->cp_proj_pair : e->cp_proj_one, rows, st));
         cap.row_slot = m + 3 * crows;
         cap.row_ctx = m + 2 * crows;
         cap.R = rows;

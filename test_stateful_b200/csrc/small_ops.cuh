@@ -88,6 +88,40 @@ __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ table, int 
     for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = src[i];
 }
 
+// Input of code-predictor stages 1..14: the stage's codec embedding row already projected to the
+// code predictor's width (table = emb_s · W_proj^T + b_proj, computed once at load: the projection
+// is linear and its inputs are a fixed table), written as the residual stream x, plus what the
+// first layer's folded input norm needs: the bf16 pair of x∘γ and per-128-column sums of x².
+// One CTA per row; warp w of an iteration covers the 128 columns of tile (w + iteration·warps).
+__global__ void cp_embed_rows_kernel(const float* __restrict__ table, int V, int H, const int64_t* __restrict__ ids,
+                                     int id_ld, const __nv_bfloat16* __restrict__ gamma, float* __restrict__ x,
+                                     __nv_bfloat16* __restrict__ xn, __nv_bfloat16* __restrict__ xn_lo,
+                                     float* __restrict__ ss) {
+    const int r = blockIdx.x;
+    griddep_wait();
+    griddep_launch();
+    int64_t id = ids[(size_t)r * id_ld];
+    if (id < 0 || id >= V) id = 0;  // stay in bounds; callers pass sampled (valid) ids
+    const float4* src = reinterpret_cast<const float4*>(table + (size_t)id * H);
+    for (int c4 = threadIdx.x; c4 < H / 4; c4 += blockDim.x) {
+        const float4 v = src[c4];
+        reinterpret_cast<float4*>(x + (size_t)r * H)[c4] = v;
+        const float a[4] = {v.x, v.y, v.z, v.w};
+        float sq = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int c = c4 * 4 + k;
+            const float xg = a[k] * __bfloat162float(gamma[c]);
+            const __nv_bfloat16 hi = __float2bfloat16(xg);
+            xn[(size_t)r * H + c] = hi;
+            xn_lo[(size_t)r * H + c] = __float2bfloat16(xg - __bfloat162float(hi));
+            sq += a[k] * a[k];
+        }
+        sq = warp_sum(sq);
+        if ((threadIdx.x & 31) == 0) ss[(size_t)r * (H / 128) + c4 / 32] = sq;
+    }
+}
+
 // Stage-0 input of the code predictor: rows [2b] = hidden[b], [2b+1] = codec_emb[tok0[b]]
 // (CodePredictorUnrolled.forward, utils.py:1019-1020), as a hi/lo operand pair
 // (the embedding is exact in bf16, its lo row is zero).
