@@ -268,8 +268,10 @@ inline int engine_build(qtts_engine* e) {
         fold_norm_out(g.o, bf(d.cp_w_post_norm, (size_t)l * cH), e->cxn, e->cxn_lo, e->css);
         fold_norm_in(g.gu, e->css, cH, d.cp_rms_eps);
         fold_norm_in(g.qkv, e->css, cH, d.cp_rms_eps);
-        if (l + 1 < d.cp_layers)
-            fold_norm_out(g.down, bf(d.cp_w_in_norm, (size_t)(l + 1) * cH), e->cxn, e->cxn_lo, e->css);
+        // the last layer's down projection folds the final norm (used from stage 1 on, where
+        // every row is a stream's last position)
+        fold_norm_out(g.down, l + 1 < d.cp_layers ? bf(d.cp_w_in_norm, (size_t)(l + 1) * cH) : bf(d.cp_w_final_norm, 0),
+                      e->cxn, e->cxn_lo, e->css);
     }
     // stage 0 projects [talker hidden (hi/lo), codec embedding]; later stages only embeddings (exact in bf16)
     QTTS_TRY(gemm_plan(&e->cp_proj_pair, e->cp_in, crows, H, d.cp_w_proj, cH, QTTS_EPI_F32, e->cx, d.cp_b_proj,
@@ -288,9 +290,14 @@ inline int engine_build(qtts_engine* e) {
     // the first layer's input norm folded into the projection
     fold_norm_out(e->cp_proj_pair, bf(d.cp_w_in_norm, 0), e->cxn, e->cxn_lo, e->css);
     e->cp_heads.resize(S);
-    for (int s = 0; s < S; ++s)
-        QTTS_TRY(gemm_plan(&e->cp_heads[s], e->chid, bmax, cH, bf(d.cp_w_lm_head, (size_t)s * d.cp_vocab * cH),
-                           d.cp_vocab, QTTS_EPI_F32, e->clogits, nullptr, nullptr, e->chid_lo));
+    for (int s = 0; s < S; ++s) {
+        // stage 0 reads the final norm of rows 2b+1 (a norm kernel); later stages the folded one
+        const bool folded = s > 0;
+        QTTS_TRY(gemm_plan(&e->cp_heads[s], folded ? e->cxn : e->chid, folded ? crows : bmax, cH,
+                           bf(d.cp_w_lm_head, (size_t)s * d.cp_vocab * cH), d.cp_vocab, QTTS_EPI_F32, e->clogits,
+                           nullptr, nullptr, folded ? e->cxn_lo : e->chid_lo));
+        if (folded) fold_norm_in(e->cp_heads[s], e->css, cH, d.cp_rms_eps);
+    }
     QTTS_TRY(gemm_plan(&e->head, e->hid, bmax, H, d.w_codec_head, d.vocab, QTTS_EPI_F32, nullptr, nullptr, nullptr,
                        e->hid_lo));
     return QTTS_OK;
@@ -444,10 +451,11 @@ inline int engine_step_impl(qtts_engine* e, const qtts_step_io& io, cudaStream_t
             QTTS_TRY(run_plan(g.gu, rows, st));
             QTTS_TRY(run_plan(g.down, rows, st));
         }
-        // last position of each stream: row 2b+1 at stage 0, row b afterwards
-        const float* last = s == 0 ? e->cx + cH : e->cx;
-        const int ld = s == 0 ? 2 * cH : cH;
-        QTTS_TRY(launch_rmsnorm(last, nr, cH, ld, d.cp_w_final_norm, d.cp_rms_eps, e->chid, st, e->chid_lo));
+        // final norm: stage 0 normalises each stream's last position (row 2b+1) with a kernel;
+        // from stage 1 on it is folded into the last down projection and the head
+        if (s == 0)
+            QTTS_TRY(launch_rmsnorm(e->cx + cH, nr, cH, 2 * cH, d.cp_w_final_norm, d.cp_rms_eps, e->chid, st,
+                                    e->chid_lo));
         QTTS_TRY(run_plan(e->cp_heads[s], nr, st));
         SampleParams cs = {};
         cs.logits = e->clogits;

@@ -73,6 +73,7 @@ constexpr int kSampleCand = 128;    // candidate buffer (>= topk, room for ties)
 __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SampleParams p) {
     __shared__ uint32_t hist[256];
     __shared__ uint32_t s_prefix, s_need;
+    __shared__ int s_stop;
     __shared__ int s_ncand;
     __shared__ float c_val[kSampleCand];
     __shared__ int c_idx[kSampleCand];
@@ -104,9 +105,11 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
         key[i] = idx < p.V ? float_key(g) : 0u;  // padding sorts below every real value
     }
 
-    // radix select of the topk-th largest key
+    // radix select of the topk-th largest key; stops early once every key at or above the
+    // bucket holding it fits the candidate buffer (the sort below then orders them all)
     uint32_t prefix = 0, mask = 0;
     uint32_t need = (uint32_t)p.topk;
+    bool early = false;
     for (int shift = 24; shift >= 0; shift -= 8) {
         for (int i = tid; i < 256; i += kSampleThreads) hist[i] = 0;
         __syncthreads();
@@ -153,30 +156,37 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
                 }
                 s_prefix = prefix | ((uint32_t)b << shift);
                 s_need = need - above;
+                // keys above the bucket + the bucket itself
+                const uint32_t bucket = hist[b];
+                s_stop = shift > 0 && (uint32_t)p.topk - (need - above) + bucket <= (uint32_t)kSampleCand;
             }
         }
         __syncthreads();
         prefix = s_prefix;
         need = s_need;
         mask |= 255u << shift;
+        early = s_stop != 0;
         __syncthreads();
+        if (early) break;
     }
-    // gather candidates: every key > prefix (fewer than topk; their order is fixed by the sort
-    // below), then the lowest-index keys == prefix until topk are taken, in index order, so the
-    // selection is deterministic when values tie
+    // gather candidates.  Early stop: every key whose high bits reach the bucket (at most
+    // kSampleCand; the sort orders them and the first topk are exactly the top-k with ties
+    // broken by index).  Otherwise every key > the k-th key (fewer than topk), then the
+    // lowest-index keys equal to it until topk are taken, in index order, so the selection is
+    // deterministic when values tie.
     if (tid == 0) s_ncand = 0;
     __syncthreads();
 #pragma unroll
     for (int i = 0; i < kSampleMaxPer; ++i) {
         const int idx = tid + i * kSampleThreads;
-        if (idx < p.V && key[i] > prefix) {
+        if (idx < p.V && (early ? key[i] >= prefix : key[i] > prefix)) {
             const int slot = atomicAdd(&s_ncand, 1);
             c_val[slot] = val[i];
             c_idx[slot] = idx;
         }
     }
     __syncthreads();
-    {
+    if (!early) {
         __shared__ int s_wcnt[kSampleThreads / 32];
         const int lane = tid & 31, wid = tid >> 5;
         int base = s_ncand;
