@@ -996,7 +996,17 @@ inline int make_map_bf16(CUtensorMap* map, const void* ptr, uint64_t rows, uint6
     return QTTS_OK;
 }
 
-inline int pick_bn(int M) { return M <= 64 ? 64 : 128; }
+// Token-tile width.  With QTTS_GEMM_BN32=1 (opt-in), up to 64 tokens run as 32-token tiles:
+// each weight tile is read by two CTAs but a CTA's split-K partial and its share of the cluster
+// exchange halve.  Measured slower on the decode step (9 808 vs 10 142 frames/s).
+inline bool gemm_bn32() {
+    static const bool on = [] {
+        const char* v = getenv("QTTS_GEMM_BN32");
+        return v && *v == '1';
+    }();
+    return on;
+}
+inline int pick_bn(int M) { return M <= 64 ? (gemm_bn32() ? 32 : 64) : 128; }
 
 // Persistent conv GEMMs for wide rows: opt-in (QTTS_GEMM_PERSIST=1).  At the decoder's
 // sizes they measured slower than the two-CTAs-per-SM form (2.43 vs 1.64 ms per
@@ -1066,7 +1076,7 @@ inline int launch_gemm_t(const CUtensorMap& mw, const CUtensorMap& mx, const CUt
 
 // Prepared GEMM: tensor maps built once (two token-tile heights, optional lo operand), reused every step.
 struct GemmPlan {
-    CUtensorMap mw, mx64, mx128, mlo64, mlo128;
+    CUtensorMap mw, mx32, mx64, mx128, mlo32, mlo64, mlo128;
     GemmParams p;
     bool split;
 };
@@ -1084,17 +1094,22 @@ inline int gemm_plan(GemmPlan* g, const void* X, int rows, int K, const void* W,
     }
     int rc = make_map_bf16(&g->mw, W, (uint64_t)N, (uint64_t)K, 128);
     if (rc) return rc;
+    rc = make_map_bf16(&g->mx32, X, (uint64_t)rows, (uint64_t)K, 32);
+    if (rc) return rc;
     rc = make_map_bf16(&g->mx64, X, (uint64_t)rows, (uint64_t)K, 64);
     if (rc) return rc;
     rc = make_map_bf16(&g->mx128, X, (uint64_t)rows, (uint64_t)K, 128);
     if (rc) return rc;
     g->split = X_lo != nullptr;
     if (g->split) {
+        rc = make_map_bf16(&g->mlo32, X_lo, (uint64_t)rows, (uint64_t)K, 32);
+        if (rc) return rc;
         rc = make_map_bf16(&g->mlo64, X_lo, (uint64_t)rows, (uint64_t)K, 64);
         if (rc) return rc;
         rc = make_map_bf16(&g->mlo128, X_lo, (uint64_t)rows, (uint64_t)K, 128);
         if (rc) return rc;
     } else {
+        g->mlo32 = g->mx32;
         g->mlo64 = g->mx64;
         g->mlo128 = g->mx128;
     }
@@ -1126,7 +1141,9 @@ inline int gemm_plan_implicit(GemmPlan* g, const void* H, int total_rows, int cp
     if (rc) return rc;
     rc = make_map_bf16(&g->mx128, H, (uint64_t)total_rows, (uint64_t)cpad, 128);
     if (rc) return rc;
+    g->mx32 = g->mx128;
     g->mx64 = g->mx128;
+    g->mlo32 = g->mx128;
     g->mlo64 = g->mx128;
     g->mlo128 = g->mx128;
     g->split = false;
@@ -1192,6 +1209,10 @@ inline int gemm_run(GemmPlan g, int M, cudaStream_t st, void* out = nullptr) {
     if (push) {
         if (g.split) return launch_gemm_t<64, 5, true, 128, true>(g.mw, g.mx64, g.mlo64, g.p, st);
         return launch_gemm_t<64, 5, false, 128, true>(g.mw, g.mx64, g.mx64, g.p, st);
+    }
+    if (bn == 32) {
+        if (g.split) return launch_gemm_t<32, 3, true>(g.mw, g.mx32, g.mlo32, g.p, st);
+        return launch_gemm_t<32, 4, false>(g.mw, g.mx32, g.mx32, g.p, st);
     }
     if (g.split) {
         if (bn == 64) {

@@ -303,14 +303,16 @@ def test_rmsnorm_and_codec_sum():
     torch.testing.assert_close(nx.cpu(), ref + text.cpu(), rtol=1e-6, atol=1e-7)  # next input stays fp32
 
 
-@pytest.mark.skipif(os.environ.get("QTTS_GEMM_PUSH") is not None, reason="already the forced run")
-def test_gemm_push_reduction_variant():
-    """The push form of the split-K reduction is opt-in (QTTS_GEMM_PUSH=1, read once per
-    process); rerun the GEMM tests in a child process with it on."""
+@pytest.mark.skipif(os.environ.get("QTTS_GEMM_PUSH") is not None or os.environ.get("QTTS_GEMM_BN32") is not None,
+                    reason="already a forced run")
+@pytest.mark.parametrize("knob", ["QTTS_GEMM_PUSH", "QTTS_GEMM_BN32"])
+def test_gemm_opt_in_variants(knob):
+    """The push form of the split-K reduction and 32-token tiles are opt-in (read once per
+    process); rerun the GEMM tests in a child process with each on."""
     import subprocess
     import sys
 
-    env = dict(os.environ, QTTS_GEMM_PUSH="1")
+    env = dict(os.environ, **{knob: "1"})
     r = subprocess.run([sys.executable, "-m", "pytest", "-x", "-q", "-m", "gpu", "-p", "no:cacheprovider", "-k", "gemm",
                         os.path.abspath(__file__)], env=env, capture_output=True, text=True, timeout=900)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
