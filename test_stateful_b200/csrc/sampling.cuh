@@ -215,53 +215,80 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
     __syncthreads();
     if (tid < 32) {
         const int n = min(s_ncand, kSampleCand);
-        // bitonic sort of 128 entries by (value desc, index asc) in one warp, 4 per lane
+        // The noise of rank j does not depend on the sort: start it first (independent work).
+        const uint64_t nkey = p.noise_key ? (uint64_t)p.noise_key[crow] : (uint64_t)crow;
+        const int nstep = (p.noise_step ? p.noise_step[crow] * 16 : 0) + p.step;
+        float gnj[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int j = tid + 32 * h;
+            gnj[h] = j >= p.topk ? 0.f
+                                 : (p.gumbel ? p.gumbel[(size_t)r * p.gumbel_ld + j] : gumbel_noise(p.seed, nkey, nstep, j));
+        }
+        // bitonic sort of 128 entries by (value desc, index asc) in registers: lane l holds
+        // positions 4l..4l+3; partners 4 or more positions apart are exchanged by shuffles
         float v[4];
         int ix[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int e = tid * 4 + j;
-            v[j] = e < n ? c_val[e] : -INFINITY;
-            ix[j] = e < n ? c_idx[e] : 0x7fffffff;
+        for (int k = 0; k < 4; ++k) {
+            const int e = tid * 4 + k;
+            v[k] = e < n ? c_val[e] : -INFINITY;
+            ix[k] = e < n ? c_idx[e] : 0x7fffffff;
         }
-        // write back to shared and sort there (simple, 128 elements)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            c_val[tid * 4 + j] = v[j];
-            c_idx[tid * 4 + j] = ix[j];
-        }
-        __syncwarp();
-        for (int k = 2; k <= kSampleCand; k <<= 1) {
-            for (int jj = k >> 1; jj > 0; jj >>= 1) {
-                for (int e = tid; e < kSampleCand; e += 32) {
-                    const int o = e ^ jj;
-                    if (o > e) {
-                        const bool up = (e & k) == 0;  // "up" = descending order block
-                        const float va = c_val[e], vb = c_val[o];
-                        const int ia = c_idx[e], ib = c_idx[o];
-                        const bool a_first = (va > vb) || (va == vb && ia < ib);
-                        if (up != a_first) {
-                            c_val[e] = vb;
-                            c_val[o] = va;
-                            c_idx[e] = ib;
-                            c_idx[o] = ia;
+        for (int size = 2; size <= kSampleCand; size <<= 1) {
+#pragma unroll
+            for (int j = size >> 1; j > 0; j >>= 1) {
+                if (j >= 4) {
+                    const int lm = j >> 2;  // partner lane = tid ^ lm, same register
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const float pv = __shfl_xor_sync(0xffffffffu, v[k], lm);
+                        const int pi = __shfl_xor_sync(0xffffffffu, ix[k], lm);
+                        const int pos = tid * 4 + k;
+                        const bool up = (pos & size) == 0;
+                        const bool lower = (pos & j) == 0;
+                        const bool me_first = (v[k] > pv) || (v[k] == pv && ix[k] < pi);
+                        const bool keep = (lower == up) ? me_first : !me_first;
+                        if (!keep) {
+                            v[k] = pv;
+                            ix[k] = pi;
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const int k2 = k ^ j;
+                        if (k2 > k) {
+                            const bool up = ((tid * 4 + k) & size) == 0;
+                            const bool a_first = (v[k] > v[k2]) || (v[k] == v[k2] && ix[k] < ix[k2]);
+                            if (up != a_first) {
+                                const float tv = v[k];
+                                v[k] = v[k2];
+                                v[k2] = tv;
+                                const int ti = ix[k];
+                                ix[k] = ix[k2];
+                                ix[k2] = ti;
+                            }
                         }
                     }
                 }
-                __syncwarp();
             }
         }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            c_val[tid * 4 + k] = v[k];
+            c_idx[tid * 4 + k] = ix[k];
+        }
+        __syncwarp();
         // Gumbel-max over the first topk ranks
         float best = -INFINITY;
         int best_j = 0x7fffffff;
-        for (int j = tid; j < p.topk; j += 32) {
-            float gn;
-            if (p.gumbel)
-                gn = p.gumbel[(size_t)r * p.gumbel_ld + j];
-            else
-                gn = gumbel_noise(p.seed, p.noise_key ? (uint64_t)p.noise_key[crow] : (uint64_t)crow,
-                                  (p.noise_step ? p.noise_step[crow] * 16 : 0) + p.step, j);
-            const float sc = c_val[j] / temp + gn;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int j = tid + 32 * h;
+            if (j >= p.topk) break;
+            const float sc = c_val[j] / temp + gnj[h];
             if (sc > best || (sc == best && j < best_j)) {
                 best = sc;
                 best_j = j;
