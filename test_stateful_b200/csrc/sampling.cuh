@@ -76,6 +76,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
     __shared__ int s_stop;
     __shared__ int s_ncand;
     __shared__ float c_val[kSampleCand];
+    __shared__ float s_noise[64];  // Gumbel noise of ranks 0..topk-1
     __shared__ int c_idx[kSampleCand];
 
     const int r = blockIdx.x, tid = threadIdx.x;
@@ -115,16 +116,10 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
         __syncthreads();
 #pragma unroll
         for (int i = 0; i < kSampleMaxPer; ++i) {
-            // warp-aggregated: logits of similar size share the high key bits, so lanes
-            // hitting the same bin add once through their lowest lane
+            // plain shared atomics: measured faster than aggregating equal bins with
+            // __match_any_sync (9.3 vs 11.3 us per 64-row launch)
             const int idx = tid + i * kSampleThreads;
-            const bool act = idx < p.V && (key[i] & mask) == prefix;
-            const uint32_t am = __ballot_sync(0xffffffffu, act);
-            if (act) {
-                const uint32_t bin = (key[i] >> shift) & 255u;
-                const uint32_t peers = __match_any_sync(am, bin);
-                if ((int)(threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&hist[bin], (uint32_t)__popc(peers));
-            }
+            if (idx < p.V && (key[i] & mask) == prefix) atomicAdd(&hist[(key[i] >> shift) & 255u], 1u);
         }
         __syncthreads();
         if (tid < 32) {
@@ -176,13 +171,22 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
     // deterministic when values tie.
     if (tid == 0) s_ncand = 0;
     __syncthreads();
+    {
+        // one shared atomic per warp and round: the lanes' slots follow from the ballot
+        const int lane = tid & 31;
 #pragma unroll
-    for (int i = 0; i < kSampleMaxPer; ++i) {
-        const int idx = tid + i * kSampleThreads;
-        if (idx < p.V && (early ? key[i] >= prefix : key[i] > prefix)) {
-            const int slot = atomicAdd(&s_ncand, 1);
-            c_val[slot] = val[i];
-            c_idx[slot] = idx;
+        for (int i = 0; i < kSampleMaxPer; ++i) {
+            const int idx = tid + i * kSampleThreads;
+            const bool c = idx < p.V && (early ? key[i] >= prefix : key[i] > prefix);
+            const unsigned b = __ballot_sync(0xffffffffu, c);
+            int base = 0;
+            if (lane == 0 && b) base = atomicAdd(&s_ncand, __popc(b));
+            base = __shfl_sync(0xffffffffu, base, 0);
+            if (c) {
+                const int slot = base + __popc(b & ((1u << lane) - 1u));
+                c_val[slot] = val[i];
+                c_idx[slot] = idx;
+            }
         }
     }
     __syncthreads();
@@ -213,18 +217,20 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
         if (tid == 0) s_ncand = min(base, p.topk);
     }
     __syncthreads();
-    if (tid < 32) {
-        const int n = min(s_ncand, kSampleCand);
-        // The noise of rank j does not depend on the sort: start it first (independent work).
+    if (tid >= 32 && tid < 64) {
+        // the noise of rank j does not depend on the sort: warp 1 makes it while warp 0 sorts
+        const int lane = tid - 32;
         const uint64_t nkey = p.noise_key ? (uint64_t)p.noise_key[crow] : (uint64_t)crow;
         const int nstep = (p.noise_step ? p.noise_step[crow] * 16 : 0) + p.step;
-        float gnj[2];
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-            const int j = tid + 32 * h;
-            gnj[h] = j >= p.topk ? 0.f
-                                 : (p.gumbel ? p.gumbel[(size_t)r * p.gumbel_ld + j] : gumbel_noise(p.seed, nkey, nstep, j));
+            const int j = lane + 32 * h;
+            if (j < p.topk)
+                s_noise[j] = p.gumbel ? p.gumbel[(size_t)r * p.gumbel_ld + j] : gumbel_noise(p.seed, nkey, nstep, j);
         }
+    }
+    if (tid < 32) {
+        const int n = min(s_ncand, kSampleCand);
         // bitonic sort of 128 entries by (value desc, index asc) in registers: lane l holds
         // positions 4l..4l+3; partners 4 or more positions apart are exchanged by shuffles
         float v[4];
@@ -280,7 +286,9 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
             c_val[tid * 4 + k] = v[k];
             c_idx[tid * 4 + k] = ix[k];
         }
-        __syncwarp();
+    }
+    __syncthreads();  // sorted candidates (warp 0) and noise (warp 1)
+    if (tid < 32) {
         // Gumbel-max over the first topk ranks
         float best = -INFINITY;
         int best_j = 0x7fffffff;
@@ -288,7 +296,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
         for (int h = 0; h < 2; ++h) {
             const int j = tid + 32 * h;
             if (j >= p.topk) break;
-            const float sc = c_val[j] / temp + gnj[h];
+            const float sc = c_val[j] / temp + s_noise[j];
             if (sc > best || (sc == best && j < best_j)) {
                 best = sc;
                 best_j = j;
