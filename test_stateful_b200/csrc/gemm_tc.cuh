@@ -7,7 +7,7 @@
 // 4 KB slice of weights.  Split-K spreads the K range of one 128-row weight
 // tile over the CTAs of a thread-block cluster (1 x splits x 1); the fp32
 // partial tiles are reduced through distributed shared memory — each CTA
-// reduces a slice of BN/splits tokens across the cluster — so there is no
+// reduces a slice of about BN/splits tokens across the cluster — so there is no
 // global workspace and no atomics, and the result is deterministic.
 //
 // Activation precision: at decode the MMA pipe is idle (the kernel waits on
@@ -587,8 +587,10 @@ __global__ void __launch_bounds__(NT) gemm_tc_kernel(const __grid_constant__ CUt
     __syncthreads();
     float* P = reinterpret_cast<float*>(smem);
     const bool good = ok && flags[0] == 0;
-    const int per = BN / p.splits;
-    const int m0 = split * per;
+    // this CTA's token slice of the reduction: [m0, m0 + per), slices differ by at most one
+    // token when splits does not divide BN
+    const int m0 = split * BN / p.splits;
+    const int per = (split + 1) * BN / p.splits - m0;
     const bool push = PUSH && p.splits > 1;
     {
         // warp w reads TMEM lane quarter w % 4; with 256 threads warps w and w + 4
@@ -1048,13 +1050,17 @@ inline int gemm_ctas_per_sm() {
     return s;
 }
 
+// Split-K factor: powers of two up to about `ctas_per_sm` CTAs per SM, at least two k-blocks
+// per CTA.  Filling every SM with exactly two CTAs measured slower: splits of 3 (talker
+// gate/up, 288 CTAs) 23.8 vs 17.8 us with 2, splits of 6 (code-predictor gate/up) 14.4 vs
+// 9.6 us with 4.  (The kernel takes any factor: token slices differ by at most one.)
 inline int pick_splits(int N, int M, int K, int BN) {
     const int tiles = (N / 128) * ceil_div(M, BN);
     const int kb = K / 64;
     const int target = gemm_ctas_per_sm() * num_sms();
     int s = 1;
     while (s * 2 <= gemm_max_splits() && tiles * s * 2 <= target + target / 5 && kb / (s * 2) >= 2 &&
-           BN % (s * 2) == 0)
+           BN / (s * 2) >= 4)
         s *= 2;
     return s;
 }
@@ -1204,7 +1210,7 @@ inline int gemm_run(GemmPlan g, int M, cudaStream_t st, void* out = nullptr) {
     // 196 KB footprint keeps the next kernel's CTAs off the SM until this one exits, so
     // programmatic dependent launch no longer overlaps their weight prefetch, and the
     // remote stores cost about what the pull's remote loads do.
-    const bool push = bn == 64 && g.p.splits > 1 && gemm_push_enabled() &&
+    const bool push = bn == 64 && g.p.splits > 1 && 64 % g.p.splits == 0 && gemm_push_enabled() &&
                       (g.p.N / 128) * g.p.splits * ceil_div(M, bn) <= num_sms();
     if (push) {
         if (g.split) return launch_gemm_t<64, 5, true, 128, true>(g.mw, g.mx64, g.mlo64, g.p, st);
