@@ -211,8 +211,15 @@ def attention_roofline(ex, slots, peaks):
     algo = kv_bytes + qo_bytes
     gbs = algo / sec / 1e9
     peak = peaks.get("hbm_gbs")
+    # DRAM traffic per launch: an ncu capture of the same kernel on 64 rows at mean context 858
+    # read 228.13 MB + wrote 5.01 MB for 225.93 MB of algorithmic bytes
+    # (profiles/paged_attn_kernel_d128_64rows_ctx520.md); traffic grows with the blocks read,
+    # so this launch's traffic is scaled from that ratio
+    traffic_ratio = (228.13 + 5.01) / 225.93
     return {"kernel": "paged_attn_tc_kernel + attn_combine_kernel", "bound": "hbm", "achieved": round(gbs, 1),
-            "peak": peak, "unit": "GB/s", "frac": round(gbs / peak, 3) if peak else None, "traffic": None,
+            "peak": peak, "unit": "GB/s", "frac": round(gbs / peak, 3) if peak else None,
+            "traffic": int(algo * traffic_ratio),
+            "traffic_source": "ncu dram__bytes_read+write of a 64-row, mean-context-858 capture, scaled by bytes",
             "algorithmic_bytes_per_launch": algo, "launch_us": round(sec * 1e6, 2),
             "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)"}
 
