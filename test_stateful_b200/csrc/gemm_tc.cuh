@@ -1030,7 +1030,8 @@ inline bool gemm_push_enabled() {
     return on;
 }
 
-// Tuning knobs read once from the environment (defaults are the measured best):
+// Tuning knobs read once from the environment (defaults are the measured best; a 2-stage ring,
+// globally or only for CTAs with at most two k-blocks, measured 2-3 % slower on the decode step):
 // QTTS_GEMM_STAGES (pipeline depth of the hi/lo kernel at BN = 64) and
 // QTTS_GEMM_MAX_SPLITS (largest split-K cluster), QTTS_GEMM_CTAS_PER_SM (split-K target).
 inline int env_int(const char* name, int dflt) {
@@ -1223,6 +1224,7 @@ inline int gemm_run(GemmPlan g, int M, cudaStream_t st, void* out = nullptr) {
     if (g.split) {
         if (bn == 64) {
             switch (gemm_stages()) {
+                case 2: return launch_gemm_t<64, 2, true>(g.mw, g.mx64, g.mlo64, g.p, st);
                 case 4: return launch_gemm_t<64, 4, true>(g.mw, g.mx64, g.mlo64, g.p, st);
                 case 6: return launch_gemm_t<64, 6, true>(g.mw, g.mx64, g.mlo64, g.p, st);
                 default: return launch_gemm_t<64, 3, true>(g.mw, g.mx64, g.mlo64, g.p, st);
