@@ -1187,8 +1187,10 @@ inline int launch_gemm_persist(const GemmPlan& g, const GemmParams& p, cudaStrea
             cudaFuncSetAttribute(gemm_conv_persist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM));
         attr = true;
     }
+    // QTTS_GEMM_PERSIST_CTAS caps the grid (e.g. to leave SMs to a concurrent stream)
+    static const int cap = env_int("QTTS_GEMM_PERSIST_CTAS", num_sms());
     const int tiles = (p.N / 128) * ceil_div(p.M, 128);
-    const int grid = tiles < num_sms() ? tiles : num_sms();
+    const int grid = tiles < cap ? tiles : cap;
     QTTS_CHECK_CUDA(launch_pdl(gemm_conv_persist_kernel, dim3(grid), dim3(kPersistThreads), L::SMEM, st,
                                dim3(1, 1, 1), g.mw, g.mx128, p));
     return QTTS_OK;
