@@ -369,12 +369,15 @@ typedef struct qtts_c2w_desc {
     const void* b_conv0;
     const float* blk_snake[4];    /* fp32 [2][cin]: exp(alpha), exp(-beta) */
     const void* blk_tw[4];        /* [pad128(s*cout)][2*cinp] (K padded to 64); cinp = pad64(cin) when the
-                                     block's input rows per stream are a multiple of 128, else cin */
+                                     block's transposed conv is implicit (below), else cin */
     const void* blk_tb[4];        /* [pad128(s*cout)] */
     const float* res_act1[4][3];  /* fp32 [2][cout] */
     const float* res_act2[4][3];
     const void* res_w1[4][3];     /* [pad128(cout)][7*coutp] (K padded to 64); coutp = pad64(cout) when the
-                                     block's rows per stream are a multiple of 128, else cout */
+                                     block's residual convs are implicit, else cout.  A conv with T input
+                                     rows per frame is implicit when T % 128 == 0, or when
+                                     R = max_chunk * T >= 512 and padding R to a multiple of 128 adds at
+                                     most R / 8 rows */
     const void* res_b1[4][3];     /* [pad128(cout)] */
     const void* res_w2[4][3];     /* [pad128(cout)][pad128(cout)] */
     const void* res_b2[4][3];

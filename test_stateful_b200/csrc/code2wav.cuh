@@ -401,6 +401,16 @@ inline int c2w_alloc(qtts_c2w* c, T** p, size_t count) {
 inline ActView view_slot(void* p, int ctx, int T, int ld) { return ActView{p, 1, ctx + T, ctx, ld}; }
 inline ActView view_rows(void* p, int T, int ld) { return ActView{p, 0, T, 0, ld}; }
 
+// Whether a convolution whose input has T rows per frame reads its operand straight from the
+// history buffer (implicit convolution).  A GEMM row tile must not span two streams, so a
+// stream's rows are padded to a multiple of 128: used when no padding is needed, or when the
+// largest call (max_chunk frames) has at least 512 rows and pads them by at most 1/8.
+inline bool c2w_implicit_rows(int T, int max_chunk) {
+    if (T % 128 == 0) return true;
+    const int R = max_chunk * T, pad = (R + 127) / 128 * 128 - R;
+    return R >= 512 && pad * 8 <= R;
+}
+
 inline ConvEpi conv_epi(const qtts_c2w* c, int T_rows, int phases, int C_o, int n_valid) {
     ConvEpi e;
     memset(&e, 0, sizeof(e));
@@ -472,8 +482,8 @@ inline int c2w_build(qtts_c2w* c) {
             set_error("c2w: decoder channels must stay multiples of 8");
             return QTTS_ERR_UNSUPPORTED;
         }
-        c->impl_tc[b] = c->T_in[b] % 128 == 0;
-        c->impl_c1[b] = c->T_blk[b] % 128 == 0;
+        c->impl_tc[b] = c2w_implicit_rows(c->T_in[b], Fm);
+        c->impl_c1[b] = c2w_implicit_rows(c->T_blk[b], Fm);
         c->cinpad[b] = c->impl_tc[b] ? pad64(c->cin[b]) : c->cin[b];
         c->cpad[b] = c->impl_c1[b] ? pad64(c->cout[b]) : c->cout[b];
         c->K_tc[b] = c->impl_tc[b] ? 2 * c->cinpad[b] : pad64(2 * c->cin[b]);
@@ -667,13 +677,22 @@ inline int c2w_im2col(const qtts_c2w* c, const __nv_bfloat16* H, int ctx, int se
 // A plan built for one frame's rows per stream, run on F frames: rows per stream and the
 // stride of the per-call (not slot-indexed) buffers scale by F; history buffers keep their
 // segment size (ctx + Fm * rows per frame).
+// An implicit convolution pads each stream's rows to whole 128-row tiles (the epilogue skips the
+// padding rows).
 inline int run_conv(GemmPlan g, int M, const int32_t* slots, cudaStream_t st, int F) {
+    const int T = g.p.conv.T_rows * F;  // rows per stream of this call
     g.p.conv.row_slot = slots;
-    g.p.conv.T_rows *= F;
+    g.p.conv.T_rows = T;
     for (ActView* v : {&g.p.conv.res, &g.p.conv.out32, &g.p.conv.out16})
         if (!v->by_slot) v->seq_rows *= F;
     g.p.ix.row_slot = slots;  // implicit convolutions read the history rows of each row's slot
-    g.p.ix.T *= F;
+    if (g.p.ix.on) {
+        const int Tpad = (T + 127) / 128 * 128;
+        g.p.ix.T = Tpad;
+        g.p.conv.T_rows = Tpad;
+        g.p.conv.T_valid = T;
+        M = M / T * Tpad;
+    }
     return gemm_run(g, M, st);
 }
 

@@ -62,6 +62,7 @@ enum ConvAct : int { ACT_NONE = 0, ACT_SNAKE = 1, ACT_GELU = 2 };
 // Columns n >= n_valid are tile padding and are not stored.
 struct ConvEpi {
     int T_rows, phases, C_o, n_valid, act;
+    int T_valid;  // rows per stream that exist (0: all T_rows); the rest pad a stream to whole row tiles
     const int32_t* row_slot;
     const __nv_bfloat16* scale;  // per channel, or null
     const float* act_p;          // SnakeBeta: [2][C_o] = exp(alpha), exp(-beta)
@@ -367,8 +368,8 @@ __device__ void gemm_epilogue(const GemmParams& p, float* R, int m0, int per, in
             int* row_o16 = row_o32 + 128;
             for (int i = threadIdx.x; i < per; i += NT) {
                 const int m_g = tile_m * BN + m0 + i;
-                const bool ok = m_g < p.M;
-                const int r = ok ? m_g / e.T_rows : 0;
+                const int r = m_g < p.M ? m_g / e.T_rows : 0;
+                const bool ok = m_g < p.M && (e.T_valid == 0 || m_g - r * e.T_rows < e.T_valid);
                 const int t0 = ok ? (m_g - r * e.T_rows) * e.phases : 0;
                 const int sl = (ok && e.row_slot) ? e.row_slot[r] : r;
                 tok_ok[i] = ok;
@@ -897,8 +898,8 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
             const int tile_m = tile / n_tiles_n, tile_n = tile - tile_m * n_tiles_n;
             if (t < 128) {  // the token rows of this tile in the three views
                 const int m_g = tile_m * BN + t;
-                const bool okm = m_g < p.M;
-                const int r = okm ? m_g / e.T_rows : 0;
+                const int r = m_g < p.M ? m_g / e.T_rows : 0;
+                const bool okm = m_g < p.M && (e.T_valid == 0 || m_g - r * e.T_rows < e.T_valid);
                 const int t0 = okm ? (m_g - r * e.T_rows) * e.phases : 0;
                 const int sl = (okm && e.row_slot) ? e.row_slot[r] : r;
                 tok_ok[t] = okm;
@@ -1136,11 +1137,12 @@ inline int gemm_plan(GemmPlan* g, const void* X, int rows, int K, const void* W,
 }
 
 // Implicit-convolution plan: X is a slot-indexed history buffer H [(slots) * seq_rows][cpad]
-// (bf16, cpad % 64 == 0), K = taps * cpad, rows per stream T % 128 == 0.
+// (bf16, cpad % 64 == 0), K = taps * cpad; a launch needs rows per stream (ix.T) % 128 == 0,
+// which callers reach by padding each stream's rows (ConvEpi::T_valid marks the real ones).
 inline int gemm_plan_implicit(GemmPlan* g, const void* H, int total_rows, int cpad, int taps, int dil, int T,
                               int seq_rows, int max_rows, const void* W, int N, const void* bias, const ConvEpi& e) {
-    if (cpad % 64 != 0 || T % 128 != 0 || N % 128 != 0) {
-        set_error("implicit conv: need channels %% 64 == 0, T %% 128 == 0, N %% 128 == 0");
+    if (cpad % 64 != 0 || N % 128 != 0) {
+        set_error("implicit conv: need channels %% 64 == 0, N %% 128 == 0");
         return QTTS_ERR_UNSUPPORTED;
     }
     const int K = taps * cpad;

@@ -49,7 +49,21 @@ def _p128(x):
     return (x + 127) // 128 * 128
 
 
-def pack_code2wav(cfg: Code2WavConfig, W: Dict[str, torch.Tensor], device) -> Dict[str, torch.Tensor]:
+def implicit_rows(T: int, max_chunk: int) -> bool:
+    """Whether a convolution with T input rows per frame reads the history buffer directly on
+    the device (implicit convolution; its weights then pad each tap's channels to 64): when T
+    is a multiple of 128, or when the largest call (max_chunk frames) has at least 512 rows per
+    stream and pads them to whole 128-row tiles by at most 1/8 (``c2w_implicit_rows`` in
+    ``csrc/code2wav.cuh`` applies the same rule)."""
+    if T % 128 == 0:
+        return True
+    rows = max_chunk * T
+    pad = -(-rows // 128) * 128 - rows
+    return rows >= 512 and pad * 8 <= rows
+
+
+def pack_code2wav(cfg: Code2WavConfig, W: Dict[str, torch.Tensor], device,
+                  max_chunk: int = 1) -> Dict[str, torch.Tensor]:
     """Packed device tensors of the decoder (keys = qtts_c2w_desc field names)."""
     dev = torch.device(device)
     f32 = {k: v.float() for k, v in W.items()}
@@ -77,7 +91,7 @@ def pack_code2wav(cfg: Code2WavConfig, W: Dict[str, torch.Tensor], device) -> Di
         m = m.reshape(o, k * ip)
         return bf(_pad_to(m, n_pad or _p128(o), k_pad or _p64(k * ip)))
 
-    # implicit-convolution blocks (rows per stream a multiple of 128) pad each tap's channels to 64
+    # implicit-convolution blocks (see implicit_rows) pad each tap's channels to 64
     T, t_in, t_blk = 4, [], []
     for r_ in cfg.upsample_rates:
         t_in.append(T)
@@ -136,7 +150,7 @@ def pack_code2wav(cfg: Code2WavConfig, W: Dict[str, torch.Tensor], device) -> Di
         k = f"c2w.decoder.{1 + b}."
         P[f"blk_snake{b}"] = snake(k + "snake.alpha", k + "snake.beta")
         w = f32[k + "transconv.weight"]  # [cin, cout, 2s]
-        cinp = _p64(cin) if t_in[b] % 128 == 0 else cin
+        cinp = _p64(cin) if implicit_rows(t_in[b], max_chunk) else cin
         rows = []
         for ph in range(s):
             r2 = torch.zeros(cout, 2, cinp)
@@ -144,7 +158,7 @@ def pack_code2wav(cfg: Code2WavConfig, W: Dict[str, torch.Tensor], device) -> Di
             r2[:, 1, :cin] = w[:, :, ph].t()      # tap x(i)
             rows.append(r2.reshape(cout, 2 * cinp))
         P[f"blk_tw{b}"] = bf(_pad_to(torch.cat(rows), _p128(s * cout), _p64(2 * cinp)))
-        coutp = _p64(cout) if t_blk[b] % 128 == 0 else cout
+        coutp = _p64(cout) if implicit_rows(t_blk[b], max_chunk) else cout
         bias = torch.zeros(_p128(s * cout))
         bias[:s * cout] = f32[k + "transconv.bias"].repeat(s)
         P[f"blk_tb{b}"] = bf(bias)
@@ -171,7 +185,7 @@ class DeviceCode2Wav:
         self.device = torch.device(device)
         self.max_slots = max_slots
         self.samples_per_frame = cfg.samples_per_frame
-        self.P = pack_code2wav(cfg, weights, self.device)
+        self.P = pack_code2wav(cfg, weights, self.device, max_chunk=max_chunk)
         self.rope_cos, self.rope_sin = rope_tables(cfg.head_dim, cfg.rope_theta, max_frames, self.device)
         P = self.P
         d = _lib.C2wDesc()
