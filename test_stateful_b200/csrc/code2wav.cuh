@@ -251,39 +251,77 @@ __global__ void __launch_bounds__(256) c2w_dwconv_ln_kernel(const float* __restr
 }
 
 // ---------------------------------------------------------------------------
-// last conv (k7, C -> 1) + clamp (code2wav_streaming.py:792-799).  The chunk
-// of 128 outputs and its 6 context rows are staged channel-major in shared
-// memory so that consecutive threads read consecutive rows.
+// last conv (k7, C -> 1) + clamp (code2wav_streaming.py:792-799).  A chunk of
+// 512 outputs and its 6 context rows are staged channel-major in shared memory.
 // ---------------------------------------------------------------------------
-constexpr int kFinalChunk = 128;
+constexpr int kFinalThreads = 128;
+constexpr int kFinalPer = 4;                             // consecutive outputs per thread
+constexpr int kFinalChunk = kFinalThreads * kFinalPer;  // outputs per CTA
+constexpr int kFinalRows = kFinalChunk + 8;             // staged rows (chunk + 6 context, even stride)
 constexpr int kFinalMaxC = 128;
 
-__global__ void __launch_bounds__(kFinalChunk) c2w_final_conv_kernel(const __nv_bfloat16* __restrict__ H,
-                                                                     int seq_rows, int C, int T,
-                                                                     const int32_t* __restrict__ slots,
-                                                                     const float* __restrict__ w, float bias,
-                                                                     float* __restrict__ wav) {
-    __shared__ __nv_bfloat16 s[kFinalMaxC][kFinalChunk + 8];
-    __shared__ float ws[7 * kFinalMaxC];
+inline size_t final_conv_smem(int C) { return (size_t)C * kFinalRows * 2 + (size_t)7 * C * 4; }
+
+// Staged channel-major, s[c][q]: thread t reads rows 4t .. 4t+9 of a channel as five bf16 pairs
+// and accumulates its four outputs from them (28 multiply-adds per 5 loads).
+__global__ void __launch_bounds__(kFinalThreads) c2w_final_conv_kernel(const __nv_bfloat16* __restrict__ H,
+                                                                       int seq_rows, int C, int T,
+                                                                       const int32_t* __restrict__ slots,
+                                                                       const float* __restrict__ w, float bias,
+                                                                       float* __restrict__ wav) {
+    extern __shared__ __align__(16) uint8_t fsm[];
+    __nv_bfloat16* s = reinterpret_cast<__nv_bfloat16*>(fsm);  // [C][kFinalRows]
+    float* ws = reinterpret_cast<float*>(fsm + (size_t)C * kFinalRows * 2);
     const int r = blockIdx.y, t0 = blockIdx.x * kFinalChunk;
     griddep_wait();
     griddep_launch();
     const __nv_bfloat16* base = H + ((size_t)slots[r] * seq_rows + t0) * C;
     const int rows = min(kFinalChunk + 6, T + 6 - t0);
-    for (int i = threadIdx.x; i < rows * C; i += kFinalChunk) {
-        const int q = i / C, c = i - q * C;
-        s[c][q] = base[(size_t)q * C + c];
-    }
-    for (int i = threadIdx.x; i < 7 * C; i += kFinalChunk) ws[i] = w[i];
-    __syncthreads();
-    const int t = t0 + threadIdx.x;
-    if (t >= T) return;
-    float acc = bias;
-    for (int c = 0; c < C; ++c) {
+    const int c8n = C / 8;
+    for (int i = threadIdx.x; i < rows * c8n; i += kFinalThreads) {
+        const int c8 = i / rows, q = i - c8 * rows;  // consecutive threads: consecutive rows
+        const uint4 u = *reinterpret_cast<const uint4*>(base + (size_t)q * C + c8 * 8);
+        const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u);
 #pragma unroll
-        for (int j = 0; j < 7; ++j) acc += ws[j * C + c] * __bfloat162float(s[c][threadIdx.x + j]);
+        for (int k = 0; k < 8; ++k) s[(size_t)(c8 * 8 + k) * kFinalRows + q] = h[k];
     }
-    wav[(size_t)r * T + t] = fminf(fmaxf(acc, -1.0f), 1.0f);
+    for (int i = threadIdx.x; i < 7 * C; i += kFinalThreads) ws[i] = w[i];
+    __syncthreads();
+    const int tl = threadIdx.x * kFinalPer;  // first output of this thread within the chunk
+    if (t0 + tl >= T) return;
+    float acc[kFinalPer];
+#pragma unroll
+    for (int k = 0; k < kFinalPer; ++k) acc[k] = bias;
+    for (int c = 0; c < C; ++c) {
+        const __nv_bfloat162* row = reinterpret_cast<const __nv_bfloat162*>(s + (size_t)c * kFinalRows + tl);
+        float x[kFinalPer + 6];
+#pragma unroll
+        for (int i = 0; i < (kFinalPer + 6) / 2; ++i) {
+            const float2 f = __bfloat1622float2(row[i]);
+            x[2 * i] = f.x;
+            x[2 * i + 1] = f.y;
+        }
+#pragma unroll
+        for (int j = 0; j < 7; ++j) {
+            const float wj = ws[j * C + c];
+#pragma unroll
+            for (int k = 0; k < kFinalPer; ++k) acc[k] += wj * x[k + j];
+        }
+    }
+    float* out = wav + (size_t)r * T + t0 + tl;  // T % 4 == 0: all four outputs exist
+    float4 o;
+    o.x = fminf(fmaxf(acc[0], -1.0f), 1.0f);
+    o.y = fminf(fmaxf(acc[1], -1.0f), 1.0f);
+    o.z = fminf(fmaxf(acc[2], -1.0f), 1.0f);
+    o.w = fminf(fmaxf(acc[3], -1.0f), 1.0f);
+    if ((reinterpret_cast<uintptr_t>(out) & 15) == 0) {
+        *reinterpret_cast<float4*>(out) = o;
+    } else {  // caller buffer not 16-byte aligned
+        out[0] = o.x;
+        out[1] = o.y;
+        out[2] = o.z;
+        out[3] = o.w;
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -491,10 +529,12 @@ inline int c2w_build(qtts_c2w* c) {
         c->K_c1[b] = c->impl_c1[b] ? 7 * c->cpad[b] : pad64(7 * c->cout[b]);
         c->N_c[b] = pad128(c->cout[b]);
     }
-    if (c->cout[3] > kFinalMaxC) {
-        set_error("c2w: last decoder width above %d", kFinalMaxC);
+    if (c->cout[3] > kFinalMaxC || (c->T_blk[3] % 4) != 0) {
+        set_error("c2w: last decoder width above %d or samples per frame not a multiple of 4", kFinalMaxC);
         return QTTS_ERR_UNSUPPORTED;
     }
+    QTTS_CHECK_CUDA(cudaFuncSetAttribute(c2w_final_conv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)final_conv_smem(kFinalMaxC)));
     c->K_pc = pad64(3 * CD);
     c->K_c0 = pad64(7 * LAT);
 
@@ -764,9 +804,9 @@ inline int c2w_step_impl(qtts_c2w* c, const int64_t* codes, int codes_ld, int F,
         }
     }
     const int T3 = F * c->T_blk[3];
-    QTTS_LAUNCH(c2w_final_conv_kernel, dim3(ceil_div(T3, kFinalChunk), n), dim3(kFinalChunk), 0, st,
-                (const __nv_bfloat16*)c->H_fin, 6 + Fm * c->T_blk[3], c->cout[3], T3, slots, d.final_w, d.final_b,
-                wav);
+    QTTS_LAUNCH(c2w_final_conv_kernel, dim3(ceil_div(T3, kFinalChunk), n), dim3(kFinalThreads),
+                final_conv_smem(c->cout[3]), st, (const __nv_bfloat16*)c->H_fin, 6 + Fm * c->T_blk[3], c->cout[3], T3,
+                slots, d.final_w, d.final_b, wav);
     QTTS_LAUNCH(c2w_roll_kernel, dim3(n, c->roll.n, kRollChunks), dim3(128), 0, st, c->roll, slots, F, c->frame);
     return QTTS_OK;
 }
