@@ -74,20 +74,6 @@ inline int launch_rmsnorm(const float* x, int M, int H, int ld, const void* w, f
 // ---------------------------------------------------------------------------
 // row gathers
 // ---------------------------------------------------------------------------
-// out[r * out_ld + c] = table[ids[r * id_ld] * H + c]   (bf16 rows)
-__global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ table, int V, int H,
-                                   const int64_t* __restrict__ ids, int id_ld, __nv_bfloat16* __restrict__ out,
-                                   int out_ld) {
-    const int r = blockIdx.x;
-    griddep_wait();
-    griddep_launch();
-    int64_t id = ids[(size_t)r * id_ld];
-    if (id < 0 || id >= V) id = 0;  // stay in bounds; callers pass sampled (valid) ids
-    const uint4* src = reinterpret_cast<const uint4*>(table + (size_t)id * H);
-    uint4* dst = reinterpret_cast<uint4*>(out + (size_t)r * out_ld);
-    for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = src[i];
-}
-
 // Input of code-predictor stages 1..14: the stage's codec embedding row already projected to the
 // code predictor's width (table = emb_s · W_proj^T + b_proj, computed once at load: the projection
 // is linear and its inputs are a fixed table), written as the residual stream x, plus what the
