@@ -105,6 +105,18 @@ struct NormIn {
     float eps;
 };
 
+// Paired QKV tiles (head_dim 64, two query heads per KV head): the weight rows are ordered
+// per KV head g as tile 2g = [q_{2g}; q_{2g+1}] and tile 2g+1 = [k_g; v_g], and the two tiles of
+// a pair share a cluster (2 x splits).  After the epilogue has stored q and the pool K/V, the
+// q tile's CTAs run the decode attention of their tokens for both heads (keys 0..position of
+// the token's block) and write its output as the o-projection's hi/lo operand.
+struct PairAttn {
+    int on;
+    __nv_bfloat16* out;     // [M][num_heads * 64]
+    __nv_bfloat16* out_lo;
+    float scale_log2;       // log2(e) / sqrt(64)
+};
+
 struct GemmParams {
     int M, N, K;
     int kblocks;   // K / 64
@@ -118,6 +130,7 @@ struct GemmParams {
     ImplicitX ix;
     NormOut nout;
     NormIn nin;
+    PairAttn pair;
 };
 
 template <int BN, int STAGES, bool SPLIT, bool PUSH = false>
@@ -132,9 +145,10 @@ struct GemmLayout {
     // not aliased with the ring, which peers may still be reading from TMA when they push
     static constexpr int RECV_BYTES = PUSH ? BN * 128 * 4 : 0;
     static constexpr int BODY = RING + RECV_BYTES;
-    static constexpr int SCRATCH_BYTES = 5 * 128 * 4;  // epilogue scratch: [0,136) norm sums / RoPE exchange,
+    static constexpr int SCRATCH_BYTES = 7 * 128 * 4;  // epilogue scratch: [0,136) norm sums / RoPE exchange,
                                                         // [256,512) token metadata, [0,512) norm-out sums,
-                                                        // [512,640) per-token inv_rms of the norm-in
+                                                        // [512,640) per-token inv_rms of the norm-in,
+                                                        // [640,896) paired-QKV attention metadata
     static constexpr int BAR_BYTES = 256;
     static constexpr int SMEM = 1024 + BODY + SCRATCH_BYTES + BAR_BYTES;
     static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "stage buffers must keep 1024-B alignment");
@@ -279,7 +293,16 @@ __device__ void gemm_epilogue(const GemmParams& p, float* R, int m0, int per, in
                 const int k_rows = e.kv_heads * D;
                 const int d = n_g % D;
                 const int warp = t >> 5, lane = t & 31;
-                const int region = n_g < q_rows ? 0 : (n_g < q_rows + k_rows ? 1 : 2);
+                // region (q / k / v) and the column within it; paired tiles: tile 2g = q heads 2g, 2g+1,
+                // tile 2g+1 = k_g then v_g
+                int region, col;
+                if (p.pair.on) {
+                    region = (tile_n & 1) ? (t < 64 ? 1 : 2) : 0;
+                    col = (tile_n & 1) ? (tile_n >> 1) * 64 + (t & 63) : (tile_n >> 1) * 128 + t;
+                } else {
+                    region = n_g < q_rows ? 0 : (n_g < q_rows + k_rows ? 1 : 2);
+                    col = region == 0 ? n_g : (region == 1 ? n_g - q_rows : n_g - q_rows - k_rows);
+                }
                 const __nv_bfloat16* nw = region == 0 ? (const __nv_bfloat16*)e.q_norm_w
                                                       : (const __nv_bfloat16*)e.k_norm_w;
                 const float wn = region < 2 ? __bfloat162float(nw[d]) : 0.f;
@@ -292,9 +315,7 @@ __device__ void gemm_epilogue(const GemmParams& p, float* R, int m0, int per, in
                 // per-token position and KV row base, written by the kernel before the reduction
                 const int* tok_pos = reinterpret_cast<const int*>(scratch) + 256;
                 const int* tok_kv = tok_pos + 128;
-                const int kv_col = region == 0 ? 0
-                                                : (((region - 1) * e.kv_heads) + (n_g - q_rows - (region == 2 ? k_rows : 0)) / D) *
-                                                      e.block_size;
+                const int kv_col = region == 0 ? 0 : (((region - 1) * e.kv_heads) + col / D) * e.block_size;
                 const float inv_d = 1.0f / (float)D;  // D is a power of two: exact
                 // 8 tokens at a time: RoPE table loads, head norms and stores of the 8 overlap;
                 // two barriers per 8 tokens (norm sums, RoPE partner exchange through R)
@@ -348,7 +369,7 @@ __device__ void gemm_epilogue(const GemmParams& p, float* R, int m0, int per, in
                             val = d < half ? val * cs[k] - partner * sn[k] : val * cs[k] + partner * sn[k];
                         }
                         if (region == 0) {
-                            reinterpret_cast<float*>(p.out)[(size_t)m_g * q_rows + n_g] = val;  // q stays fp32
+                            reinterpret_cast<float*>(p.out)[(size_t)m_g * q_rows + col] = val;  // q stays fp32
                         } else if (tok_kv[i] >= 0) {
                             reinterpret_cast<kv_t*>(e.kv_pool)[(size_t)(tok_kv[i] + kv_col) * D + d] = to_kv(val);
                         }
@@ -458,6 +479,97 @@ __device__ void gemm_epilogue(const GemmParams& p, float* R, int m0, int per, in
     }
 }
 
+// Decode attention of a paired QKV launch (see PairAttn), run after the pair's epilogues have
+// stored q (fp32, p.out) and this step's K/V into the pool: the eight warps of the pair take
+// tokens gw, gw + 8, ... of the CTA's token slice; a warp loads the token's keys and values
+// 0..nk-1 for KV head g (lane l owns dims 2l, 2l+1), scores both query heads, softmax, and
+// writes the two heads' outputs as a bf16 hi/lo pair.  Same math as short_attn_kernel.
+template <int BN>
+__device__ void pair_attention(const GemmParams& p, int m0, int per, int tile_n, int tile_m, int pm,
+                               const float* scratch) {
+    const qtts_qkv_epilogue& e = p.qkv;
+    const int* tok_kb = reinterpret_cast<const int*>(scratch) + 640;
+    const int* tok_nk = tok_kb + 128;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = tile_n >> 1, h0 = 2 * g;
+    const int q_cols = e.num_heads * 64;
+    const kv_t* kv = reinterpret_cast<const kv_t*>(e.kv_pool);
+    const float* q = reinterpret_cast<const float*>(p.out);
+    for (int i = pm * 4 + warp; i < per; i += 8) {
+        const int m_g = tile_m * BN + m0 + i;
+        if (m_g >= p.M) break;
+        const int nk = min(tok_nk[i], 16);
+        const size_t orow = (size_t)m_g * q_cols + h0 * 64 + 2 * lane;
+        if (nk <= 0) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                *reinterpret_cast<__nv_bfloat162*>(p.pair.out + orow + h * 64) = __floats2bfloat162_rn(0.f, 0.f);
+                *reinterpret_cast<__nv_bfloat162*>(p.pair.out_lo + orow + h * 64) = __floats2bfloat162_rn(0.f, 0.f);
+            }
+            continue;
+        }
+        const size_t krow = (size_t)tok_kb[i] + (size_t)g * e.block_size;
+        const size_t vrow = (size_t)tok_kb[i] + (size_t)(e.kv_heads + g) * e.block_size;
+        __half2 kr[16], vr[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            // L2 loads (.cg): this step's rows were stored by the other CTA of the pair
+            kr[j] = j < nk ? __ldcg(reinterpret_cast<const __half2*>(kv + (krow + j) * 64 + 2 * lane)) : __float2half2_rn(0.f);
+            vr[j] = j < nk ? __ldcg(reinterpret_cast<const __half2*>(kv + (vrow + j) * 64 + 2 * lane)) : __float2half2_rn(0.f);
+        }
+        const float2 qa = __ldcg(reinterpret_cast<const float2*>(q + orow));
+        const float2 qb = __ldcg(reinterpret_cast<const float2*>(q + orow + 64));
+        float sa[16], sb[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const float2 k = __half22float2(kr[j]);
+            sa[j] = qa.x * k.x + qa.y * k.y;
+            sb[j] = qb.x * k.x + qb.y * k.y;
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                sa[j] += __shfl_xor_sync(0xffffffffu, sa[j], off);
+                sb[j] += __shfl_xor_sync(0xffffffffu, sb[j], off);
+            }
+        }
+        float ma = -INFINITY, mb = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            sa[j] *= p.pair.scale_log2;
+            sb[j] *= p.pair.scale_log2;
+            if (j < nk) {
+                ma = fmaxf(ma, sa[j]);
+                mb = fmaxf(mb, sb[j]);
+            }
+        }
+        float la = 0.f, lb = 0.f, oa0 = 0.f, oa1 = 0.f, ob0 = 0.f, ob1 = 0.f;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const float pa = j < nk ? exp2f(sa[j] - ma) : 0.f;
+            const float pb = j < nk ? exp2f(sb[j] - mb) : 0.f;
+            const float2 v = __half22float2(vr[j]);
+            la += pa;
+            lb += pb;
+            oa0 += pa * v.x;
+            oa1 += pa * v.y;
+            ob0 += pb * v.x;
+            ob1 += pb * v.y;
+        }
+        const float ia = 1.0f / la, ib = 1.0f / lb;
+        const float o[4] = {oa0 * ia, oa1 * ia, ob0 * ib, ob1 * ib};
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const __nv_bfloat162 hi = __floats2bfloat162_rn(o[2 * h], o[2 * h + 1]);
+            const float2 hf = __bfloat1622float2(hi);
+            *reinterpret_cast<__nv_bfloat162*>(p.pair.out + orow + h * 64) = hi;
+            *reinterpret_cast<__nv_bfloat162*>(p.pair.out_lo + orow + h * 64) =
+                __floats2bfloat162_rn(o[2 * h] - hf.x, o[2 * h + 1] - hf.y);
+        }
+    }
+}
+
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
@@ -480,7 +592,10 @@ __global__ void __launch_bounds__(NT) gemm_tc_kernel(const __grid_constant__ CUt
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tile_n = blockIdx.x, tile_m = blockIdx.z;
-    const int split = (int)cluster_ctarank();  // cluster is (1, splits, 1): rank == blockIdx.y
+    // cluster (1, splits, 1): rank = split; paired QKV tiles: (2, splits, 1), rank = member + 2 * split
+    const int crank = (int)cluster_ctarank();
+    const int split = p.pair.on ? crank >> 1 : crank;
+    const int pm = p.pair.on ? crank & 1 : 0;  // 0: the q tile of the pair, 1: the k|v tile
     const int per_split = p.kblocks / p.splits, rem = p.kblocks % p.splits;
     const int kb0 = split * per_split + min(split, rem);
     const int nkb = per_split + (split < rem ? 1 : 0);
@@ -655,9 +770,12 @@ __global__ void __launch_bounds__(NT) gemm_tc_kernel(const __grid_constant__ CUt
             const int pos = m_g < p.M ? e.row_pos[m_g] : 0;
             const int slot = m_g < p.M ? e.slot_mapping[m_g] : -1;
             tok_pos[i] = pos < 0 ? 0 : (pos >= e.max_pos ? e.max_pos - 1 : pos);  // table bounds
-            tok_kv[i] = slot < 0 ? -1
-                                 : ((slot / e.block_size) * e.num_layers + e.layer) * 2 * e.kv_heads * e.block_size +
-                                       slot % e.block_size;
+            const int kb = slot < 0 ? 0 : ((slot / e.block_size) * e.num_layers + e.layer) * 2 * e.kv_heads * e.block_size;
+            tok_kv[i] = slot < 0 ? -1 : kb + slot % e.block_size;
+            if (p.pair.on) {  // the token's block (keys 0 .. its offset) for the pair's attention
+                reinterpret_cast<int*>(scratch)[640 + i] = kb;
+                reinterpret_cast<int*>(scratch)[768 + i] = slot < 0 ? 0 : slot % e.block_size + 1;
+            }
         }
     }
     float pre_old[8];
@@ -705,8 +823,9 @@ __global__ void __launch_bounds__(NT) gemm_tc_kernel(const __grid_constant__ CUt
 #pragma unroll
             for (int r = 0; r < 8; ++r) {
                 if (r < p.splits) {
-                    v[0][r] = ld_dsmem_f32x4(map_to_rank(base + (uint32_t)e * 16u, (uint32_t)r));
-                    if (two) v[1][r] = ld_dsmem_f32x4(map_to_rank(base + (uint32_t)e2 * 16u, (uint32_t)r));
+                    const uint32_t peer = p.pair.on ? (uint32_t)(2 * r + pm) : (uint32_t)r;
+                    v[0][r] = ld_dsmem_f32x4(map_to_rank(base + (uint32_t)e * 16u, peer));
+                    if (two) v[1][r] = ld_dsmem_f32x4(map_to_rank(base + (uint32_t)e2 * 16u, peer));
                 }
             }
 #pragma unroll
@@ -725,13 +844,22 @@ __global__ void __launch_bounds__(NT) gemm_tc_kernel(const __grid_constant__ CUt
                 *reinterpret_cast<float4*>(P + m0 * 128 + (h ? e2 : e) * 4) = acc;
             }
         }
-        cluster_arrive();  // done reading the peers' shared memory
+        if (!p.pair.on) cluster_arrive();  // done reading the peers' shared memory
         __syncthreads();
     } else if (p.nin.ss || p.epilogue == QTTS_EPI_QKV_ROPE) {
         __syncthreads();
     }
     gemm_epilogue<BN, NT>(p, P, m0, per, tile_n, tile_m, scratch, prefetch ? pre_old : nullptr);
-    if (p.splits > 1 && !push) cluster_wait();  // no CTA leaves while a peer may still read its shared memory
+    if (p.pair.on) {
+        // both tiles' stores (q, pool K/V) reach the cluster before either reads them; this
+        // barrier also covers "done reading the peers' shared memory"
+        __syncthreads();
+        cluster_arrive();
+        cluster_wait();
+        if constexpr (NT == 128) pair_attention<BN>(p, m0, per, tile_n, tile_m, pm, scratch);
+    } else if (p.splits > 1 && !push) {
+        cluster_wait();  // no CTA leaves while a peer may still read its shared memory
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -1023,6 +1151,17 @@ inline bool gemm_persist_enabled() {
     return on;
 }
 
+// Paired QKV launches use clusters of 2 x splits CTAs; above 8 (portable) the kernel opts in to
+// non-portable cluster sizes (up to 16).  QTTS_GEMM_PAIR_SPLITS caps splits (default 8).
+inline int gemm_pair_max_splits() {
+    static const int s = [] {
+        const char* v = getenv("QTTS_GEMM_PAIR_SPLITS");
+        const int x = (v && *v) ? atoi(v) : 8;
+        return x < 1 ? 1 : (x > 8 ? 8 : x);
+    }();
+    return s;
+}
+
 inline bool gemm_push_enabled() {
     static const bool on = [] {
         const char* v = getenv("QTTS_GEMM_PUSH");
@@ -1075,10 +1214,11 @@ inline int launch_gemm_t(const CUtensorMap& mw, const CUtensorMap& mx, const CUt
     static bool attr_done = false;
     if (!attr_done) {
         QTTS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM));
+        QTTS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
         attr_done = true;
     }
     QTTS_CHECK_CUDA(launch_pdl(kern, dim3(p.N / 128, p.splits, ceil_div(p.M, BN)), dim3(NT, 1, 1), L::SMEM, st,
-                               dim3(1, p.splits, 1), mw, mx, mxlo, p));
+                               dim3(p.pair.on ? 2 : 1, p.splits, 1), mw, mx, mxlo, p));
     return QTTS_OK;
 }
 
@@ -1208,6 +1348,7 @@ inline int gemm_run(GemmPlan g, int M, cudaStream_t st, void* out = nullptr) {
     }
     g.p.M = M;
     g.p.splits = pick_splits(g.p.N, M, g.p.K, bn);
+    if (g.p.pair.on && g.p.splits > gemm_pair_max_splits()) g.p.splits = gemm_pair_max_splits();
     if (out) g.p.out = out;
     // Opt-in (QTTS_GEMM_PUSH=1): split-K launches that fit one CTA per SM reduce by
     // pushing partials from registers into the owner's receive buffer (5-stage ring +
@@ -1215,7 +1356,7 @@ inline int gemm_run(GemmPlan g, int M, cudaStream_t st, void* out = nullptr) {
     // 196 KB footprint keeps the next kernel's CTAs off the SM until this one exits, so
     // programmatic dependent launch no longer overlaps their weight prefetch, and the
     // remote stores cost about what the pull's remote loads do.
-    const bool push = bn == 64 && g.p.splits > 1 && 64 % g.p.splits == 0 && gemm_push_enabled() &&
+    const bool push = bn == 64 && g.p.splits > 1 && 64 % g.p.splits == 0 && !g.p.pair.on && gemm_push_enabled() &&
                       (g.p.N / 128) * g.p.splits * ceil_div(M, bn) <= num_sms();
     if (push) {
         if (g.split) return launch_gemm_t<64, 5, true, 128, true>(g.mw, g.mx64, g.mlo64, g.p, st);

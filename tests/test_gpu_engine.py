@@ -264,3 +264,16 @@ def test_full_width_code_predictor_stage_logits():
     assert talk.worst <= LOGIT_TOL
     assert cpt.worst <= LOGIT_TOL
     assert cpt.rate >= 0.95  # 90 argmaxes; near-ties of random weights may flip a few
+
+
+@pytest.mark.skipif(os.environ.get("QTTS_CP_PAIR") is not None, reason="already the forced run")
+def test_engine_with_fused_code_predictor_attention():
+    """The paired-QKV form (decode attention fused into the code predictor's QKV GEMM) is opt-in
+    (QTTS_CP_PAIR=1, read when an engine is built); rerun this file's parity cases with it on."""
+    import subprocess
+    import sys
+
+    env = dict(os.environ, QTTS_CP_PAIR="1")
+    r = subprocess.run([sys.executable, "-m", "pytest", "-x", "-q", "-m", "gpu", "-p", "no:cacheprovider",
+                        os.path.abspath(__file__)], env=env, capture_output=True, text=True, timeout=1200)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
