@@ -12,9 +12,10 @@
 //
 // Activation precision: at decode the MMA pipe is idle (the kernel waits on
 // weight bytes), so an activation operand can be carried as a bf16 pair
-// hi + lo (hi = bf16(x), lo = bf16(x - hi)); the UMMA issuer then runs two
-// MMAs per k-slice on the same weight tile and TMEM accumulates W·hi + W·lo,
-// recovering ~16 mantissa bits of the fp32 activation for no extra HBM bytes.
+// hi + lo (hi = bf16(x), lo = bf16(x - hi)); the lo tile follows the hi tile in
+// shared memory, so one UMMA of N = 2·BN per k-slice puts W·hi and W·lo in
+// adjacent TMEM columns, which the staging adds: ~16 mantissa bits of the fp32
+// activation for no extra HBM bytes.
 //
 // Roles in a 128- (or 256-) thread CTA: warp 0 lane 0 issues TMA loads into a
 // STAGES-deep ring (full/empty mbarriers), warp 1 lane 0 issues UMMAs and
@@ -623,7 +624,7 @@ __global__ void __launch_bounds__(NT) gemm_tc_kernel(const __grid_constant__ CUt
     griddep_wait();  // activations, outputs and the KV pool belong to earlier kernels
     griddep_launch();
     if (warp == 2) {
-        tmem_alloc(tmem_slot, BN);
+        tmem_alloc(tmem_slot, SPLIT ? 2 * BN : BN);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -664,7 +665,9 @@ __global__ void __launch_bounds__(NT) gemm_tc_kernel(const __grid_constant__ CUt
         flags[1] = issued;
     } else if (warp == 1 && lane == 0) {
         // ---------------- UMMA issuer ----------------
-        const uint32_t idesc = make_idesc_bf16(128, BN);
+        // hi/lo operands: the lo tile sits right after the hi tile, so one UMMA of N = 2 BN
+        // accumulates W·hi into columns [0, BN) and W·lo into [BN, 2 BN); staging adds them
+        const uint32_t idesc = make_idesc_bf16(128, SPLIT ? 2 * BN : BN);
         int consumed = 0;
         for (int i = 0; i < nkb; ++i) {
             const int s = i % STAGES;
@@ -677,12 +680,9 @@ __global__ void __launch_bounds__(NT) gemm_tc_kernel(const __grid_constant__ CUt
             const uint32_t a = smem_u32(smem + s * L::STAGE_BYTES);
             const uint64_t da = make_sw128_desc(a);
             const uint64_t db = make_sw128_desc(a + L::A_BYTES);
-            const uint64_t dl = make_sw128_desc(a + L::A_BYTES + L::B_BYTES);
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {  // 4 x UMMA_K(16) = 64; +32 B per step inside the swizzle atom
+            for (int kk = 0; kk < 4; ++kk)  // 4 x UMMA_K(16) = 64; +32 B per step inside the swizzle atom
                 umma_bf16(tmem, da + 2 * kk, db + 2 * kk, idesc, (i > 0 || kk > 0) ? 1u : 0u);
-                if (SPLIT) umma_bf16(tmem, da + 2 * kk, dl + 2 * kk, idesc, 1u);
-            }
             umma_commit(&empty[s]);
             ++consumed;
         }
@@ -721,6 +721,12 @@ __global__ void __launch_bounds__(NT) gemm_tc_kernel(const __grid_constant__ CUt
         for (int c = half * COLS; c < (half + 1) * COLS; c += 16) {
             float v[16];
             tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c, v);
+            if (SPLIT) {
+                float vl[16];
+                tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(c + BN), vl);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] += vl[j];
+            }
             if (push) {
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
@@ -739,7 +745,7 @@ __global__ void __launch_bounds__(NT) gemm_tc_kernel(const __grid_constant__ CUt
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 2) tmem_dealloc(tmem, BN);
+    if (warp == 2) tmem_dealloc(tmem, SPLIT ? 2 * BN : BN);
 
     // ---------------- split-K reduction across the cluster ----------------
     // pull: arrive = this CTA's partial is in its shared memory; push: arrive = this

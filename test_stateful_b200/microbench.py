@@ -69,7 +69,7 @@ def bench_attention(rows: int, ctx_mean: int, launches: int, layers: int = 4, se
             "algorithmic_bytes": algo, "achieved_gbs": algo / sec / 1e9}
 
 
-def bench_gemm(n: int, k: int, m: int, launches: int, seed: int = 0):
+def bench_gemm(n: int, k: int, m: int, launches: int, seed: int = 0, plain: bool = False):
     dev = "cuda"
     g = torch.Generator(device=dev).manual_seed(seed)
     copies = max(2, -(-300_000_000 // (n * k * 2)))  # > 2x L2 of distinct weights
@@ -77,6 +77,8 @@ def bench_gemm(n: int, k: int, m: int, launches: int, seed: int = 0):
     x = torch.randn(m, k, generator=g, device=dev)
     hi, lo = ops.split_hilo(x)
     out = torch.empty(m, n, device=dev)
+    if plain:  # one bf16 MMA per k-slice instead of the hi/lo pair
+        lo = None
     for i in range(3):
         ops.gemm(hi, ws[i % copies], _lib.EPI_F32, out=out, x_lo=lo)
     torch.cuda.synchronize()
@@ -96,7 +98,8 @@ def bench_gemm(n: int, k: int, m: int, launches: int, seed: int = 0):
         s.synchronize()
     sec = e0.elapsed_time(e1) / 1e3 / launches
     algo = n * k * 2 + m * k * 4 + m * n * 4
-    return {"kernel": "gemm_tc_kernel<64,3,split>", "n": n, "k": k, "m": m, "launch_us": sec * 1e6,
+    return {"kernel": "gemm_tc_kernel<64,4,bf16>" if plain else "gemm_tc_kernel<64,3,hi/lo>", "n": n, "k": k,
+            "m": m, "launch_us": sec * 1e6,
             "algorithmic_bytes": algo, "achieved_gbs": algo / sec / 1e9,
             "tflops": 2 * 2 * m * n * k / sec / 1e12}
 
@@ -158,13 +161,14 @@ def main():
     ap.add_argument("--launches", type=int, default=50)
     ap.add_argument("--split", type=int, default=0, help="attention: KV blocks per split (0: library default)")
     ap.add_argument("--chunk", type=int, default=1, help="code2wav: frames per stream per call")
+    ap.add_argument("--plain", action="store_true", help="gemm: plain bf16 activations (no lo operand)")
     a = ap.parse_args()
     if a.what == "attention":
         r = bench_attention(a.rows, a.ctx_mean, a.launches, split=a.split)
     elif a.what == "code2wav":
         r = bench_code2wav(a.rows, a.launches, chunk=a.chunk)
     else:
-        r = bench_gemm(a.n, a.k, a.m, a.launches)
+        r = bench_gemm(a.n, a.k, a.m, a.launches, plain=a.plain)
     print(json.dumps(r))
 
 
