@@ -402,6 +402,11 @@ int qtts_c2w_step(qtts_c2w* c, const int64_t* codes, int codes_ld, int frames, c
                   float* wav, qtts_stream_t stream);
 /* Kernels the last qtts_c2w_step enqueued (host counter). */
 int qtts_c2w_launches(const qtts_c2w* c);
+/* background != 0: the decoder's steps run beside a latency-critical stream (the executor runs
+ * step t's code2wav while step t+1's talker runs), so its kernels launch without programmatic
+ * dependent launch: a waiting kernel's CTAs would otherwise hold SMs the other stream needs.
+ * Default 0.  No counterpart in the reference (its code2wav is inside the fused plan). */
+int qtts_c2w_set_background(qtts_c2w* c, int background);
 
 #ifdef __cplusplus
 }

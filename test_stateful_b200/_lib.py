@@ -103,6 +103,7 @@ EXPORTS = [
     "qtts_codec_sum",
     "qtts_engine_create", "qtts_engine_destroy", "qtts_engine_step",
     "qtts_c2w_create", "qtts_c2w_destroy", "qtts_c2w_reset", "qtts_c2w_step", "qtts_c2w_launches",
+    "qtts_c2w_set_background",
 ]
 
 _lib = None
@@ -149,6 +150,7 @@ def load() -> C.CDLL:
         "qtts_c2w_reset": ([P, P, C.c_int, P], C.c_int),
         "qtts_c2w_step": ([P, P, C.c_int, C.c_int, P, C.c_int, P, P], C.c_int),
         "qtts_c2w_launches": ([P], C.c_int),
+        "qtts_c2w_set_background": ([P, C.c_int], C.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)

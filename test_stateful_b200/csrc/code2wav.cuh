@@ -395,6 +395,7 @@ __global__ void __launch_bounds__(128) c2w_reset_kernel(const __grid_constant__ 
 // ---------------------------------------------------------------------------
 struct qtts_c2w {
     qtts_c2w_desc d;
+    bool background = false;   // launches without programmatic dependent launch (qtts_c2w_set_background)
     int S;                     // max streams per step (= max slots)
     int Fm;                    // max frames per stream per call (chunk)
     int T_up[2], T_in[4], T_blk[4], cin[4], cout[4];  // rows per stream per FRAME
@@ -814,7 +815,9 @@ inline int c2w_step_impl(qtts_c2w* c, const int64_t* codes, int codes_ld, int F,
 inline int c2w_step(qtts_c2w* c, const int64_t* codes, int codes_ld, int F, const int32_t* slots, int n, float* wav,
                     cudaStream_t st) {
     const int before = g_launch_count;
+    if (c->background) ++g_pdl_suppress;
     const int rc = c2w_step_impl(c, codes, codes_ld, F, slots, n, wav, st);
+    if (c->background) --g_pdl_suppress;
     c->launches = g_launch_count - before;
     return rc;
 }

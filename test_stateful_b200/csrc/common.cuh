@@ -326,6 +326,12 @@ inline bool pdl_enabled() {
     return on;
 }
 
+// Launches made while this is non-zero go without programmatic dependent launch (a code2wav
+// decoder marked as background: its CTAs would otherwise sit resident, holding shared memory,
+// while they wait for their predecessor, keeping a concurrent stream's CTAs off those SMs).
+// Host-side state of the one engine thread (as the reference's executor).
+inline int g_pdl_suppress = 0;
+
 // Launch with the programmatic-serialization attribute (and an optional cluster shape).
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
@@ -337,7 +343,7 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
     cfg.stream = st;
     cudaLaunchAttribute attr[2];
     int n = 0;
-    if (pdl_enabled()) {
+    if (pdl_enabled() && !g_pdl_suppress) {
         attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
         attr[n].val.programmaticStreamSerializationAllowed = 1;
         ++n;

@@ -298,6 +298,12 @@ int qtts_c2w_step(qtts_c2w* c, const int64_t* codes, int codes_ld, int frames, c
 
 int qtts_c2w_launches(const qtts_c2w* c) { return c ? c->launches : 0; }
 
+int qtts_c2w_set_background(qtts_c2w* c, int background) {
+    QTTS_REQUIRE(c, "c2w_set_background: null decoder");
+    c->background = background != 0;
+    return QTTS_OK;
+}
+
 }  // extern "C"
 
 // ---------------------------------------------------------------------------

@@ -224,6 +224,11 @@ class DeviceCode2Wav:
         self.handle = h
         self.last_launches = 0
 
+    def set_background(self, on: bool = True) -> None:
+        """Mark the decoder as running beside a latency-critical stream (its kernels then launch
+        without programmatic dependent launch; see ``qtts_c2w_set_background``)."""
+        _lib.check(_lib.load().qtts_c2w_set_background(self.handle, int(bool(on))), "c2w_set_background")
+
     def reset(self, slots: torch.Tensor, stream=None) -> None:
         """Start new streams (frame 0, zero conv/transconv state) on ``slots`` (device int32)."""
         lib = _lib.load()

@@ -189,6 +189,7 @@ class B200Executor:
                 # one frame per decode step plus the prefill frame
                 self._c2w = DeviceCode2Wav(cfg.c2w, Wc, self._device, max_slots=self._max_batch,
                                            max_frames=self._max_seq_len + 1)
+                self._c2w.set_background(True)  # runs beside the next step's talker (stream B)
         self._weights = None
         self._c2w_weights = None
         self._alloc_state()
