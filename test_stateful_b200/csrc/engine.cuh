@@ -464,11 +464,7 @@ inline int engine_step_impl(qtts_engine* e, const qtts_step_io& io, cudaStream_t
                         (const __nv_bfloat16*)e->hid_lo, bf(d.w_codec_emb, 0), d.vocab, H, codes_in, G, e->cp_in,
                         e->cp_in_lo);
             QTTS_TRY(run_plan(e->cp_proj_pair, rows, st));
-        } else {
-            QTTS_LAUNCH(cp_embed_rows_kernel, dim3(nr), dim3(256), 0, st,
-                        (const float*)e->cp_tab + (size_t)(s - 1) * d.cp_vocab * cH, d.cp_vocab, cH, codes_in + s, G,
-                        bf(d.cp_w_in_norm, 0), e->cx, e->cxn, e->cxn_lo, e->css);
-        }
+        }  // stages 1..: the previous stage's sampling kernel wrote the input (next_table below)
         cap.row_slot = m + 3 * crows;
         cap.row_ctx = m + 2 * crows;
         cap.R = rows;
@@ -509,6 +505,18 @@ inline int engine_step_impl(qtts_engine* e, const qtts_step_io& io, cudaStream_t
         cs.eos_id = -1;
         cs.tok_out = io.full_codec_out + 1 + s;
         cs.tok_ld = G;
+        if (s + 1 < d.cp_stages) {  // the next stage's input: its projected embedding of this code
+            cs.next_table = (const float*)e->cp_tab + (size_t)s * d.cp_vocab * cH;
+            cs.next_V = d.cp_vocab;
+            cs.next_H = cH;
+            cs.next_ids = codes_in + 1 + s;
+            cs.next_ld = G;
+            cs.next_gamma = bf(d.cp_w_in_norm, 0);
+            cs.next_x = e->cx;
+            cs.next_xn = e->cxn;
+            cs.next_xn_lo = e->cxn_lo;
+            cs.next_ss = e->css;
+        }
         QTTS_TRY(launch_sample(cs, st));
         if (io.cp_logits_out)
             QTTS_CHECK_CUDA(cudaMemcpy2DAsync(io.cp_logits_out + (size_t)s * d.cp_vocab,

@@ -18,6 +18,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "small_ops.cuh"
 
 namespace qtts {
 
@@ -37,6 +38,17 @@ struct SampleParams {
     int eos_id;
     int64_t* tok_out;
     int tok_ld;
+    // code predictor: after sampling, the CTA of row r also writes the next stage's input,
+    // embed_projected_row(table, next_ids[r * next_ld]) (table null: off)
+    const float* next_table;
+    int next_V, next_H;
+    const int64_t* next_ids;  // the sampled token's slot, or a forced code
+    int next_ld;
+    const __nv_bfloat16* next_gamma;
+    float* next_x;
+    __nv_bfloat16* next_xn;
+    __nv_bfloat16* next_xn_lo;
+    float* next_ss;
 };
 
 __device__ __forceinline__ uint32_t float_key(float f) {
@@ -316,6 +328,11 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
             p.tok_out[(size_t)r * p.tok_ld] = tok;
             if (cnt_rw) cnt_rw[tok] += 1;
         }
+    }
+    if (p.next_table) {
+        __syncthreads();  // thread 0's token store is visible to the block
+        embed_projected_row(p.next_table, p.next_V, p.next_H, p.next_ids[(size_t)r * p.next_ld], p.next_gamma,
+                            p.next_x, p.next_xn, p.next_xn_lo, p.next_ss, r);
     }
 }
 

@@ -78,15 +78,12 @@ inline int launch_rmsnorm(const float* x, int M, int H, int ld, const void* w, f
 // code predictor's width (table = emb_s · W_proj^T + b_proj, computed once at load: the projection
 // is linear and its inputs are a fixed table), written as the residual stream x, plus what the
 // first layer's folded input norm needs: the bf16 pair of x∘γ and per-128-column sums of x².
-// One CTA per row; warp w of an iteration covers the 128 columns of tile (w + iteration·warps).
-__global__ void cp_embed_rows_kernel(const float* __restrict__ table, int V, int H, const int64_t* __restrict__ ids,
-                                     int id_ld, const __nv_bfloat16* __restrict__ gamma, float* __restrict__ x,
-                                     __nv_bfloat16* __restrict__ xn, __nv_bfloat16* __restrict__ xn_lo,
-                                     float* __restrict__ ss) {
-    const int r = blockIdx.x;
-    griddep_wait();
-    griddep_launch();
-    int64_t id = ids[(size_t)r * id_ld];
+// Run by the whole CTA of row r (the code predictor's sampling kernel, right after it picks the
+// code); warp w of an iteration covers the 128 columns of tile (w + iteration·warps).
+__device__ __forceinline__ void embed_projected_row(const float* __restrict__ table, int V, int H, int64_t id,
+                                                    const __nv_bfloat16* __restrict__ gamma, float* __restrict__ x,
+                                                    __nv_bfloat16* __restrict__ xn, __nv_bfloat16* __restrict__ xn_lo,
+                                                    float* __restrict__ ss, int r) {
     if (id < 0 || id >= V) id = 0;  // stay in bounds; callers pass sampled (valid) ids
     const float4* src = reinterpret_cast<const float4*>(table + (size_t)id * H);
     for (int c4 = threadIdx.x; c4 < H / 4; c4 += blockDim.x) {
@@ -107,6 +104,7 @@ __global__ void cp_embed_rows_kernel(const float* __restrict__ table, int V, int
         if ((threadIdx.x & 31) == 0) ss[(size_t)r * (H / 128) + c4 / 32] = sq;
     }
 }
+
 
 // Stage-0 input of the code predictor: rows [2b] = hidden[b], [2b+1] = codec_emb[tok0[b]]
 // (CodePredictorUnrolled.forward, utils.py:1019-1020), as a hi/lo operand pair
