@@ -161,3 +161,20 @@ def test_two_rank_gloo_routing_and_max_timing():
     assert sorted(mine0 + mine1) == sorted(f"s{i}" for i in range(10))
     assert n0 == n1 == 10
     assert w0 == w1 == 2.5
+
+
+def test_code2wav_implicit_convolution_rule():
+    """Which code2wav convolutions read the history buffer directly (and so get 64-channel
+    padded taps in their packed weights): rows per frame a multiple of 128, or a largest call
+    of >= 512 rows per stream padded to whole 128-row tiles by at most 1/8 (the device rule,
+    ``c2w_implicit_rows``)."""
+    from test_stateful_b200.runtime.code2wav import implicit_rows
+
+    t_in, t_blk = [4, 32, 160, 640], [32, 160, 640, 1920]  # decoder blocks, rows per frame
+    assert [implicit_rows(t, 1) for t in t_in] == [False, False, False, True]
+    assert [implicit_rows(t, 1) for t in t_blk] == [False, False, True, True]
+    assert [implicit_rows(t, 25) for t in t_in] == [False, True, True, True]   # 100 < 512 rows
+    assert [implicit_rows(t, 25) for t in t_blk] == [True, True, True, True]   # 800 -> 896: 12 %
+    assert implicit_rows(100, 6)       # 600 rows -> 640: pads 40 <= 600 / 8
+    assert not implicit_rows(70, 7)    # 490 rows: below 512
+    assert not implicit_rows(40, 13)   # 520 rows -> 640: pads 120 > 65
