@@ -103,7 +103,8 @@ class GPUFuture:
         eos_id = self._executor._config.talker.codec_eos_id if self._executor else 2150
         eos = (codes[:, 0] == eos_id).tolist() if codes is not None else [False] * n
         if self._wav_host is not None:
-            audio = [self._wav_host[i].numpy().tobytes() for i in range(n)]
+            wav = self._wav_host[:n].numpy()  # one view of the pinned buffer, then a bytes copy per row
+            audio = [wav[i].tobytes() for i in range(n)]
         else:
             audio = [None] * n
         return StepOutput(slots=self._slots, eos_flags=eos, audio_chunks=audio,
@@ -445,8 +446,7 @@ class B200Executor:
         timing loops that replay the same batch); returns the launches per step."""
         n = len(slots)
         for par in (0, 1):
-            for i, s in enumerate(slots):
-                self.slots_host_buf[par][i] = s.slot_id
+            self.slots_host_buf[par][:n].numpy()[:] = [s.slot_id for s in slots]
             self.slots_buf[par][:n].copy_(self.slots_host_buf[par][:n])
         torch.cuda.synchronize(self._device)
         g = self._graphs.get(n)
@@ -474,8 +474,7 @@ class B200Executor:
         par = self._parity
         if self._done_a[par] is not None:  # the staging copy of step t - 2 has been consumed
             self._done_a[par].synchronize()
-        for i, s in enumerate(slots):
-            self.slots_host_buf[par][i] = s.slot_id
+        self.slots_host_buf[par][:n].numpy()[:] = [s.slot_id for s in slots]
         graphs = None
         if self._use_graphs:
             if n not in self._graphs:
