@@ -277,8 +277,9 @@ def cpu_oracle_rate(n_streams=4, ctx=256, steps=40, warmup=1):
 def run_reference(rank, world):
     if rank != 0:
         return
-    # the arm's own --steps / --warmup, each step a 4-stream sample of the 64-stream step
-    base = cpu_oracle_rate(steps=max(1, ARGS.steps), warmup=ARGS.warmup)
+    # the arm's own --steps / --warmup; each step is a two-stream sample of the 64-stream step
+    # (0.1-0.2 s of CPU work on 16 threads, so the default 512 steps end within about two minutes)
+    base = cpu_oracle_rate(n_streams=2, steps=max(1, ARGS.steps), warmup=ARGS.warmup)
     line = {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": UNIT, "n_gpus": world,
             "steps": ARGS.steps, "warmup": ARGS.warmup, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
