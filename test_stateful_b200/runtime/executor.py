@@ -359,6 +359,39 @@ class B200Executor:
         codes = self.codes[:1].cpu()
         return audio, bool(int(codes[0, 0]) == self._config.talker.codec_eos_id)
 
+    def iter_prefill(self, slot: SlotState, prefill_embeds: torch.Tensor, chunk: int = 128):
+        """Chunked prefill (the first "next" item after the decode step: prefill interleaved with
+        decode).  A generator: each ``next()`` runs one engine step over the following
+        ``chunk`` prompt tokens (KV appended after the previous chunk's; no sampling) and yields
+        ``None``; the last chunk samples the first frame, and the final ``next()`` yields
+        ``prefill``'s ``(audio bytes, eos)``.  A serving loop calls ``next()`` between decode
+        steps, so a long prompt never stalls the running streams for more than one chunk.
+        Prompts longer than ``max_prefill_rows`` are accepted (each chunk is at most that)."""
+        seq = int(prefill_embeds.shape[1])
+        if chunk < 1:
+            raise ValueError("chunk must be >= 1")
+        chunk = min(chunk, self._max_input_len)
+        self._kv_pool.init_kv_tensors(slot)
+        self._configure_sampling(slot)
+        for start in range(0, seq, chunk):
+            last = start + chunk >= seq
+            self._prefill_call(slot, prefill_embeds[:, start:start + chunk], sample=1 if last else 0)
+            if not last:
+                yield None
+        slot.position_offset = 0
+        slot.frame_idx += 1
+        slot.next_embed = self.next_x[slot.slot_id]
+        audio = self._first_frame_audio()
+        codes = self.codes[:1].cpu()
+        yield audio, bool(int(codes[0, 0]) == self._config.talker.codec_eos_id)
+
+    def prefill_chunked(self, slot: SlotState, prefill_embeds: torch.Tensor, chunk: int = 128):
+        """``prefill`` cut into engine steps of at most ``chunk`` tokens (see ``iter_prefill``)."""
+        result = None
+        for result in self.iter_prefill(slot, prefill_embeds, chunk):
+            pass
+        return result
+
     def prefill_prefix_only(self, slot: SlotState, prefill_embeds: torch.Tensor) -> None:
         """executor.py:879-950: KV for a cacheable prefix, no sampling."""
         seq = int(prefill_embeds.shape[1])

@@ -102,3 +102,59 @@ def test_executor_lookahead_matches_sequential_steps():
     for k in range(len(c_seq)):
         assert torch.equal(c_seq[k], c_la[k]), k
         assert a_seq[k] == a_la[k], k
+
+
+def test_chunked_prefill_interleaved_with_decode():
+    """Chunked prefill (engine steps of 8 prompt tokens, only the last one sampling) gives the
+    first frame of a single-shot prefill, and running its chunks between decode steps of other
+    streams leaves those streams' codes and audio unchanged (greedy, so both runs are
+    deterministic)."""
+    cfg = tiny_engine_config()
+    W = wmod.make_talker_weights(cfg.talker, 6)
+    W.update(wmod.make_cp_weights(cfg.cp, 6))
+    Wc = wmod.make_code2wav_weights(cfg.c2w, 6)
+    g = torch.Generator().manual_seed(3)
+    prompts = [(torch.randn(1, n, cfg.talker.hidden_size, generator=g) * 0.02) for n in (9, 13, 21)]
+
+    def run(chunked):
+        ex = B200Executor(max_batch_size=4, max_seq_len=96, model_config=cfg, do_sample=False, random_seed=2,
+                          num_blocks=64, weights=dict(W), c2w_weights=dict(Wc), max_prefill_rows=64)
+        ex.load()
+        old = []
+        for i, p in enumerate(prompts[:2]):
+            s = ex.kv_pool.allocate(f"s{i}")
+            ex.prefill(s, p.to(DEV))
+            old.append(s)
+        new = ex.kv_pool.allocate("new")
+        outs = []
+        if chunked:
+            it = ex.iter_prefill(new, prompts[2].to(DEV), chunk=8)
+            first = None
+            for _ in range(3):  # 21 tokens: chunks of 8, 8, 5 between decode steps of the others
+                out = ex.launch_decode_step(old).wait()
+                outs.append((out.full_codec.clone(), list(out.audio_chunks)))
+                first = next(it)
+            assert first is not None
+        else:
+            for _ in range(3):
+                out = ex.launch_decode_step(old).wait()
+                outs.append((out.full_codec.clone(), list(out.audio_chunks)))
+            first = ex.prefill(new, prompts[2].to(DEV))
+        logits = ex.logits[0].float().cpu().clone()
+        codes0 = ex.codes[0].cpu().clone()
+        nxt = ex.launch_decode_step(old + [new]).wait()
+        assert _lib.device_error() == 0
+        ex.shutdown()
+        return outs, first, logits, codes0, nxt
+
+    o_seq, f_seq, l_seq, c_seq, n_seq = run(False)
+    o_chk, f_chk, l_chk, c_chk, n_chk = run(True)
+    for (ca, aa), (cb, ab) in zip(o_seq, o_chk):  # the running streams are untouched
+        assert torch.equal(ca, cb)
+        assert aa == ab
+    rel = float((l_seq - l_chk).abs().max() / l_seq.abs().max())
+    assert rel < 1e-3, rel  # split-K order differs with the chunk's row count
+    assert torch.equal(c_seq, c_chk)
+    assert f_seq[1] == f_chk[1]
+    assert _snr(np.frombuffer(f_seq[0], np.float32), np.frombuffer(f_chk[0], np.float32)) >= 30.0
+    assert torch.equal(n_seq.full_codec, n_chk.full_codec)
