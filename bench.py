@@ -1,5 +1,5 @@
 #!/usr/bin/env python3
-"""Codec frames/s/GPU of the continuous-batching decode step (BASELINE cfg2).
+"""Codec frames/s/GPU of the continuous-batching decode step (64 ragged streams, 512 steps).
 
 Workload (seeded synthetic, no dataset): 64 concurrent streams per GPU, prompt
 lengths U{16..512} whose first min(96, L) token ids are a shared prefix
@@ -49,7 +49,7 @@ SEED = 1
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=512)  # BASELINE cfg2: 512 decode steps
+    ap.add_argument("--steps", type=int, default=512)  # the benchmark workload: 512 decode steps
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -38,7 +38,7 @@ def prompt_ids(lengths: Sequence[int], seed: int) -> List[torch.Tensor]:
 
 
 def shared_prefix_prompts(n_streams: int, lo: int, hi: int, prefix_len: int, seed: int) -> List[torch.Tensor]:
-    """BASELINE cfg2: lengths U{lo..hi}; the first ``min(prefix_len, L)`` ids are common."""
+    """Benchmark prompts: lengths U{lo..hi}; the first ``min(prefix_len, L)`` ids are common."""
     g = _gen(seed, 19)
     lengths = torch.randint(lo, hi + 1, (n_streams,), generator=g).tolist()
     prefix = torch.randint(0, TEXT_VOCAB, (prefix_len,), generator=g)

@@ -620,7 +620,7 @@ def make_code2wav(ref: Path, out, seed=5, steps=78, starts=(0, 9)):
 
 
 def make_cfg1_long(out, steps=512):
-    """BASELINE configs[0] streams (seed 0, prompts {37, 64, 91, 128}, greedy) for ``steps``
+    """The CPU reference case's streams (seed 0, prompts {37, 64, 91, 128}, greedy) for ``steps``
     decode steps, run by the ORACLE (oracle/engine.py): the reference's own modules pin the
     oracle over the first 32 steps (cfg1_full_greedy.npz); this fixture extends the horizon to
     the 512-step agreement bar.  Stores the greedy codes and every 64th step's logits (fp16)."""
@@ -647,7 +647,7 @@ def make_cfg1_long(out, steps=512):
 
 
 def make_code2wav_chunked(ref: Path, out, seed=6, chunks=(25, 25, 25, 7), start1=1):
-    """Multi-frame chunks through the reference wrapper (BASELINE cfg4): per call T frames per
+    """Multi-frame chunks through the reference wrapper (25-frame chunks with carried state): per call T frames per
     slot, past KV capped at window - T frames (the executor's max_past = window - chunk_T,
     executor.py:1374-1380), bias = -inf on each slot's left padding plus the causal mask inside
     the chunk, delta KV appended.  Slot 1 joins at call ``start1`` (ragged pasts)."""
@@ -753,7 +753,7 @@ def main():
                         **run_trajectory(ref_mods, tiny, seed=4, lengths=[5, 13, 21], steps=12, do_sample=False))
     print(f"tiny fixtures done in {time.time() - t0:.1f}s", flush=True)
     if not args.skip_full:
-        # full talker, seed 0, fp32, prompts {37,64,91,128}, 32 greedy steps
+        # the CPU reference case: full talker, seed 0, fp32, prompts {37,64,91,128}, 32 greedy steps
         t0 = time.time()
         r = run_trajectory(ref_mods, EngineConfig(), seed=0, lengths=[37, 64, 91, 128], steps=32, do_sample=False)
         r.pop("gumbel"); r.pop("cp_gumbel")

@@ -68,7 +68,7 @@ def test_code2wav_state_shapes_match_reference_layout():
 
 
 def test_code2wav_oracle_matches_reference_chunked_stream():
-    """BASELINE cfg4 semantics: chunks of T frames (here 25, 25, 25, 7) with carried state;
+    """Chunked semantics: chunks of T frames (here 25, 25, 25, 7) with carried state;
     each chunk sees at most window - T past frames plus its own frames causally.  Fixture
     from the reference wrapper, two slots with ragged pasts (wav stored as fp16)."""
     z = np.load(os.path.join(GOLDEN, "code2wav_chunked_tiny.npz"))

@@ -108,7 +108,7 @@ def test_code2wav_reset_replays_identically():
 
 
 def test_code2wav_chunked_matches_reference_fixture():
-    """BASELINE cfg4: chunks of 25, 25, 25 and 7 frames per call with carried state, two slots
+    """Chunked decode: chunks of 25, 25, 25 and 7 frames per call with carried state, two slots
     with ragged pasts (slot 1 joins one call later), against the reference wrapper's output."""
     z = np.load(os.path.join(GOLDEN, "code2wav_chunked_tiny.npz"))
     cfg = tiny_code2wav_config()

@@ -214,7 +214,7 @@ def test_cfg1_full_model_512_step_greedy_agreement():
 
 
 def test_cfg1_full_model_greedy_against_reference():
-    """BASELINE configs[0] on the device: full 28-layer talker, seed 0, prompts
+    """The CPU reference case on the device: full 28-layer talker, seed 0, prompts
     {37, 64, 91, 128}, 32 greedy steps, against the reference's fp32 run."""
     path = os.path.join(GOLDEN, "cfg1_full_greedy.npz")
     if not os.path.exists(path):

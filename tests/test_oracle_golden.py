@@ -78,7 +78,7 @@ def test_tiny_trajectory(name):
 
 @pytest.mark.slow
 def test_cfg1_full_greedy():
-    """full 28-layer talker, seed 0, fp32, 4 ragged prompts, 32 greedy steps."""
+    """The CPU reference case: full 28-layer talker, seed 0, fp32, 4 ragged prompts, 32 greedy steps."""
     path = os.path.join(GOLDEN, "cfg1_full_greedy.npz")
     if not os.path.exists(path):
         pytest.skip("cfg1 fixture not generated")
