@@ -1143,7 +1143,16 @@ inline bool gemm_bn32() {
     }();
     return on;
 }
-inline int pick_bn(int M) { return M <= 64 ? (gemm_bn32() ? 32 : 64) : 128; }
+// Rows up to QTTS_GEMM_BN64_MAX_M (default 128: the code predictor's two-row first stage, +2 %
+// over 128-token tiles) use 64-token tiles; more rows use 128-token tiles.
+inline int gemm_bn64_max_m() {
+    static const int m = [] {
+        const char* v = getenv("QTTS_GEMM_BN64_MAX_M");
+        return (v && *v) ? atoi(v) : 128;
+    }();
+    return m;
+}
+inline int pick_bn(int M) { return M <= 64 ? (gemm_bn32() ? 32 : 64) : (M <= gemm_bn64_max_m() ? 64 : 128); }
 
 // Persistent conv GEMMs for wide rows: opt-in (QTTS_GEMM_PERSIST=1).  At the decoder's
 // sizes they measured slower than the two-CTAs-per-SM form (2.43 vs 1.64 ms per
@@ -1347,7 +1356,7 @@ inline int launch_gemm_persist(const GemmPlan& g, const GemmParams& p, cudaStrea
 // Launch on the first M rows of the plan's X buffer(s).
 inline int gemm_run(GemmPlan g, int M, cudaStream_t st, void* out = nullptr) {
     if (M <= 0) return QTTS_OK;
-    const int bn = pick_bn(M);
+    const int bn = g.p.ix.on ? 128 : pick_bn(M);  // implicit convolutions tile whole 128-row stream blocks
     if (g.p.ix.on && (bn != 128 || M % g.p.ix.T != 0)) {
         set_error("implicit conv: rows must be whole streams of T >= 128 steps (M=%d T=%d)", M, g.p.ix.T);
         return QTTS_ERR_INVALID;
