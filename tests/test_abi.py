@@ -79,3 +79,20 @@ def test_invalid_arguments_return_status_codes():
     assert lib.qtts_engine_step(None, None, None) == _lib.ERR_INVALID
     with pytest.raises(RuntimeError):
         _lib.check(_lib.ERR_POOL_EXHAUSTED, "append")
+
+
+def test_no_cpu_fallback():
+    """Without a CUDA device the product path refuses to run rather than computing on the host:
+    the executor will not construct, and the kernel wrappers reject host tensors before any call."""
+    import torch
+
+    from test_stateful_b200 import ops
+    from test_stateful_b200.runtime.executor import B200Executor
+
+    if not torch.cuda.is_available():
+        with pytest.raises(RuntimeError, match="no CPU path"):
+            B200Executor(max_batch_size=1, max_seq_len=16)
+    x = torch.zeros(64, 2048, dtype=torch.bfloat16)
+    w = torch.zeros(2048, 2048, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA tensors only"):
+        ops.gemm(x, w)
