@@ -42,6 +42,13 @@ int qtts_version(void);
 int qtts_last_error(char* buf, size_t size);
 /* Read and clear the device-side error word set by bounded waits (0 = none). */
 int qtts_device_error(int* out);
+/* Self-test of the bounded device wait that every mbarrier wait of the library uses (no
+ * counterpart in the reference, whose waits are TensorRT's): one thread waits up to
+ * limit_ns (<= 2 s) on an mbarrier phase.  arrive = 0: nothing completes the phase, the wait
+ * runs out, the device error word records it and status[0] (device int32) = QTTS_ERR_TIMEOUT;
+ * arrive = 1: the phase completes and status[0] = QTTS_OK.  No trap, no hang: the kernel
+ * returns and the context stays usable. */
+int qtts_selftest_bounded_wait(unsigned long long limit_ns, int arrive, int32_t* status, qtts_stream_t stream);
 
 /* ========================================================================
  * Paged KV pool state (on device)
@@ -174,10 +181,13 @@ int qtts_paged_attention(const void* q, int R, int num_heads, int kv_heads, int 
  * when they run attention (a plugin host that owns every allocation and passes only the
  * call's tensors, or a latency-bound thread that must not call cudaMalloc).  No counterpart
  * in the reference.  The split-KV partials live in a static device array of the library
- * (4 MiB, held on every GPU that loads it), so nothing is allocated; shapes with
- * num_rows * num_heads * max_splits * head_dim > 1048576 are rejected with QTTS_ERR_INVALID.
+ * (4.25 MiB, held on every GPU that loads it), so nothing is allocated; shapes with
+ * num_rows * num_heads * max_splits * head_dim > 1048576 are rejected with QTTS_ERR_INVALID
+ * (every head_dim the kernels take, 32 to 128, fits up to that limit).
  * The first call on a device looks up the array's address; make that call before any stream
- * capture.  Calls share the array: two calls that overlap on the GPU race. */
+ * capture.  The address is kept for the life of the process, so cudaDeviceReset followed by
+ * more calls on that device is not supported.  Calls share the array: two calls that overlap
+ * on the GPU race. */
 int qtts_paged_attention_noalloc(const void* q, int R, int num_heads, int kv_heads, int head_dim,
                                  const void* kv_pool, int layer, int num_layers, int block_size,
                                  int num_blocks, const int32_t* block_table, int max_blocks_per_seq,
@@ -194,6 +204,15 @@ int qtts_sample(const float* logits, int R, int V, int ld, int topk, const float
                 int gumbel_ld, uint64_t seed, const int64_t* noise_key, int step,
                 const float* temperature, const float* penalty, int64_t* counts, int eos_id,
                 int64_t* tok_out, int tok_ld, qtts_stream_t stream);
+
+/* The sampling noise the library draws in-kernel, written out: out[r][j] (fp32 [R][cols]) =
+ * -log(-log(clamp(u, 1e-8, 1))) with u from Philox4x32-10 keyed by (seed, keys[r],
+ * 16 * frames[r] + stage, j); stage 0 = talker head, 1 + s = code-predictor stage s.
+ * keys int64 [R], frames int32 [R] (the per-slot key and frame counter of the engine step).
+ * Replaces, for inspection and parity, the per-slot noise tensors the reference builds on the
+ * host (engine/backend/executor.py:1229-1253). */
+int qtts_philox_gumbel(uint64_t seed, const int64_t* keys, const int32_t* frames, int stage, int R, int cols,
+                       float* out, qtts_stream_t stream);
 
 /* Codec embedding sum (scripts/python/codec_embedding_sum.py:71-83):
  * out[r] = bf16round(Σ_g T_g[codes[r][g]] + text_add[r]) as fp32 [R][H];

@@ -96,11 +96,11 @@ class C2wDesc(C.Structure):
 
 # every symbol the header declares, in header order
 EXPORTS = [
-    "qtts_version", "qtts_last_error", "qtts_device_error",
+    "qtts_version", "qtts_last_error", "qtts_device_error", "qtts_selftest_bounded_wait",
     "qtts_sched_init", "qtts_sched_append", "qtts_kv_copy_blocks", "qtts_sched_share_prefix",
     "qtts_sched_make_entry", "qtts_sched_drop_blocks", "qtts_sched_release", "qtts_kv_scatter", "qtts_kv_gather",
     "qtts_gemm", "qtts_rmsnorm", "qtts_paged_attention", "qtts_paged_attention_noalloc", "qtts_sample",
-    "qtts_codec_sum",
+    "qtts_philox_gumbel", "qtts_codec_sum",
     "qtts_engine_create", "qtts_engine_destroy", "qtts_engine_step",
     "qtts_c2w_create", "qtts_c2w_destroy", "qtts_c2w_reset", "qtts_c2w_step", "qtts_c2w_launches",
     "qtts_c2w_set_background",
@@ -124,6 +124,7 @@ def load() -> C.CDLL:
         "qtts_version": ([], C.c_int),
         "qtts_last_error": ([C.c_char_p, C.c_size_t], C.c_int),
         "qtts_device_error": ([C.POINTER(C.c_int)], C.c_int),
+        "qtts_selftest_bounded_wait": ([C.c_ulonglong, C.c_int, P, P], C.c_int),
         "qtts_sched_init": ([C.POINTER(PagedState), P], C.c_int),
         "qtts_sched_append": ([C.POINTER(PagedState), P, C.c_int, C.c_int, P, P, P, P, P, P, P], C.c_int),
         "qtts_kv_copy_blocks": ([P, C.c_size_t, C.c_int, P, P, C.c_int, P], C.c_int),
@@ -141,6 +142,7 @@ def load() -> C.CDLL:
                                           C.c_int, P, C.c_int, P, P, C.c_int, P, P, P], C.c_int),
         "qtts_sample": ([P, C.c_int, C.c_int, C.c_int, C.c_int, P, C.c_int, C.c_uint64, P, C.c_int, P, P, P,
                          C.c_int, P, C.c_int, P], C.c_int),
+        "qtts_philox_gumbel": ([C.c_uint64, P, P, C.c_int, C.c_int, C.c_int, P, P], C.c_int),
         "qtts_codec_sum": ([P, C.c_int, C.c_int, P, C.c_int, P, C.c_int, C.c_int, P, P, P, P], C.c_int),
         "qtts_engine_create": ([C.POINTER(ModelDesc), C.POINTER(P)], C.c_int),
         "qtts_engine_destroy": ([P], C.c_int),

@@ -778,11 +778,7 @@ template <int D, int S>
 inline int launch_attention_s(const AttnParams& p, cudaStream_t st) {
     using L = AttnLayout<D, S>;
     auto kern = paged_attn_kernel<D, S>;
-    static bool attr = false;
-    if (!attr) {
-        QTTS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM));
-        attr = true;
-    }
+    QTTS_CHECK_CUDA((func_attr_once<paged_attn_kernel<D, S>>(L::SMEM)));
     QTTS_LAUNCH(kern, dim3(p.R, p.kv_heads, p.max_splits), dim3(128), L::SMEM, st, p);
     return QTTS_OK;
 }
@@ -794,11 +790,7 @@ inline int launch_attention_tc(const AttnParams& p, cudaStream_t st) {
     const int rc = make_kv_map(&map, p);
     if (rc) return rc;
     auto kern = paged_attn_tc_kernel<S>;
-    static bool attr = false;
-    if (!attr) {
-        QTTS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM));
-        attr = true;
-    }
+    QTTS_CHECK_CUDA((func_attr_once<paged_attn_tc_kernel<S>>(L::SMEM)));
     const int items = p.R * p.kv_heads * p.max_splits;  // one (split, row, kv head) per warp
     QTTS_LAUNCH(kern, dim3(ceil_div(items, 4)), dim3(128), L::SMEM, st, map, p);
     return QTTS_OK;

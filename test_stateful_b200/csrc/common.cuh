@@ -9,6 +9,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <string>
@@ -40,6 +41,27 @@ void set_error(const char* fmt, ...);
         }                                  \
     } while (0)
 
+// One-time kernel attribute set-up, per kernel and device.  cudaFuncSetAttribute
+// applies to the current device only, so a process that drives several GPUs
+// needs it once on each; the kernel is a template argument so every kernel has
+// its own record.  The bit of a device is set after its calls succeed (two
+// threads racing on the first call both set the same values, which is
+// harmless).  Devices past 63 set the attributes on every call.
+template <auto Kernel>
+inline cudaError_t func_attr_once(int smem_bytes, bool nonportable_cluster = false) {
+    static std::atomic<unsigned long long> done{0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const unsigned long long bit = dev < 64 ? (1ull << dev) : 0ull;
+    if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+    e = cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+    if (e == cudaSuccess && nonportable_cluster)
+        e = cudaFuncSetAttribute(Kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_acq_rel);
+    return e;
+}
+
 #define QTTS_LAUNCH_CHECK()                                                                   \
     do {                                                                                      \
         cudaError_t _e = cudaGetLastError();                                                  \
@@ -62,6 +84,7 @@ enum DeviceErr : int {
     DEV_ERR_ATTN_WAIT = 4,
     DEV_ERR_DRAIN = 5,
     DEV_ERR_BAD_SLOT = 6,  // a code2wav row named a slot outside the decoder's range
+    DEV_ERR_SELFTEST_WAIT = 7,  // qtts_selftest_bounded_wait: the wait ran out, as the test intends
 };
 
 // Wall-clock limit of every device-side wait (ns).  A correct kernel waits
@@ -114,17 +137,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait on an mbarrier phase.  Returns false (and records `err`) when
-// the phase did not complete within kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int err) {
+// the phase did not complete within `limit_ns` of %globaltimer.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, int err,
+                                              unsigned long long limit_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     const unsigned long long t0 = globaltimer();
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (globaltimer() - t0 > kWaitLimitNs) {
+        if (globaltimer() - t0 > limit_ns) {
             record_error(err);
             return false;
         }
     }
+}
+
+// The wait every kernel uses: kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int err) {
+    return mbar_wait_for(bar, parity, err, kWaitLimitNs);
 }
 
 __device__ __forceinline__ void fence_proxy_async_smem() {

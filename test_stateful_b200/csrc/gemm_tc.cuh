@@ -1226,12 +1226,7 @@ inline int launch_gemm_t(const CUtensorMap& mw, const CUtensorMap& mx, const CUt
                          cudaStream_t st) {
     using L = GemmLayout<BN, STAGES, SPLIT, PUSH>;
     auto kern = gemm_tc_kernel<BN, STAGES, SPLIT, NT, PUSH>;
-    static bool attr_done = false;
-    if (!attr_done) {
-        QTTS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM));
-        QTTS_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
-        attr_done = true;
-    }
+    QTTS_CHECK_CUDA((func_attr_once<gemm_tc_kernel<BN, STAGES, SPLIT, NT, PUSH>>(L::SMEM, /*nonportable_cluster=*/true)));
     QTTS_CHECK_CUDA(launch_pdl(kern, dim3(p.N / 128, p.splits, ceil_div(p.M, BN)), dim3(NT, 1, 1), L::SMEM, st,
                                dim3(p.pair.on ? 2 : 1, p.splits, 1), mw, mx, mxlo, p));
     return QTTS_OK;
@@ -1338,12 +1333,7 @@ inline bool gemm_persist_ok(const GemmPlan& g, int M) {
 
 inline int launch_gemm_persist(const GemmPlan& g, const GemmParams& p, cudaStream_t st) {
     using L = PersistLayout;
-    static bool attr = false;
-    if (!attr) {
-        QTTS_CHECK_CUDA(
-            cudaFuncSetAttribute(gemm_conv_persist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM));
-        attr = true;
-    }
+    QTTS_CHECK_CUDA((func_attr_once<gemm_conv_persist_kernel>(L::SMEM)));
     // QTTS_GEMM_PERSIST_CTAS caps the grid (e.g. to leave SMs to a concurrent stream)
     static const int cap = env_int("QTTS_GEMM_PERSIST_CTAS", num_sms());
     const int tiles = (p.N / 128) * ceil_div(p.M, 128);

@@ -206,6 +206,16 @@ int qtts_sample(const float* logits, int R, int V, int ld, int topk, const float
     return launch_sample(p, (cudaStream_t)stream);
 }
 
+int qtts_philox_gumbel(uint64_t seed, const int64_t* keys, const int32_t* frames, int stage, int R, int cols,
+                       float* out, qtts_stream_t stream) {
+    QTTS_REQUIRE(keys && frames && out && R >= 0 && cols > 0 && cols <= 4096, "philox_gumbel: bad arguments");
+    QTTS_REQUIRE(stage >= 0 && stage < 16, "philox_gumbel: stage %d outside [0, 16)", stage);
+    if (R == 0) return QTTS_OK;
+    philox_gumbel_kernel<<<R, 64, 0, (cudaStream_t)stream>>>(seed, keys, frames, stage, cols, out);
+    QTTS_LAUNCH_CHECK();
+    return QTTS_OK;
+}
+
 int qtts_codec_sum(const int64_t* codes, int R, int G, const void* talker_table, int V0, const void* cp_tables, int Vc,
                    int H, const float* text_add, float* codec_sum_out, float* next_x, qtts_stream_t stream) {
     QTTS_REQUIRE(codes && talker_table && next_x && R >= 0 && G >= 1 && H % 2 == 0, "codec_sum: bad arguments");
@@ -307,6 +317,36 @@ int qtts_c2w_set_background(qtts_c2w* c, int background) {
 }  // extern "C"
 
 // ---------------------------------------------------------------------------
+// Self-test of the bounded device wait (the failure path of every mbarrier
+// wait in the library): one thread waits on an mbarrier phase with the
+// caller's limit.  With arrive = 0 nothing completes the phase, so the wait
+// runs out, records DEV_ERR_SELFTEST_WAIT in the device error word and the
+// kernel writes QTTS_ERR_TIMEOUT to *status and returns; with arrive = 1 the
+// thread arrives first and the wait succeeds (QTTS_OK).  The context stays
+// usable either way.
+// ---------------------------------------------------------------------------
+namespace qtts {
+__global__ void selftest_wait_kernel(unsigned long long limit_ns, int arrive, int32_t* status) {
+    __shared__ __align__(8) uint64_t bar;
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    if (arrive) mbar_arrive(&bar);
+    const bool ok = mbar_wait_for(&bar, 0, DEV_ERR_SELFTEST_WAIT, limit_ns);
+    status[0] = ok ? QTTS_OK : QTTS_ERR_TIMEOUT;
+}
+}  // namespace qtts
+
+extern "C" int qtts_selftest_bounded_wait(unsigned long long limit_ns, int arrive, int32_t* status,
+                                          qtts_stream_t stream) {
+    QTTS_REQUIRE(status, "selftest_bounded_wait: null status");
+    QTTS_REQUIRE(limit_ns > 0 && limit_ns <= kWaitLimitNs, "selftest_bounded_wait: limit %llu ns outside (0, %llu]",
+                 limit_ns, kWaitLimitNs);
+    selftest_wait_kernel<<<1, 1, 0, (cudaStream_t)stream>>>(limit_ns, arrive, status);
+    QTTS_LAUNCH_CHECK();
+    return QTTS_OK;
+}
+
+// ---------------------------------------------------------------------------
 // Paged attention without caller scratch.
 //
 // qtts_paged_attention needs two scratch buffers for its split-KV partial
@@ -320,7 +360,12 @@ int qtts_c2w_set_background(qtts_c2w* c, int background) {
 //
 // Limit: R * num_heads * max_splits * head_dim <= kNoAllocMaxPartials
 // (4 MiB of fp32, e.g. 64 rows x 16 heads x 8 splits (2048 keys) x 128),
-// with max_splits = ceil(ceil(max_ctx / 16) / QTTS_ATTN_SPLIT_BLOCKS).
+// with max_splits = ceil(ceil(max_ctx / 16) / QTTS_ATTN_SPLIT_BLOCKS).  The
+// (max, sum) area is sized for the smallest head_dim the kernels take (32),
+// so every shape within that limit fits.
+// The device address of the array is looked up once per device and kept for
+// the life of the process; a cudaDeviceReset followed by new work on that
+// device is not supported by this entry point.
 // Nothing in the array needs to start at zero: each call writes every partial
 // it later reads.  All calls share the one array, so two calls that overlap
 // on the GPU (different streams, no ordering between them) race on it.
@@ -328,7 +373,8 @@ int qtts_c2w_set_background(qtts_c2w* c, int background) {
 namespace {
 
 constexpr size_t kNoAllocMaxPartials = size_t(1) << 20;               // o partials, floats
-constexpr size_t kNoAllocMaxStats = kNoAllocMaxPartials / 64;         // (max, sum) pairs, floats
+constexpr int kNoAllocMinHeadDim = 32;                                 // smallest head_dim the kernels take
+constexpr size_t kNoAllocMaxStats = kNoAllocMaxPartials / kNoAllocMinHeadDim * 2;  // (max, sum) pairs, floats
 static __device__ __align__(256) float g_noalloc_attn_scratch[kNoAllocMaxPartials + kNoAllocMaxStats];
 
 constexpr int kMaxDevices = 64;
@@ -364,14 +410,21 @@ extern "C" int qtts_paged_attention_noalloc(const void* q, int R, int num_heads,
                                             int num_blocks, const int32_t* block_table, int max_blocks_per_seq,
                                             const int32_t* row_slot, const int32_t* row_ctx, int max_ctx, void* out,
                                             void* out_lo, qtts_stream_t stream) {
-    QTTS_REQUIRE(R >= 0 && num_heads > 0 && head_dim > 0 && max_ctx > 0, "paged_attention_noalloc: bad shape");
+    QTTS_REQUIRE(R >= 0 && num_heads > 0 && head_dim >= kNoAllocMinHeadDim && max_ctx > 0,
+                 "paged_attention_noalloc: bad shape (head_dim %d; the static scratch serves head_dim >= %d)",
+                 head_dim, kNoAllocMinHeadDim);
     const size_t splits = (size_t)attn_max_splits(max_ctx);
     const size_t need_o = (size_t)R * num_heads * splits * head_dim;
     const size_t need_ml = (size_t)R * num_heads * splits * 2;
-    if (need_o > kNoAllocMaxPartials || need_ml > kNoAllocMaxStats) {
+    if (need_o > kNoAllocMaxPartials) {
         set_error("paged_attention_noalloc: %zu rows x heads x splits x head_dim partials exceed the static scratch "
                   "of %zu floats; use fewer rows or qtts_paged_attention with caller scratch",
                   need_o, kNoAllocMaxPartials);
+        return QTTS_ERR_INVALID;
+    }
+    if (need_ml > kNoAllocMaxStats) {  // cannot happen for head_dim >= 32 once need_o fits
+        set_error("paged_attention_noalloc: %zu (max, sum) floats exceed the static scratch of %zu floats",
+                  need_ml, kNoAllocMaxStats);
         return QTTS_ERR_INVALID;
     }
     float* scratch = nullptr;

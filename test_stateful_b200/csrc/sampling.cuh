@@ -336,6 +336,17 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SamplePara
     }
 }
 
+// The Gumbel noise the samplers draw when it is not supplied: out[r][j] =
+// gumbel_noise(seed, keys[r], 16 * frames[r] + stage, j), stage 0 = the talker
+// head, 1 + s = code-predictor stage s (the counter layout of sample_kernel).
+__global__ void philox_gumbel_kernel(uint64_t seed, const int64_t* keys, const int32_t* frames, int stage, int cols,
+                                     float* out) {
+    const int r = blockIdx.x;
+    const uint64_t key = (uint64_t)keys[r];
+    const int step = frames[r] * 16 + stage;
+    for (int j = threadIdx.x; j < cols; j += blockDim.x) out[(size_t)r * cols + j] = gumbel_noise(seed, key, step, j);
+}
+
 inline int launch_sample(const SampleParams& p, cudaStream_t st) {
     if (p.R <= 0) return QTTS_OK;
     if (p.V > kSampleThreads * kSampleMaxPer || p.topk < 1 || p.topk > 64 || p.topk > p.V) {

@@ -107,6 +107,17 @@ def sample(logits: torch.Tensor, topk: int, gumbel: Optional[torch.Tensor] = Non
     return tok_out
 
 
+def philox_gumbel(seed: int, keys: torch.Tensor, frames: torch.Tensor, stage: int, cols: int = 50) -> torch.Tensor:
+    """The Gumbel rows the samplers draw in-kernel for per-row ``keys`` (int64) and frame
+    counters ``frames`` (int32) at ``stage`` (0: talker head, 1 + s: code-predictor stage s)."""
+    _need_cuda(keys, frames)
+    R = keys.numel()
+    out = torch.empty(R, cols, device=keys.device, dtype=torch.float32)
+    _lib.check(_lib.load().qtts_philox_gumbel(int(seed) & ((1 << 64) - 1), keys.data_ptr(), frames.data_ptr(), stage,
+                                              R, cols, out.data_ptr(), _lib.stream_ptr()), "philox_gumbel")
+    return out
+
+
 def codec_sum(codes: torch.Tensor, talker_table: torch.Tensor, cp_tables: torch.Tensor,
               text_add: Optional[torch.Tensor] = None):
     """Returns ``(codec_sum fp32 [R,H], next_x fp32 [R,H])``."""

@@ -499,6 +499,9 @@ class B200Executor:
         n = len(slots)
         if n == 0 or n > self._max_batch:
             raise ValueError(f"batch of {n} slots outside [1, {self._max_batch}]")
+        if len({s.slot_id for s in slots}) != n:
+            # two rows of one slot would append to the same block-table row and KV position
+            raise ValueError("a decode batch lists the same slot twice")
         cap = self._max_seq_len
         for s in slots:
             if s.past_len + 1 > cap:

@@ -316,3 +316,31 @@ def test_gemm_opt_in_variants(knob):
     r = subprocess.run([sys.executable, "-m", "pytest", "-x", "-q", "-m", "gpu", "-p", "no:cacheprovider", "-k", "gemm",
                         os.path.abspath(__file__)], env=env, capture_output=True, text=True, timeout=900)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
+
+
+# --------------------------------------------------------------------- bounded device waits
+def test_bounded_wait_runs_out_and_returns_a_status():
+    """The failure path of every mbarrier wait in the library: a wait on a phase that nothing
+    completes gives up after its limit, records the device error word and returns; the
+    context stays usable (a second launch that does arrive succeeds)."""
+    import time
+
+    lib = _lib.load()
+    status = torch.full((1,), 12345, dtype=torch.int32, device=DEV)
+    assert _lib.device_error() == 0
+    t0 = time.perf_counter()
+    _lib.check(lib.qtts_selftest_bounded_wait(20_000_000, 0, status.data_ptr(), _lib.stream_ptr()), "selftest")
+    torch.cuda.synchronize()
+    waited = time.perf_counter() - t0
+    assert int(status.item()) == _lib.ERR_TIMEOUT
+    assert waited >= 0.015, waited  # it did wait about the limit (20 ms), then returned
+    assert _lib.device_error() == 7  # DEV_ERR_SELFTEST_WAIT; reading clears the word
+    assert _lib.device_error() == 0
+    status.fill_(12345)
+    _lib.check(lib.qtts_selftest_bounded_wait(20_000_000, 1, status.data_ptr(), _lib.stream_ptr()), "selftest")
+    torch.cuda.synchronize()
+    assert int(status.item()) == _lib.OK
+    assert _lib.device_error() == 0
+    # out-of-range limits are refused on the host
+    assert lib.qtts_selftest_bounded_wait(0, 0, status.data_ptr(), _lib.stream_ptr()) == _lib.ERR_INVALID
+    assert lib.qtts_selftest_bounded_wait(3_000_000_000, 0, status.data_ptr(), _lib.stream_ptr()) == _lib.ERR_INVALID

@@ -70,6 +70,22 @@ def test_noalloc_matches_caller_scratch_on_two_calls_in_a_row():
     assert _lib.device_error() == 0
 
 
+def test_noalloc_takes_every_head_dim_up_to_the_limit():
+    # rows x heads x splits x head_dim exactly at the 1 Mi-float limit for head_dim 64 and 32:
+    # the (max, sum) area scales with 1/head_dim, so the smallest head_dim needs the most of it
+    for seed, d, n_rows in ((4, 64, 128), (5, 32, 256)):
+        max_ctx = MBPS * BS                      # 2048 keys -> 8 splits of 16 blocks
+        assert n_rows * HQ * 8 * d == 1 << 20
+        g = torch.Generator().manual_seed(seed)
+        ctxs = torch.randint(1, max_ctx + 1, (n_rows,), generator=g).tolist()
+        kv, table, q, ctx, rows = _case(seed, ctxs, d)
+        want = _with_caller_scratch(kv, table, q, ctx, rows, 2, max_ctx)
+        got = _without_scratch(kv, table, q, ctx, rows, 2, max_ctx)
+        torch.cuda.synchronize()
+        torch.testing.assert_close(got, want, rtol=1e-3, atol=1e-4)
+    assert _lib.device_error() == 0
+
+
 def test_noalloc_rejects_shapes_beyond_the_static_scratch():
     kv, table, q, ctx, rows = _case(3, [16] * 4, 128)
     big_rows = 600  # 600 rows x 16 heads x 1 split x 128 > 1 Mi partials
