@@ -41,8 +41,31 @@ class OracleEngine:
         self.past[sid] = S
         return r
 
-    def decode(self, sids: Sequence[int], embeds: torch.Tensor, counts, gumbel, cp_gumbel, temp, pen):
-        """One batched decode step; ``embeds [B, H]``."""
+    def share_prefix(self, dst: int, src: int, n: int) -> None:
+        """Stream ``dst`` starts from the first ``n`` KV positions of ``src``: the copy a
+        prefix-cache hit makes (engine/backend/engine_loop.py:823-835)."""
+        self.k[dst] = [k[:, :n].clone() for k in self.k[src]]
+        self.v[dst] = [v[:, :n].clone() for v in self.v[src]]
+        self.past[dst] = n
+
+    def extend(self, sid: int, embeds: torch.Tensor, counts, gumbel, cp_gumbel, temp, pen, force=None):
+        """``embeds [S, H]`` appended to stream ``sid``'s KV in one fused call (batch 1):
+        Executor.prefill_from_prefix (engine/backend/executor.py:952-1081)."""
+        S = embeds.shape[0]
+        P = self.past[sid]
+        pos = (torch.arange(S) + P).unsqueeze(0)
+        pk = [k.unsqueeze(0) for k in self.k[sid]]
+        pv = [v.unsqueeze(0) for v in self.v[sid]]
+        r = M.fused_step(self.W, self.t, self.c, embeds.unsqueeze(0), pos, pk, pv, [P], counts.unsqueeze(0),
+                         gumbel, cp_gumbel, temp, pen, self.table, force=force)
+        for l in range(self.t.num_layers):
+            self.k[sid][l] = torch.cat([self.k[sid][l], r["new_k"][l][0]], dim=1)
+            self.v[sid][l] = torch.cat([self.v[sid][l], r["new_v"][l][0]], dim=1)
+        self.past[sid] = P + S
+        return r
+
+    def decode(self, sids: Sequence[int], embeds: torch.Tensor, counts, gumbel, cp_gumbel, temp, pen, force=None):
+        """One batched decode step; ``embeds [B, H]``; ``force``: see ``model.fused_step``."""
         B = len(sids)
         lens = [self.past[s] for s in sids]
         P = max(lens)
@@ -57,7 +80,7 @@ class OracleEngine:
             pv.append(vv)
         pos = torch.tensor(lens).unsqueeze(1)
         r = M.fused_step(self.W, self.t, self.c, embeds.unsqueeze(1), pos, pk, pv, lens, counts,
-                         gumbel, cp_gumbel, temp, pen, self.table)
+                         gumbel, cp_gumbel, temp, pen, self.table, force=force)
         for i, s in enumerate(sids):
             for l in range(self.t.num_layers):
                 self.k[s][l] = torch.cat([self.k[s][l], r["new_k"][l][i]], dim=1)

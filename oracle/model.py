@@ -262,17 +262,20 @@ def codec_sum(table: Tensor, codes: Tensor) -> Tensor:
 # ----------------------------------------------------------------------------
 
 def fused_step(W, tcfg, ccfg, embeds, positions, past_k, past_v, past_lens, token_counts,
-               gumbel, cp_gumbel, temperature, penalty, table=None):
+               gumbel, cp_gumbel, temperature, penalty, table=None, force=None):
     """talker_unified_modules.py:357-401 for ``S`` new tokens per stream.
 
     Returns a dict with ``hidden, logits, new_k, new_v, tok0, counts,
-    cp_tokens, full_codec, codec_sum``.
+    cp_tokens, full_codec, codec_sum``.  Test hook: ``force [B, 1+num_stages]``
+    makes the code predictor consume ``force[:, 0]`` as tok0 and ``force[:, s]``
+    after stage s-1 (teacher forcing); the returned tokens are still this
+    step's own samples, and ``counts`` is updated with them.
     """
     hidden, logits, new_k, new_v = talker_forward(W, tcfg, embeds, positions, past_k, past_v, past_lens)
     tok0, counts = talker_sample(logits[:, -1, :], token_counts, gumbel, temperature, penalty,
                                  tcfg.codec_eos_id, tcfg.logits_topk)
-    cp_tok = code_predictor(W, ccfg, W["talker.codec_embedding.weight"], hidden[:, -1:, :], tok0,
-                            cp_gumbel, temperature)
+    cp_tok = code_predictor(W, ccfg, W["talker.codec_embedding.weight"], hidden[:, -1:, :],
+                            tok0 if force is None else force[:, 0], cp_gumbel, temperature, force=force)
     full = torch.cat([tok0.unsqueeze(1), cp_tok], dim=1)
     if table is None:
         table = stacked_codec_table(W, ccfg.num_stages)

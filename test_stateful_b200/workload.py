@@ -47,3 +47,52 @@ def shared_prefix_prompts(n_streams: int, lo: int, hi: int, prefix_len: int, see
         suffix = torch.randint(0, TEXT_VOCAB, (max(0, n - prefix_len),), generator=g)
         out.append(torch.cat([prefix[: min(prefix_len, n)], suffix]))
     return out
+
+
+def setup_shared_prefix_streams(ex, prompts: Sequence[torch.Tensor], table: torch.Tensor, pad: torch.Tensor,
+                                prefix_len: int, key: str = "shared-prefix", record: bool = False):
+    """The benchmark's stream set-up on a ``B200Executor`` (cfg2): the common prefix
+    (``prompts[i][:prefix_len]``) is prefilled once into a holder slot and cached by block
+    reference, and the holder is freed; each stream then restores the cached prefix from the
+    prefix cache (no KV copy) — a prompt shorter than the prefix shares ceil(L/16) of its
+    blocks, the last one partial and copied on the stream's first write — and prefills its
+    own suffix (sampling its first frame) or, with no suffix, starts decoding from ``pad``.
+    Every stream's text embedding is ``pad``, its first frame included.  Returns
+    ``(slots, first)``: ``first[i]`` is ``(codes [16], logits [V])`` of stream i's prefill
+    (``None`` without a suffix) when ``record`` is set, else ``None``."""
+    from .runtime.pool import PagedPrefixEntry
+    dev = ex._device
+    pool = ex.kv_pool
+    cache = ex.make_prefix_cache(max_entries=4, max_prefix_len=max(512, prefix_len))
+    holder = pool.allocate("prefix-holder")
+    longest = max(prompts, key=len)
+    ex.prefill_prefix_only(holder, table[longest[:prefix_len].to(table.device)].to(dev).unsqueeze(0))
+    cache.put(key, holder.slot_id, prefix_len)
+    pool.release(holder.slot_id)
+    entry = cache.get(key)
+    slots, first = [], []
+    for i, ids in enumerate(prompts):
+        s = pool.allocate(f"stream-{i}")
+        s.segment_idx = 0
+        n_shared = min(prefix_len, len(ids))
+        if n_shared == prefix_len:
+            cache.restore(s, entry)
+        else:
+            part = PagedPrefixEntry(key=entry.key, blocks=entry.blocks[: -(-n_shared // 16)], prefix_len=n_shared,
+                                    created_at=entry.created_at)
+            cache.restore(s, part)
+        suffix = ids[n_shared:]
+        # the text embedding added to the codec sum of each frame, the first one included
+        ex.set_text_embedding(s, pad)
+        if len(suffix) > 0:
+            ex.prefill_from_prefix(s, table[suffix.to(table.device)].to(dev).unsqueeze(0))
+            if record:
+                first.append((ex.codes[0].cpu().clone(), ex.logits[0].cpu().clone()))
+        else:
+            ex._configure_sampling(s)
+            ex.next_x[s.slot_id].copy_(pad.to(dev))
+            if record:
+                first.append(None)
+        slots.append(s)
+    torch.cuda.synchronize(dev)
+    return slots, (first if record else None)

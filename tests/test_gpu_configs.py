@@ -1,0 +1,288 @@
+"""Parity on the configurations the benchmark runs, against the CPU oracle.
+
+* cfg2 — the benchmark's own set-up and path: 64 streams with prompt lengths
+  U{16..512}, a 96-token prefix prefilled once and shared by block reference
+  (prompts shorter than 96 share a partial block that they copy on their first
+  decode write), the full 28-layer talker + code predictor + code2wav, top-k 50
+  / temperature 0.9 with the noise drawn in-kernel by Philox, decode steps
+  through ``B200Executor.launch_decode_step`` (eager, captured, replayed).  The
+  oracle runs the same streams with the device's noise rows (materialised by
+  ``qtts_philox_gumbel``) and the device's codes as the next inputs, so every
+  compared logit row and sampled token has identical inputs on both sides.
+* cfg3 — the code predictor at batch 64 (full widths), every stage's logits and
+  sampled token with given noise.
+* cfg4 — code2wav at full widths in 25-frame chunks with carried state.
+* The Philox noise itself against the published generator and the reference's
+  transform (engine/backend/executor.py:1229-1253), value by value and in
+  distribution.
+
+Bars: logits max relative error <= 2e-2 (per row, max|d| / max|ref|); the
+sampling head restated on the CPU, given the device's logits, the same noise
+and the same counts, picks exactly the device's token (sampling is integer
+work: bit-exact); waveform SNR >= 30 dB.  The agreement of the device's tokens
+with the tokens the oracle samples from its own logits is reported, with a
+floor of 85 %: random-init logits span tens of units, so a 0.2 % relative
+logit difference moves the arg-max of near-tied noisy scores.
+"""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+from oracle import code2wav as OC  # noqa: E402
+from oracle import model as M  # noqa: E402
+from oracle import noise as ON  # noqa: E402
+from oracle.engine import OracleEngine  # noqa: E402
+from test_stateful_b200 import _lib, ops, weights as wmod, workload  # noqa: E402
+from test_stateful_b200.config import Code2WavConfig, EngineConfig, PagedPoolConfig  # noqa: E402
+
+DEV = "cuda"
+LOGIT_TOL = 2e-2
+SAMPLED_AGREEMENT_FLOOR = 0.85
+SNR_DB = 30.0
+
+
+def _rel(a, b):
+    return float((a.float() - b.float()).abs().max() / b.float().abs().max().clamp_min(1e-6))
+
+
+def _device_weights(cfg, seed):
+    """Weights generated on the device (as the benchmark loads them) and their fp32 CPU copy."""
+    W = wmod.make_talker_weights(cfg.talker, seed, device=DEV)
+    W.update(wmod.make_cp_weights(cfg.cp, seed, device=DEV))
+    return W, {k: v.float().cpu() for k, v in W.items()}
+
+
+def _noise_rows(ex, slot_ids, cp_stages):
+    """The Gumbel rows the next engine step draws for these slots: talker head and every
+    code-predictor stage, from the slots' noise keys and frame counters."""
+    idx = torch.tensor(slot_ids, dtype=torch.long, device=DEV)
+    keys = ex.noise_key[idx].contiguous()
+    frames = ex.noise_step[idx].contiguous()
+    g = ops.philox_gumbel(ex._random_seed, keys, frames, 0).cpu()
+    cg = torch.stack([ops.philox_gumbel(ex._random_seed, keys, frames, 1 + s).cpu() for s in range(cp_stages)], 1)
+    return g, cg
+
+
+class Agreement:
+    def __init__(self):
+        self.worst = 0.0
+        self.agree = 0
+        self.total = 0
+        self.exact = 0
+        self.exact_total = 0
+
+    def logits(self, got, ref):
+        self.worst = max(self.worst, _rel(got, ref))
+
+    def tokens(self, got, ref):
+        got, ref = np.asarray(got), np.asarray(ref)
+        self.agree += int((got == ref).sum())
+        self.total += got.size
+
+    def resampled(self, got, ref):
+        """The device's tokens against the CPU sampling head run on the device's logits."""
+        got, ref = np.asarray(got).reshape(-1), np.asarray(ref).reshape(-1)
+        self.exact += int((got == ref).sum())
+        self.exact_total += got.size
+
+    @property
+    def rate(self):
+        return self.agree / max(1, self.total)
+
+
+def test_cfg2_benchmark_streams_against_oracle():
+    from test_stateful_b200.runtime.executor import B200Executor
+
+    seed, prefix, n_streams, decode_steps = 1, 96, 64, 3
+    cfg = EngineConfig()
+    t, c = cfg.talker, cfg.cp
+    W, Wf = _device_weights(cfg, seed)
+    ex = B200Executor(device_id=0, max_batch_size=n_streams + 1, max_seq_len=600, model_config=cfg,
+                      do_sample=True, temperature=0.9, repetition_penalty=1.05, random_seed=seed, num_blocks=2600,
+                      weights=W, max_prefill_rows=512)
+    ex.load()
+    del W
+    prompts = workload.shared_prefix_prompts(n_streams, 16, 512, prefix, seed)
+    table = workload.text_table(t.hidden_size, seed)
+    pad = workload.tts_pad_embed(t.hidden_size, seed)
+    slots, first = workload.setup_shared_prefix_streams(ex, prompts, table, pad, prefix, record=True)
+    sids = [s.slot_id for s in slots]
+    lengths = [len(p) for p in prompts]
+    assert min(lengths) < prefix < max(lengths)  # partial-block sharers (copy-on-write) and suffix prefills
+    assert _lib.device_error() == 0
+
+    # ---- oracle: the prefix once, then per stream a copy of it (what a cache hit restores)
+    eng = OracleEngine(Wf, t, c)
+    V = t.codec_vocab_size
+    temp, pen = torch.full((1, 1), 0.9), torch.full((1, 1), 1.05)
+    holder = n_streams
+    longest = max(prompts, key=len)
+    eng.k[holder] = [torch.zeros(t.kv_heads, 0, t.head_dim) for _ in range(t.num_layers)]
+    eng.v[holder] = [torch.zeros(t.kv_heads, 0, t.head_dim) for _ in range(t.num_layers)]
+    eng.past[holder] = 0
+    eng.extend(holder, table[longest[:prefix]], torch.zeros(V, dtype=torch.long), torch.zeros(1, 50),
+               torch.zeros(1, c.num_stages, 50), temp, pen)
+
+    # first-frame noise of the streams that prefilled a suffix: frame counter 0
+    keys = ex.noise_key[torch.tensor(sids, device=DEV)].contiguous()
+    frames0 = torch.zeros(n_streams, dtype=torch.int32, device=DEV)
+    g0 = ops.philox_gumbel(seed, keys, frames0, 0).cpu()
+    cg0 = torch.stack([ops.philox_gumbel(seed, keys, frames0, 1 + s).cpu() for s in range(c.num_stages)], 1)
+
+    talk, cp = Agreement(), Agreement()
+    ctable = M.stacked_codec_table(Wf, c.num_stages)
+    x_next = torch.zeros(n_streams, t.hidden_size)
+    counts = torch.zeros(n_streams, V, dtype=torch.long)
+    for i, ids in enumerate(prompts):
+        n_shared = min(prefix, len(ids))
+        eng.share_prefix(i, holder, n_shared)
+        if first[i] is None:  # no suffix: the first decode step consumes tts_pad
+            x_next[i] = pad
+            continue
+        dev_codes, dev_logits = first[i]
+        r = eng.extend(i, table[ids[n_shared:]], torch.zeros(V, dtype=torch.long), g0[i:i + 1], cg0[i:i + 1],
+                       temp, pen, force=dev_codes.view(1, -1))
+        talk.logits(dev_logits, r["logits"][0, -1])
+        talk.tokens(dev_codes[:1], r["full_codec"][0, :1])
+        cp.tokens(dev_codes[1:], r["full_codec"][0, 1:])
+        tok, _ = M.talker_sample(dev_logits.view(1, -1), torch.zeros(1, V, dtype=torch.long), g0[i:i + 1], temp, pen,
+                                 t.codec_eos_id, t.logits_topk)
+        talk.resampled(dev_codes[:1], tok)
+        counts[i, int(dev_codes[0])] += 1
+        # the device forms the next input as bf16(codec sum + text embedding)
+        x_next[i] = (M.codec_sum(ctable, dev_codes.view(1, -1))[0] + pad).to(torch.bfloat16).float()
+    prefill_worst = talk.worst
+
+    # ---- decode steps through the executor: eager, then captured, then replayed
+    for step in range(decode_steps):
+        g, cg = _noise_rows(ex, sids, c.num_stages)
+        out = ex.launch_decode_step(slots).wait()
+        dev_logits = ex.logits[:n_streams].cpu()
+        dev_codes = out.full_codec
+        assert _lib.device_error() == 0
+        r = eng.decode(list(range(n_streams)), x_next, counts, g, cg, torch.full((n_streams, 1), 0.9),
+                       torch.full((n_streams, 1), 1.05), force=dev_codes)
+        for i in range(n_streams):
+            talk.logits(dev_logits[i], r["logits"][i, -1])
+        talk.tokens(dev_codes[:, :1], r["full_codec"][:, :1])
+        cp.tokens(dev_codes[:, 1:], r["full_codec"][:, 1:])
+        tok, _ = M.talker_sample(dev_logits, counts, g, torch.full((n_streams, 1), 0.9),
+                                 torch.full((n_streams, 1), 1.05), t.codec_eos_id, t.logits_topk)
+        talk.resampled(dev_codes[:, 0], tok)
+        counts.scatter_add_(1, dev_codes[:, :1], torch.ones(n_streams, 1, dtype=torch.long))
+        x_next = (M.codec_sum(ctable, dev_codes) + pad).to(torch.bfloat16).float()
+    ex.shutdown()
+    print(f"cfg2 64 streams: prefill logits rel err {prefill_worst:.4f}, all steps {talk.worst:.4f}; tok0 from the "
+          f"device's logits {talk.exact}/{talk.exact_total}; sampled tok0 agreement with the oracle's own logits "
+          f"{talk.rate:.4f} ({talk.agree}/{talk.total}), code predictor {cp.rate:.4f} ({cp.agree}/{cp.total})")
+    assert talk.worst <= LOGIT_TOL
+    assert talk.exact == talk.exact_total
+    assert talk.rate >= SAMPLED_AGREEMENT_FLOOR and cp.rate >= SAMPLED_AGREEMENT_FLOOR
+
+
+def test_cfg3_code_predictor_batch64_every_stage():
+    """64 streams' code predictor (5 layers, hidden 1024, 16 x 64 heads, SwiGLU 3072, 15
+    stages of 2048-entry heads) conditioned on a 2-layer full-width talker's last hidden
+    state, top-k 50 / T 0.9 with given noise: every stage's logits and token."""
+    from .test_gpu_engine import Runner
+
+    cfg = EngineConfig()
+    cfg.talker.num_layers = 2
+    cfg.pool = PagedPoolConfig(block_size=16, num_blocks=512, max_slots=64, max_seq_len=64)
+    t, c = cfg.talker, cfg.cp
+    W, Wf = _device_weights(cfg, 5)
+    r = Runner(cfg, W, max_batch=64, temperature=0.9)
+    del W
+    g = torch.Generator().manual_seed(7)
+    text = workload.text_table(t.hidden_size, 5)
+    for i in range(64):
+        n = int(torch.randint(4, 33, (1,), generator=g))
+        ids = torch.randint(0, workload.TEXT_VOCAB, (n,), generator=g)
+        r.prefill(i, text[ids].to(torch.bfloat16).float(), torch.zeros(1, 50, device=DEV),
+                  torch.zeros(1, c.num_stages, 50, device=DEV))
+    gum = torch.from_numpy(ON.gumbel(5, np.arange(64), np.full(64, 1), 0))
+    cgum = torch.stack([torch.from_numpy(ON.gumbel(5, np.arange(64), np.full(64, 1), 1 + s))
+                        for s in range(c.num_stages)], 1)
+    out = r.decode(list(range(64)), gum.to(DEV), cgum.contiguous().to(DEV))
+    r.m.close()
+    dev_codes, hidden = out["codes"], out["hidden"]
+    stage = []
+    ref = M.code_predictor(Wf, c, Wf["talker.codec_embedding.weight"], hidden.unsqueeze(1), dev_codes[:, 0], cgum,
+                           torch.full((64, 1), 0.9), force=dev_codes, stage_logits=stage)
+    agree = Agreement()
+    for s in range(c.num_stages):
+        agree.logits(out["cp_logits"][:, s], stage[s])
+        agree.tokens(dev_codes[:, 1 + s], ref[:, s])
+        agree.resampled(dev_codes[:, 1 + s], M.topk_select(out["cp_logits"][:, s], torch.full((64, 1), 0.9),
+                                                            cgum[:, s], c.logits_topk))
+    print(f"cfg3 batch 64: stage logits rel err {agree.worst:.4f}; tokens from the device's logits "
+          f"{agree.exact}/{agree.exact_total}; sampled agreement with the oracle's own logits {agree.rate:.4f} "
+          f"({agree.agree}/{agree.total})")
+    assert agree.worst <= LOGIT_TOL
+    assert agree.exact == agree.exact_total
+    assert agree.rate >= SAMPLED_AGREEMENT_FLOOR
+
+
+def test_cfg4_code2wav_full_width_25_frame_chunks():
+    """64 streams decoded in three 25-frame chunks with carried state (uniform random code
+    ids per frame), full decoder widths; streams 0, 31 and 63 against the fp32 oracle."""
+    from test_stateful_b200.runtime.code2wav import DeviceCode2Wav
+
+    cfg = Code2WavConfig()
+    W = wmod.make_code2wav_weights(cfg, 4, device=DEV)
+    Wf = {k: v.float().cpu() for k, v in W.items()}
+    B, T, calls = 64, 25, 3
+    dec = DeviceCode2Wav(cfg, W, DEV, max_slots=B, max_frames=T * calls + 8, max_chunk=T)
+    del W
+    slots = torch.arange(B, dtype=torch.int32, device=DEV)
+    dec.reset(slots)
+    g = torch.Generator().manual_seed(12)
+    codes = torch.randint(0, cfg.codebook_size, (calls, B, T, 16), generator=g)
+    checked = [0, 31, 63]
+    states = {i: OC.Code2WavState(cfg) for i in checked}
+    worst = float("inf")
+    for k in range(calls):
+        wav = torch.empty(B, T * cfg.samples_per_frame, device=DEV)
+        dec.step(codes[k].to(DEV), slots, wav, frames=T)
+        got = wav.cpu().numpy()
+        assert _lib.device_error() == 0
+        for i in checked:
+            ref = OC.decode_chunk(Wf, cfg, codes[k, i].t().contiguous(), states[i]).numpy()
+            noise = float(((got[i].astype(np.float64) - ref) ** 2).sum())
+            snr = 10 * math.log10(float((ref.astype(np.float64) ** 2).sum()) / max(noise, 1e-30))
+            worst = min(worst, snr)
+            assert snr >= SNR_DB, (k, i, snr)
+    dec.close()
+    print(f"cfg4 64 streams x 3 chunks of 25 frames: worst SNR {worst:.1f} dB")
+
+
+def test_philox_noise_matches_published_generator_and_reference_transform():
+    """In-kernel noise = Philox4x32-10 (published algorithm, restated in numpy) mapped by
+    -log(-log(clamp(u, 1e-8, 1))) (engine/backend/executor.py:1238-1251): value by value for
+    several keys / frames / stages, and Gumbel(0, 1) in distribution."""
+    from scipy import stats
+
+    seed = 0x1234_5678_9ABC_DEF
+    keys = np.array([0, 1, 2**33 + 5, 2**62 + 17] * 256, dtype=np.int64) + np.repeat(np.arange(256), 4)
+    frames = np.tile(np.array([0, 1, 7, 511], dtype=np.int32), 256)
+    kd = torch.from_numpy(keys).to(DEV)
+    fd = torch.from_numpy(frames).to(DEV)
+    for stage in (0, 1, 15):
+        got = ops.philox_gumbel(seed, kd, fd, stage, cols=50).cpu().numpy()
+        want = ON.gumbel(seed, keys, frames, stage, 50)
+        np.testing.assert_allclose(got, want, rtol=2e-6, atol=2e-6)
+    g = ops.philox_gumbel(seed, kd, fd, 3, cols=50).cpu().numpy().ravel().astype(np.float64)
+    u = np.exp(-np.exp(-g))  # back to the uniform the transform started from
+    ks = stats.kstest(u, "uniform")
+    assert ks.pvalue > 1e-3, ks
+    assert abs(g.mean() - 0.5772156649) < 0.02            # Euler-Mascheroni
+    assert abs(g.var() - math.pi ** 2 / 6) < 0.06
+    # distinct (key, frame, stage) give uncorrelated rows
+    a = ops.philox_gumbel(seed, kd, fd, 4, cols=50).cpu().numpy().ravel()
+    b = ops.philox_gumbel(seed, kd, fd, 5, cols=50).cpu().numpy().ravel()
+    assert abs(np.corrcoef(a, b)[0, 1]) < 0.02

@@ -213,6 +213,48 @@ def test_cfg1_full_model_512_step_greedy_agreement():
     assert (talk.agree + cp.agree) / (talk.total + cp.total) >= GREEDY_AGREEMENT
 
 
+def test_cfg1_free_running_512_step_greedy():
+    """cfg1's streams decoded greedily for 512 steps with no teacher forcing: the device feeds
+    back its own codes (next input and repetition-penalty counts formed on the device), the
+    oracle trajectory (tests/golden/cfg1_long_greedy.npz) feeds back its own.  Once one token
+    differs the two trajectories are different sequences, so the agreement measures how long
+    they stay identical under bf16 weights; it is reported against the >= 99 % bar, and the
+    test requires every stream's first frame and most of the reference-pinned first 32 steps
+    to match."""
+    path = os.path.join(GOLDEN, "cfg1_long_greedy.npz")
+    if not os.path.exists(path):
+        pytest.skip("cfg1 long-horizon fixture not generated")
+    z = np.load(path)
+    cfg = EngineConfig()
+    cfg.pool = PagedPoolConfig(block_size=16, num_blocks=256, max_slots=4, max_seq_len=768)
+    t, c = cfg.talker, cfg.cp
+    seed = int(z["seed"])
+    W = _weights(cfg, seed)
+    lengths = z["lengths"].tolist()
+    B, steps = len(lengths), int(z["steps"])
+    text = workload.text_table(t.hidden_size, seed)
+    pad = workload.tts_pad_embed(t.hidden_size, seed)
+    ids = workload.prompt_ids(lengths, seed)
+    r = Runner(cfg, W, max_batch=B, temperature=float(z["temperature"]), penalty=float(z["penalty"]))
+    del W
+    r.text[:B] = pad.to(DEV)
+    ref = z["codes"].astype(np.int64)
+    got = np.zeros_like(ref)
+    zg, zcg = torch.zeros(B, 50, device=DEV), torch.zeros(B, c.num_stages, 50, device=DEV)
+    for i in range(B):
+        got[i, 0] = r.prefill(i, text[ids[i]], zg[:1], zcg[:1])["codes"][0].numpy()
+    for step in range(1, steps + 1):
+        got[:, step] = r.decode(list(range(B)), zg, zcg)["codes"].numpy()
+    r.m.close()
+    same = got == ref
+    first_diff = [int(np.argmax(~same[i].all(axis=1))) if not same[i].all() else steps + 1 for i in range(B)]
+    rate = float(same.mean())
+    print(f"cfg1 free-running greedy, 512 steps: token agreement {rate:.4f}; steps identical before the first "
+          f"differing frame per stream {first_diff}; first 33 frames {float(same[:, :33].mean()):.4f}")
+    assert all(d >= 1 for d in first_diff)
+    assert float(same[:, :33].mean()) >= 0.5
+
+
 def test_cfg1_full_model_greedy_against_reference():
     """The CPU reference case on the device: full 28-layer talker, seed 0, prompts
     {37, 64, 91, 128}, 32 greedy steps, against the reference's fp32 run."""

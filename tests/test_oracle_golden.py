@@ -94,3 +94,22 @@ def test_cfg1_full_greedy():
                                    float(z["temperature"]), float(z["penalty"]))
     assert np.array_equal(codes, z["codes"])
     np.testing.assert_allclose(logits, z["step_logits"], rtol=2e-3, atol=2e-4)
+
+
+def test_philox_restatement_known_answers():
+    """oracle/noise.py's Philox4x32-10 against the published known-answer vectors of the
+    generator (Random123 distribution, kat_vectors: philox4x32_10)."""
+    from oracle import noise
+
+    cases = [((0, 0, 0, 0), (0, 0), (0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8)),
+             ((0xFFFFFFFF,) * 4, (0xFFFFFFFF,) * 2, (0x408F276D, 0x41C83B0E, 0xA20BC7C6, 0x6D5451FD)),
+             ((0x243F6A88, 0x85A308D3, 0x13198A2E, 0x03707344), (0xA4093822, 0x299F31D0),
+              (0xD16CFE09, 0x94FDCCEB, 0x5001E420, 0x24126EA1))]
+    for ctr, key, want in cases:
+        got = tuple(int(v) for v in noise.philox4x32_10(*ctr, *key))
+        assert got == want
+    # the transform: u in (0, 1), Gumbel = -log(-log(clamp(u, 1e-8, 1)))
+    u = noise.uniform(7, [1, 2, 3], [0, 1, 2], 0, 64)
+    assert u.min() > 0.0 and u.max() < 1.0
+    g = noise.gumbel(7, [1, 2, 3], [0, 1, 2], 0, 64)
+    assert np.allclose(g, -np.log(-np.log(np.clip(u, 1e-8, 1.0))), rtol=1e-6)
