@@ -19,8 +19,11 @@ per-step text embeddings copied from pinned host memory and the codec frames
 and audio chunks copied back every step.
 
 ``--impl reference`` times the CPU oracle (a restatement of the reference's
-PyTorch modules, fp32) on the host cores.  Under torchrun each rank is an
-independent replica (request-sharded, no collective on the decode path).
+PyTorch modules, fp32: talker, sampling head, code predictor with its full
+per-stage recompute, streaming code2wav) on the host cores, on the same 64
+streams and config.  Under torchrun each rank is an independent replica
+(request-sharded, no collective on the decode path); rank 0 times the CPU
+baseline only after every rank has left the process group.
 """
 
 from __future__ import annotations
@@ -46,6 +49,24 @@ PREFIX = 96
 SEED = 1
 
 
+def workload_config(world: int) -> dict:
+    """The ``config`` both arms print (the same dict, so the two lines compare like for like)."""
+    return {"workload": "cfg2: 64 ragged streams/GPU, ctx U{16..512} + 96-token shared prefix, "
+                        "8192 x 16-token KV blocks, top-k 50 / T 0.9 sampling, 512 decode steps",
+            "streams_per_gpu": STREAMS, "parallelism": f"replicas x{world} (request-sharded, no collective)",
+            "l2": "inputs larger than L2 (KV ~4 GB + weights ~3 GB read per step)",
+            "step": "talker 28 layers + sampling + 15-stage code predictor + codec sum + "
+                    "streaming code2wav (1920 samples/stream)"}
+
+
+def host_threads() -> int:
+    """Host cores this process may run on (the GPU box's cgroup/affinity, not the machine's)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -57,6 +78,11 @@ def parse():
     ap.add_argument("--profile", action="store_true",
                     help="timed region only, inside an NVTX range 'timed' (for ncu --nvtx-include timed/); "
                          "no CPU baseline, e2e or roofline pass")
+    ap.add_argument("--roofline-only", action="store_true",
+                    help="build the workload, run the roofline passes once and print them (the small case "
+                         "for an ncu DRAM capture of the attention and GEMM kernels)")
+    ap.add_argument("--num-blocks", type=int, default=8192,
+                    help="KV pool blocks (8192 = the benchmark's pool; the streams use about 2300)")
     return ap.parse_args()
 
 
@@ -120,51 +146,51 @@ def build_workload(device):
     max_seq = 512 + steps_total + 16
     ex = B200Executor(device_id=device.index or 0, max_batch_size=STREAMS + 1, max_seq_len=max_seq,
                       model_config=EngineConfig(), do_sample=True, temperature=0.9, repetition_penalty=1.05,
-                      random_seed=SEED, num_blocks=8192, weight_seed=SEED, max_prefill_rows=512)
+                      random_seed=SEED, num_blocks=ARGS.num_blocks, weight_seed=SEED, max_prefill_rows=512)
     ex.load()
     t = ex._config.talker
     prompts = workload.shared_prefix_prompts(STREAMS, 16, 512, PREFIX, SEED)
     table = workload.text_table(t.hidden_size, SEED, device=device)
     pad = workload.tts_pad_embed(t.hidden_size, SEED, device=device)
-    pool = ex.kv_pool
-    cache = ex.make_prefix_cache(max_entries=4, max_prefix_len=512)
-    # the shared prefix: prefill once into a holder slot, cache its blocks, free the slot
-    holder = pool.allocate("prefix-holder")
-    longest = max(prompts, key=len)
-    ex.prefill_prefix_only(holder, table[longest[:PREFIX].to(device)].unsqueeze(0))
-    cache.put("shared-96", holder.slot_id, PREFIX)
-    pool.release(holder.slot_id)
-    entry = cache.get("shared-96")
-    slots = []
-    for i, ids in enumerate(prompts):
-        s = pool.allocate(f"stream-{i}")
-        s.segment_idx = 0
-        n_shared = min(PREFIX, len(ids))
-        cache.restore(s, entry) if n_shared == PREFIX else _share_partial(cache, s, entry, n_shared)
-        suffix = ids[n_shared:]
-        if len(suffix) > 0:
-            ex.prefill_from_prefix(s, table[suffix.to(device)].unsqueeze(0))
-        else:
-            ex._configure_sampling(s)
-            ex.next_x[s.slot_id].copy_(pad)
-        ex.set_text_embedding(s, pad)
-        slots.append(s)
-    torch.cuda.synchronize(device)
+    slots, _ = workload.setup_shared_prefix_streams(ex, prompts, table, pad, PREFIX)
     return ex, slots, prompts, pad
 
 
-def _share_partial(cache, slot, entry, n):
-    """A prompt shorter than the prefix shares ceil(n/16) prefix blocks; the
-    last one is partial and gets copied on the first write (copy-on-write)."""
-    from test_stateful_b200.runtime.pool import PagedPrefixEntry
-    part = PagedPrefixEntry(key=entry.key, blocks=entry.blocks[: -(-n // 16)], prefix_len=n,
-                            created_at=entry.created_at)
-    cache.restore(slot, part)
-
-
 # ----------------------------------------------------------------------------- roofline helpers
+# DRAM traffic per launch from an ncu capture of the same kernels on this workload
+# (bench.py --roofline-only --num-blocks 2600, dram__bytes_read.sum + dram__bytes_write.sum):
+# attention read 44 404 792 + wrote 1 986 bytes per launch for 43 307 008 unique KV bytes (the
+# 96-token prefix every row shares is read from DRAM once), GEMM 26 023 022 + 570 bytes per
+# launch for 27 262 976 algorithmic bytes (its activations stay in L2).  Traffic scales with the
+# unique blocks read (attention) and the weight bytes (GEMM).
+ATTN_TRAFFIC_PER_UNIQUE = (44404792 + 1986) / 43307008
+GEMM_TRAFFIC_RATIO = (26023022 + 570) / 27262976
+
+
+def _replay_timed(fn, reps):
+    """Capture ``reps`` calls of ``fn(i)`` in a CUDA graph on a side stream, warm it, and time
+    one replay with CUDA events on that stream; returns seconds per call."""
+    gs = torch.cuda.Stream()
+    with torch.cuda.stream(gs):
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=gs):
+            for i in range(reps):
+                fn(i)
+        graph.replay()
+        gs.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(gs)
+        graph.replay()
+        e1.record(gs)
+        gs.synchronize()
+    return e0.elapsed_time(e1) / 1e3 / reps
+
+
 def attention_roofline(ex, slots, peaks):
-    """Paged decode attention at the workload's final state, timed with CUDA events."""
+    """Paged decode attention at the workload's current state (every layer of the pool,
+    twice), timed with CUDA events.  Algorithmic bytes count each row's visible keys (the
+    shared prefix once per row, as the reference's per-stream gather reads it); unique bytes
+    count every KV block once, with the most keys any row reads from it."""
     from test_stateful_b200 import ops
     m = ex.model
     t = ex._config.talker
@@ -176,51 +202,86 @@ def attention_roofline(ex, slots, peaks):
     max_ctx = ex._config.pool.max_blocks_per_seq * 16
     out = torch.empty(n, t.num_heads * t.head_dim, device=dev, dtype=torch.bfloat16)
     nb = -(-max_ctx // 16)
-    splits = max(1, -(-nb // 1))  # scratch for any split size
-    ws_o = torch.empty(n * t.num_heads * splits * t.head_dim, device=dev)
-    ws_ml = torch.empty(n * t.num_heads * splits * 2, device=dev)
+    ws_o = torch.empty(n * t.num_heads * nb * t.head_dim, device=dev)   # scratch for any split size
+    ws_ml = torch.empty(n * t.num_heads * nb * 2, device=dev)
     table = m.pool.block_table
-
     split = int(os.environ.get("QTTS_ATTN_SPLIT", "8"))  # the engine's split size
 
-    def run(layer):
-        ops.paged_attention(q, m.pool.kv, layer, table, row_slot, ctx, max_ctx, out=out, ws_o=ws_o, ws_ml=ws_ml,
-                            split_blocks=split)
+    def run(i):
+        ops.paged_attention(q, m.pool.kv, i % t.num_layers, table, row_slot, ctx, max_ctx, out=out, ws_o=ws_o,
+                            ws_ml=ws_ml, split_blocks=split)
 
     for layer in range(3):
         run(layer)
     torch.cuda.synchronize()
-    # all layers of the pool, twice, captured in a CUDA graph and replayed on one stream
-    reps = 2 * t.num_layers
-    gs = torch.cuda.Stream()
-    with torch.cuda.stream(gs):
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=gs):
-            for i in range(reps):
-                run(i % t.num_layers)
-        graph.replay()
-        gs.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(gs)
-        graph.replay()
-        e1.record(gs)
-        gs.synchronize()
-    sec = e0.elapsed_time(e1) / 1e3 / reps
-    kv_bytes = int(ctx.sum()) * 2 * t.kv_heads * t.head_dim * 2      # K+V of one layer
+    sec = _replay_timed(run, 2 * t.num_layers)
+    per_key = 2 * t.kv_heads * t.head_dim * 2                 # K+V of one layer, fp16
+    kv_bytes = int(ctx.sum()) * per_key
     qo_bytes = n * t.num_heads * t.head_dim * (4 + 2)
     algo = kv_bytes + qo_bytes
+    # unique blocks: the most keys any row reads from each block id
+    tab = table[row_slot.long()].cpu()
+    keys_in_block = {}
+    for r, c in enumerate(ctx.cpu().tolist()):
+        for j in range(-(-c // 16)):
+            b = int(tab[r, j])
+            keys_in_block[b] = max(keys_in_block.get(b, 0), min(16, c - 16 * j))
+    unique = sum(keys_in_block.values()) * per_key + qo_bytes
     gbs = algo / sec / 1e9
     peak = peaks.get("hbm_gbs")
-    # DRAM traffic per launch: an ncu capture of the same kernel on 64 rows at mean context 858
-    # read 228.13 MB + wrote 5.01 MB for 225.93 MB of algorithmic bytes
-    # (profiles/paged_attn_kernel_d128_64rows_ctx520.md); traffic grows with the blocks read,
-    # so this launch's traffic is scaled from that ratio
-    traffic_ratio = (228.13 + 5.01) / 225.93
     return {"kernel": "paged_attn_tc_kernel + attn_combine_kernel", "bound": "hbm", "achieved": round(gbs, 1),
             "peak": peak, "unit": "GB/s", "frac": round(gbs / peak, 3) if peak else None,
-            "traffic": int(algo * traffic_ratio),
-            "traffic_source": "ncu dram__bytes_read+write of a 64-row, mean-context-858 capture, scaled by bytes",
-            "algorithmic_bytes_per_launch": algo, "launch_us": round(sec * 1e6, 2),
+            "traffic": int(unique * ATTN_TRAFFIC_PER_UNIQUE),
+            "traffic_source": "ncu dram__bytes_read+write per launch over unique KV bytes, scaled to this launch",
+            "algorithmic_bytes_per_launch": algo, "unique_bytes_per_launch": unique,
+            "achieved_unique": round(unique / sec / 1e9, 1),
+            "frac_unique": round(unique / sec / 1e9 / peak, 3) if peak else None,
+            "ctx_mean": round(float(ctx.float().mean()), 1), "launch_us": round(sec * 1e6, 2),
+            "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)"}
+
+
+def gemm_roofline(ex, peaks):
+    """The dominant kernel of the step, gemm_tc_kernel<64,3,hi/lo> (about two thirds of the
+    step's launch time), on the talker's projections: the 28 layers' QKV, O, gate/up and down
+    weights of the loaded model at M = 64 tokens with bf16 hi/lo activation operands, one
+    CUDA graph of all 112 launches (weights 2.83 GB > L2, so every launch streams from HBM),
+    timed with CUDA events.  Plain fp32 epilogues stand in for the step's fused ones (QKV norm
+    + RoPE + KV store, SwiGLU, residual); their extra bytes are a few MB per step."""
+    from test_stateful_b200 import _lib, ops
+    m = ex.model
+    t = ex._config.talker
+    dev = m.w_qkv.device
+    g = torch.Generator(device=dev).manual_seed(0)
+    acts = {}
+    for K in sorted({t.hidden_size, t.q_size, t.intermediate_size}):
+        acts[K] = ops.split_hilo(torch.randn(STREAMS, K, generator=g, device=dev))
+    shapes = []
+    for l in range(t.num_layers):
+        for w in (m.w_qkv[l], m.w_o[l], m.w_gate_up[l], m.w_down[l]):
+            shapes.append(w)
+    outs = {}
+    for w in shapes:
+        outs.setdefault(w.shape[0], torch.empty(STREAMS, w.shape[0], device=dev))
+
+    def run(i):
+        w = shapes[i % len(shapes)]
+        hi, lo = acts[w.shape[1]]
+        ops.gemm(hi, w, _lib.EPI_F32, out=outs[w.shape[0]], x_lo=lo)
+
+    for i in range(4):
+        run(i)
+    torch.cuda.synchronize()
+    sec = _replay_timed(run, len(shapes))
+    algo = sum(w.shape[0] * w.shape[1] * 2 + STREAMS * w.shape[1] * 4 + STREAMS * w.shape[0] * 4
+               for w in shapes) / len(shapes)
+    gbs = algo / sec / 1e9
+    peak = peaks.get("hbm_gbs")
+    return {"kernel": "gemm_tc_kernel<64,3,hi/lo> (talker QKV/O/gate-up/down, M = 64)", "bound": "hbm",
+            "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s", "frac": round(gbs / peak, 3) if peak else None,
+            "traffic": int(algo * GEMM_TRAFFIC_RATIO),
+            "traffic_source": "ncu dram__bytes_read+write per launch over algorithmic bytes, scaled to this launch",
+            "algorithmic_bytes_per_launch": int(algo), "launches": len(shapes),
+            "launch_us": round(sec * 1e6, 2), "talker_projections_ms": round(sec * len(shapes) * 1e3, 3),
             "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)"}
 
 
@@ -233,58 +294,96 @@ def load_peaks():
 
 
 # ----------------------------------------------------------------------------- CPU baseline
-def cpu_oracle_rate(n_streams=4, ctx=256, steps=40, warmup=1):
-    """The oracle (fp32, all host threads) on a bounded sample of the workload:
-    ``warmup`` untimed then ``steps`` timed decode steps of ``n_streams`` streams starting
-    at context ``ctx`` (about 10 s of CPU work at the default)."""
-    from oracle.engine import OracleEngine
-    from oracle import model as M
-    from test_stateful_b200 import weights as wmod
-    from test_stateful_b200.config import EngineConfig
-    torch.set_num_threads(os.cpu_count() or 1)
-    cfg = EngineConfig()
-    t, c = cfg.talker, cfg.cp
-    W = wmod.make_talker_weights(t, SEED, dtype=torch.float32)
-    W.update(wmod.make_cp_weights(c, SEED, dtype=torch.float32))
-    eng = OracleEngine(W, t, c)
-    g = torch.Generator().manual_seed(0)
-    for i in range(n_streams):
-        eng.k[i] = [torch.randn(t.kv_heads, ctx, t.head_dim, generator=g) * 0.5 for _ in range(t.num_layers)]
-        eng.v[i] = [torch.randn(t.kv_heads, ctx, t.head_dim, generator=g) * 0.5 for _ in range(t.num_layers)]
-        eng.past[i] = ctx
-    x = torch.randn(n_streams, t.hidden_size, generator=g) * 0.02
-    counts = torch.zeros(n_streams, t.codec_vocab_size, dtype=torch.long)
-    temp = torch.full((n_streams, 1), 0.9)
-    pen = torch.full((n_streams, 1), 1.05)
-    t0 = None
-    for k in range(warmup + steps):
-        if k == warmup:
-            t0 = time.perf_counter()
-        gum = M.gumbel_from_uniform(torch.rand(n_streams, 50, generator=g))
-        cgum = M.gumbel_from_uniform(torch.rand(n_streams, c.num_stages, 50, generator=g))
-        r = eng.decode(list(range(n_streams)), x, counts, gum, cgum, temp, pen)
-        x = r["codec_sum"]
-        counts = r["counts"]
-    dt = time.perf_counter() - t0
-    frames = n_streams * steps
-    return {"value": round(frames / dt, 3), "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"{steps} decode steps x {n_streams} streams at context {ctx}, full 28-layer talker + "
-                      f"15-stage code predictor (reference full recompute), fp32, {torch.get_num_threads()} threads",
+class CpuStep:
+    """The oracle (fp32 CPU restatement of the reference's talker, sampling head, code
+    predictor with its full per-stage recompute, codec sum and streaming code2wav) set up on
+    the benchmark's streams: their cfg2 context lengths, KV of random values (the values do not
+    change the work), all host threads.  ``step(n)`` runs one decode step of the first n
+    streams, code2wav included, and returns its seconds."""
+
+    def __init__(self):
+        from oracle.engine import OracleEngine
+        from oracle import code2wav as OC
+        from test_stateful_b200 import weights as wmod, workload
+        from test_stateful_b200.config import EngineConfig
+        torch.set_num_threads(host_threads())
+        cfg = EngineConfig()
+        t, c = cfg.talker, cfg.cp
+        W = wmod.make_talker_weights(t, SEED, dtype=torch.float32)
+        W.update(wmod.make_cp_weights(c, SEED, dtype=torch.float32))
+        self.Wc = wmod.make_code2wav_weights(cfg.c2w, SEED, dtype=torch.float32)
+        self.cfg, self.OC = cfg, OC
+        self.eng = OracleEngine(W, t, c)
+        g = torch.Generator().manual_seed(0)
+        lengths = [len(p) for p in workload.shared_prefix_prompts(STREAMS, 16, 512, PREFIX, SEED)]
+        for i, n in enumerate(lengths):
+            self.eng.k[i] = [torch.randn(t.kv_heads, n, t.head_dim, generator=g) * 0.5 for _ in range(t.num_layers)]
+            self.eng.v[i] = [torch.randn(t.kv_heads, n, t.head_dim, generator=g) * 0.5 for _ in range(t.num_layers)]
+            self.eng.past[i] = n
+        self.c2w_state = [OC.Code2WavState(cfg.c2w) for _ in range(STREAMS)]
+        self.x = torch.randn(STREAMS, t.hidden_size, generator=g) * 0.02
+        self.counts = torch.zeros(STREAMS, t.codec_vocab_size, dtype=torch.long)
+        self.g = g
+        self.lengths = lengths
+
+    def step(self, n: int) -> float:
+        from oracle import model as M
+        c = self.cfg.cp
+        t0 = time.perf_counter()
+        gum = M.gumbel_from_uniform(torch.rand(n, 50, generator=self.g))
+        cgum = M.gumbel_from_uniform(torch.rand(n, c.num_stages, 50, generator=self.g))
+        r = self.eng.decode(list(range(n)), self.x[:n], self.counts[:n], gum, cgum, torch.full((n, 1), 0.9),
+                            torch.full((n, 1), 1.05))
+        for i in range(n):
+            self.OC.decode_chunk(self.Wc, self.cfg.c2w, r["full_codec"][i].view(-1, 1), self.c2w_state[i])
+        self.x[:n] = r["codec_sum"]
+        self.counts[:n] = r["counts"]
+        return time.perf_counter() - t0
+
+
+def cpu_baseline_rate(n_streams=STREAMS, steps=6, warmup=1):
+    """``cpu_baseline`` of the GPU arm: ``steps`` timed decode steps of the oracle over the
+    benchmark's first ``n_streams`` streams (about 15-30 s of CPU work at the default)."""
+    cs = CpuStep()
+    for _ in range(warmup):
+        cs.step(n_streams)
+    dt = sum(cs.step(n_streams) for _ in range(steps))
+    return {"value": round(n_streams * steps / dt, 3), "unit": UNIT, "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"{steps} decode steps of the benchmark's first {n_streams} streams (cfg2 contexts, "
+                      f"{sum(cs.lengths[:n_streams]) / n_streams:.0f} mean), full 28-layer talker + 15-stage code "
+                      f"predictor (the reference's full recompute) + streaming code2wav, fp32, "
+                      f"{torch.get_num_threads()} threads",
             "seconds": round(dt, 2)}
 
 
 # ----------------------------------------------------------------------------- main arms
 def run_reference(rank, world):
+    """The reference arm: the oracle port of the reference's CPU path on this box's host cores,
+    same workload and config as the GPU arm.  Each of the arm's --warmup + --steps steps is one
+    decode step (code2wav included) of the first n of the 64 streams, n chosen after the first
+    warm-up step so the whole arm ends in about ``budget`` seconds; frames/s = n * steps / time."""
     if rank != 0:
         return
-    # the arm's own --steps / --warmup; each step is a two-stream sample of the 64-stream step
-    # (0.1-0.2 s of CPU work on 16 threads, so the default 512 steps end within about two minutes)
-    base = cpu_oracle_rate(n_streams=2, steps=max(1, ARGS.steps), warmup=ARGS.warmup)
+    budget = 150.0
+    cs = CpuStep()
+    probe_n = 8
+    t_probe = cs.step(probe_n)  # counts as the first warm-up step
+    per_step = budget / max(1, ARGS.steps + ARGS.warmup)
+    n = max(1, min(STREAMS, int(per_step / (t_probe / probe_n))))
+    for _ in range(max(0, ARGS.warmup - 1)):
+        cs.step(n)
+    dt = sum(cs.step(n) for _ in range(ARGS.steps))
+    value = n * ARGS.steps / dt
+    base = {"value": round(value, 3), "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{ARGS.steps} decode steps of the benchmark's first {n} of {STREAMS} streams (cfg2 contexts), "
+                      f"full 28-layer talker + 15-stage code predictor (the reference's full recompute) + streaming "
+                      f"code2wav, fp32, {torch.get_num_threads()} threads",
+            "seconds": round(dt, 2)}
     line = {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": UNIT, "n_gpus": world,
-            "steps": ARGS.steps, "warmup": ARGS.warmup, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "cfg2 decode step (bounded CPU sample)", "streams": STREAMS},
-            "cpu_baseline": base,
+            "steps": ARGS.steps, "warmup": ARGS.warmup, "ms_per_step": round(dt / ARGS.steps * 1e3, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": workload_config(world), "cpu_baseline": base,
             "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -293,11 +392,25 @@ def run_b200(rank, world, local):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     if world > 1:
+        import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=600))
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=600))
     ex, slots, prompts, pad = build_workload(dev)
     n = len(slots)
     stream = ex._stream
+    peaks = load_peaks()
+
+    if ARGS.roofline_only:
+        torch.cuda.nvtx.range_push("roofline")  # for ncu --nvtx --nvtx-include roofline/
+        roof = {"gemm": gemm_roofline(ex, peaks), "attention": attention_roofline(ex, slots, peaks)}
+        torch.cuda.nvtx.range_pop()
+        if rank == 0:
+            print(json.dumps({"roofline_only": True, **roof}), flush=True)
+        ex._graphs.clear()
+        ex.shutdown()
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return
 
     # warm-up: eager step, capture, replays
     for _ in range(max(1, ARGS.warmup)):
@@ -351,6 +464,8 @@ def run_b200(rank, world, local):
                               "ms_per_step": round(total_ms / ARGS.steps, 4), "kernels_per_step": launches}))
         ex._graphs.clear()
         ex.shutdown()
+        if world > 1:
+            torch.distributed.destroy_process_group()
         return
 
     # ---- e2e through the executor call with host buffers
@@ -385,41 +500,38 @@ def run_b200(rank, world, local):
     h2d = t_host.numel() * 4 + n * 4
     d2h = n * (1 + ex._config.cp.num_stages) * 8 + 4 + n * ex._config.c2w.samples_per_frame * 4
 
-    peaks = load_peaks()
-    roof = attention_roofline(ex, slots, peaks)
+    roof_gemm = gemm_roofline(ex, peaks)
+    roof_attn = attention_roofline(ex, slots, peaks)
     ctx_now = [s.past_len for s in slots]
-    cpu = None
-    if rank == 0 and not ARGS.no_cpu_baseline:
-        cpu = cpu_oracle_rate()
-    if rank == 0:
-        line = {
-            "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": ARGS.steps,
-            "warmup": ARGS.warmup, "ms_per_step": round(total_ms / ARGS.steps, 4),
-            "p50_step_ms": round(statistics.median(per_step), 4), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "cfg2: 64 ragged streams/GPU, ctx U{16..512} + 96-token shared prefix, "
-                                   "8192 x 16-token KV blocks, top-k 50 / T 0.9 Philox sampling",
-                       "streams_per_gpu": n, "parallelism": f"replicas x{world} (request-sharded, no collective)",
-                       "l2": "inputs larger than L2 (KV ~4 GB + weights ~3 GB read per step)",
-                       "step": "talker 28 layers + sampling + 15-stage code predictor + codec sum + "
-                               "streaming code2wav (1920 samples/stream)",
-                       "pipeline": "two streams: step k's code2wav overlaps step k+1's talker + code predictor; "
-                                   "timed from step 0's start to the last step's code2wav end",
-                       "ctx_mean_end": round(sum(ctx_now) / len(ctx_now), 1)},
-            "gpu_launches": launches * ARGS.steps,
-            "roofline": roof,
-            "cpu_baseline": cpu,
-            "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "steps": ARGS.e2e_steps, "path": "B200Executor.launch_decode_step -> GPUFuture.wait",
-                    "lookahead": "step k+1 launched before step k's results are read"},
-            "clocks": clk,
-        }
-        print(json.dumps(line), flush=True)
     ex._graphs.clear()
     ex.shutdown()
     if world > 1:
+        # every rank is done with the GPU and with collectives before rank 0 spends host time
+        # on the CPU baseline: no rank waits in a collective meanwhile
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
+    if rank != 0:
+        return
+    cpu = None if ARGS.no_cpu_baseline else cpu_baseline_rate()
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": ARGS.steps,
+        "warmup": ARGS.warmup, "ms_per_step": round(total_ms / ARGS.steps, 4),
+        "p50_step_ms": round(statistics.median(per_step), 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": workload_config(world),
+        "ctx_mean_end": round(sum(ctx_now) / len(ctx_now), 1),
+        "pipeline": "two streams: step k's code2wav overlaps step k+1's talker + code predictor; "
+                    "timed from step 0's start to the last step's code2wav end",
+        "gpu_launches": launches * ARGS.steps,
+        "roofline": roof_gemm,
+        "roofline_attention": roof_attn,
+        "cpu_baseline": cpu,
+        "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "steps": ARGS.e2e_steps, "path": "B200Executor.launch_decode_step -> GPUFuture.wait",
+                "lookahead": "step k+1 launched before step k's results are read"},
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
 
 
 def main():
