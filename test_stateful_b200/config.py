@@ -149,6 +149,61 @@ class EngineConfig:
     def to_dict(self) -> dict:
         return asdict(self)
 
+    # -- the flat fields of the reference's ModelConfig (engine/backend/kv_cache_pool.py:36-60),
+    #    which the engine loop reads from ``executor._config`` (engine_loop.py:242-243, 2105)
+    @property
+    def num_layers(self) -> int:
+        return self.talker.num_layers
+
+    @property
+    def kv_heads(self) -> int:
+        return self.talker.kv_heads
+
+    @property
+    def head_dim(self) -> int:
+        return self.talker.head_dim
+
+    @property
+    def hidden_size(self) -> int:
+        return self.talker.hidden_size
+
+    @property
+    def max_seq_len(self) -> int:
+        return self.pool.max_seq_len
+
+    @property
+    def dtype(self):
+        import torch
+        return torch.bfloat16
+
+    @property
+    def codec_vocab_size(self) -> int:
+        return self.talker.codec_vocab_size
+
+    @property
+    def logits_topk(self) -> int:
+        return self.talker.logits_topk
+
+    @property
+    def cp_num_stages(self) -> int:
+        return self.cp.num_stages
+
+    @property
+    def n_c2w_layers(self) -> int:
+        return self.c2w.num_layers
+
+    @property
+    def c2w_kv_heads(self) -> int:
+        return self.c2w.kv_heads
+
+    @property
+    def c2w_head_dim(self) -> int:
+        return self.c2w.head_dim
+
+    @property
+    def c2w_sliding_window(self) -> int:
+        return self.c2w.window
+
 
 def tiny_engine_config(num_layers: int = 2) -> EngineConfig:
     """A small configuration with the talker's vocab and head layout intact.

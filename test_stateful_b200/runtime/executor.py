@@ -78,6 +78,40 @@ class StepOutput:
     step_input_embeds: Optional[torch.Tensor] = None
 
 
+class BatchRows:
+    """``StepOutput.codec_sum`` as the engine loop indexes it: row i of the step's batch,
+    ``codec_sum[i:i+1]`` -> ``[1, 1, H]`` (engine_loop.py:2170-2197), read from the
+    slot-indexed codec-sum buffer of the step's parity (valid until the step two launches
+    later reuses it, i.e. while the loop processes this step's output)."""
+
+    def __init__(self, buf: torch.Tensor, slot_ids: List[int]):
+        self._buf = buf
+        self._ids = slot_ids
+
+    @property
+    def dtype(self):
+        return self._buf.dtype
+
+    @property
+    def device(self):
+        return self._buf.device
+
+    @property
+    def shape(self):
+        return (len(self._ids), 1, self._buf.shape[-1])
+
+    def __len__(self):
+        return len(self._ids)
+
+    def __getitem__(self, key) -> torch.Tensor:
+        if isinstance(key, int):
+            return self._buf[self._ids[key]].view(1, -1)
+        return self._buf[self._ids[key]].unsqueeze(1)
+
+    def tensor(self) -> torch.Tensor:
+        return self[:]
+
+
 @dataclass
 class GPUFuture:
     """Handle to an in-flight decode step (executor.py:357-452)."""
@@ -88,7 +122,7 @@ class GPUFuture:
     _original_past_lens: List[int] = field(default_factory=list)
     _codes_host: Optional[torch.Tensor] = None
     _codes_dev: Optional[torch.Tensor] = None
-    _codec_sum: Optional[torch.Tensor] = None
+    _codec_sum: Optional[BatchRows] = None
     _status_host: Optional[torch.Tensor] = None
     _wav_host: Optional[torch.Tensor] = None
 
@@ -206,6 +240,8 @@ class B200Executor:
 
     def shutdown(self) -> None:
         self._graphs.clear()
+        if self._kv_pool is not None:
+            self._kv_pool.close()
         if self._c2w is not None:
             self._c2w.close()
         self._c2w = None
@@ -240,7 +276,9 @@ class B200Executor:
         self.counts = torch.zeros(S, t.codec_vocab_size, dtype=i64, device=dev)
         self.next_x = torch.zeros(S, t.hidden_size, dtype=f32, device=dev)
         self.text_add = torch.zeros(S, t.hidden_size, dtype=f32, device=dev)
-        self.codec_sum = torch.zeros(S, t.hidden_size, dtype=f32, device=dev)
+        # codec sums by parity like the codes: the engine loop reads step t's while t + 1 runs
+        self.codec_sum_buf = torch.zeros(3, S, t.hidden_size, dtype=f32, device=dev)
+        self.codec_sum = self.codec_sum_buf[2]
         self.temperature = torch.ones(S, dtype=f32, device=dev)
         self.penalty = torch.full((S,), self._repetition_penalty, dtype=f32, device=dev)
         self.noise_key = torch.zeros(S, dtype=i64, device=dev)
@@ -264,20 +302,27 @@ class B200Executor:
         self.wav = torch.zeros(B, spf, dtype=f32, device=dev) if self._enable_c2w else None
         self.wav_host_buf = torch.zeros(3, B, spf, dtype=f32).pin_memory() if self._enable_c2w else None
         self.wav_host = self.wav_host_buf[2] if self._enable_c2w else None
+        # each slot's own next-input row: a slot whose next_embed is this view feeds the step
+        # what the previous step computed on the device; any other tensor there (the engine
+        # loop's codec_sum + text, engine_loop.py:2170-2197) is copied in before the step
+        self._own_next = [self.next_x[i] for i in range(S)]
 
     def _reset_slot_state(self, slot_id: int) -> None:
-        self.counts[slot_id].zero_()
+        with torch.cuda.stream(self._stream):  # ordered before the steps that read it
+            self.counts[slot_id].zero_()
 
     def _configure_sampling(self, slot: SlotState) -> None:
-        """Per-slot sampling parameters (executor.py:1212-1227, 1335-1350)."""
+        """Per-slot sampling parameters (executor.py:1212-1227, 1335-1350), written on the
+        step stream so the next step sees them."""
         sid = slot.slot_id
         identity = slot.session_id if slot.session_id is not None else f"slot:{sid}"
         seed = stable_sampling_seed(self._random_seed, identity, slot.segment_idx)
         slot.sampling_seed = seed
-        self.noise_key[sid] = seed
-        self.noise_step[sid] = 0
-        self.temperature[sid] = self._temperature if self._do_sample else 1.0
-        self.penalty[sid] = self._repetition_penalty
+        with torch.cuda.stream(self._stream):
+            self.noise_key[sid] = seed
+            self.noise_step[sid] = 0
+            self.temperature[sid] = self._temperature if self._do_sample else 1.0
+            self.penalty[sid] = self._repetition_penalty
 
     def _io(self, n_rows: int, n_new: int, x_in: torch.Tensor, sample: int, parity: int = 2) -> _lib.StepIO:
         io = _lib.StepIO()
@@ -301,7 +346,7 @@ class B200Executor:
         io.hidden_out = self.hidden.data_ptr()
         io.logits_out = self.logits.data_ptr()
         io.full_codec_out = self.codes_buf[parity].data_ptr()
-        io.codec_sum_out = self.codec_sum.data_ptr()
+        io.codec_sum_out = self.codec_sum_buf[parity].data_ptr()
         io.next_x_out = self.next_x.data_ptr()
         io.status = self.status.data_ptr()
         return io
@@ -309,10 +354,12 @@ class B200Executor:
     def set_text_embedding(self, slot: SlotState, emb: Optional[torch.Tensor]) -> None:
         """Text embedding added to the codec sum to form the slot's next input
         (engine_loop.py:2170-2203: trailing[text_idx] or tts_pad)."""
-        if emb is None:
-            self.text_add[slot.slot_id].zero_()
-        else:
-            self.text_add[slot.slot_id].copy_(emb.reshape(-1).to(self._device, torch.float32), non_blocking=True)
+        self._stream.wait_stream(torch.cuda.current_stream(self._device))  # emb may come from that stream
+        with torch.cuda.stream(self._stream):
+            if emb is None:
+                self.text_add[slot.slot_id].zero_()
+            else:
+                self.text_add[slot.slot_id].copy_(emb.reshape(-1).to(self._device, torch.float32), non_blocking=True)
 
     # -- prefill ----------------------------------------------------------
     def _validate_prefill_len(self, seq: int, stage: str) -> None:
@@ -323,6 +370,7 @@ class B200Executor:
     def _prefill_call(self, slot: SlotState, embeds: torch.Tensor, sample: int) -> None:
         seq = int(embeds.shape[-2]) if embeds.dim() == 3 else int(embeds.shape[0])
         x = embeds.reshape(seq, -1).to(self._device, torch.float32).contiguous()
+        self._stream.wait_stream(torch.cuda.current_stream(self._device))  # x is made on that stream
         with torch.cuda.stream(self._stream):
             self.slots_dev[:1].fill_(slot.slot_id)
             self._model.step(self._io(1, seq, x, sample), self._stream)
@@ -354,7 +402,7 @@ class B200Executor:
         self._prefill_call(slot, prefill_embeds, sample=1)
         slot.position_offset = 0
         slot.frame_idx += 1
-        slot.next_embed = self.next_x[slot.slot_id]
+        slot.next_embed = self._own_next[slot.slot_id]
         audio = self._first_frame_audio()
         codes = self.codes[:1].cpu()
         return audio, bool(int(codes[0, 0]) == self._config.talker.codec_eos_id)
@@ -380,7 +428,7 @@ class B200Executor:
                 yield None
         slot.position_offset = 0
         slot.frame_idx += 1
-        slot.next_embed = self.next_x[slot.slot_id]
+        slot.next_embed = self._own_next[slot.slot_id]
         audio = self._first_frame_audio()
         codes = self.codes[:1].cpu()
         yield audio, bool(int(codes[0, 0]) == self._config.talker.codec_eos_id)
@@ -407,7 +455,7 @@ class B200Executor:
         self._configure_sampling(slot)
         self._prefill_call(slot, request_prefill_embeds, sample=1)
         slot.frame_idx += 1
-        slot.next_embed = self.next_x[slot.slot_id]
+        slot.next_embed = self._own_next[slot.slot_id]
         audio = self._first_frame_audio()
         codes = self.codes[:1].cpu()
         return audio, bool(int(codes[0, 0]) == self._config.talker.codec_eos_id)
@@ -507,6 +555,8 @@ class B200Executor:
             if s.past_len + 1 > cap:
                 raise ValueError(f"slot {s.slot_id} is at max_seq_len={cap}")
         original = [s.past_len for s in slots]
+        self._kv_pool.flush_drops()
+        self._stage_host_inputs(slots)
         par = self._parity
         if self._done_a[par] is not None:  # the staging copy of step t - 2 has been consumed
             self._done_a[par].synchronize()
@@ -521,14 +571,51 @@ class B200Executor:
             if self._graphs[n] is not None:
                 graphs = self._graphs[n][0]
         par, ev_a, ev_b = self._enqueue_step(n, upload=True, graphs=graphs)
+        own = self._own_next
         for s in slots:
             s.past_len += 1
             s.frame_idx += 1
+            s.next_embed = own[s.slot_id]
             s.touch()
         return GPUFuture(_executor=self, _event=ev_b, _slots=list(slots), _original_past_lens=original,
                          _codes_host=self.codes_host_buf[par], _codes_dev=self.codes_buf[par],
-                         _codec_sum=self.codec_sum, _status_host=self.status_host_buf[par],
+                         _codec_sum=BatchRows(self.codec_sum_buf[par], [s.slot_id for s in slots]),
+                         _status_host=self.status_host_buf[par],
                          _wav_host=self.wav_host_buf[par] if self._c2w is not None else None)
+
+    def _stage_host_inputs(self, slots: List[SlotState]) -> None:
+        """What the reference engine loop hands a decode step through its slots.
+
+        * A slot whose ``next_embed`` is not the device's own row (the loop sets
+          ``codec_sum + trailing text`` itself, engine_loop.py:2170-2197, or a primed prefix
+          suffix, 913-928) has that tensor copied into its input row before the step.
+        * A slot at ``frame_idx == 0`` starts a stream without a prefill of this executor (a
+          prefix-cache hit or a prefix-only prefill primed by the loop, engine_loop.py:801-835,
+          893-928): its sampling state is set and its code2wav state zeroed, as ``prefill``
+          does for the streams it starts.
+        """
+        own = self._own_next
+        moved = [s for s in slots if s.next_embed is not None and s.next_embed is not own[s.slot_id]]
+        fresh = [s for s in slots if s.frame_idx == 0]
+        if not moved and not fresh:
+            return
+        cur = torch.cuda.current_stream(self._device)
+        self._stream.wait_stream(cur)  # the loop made its tensors on that stream
+        for s in fresh:
+            self._configure_sampling(s)
+        with torch.cuda.stream(self._stream):
+            if moved:
+                for s in moved:
+                    s.next_embed.record_stream(self._stream)
+                rows = torch.cat([s.next_embed.reshape(1, -1).to(self._device, torch.float32) for s in moved])
+                idx = torch.tensor([s.slot_id for s in moved], dtype=torch.long, device=self._device)
+                self.next_x.index_copy_(0, idx, rows)
+        if fresh and self._c2w is not None:
+            b = self._c2w_stream
+            b.wait_stream(self._stream)
+            with torch.cuda.stream(b):
+                ids = torch.tensor([s.slot_id for s in fresh], dtype=torch.int32, device=self._device)
+                self._c2w.reset(ids, stream=b)
 
     def warmup(self, n_rounds: int = 3) -> None:
         """executor.py:1541-1605: a throw-away slot through prefill and decode."""

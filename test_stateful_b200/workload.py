@@ -60,7 +60,6 @@ def setup_shared_prefix_streams(ex, prompts: Sequence[torch.Tensor], table: torc
     Every stream's text embedding is ``pad``, its first frame included.  Returns
     ``(slots, first)``: ``first[i]`` is ``(codes [16], logits [V])`` of stream i's prefill
     (``None`` without a suffix) when ``record`` is set, else ``None``."""
-    from .runtime.pool import PagedPrefixEntry
     dev = ex._device
     pool = ex.kv_pool
     cache = ex.make_prefix_cache(max_entries=4, max_prefix_len=max(512, prefix_len))
@@ -75,12 +74,8 @@ def setup_shared_prefix_streams(ex, prompts: Sequence[torch.Tensor], table: torc
         s = pool.allocate(f"stream-{i}")
         s.segment_idx = 0
         n_shared = min(prefix_len, len(ids))
-        if n_shared == prefix_len:
-            cache.restore(s, entry)
-        else:
-            part = PagedPrefixEntry(key=entry.key, blocks=entry.blocks[: -(-n_shared // 16)], prefix_len=n_shared,
-                                    created_at=entry.created_at)
-            cache.restore(s, part)
+        # the whole cached prefix, or (prompt shorter than it) its first n_shared positions
+        cache.restore(s, entry if n_shared == prefix_len else entry.talker_kv[0, :, :, :n_shared, :])
         suffix = ids[n_shared:]
         # the text embedding added to the codec sum of each frame, the first one included
         ex.set_text_embedding(s, pad)

@@ -70,6 +70,11 @@ class _FakeSched:
 class _FakePool:
     def __init__(self):
         self._sched = _FakeSched()
+        self._pending_drops = []
+
+    def flush_drops(self):
+        while self._pending_drops:
+            self._sched.drop_blocks(self._pending_drops.pop())
 
 
 def _cache(**kw):
