@@ -415,6 +415,7 @@ def run_b200(rank, world, local):
     # warm-up: eager step, capture, replays
     for _ in range(max(1, ARGS.warmup)):
         ex.launch_decode_step(slots).wait()
+        ex.advance(slots)
     launches = ex.prepare_replay(slots)  # CUDA graphs of the step (stream A: talker + CP; B: code2wav)
     for _ in range(2):
         ex.replay_step(n)
@@ -484,6 +485,7 @@ def run_b200(rank, world, local):
             staged.copy_(t_host, non_blocking=True)
             ex.text_add.index_copy_(0, idx, staged)
         fut = ex.launch_decode_step(slots)
+        ex.advance(slots)  # the loop's per-slot counters, before the next launch
         if pending is not None:
             out = pending.wait()
             _ = out.full_codec, out.audio_chunks

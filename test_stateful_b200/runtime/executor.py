@@ -318,6 +318,9 @@ class B200Executor:
         identity = slot.session_id if slot.session_id is not None else f"slot:{sid}"
         seed = stable_sampling_seed(self._random_seed, identity, slot.segment_idx)
         slot.sampling_seed = seed
+        self._write_sampling_state(sid, seed)
+
+    def _write_sampling_state(self, sid: int, seed: int) -> None:
         with torch.cuda.stream(self._stream):
             self.noise_key[sid] = seed
             self.noise_step[sid] = 0
@@ -572,16 +575,23 @@ class B200Executor:
                 graphs = self._graphs[n][0]
         par, ev_a, ev_b = self._enqueue_step(n, upload=True, graphs=graphs)
         own = self._own_next
-        for s in slots:
-            s.past_len += 1
-            s.frame_idx += 1
+        for s in slots:  # the device formed each slot's next input; the loop may replace it
             s.next_embed = own[s.slot_id]
-            s.touch()
         return GPUFuture(_executor=self, _event=ev_b, _slots=list(slots), _original_past_lens=original,
                          _codes_host=self.codes_host_buf[par], _codes_dev=self.codes_buf[par],
                          _codec_sum=BatchRows(self.codec_sum_buf[par], [s.slot_id for s in slots]),
                          _status_host=self.status_host_buf[par],
                          _wav_host=self.wav_host_buf[par] if self._c2w is not None else None)
+
+    @staticmethod
+    def advance(slots: List[SlotState]) -> None:
+        """The per-slot counters the engine loop advances for each decode step it launched
+        (engine_loop.py:2163-2165): a caller that drives ``launch_decode_step`` without the
+        reference loop calls this once per launched step, before launching the next one."""
+        for s in slots:
+            s.past_len += 1
+            s.frame_idx += 1
+            s.touch()
 
     def _stage_host_inputs(self, slots: List[SlotState]) -> None:
         """What the reference engine loop hands a decode step through its slots.
@@ -599,14 +609,20 @@ class B200Executor:
         fresh = [s for s in slots if s.frame_idx == 0]
         if not moved and not fresh:
             return
-        cur = torch.cuda.current_stream(self._device)
-        self._stream.wait_stream(cur)  # the loop made its tensors on that stream
         for s in fresh:
             self._configure_sampling(s)
+        self._apply_host_inputs(moved, fresh)
+
+    def _apply_host_inputs(self, moved: List[SlotState], fresh: List[SlotState]) -> None:
+        """Device side of ``_stage_host_inputs``: copy the moved inputs in, zero the fresh
+        streams' code2wav state."""
+        cur = torch.cuda.current_stream(self._device)
+        self._stream.wait_stream(cur)  # the loop made its tensors on that stream
         with torch.cuda.stream(self._stream):
             if moved:
                 for s in moved:
-                    s.next_embed.record_stream(self._stream)
+                    if s.next_embed.is_cuda:
+                        s.next_embed.record_stream(self._stream)
                 rows = torch.cat([s.next_embed.reshape(1, -1).to(self._device, torch.float32) for s in moved])
                 idx = torch.tensor([s.slot_id for s in moved], dtype=torch.long, device=self._device)
                 self.next_x.index_copy_(0, idx, rows)
@@ -627,5 +643,6 @@ class B200Executor:
             self.prefill(slot, dummy)
             for _ in range(n_rounds):
                 self.launch_decode_step([slot]).wait()
+                self.advance([slot])
         finally:
             self._kv_pool.release(slot.slot_id)

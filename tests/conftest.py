@@ -14,3 +14,17 @@ def pytest_configure(config):
 
 
 GOLDEN = os.path.join(ROOT, "tests", "golden")
+
+
+def reference_root():
+    """The reference checkout, for the CPU tests that import its host code: QTTS_REFERENCE, or a
+    directory named ``reference`` beside this repository; None when neither exists (the GPU box
+    has no copy of it)."""
+    from pathlib import Path
+    cand = os.environ.get("QTTS_REFERENCE")
+    paths = [Path(cand)] if cand else []
+    paths.append(Path(ROOT).resolve().parent / "reference")
+    for p in paths:
+        if (p / "engine" / "backend" / "engine_loop.py").exists():
+            return p
+    return None

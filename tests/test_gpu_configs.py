@@ -162,6 +162,7 @@ def test_cfg2_benchmark_streams_against_oracle():
     for step in range(decode_steps):
         g, cg = _noise_rows(ex, sids, c.num_stages)
         out = ex.launch_decode_step(slots).wait()
+        ex.advance(slots)
         dev_logits = ex.logits[:n_streams].cpu()
         dev_codes = out.full_codec
         assert _lib.device_error() == 0

@@ -40,6 +40,7 @@ def test_executor_decode_steps_emit_audio_matching_oracle():
         audio.append([np.frombuffer(a, np.float32)])
     for _ in range(6):  # eager, capture, replays
         out = ex.launch_decode_step(slots).wait()
+        ex.advance(slots)
         for i in range(len(slots)):
             frames[i].append(out.full_codec[i].clone())
             audio[i].append(np.frombuffer(out.audio_chunks[i], np.float32))
@@ -79,6 +80,7 @@ def test_executor_lookahead_matches_sequential_steps():
         pending = None
         for _ in range(8):  # eager, capture, replays
             fut = ex.launch_decode_step(slots)
+            ex.advance(slots)
             if not lookahead:
                 out = fut.wait()
                 codes.append(out.full_codec.clone())
@@ -132,12 +134,14 @@ def test_chunked_prefill_interleaved_with_decode():
             first = None
             for _ in range(3):  # 21 tokens: chunks of 8, 8, 5 between decode steps of the others
                 out = ex.launch_decode_step(old).wait()
+                ex.advance(old)
                 outs.append((out.full_codec.clone(), list(out.audio_chunks)))
                 first = next(it)
             assert first is not None
         else:
             for _ in range(3):
                 out = ex.launch_decode_step(old).wait()
+                ex.advance(old)
                 outs.append((out.full_codec.clone(), list(out.audio_chunks)))
             first = ex.prefill(new, prompts[2].to(DEV))
         logits = ex.logits[0].float().cpu().clone()
