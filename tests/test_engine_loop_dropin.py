@@ -223,7 +223,9 @@ class _ImmediateLoop:
 
 
 def test_reference_engine_loop_drives_the_b200_host_layer(monkeypatch):
-    sys.path.insert(0, str(REF))
+    # after this repository's own packages (the reference has a ``tests`` package too), and only
+    # for the duration of this test
+    monkeypatch.setattr(sys, "path", sys.path + [str(REF)])
     from engine.backend.engine_loop import EngineLoop
     from engine.core.types import EngineRequest, RequestType, ResultType
 
