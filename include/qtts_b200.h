@@ -177,6 +177,18 @@ int qtts_paged_attention(const void* q, int R, int num_heads, int kv_heads, int 
                          const int32_t* row_slot, const int32_t* row_ctx, int max_ctx, int split_blocks,
                          float* ws_o, float* ws_ml, void* out, void* out_lo, qtts_stream_t stream);
 
+/* Chunked-prefill form of qtts_paged_attention (head_dim 128): the R rows are R / rows_per_stream
+ * streams of rows_per_stream consecutive query tokens (row_slot equal within a stream, row_ctx
+ * each token's visible keys: its stream's earlier KV plus the chunk up to itself — the causal
+ * mask of talker_unified_modules.py:282-294).  Tiles of 8 queries share every KV block they
+ * read, instead of each row reading its whole context.  Same output and scratch as
+ * qtts_paged_attention (executor.py:759-877 runs this attention inside its fused prefill). */
+int qtts_paged_attention_prefill(const void* q, int R, int rows_per_stream, int num_heads, int kv_heads,
+                                 int head_dim, const void* kv_pool, int layer, int num_layers, int block_size,
+                                 int num_blocks, const int32_t* block_table, int max_blocks_per_seq,
+                                 const int32_t* row_slot, const int32_t* row_ctx, int max_ctx, int split_blocks,
+                                 float* ws_o, float* ws_ml, void* out, void* out_lo, qtts_stream_t stream);
+
 /* Same computation as qtts_paged_attention, for callers that cannot allocate device memory
  * when they run attention (a plugin host that owns every allocation and passes only the
  * call's tensors, or a latency-bound thread that must not call cudaMalloc).  No counterpart

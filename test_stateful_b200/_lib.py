@@ -99,7 +99,8 @@ EXPORTS = [
     "qtts_version", "qtts_last_error", "qtts_device_error", "qtts_selftest_bounded_wait",
     "qtts_sched_init", "qtts_sched_append", "qtts_kv_copy_blocks", "qtts_sched_share_prefix",
     "qtts_sched_make_entry", "qtts_sched_drop_blocks", "qtts_sched_release", "qtts_kv_scatter", "qtts_kv_gather",
-    "qtts_gemm", "qtts_rmsnorm", "qtts_paged_attention", "qtts_paged_attention_noalloc", "qtts_sample",
+    "qtts_gemm", "qtts_rmsnorm", "qtts_paged_attention", "qtts_paged_attention_prefill",
+    "qtts_paged_attention_noalloc", "qtts_sample",
     "qtts_philox_gumbel", "qtts_codec_sum",
     "qtts_engine_create", "qtts_engine_destroy", "qtts_engine_step",
     "qtts_c2w_create", "qtts_c2w_destroy", "qtts_c2w_reset", "qtts_c2w_step", "qtts_c2w_launches",
@@ -138,6 +139,9 @@ def load() -> C.CDLL:
         "qtts_rmsnorm": ([P, C.c_int, C.c_int, C.c_int, P, C.c_float, P, P, P], C.c_int),
         "qtts_paged_attention": ([P, C.c_int, C.c_int, C.c_int, C.c_int, P, C.c_int, C.c_int, C.c_int, C.c_int,
                                   P, C.c_int, P, P, C.c_int, C.c_int, P, P, P, P, P], C.c_int),
+        "qtts_paged_attention_prefill": ([P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, P, C.c_int, C.c_int,
+                                          C.c_int, C.c_int, P, C.c_int, P, P, C.c_int, C.c_int, P, P, P, P, P],
+                                         C.c_int),
         "qtts_paged_attention_noalloc": ([P, C.c_int, C.c_int, C.c_int, C.c_int, P, C.c_int, C.c_int, C.c_int,
                                           C.c_int, P, C.c_int, P, P, C.c_int, P, P, P], C.c_int),
         "qtts_sample": ([P, C.c_int, C.c_int, C.c_int, C.c_int, P, C.c_int, C.c_uint64, P, C.c_int, P, P, P,

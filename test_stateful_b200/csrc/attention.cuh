@@ -44,6 +44,8 @@ struct AttnParams {
     int R;
     int static_meta;  // row_slot / row_ctx / block_table are not written by earlier kernels of the
                       // stream, so a kernel may read them before waiting on its predecessor
+    int rows_per_stream;  // chunked prefill: rows come as R / rows_per_stream streams of this many
+                          // consecutive query tokens (0 or 1: independent rows)
 };
 
 // Ring depth per warp (QTTS_ATTN_STAGES, default below): 3 stages x 8 KB x 4
@@ -793,6 +795,317 @@ inline int launch_attention_tc(const AttnParams& p, cudaStream_t st) {
     QTTS_CHECK_CUDA((func_attr_once<paged_attn_tc_kernel<S>>(L::SMEM)));
     const int items = p.R * p.kv_heads * p.max_splits;  // one (split, row, kv head) per warp
     QTTS_LAUNCH(kern, dim3(ceil_div(items, 4)), dim3(128), L::SMEM, st, map, p);
+    return QTTS_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Chunked prefill, head_dim 128: the rows of a prefill step are streams of
+// rows_per_stream consecutive query tokens, each row seeing its first row_ctx
+// keys (the causal mask of talker_unified_modules.py:282-288 over the chunk,
+// after the stream's earlier KV).  One warp per work item (8-token query tile of
+// one stream, kv head, split of split_blocks KV blocks): each KV block is staged
+// once (TMA, 128-B swizzle, the decode kernel's ring) and serves the tile's 8
+// queries x 2 heads, instead of being read again for every query row.
+//
+// Per 16-token block, on the tensor pipe (mma.sync m16n8k16, fp16 in, fp32 acc):
+//   S[16][16] = Q[16 rows][128] · K^T[128][16 keys]   rows = (query i, head h):
+//       row i for head 0, row 8 + i for head 1; Q carried as an fp16 hi/lo pair
+//   masked per (query, key), online softmax per row in the log2 domain
+//   O[16][128] += P[16][16] · V[16][128]               P as an fp16 hi/lo pair,
+//       taken straight from S's accumulator layout (no shuffles)
+// Output per row as the decode kernel: final when the row has one split of keys,
+// otherwise (o, max, sum) partials that attn_combine_kernel folds.
+// ---------------------------------------------------------------------------
+constexpr int kPrefillTile = 8;  // query tokens per warp work item
+
+template <int S>
+__global__ void __launch_bounds__(128) paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmKV,
+                                                               const AttnParams p) {
+    constexpr int D = 128;
+    using L = AttnTcLayout<S>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 4 * L::WARP_BYTES);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int gq = lane >> 2, qq = lane & 3;  // mma fragment coordinates
+    griddep_wait();
+    griddep_launch();
+    const int SPS = p.rows_per_stream;
+    const int n_streams = p.R / SPS;
+    const int n_tiles = (SPS + kPrefillTile - 1) / kPrefillTile;
+    const int item = blockIdx.x * 4 + warp;
+    if (item >= n_streams * n_tiles * p.kv_heads * p.max_splits) return;  // warp-uniform
+    int rest = item;
+    const int g = rest % p.kv_heads;
+    rest /= p.kv_heads;
+    const int tile = rest % n_tiles;
+    rest /= n_tiles;
+    const int b = rest % n_streams;
+    const int sp = rest / n_streams;
+    const int r0 = b * SPS + tile * kPrefillTile;
+    const int nq = min(kPrefillTile, SPS - tile * kPrefillTile);
+    // this lane's query (row gq of the tile) and its key count; the tile reads up to the largest
+    const bool q_ok = gq < nq;
+    const int ctx_q = q_ok ? p.row_ctx[r0 + gq] : 0;
+    int ctx_max = ctx_q;
+#pragma unroll
+    for (int off = 4; off <= 16; off <<= 1) ctx_max = max(ctx_max, __shfl_xor_sync(0xffffffffu, ctx_max, off));
+    const int nbt = (ctx_max + 15) >> 4;
+    const int b_start = sp * p.split_blocks;
+    const int b_end = min(nbt, b_start + p.split_blocks);
+    const int nbt_q = (ctx_q + 15) >> 4;
+    const int ns_q = min(p.max_splits, (nbt_q + p.split_blocks - 1) / p.split_blocks);  // splits of this query
+    const size_t hrow0 = (size_t)(r0 + gq) * p.num_heads + g * 2;  // head 0 of this lane's query
+    if (b_start >= b_end) {
+        if (sp == 0 && q_ok && ctx_q <= 0 && qq == 0) {  // no keys (only after a scheduler error): zeros
+            for (int i = 0; i < 2 * D; ++i) {
+                p.out[hrow0 * D + i] = __float2bfloat16(0.f);
+                if (p.out_lo) p.out_lo[hrow0 * D + i] = __float2bfloat16(0.f);
+            }
+        }
+        return;
+    }
+    const int slot = p.row_slot[r0];
+
+    // Q fragments (A operand): lane (gq, qq) holds rows gq (head 0) and gq + 8 (head 1) of
+    // query gq, dims 16 ks + 2 qq (+1) and + 8 (+9), scaled into the log2 domain
+    uint32_t qh[8][4], ql[8][4];
+    {
+        const float* q0p = p.q + hrow0 * D;
+        const float* q1p = q0p + D;
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+            const int d0 = 16 * ks + 2 * qq;
+            float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            if (q_ok) {
+                v[0] = q0p[d0] * p.scale_log2;
+                v[1] = q0p[d0 + 1] * p.scale_log2;
+                v[2] = q1p[d0] * p.scale_log2;
+                v[3] = q1p[d0 + 1] * p.scale_log2;
+                v[4] = q0p[d0 + 8] * p.scale_log2;
+                v[5] = q0p[d0 + 9] * p.scale_log2;
+                v[6] = q1p[d0 + 8] * p.scale_log2;
+                v[7] = q1p[d0 + 9] * p.scale_log2;
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) split_h2(v[2 * j], v[2 * j + 1], qh[ks][j], ql[ks][j]);
+        }
+    }
+
+    uint8_t* wbuf = smem + warp * L::WARP_BYTES;
+    uint64_t* wbar = bars + warp * S;
+    if (lane == 0) {
+        for (int s = 0; s < S; ++s) mbar_init(&wbar[s], 1);
+        tma_prefetch_desc(&tmKV);
+        fence_mbar_init();
+    }
+    __syncwarp();
+
+    const int n_mine = b_end - b_start;
+    auto issue = [&](int i) {
+        const int jb = b_start + i;
+        const int s = i % S;
+        int blk = jb < p.mbps ? p.block_table[(size_t)slot * p.mbps + jb] : -1;
+        if (blk < 0 || blk >= p.num_blocks) {
+            record_error(DEV_ERR_ATTN_WAIT);
+            blk = 0;  // stay in bounds; the error word reports the bad table entry
+        }
+        const int krow = (((blk * p.num_layers + p.layer) * 2 + 0) * p.kv_heads + g) * 16;
+        const int vrow = krow + p.kv_heads * 16;
+        uint8_t* dst = wbuf + s * kTcStage;
+        mbar_arrive_expect_tx(&wbar[s], kTcStage);
+        tma_load_2d(dst, &tmKV, &wbar[s], 0, krow);
+        tma_load_2d(dst + kTcBox, &tmKV, &wbar[s], 64, krow);
+        tma_load_2d(dst + 2 * kTcBox, &tmKV, &wbar[s], 0, vrow);
+        tma_load_2d(dst + 3 * kTcBox, &tmKV, &wbar[s], 64, vrow);
+    };
+
+    int issued = 0;
+    if (lane == 0) {
+        for (int i = 0; i < n_mine && i < S; ++i) issue(i);
+        issued = min(n_mine, S);
+    }
+    issued = __shfl_sync(0xffffffffu, issued, 0);
+
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;  // rows (query gq, head 0 / 1)
+    float o[16][4];
+#pragma unroll
+    for (int dt = 0; dt < 16; ++dt) o[dt][0] = o[dt][1] = o[dt][2] = o[dt][3] = 0.f;
+
+    // ldmatrix row addresses: lane supplies row (lane & 7) of matrix (lane >> 3)
+    const int mi = lane >> 3, rr = lane & 7;
+    const int kb_key = (mi >> 1) * 8 + rr, kb_dim = (mi & 1) * 8;  // K^T as the B operand (rows = keys)
+    const int vb_key = (mi & 1) * 8 + rr, vb_dim = (mi >> 1) * 8;  // V as the B operand (transposed load)
+
+    int done = 0;
+    bool failed = false;
+    for (int i = 0; i < n_mine; ++i) {
+        const int s = i % S;
+        if (!mbar_wait(&wbar[s], (uint32_t)(i / S) & 1u, DEV_ERR_ATTN_WAIT)) {
+            failed = true;
+            break;
+        }
+        const uint32_t kb = smem_u32(wbuf + s * kTcStage);
+        const uint32_t vb = kb + 2 * kTcBox;
+        const int jb = b_start + i;
+
+        // ---- S = Q K^T: two 8-key n-tiles
+        float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+            uint32_t kf[4];
+            ldsm_x4(tc_sw128(kb, kb_key, 16 * ks + kb_dim), kf);
+            mma_16816(sc[0], qh[ks], kf[0], kf[1]);
+            mma_16816(sc[0], ql[ks], kf[0], kf[1]);
+            mma_16816(sc[1], qh[ks], kf[2], kf[3]);
+            mma_16816(sc[1], ql[ks], kf[2], kf[3]);
+        }
+        // sc[nt][0,1] = (head 0, keys 16 jb + 8 nt + 2 qq, +1), sc[nt][2,3] = head 1, same keys
+        float bm0 = -INFINITY, bm1 = -INFINITY;
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int key = jb * 16 + nt * 8 + 2 * qq + (e & 1);
+                if (key >= ctx_q) sc[nt][e] = -INFINITY;
+            }
+            bm0 = fmaxf(bm0, fmaxf(sc[nt][0], sc[nt][1]));
+            bm1 = fmaxf(bm1, fmaxf(sc[nt][2], sc[nt][3]));
+        }
+#pragma unroll
+        for (int off = 1; off <= 2; off <<= 1) {
+            bm0 = fmaxf(bm0, __shfl_xor_sync(0xffffffffu, bm0, off));
+            bm1 = fmaxf(bm1, __shfl_xor_sync(0xffffffffu, bm1, off));
+        }
+        const float mn0 = fmaxf(m0, bm0), mn1 = fmaxf(m1, bm1);
+        const float a0 = m0 == -INFINITY ? 0.f : exp2f(m0 - mn0);
+        const float a1 = m1 == -INFINITY ? 0.f : exp2f(m1 - mn1);
+        float pr[2][4];
+        float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float mref = e < 2 ? mn0 : mn1;
+                pr[nt][e] = sc[nt][e] == -INFINITY ? 0.f : exp2f(sc[nt][e] - mref);
+            }
+            ps0 += pr[nt][0] + pr[nt][1];
+            ps1 += pr[nt][2] + pr[nt][3];
+        }
+#pragma unroll
+        for (int off = 1; off <= 2; off <<= 1) {
+            ps0 += __shfl_xor_sync(0xffffffffu, ps0, off);
+            ps1 += __shfl_xor_sync(0xffffffffu, ps1, off);
+        }
+        l0 = l0 * a0 + ps0;
+        l1 = l1 * a1 + ps1;
+        m0 = mn0;
+        m1 = mn1;
+#pragma unroll
+        for (int dt = 0; dt < 16; ++dt) {
+            o[dt][0] *= a0;
+            o[dt][1] *= a0;
+            o[dt][2] *= a1;
+            o[dt][3] *= a1;
+        }
+        // ---- P as the A operand, straight from the accumulator layout: rows gq / gq + 8,
+        // keys 2 qq (+1) in regs 0 / 1 and 8 + 2 qq (+1) in regs 2 / 3
+        uint32_t ph[4], pl[4];
+        split_h2(pr[0][0], pr[0][1], ph[0], pl[0]);
+        split_h2(pr[0][2], pr[0][3], ph[1], pl[1]);
+        split_h2(pr[1][0], pr[1][1], ph[2], pl[2]);
+        split_h2(pr[1][2], pr[1][3], ph[3], pl[3]);
+        // ---- O += P V: 16 dim tiles of 8, two per transposed ldmatrix
+#pragma unroll
+        for (int dp = 0; dp < 8; ++dp) {
+            uint32_t vf[4];
+            ldsm_x4_t(tc_sw128(vb, vb_key, 16 * dp + vb_dim), vf);
+            mma_16816(o[2 * dp], ph, vf[0], vf[1]);
+            mma_16816(o[2 * dp], pl, vf[0], vf[1]);
+            mma_16816(o[2 * dp + 1], ph, vf[2], vf[3]);
+            mma_16816(o[2 * dp + 1], pl, vf[2], vf[3]);
+        }
+        ++done;
+        __syncwarp();
+        if (lane == 0 && i + S < n_mine) {
+            fence_proxy_async_smem();
+            issue(i + S);
+            ++issued;
+        }
+        issued = __shfl_sync(0xffffffffu, issued, 0);
+    }
+    if (failed && lane == 0) {
+        for (int i = done; i < issued; ++i) mbar_wait(&wbar[i % S], (uint32_t)(i / S) & 1u, DEV_ERR_DRAIN);
+    }
+    if (!q_ok || sp >= ns_q) return;  // padding query, or a split without keys of this query
+
+    // ---- rows (query gq, heads 0 / 1): dims 8 dt + 2 qq (+1)
+    if (ns_q == 1) {  // all of this query's keys were in this split: final output
+        const float i0 = l0 > 0.f ? 1.f / l0 : 0.f, i1 = l1 > 0.f ? 1.f / l1 : 0.f;
+#pragma unroll
+        for (int dt = 0; dt < 16; ++dt) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int h = e >> 1, d = 8 * dt + 2 * qq + (e & 1);
+                const float ov = o[dt][e] * (h ? i1 : i0);
+                const __nv_bfloat16 hi = __float2bfloat16(ov);
+                p.out[(hrow0 + h) * D + d] = hi;
+                if (p.out_lo) p.out_lo[(hrow0 + h) * D + d] = __float2bfloat16(ov - __bfloat162float(hi));
+            }
+        }
+        return;
+    }
+#pragma unroll
+    for (int dt = 0; dt < 16; ++dt) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int h = e >> 1, d = 8 * dt + 2 * qq + (e & 1);
+            p.ws_o[((hrow0 + h) * p.max_splits + sp) * D + d] = o[dt][e];
+        }
+    }
+    if (qq == 0) {
+        p.ws_ml[((hrow0 + 0) * p.max_splits + sp) * 2 + 0] = m0;
+        p.ws_ml[((hrow0 + 0) * p.max_splits + sp) * 2 + 1] = l0;
+        p.ws_ml[((hrow0 + 1) * p.max_splits + sp) * 2 + 0] = m1;
+        p.ws_ml[((hrow0 + 1) * p.max_splits + sp) * 2 + 1] = l1;
+    }
+}
+
+template <int S>
+inline int launch_prefill_tc(const AttnParams& p, cudaStream_t st) {
+    using L = AttnTcLayout<S>;
+    CUtensorMap map;
+    const int rc = make_kv_map(&map, p);
+    if (rc) return rc;
+    auto kern = paged_prefill_tc_kernel<S>;
+    QTTS_CHECK_CUDA((func_attr_once<paged_prefill_tc_kernel<S>>(L::SMEM)));
+    const int n_tiles = (p.rows_per_stream + kPrefillTile - 1) / kPrefillTile;
+    const int items = (p.R / p.rows_per_stream) * n_tiles * p.kv_heads * p.max_splits;
+    QTTS_LAUNCH(kern, dim3(ceil_div(items, 4)), dim3(128), L::SMEM, st, map, p);
+    return QTTS_OK;
+}
+
+// The engine's prefill steps use the query-tile kernel unless QTTS_PREFILL_TILES=0 (one row per
+// query through the decode kernel).
+inline bool attn_prefill_tiles() {
+    static const bool on = [] {
+        const char* v = getenv("QTTS_PREFILL_TILES");
+        return !(v && *v == '0');
+    }();
+    return on;
+}
+
+// Prefill rows (head_dim 128): query tiles share each KV block; the split partials fold as in decode.
+inline int launch_prefill_attention(const AttnParams& p, cudaStream_t st) {
+    if (p.R <= 0) return QTTS_OK;
+    if (p.rows_per_stream < 1 || p.R % p.rows_per_stream != 0) {
+        set_error("prefill attention: %d rows are not streams of %d tokens", p.R, p.rows_per_stream);
+        return QTTS_ERR_INVALID;
+    }
+    const int rc = launch_prefill_tc<2>(p, st);
+    if (rc) return rc;
+    if (p.max_splits > 1) QTTS_LAUNCH(attn_combine_kernel<128>, dim3(p.R, p.num_heads), dim3(128), 0, st, p);
     return QTTS_OK;
 }
 

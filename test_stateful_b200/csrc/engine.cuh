@@ -388,6 +388,7 @@ inline int engine_step_impl(qtts_engine* e, const qtts_step_io& io, cudaStream_t
     ap.out = e->attn;
     ap.out_lo = e->attn_lo;
     ap.R = R;
+    ap.rows_per_stream = nn;
 
     // ---- talker layers
     for (int l = 0; l < d.layers; ++l) {
@@ -396,7 +397,10 @@ inline int engine_step_impl(qtts_engine* e, const qtts_step_io& io, cudaStream_t
             QTTS_TRY(launch_rmsnorm(e->x, R, H, H, bf(d.w_in_norm, 0), d.rms_eps, e->xn, st, e->xn_lo));
         QTTS_TRY(run_plan(g.qkv, R, st));
         ap.layer = l;
-        QTTS_TRY(launch_attention(ap, D, st));
+        if (nn > 1 && D == 128 && attn_use_tc() && attn_prefill_tiles())
+            QTTS_TRY(launch_prefill_attention(ap, st));  // query tiles of the chunk share each KV block
+        else
+            QTTS_TRY(launch_attention(ap, D, st));
         QTTS_TRY(run_plan(g.o, R, st));  // + post-attention norm (folded)
         QTTS_TRY(run_plan(g.gu, R, st));
         QTTS_TRY(run_plan(g.down, R, st));

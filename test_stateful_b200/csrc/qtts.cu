@@ -197,6 +197,47 @@ int qtts_paged_attention(const void* q, int R, int num_heads, int kv_heads, int 
     return launch_attention(p, head_dim, (cudaStream_t)stream);
 }
 
+int qtts_paged_attention_prefill(const void* q, int R, int rows_per_stream, int num_heads, int kv_heads,
+                                 int head_dim, const void* kv_pool, int layer, int num_layers, int block_size,
+                                 int num_blocks, const int32_t* block_table, int max_blocks_per_seq,
+                                 const int32_t* row_slot, const int32_t* row_ctx, int max_ctx, int split_blocks,
+                                 float* ws_o, float* ws_ml, void* out, void* out_lo, qtts_stream_t stream) {
+    QTTS_REQUIRE(q && kv_pool && block_table && row_slot && row_ctx && ws_o && ws_ml && out && R >= 0,
+                 "paged_attention_prefill: null pointer");
+    QTTS_REQUIRE(head_dim == 128, "paged_attention_prefill: head_dim %d (the tile kernel takes 128)", head_dim);
+    QTTS_REQUIRE(rows_per_stream >= 1 && R % rows_per_stream == 0,
+                 "paged_attention_prefill: %d rows are not streams of %d tokens", R, rows_per_stream);
+    QTTS_REQUIRE(block_size == 16, "paged_attention_prefill: block_size must be 16");
+    QTTS_REQUIRE(kv_heads > 0 && num_heads == 2 * kv_heads,
+                 "paged_attention_prefill: needs 2 query heads per kv head");
+    QTTS_REQUIRE(layer >= 0 && layer < num_layers && max_ctx > 0 && max_ctx <= max_blocks_per_seq * block_size,
+                 "paged_attention_prefill: layer / max_ctx out of range");
+    QTTS_REQUIRE(split_blocks >= 0 && split_blocks <= 1024, "paged_attention_prefill: split_blocks out of range");
+    AttnParams p = {};
+    p.q = reinterpret_cast<const float*>(q);
+    p.kv = reinterpret_cast<const kv_t*>(kv_pool);
+    p.num_heads = num_heads;
+    p.kv_heads = kv_heads;
+    p.layer = layer;
+    p.num_layers = num_layers;
+    p.block_size = block_size;
+    p.num_blocks = num_blocks;
+    p.block_table = block_table;
+    p.mbps = max_blocks_per_seq;
+    p.row_slot = row_slot;
+    p.row_ctx = row_ctx;
+    p.split_blocks = split_blocks > 0 ? split_blocks : QTTS_ATTN_SPLIT_BLOCKS;
+    p.max_splits = attn_max_splits(max_ctx, p.split_blocks);
+    p.scale_log2 = 1.4426950408889634f / sqrtf((float)head_dim);
+    p.ws_o = ws_o;
+    p.ws_ml = ws_ml;
+    p.out = reinterpret_cast<__nv_bfloat16*>(out);
+    p.out_lo = reinterpret_cast<__nv_bfloat16*>(out_lo);
+    p.R = R;
+    p.rows_per_stream = rows_per_stream;
+    return launch_prefill_attention(p, (cudaStream_t)stream);
+}
+
 int qtts_sample(const float* logits, int R, int V, int ld, int topk, const float* gumbel, int gumbel_ld, uint64_t seed,
                 const int64_t* noise_key, int step, const float* temperature, const float* penalty, int64_t* counts,
                 int eos_id, int64_t* tok_out, int tok_ld, qtts_stream_t stream) {

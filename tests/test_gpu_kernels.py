@@ -173,6 +173,60 @@ def test_paged_attention_ragged(D):
         torch.testing.assert_close(out[r].cpu(), ref, rtol=1e-3, atol=1e-4)  # fp32 softmax/PV, hi+lo output
 
 
+@pytest.mark.parametrize("split", [0, 2])
+def test_paged_prefill_attention_query_tiles(split):
+    """Chunked prefill (qtts_paged_attention_prefill): streams of S query rows with causal key
+    counts past + t + 1 (talker_unified_modules.py:282-294), S not a multiple of the 8-token
+    tile, pasts that start mid-block, several splits per row (split = 2 blocks) or one
+    (default 16), against an fp32 torch statement of the same attention and against the
+    one-row-per-query decode kernel."""
+    D, Hkv, Hq, L, layer, nb, mbps = 128, 8, 16, 2, 1, 400, 40
+    S = 21
+    pasts = [0, 37, 300, 5]
+    n = len(pasts)
+    g = _gen(33)
+    kv = (torch.randn(nb, L, 2, Hkv, 16, D, generator=g)).to(torch.float16).to(DEV)
+    table = torch.full((n, mbps), -1, dtype=torch.int32)
+    perm = torch.randperm(nb, generator=g)
+    for b, pl in enumerate(pasts):
+        k = -(-(pl + S) // 16)
+        table[b, :k] = perm[b * mbps: b * mbps + k]
+    R = n * S
+    q = torch.randn(R, Hq, D, generator=g).to(DEV)
+    row_slot = torch.tensor([b for b in range(n) for _ in range(S)], dtype=torch.int32, device=DEV)
+    ctxs = [pl + t + 1 for pl in pasts for t in range(S)]
+    row_ctx = torch.tensor(ctxs, dtype=torch.int32, device=DEV)
+    max_ctx = mbps * 16
+    sb = split or _lib.ATTN_SPLIT_BLOCKS
+    splits = max(1, -(-(-(-max_ctx // 16)) // sb))
+    ws_o = torch.empty(R * Hq * splits * D, device=DEV)
+    ws_ml = torch.empty(R * Hq * splits * 2, device=DEV)
+    out = torch.empty(R, Hq * D, device=DEV, dtype=torch.bfloat16)
+    out_lo = torch.empty_like(out)
+    tdev = table.to(DEV)
+    rc = _lib.load().qtts_paged_attention_prefill(q.data_ptr(), R, S, Hq, Hkv, D, kv.data_ptr(), layer, L, 16, nb,
+                                                  tdev.data_ptr(), mbps, row_slot.data_ptr(), row_ctx.data_ptr(),
+                                                  max_ctx, split, ws_o.data_ptr(), ws_ml.data_ptr(), out.data_ptr(),
+                                                  out_lo.data_ptr(), _lib.stream_ptr())
+    _lib.check(rc, "paged_attention_prefill")
+    got = (out.float() + out_lo.float()).cpu()
+    dec_lo = torch.empty_like(out)
+    dec = ops.paged_attention(q, kv, layer, tdev, row_slot, row_ctx, max_ctx, out_lo=dec_lo, split_blocks=split)
+    dec = (dec.float() + dec_lo.float()).cpu()
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    kvc, qc = kv.float().cpu(), q.float().cpu()
+    for r, c in enumerate(ctxs):
+        b = r // S
+        blocks = table[b, : -(-c // 16)].long()
+        K = kvc[blocks, layer, 0].permute(1, 0, 2, 3).reshape(Hkv, -1, D)[:, :c].repeat_interleave(2, 0)
+        V = kvc[blocks, layer, 1].permute(1, 0, 2, 3).reshape(Hkv, -1, D)[:, :c].repeat_interleave(2, 0)
+        p = torch.softmax((qc[r].unsqueeze(1) @ K.transpose(1, 2)).squeeze(1) / D ** 0.5, dim=-1)
+        ref = (p.unsqueeze(1) @ V).squeeze(1).reshape(-1)
+        torch.testing.assert_close(got[r], ref, rtol=1e-3, atol=1e-4)
+        torch.testing.assert_close(got[r], dec[r], rtol=1e-3, atol=1e-4)
+
+
 # --------------------------------------------------------------------- scheduler
 def _pool(num_blocks=16, max_slots=6, mbps=8):
     cfg = EngineConfig(talker=TalkerConfig(num_layers=1, kv_heads=1, head_dim=8),
