@@ -1,8 +1,8 @@
 """Single-kernel timing on small cases that still exceed L2 (126 MB).
 
-    python -m test_stateful_b200.microbench attention [--rows 64] [--ctx-mean 520] [--launches 50]
-    python -m test_stateful_b200.microbench gemm [--n 12288] [--k 2048] [--m 64] [--launches 50]
-    python -m test_stateful_b200.microbench code2wav [--rows 64] [--launches 50] [--chunk 25]
+    python microbench.py attention [--rows 64] [--ctx-mean 520] [--launches 50]
+    python microbench.py gemm [--n 12288] [--k 2048] [--m 64] [--launches 50]
+    python microbench.py code2wav [--rows 64] [--launches 50] [--chunk 25]
 
 Prints one JSON line with the mean launch time (CUDA events) and the
 achieved bandwidth over the kernel's algorithmic bytes:
@@ -16,10 +16,14 @@ from __future__ import annotations
 
 import argparse
 import json
+import os
+import sys
 
-import torch
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
 
-from . import _lib, ops
+import torch  # noqa: E402
+
+from test_stateful_b200 import _lib, ops  # noqa: E402
 
 
 def bench_attention(rows: int, ctx_mean: int, launches: int, layers: int = 4, seed: int = 0, split: int = 0):
@@ -107,9 +111,9 @@ def bench_gemm(n: int, k: int, m: int, launches: int, seed: int = 0, plain: bool
 def bench_code2wav(rows: int, launches: int, seed: int = 0, chunk: int = 1):
     """One code2wav call (full decoder widths) for `rows` streams x `chunk` frames,
     captured in a CUDA graph and replayed; frames/s = rows * chunk / call time."""
-    from . import weights as wmod
-    from .config import Code2WavConfig
-    from .runtime.code2wav import DeviceCode2Wav
+    from test_stateful_b200 import weights as wmod
+    from test_stateful_b200.config import Code2WavConfig
+    from test_stateful_b200.runtime.code2wav import DeviceCode2Wav
     dev = "cuda"
     cfg = Code2WavConfig()
     dec = DeviceCode2Wav(cfg, wmod.make_code2wav_weights(cfg, seed), dev, max_slots=rows, max_frames=4096,

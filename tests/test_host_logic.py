@@ -1,5 +1,4 @@
-"""Host-side logic of the B200 backend on the CPU: MLFQ ordering (same contract
-as engine/core/mlfq.py), the paged prefix cache's LRU bookkeeping (same
+"""Host-side logic of the B200 backend on the CPU: the paged prefix cache's LRU bookkeeping (same
 contract as engine/backend/prefix_cache.py, with block references instead of
 clones), per-slot seeds (engine/backend/executor.py:45-52) and the replica
 router, including a world-size-2 gloo run."""
@@ -13,39 +12,9 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from test_stateful_b200.runtime.mlfq import MLFQConfig, MLFQMeta, MLFQScheduler
 from test_stateful_b200.runtime.replicas import ReplicaRouter, assign_sessions, max_over_ranks, share_routing
 
 from .conftest import GOLDEN
-
-
-# ----------------------------------------------------------------------------- MLFQ
-def test_mlfq_demotion_and_boundary_reset():
-    s = MLFQScheduler(MLFQConfig(q1_threshold=3, q2_threshold=5))
-    m = MLFQMeta()
-    for _ in range(3):
-        s.on_step_done(m)
-    assert m.level == 1
-    for _ in range(2):
-        s.on_step_done(m)
-    assert m.level == 2
-    s.on_segment_boundary(m)
-    assert (m.level, m.decode_steps) == (0, 0)
-
-
-def test_mlfq_select_batch_orders_levels_and_truncates():
-    s = MLFQScheduler()
-    metas = {n: MLFQMeta(level=l) for n, l in [("a", 2), ("b", 0), ("c", 1), ("d", 0), ("e", 2)]}
-    out = s.select_batch(list(metas), 10, get_meta=metas.get)
-    assert out == ["b", "d", "c", "a", "e"]
-    assert s.select_batch(list(metas), 3, get_meta=metas.get) == ["b", "d", "c"]
-
-
-def test_mlfq_aging_boosts_starved():
-    s = MLFQScheduler(MLFQConfig(aging_interval=2, starvation_limit=1))
-    m = MLFQMeta(level=2, steps_since_schedule=5)
-    assert s.tick([m]) == 0
-    assert s.tick([m]) == 1 and m.level == 0
 
 
 # ----------------------------------------------------------------------------- prefix cache
