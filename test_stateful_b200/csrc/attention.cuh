@@ -867,6 +867,13 @@ __global__ void __launch_bounds__(128) paged_prefill_tc_kernel(const __grid_cons
         return;
     }
     const int slot = p.row_slot[r0];
+    // self-check: the rows' buffers hold R rows; a slot outside the table is skipped
+    const size_t qo_limit = (size_t)p.R * p.num_heads * D;
+    const size_t ws_limit = (size_t)p.R * p.num_heads * p.max_splits;
+    if (slot < 0 || r0 + nq > p.R) {
+        if (lane == 0) record_error(DEV_ERR_ATTN_BOUNDS);
+        return;
+    }
 
     // Q fragments (A operand): lane (gq, qq) holds rows gq (head 0) and gq + 8 (head 1) of
     // query gq, dims 16 ks + 2 qq (+1) and + 8 (+9), scaled into the log2 domain
@@ -1039,6 +1046,10 @@ __global__ void __launch_bounds__(128) paged_prefill_tc_kernel(const __grid_cons
         for (int i = done; i < issued; ++i) mbar_wait(&wbar[i % S], (uint32_t)(i / S) & 1u, DEV_ERR_DRAIN);
     }
     if (!q_ok || sp >= ns_q) return;  // padding query, or a split without keys of this query
+    if ((hrow0 + 2) * D > qo_limit || (hrow0 + 2) * p.max_splits > ws_limit) {
+        record_error(DEV_ERR_ATTN_BOUNDS);
+        return;
+    }
 
     // ---- rows (query gq, heads 0 / 1): dims 8 dt + 2 qq (+1)
     if (ns_q == 1) {  // all of this query's keys were in this split: final output
