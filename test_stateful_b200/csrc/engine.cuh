@@ -20,6 +20,7 @@
 
 #include "attention.cuh"
 #include "common.cuh"
+#include "cp_cluster.cuh"
 #include "gemm_tc.cuh"
 #include "sampling.cuh"
 #include "sched.cuh"
@@ -84,6 +85,10 @@ struct qtts_engine {
     float* cp_tab = nullptr;  // [cp_stages - 1][cp_vocab][cH]: stage embeddings through the projection
     __nv_bfloat16* cp_qkv_pair = nullptr;  // code-predictor QKV rows in paired-tile order (PairAttn)
     bool cp_pair = false;
+    // code-predictor stages >= 1 as one cluster kernel each (cp_cluster.cuh): weights packed
+    // in mma.sync fragment order
+    bool cp_cluster = false;
+    uint4 *cpc_qkv = nullptr, *cpc_o = nullptr, *cpc_gu = nullptr, *cpc_down = nullptr, *cpc_head = nullptr;
     std::vector<qtts::GemmPlan> cp_heads;
 };
 
@@ -322,6 +327,37 @@ inline int engine_build(qtts_engine* e) {
     }
     // the first layer's input norm folded into the projection
     fold_norm_out(e->cp_proj_pair, bf(d.cp_w_in_norm, 0), e->cxn, e->cxn_lo, e->css);
+    // Stages >= 1 as one cluster kernel per stage (QTTS_CP_CLUSTER=0: the per-GEMM path), for
+    // the code predictor's shape (hidden 1024, 16 x 64 heads, 8 kv heads, SwiGLU 3072, 5
+    // layers, 2048-entry heads)
+    {
+        const char* v = getenv("QTTS_CP_CLUSTER");
+        e->cp_cluster = !(v && *v == '0') && cH == kCpcH && cI == kCpcI && cHq == kCpcHq && cHkv == kCpcHkv &&
+                        cD == kCpcD && d.cp_layers == kCpcL && d.cp_vocab == kCpcV && d.cp_rope_cos != nullptr;
+        if (e->cp_cluster) {
+            const size_t nq = (size_t)kCpcQkv * cH / 8, no = (size_t)cH * cH / 8, ngu = (size_t)2 * cI * cH / 8,
+                         nd = (size_t)cH * cI / 8, nh = (size_t)d.cp_vocab * cH / 8;  // uint4 per matrix
+            QTTS_TRY(dev_alloc(e, &e->cpc_qkv, nq * kCpcL));
+            QTTS_TRY(dev_alloc(e, &e->cpc_o, no * kCpcL));
+            QTTS_TRY(dev_alloc(e, &e->cpc_gu, ngu * kCpcL));
+            QTTS_TRY(dev_alloc(e, &e->cpc_down, nd * kCpcL));
+            QTTS_TRY(dev_alloc(e, &e->cpc_head, nh * S));
+            for (int l = 0; l < kCpcL; ++l) {
+                QTTS_TRY(pack_a_frag(bf(d.cp_w_qkv, (size_t)l * kCpcQkv * cH), cH, 0, kCpcQkv, cH, e->cpc_qkv + l * nq, 0));
+                QTTS_TRY(pack_a_frag(bf(d.cp_w_o, (size_t)l * cH * cH), cH, 0, cH, cH, e->cpc_o + l * no, 0));
+                QTTS_TRY(pack_a_frag(bf(d.cp_w_gate_up, (size_t)l * 2 * cI * cH), cH, 0, 2 * cI, cH,
+                                     e->cpc_gu + l * ngu, 0));
+                // down: per CTA r the columns (SwiGLU features) [192 r, +192) it computes
+                for (int r = 0; r < kCpcCtas; ++r)
+                    QTTS_TRY(pack_a_frag(bf(d.cp_w_down, (size_t)l * cH * cI), cI, kCpcFeat * r, cH, kCpcFeat,
+                                         e->cpc_down + l * nd + (size_t)r * cH * kCpcFeat / 8, 0));
+            }
+            for (int st = 0; st < S; ++st)
+                QTTS_TRY(pack_a_frag(bf(d.cp_w_lm_head, (size_t)st * d.cp_vocab * cH), cH, 0, d.cp_vocab, cH,
+                                     e->cpc_head + st * nh, 0));
+            QTTS_CHECK_CUDA(cudaStreamSynchronize(0));
+        }
+    }
     e->cp_heads.resize(S);
     for (int s = 0; s < S; ++s) {
         // stage 0 reads the final norm of rows 2b+1 (a norm kernel); later stages the folded one
@@ -460,9 +496,39 @@ inline int engine_step_impl(qtts_engine* e, const qtts_step_io& io, cudaStream_t
 
     // the tokens the next stage consumes: sampled, or forced by a parity test
     const int64_t* codes_in = io.force_codes ? io.force_codes : io.full_codec_out;
+    CpClusterParams cpc = {};
+    if (e->cp_cluster) {
+        cpc.nr = nr;
+        cpc.bmax = e->bmax;
+        cpc.x_in = e->cx;
+        cpc.logits = e->clogits;
+        cpc.kv = e->cp_kv;
+        const size_t nq = (size_t)kCpcQkv * cH / 8, no = (size_t)cH * cH / 8, ngu = (size_t)2 * d.cp_inter * cH / 8,
+                     nd = (size_t)cH * d.cp_inter / 8;
+        for (int l = 0; l < kCpcL; ++l) {
+            cpc.w_qkv[l] = e->cpc_qkv + l * nq;
+            cpc.w_o[l] = e->cpc_o + l * no;
+            cpc.w_gu[l] = e->cpc_gu + l * ngu;
+            cpc.w_down[l] = e->cpc_down + l * nd;
+        }
+        cpc.in_norm = bf(d.cp_w_in_norm, 0);
+        cpc.post_norm = bf(d.cp_w_post_norm, 0);
+        cpc.q_norm = bf(d.cp_w_q_norm, 0);
+        cpc.k_norm = bf(d.cp_w_k_norm, 0);
+        cpc.final_norm = bf(d.cp_w_final_norm, 0);
+        cpc.rope_cos = d.cp_rope_cos;
+        cpc.rope_sin = d.cp_rope_sin;
+        cpc.eps = d.cp_rms_eps;
+    }
     for (int s = 0; s < d.cp_stages; ++s) {
         const int rows = s == 0 ? 2 * nr : nr;
         const int32_t* m = e->cp_meta + (size_t)s * 4 * crows;
+        if (s > 0 && e->cp_cluster) {
+            // the stage's 5 layers and lm_head in one cluster launch: logits -> e->clogits
+            cpc.stage = s;
+            cpc.w_head = e->cpc_head + (size_t)s * d.cp_vocab * cH / 8;
+            QTTS_TRY(launch_cp_cluster_stage(cpc, st));
+        } else {
         if (s == 0) {
             QTTS_LAUNCH(cp_stage0_rows_kernel, dim3(nr), dim3(128), 0, st, (const __nv_bfloat16*)e->hid,
                         (const __nv_bfloat16*)e->hid_lo, bf(d.w_codec_emb, 0), d.vocab, H, codes_in, G, e->cp_in,
@@ -490,6 +556,7 @@ inline int engine_step_impl(qtts_engine* e, const qtts_step_io& io, cudaStream_t
             QTTS_TRY(launch_rmsnorm(e->cx + cH, nr, cH, 2 * cH, d.cp_w_final_norm, d.cp_rms_eps, e->chid, st,
                                     e->chid_lo));
         QTTS_TRY(run_plan(e->cp_heads[s], nr, st));
+        }  // per-GEMM stage
         SampleParams cs = {};
         cs.logits = e->clogits;
         cs.R = nr;
