@@ -327,12 +327,12 @@ inline int engine_build(qtts_engine* e) {
     }
     // the first layer's input norm folded into the projection
     fold_norm_out(e->cp_proj_pair, bf(d.cp_w_in_norm, 0), e->cxn, e->cxn_lo, e->css);
-    // Stages >= 1 as one cluster kernel per stage (QTTS_CP_CLUSTER=0: the per-GEMM path), for
-    // the code predictor's shape (hidden 1024, 16 x 64 heads, 8 kv heads, SwiGLU 3072, 5
-    // layers, 2048-entry heads)
+    // Stages >= 1 as one cluster kernel per stage (opt-in: QTTS_CP_CLUSTER=1; the default is the
+    // per-GEMM path), for the code predictor's shape (hidden 1024, 16 x 64 heads, 8 kv heads,
+    // SwiGLU 3072, 5 layers, 2048-entry heads)
     {
         const char* v = getenv("QTTS_CP_CLUSTER");
-        e->cp_cluster = !(v && *v == '0') && cH == kCpcH && cI == kCpcI && cHq == kCpcHq && cHkv == kCpcHkv &&
+        e->cp_cluster = (v && *v == '1') && cH == kCpcH && cI == kCpcI && cHq == kCpcHq && cHkv == kCpcHkv &&
                         cD == kCpcD && d.cp_layers == kCpcL && d.cp_vocab == kCpcV && d.cp_rope_cos != nullptr;
         if (e->cp_cluster) {
             const size_t nq = (size_t)kCpcQkv * cH / 8, no = (size_t)cH * cH / 8, ngu = (size_t)2 * cI * cH / 8,
