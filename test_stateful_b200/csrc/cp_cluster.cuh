@@ -44,7 +44,17 @@ constexpr int kCpcQkv = (kCpcHq + 2 * kCpcHkv) * kCpcD;  // 2048 rows
 constexpr int kCpcActLd = kCpcH + 8;                    // bf16 per operand row (16-B pad: conflict-free B loads)
 constexpr int kCpcFeat = kCpcI / kCpcCtas;              // 192 SwiGLU features per CTA
 constexpr int kCpcFeatLd = kCpcFeat + 8;
-constexpr int kCpcPf = 4;                               // weight tiles in flight per warp
+#ifndef CPC_PF
+#define CPC_PF 4
+#endif
+constexpr int kCpcPf = CPC_PF;                          // weight tiles in flight per warp
+
+// optional per-phase timestamps (a profiling build defines CPC_STAMP(i))
+#ifndef CPC_STAMP
+#define CPC_STAMP(i) \
+    do {             \
+    } while (0)
+#endif
 
 struct CpClusterParams {
     int nr;       // streams (rows of x_in / logits)
@@ -238,11 +248,13 @@ __global__ void __launch_bounds__(kCpcThreads, 1) cp_cluster_stage_kernel(const 
         xs[e] = b0 + t < p.nr ? p.x_in[(size_t)(b0 + t) * kCpcH + c] : 0.f;
     }
     __syncthreads();
+    CPC_STAMP(0);
 
     for (int l = 0; l < kCpcL; ++l) {
         // ---- input norm, QKV rows [128 rank, +128)
         cpc_norm(xs, p.in_norm + (size_t)l * kCpcH, p.eps, inv, act_hi, act_lo);
         cpc_gemm_rows(p.w_qkv[l], 8 * rank, 8, kCpcH / 16, 2, act_hi, act_lo, kCpcActLd, part, outb, 128);
+        CPC_STAMP(1 + 7 * l);
         // ---- epilogue per (token, head of this CTA): q/k RMSNorm + RoPE; q kept, k/v to the cache
         {
             const int t = warp >> 1, hh = warp & 1;  // 16 warps = 8 tokens x 2 heads
@@ -277,6 +289,7 @@ __global__ void __launch_bounds__(kCpcThreads, 1) cp_cluster_stage_kernel(const 
             }
         }
         cluster_sync();  // A: the new K/V rows are in the cache; every CTA is done reading act
+        CPC_STAMP(2 + 7 * l);
         // ---- attention: CTA r < 8 owns q heads 2r, 2r+1 (kv head r); one warp per (token, head)
         if (rank < 8) {
             const int t = warp >> 1, hh = warp & 1, head = 2 * rank + hh;
@@ -325,6 +338,7 @@ __global__ void __launch_bounds__(kCpcThreads, 1) cp_cluster_stage_kernel(const 
             }
         }
         cluster_sync();  // B: every CTA holds the whole attention output
+        CPC_STAMP(3 + 7 * l);
         // ---- O rows [64 rank, +64) + residual, slice to every CTA
         cpc_gemm_rows(p.w_o[l], 4 * rank, 4, kCpcH / 16, 4, act_hi, act_lo, kCpcActLd, part, outb, 64);
         for (int e = threadIdx.x; e < kCpcTok * 64; e += kCpcThreads) {
@@ -334,6 +348,7 @@ __global__ void __launch_bounds__(kCpcThreads, 1) cp_cluster_stage_kernel(const 
         __syncthreads();
         cpc_broadcast_xslice(xs, rank);
         cluster_sync();  // C: x complete in every CTA
+        CPC_STAMP(4 + 7 * l);
         // ---- post-attention norm, gate/up rows [384 rank, +384) -> SwiGLU features [192 rank, +192)
         cpc_norm(xs, p.post_norm + (size_t)l * kCpcH, p.eps, inv, act_hi, act_lo);
         cpc_gemm_rows(p.w_gu[l], 24 * rank, 24, kCpcH / 16, 2, act_hi, act_lo, kCpcActLd, part, outb, 384);
@@ -347,6 +362,7 @@ __global__ void __launch_bounds__(kCpcThreads, 1) cp_cluster_stage_kernel(const 
             feat_lo[t * kCpcFeatLd + f] = __float2bfloat16(a - __bfloat162float(hi));
         }
         __syncthreads();
+        CPC_STAMP(5 + 7 * l);
         // ---- down: all 1024 output rows over this CTA's 192 features; partial columns
         // [64 j, +64) go to CTA j (reduce-scatter)
         {
@@ -367,6 +383,7 @@ __global__ void __launch_bounds__(kCpcThreads, 1) cp_cluster_stage_kernel(const 
             }
         }
         cluster_sync();  // D: every CTA's partials for its columns have arrived
+        CPC_STAMP(6 + 7 * l);
         for (int e = threadIdx.x; e < kCpcTok * 64; e += kCpcThreads) {
             const int t = e / 64, c = e % 64;
             float s = 0.f;
@@ -376,10 +393,12 @@ __global__ void __launch_bounds__(kCpcThreads, 1) cp_cluster_stage_kernel(const 
         __syncthreads();
         cpc_broadcast_xslice(xs, rank);
         cluster_sync();  // E: x complete in every CTA
+        CPC_STAMP(7 + 7 * l);
     }
     // ---- final norm, lm_head rows [128 rank, +128) -> logits
     cpc_norm(xs, p.final_norm, p.eps, inv, act_hi, act_lo);
     cpc_gemm_rows(p.w_head, 8 * rank, 8, kCpcH / 16, 2, act_hi, act_lo, kCpcActLd, part, outb, 128);
+    CPC_STAMP(36);
     griddep_launch();
     for (int e = threadIdx.x; e < kCpcTok * 128; e += kCpcThreads) {
         const int t = e / 128, c = e % 128;

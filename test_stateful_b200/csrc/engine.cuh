@@ -21,6 +21,7 @@
 #include "attention.cuh"
 #include "common.cuh"
 #include "cp_cluster.cuh"
+#include "cp_persist.cuh"
 #include "gemm_tc.cuh"
 #include "sampling.cuh"
 #include "sched.cuh"
@@ -30,6 +31,7 @@ namespace qtts {
 
 struct LayerGemms {
     GemmPlan qkv, o, gu, down;
+    GemmPlan qkv_pair;  // code predictor: QKV in paired-tile order (persistent program)
 };
 
 struct DevBuf {
@@ -90,6 +92,12 @@ struct qtts_engine {
     bool cp_cluster = false;
     uint4 *cpc_qkv = nullptr, *cpc_o = nullptr, *cpc_gu = nullptr, *cpc_down = nullptr, *cpc_head = nullptr;
     std::vector<qtts::GemmPlan> cp_heads;
+    // code-predictor stages >= 1 as one persistent launch each (cp_persist.cuh): per stage a
+    // program of cpp_phases GEMM phases, and the grid barrier's two counters
+    bool cp_persist = false;
+    qtts::CpPhase* cpp_prog = nullptr;
+    int cpp_phases = 0;
+    unsigned* cpp_bar = nullptr;
 };
 
 namespace qtts {
@@ -252,7 +260,11 @@ inline int engine_build(qtts_engine* e) {
     {
         const char* v = getenv("QTTS_CP_PAIR");
         e->cp_pair = cD == 64 && cHq == 2 * cHkv && v && *v == '1';
-        if (e->cp_pair) QTTS_TRY(dev_alloc(e, &e->cp_qkv_pair, (size_t)d.cp_layers * e->cp_qkv_rows * cH));
+        // Opt-in (QTTS_CP_PERSIST=1): stages >= 1 as one persistent launch (paired QKV tiles).
+        const char* w = getenv("QTTS_CP_PERSIST");
+        e->cp_persist = cD == 64 && cHq == 2 * cHkv && S > 1 && w && *w == '1' && cp_persist_clusters() > 0;
+        if (e->cp_pair || e->cp_persist)
+            QTTS_TRY(dev_alloc(e, &e->cp_qkv_pair, (size_t)d.cp_layers * e->cp_qkv_rows * cH));
     }
     e->cg.resize(d.cp_layers);
     for (int l = 0; l < d.cp_layers; ++l) {
@@ -274,7 +286,8 @@ inline int engine_build(qtts_engine* e) {
         q.num_layers = d.cp_layers;
         q.block_size = 16;
         const __nv_bfloat16* wqkv = bf(d.cp_w_qkv, (size_t)l * e->cp_qkv_rows * cH);
-        if (e->cp_pair) {
+        const __nv_bfloat16* wqkv_pair = nullptr;
+        if (e->cp_qkv_pair) {
             // rows per KV head g: tile 2g = q heads 2g, 2g+1; tile 2g+1 = k_g, v_g
             __nv_bfloat16* dst = e->cp_qkv_pair + (size_t)l * e->cp_qkv_rows * cH;
             const size_t row = (size_t)cH * sizeof(__nv_bfloat16);
@@ -287,7 +300,8 @@ inline int engine_build(qtts_engine* e) {
                                            wqkv + (size_t)(cHq * 64 + cHkv * 64 + 64 * g2) * cH, 64 * row,
                                            cudaMemcpyDeviceToDevice));
             }
-            wqkv = dst;
+            wqkv_pair = dst;
+            if (e->cp_pair) wqkv = dst;
         }
         QTTS_TRY(gemm_plan(&g.qkv, e->cxn, crows, cH, wqkv, e->cp_qkv_rows, QTTS_EPI_QKV_ROPE, e->cq, nullptr, &q,
                            e->cxn_lo));
@@ -296,6 +310,14 @@ inline int engine_build(qtts_engine* e) {
             g.qkv.p.pair.out = e->cattn;
             g.qkv.p.pair.out_lo = e->cattn_lo;
             g.qkv.p.pair.scale_log2 = 1.4426950408889634f / sqrtf((float)cD);
+        }
+        if (wqkv_pair) {
+            QTTS_TRY(gemm_plan(&g.qkv_pair, e->cxn, crows, cH, wqkv_pair, e->cp_qkv_rows, QTTS_EPI_QKV_ROPE, e->cq,
+                               nullptr, &q, e->cxn_lo));
+            g.qkv_pair.p.pair.on = 1;
+            g.qkv_pair.p.pair.out = e->cattn;
+            g.qkv_pair.p.pair.out_lo = e->cattn_lo;
+            g.qkv_pair.p.pair.scale_log2 = 1.4426950408889634f / sqrtf((float)cD);
         }
         QTTS_TRY(gemm_plan(&g.o, e->cattn, crows, cHq * cD, bf(d.cp_w_o, (size_t)l * cH * cHq * cD), cH,
                            QTTS_EPI_RESIDUAL, e->cx, nullptr, nullptr, e->cattn_lo));
@@ -306,6 +328,7 @@ inline int engine_build(qtts_engine* e) {
         fold_norm_out(g.o, bf(d.cp_w_post_norm, (size_t)l * cH), e->cxn, e->cxn_lo, e->css);
         fold_norm_in(g.gu, e->css, cH, d.cp_rms_eps);
         fold_norm_in(g.qkv, e->css, cH, d.cp_rms_eps);
+        if (wqkv_pair) fold_norm_in(g.qkv_pair, e->css, cH, d.cp_rms_eps);
         // the last layer's down projection folds the final norm (used from stage 1 on, where
         // every row is a stream's last position)
         fold_norm_out(g.down, l + 1 < d.cp_layers ? bf(d.cp_w_in_norm, (size_t)(l + 1) * cH) : bf(d.cp_w_final_norm, 0),
@@ -366,6 +389,37 @@ inline int engine_build(qtts_engine* e) {
                            bf(d.cp_w_lm_head, (size_t)s * d.cp_vocab * cH), d.cp_vocab, QTTS_EPI_F32, e->clogits,
                            nullptr, nullptr, folded ? e->cxn_lo : e->chid_lo));
         if (folded) fold_norm_in(e->cp_heads[s], e->css, cH, d.cp_rms_eps);
+    }
+    if (e->cp_persist) {
+        // per stage s >= 1: [QKV pair, O, gate/up, down] x layers, lm_head
+        e->cpp_phases = 4 * d.cp_layers + 1;
+        if (e->cpp_phases > kCppMaxPhases) {
+            set_error("cp_persist: %d phases (max %d)", e->cpp_phases, kCppMaxPhases);
+            return QTTS_ERR_UNSUPPORTED;
+        }
+        std::vector<CpPhase> prog((size_t)(S - 1) * e->cpp_phases);
+        for (int s = 1; s < S; ++s) {
+            CpPhase* ph = prog.data() + (size_t)(s - 1) * e->cpp_phases;
+            const int32_t* m = e->cp_meta + (size_t)s * 4 * crows;
+            // tiles per cluster: gate/up's 48 tiles as 4 tiles x split-K 2 (one round over the
+            // clusters), the others split-K 8 (paired QKV: 2 x 4)
+            const int gu_members = env_int("QTTS_CPP_GU_MEMBERS", 4);
+            for (int l = 0; l < d.cp_layers; ++l) {
+                const LayerGemms& g = e->cg[l];
+                QTTS_TRY(cp_phase_from_plan(ph, g.qkv_pair, true, 2));
+                ph->p.qkv.row_pos = m + crows;
+                ph->p.qkv.slot_mapping = m;
+                QTTS_TRY(cp_phase_from_plan(ph + 1, g.o, false, 1));
+                QTTS_TRY(cp_phase_from_plan(ph + 2, g.gu, false, gu_members));
+                QTTS_TRY(cp_phase_from_plan(ph + 3, g.down, false, 1));
+                ph += 4;
+            }
+            QTTS_TRY(cp_phase_from_plan(ph, e->cp_heads[s], false, 1));
+        }
+        QTTS_TRY(dev_alloc(e, &e->cpp_prog, prog.size()));
+        QTTS_CHECK_CUDA(cudaMemcpy(e->cpp_prog, prog.data(), prog.size() * sizeof(CpPhase), cudaMemcpyHostToDevice));
+        QTTS_TRY(dev_alloc(e, &e->cpp_bar, 2));
+        QTTS_CHECK_CUDA(cudaMemset(e->cpp_bar, 0, 2 * sizeof(unsigned)));
     }
     QTTS_TRY(gemm_plan(&e->head, e->hid, bmax, H, d.w_codec_head, d.vocab, QTTS_EPI_F32, nullptr, nullptr, nullptr,
                        e->hid_lo));
@@ -523,7 +577,11 @@ inline int engine_step_impl(qtts_engine* e, const qtts_step_io& io, cudaStream_t
     for (int s = 0; s < d.cp_stages; ++s) {
         const int rows = s == 0 ? 2 * nr : nr;
         const int32_t* m = e->cp_meta + (size_t)s * 4 * crows;
-        if (s > 0 && e->cp_cluster) {
+        if (s > 0 && e->cp_persist) {
+            // the stage's 5 layers and lm_head in one persistent launch: logits -> e->clogits
+            QTTS_TRY(launch_cp_persist(e->cpp_prog + (size_t)(s - 1) * e->cpp_phases, e->cpp_phases, nr, e->cpp_bar,
+                                       st));
+        } else if (s > 0 && e->cp_cluster) {
             // the stage's 5 layers and lm_head in one cluster launch: logits -> e->clogits
             cpc.stage = s;
             cpc.w_head = e->cpc_head + (size_t)s * d.cp_vocab * cH / 8;

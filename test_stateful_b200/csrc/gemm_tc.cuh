@@ -201,7 +201,7 @@ __device__ void gemm_epilogue(const GemmParams& p, float* R, int m0, int per, in
                     float old[B];
 #pragma unroll
                     for (int u = 0; u < B; ++u)
-                        old[u] = pre_old ? pre_old[u] : (ok[u] ? reinterpret_cast<const float*>(p.out)[o[u]] : 0.f);
+                        old[u] = pre_old ? pre_old[u] : (ok[u] ? __ldcg(reinterpret_cast<const float*>(p.out) + o[u]) : 0.f);
 #pragma unroll
                     for (int u = 0; u < B; ++u) {
                         v[u] += old[u];
@@ -572,6 +572,104 @@ __device__ void pair_attention(const GemmParams& p, int m0, int per, int tile_n,
 }
 
 // ---------------------------------------------------------------------------
+// pieces of a split-K tile shared by the per-launch kernel and the persistent
+// code-predictor kernel (cp_persist.cuh)
+// ---------------------------------------------------------------------------
+
+// Per-token data the epilogue needs, gathered while the cluster reduction runs: the folded
+// norm's inv_rms (scratch[512 + i], from the producer's per-tile sums of squares, read through
+// L2 because a persistent kernel's earlier phase wrote them) and the QKV epilogue's token
+// metadata.
+template <int BN, int NT>
+__device__ __forceinline__ void epilogue_meta(const GemmParams& p, float* scratch, int m0, int per, int tile_m) {
+    if (p.nin.ss) {
+        for (int i = threadIdx.x; i < per; i += NT) {
+            const int m_g = tile_m * BN + m0 + i;
+            float tot = 0.f;
+            if (m_g < p.M) {
+                const float* q = p.nin.ss + (size_t)m_g * p.nin.parts;
+                for (int j = 0; j < p.nin.parts; ++j) tot += __ldcg(q + j);  // fixed order: deterministic
+            }
+            scratch[512 + i] = rsqrtf(tot / (float)p.nin.K + p.nin.eps);
+        }
+    }
+    if (p.epilogue == QTTS_EPI_QKV_ROPE) {
+        // token metadata of the QKV epilogue: clamped RoPE position, and the KV-pool row of
+        // (block, layer, k, head 0, offset) for the token's slot (-1: not stored)
+        const qtts_qkv_epilogue& e = p.qkv;
+        int* tok_pos = reinterpret_cast<int*>(scratch) + 256;
+        int* tok_kv = tok_pos + 128;
+        for (int i = threadIdx.x; i < per; i += NT) {
+            const int m_g = tile_m * BN + m0 + i;
+            const int pos = m_g < p.M ? e.row_pos[m_g] : 0;
+            const int slot = m_g < p.M ? e.slot_mapping[m_g] : -1;
+            tok_pos[i] = pos < 0 ? 0 : (pos >= e.max_pos ? e.max_pos - 1 : pos);  // table bounds
+            const int kb = slot < 0 ? 0 : ((slot / e.block_size) * e.num_layers + e.layer) * 2 * e.kv_heads * e.block_size;
+            tok_kv[i] = slot < 0 ? -1 : kb + slot % e.block_size;
+            if (p.pair.on) {  // the token's block (keys 0 .. its offset) for the pair's attention
+                reinterpret_cast<int*>(scratch)[640 + i] = kb;
+                reinterpret_cast<int*>(scratch)[768 + i] = slot < 0 ? 0 : slot % e.block_size + 1;
+            }
+        }
+    }
+}
+
+// The residual epilogue's old values of this thread's row for up to 8 tokens, loaded early
+// (through L2: the residual stream is rewritten by other CTAs between phases).
+template <int BN, int NT>
+__device__ __forceinline__ void residual_prefetch(const GemmParams& p, int m0, int per, int tile_n, int tile_m,
+                                                  float (&pre_old)[8]) {
+    const int t = threadIdx.x & 127, grp = threadIdx.x >> 7;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+        const int i = grp + (NT / 128) * u;
+        const int m_g = tile_m * BN + m0 + i;
+        pre_old[u] = (i < per && m_g < p.M)
+                         ? __ldcg(reinterpret_cast<const float*>(p.out) + (size_t)m_g * p.N + tile_n * 128 + t)
+                         : 0.f;
+    }
+}
+
+// Split-K reduction of this CTA's token slice [m0, m0 + per): the fp32 partials P[token][128]
+// of the cluster's CTAs (each in its own shared memory) are summed in a fixed order into this
+// CTA's P.  A cluster of `members` tiles x splits: the splits of member pm are ranks
+// members * r + pm (paired QKV tiles: members 2).  The loads of two float4 chunks from every
+// split are issued before any is consumed, so the remote-shared-memory latency is paid once
+// per 16 loads.
+template <int NT>
+__device__ __forceinline__ void cluster_reduce_slice(float* P, int m0, int per, int splits, int members, int pm) {
+    const uint32_t base = smem_u32(P + m0 * 128);
+    for (int e = threadIdx.x; e < per * 32; e += 2 * NT) {
+        const int e2 = e + NT;
+        const bool two = e2 < per * 32;
+        float4 v[2][8];
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+            if (r < splits) {
+                const uint32_t peer = (uint32_t)(members * r + pm);
+                v[0][r] = ld_dsmem_f32x4(map_to_rank(base + (uint32_t)e * 16u, peer));
+                if (two) v[1][r] = ld_dsmem_f32x4(map_to_rank(base + (uint32_t)e2 * 16u, peer));
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            if (h == 1 && !two) break;
+            float4 acc = v[h][0];
+#pragma unroll
+            for (int r = 1; r < 8; ++r) {  // fixed order: deterministic
+                if (r < splits) {
+                    acc.x += v[h][r].x;
+                    acc.y += v[h][r].y;
+                    acc.z += v[h][r].z;
+                    acc.w += v[h][r].w;
+                }
+            }
+            *reinterpret_cast<float4*>(P + m0 * 128 + (h ? e2 : e) * 4) = acc;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
 template <int BN, int STAGES, bool SPLIT, int NT, bool PUSH = false>
@@ -754,49 +852,10 @@ __global__ void __launch_bounds__(NT) gemm_tc_kernel(const __grid_constant__ CUt
     // Loads the epilogue needs are issued between arriving at the cluster barrier
     // and waiting on it, so they overlap the barrier and the reduction: the old
     // residual (when the token slice is one batch) and the norm-in partial sums.
-    if (p.nin.ss) {
-        for (int i = threadIdx.x; i < per; i += NT) {
-            const int m_g = tile_m * BN + m0 + i;
-            float tot = 0.f;
-            if (m_g < p.M) {
-                const float* q = p.nin.ss + (size_t)m_g * p.nin.parts;
-                for (int j = 0; j < p.nin.parts; ++j) tot += q[j];  // fixed order: deterministic
-            }
-            scratch[512 + i] = rsqrtf(tot / (float)p.nin.K + p.nin.eps);
-        }
-    }
-    if (p.epilogue == QTTS_EPI_QKV_ROPE) {
-        // token metadata of the QKV epilogue: clamped RoPE position, and the KV-pool row of
-        // (block, layer, k, head 0, offset) for the token's slot (-1: not stored)
-        const qtts_qkv_epilogue& e = p.qkv;
-        int* tok_pos = reinterpret_cast<int*>(scratch) + 256;
-        int* tok_kv = tok_pos + 128;
-        for (int i = threadIdx.x; i < per; i += NT) {
-            const int m_g = tile_m * BN + m0 + i;
-            const int pos = m_g < p.M ? e.row_pos[m_g] : 0;
-            const int slot = m_g < p.M ? e.slot_mapping[m_g] : -1;
-            tok_pos[i] = pos < 0 ? 0 : (pos >= e.max_pos ? e.max_pos - 1 : pos);  // table bounds
-            const int kb = slot < 0 ? 0 : ((slot / e.block_size) * e.num_layers + e.layer) * 2 * e.kv_heads * e.block_size;
-            tok_kv[i] = slot < 0 ? -1 : kb + slot % e.block_size;
-            if (p.pair.on) {  // the token's block (keys 0 .. its offset) for the pair's attention
-                reinterpret_cast<int*>(scratch)[640 + i] = kb;
-                reinterpret_cast<int*>(scratch)[768 + i] = slot < 0 ? 0 : slot % e.block_size + 1;
-            }
-        }
-    }
+    epilogue_meta<BN, NT>(p, scratch, m0, per, tile_m);
     float pre_old[8];
     const bool prefetch = p.epilogue == QTTS_EPI_RESIDUAL && per <= 8 * (NT / 128);
-    if (prefetch) {
-        const int t = threadIdx.x & 127, grp = threadIdx.x >> 7;
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const int i = grp + (NT / 128) * u;
-            const int m_g = tile_m * BN + m0 + i;
-            pre_old[u] = (i < per && m_g < p.M)
-                             ? reinterpret_cast<const float*>(p.out)[(size_t)m_g * p.N + tile_n * 128 + t]
-                             : 0.f;
-        }
-    }
+    if (prefetch) residual_prefetch<BN, NT>(p, m0, per, tile_n, tile_m, pre_old);
     if (push) {
         cluster_wait();  // every peer's partial of this CTA's token slice has landed here
         const float* recv = reinterpret_cast<const float*>(smem + L::RING);
@@ -818,38 +877,7 @@ __global__ void __launch_bounds__(NT) gemm_tc_kernel(const __grid_constant__ CUt
         __syncthreads();
     } else if (p.splits > 1) {
         cluster_wait();  // every CTA's partial is in its shared memory
-        // this CTA's token slice, as float4 chunks: the loads of two chunks from
-        // every split are issued before any is consumed, so the remote-shared-memory
-        // latency is paid once per 16 loads
-        const uint32_t base = smem_u32(P + m0 * 128);
-        for (int e = threadIdx.x; e < per * 32; e += 2 * NT) {
-            const int e2 = e + NT;
-            const bool two = e2 < per * 32;
-            float4 v[2][8];
-#pragma unroll
-            for (int r = 0; r < 8; ++r) {
-                if (r < p.splits) {
-                    const uint32_t peer = p.pair.on ? (uint32_t)(2 * r + pm) : (uint32_t)r;
-                    v[0][r] = ld_dsmem_f32x4(map_to_rank(base + (uint32_t)e * 16u, peer));
-                    if (two) v[1][r] = ld_dsmem_f32x4(map_to_rank(base + (uint32_t)e2 * 16u, peer));
-                }
-            }
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                if (h == 1 && !two) break;
-                float4 acc = v[h][0];
-#pragma unroll
-                for (int r = 1; r < 8; ++r) {  // fixed order: deterministic
-                    if (r < p.splits) {
-                        acc.x += v[h][r].x;
-                        acc.y += v[h][r].y;
-                        acc.z += v[h][r].z;
-                        acc.w += v[h][r].w;
-                    }
-                }
-                *reinterpret_cast<float4*>(P + m0 * 128 + (h ? e2 : e) * 4) = acc;
-            }
-        }
+        cluster_reduce_slice<NT>(P, m0, per, p.splits, p.pair.on ? 2 : 1, pm);
         if (!p.pair.on) cluster_arrive();  // done reading the peers' shared memory
         __syncthreads();
     } else if (p.nin.ss || p.epilogue == QTTS_EPI_QKV_ROPE) {

@@ -270,13 +270,15 @@ def test_cfg1_full_model_greedy_against_reference():
     assert (talk.agree + cp.agree) / (talk.total + cp.total) >= GREEDY_AGREEMENT
 
 
-@pytest.mark.parametrize("cp_cluster", ["0", "1"], ids=["per-gemm", "cluster"])
-def test_full_width_code_predictor_stage_logits(cp_cluster, monkeypatch):
+@pytest.mark.parametrize("cp_form", ["per-gemm", "cluster", "persist"])
+def test_full_width_code_predictor_stage_logits(cp_form, monkeypatch):
     """Full talker/CP widths with 4 talker layers: the device's code-predictor
     logits at every stage against the oracle's (same hidden, same forced tokens).
-    Both forms of the stages >= 1: the per-GEMM launches and the one-launch cluster
-    kernel (QTTS_CP_CLUSTER=1, read when the engine is built)."""
-    monkeypatch.setenv("QTTS_CP_CLUSTER", cp_cluster)
+    Every form of the stages >= 1 (read when the engine is built): the per-GEMM
+    launches, the one-launch cluster kernel (QTTS_CP_CLUSTER=1) and the persistent
+    program (QTTS_CP_PERSIST=1)."""
+    monkeypatch.setenv("QTTS_CP_CLUSTER", "1" if cp_form == "cluster" else "0")
+    monkeypatch.setenv("QTTS_CP_PERSIST", "1" if cp_form == "persist" else "0")
     cfg = EngineConfig()
     cfg.talker.num_layers = 4
     cfg.pool = PagedPoolConfig(block_size=16, num_blocks=256, max_slots=8, max_seq_len=512)
@@ -305,7 +307,7 @@ def test_full_width_code_predictor_stage_logits(cp_cluster, monkeypatch):
             cpt.logits(out["cp_logits"][0, s], stage[s][0])
             cpt.tokens(out["cp_logits"][0, s].argmax(), stage[s][0].argmax())
     r.m.close()
-    print(f"full-width ({cp_cluster=}): talker rel err {talk.worst:.4f}, cp stage rel err {cpt.worst:.4f}, "
+    print(f"full-width ({cp_form}): talker rel err {talk.worst:.4f}, cp stage rel err {cpt.worst:.4f}, "
           f"cp greedy agreement {cpt.rate:.4f}")
     assert talk.worst <= LOGIT_TOL
     assert cpt.worst <= LOGIT_TOL
