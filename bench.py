@@ -83,6 +83,9 @@ def parse():
                          "for an ncu DRAM capture of the attention and GEMM kernels)")
     ap.add_argument("--num-blocks", type=int, default=8192,
                     help="KV pool blocks (8192 = the benchmark's pool; the streams use about 2300)")
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg5"],
+                    help="cfg2: the decode-step benchmark (default); cfg5: whole-box serving run — "
+                         "128 requests/GPU arriving as a Poisson process at 25 req/s/GPU (200 req/s on 8 GPUs)")
     return ap.parse_args()
 
 
@@ -536,12 +539,101 @@ def run_b200(rank, world, local):
     print(json.dumps(line), flush=True)
 
 
+CFG5_PER_GPU = 128          # requests (streams) per GPU
+CFG5_RATE_PER_GPU = 25.0    # requests/s per GPU: 200 req/s over 8 GPUs
+CFG5_SEED = 5
+
+
+def run_cfg5(rank, world, local):
+    """BASELINE configs[4] on this box's GPUs: the whole-box request stream (128 x world
+    requests at 25 x world req/s, prompts U{8..128} ids, 25-250 frames, 30 % opening with one of
+    8 shared 96-id prefixes) is routed once (``ReplicaRouter``: least-loaded, prefix affinity)
+    and every rank serves its share with ``serve_replica`` (chunked prefill interleaved with
+    decode; talker, code predictor, sampling and code2wav per step).  Wall-clock timing: the
+    run is paced by the arrivals, so the device is idle between them by design."""
+    from test_stateful_b200 import workload
+    from test_stateful_b200.config import EngineConfig
+    from test_stateful_b200.runtime.executor import B200Executor
+    from test_stateful_b200.runtime.replicas import max_over_ranks, share_routing
+    from test_stateful_b200.runtime.serving_loop import cfg5_requests, percentile, prefix_key, serve_replica
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=600))
+    reqs, prefixes = cfg5_requests(CFG5_PER_GPU * world, CFG5_RATE_PER_GPU * world, CFG5_SEED)
+    mine_sessions, _ = share_routing([(r.rid, prefix_key(r)) for r in reqs], rank, world, CFG5_PER_GPU)
+    mine_ids = {sid for sid, _key in mine_sessions}
+    mine = [r for r in reqs if r.rid in mine_ids]
+    cfg = EngineConfig()
+    ex = B200Executor(device_id=local, max_batch_size=CFG5_PER_GPU, max_seq_len=512, model_config=cfg,
+                      do_sample=True, temperature=0.9, random_seed=CFG5_SEED + rank, num_blocks=ARGS.num_blocks,
+                      weight_seed=SEED)
+    ex.load()
+    t = cfg.talker
+    table = workload.text_table(t.hidden_size, SEED, device=dev)
+    pad = workload.tts_pad_embed(t.hidden_size, SEED, device=dev)
+    ex.warmup()
+    t_cap = time.perf_counter()
+    ex.capture_graphs(range(1, CFG5_PER_GPU + 1))
+    t_cap = time.perf_counter() - t_cap
+    if world > 1:
+        torch.distributed.barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    st = serve_replica(ex, mine, prefixes, table, pad, prefill_chunk=64)
+    clk = clocks.stop()
+    wall = max_over_ranks(st.wall_s, world, device=dev)
+    frames = st.frames
+    if world > 1:
+        tot = torch.tensor([float(frames), float(st.completed)], dtype=torch.float64, device=dev)
+        torch.distributed.all_reduce(tot)
+        frames, completed = int(tot[0].item()), int(tot[1].item())
+    else:
+        completed = st.completed
+    ex._graphs.clear()
+    ex.shutdown()
+    if world > 1:
+        torch.distributed.destroy_process_group()
+    if rank != 0:
+        return
+    value = frames / wall
+    line = {
+        "metric": "codec frames/s, whole-box serving (cfg5): Poisson arrivals, chunked prefill interleaved with "
+                  "decode, talker + code predictor + sampling + code2wav per step",
+        "value": round(value, 1), "unit": UNIT, "n_gpus": world, "per_gpu": round(value / world, 1),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded Poisson arrivals and random prompt ids; random-init weights)",
+        "config": {"workload": "cfg5: 128 requests/GPU at 25 req/s/GPU (200 req/s on 8 GPUs), prompts U{8..128} "
+                               "ids, 25-250 frames (2-20 s), 30% open with one of 8 shared 96-id prefixes",
+                   "requests": len(reqs), "parallelism": f"replicas x{world} (ReplicaRouter: least-loaded, "
+                                                          "prefix affinity; no collective)",
+                   "prefill_chunk": 64, "graphs_captured": f"batch sizes 1..{CFG5_PER_GPU} ({t_cap:.1f} s)"},
+        "wall_s": round(wall, 3), "frames": frames, "completed": completed,
+        "rank0": {"requests": len(mine), "frames": st.frames, "decode_steps": st.decode_steps,
+                  "max_running": st.max_running, "prefill_calls": st.prefill_calls,
+                  "prefix_hits": st.prefix_hits, "prefix_misses": st.prefix_misses,
+                  "ttfa_ms_p50": round(1e3 * percentile(st.ttfa_s, 50), 2),
+                  "ttfa_ms_p90": round(1e3 * percentile(st.ttfa_s, 90), 2),
+                  "step_ms_p50": round(1e3 * percentile(st.step_s, 50), 3) if st.step_s else None,
+                  "step_ms_p90": round(1e3 * percentile(st.step_s, 90), 3) if st.step_s else None,
+                  "audio_s_per_wall_s": round(st.frames / 12.5 / st.wall_s, 1)},
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     global ARGS
     ARGS = parse()
     rank, world, local = dist_env()
     if ARGS.impl == "reference":
         run_reference(rank, world)
+        return
+    if ARGS.workload == "cfg5":
+        run_cfg5(rank, world, local)
         return
     run_b200(rank, world, local)
 

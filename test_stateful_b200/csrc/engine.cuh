@@ -423,6 +423,28 @@ inline int engine_build(qtts_engine* e) {
     }
     QTTS_TRY(gemm_plan(&e->head, e->hid, bmax, H, d.w_codec_head, d.vocab, QTTS_EPI_F32, nullptr, nullptr, nullptr,
                        e->hid_lo));
+    // Each projection prefetches the next one's weights into L2 while its own chain of
+    // latencies runs (QTTS_L2_CHAIN=0: off): talker qkv -> o -> gate/up -> down -> next layer's
+    // qkv (the last layer: the codec head); code predictor likewise, its last down -> the first
+    // qkv of the next stage (the stage's lm_head is small)
+    if (env_int("QTTS_L2_CHAIN", 1)) {
+        for (int l = 0; l < d.layers; ++l) {
+            LayerGemms& g = e->tg[l];
+            gemm_chain_l2(g.qkv, g.o);
+            gemm_chain_l2(g.o, g.gu);
+            gemm_chain_l2(g.gu, g.down);
+            gemm_chain_l2(g.down, l + 1 < d.layers ? e->tg[l + 1].qkv : e->head);
+        }
+        for (int l = 0; l < d.cp_layers; ++l) {
+            LayerGemms& g = e->cg[l];
+            const LayerGemms& n = e->cg[(l + 1) % d.cp_layers];
+            gemm_chain_l2(g.qkv, g.o);
+            if (e->cp_qkv_pair) gemm_chain_l2(g.qkv_pair, g.o);
+            gemm_chain_l2(g.o, g.gu);
+            gemm_chain_l2(g.gu, g.down);
+            gemm_chain_l2(g.down, e->cp_persist ? n.qkv_pair : n.qkv);
+        }
+    }
     return QTTS_OK;
 }
 

@@ -132,6 +132,10 @@ struct GemmParams {
     NormOut nout;
     NormIn nin;
     PairAttn pair;
+    // L2 prefetch hint: the weights of the GEMM that runs after this one (prefetched in
+    // slices by the launch's CTAs while their own chain of latencies runs), or NULL
+    const uint8_t* l2_next;
+    unsigned long long l2_next_bytes;
 };
 
 template <int BN, int STAGES, bool SPLIT, bool PUSH = false>
@@ -571,6 +575,19 @@ __device__ void pair_attention(const GemmParams& p, int m0, int per, int tile_n,
     }
 }
 
+// This CTA's slice of the L2 prefetch of the next GEMM's weights (GemmParams::l2_next):
+// 4 KB-aligned slices, one bulk prefetch per 32 KB.  A hint: no data moves into the SM.
+__device__ __forceinline__ void l2_prefetch_slice(const uint8_t* base, unsigned long long bytes, int cta, int ctas) {
+    const unsigned long long per = ((bytes / (unsigned long long)ctas) + 4095ull) & ~4095ull;
+    const unsigned long long b0 = (unsigned long long)cta * per;
+    const unsigned long long b1 = b0 + per < bytes ? b0 + per : bytes;
+    for (unsigned long long o = b0; o < b1; o += 32768ull) {
+        const unsigned long long rest = b1 - o;
+        const uint32_t n = (uint32_t)(rest < 32768ull ? rest : 32768ull) & ~15u;
+        if (n) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base + o), "r"(n) : "memory");
+    }
+}
+
 // ---------------------------------------------------------------------------
 // pieces of a split-K tile shared by the per-launch kernel and the persistent
 // code-predictor kernel (cp_persist.cuh)
@@ -719,6 +736,10 @@ __global__ void __launch_bounds__(NT) gemm_tc_kernel(const __grid_constant__ CUt
             tma_load_2d(smem + i * L::STAGE_BYTES, &tmW, &full[i], (kb0 + i) * 64, tile_n * 128);
         }
     }
+    if (p.l2_next && threadIdx.x == 96)  // warp 3 has no role before the epilogue
+        l2_prefetch_slice(p.l2_next, p.l2_next_bytes,
+                          (int)(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z)),
+                          (int)(gridDim.x * gridDim.y * gridDim.z));
     griddep_wait();  // activations, outputs and the KV pool belong to earlier kernels
     griddep_launch();
     if (warp == 2) {
@@ -1265,7 +1286,15 @@ struct GemmPlan {
     CUtensorMap mw, mx32, mx64, mx128, mlo32, mlo64, mlo128;
     GemmParams p;
     bool split;
+    const void* w;       // the weight matrix [N][K] bf16
+    size_t w_bytes;
 };
+
+// Prefetch `next`'s weights into L2 from the launches of `g` (see GemmParams::l2_next).
+inline void gemm_chain_l2(GemmPlan& g, const GemmPlan& next) {
+    g.p.l2_next = reinterpret_cast<const uint8_t*>(next.w);
+    g.p.l2_next_bytes = next.w_bytes;
+}
 
 inline int gemm_plan(GemmPlan* g, const void* X, int rows, int K, const void* W, int N, int epilogue, void* out,
                      const void* bias, const qtts_qkv_epilogue* qkv, const void* X_lo = nullptr,
@@ -1299,6 +1328,8 @@ inline int gemm_plan(GemmPlan* g, const void* X, int rows, int K, const void* W,
         g->mlo64 = g->mx64;
         g->mlo128 = g->mx128;
     }
+    g->w = W;
+    g->w_bytes = (size_t)N * K * sizeof(__nv_bfloat16);
     GemmParams& p = g->p;
     memset(&p, 0, sizeof(p));
     p.M = rows;

@@ -410,19 +410,22 @@ class B200Executor:
         codes = self.codes[:1].cpu()
         return audio, bool(int(codes[0, 0]) == self._config.talker.codec_eos_id)
 
-    def iter_prefill(self, slot: SlotState, prefill_embeds: torch.Tensor, chunk: int = 128):
+    def iter_prefill(self, slot: SlotState, prefill_embeds: torch.Tensor, chunk: int = 128, keep_kv: bool = False):
         """Chunked prefill (the first "next" item after the decode step: prefill interleaved with
         decode).  A generator: each ``next()`` runs one engine step over the following
         ``chunk`` prompt tokens (KV appended after the previous chunk's; no sampling) and yields
         ``None``; the last chunk samples the first frame, and the final ``next()`` yields
         ``prefill``'s ``(audio bytes, eos)``.  A serving loop calls ``next()`` between decode
         steps, so a long prompt never stalls the running streams for more than one chunk.
-        Prompts longer than ``max_prefill_rows`` are accepted (each chunk is at most that)."""
+        Prompts longer than ``max_prefill_rows`` are accepted (each chunk is at most that).
+        ``keep_kv``: append after the KV the slot already holds (a restored or freshly cached
+        prefix), as ``prefill_from_prefix`` does, instead of starting an empty sequence."""
         seq = int(prefill_embeds.shape[1])
         if chunk < 1:
             raise ValueError("chunk must be >= 1")
         chunk = min(chunk, self._max_input_len)
-        self._kv_pool.init_kv_tensors(slot)
+        if not keep_kv:
+            self._kv_pool.init_kv_tensors(slot)
         self._configure_sampling(slot)
         for start in range(0, seq, chunk):
             last = start + chunk >= seq
@@ -538,6 +541,19 @@ class B200Executor:
             g = self._capture(n)
             self._graphs[n] = g
         return g[1]
+
+    def capture_graphs(self, sizes) -> None:
+        """Capture the decode-step CUDA graphs of every batch size in ``sizes`` ahead of time (a
+        serving loop whose batch size changes every few steps would otherwise pay a capture the
+        second time each size occurs)."""
+        torch.cuda.synchronize(self._device)
+        for n in sizes:
+            n = int(n)
+            if not 1 <= n <= self._max_batch:
+                raise ValueError(f"batch size {n} outside [1, {self._max_batch}]")
+            if self._graphs.get(n) is None:
+                self._graphs[n] = self._capture(n)
+        torch.cuda.synchronize(self._device)
 
     def replay_step(self, n: int):
         """One decode step of the batch `prepare_replay` set up; returns (event after
