@@ -423,11 +423,15 @@ inline int engine_build(qtts_engine* e) {
     }
     QTTS_TRY(gemm_plan(&e->head, e->hid, bmax, H, d.w_codec_head, d.vocab, QTTS_EPI_F32, nullptr, nullptr, nullptr,
                        e->hid_lo));
-    // Each projection prefetches the next one's weights into L2 while its own chain of
-    // latencies runs (QTTS_L2_CHAIN=0: off): talker qkv -> o -> gate/up -> down -> next layer's
-    // qkv (the last layer: the codec head); code predictor likewise, its last down -> the first
-    // qkv of the next stage (the stage's lm_head is small)
-    if (env_int("QTTS_L2_CHAIN", 1)) {
+    // A projection prefetches the next one's weights into L2 while its own chain of latencies
+    // runs.  QTTS_L2_CHAIN=1 (default): the code predictor's qkv -> o -> gate/up -> down -> next
+    // layer's qkv (the last down -> the first qkv of the next stage; the lm_head is small),
+    // whose 124 MB of weights per stage about fill L2; 2: the talker's projections as well
+    // (qkv -> o -> gate/up -> down -> next qkv, the last -> the codec head), measured 3.6 %
+    // slower on the talker, whose weights stream from HBM at a rate the prefetch does not
+    // raise; 0: off.
+    const int l2_chain = env_int("QTTS_L2_CHAIN", 1);
+    if (l2_chain >= 2) {
         for (int l = 0; l < d.layers; ++l) {
             LayerGemms& g = e->tg[l];
             gemm_chain_l2(g.qkv, g.o);
@@ -435,6 +439,8 @@ inline int engine_build(qtts_engine* e) {
             gemm_chain_l2(g.gu, g.down);
             gemm_chain_l2(g.down, l + 1 < d.layers ? e->tg[l + 1].qkv : e->head);
         }
+    }
+    if (l2_chain >= 1) {
         for (int l = 0; l < d.cp_layers; ++l) {
             LayerGemms& g = e->cg[l];
             const LayerGemms& n = e->cg[(l + 1) % d.cp_layers];
