@@ -1,6 +1,7 @@
 """Single-kernel timing on small cases that still exceed L2 (126 MB).
 
     python microbench.py attention [--rows 64] [--ctx-mean 520] [--launches 50]
+    python microbench.py prefill-attention [--streams 8] [--prefill-chunk 128] [--past 384]
     python microbench.py gemm [--n 12288] [--k 2048] [--m 64] [--launches 50]
     python microbench.py code2wav [--rows 64] [--launches 50] [--chunk 25]
 
@@ -71,6 +72,60 @@ def bench_attention(rows: int, ctx_mean: int, launches: int, layers: int = 4, se
     algo = int(ctx.sum()) * 2 * 8 * 128 * 2 + rows * 16 * 128 * (4 + 4)
     return {"kernel": "paged_attn_tc_kernel", "split_blocks": split or 16, "rows": rows, "ctx_sum": int(ctx.sum()), "launch_us": sec * 1e6,
             "algorithmic_bytes": algo, "achieved_gbs": algo / sec / 1e9}
+
+
+def bench_prefill_attention(streams: int, chunk: int, past: int, launches: int, layers: int = 8, seed: int = 0,
+                            split: int = 0):
+    """One prompt chunk per stream: ``chunk`` query rows at positions past .. past + chunk - 1
+    (causal key counts past + t + 1), every stream's blocks scattered over the pool.  Times the
+    query-tile prefill kernel and, for comparison, the decode kernel given the same rows (one
+    row per query, each re-reading its whole context).  Bytes counted once per launch: the K+V
+    of every key the chunk sees + q in / out ("unique")."""
+    dev = "cuda"
+    g = torch.Generator().manual_seed(seed)
+    ctx_end = past + chunk
+    nblk = -(-ctx_end // 16)
+    total = streams * nblk
+    kv = torch.randn(total, layers, 2, 8, 16, 128, generator=g).to(torch.float16).to(dev)
+    perm = torch.randperm(total, generator=g).to(torch.int32)
+    table = perm.view(streams, nblk).contiguous().to(dev)
+    R = streams * chunk
+    q = torch.randn(R, 16, 128, generator=g).to(dev)
+    row_slot = torch.tensor([b for b in range(streams) for _ in range(chunk)], dtype=torch.int32, device=dev)
+    row_ctx = torch.tensor([past + t + 1 for _ in range(streams) for t in range(chunk)], dtype=torch.int32,
+                           device=dev)
+    max_ctx = nblk * 16
+    out = torch.empty(R, 16 * 128, device=dev, dtype=torch.bfloat16)
+    out_lo = torch.empty_like(out)
+
+    def timed(fn):
+        for i in range(3):
+            fn(i % layers)
+        torch.cuda.synchronize()
+        s = torch.cuda.Stream()
+        with torch.cuda.stream(s):
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=s):
+                for i in range(launches):
+                    fn(i % layers)
+            graph.replay()
+            s.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            graph.replay()
+            e1.record(s)
+            s.synchronize()
+        return e0.elapsed_time(e1) / 1e3 / launches
+
+    t_pre = timed(lambda l: ops.paged_attention_prefill(q, kv, l, table, row_slot, row_ctx, max_ctx, chunk, out=out,
+                                                        out_lo=out_lo, split_blocks=split))
+    t_dec = timed(lambda l: ops.paged_attention(q, kv, l, table, row_slot, row_ctx, max_ctx, out=out, out_lo=out_lo,
+                                                split_blocks=split))
+    unique = streams * ctx_end * 2 * 8 * 128 * 2 + R * 16 * 128 * (4 + 4)
+    return {"kernel": "paged_prefill_tc_kernel (8-query tiles)", "streams": streams, "chunk": chunk, "past": past,
+            "split_blocks": split or 16, "launch_us": t_pre * 1e6, "unique_bytes": unique,
+            "achieved_unique_gbs": unique / t_pre / 1e9, "prefill_tokens_per_s": R / t_pre,
+            "decode_kernel_same_rows_us": t_dec * 1e6, "speedup_vs_decode_rows": t_dec / t_pre}
 
 
 def bench_gemm(n: int, k: int, m: int, launches: int, seed: int = 0, plain: bool = False):
@@ -156,7 +211,10 @@ def bench_code2wav(rows: int, launches: int, seed: int = 0, chunk: int = 1):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["attention", "gemm", "code2wav"])
+    ap.add_argument("what", choices=["attention", "prefill-attention", "gemm", "code2wav"])
+    ap.add_argument("--streams", type=int, default=8, help="prefill-attention: streams with one chunk each")
+    ap.add_argument("--prefill-chunk", type=int, default=128, help="prefill-attention: query rows per stream")
+    ap.add_argument("--past", type=int, default=384, help="prefill-attention: positions before the chunk")
     ap.add_argument("--rows", type=int, default=64)
     ap.add_argument("--ctx-mean", type=int, default=520)
     ap.add_argument("--n", type=int, default=12288)
@@ -169,6 +227,8 @@ def main():
     a = ap.parse_args()
     if a.what == "attention":
         r = bench_attention(a.rows, a.ctx_mean, a.launches, split=a.split)
+    elif a.what == "prefill-attention":
+        r = bench_prefill_attention(a.streams, a.prefill_chunk, a.past, a.launches, split=a.split)
     elif a.what == "code2wav":
         r = bench_code2wav(a.rows, a.launches, chunk=a.chunk)
     else:

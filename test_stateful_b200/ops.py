@@ -89,6 +89,34 @@ def paged_attention(q: torch.Tensor, kv_pool: torch.Tensor, layer: int, block_ta
     return out
 
 
+def paged_attention_prefill(q: torch.Tensor, kv_pool: torch.Tensor, layer: int, block_table: torch.Tensor,
+                            row_slot: torch.Tensor, row_ctx: torch.Tensor, max_ctx: int, rows_per_stream: int,
+                            out: Optional[torch.Tensor] = None, ws_o: Optional[torch.Tensor] = None,
+                            ws_ml: Optional[torch.Tensor] = None, out_lo: Optional[torch.Tensor] = None,
+                            split_blocks: int = 0) -> torch.Tensor:
+    """Chunked-prefill attention (head_dim 128): ``q [R, Hq, D]`` holds ``R / rows_per_stream``
+    streams of ``rows_per_stream`` consecutive query rows each (row_ctx causal: past + t + 1);
+    the 8-query tiles of a stream share every KV block they read."""
+    _need_cuda(q, kv_pool, block_table, row_slot, row_ctx)
+    R, Hq, D = q.shape
+    nb, L, _, Hkv, bs, _ = kv_pool.shape
+    n_blocks = -(-max_ctx // bs)
+    splits = max(1, -(-n_blocks // (split_blocks or _lib.ATTN_SPLIT_BLOCKS)))
+    if out is None:
+        out = torch.empty(R, Hq * D, device=q.device, dtype=torch.bfloat16)
+    if ws_o is None:
+        ws_o = torch.empty(R * Hq * splits * D, device=q.device, dtype=torch.float32)
+    if ws_ml is None:
+        ws_ml = torch.empty(R * Hq * splits * 2, device=q.device, dtype=torch.float32)
+    rc = _lib.load().qtts_paged_attention_prefill(q.data_ptr(), R, rows_per_stream, Hq, Hkv, D, kv_pool.data_ptr(),
+                                                  layer, L, bs, nb, block_table.data_ptr(), block_table.shape[-1],
+                                                  row_slot.data_ptr(), row_ctx.data_ptr(), max_ctx, split_blocks,
+                                                  ws_o.data_ptr(), ws_ml.data_ptr(), out.data_ptr(), _lib.ptr(out_lo),
+                                                  _lib.stream_ptr())
+    _lib.check(rc, "paged_attention_prefill")
+    return out
+
+
 def sample(logits: torch.Tensor, topk: int, gumbel: Optional[torch.Tensor] = None, temperature=None, penalty=None,
            counts: Optional[torch.Tensor] = None, eos_id: int = -1, seed: int = 0,
            noise_key: Optional[torch.Tensor] = None, step: int = 0, tok_out: Optional[torch.Tensor] = None,
