@@ -439,6 +439,32 @@ int qtts_c2w_launches(const qtts_c2w* c);
  * Default 0.  No counterpart in the reference (its code2wav is inside the fused plan). */
 int qtts_c2w_set_background(qtts_c2w* c, int background);
 
+/* Streaming state of one slot in this decoder's own layout, for installing a warm state
+ * (Executor.apply_c2w_warm_state, engine/backend/executor.py:715-757; the reference's state is
+ * the wrapper's 2*layers KV + 17 conv + 4 transposed-conv tensors,
+ * scripts/export/code2wav_streaming.py:159-193).  Part 0 is the attention window
+ * [layers][2 (k, v)][heads][window][head_dim] fp16 (frame f at window position f % window, its
+ * key RoPE-rotated at position f); parts 1..17 are the causal convolutions' left contexts in the
+ * reference's order (conv_state_0..16: [ctx rows][channels], the activated conv inputs); parts
+ * 18..21 the transposed convolutions' previous input row (one row of the block's activated
+ * input: this decoder keeps x(i-1) where the reference keeps the bias-free overlap tail
+ * W[:, :, s:] x(i-1)).  A part is `rows` rows of `row_elems` elements of `dtype` (0 bf16,
+ * 1 fp32, 2 fp16), the first `valid_elems` of a row real channels, the rest zero. */
+typedef struct qtts_c2w_state_part {
+    int32_t rows;
+    int32_t row_elems;
+    int32_t valid_elems;
+    int32_t dtype;
+} qtts_c2w_state_part;
+#define QTTS_C2W_STATE_PARTS 22
+/* Fills parts[0 .. QTTS_C2W_STATE_PARTS) (max_parts must be at least that). */
+int qtts_c2w_state_layout(const qtts_c2w* c, qtts_c2w_state_part* parts, int max_parts);
+/* Copy `bytes` (= the part's rows * row_elems * element size) from `src` (device, the part's
+ * layout, contiguous) into part `part` of `slot` (0 <= slot < max_slots); stream-ordered. */
+int qtts_c2w_write_state(qtts_c2w* c, int slot, int part, const void* src, size_t bytes, qtts_stream_t stream);
+/* Set the slot's frame counter (frames decoded so far: the next frame's RoPE position). */
+int qtts_c2w_set_frame(qtts_c2w* c, int slot, int frame, qtts_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

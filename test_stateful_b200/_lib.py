@@ -104,8 +104,15 @@ EXPORTS = [
     "qtts_philox_gumbel", "qtts_codec_sum",
     "qtts_engine_create", "qtts_engine_destroy", "qtts_engine_step",
     "qtts_c2w_create", "qtts_c2w_destroy", "qtts_c2w_reset", "qtts_c2w_step", "qtts_c2w_launches",
-    "qtts_c2w_set_background",
+    "qtts_c2w_set_background", "qtts_c2w_state_layout", "qtts_c2w_write_state", "qtts_c2w_set_frame",
 ]
+
+C2W_STATE_PARTS = 22
+
+
+class C2wStatePart(C.Structure):
+    """qtts_c2w_state_part: one part of a slot's code2wav state in the decoder's layout."""
+    _fields_ = [("rows", C.c_int32), ("row_elems", C.c_int32), ("valid_elems", C.c_int32), ("dtype", C.c_int32)]
 
 _lib = None
 
@@ -157,6 +164,9 @@ def load() -> C.CDLL:
         "qtts_c2w_step": ([P, P, C.c_int, C.c_int, P, C.c_int, P, P], C.c_int),
         "qtts_c2w_launches": ([P], C.c_int),
         "qtts_c2w_set_background": ([P, C.c_int], C.c_int),
+        "qtts_c2w_state_layout": ([P, C.POINTER(C2wStatePart), C.c_int], C.c_int),
+        "qtts_c2w_write_state": ([P, C.c_int, C.c_int, P, C.c_size_t, P], C.c_int),
+        "qtts_c2w_set_frame": ([P, C.c_int, C.c_int, P], C.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)

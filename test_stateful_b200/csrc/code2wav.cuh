@@ -828,4 +828,80 @@ inline int c2w_reset(qtts_c2w* c, const int32_t* slots, int n, cudaStream_t st) 
     return QTTS_OK;
 }
 
+// ---------------------------------------------------------------------------
+// warm state: the per-slot state in this decoder's layout (qtts_c2w_state_part)
+// ---------------------------------------------------------------------------
+constexpr int kC2wStateParts = 22;
+
+// valid channels of roll job j (the reference's state order: conv 0..16, transconv 0..3)
+inline int c2w_state_channels(const qtts_c2w* c, int j) {
+    const qtts_c2w_desc& d = c->d;
+    if (j == 0) return d.codebook_dim;
+    if (j <= 3) return d.latent;
+    if (j <= 15) return c->cout[(j - 4) / 3];
+    if (j == 16) return c->cout[3];
+    return c->cin[j - 17];
+}
+
+inline int c2w_state_layout(const qtts_c2w* c, qtts_c2w_state_part* parts, int max_parts) {
+    if (!parts || max_parts < kC2wStateParts || c->roll.n != kC2wStateParts - 1) {
+        set_error("c2w_state_layout: need room for %d parts", kC2wStateParts);
+        return QTTS_ERR_INVALID;
+    }
+    const qtts_c2w_desc& d = c->d;
+    parts[0].rows = d.layers * 2 * d.heads * d.window;
+    parts[0].row_elems = d.head_dim;
+    parts[0].valid_elems = d.head_dim;
+    parts[0].dtype = 2;
+    for (int j = 0; j < c->roll.n; ++j) {
+        const RollJob& r = c->roll.job[j];
+        const int esz = (j == 1 || j == 2) ? 4 : 2;  // the ConvNeXt inputs are kept in fp32
+        parts[1 + j].rows = r.ctx;
+        parts[1 + j].row_elems = r.row_bytes / esz;
+        parts[1 + j].valid_elems = c2w_state_channels(c, j);
+        parts[1 + j].dtype = esz == 4 ? 1 : 0;
+    }
+    return QTTS_OK;
+}
+
+__global__ void c2w_set_frame_kernel(int32_t* frame, int slot, int value) {
+    griddep_wait();
+    griddep_launch();
+    if (threadIdx.x == 0) frame[slot] = value;
+}
+
+inline int c2w_write_state(qtts_c2w* c, int slot, int part, const void* src, size_t bytes, cudaStream_t st) {
+    if (slot < 0 || slot >= c->S || part < 0 || part >= kC2wStateParts || !src) {
+        set_error("c2w_write_state: slot %d / part %d outside [0, %d) / [0, %d)", slot, part, c->S, kC2wStateParts);
+        return QTTS_ERR_INVALID;
+    }
+    const qtts_c2w_desc& d = c->d;
+    void* dst;
+    size_t want;
+    if (part == 0) {
+        want = (size_t)d.layers * 2 * d.heads * d.window * d.head_dim * sizeof(kv_t);
+        dst = c->ring + (size_t)slot * d.layers * 2 * d.heads * d.window * d.head_dim;
+    } else {
+        const RollJob& r = c->roll.job[part - 1];
+        want = (size_t)r.ctx * r.row_bytes;  // rows [0, ctx) of the slot's segment
+        dst = r.ptr + (size_t)slot * r.seq_rows * r.row_bytes;
+    }
+    if (bytes != want) {
+        set_error("c2w_write_state: part %d holds %zu bytes, got %zu", part, want, bytes);
+        return QTTS_ERR_INVALID;
+    }
+    QTTS_CHECK_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, st));
+    return QTTS_OK;
+}
+
+inline int c2w_set_frame(qtts_c2w* c, int slot, int frame, cudaStream_t st) {
+    if (slot < 0 || slot >= c->S || frame < 0 || frame >= c->d.max_frames) {
+        set_error("c2w_set_frame: slot %d / frame %d outside [0, %d) / [0, %d)", slot, frame, c->S,
+                  c->d.max_frames);
+        return QTTS_ERR_INVALID;
+    }
+    QTTS_LAUNCH(c2w_set_frame_kernel, dim3(1), dim3(32), 0, st, c->frame, slot, frame);
+    return QTTS_OK;
+}
+
 }  // namespace qtts

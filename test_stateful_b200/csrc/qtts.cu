@@ -349,6 +349,21 @@ int qtts_c2w_step(qtts_c2w* c, const int64_t* codes, int codes_ld, int frames, c
 
 int qtts_c2w_launches(const qtts_c2w* c) { return c ? c->launches : 0; }
 
+int qtts_c2w_state_layout(const qtts_c2w* c, qtts_c2w_state_part* parts, int max_parts) {
+    QTTS_REQUIRE(c, "c2w_state_layout: null decoder");
+    return c2w_state_layout(c, parts, max_parts);
+}
+
+int qtts_c2w_write_state(qtts_c2w* c, int slot, int part, const void* src, size_t bytes, qtts_stream_t stream) {
+    QTTS_REQUIRE(c, "c2w_write_state: null decoder");
+    return c2w_write_state(c, slot, part, src, bytes, (cudaStream_t)stream);
+}
+
+int qtts_c2w_set_frame(qtts_c2w* c, int slot, int frame, qtts_stream_t stream) {
+    QTTS_REQUIRE(c, "c2w_set_frame: null decoder");
+    return c2w_set_frame(c, slot, frame, (cudaStream_t)stream);
+}
+
 int qtts_c2w_set_background(qtts_c2w* c, int background) {
     QTTS_REQUIRE(c, "c2w_set_background: null decoder");
     c->background = background != 0;

@@ -26,7 +26,7 @@ Packing (all one-time, at load):
 from __future__ import annotations
 
 import ctypes as C
-from typing import Dict
+from typing import Dict, List
 
 import torch
 
@@ -176,6 +176,93 @@ def pack_code2wav(cfg: Code2WavConfig, W: Dict[str, torch.Tensor], device,
     return P
 
 
+_STATE_DTYPES = {0: torch.bfloat16, 1: torch.float32, 2: torch.float16}
+
+
+def expected_state_layout(cfg: Code2WavConfig, max_chunk: int = 1):
+    """The decoder's state parts (``qtts_c2w_state_layout``) computed on the host: the window
+    KV, then the causal convolutions' contexts (pre_conv, the two ConvNeXt depthwise inputs in
+    fp32, conv k7, 4 blocks x 3 residual units, the last conv) and the 4 transposed convs'
+    previous input rows; implicit-convolution buffers pad their channels to 64."""
+    parts = [(cfg.num_layers * 2 * cfg.num_heads * cfg.window, cfg.head_dim, cfg.head_dim, 2)]
+    parts.append((2, cfg.codebook_dim, cfg.codebook_dim, 0))
+    parts += [(6, cfg.latent_dim, cfg.latent_dim, 1)] * 2
+    parts.append((6, cfg.latent_dim, cfg.latent_dim, 0))
+    T, t_in, t_blk = 4, [], []
+    for r_ in cfg.upsample_rates:
+        t_in.append(T)
+        T *= r_
+        t_blk.append(T)
+    dims = cfg.block_dims()
+    for b, (cin, cout, _) in enumerate(dims):
+        cp = _p64(cout) if implicit_rows(t_blk[b], max_chunk) else cout
+        parts += [(6 * d, cp, cout, 0) for d in cfg.dilations]
+    parts.append((6, dims[-1][1], dims[-1][1], 0))
+    for b, (cin, _, _) in enumerate(dims):
+        parts.append((1, _p64(cin) if implicit_rows(t_in[b], max_chunk) else cin, cin, 0))
+    return parts
+
+
+def warm_state_parts(cfg: Code2WavConfig, packed: Dict[str, torch.Tensor], layout, c2w_kv, conv_states,
+                     transconv_states, frame_idx: int, device) -> List[torch.Tensor]:
+    """A warm decoder state in the reference's layout (``Executor.apply_c2w_warm_state``,
+    engine/backend/executor.py:715-757) as this decoder's state parts (``qtts_c2w_state_part``).
+
+    * ``c2w_kv`` [1, 2 * layers, heads, T, head_dim] (k, v of layer l at 2l, 2l + 1; keys
+      RoPE-rotated at their absolute frame): cropped to window - 1 past frames as the reference
+      does, frame ``frame_idx - T + i`` written at window position ``(frame_idx - T + i) % window``.
+    * ``conv_states[j]`` [1, channels, ctx] (the activated conv inputs,
+      code2wav_streaming.py:73-93): transposed to rows, channels zero-padded to the row.
+    * ``transconv_states[b]`` [1, C_out, s]: the reference keeps the bias-free overlap tail
+      ``tail[c, p] = sum_i W[i, c, s + p] x_prev[i]`` (code2wav_streaming.py:96-126); this
+      decoder keeps ``x_prev`` itself.  With C_out * s >= C_in the map is injective for a
+      full-rank W, so ``x_prev`` is its least-squares solution, using the packed x(i-1) tap of
+      the block's transposed-conv weights (rows (phase, out channel)).
+
+    Raises ``ValueError`` on any shape that does not match this decoder."""
+    dev = torch.device(device)
+    parts: List[torch.Tensor] = []
+    L, H, D, Wn = cfg.num_layers, cfg.num_heads, cfg.head_dim, cfg.window
+    kv = torch.as_tensor(c2w_kv).to(dev, torch.float32)
+    if kv.dim() == 5:
+        if kv.shape[0] != 1:
+            raise ValueError(f"c2w_kv batch {kv.shape[0]} != 1")
+        kv = kv[0]
+    if kv.dim() != 4 or tuple(kv.shape[:2]) != (2 * L, H) or kv.shape[3] != D:
+        raise ValueError(f"c2w_kv shape {tuple(kv.shape)} does not match [2*{L}, {H}, T, {D}]")
+    kv = kv[:, :, -max(1, Wn - 1):, :]
+    T = kv.shape[2]
+    ring = torch.zeros(2 * L, H, Wn, D, device=dev, dtype=torch.float32)
+    pos = (torch.arange(T, device=dev) + (int(frame_idx) - T)) % Wn
+    ring[:, :, pos, :] = kv
+    parts.append(ring.reshape(-1, D).to(torch.float16).contiguous())
+    if len(conv_states) != len(layout) - 1 - 4 or len(transconv_states) != 4:
+        raise ValueError(f"{len(conv_states)} conv / {len(transconv_states)} transconv states, expected "
+                         f"{len(layout) - 5} / 4")
+    for j, st in enumerate(conv_states):
+        rows, row_elems, valid, dt = layout[1 + j]
+        t = torch.as_tensor(st).to(dev, torch.float32)
+        t = t.reshape(t.shape[-2], t.shape[-1])  # [channels, ctx]
+        if tuple(t.shape) != (valid, rows):
+            raise ValueError(f"conv_state_{j} shape {tuple(t.shape)} != [{valid}, {rows}]")
+        part = torch.zeros(rows, row_elems, device=dev, dtype=torch.float32)
+        part[:, :valid] = t.t()
+        parts.append(part.to(_STATE_DTYPES[dt]).contiguous())
+    for b, (st, (cin, cout, s)) in enumerate(zip(transconv_states, cfg.block_dims())):
+        rows, row_elems, valid, dt = layout[1 + len(conv_states) + b]
+        tail = torch.as_tensor(st).to(dev, torch.float32)
+        tail = tail.reshape(tail.shape[-2], tail.shape[-1])  # [C_out, s]
+        if tuple(tail.shape) != (cout, s) or valid != cin or rows != 1:
+            raise ValueError(f"transconv_overlap_{b} shape {tuple(tail.shape)} != [{cout}, {s}]")
+        A = packed[f"blk_tw{b}"][: s * cout, :cin].to(torch.float32)  # tap x(i-1), rows (phase, c)
+        rhs = tail.t().reshape(-1, 1)
+        x_prev = torch.linalg.lstsq(A, rhs).solution[:, 0]
+        part = torch.zeros(1, row_elems, device=dev, dtype=torch.float32)
+        part[0, :cin] = x_prev
+        parts.append(part.to(_STATE_DTYPES[dt]).contiguous())
+    return parts
+
+
 class DeviceCode2Wav:
     """Packed weights + native decoder state for ``max_slots`` streams on one GPU."""
 
@@ -248,6 +335,29 @@ class DeviceCode2Wav:
         _lib.check(lib.qtts_c2w_step(self.handle, _lib.ptr(codes), ld, frames, _lib.ptr(slots), n,
                                      _lib.ptr(wav), _lib.stream_ptr(stream)), "c2w_step")
         self.last_launches = lib.qtts_c2w_launches(self.handle)
+
+    def state_layout(self):
+        """[(rows, row_elems, valid_elems, dtype)] of the 22 state parts (``qtts_c2w_state_layout``)."""
+        parts = (_lib.C2wStatePart * _lib.C2W_STATE_PARTS)()
+        _lib.check(_lib.load().qtts_c2w_state_layout(self.handle, parts, _lib.C2W_STATE_PARTS), "c2w_state_layout")
+        return [(p.rows, p.row_elems, p.valid_elems, p.dtype) for p in parts]
+
+    def install_state(self, slot: int, parts: List[torch.Tensor], frame: int, stream=None) -> None:
+        """Write a slot's state parts (``warm_state_parts``) and set its frame counter, ordered on
+        ``stream``."""
+        lib = _lib.load()
+        layout = self.state_layout()
+        if len(parts) != len(layout):
+            raise ValueError(f"{len(parts)} state parts, the decoder has {len(layout)}")
+        for i, (t, (rows, row_elems, _, dt)) in enumerate(zip(parts, layout)):
+            if (tuple(t.shape) != (rows, row_elems) or t.dtype != _STATE_DTYPES[dt] or not t.is_contiguous()
+                    or t.device != self.device):
+                raise ValueError(f"state part {i}: {tuple(t.shape)} {t.dtype} != ({rows}, {row_elems}) "
+                                 f"{_STATE_DTYPES[dt]} on {self.device}")
+            _lib.check(lib.qtts_c2w_write_state(self.handle, int(slot), i, t.data_ptr(), t.numel() * t.element_size(),
+                                                _lib.stream_ptr(stream)), "c2w_write_state")
+        _lib.check(lib.qtts_c2w_set_frame(self.handle, int(slot), int(frame), _lib.stream_ptr(stream)),
+                   "c2w_set_frame")
 
     def close(self) -> None:
         if self.handle:

@@ -39,7 +39,7 @@ import torch
 from .. import _lib
 from ..config import EngineConfig, PagedPoolConfig
 from ..weights import make_code2wav_weights, make_cp_weights, make_talker_weights
-from .code2wav import DeviceCode2Wav
+from .code2wav import DeviceCode2Wav, warm_state_parts
 from .model import DeviceModel
 from .pool import PagedKVCachePool, PagedPrefixKVCache, SlotState
 
@@ -189,6 +189,7 @@ class B200Executor:
         self._parity = 0
         self._done_a: List[Any] = [None, None]
         self._done_b: List[Any] = [None, None]
+        self._c2w_warm: Dict[int, Any] = {}  # slot -> session whose warm code2wav state is installed
 
     # -- properties the engine loop reads ---------------------------------
     @property
@@ -260,13 +261,36 @@ class B200Executor:
         return []
 
     def apply_c2w_warm_state(self, slot: SlotState, c2w_kv, conv_states, transconv_states, frame_idx: int) -> bool:
-        """executor.py:715-757.  A warm state in the reference's tensor layout is
-        not installed (this backend keeps the decoder state on the device in
-        its own layout); like the reference on a mismatched state, the call
-        returns False and the stream starts from zero state."""
-        if c2w_kv is not None:
-            logger.warning("Code2Wav warm state not applied on the b200 backend (slot=%d)", slot.slot_id)
-        return False
+        """executor.py:715-757: install a warmed code2wav state (the reference's tensors: 2 x layers
+        window KV as one [1, 2L, heads, T, head_dim] tensor, 17 conv states, 4 transposed-conv
+        overlap tails) before the slot's first target frame.  The tensors are converted to this
+        decoder's layout (``warm_state_parts``: the overlap tails back to the previous input row
+        by least squares) and written into the slot's device state, ordered on the code2wav
+        stream; the slot's next prefill then decodes its first frame from that state instead of
+        from zero.  Returns False (state not applied, as the reference does on a mismatch) for
+        missing tensors, wrong counts or shapes."""
+        if c2w_kv is None or conv_states is None or transconv_states is None or self._c2w is None:
+            return False
+        if len(conv_states) != 17 or len(transconv_states) != 4:
+            logger.warning("Skipping Code2Wav warm state: %d conv / %d transconv states (expected 17 / 4)",
+                           len(conv_states), len(transconv_states))
+            return False
+        cur = torch.cuda.current_stream(self._device)
+        try:
+            with torch.cuda.stream(cur):
+                parts = warm_state_parts(self._config.c2w, self._c2w.P, self._c2w.state_layout(), c2w_kv,
+                                         conv_states, transconv_states, int(frame_idx), self._device)
+        except ValueError as exc:
+            logger.warning("Skipping Code2Wav warm state (slot=%d): %s", slot.slot_id, exc)
+            return False
+        b = self._c2w_stream  # every code2wav call runs on this stream, in order
+        b.wait_stream(cur)
+        for t in parts:
+            t.record_stream(b)
+        self._c2w.install_state(slot.slot_id, parts, max(0, int(frame_idx)), stream=b)
+        slot.frame_idx = max(0, int(frame_idx))
+        self._c2w_warm[slot.slot_id] = slot.session_id
+        return True
 
     # -- per-slot device state --------------------------------------------
     def _alloc_state(self) -> None:
@@ -382,15 +406,18 @@ class B200Executor:
         _lib.check(int(self.status_host[0]), "prefill scheduler")
         slot.past_len += seq
 
-    def _first_frame_audio(self) -> Optional[bytes]:
-        """Code2wav of the frame a prefill sampled, from zero decoder state
-        (the fused prefill runs code2wav on it: executor.py:859-877)."""
+    def _first_frame_audio(self, slot: SlotState) -> Optional[bytes]:
+        """Code2wav of the frame a prefill sampled (the fused prefill runs code2wav on it:
+        executor.py:859-877), from zero decoder state — or from the warm state
+        ``apply_c2w_warm_state`` installed for this session."""
         if self._c2w is None:
             return None
+        warm = self._c2w_warm.pop(slot.slot_id, None)
         cs = self._c2w_stream  # every code2wav call runs on this stream, in order
         cs.wait_stream(self._stream)
         with torch.cuda.stream(cs):
-            self._c2w.reset(self.slots_dev[:1], stream=cs)
+            if warm is None or warm != slot.session_id:
+                self._c2w.reset(self.slots_dev[:1], stream=cs)
             self._c2w.step(self.codes, self.slots_dev, self.wav, n=1, stream=cs)
             self.wav_host[:1].copy_(self.wav[:1], non_blocking=True)
         cs.synchronize()
@@ -406,7 +433,7 @@ class B200Executor:
         slot.position_offset = 0
         slot.frame_idx += 1
         slot.next_embed = self._own_next[slot.slot_id]
-        audio = self._first_frame_audio()
+        audio = self._first_frame_audio(slot)
         codes = self.codes[:1].cpu()
         return audio, bool(int(codes[0, 0]) == self._config.talker.codec_eos_id)
 
@@ -435,7 +462,7 @@ class B200Executor:
         slot.position_offset = 0
         slot.frame_idx += 1
         slot.next_embed = self._own_next[slot.slot_id]
-        audio = self._first_frame_audio()
+        audio = self._first_frame_audio(slot)
         codes = self.codes[:1].cpu()
         yield audio, bool(int(codes[0, 0]) == self._config.talker.codec_eos_id)
 
@@ -462,7 +489,7 @@ class B200Executor:
         self._prefill_call(slot, request_prefill_embeds, sample=1)
         slot.frame_idx += 1
         slot.next_embed = self._own_next[slot.slot_id]
-        audio = self._first_frame_audio()
+        audio = self._first_frame_audio(slot)
         codes = self.codes[:1].cpu()
         return audio, bool(int(codes[0, 0]) == self._config.talker.codec_eos_id)
 

@@ -705,6 +705,55 @@ def make_code2wav_chunked(ref: Path, out, seed=6, chunks=(25, 25, 25, 7), start1
                         wav0=np.concatenate(wav[0]).astype(np.float16), wav1=np.concatenate(wav[1]).astype(np.float16))
 
 
+def make_code2wav_warm(ref: Path, out, seed=7, warm=80, cont=10):
+    """A warm state as the reference hands it to ``Executor.apply_c2w_warm_state``
+    (engine/backend/executor.py:715-757): one stream decoded frame by frame through the wrapper
+    for ``warm`` frames from zero state (past KV kept at window - 1 frames, as the executor
+    crops it), its state recorded — KV [1, 2L, H, T, hd], the 17 conv states, the 4 transposed-
+    conv overlap tails, the frame index — then ``cont`` more frames decoded from it (their audio
+    is what a backend given that state must reproduce)."""
+    sys.path.insert(0, str(ref / "scripts" / "export"))
+    import code2wav_streaming as c2ws
+    from test_stateful_b200.config import tiny_code2wav_config
+    c = tiny_code2wav_config()
+    W = wmod.to_fp32(wmod.make_code2wav_weights(c, seed))
+    dec = build_code2wav_standin(c, W)
+    wrap = c2ws.Code2WavStreamingWrapper(dec, window_size=c.window, emit_delta_kv=True).eval()
+    shapes = c2ws.get_initial_state_shapes(dec, batch_size=1)
+    conv = [torch.zeros(s) for n, s in shapes if n.startswith("conv_state")]
+    trans = [torch.zeros(s) for n, s in shapes if n.startswith("transconv")]
+    L2 = 2 * c.num_layers
+    g = torch.Generator().manual_seed(seed)
+    codes = torch.randint(0, c.codebook_size, (warm + cont, c.num_codebooks), generator=g)
+    kv = None
+    max_past = c.window - 1
+    rec = None
+    wav = []
+    with torch.no_grad():
+        for t in range(warm + cont):
+            if t == warm:
+                rec = (kv.clone(), [x.clone() for x in conv], [x.clone() for x in trans], t)
+            sl = 0 if kv is None else kv.shape[3]
+            P = max(1, sl)
+            bias = torch.zeros(1, 1, 1, P + 1)
+            bias[:, :, :, :P - sl] = float("-inf")
+            k = kv if kv is not None else torch.zeros(1, L2, c.kv_heads, 0, c.head_dim)
+            past = nn.functional.pad(k, (0, 0, P - sl, 0))
+            states = [past[:, j] for j in range(L2)] + conv + trans
+            outs = wrap(codes[t].view(1, -1, 1), torch.tensor([[float(t)]]), bias, *states)
+            d = torch.stack(outs[1:1 + L2], dim=1)
+            kv = d if kv is None else torch.cat([kv, d], 3)[:, :, :, -max_past:]
+            conv = [x.clone() for x in outs[1 + L2:1 + L2 + len(conv)]]
+            trans = [x.clone() for x in outs[1 + L2 + len(conv):]]
+            if t >= warm:
+                wav.append(outs[0][0].numpy())
+    kv0, conv0, trans0, frame0 = rec
+    arrays = {f"conv_{j}": x.numpy() for j, x in enumerate(conv0)}
+    arrays.update({f"trans_{b}": x.numpy() for b, x in enumerate(trans0)})
+    np.savez_compressed(out, codes=codes.numpy().astype(np.int32), kv=kv0.numpy(), frame=np.int32(frame0),
+                        wav=np.stack(wav).astype(np.float32), seed=np.int64(seed), **arrays)
+
+
 def make_seeds(out):
     """Per-(session, segment) sampling seeds from engine/backend/executor.py:45-52."""
     from engine.backend import executor as ref_executor
@@ -739,9 +788,14 @@ def main():
     if args.only == "code2wav":
         make_code2wav(args.reference.resolve(), HERE / "code2wav_tiny.npz")
         make_code2wav_chunked(args.reference.resolve(), HERE / "code2wav_chunked_tiny.npz")
+        make_code2wav_warm(args.reference.resolve(), HERE / "code2wav_warm_tiny.npz")
+        return
+    if args.only == "code2wav_warm":
+        make_code2wav_warm(args.reference.resolve(), HERE / "code2wav_warm_tiny.npz")
         return
     make_code2wav(args.reference.resolve(), HERE / "code2wav_tiny.npz")
     make_code2wav_chunked(args.reference.resolve(), HERE / "code2wav_chunked_tiny.npz")
+    make_code2wav_warm(args.reference.resolve(), HERE / "code2wav_warm_tiny.npz")
     make_seeds(HERE / "seeds.npz")
     t0 = time.time()
     make_fused_tiny(ref_mods, HERE / "fused_tiny.npz")

@@ -86,3 +86,67 @@ def test_code2wav_oracle_matches_reference_chunked_stream():
         got = np.concatenate(out)
         assert got.shape == ref.shape
         np.testing.assert_allclose(got, ref.astype(np.float32), rtol=0, atol=1.5e-3)
+
+
+def _warm_fixture():
+    z = np.load(os.path.join(GOLDEN, "code2wav_warm_tiny.npz"))
+    conv = [torch.from_numpy(z[f"conv_{j}"]) for j in range(17)]
+    trans = [torch.from_numpy(z[f"trans_{b}"]) for b in range(4)]
+    return z, torch.from_numpy(z["kv"]), conv, trans, int(z["frame"])
+
+
+def test_code2wav_oracle_continues_reference_warm_state():
+    """``code2wav_warm_tiny.npz``: the wrapper's state after 80 frames (the warm state
+    ``Executor.apply_c2w_warm_state`` receives) and the 10 frames it decodes next.  The oracle,
+    started from that state, decodes the same 10 frames."""
+    z, kv, conv, trans, frame = _warm_fixture()
+    cfg = tiny_code2wav_config()
+    W = wmod.to_fp32(wmod.make_code2wav_weights(cfg, int(z["seed"])))
+    st = C.Code2WavState(cfg)
+    st.kv = [(kv[:, 2 * l], kv[:, 2 * l + 1]) for l in range(cfg.num_layers)]
+    st.conv = [x.clone() for x in conv]
+    st.trans = [x.clone() for x in trans]
+    st.frame = frame
+    codes = z["codes"]
+    for i in range(z["wav"].shape[0]):
+        w = C.decode_chunk(W, cfg, torch.from_numpy(codes[frame + i]).view(-1, 1), st).numpy()
+        np.testing.assert_allclose(w, z["wav"][i], rtol=0, atol=2e-5)
+
+
+def test_warm_state_conversion_to_decoder_layout():
+    """``warm_state_parts`` on the reference's warm state (CPU): every window frame lands at
+    position frame % window of its (layer, k/v, head) row; conv contexts become rows, zero
+    padded; each transposed conv's previous input row, recovered by least squares from the
+    bias-free overlap tail, reproduces that tail through the fp32 weights."""
+    from test_stateful_b200.runtime.code2wav import expected_state_layout, pack_code2wav, warm_state_parts
+
+    z, kv, conv, trans, frame = _warm_fixture()
+    cfg = tiny_code2wav_config()
+    Wd = wmod.make_code2wav_weights(cfg, int(z["seed"]))
+    W = wmod.to_fp32(Wd)
+    P = pack_code2wav(cfg, Wd, "cpu")
+    layout = expected_state_layout(cfg, 1)
+    parts = warm_state_parts(cfg, P, layout, kv, conv, trans, frame, "cpu")
+    assert [tuple(p.shape) for p in parts] == [(r, e) for r, e, _, _ in layout]
+    L, H, Wn, D = cfg.num_layers, cfg.num_heads, cfg.window, cfg.head_dim
+    ring = parts[0].float().view(2 * L, H, Wn, D)
+    T = kv.shape[3]
+    for i in (0, T // 2, T - 1):
+        f = frame - T + i
+        torch.testing.assert_close(ring[:, :, f % Wn], kv[0, :, :, i].to(torch.float16).float())
+    assert float(ring[:, :, frame % Wn].abs().max()) == 0.0  # the next frame's position is still free
+    for j in range(17):
+        rows, row_elems, valid, _ = layout[1 + j]
+        got = parts[1 + j].float()
+        ref = conv[j][0].t()
+        want = ref if parts[1 + j].dtype == torch.float32 else ref.to(torch.bfloat16).float()
+        torch.testing.assert_close(got[:, :valid], want)
+        if row_elems > valid:
+            assert float(got[:, valid:].abs().max()) == 0.0
+    for b, (cin, cout, s) in enumerate(cfg.block_dims()):
+        x = parts[18 + b].float()[0, :cin]
+        w = W[f"c2w.decoder.{1 + b}.transconv.weight"]  # [cin, cout, 2s]
+        tail = torch.einsum("i,icp->cp", x, w[:, :, s:])
+        ref = trans[b][0]
+        rel = float((tail - ref).abs().max() / ref.abs().max())
+        assert rel < 2e-2, (b, rel)  # bf16 packed weights, bf16 state row

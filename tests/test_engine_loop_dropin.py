@@ -151,7 +151,7 @@ class _CpuStandInExecutor(B200Executor):
             self._emit(2, 0, slot, embeds.reshape(seq, -1)[-1].float())
         slot.past_len += seq
 
-    def _first_frame_audio(self):
+    def _first_frame_audio(self, slot):
         return self.wav_host_buf[2][0].numpy().tobytes()
 
     def _apply_host_inputs(self, moved, fresh):

@@ -149,3 +149,73 @@ def test_code2wav_parity_with_persistent_conv_gemm():
     r = subprocess.run([sys.executable, "-m", "pytest", "-x", "-q", "-m", "gpu", "-p", "no:cacheprovider",
                         os.path.abspath(__file__)], env=env, capture_output=True, text=True, timeout=900)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
+
+
+def test_code2wav_warm_state_through_executor_matches_reference():
+    """``apply_c2w_warm_state`` with the reference wrapper's state after 80 frames
+    (``code2wav_warm_tiny.npz``: window KV, 17 conv states, 4 transposed-conv overlap tails):
+    the next 10 frames decoded on that slot match the wrapper's own continuation; the
+    library's state layout is the one the host computes; a mismatched state is refused; and the
+    slot's next prefill decodes its first frame from the installed state (no reset)."""
+    from test_stateful_b200.config import tiny_engine_config
+    from test_stateful_b200.runtime.code2wav import expected_state_layout
+    from test_stateful_b200.runtime.executor import B200Executor
+
+    z = np.load(os.path.join(GOLDEN, "code2wav_warm_tiny.npz"))
+    cfg = tiny_engine_config()
+    seed = int(z["seed"])
+    Wt = wmod.make_talker_weights(cfg.talker, 2)
+    Wt.update(wmod.make_cp_weights(cfg.cp, 2))
+    ex = B200Executor(max_batch_size=4, max_seq_len=160, model_config=cfg, do_sample=False, random_seed=1,
+                      num_blocks=64, weights=Wt, c2w_weights=wmod.make_code2wav_weights(cfg.c2w, seed),
+                      max_prefill_rows=64)
+    ex.load()
+    try:
+        assert ex._c2w.state_layout() == expected_state_layout(cfg.c2w, ex._c2w.max_chunk)
+        kv = torch.from_numpy(z["kv"])
+        conv = [torch.from_numpy(z[f"conv_{j}"]) for j in range(17)]
+        trans = [torch.from_numpy(z[f"trans_{b}"]) for b in range(4)]
+        frame = int(z["frame"])
+        pool = ex.kv_pool
+        slot = pool.allocate("warm")
+        assert not ex.apply_c2w_warm_state(slot, kv, conv[:16], trans, frame)  # wrong count: refused
+        assert not ex.apply_c2w_warm_state(slot, kv[:, :, :2], conv, trans, frame)  # wrong KV heads
+        assert ex.apply_c2w_warm_state(slot, kv, conv, trans, frame)
+        assert slot.frame_idx == frame
+        codes, ref = z["codes"], z["wav"]
+        slots = torch.tensor([slot.slot_id], dtype=torch.int32, device=DEV)
+        out = np.zeros_like(ref)
+        b = ex._c2w_stream
+        with torch.cuda.stream(b):
+            for i in range(ref.shape[0]):
+                cds = torch.from_numpy(codes[frame + i]).long().view(1, -1).to(DEV)
+                wav = torch.empty(1, cfg.c2w.samples_per_frame, device=DEV)
+                ex._c2w.step(cds, slots, wav, stream=b)
+                out[i] = wav.cpu().numpy()
+        torch.cuda.synchronize()
+        assert _lib.device_error() == 0
+        s = snr_db(ref, out)
+        print(f"code2wav from the reference's warm state: SNR {s:.1f} dB over {ref.shape[0]} frames")
+        assert s >= SNR_DB, s
+
+        # the prefill of a warm slot keeps the installed state: its first frame differs from the
+        # same prefill on a cold slot (same session, same sampled codes)
+        g = torch.Generator().manual_seed(4)
+        emb = (torch.randn(1, 12, cfg.talker.hidden_size, generator=g) * 0.02).to(DEV)
+        pool.release(slot.slot_id)
+        cold = pool.allocate("s")
+        audio_cold, _ = ex.prefill(cold, emb)
+        codes_cold = ex.codes[0].cpu().clone()
+        pool.release(cold.slot_id)
+        warm = pool.allocate("s")
+        assert ex.apply_c2w_warm_state(warm, kv, conv, trans, frame)
+        audio_warm, _ = ex.prefill(warm, emb)
+        assert torch.equal(ex.codes[0].cpu(), codes_cold)
+        assert warm.slot_id not in ex._c2w_warm  # consumed by the prefill
+        a = np.frombuffer(audio_cold, np.float32)
+        w = np.frombuffer(audio_warm, np.float32)
+        assert float(np.abs(a - w).max()) > 1e-4
+        pool.release(warm.slot_id)
+    finally:
+        ex._graphs.clear()
+        ex.shutdown()
