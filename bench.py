@@ -232,7 +232,9 @@ def attention_roofline(ex, slots, peaks):
     unique = sum(keys_in_block.values()) * per_key + qo_bytes
     gbs = algo / sec / 1e9
     peak = peaks.get("hbm_gbs")
-    return {"kernel": "paged_attn_tc_kernel + attn_combine_kernel", "bound": "hbm", "achieved": round(gbs, 1),
+    kernel = ("paged_attn_tc_row_kernel (one CTA per row and kv head)" if os.environ.get("QTTS_ATTN_ROWS", "1") != "0"
+              else "paged_attn_tc_kernel + attn_combine_kernel")
+    return {"kernel": kernel, "bound": "hbm", "achieved": round(gbs, 1),
             "peak": peak, "unit": "GB/s", "frac": round(gbs / peak, 3) if peak else None,
             "traffic": int(unique * ATTN_TRAFFIC_PER_UNIQUE),
             "traffic_source": "ncu dram__bytes_read+write per launch over unique KV bytes, scaled to this launch",

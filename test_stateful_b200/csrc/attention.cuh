@@ -624,6 +624,270 @@ inline int make_kv_map(CUtensorMap* map, const AttnParams& p) {
     return QTTS_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Decode attention without split partials: one CTA per (row, kv head); its W warps take the
+// row's KV blocks w, w + W, w + 2W, ... (each with its own TMA ring, the math of
+// paged_attn_tc_kernel), and the W partial softmax states (max, sum, unnormalised O) are
+// folded in shared memory into the final output.  No workspace and no combine launch.
+// ---------------------------------------------------------------------------
+template <int S, int W>
+struct AttnRowLayout {
+    static constexpr int RING = W * S * kTcStage;
+    static constexpr int COMB = W * (4 + 2 * 128) * 4;  // per warp: m0 m1 l0 l1, O [2 heads][128]
+    static constexpr int SMEM = 1024 + RING + COMB + W * S * 8;
+};
+
+template <int S, int W>
+__global__ void __launch_bounds__(W * 32) paged_attn_tc_row_kernel(const __grid_constant__ CUtensorMap tmKV,
+                                                                   const AttnParams p) {
+    constexpr int D = 128;
+    using L = AttnRowLayout<S, W>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    float* comb = reinterpret_cast<float*>(smem + L::RING);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::RING + L::COMB);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int gq = lane >> 2, qq = lane & 3;  // mma fragment coordinates
+    griddep_wait();
+    griddep_launch();
+    const int g = blockIdx.x % p.kv_heads;  // CTA-uniform
+    const int r = blockIdx.x / p.kv_heads;
+    if (r >= p.R) return;
+    const int ctx = p.row_ctx[r];
+    const int nbt = (ctx + 15) >> 4;
+    const size_t hrow0 = (size_t)r * p.num_heads + g * 2;
+    const int slot = p.row_slot[r];
+    if (nbt <= 0 || slot < 0) {  // CTA-uniform: a row with no keys (only after a scheduler error)
+        for (int i = threadIdx.x; i < 2 * D; i += W * 32) {
+            p.out[hrow0 * D + i] = __float2bfloat16(0.f);
+            if (p.out_lo) p.out_lo[hrow0 * D + i] = __float2bfloat16(0.f);
+        }
+        return;
+    }
+    const int n_mine = warp < nbt ? (nbt - warp + W - 1) / W : 0;  // blocks warp, warp + W, ...
+
+    // Q^T fragments (B operand): lane (gq, qq) holds head gq's dims 16s + 2qq (+1) and +8 (+9)
+    uint32_t qh[8][2], ql[8][2];
+    {
+        const float* qb = p.q + (hrow0 + (gq < 2 ? gq : 0)) * D;
+#pragma unroll
+        for (int s2 = 0; s2 < 8; ++s2) {
+            const int d0 = 16 * s2 + 2 * qq;
+            float v[4] = {0.f, 0.f, 0.f, 0.f};
+            if (gq < 2) {
+                v[0] = qb[d0] * p.scale_log2;
+                v[1] = qb[d0 + 1] * p.scale_log2;
+                v[2] = qb[d0 + 8] * p.scale_log2;
+                v[3] = qb[d0 + 9] * p.scale_log2;
+            }
+            split_h2(v[0], v[1], qh[s2][0], ql[s2][0]);
+            split_h2(v[2], v[3], qh[s2][1], ql[s2][1]);
+        }
+    }
+
+    uint8_t* wbuf = smem + warp * S * kTcStage;
+    uint64_t* wbar = bars + warp * S;
+    if (lane == 0) {
+        for (int s2 = 0; s2 < S; ++s2) mbar_init(&wbar[s2], 1);
+        tma_prefetch_desc(&tmKV);
+        fence_mbar_init();
+    }
+    __syncwarp();
+
+    auto issue = [&](int i) {
+        const int jb = warp + W * i;
+        const int s2 = i % S;
+        int blk = jb < p.mbps ? p.block_table[(size_t)slot * p.mbps + jb] : -1;
+        if (blk < 0 || blk >= p.num_blocks) {
+            record_error(DEV_ERR_ATTN_WAIT);
+            blk = 0;  // stay in bounds; the error word reports the bad table entry
+        }
+        const int krow = (((blk * p.num_layers + p.layer) * 2 + 0) * p.kv_heads + g) * 16;
+        const int vrow = krow + p.kv_heads * 16;
+        uint8_t* dst = wbuf + s2 * kTcStage;
+        mbar_arrive_expect_tx(&wbar[s2], kTcStage);
+        tma_load_2d(dst, &tmKV, &wbar[s2], 0, krow);
+        tma_load_2d(dst + kTcBox, &tmKV, &wbar[s2], 64, krow);
+        tma_load_2d(dst + 2 * kTcBox, &tmKV, &wbar[s2], 0, vrow);
+        tma_load_2d(dst + 3 * kTcBox, &tmKV, &wbar[s2], 64, vrow);
+    };
+
+    int issued = 0;
+    if (lane == 0) {
+        for (int i = 0; i < n_mine && i < S; ++i) issue(i);
+        issued = min(n_mine, S);
+    }
+    issued = __shfl_sync(0xffffffffu, issued, 0);
+
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    float o[8][4];
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+
+    const int mi = lane >> 3, rr = lane & 7;
+    const int k_tok = (mi & 1) * 8 + rr, k_dim = (mi >> 1) * 8;  // K as the A operand (rows = tokens)
+    const int v_tok = (mi >> 1) * 8 + rr, v_dim = (mi & 1) * 8;  // V^T as the A operand (transposed load)
+
+    int done = 0;
+    bool failed = false;
+    for (int i = 0; i < n_mine; ++i) {
+        const int s2 = i % S;
+        if (!mbar_wait(&wbar[s2], (uint32_t)(i / S) & 1u, DEV_ERR_ATTN_WAIT)) {
+            failed = true;
+            break;
+        }
+        const uint32_t kb = smem_u32(wbuf + s2 * kTcStage);
+        const uint32_t vb = kb + 2 * kTcBox;
+        const int jb = warp + W * i;
+
+        float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+            uint32_t a[4];
+            ldsm_x4(tc_sw128(kb, k_tok, 16 * ks + k_dim), a);
+            mma_16816(sc, a, qh[ks][0], qh[ks][1]);
+            mma_16816(sc, a, ql[ks][0], ql[ks][1]);
+        }
+        const int tA = jb * 16 + gq, tB = tA + 8;
+        const float s00 = tA < ctx ? sc[0] : -INFINITY, s01 = tA < ctx ? sc[1] : -INFINITY;
+        const float s10 = tB < ctx ? sc[2] : -INFINITY, s11 = tB < ctx ? sc[3] : -INFINITY;
+        float bm0 = fmaxf(s00, s10), bm1 = fmaxf(s01, s11);
+#pragma unroll
+        for (int off = 4; off <= 16; off <<= 1) {
+            bm0 = fmaxf(bm0, __shfl_xor_sync(0xffffffffu, bm0, off));
+            bm1 = fmaxf(bm1, __shfl_xor_sync(0xffffffffu, bm1, off));
+        }
+        const float mn0 = fmaxf(m0, bm0), mn1 = fmaxf(m1, bm1);
+        float a0 = m0 == -INFINITY ? 0.f : exp2f(m0 - mn0);
+        float a1 = m1 == -INFINITY ? 0.f : exp2f(m1 - mn1);
+        const float p00 = s00 == -INFINITY ? 0.f : exp2f(s00 - mn0);
+        const float p01 = s01 == -INFINITY ? 0.f : exp2f(s01 - mn1);
+        const float p10 = s10 == -INFINITY ? 0.f : exp2f(s10 - mn0);
+        const float p11 = s11 == -INFINITY ? 0.f : exp2f(s11 - mn1);
+        float ps0 = p00 + p10, ps1 = p01 + p11;
+#pragma unroll
+        for (int off = 4; off <= 16; off <<= 1) {
+            ps0 += __shfl_xor_sync(0xffffffffu, ps0, off);
+            ps1 += __shfl_xor_sync(0xffffffffu, ps1, off);
+        }
+        l0 = l0 * a0 + ps0;
+        l1 = l1 * a1 + ps1;
+        m0 = mn0;
+        m1 = mn1;
+        if (qq != 0) a0 = a1 = 0.f;  // these lanes' O^T columns are padding heads (kept at zero)
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+            o[mt][0] *= a0;
+            o[mt][1] *= a1;
+            o[mt][2] *= a0;
+            o[mt][3] *= a1;
+        }
+        const int src1 = 8 * qq, src2 = 8 * qq + 4;
+        const float x0 = __shfl_sync(0xffffffffu, p00, src1), x1 = __shfl_sync(0xffffffffu, p01, src1);
+        const float y0 = __shfl_sync(0xffffffffu, p00, src2), y1 = __shfl_sync(0xffffffffu, p01, src2);
+        const float z0 = __shfl_sync(0xffffffffu, p10, src1), z1 = __shfl_sync(0xffffffffu, p11, src1);
+        const float w0 = __shfl_sync(0xffffffffu, p10, src2), w1 = __shfl_sync(0xffffffffu, p11, src2);
+        float pa = 0.f, pb = 0.f, pc = 0.f, pd = 0.f;
+        if (gq == 0) {
+            pa = x0; pb = y0; pc = z0; pd = w0;
+        } else if (gq == 1) {
+            pa = x1; pb = y1; pc = z1; pd = w1;
+        }
+        uint32_t bh0, bl0, bh1, bl1;
+        split_h2(pa, pb, bh0, bl0);
+        split_h2(pc, pd, bh1, bl1);
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+            uint32_t a[4];
+            ldsm_x4_t(tc_sw128(vb, v_tok, 16 * mt + v_dim), a);
+            mma_16816(o[mt], a, bh0, bh1);
+            mma_16816(o[mt], a, bl0, bl1);
+        }
+        ++done;
+        __syncwarp();
+        if (lane == 0 && i + S < n_mine) {
+            fence_proxy_async_smem();
+            issue(i + S);
+            ++issued;
+        }
+        issued = __shfl_sync(0xffffffffu, issued, 0);
+    }
+    if (failed && lane == 0) {
+        for (int i = done; i < issued; ++i) mbar_wait(&wbar[i % S], (uint32_t)(i / S) & 1u, DEV_ERR_DRAIN);
+    }
+
+    // ---- this warp's partial state into shared memory; lanes with qq == 0 hold
+    // O^T[dims 16 mt + gq (+8)][heads 0, 1]
+    float* cw = comb + warp * (4 + 2 * D);
+    if (lane == 0) {
+        cw[0] = failed ? -INFINITY : m0;
+        cw[1] = failed ? -INFINITY : m1;
+        cw[2] = l0;
+        cw[3] = l1;
+    }
+    if (qq == 0) {
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int h = e & 1, d = 16 * mt + gq + (e >> 1) * 8;
+                cw[4 + h * D + d] = o[mt][e];
+            }
+        }
+    }
+    __syncthreads();
+    // ---- fold the W partial states (fixed order): out = Σ o_w 2^(m_w - M) / Σ l_w 2^(m_w - M)
+    for (int t = threadIdx.x; t < 2 * D; t += W * 32) {
+        const int h = t / D, d = t - h * D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < W; ++w) M = fmaxf(M, comb[w * (4 + 2 * D) + h]);
+        float num = 0.f, den = 0.f;
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < W; ++w) {
+                const float* cv = comb + w * (4 + 2 * D);
+                const float mw = cv[h];
+                if (mw == -INFINITY) continue;
+                const float sc = exp2f(mw - M);
+                num += cv[4 + h * D + d] * sc;
+                den += cv[2 + h] * sc;
+            }
+        }
+        const float ov = den > 0.f ? num / den : 0.f;
+        const __nv_bfloat16 hi = __float2bfloat16(ov);
+        p.out[(hrow0 + h) * D + d] = hi;
+        if (p.out_lo) p.out_lo[(hrow0 + h) * D + d] = __float2bfloat16(ov - __bfloat162float(hi));
+    }
+}
+
+template <int S>
+inline int launch_attention_tc_rows(const AttnParams& p, cudaStream_t st) {
+    constexpr int W = 4;
+    using L = AttnRowLayout<S, W>;
+    CUtensorMap map;
+    const int rc = make_kv_map(&map, p);
+    if (rc) return rc;
+    auto kern = paged_attn_tc_row_kernel<S, W>;
+    QTTS_CHECK_CUDA((func_attr_once<paged_attn_tc_row_kernel<S, W>>(L::SMEM)));
+    QTTS_LAUNCH(kern, dim3(p.R * p.kv_heads), dim3(W * 32), L::SMEM, st, map, p);
+    return QTTS_OK;
+}
+
+// head_dim 128 decode attention as one CTA per (row, kv head), no split partials or combine
+// launch (QTTS_ATTN_ROWS=0: the split form, paged_attn_tc_kernel + attn_combine_kernel).
+// Measured per layer, 64 rows: 14.95 vs 17.0 us at mean context 247 (the benchmark's start),
+// 23.0 vs 26.5 us at 346 without prefix sharing, equal (18.85 vs 18.82 us) at the benchmark's
+// context 346 with its shared prefix, where the longest rows' warps set the time.
+inline bool attn_rows() {
+    static const bool on = [] {
+        const char* v = getenv("QTTS_ATTN_ROWS");
+        return !(v && *v == '0');
+    }();
+    return on;
+}
+
 // Fold split partials: out = Σ_s o_s 2^(m_s - M) / Σ_s l_s 2^(m_s - M), bf16.
 template <int D>
 __global__ void attn_combine_kernel(const AttnParams p) {
@@ -1132,6 +1396,8 @@ inline bool attn_use_tc() {
 template <int D>
 inline int launch_attention_d(const AttnParams& p, cudaStream_t st) {
     int rc;
+    if (D == 128 && attn_use_tc() && attn_rows())
+        return attn_stages() == 3 ? launch_attention_tc_rows<3>(p, st) : launch_attention_tc_rows<2>(p, st);
     if (D == 128 && attn_use_tc()) {
         rc = attn_stages() == 3 ? launch_attention_tc<3>(p, st) : launch_attention_tc<2>(p, st);
         if (rc) return rc;

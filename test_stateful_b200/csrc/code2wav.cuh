@@ -419,6 +419,7 @@ struct qtts_c2w {
     __nv_bfloat16* X2[4] = {};
     qtts::RollTable roll;
     std::vector<void*> allocs;
+    std::vector<std::pair<const void*, size_t>> alloc_bytes;  // usable bytes of each allocation
     qtts::GemmPlan pre_conv, in_proj, out_proj, conv0;
     std::vector<qtts::LayerGemms> layer;
     qtts::GemmPlan up_t[2], pw1[2], pw2[2], blk_t[4], c1[4][3], c2[4][3];
@@ -433,12 +434,24 @@ inline int c2w_alloc(qtts_c2w* c, T** p, size_t count) {
     QTTS_CHECK_CUDA(cudaMalloc(&ptr, count * sizeof(T) + 256));
     QTTS_CHECK_CUDA(cudaMemset(ptr, 0, count * sizeof(T) + 256));
     c->allocs.push_back(ptr);
+    c->alloc_bytes.emplace_back(ptr, count * sizeof(T));
     *p = reinterpret_cast<T*>(ptr);
     return QTTS_OK;
 }
 
-inline ActView view_slot(void* p, int ctx, int T, int ld) { return ActView{p, 1, ctx + T, ctx, ld}; }
-inline ActView view_rows(void* p, int T, int ld) { return ActView{p, 0, T, 0, ld}; }
+// bytes of the decoder allocation `p` starts (0 when p is not one of them: not checked)
+inline unsigned long long c2w_bytes(const qtts_c2w* c, const void* p) {
+    for (const auto& a : c->alloc_bytes)
+        if (a.first == p) return a.second;
+    return 0;
+}
+
+inline ActView view_slot(const qtts_c2w* c, void* p, int ctx, int T, int ld) {
+    return ActView{p, 1, ctx + T, ctx, ld, c2w_bytes(c, p)};
+}
+inline ActView view_rows(const qtts_c2w* c, void* p, int T, int ld) {
+    return ActView{p, 0, T, 0, ld, c2w_bytes(c, p)};
+}
 
 // Whether a convolution whose input has T rows per frame reads its operand straight from the
 // history buffer (implicit convolution).  A GEMM row tile must not span two streams, so a
@@ -624,7 +637,7 @@ inline int c2w_build(qtts_c2w* c) {
                            QTTS_EPI_QKV_ROPE, c->qbuf, nullptr, &q, c->xn_lo));
         ConvEpi eo = conv_epi(c, 1, 1, HID, HID);
         eo.scale = bf(d.attn_scale, (size_t)l * HID);
-        eo.res = view_rows(c->x, 1, HID);
+        eo.res = view_rows(c, c->x, 1, HID);
         eo.out32 = eo.res;
         QTTS_TRY(conv_plan(&g.o, c->attn, SF, HID, bf(d.w_o, (size_t)l * HID * HID), HID, nullptr, eo, c->attn_lo));
         QTTS_TRY(gemm_plan(&g.gu, c->xn, SF, HID, bf(d.w_gate_up, (size_t)l * 2 * I * HID), 2 * I, QTTS_EPI_SWIGLU,
@@ -639,16 +652,16 @@ inline int c2w_build(qtts_c2w* c) {
     for (int i = 0; i < 2; ++i) {
         const int Tin = i == 0 ? 1 : 2, To = c->T_up[i];
         ConvEpi et = conv_epi(c, Tin, 2, LAT, 2 * LAT);
-        et.out32 = view_slot(c->H_dw[i], 6, Fm * To, LAT);
+        et.out32 = view_slot(c, c->H_dw[i], 6, Fm * To, LAT);
         QTTS_TRY(conv_plan(&c->up_t[i], i == 0 ? c->U0 : c->U1, SF * Tin, LAT, d.up_w[i], 2 * LAT, d.up_b[i], et));
         ConvEpi e1 = conv_epi(c, 1, 1, CN, CN);
         e1.act = ACT_GELU;
-        e1.out16 = view_rows(c->Xg, 1, CN);
+        e1.out16 = view_rows(c, c->Xg, 1, CN);
         QTTS_TRY(conv_plan(&c->pw1[i], c->Xln, SF * To, LAT, d.pw1_w[i], CN, d.pw1_b[i], e1));
         ConvEpi e2 = conv_epi(c, To, 1, LAT, LAT);
         e2.scale = reinterpret_cast<const __nv_bfloat16*>(d.gamma[i]);
-        e2.res = view_slot(c->H_dw[i], 6, Fm * To, LAT);
-        e2.out16 = i == 0 ? view_rows(c->U1, 2, LAT) : view_slot(c->H_c0, 6, Fm * 4, LAT);
+        e2.res = view_slot(c, c->H_dw[i], 6, Fm * To, LAT);
+        e2.out16 = i == 0 ? view_rows(c, c->U1, 2, LAT) : view_slot(c, c->H_c0, 6, Fm * 4, LAT);
         QTTS_TRY(conv_plan(&c->pw2[i], c->Xg, SF * To, CN, d.pw2_w[i], LAT, d.pw2_b[i], e2));
     }
     // ---- decoder conv k7 (latent -> decoder_dim), then SnakeBeta of block 0 into its transconv input
@@ -656,16 +669,16 @@ inline int c2w_build(qtts_c2w* c) {
         ConvEpi e = conv_epi(c, 4, 1, D0, D0);
         e.act = ACT_SNAKE;
         e.act_p = d.blk_snake[0];
-        e.out16 = view_slot(c->H_tc[0], 1, Fm * 4, c->cinpad[0]);
+        e.out16 = view_slot(c, c->H_tc[0], 1, Fm * 4, c->cinpad[0]);
         QTTS_TRY(conv_plan(&c->conv0, c->Xa, SF * 4, c->K_c0, d.w_conv0, pad128(D0), d.b_conv0, e));
     }
     for (int b = 0; b < 4; ++b) {
         const int Tb = c->T_blk[b], co = c->cout[b], s = d.rates[b];
         ConvEpi et = conv_epi(c, c->T_in[b], s, co, s * co);
-        et.out32 = view_rows(c->h[b], Tb, co);
+        et.out32 = view_rows(c, c->h[b], Tb, co);
         et.act = ACT_SNAKE;
         et.act_p = d.res_act1[b][0];
-        et.out16 = view_slot(c->H_res[b][0], 6 * d.dilations[0], Fm * Tb, c->cpad[b]);
+        et.out16 = view_slot(c, c->H_res[b][0], 6 * d.dilations[0], Fm * Tb, c->cpad[b]);
         if (c->impl_tc[b])
             QTTS_TRY(gemm_plan_implicit(&c->blk_t[b], c->H_tc[b], S1 * (1 + Fm * c->T_in[b]), c->cinpad[b], 2, 1,
                                         c->T_in[b], 1 + Fm * c->T_in[b], SF * c->T_in[b], d.blk_tw[b], c->N_tc[b],
@@ -677,7 +690,7 @@ inline int c2w_build(qtts_c2w* c) {
             ConvEpi e1 = conv_epi(c, Tb, 1, co, co);
             e1.act = ACT_SNAKE;
             e1.act_p = d.res_act2[b][j];
-            e1.out16 = view_rows(c->X2[b], Tb, c->N_c[b]);
+            e1.out16 = view_rows(c, c->X2[b], Tb, c->N_c[b]);
             const int dil = d.dilations[j];
             if (c->impl_c1[b])
                 QTTS_TRY(gemm_plan_implicit(&c->c1[b][j], c->H_res[b][j], S1 * (6 * dil + Fm * Tb), c->cpad[b], 7,
@@ -687,18 +700,18 @@ inline int c2w_build(qtts_c2w* c) {
                 QTTS_TRY(conv_plan(&c->c1[b][j], c->Xa, SF * Tb, c->K_c1[b], d.res_w1[b][j], c->N_c[b],
                                    d.res_b1[b][j], e1));
             ConvEpi e2 = conv_epi(c, Tb, 1, co, co);
-            e2.res = view_rows(c->h[b], Tb, co);
+            e2.res = view_rows(c, c->h[b], Tb, co);
             e2.out32 = e2.res;
             e2.act = ACT_SNAKE;
             if (j < 2) {
                 e2.act_p = d.res_act1[b][j + 1];
-                e2.out16 = view_slot(c->H_res[b][j + 1], 6 * d.dilations[j + 1], Fm * Tb, c->cpad[b]);
+                e2.out16 = view_slot(c, c->H_res[b][j + 1], 6 * d.dilations[j + 1], Fm * Tb, c->cpad[b]);
             } else if (b < 3) {
                 e2.act_p = d.blk_snake[b + 1];
-                e2.out16 = view_slot(c->H_tc[b + 1], 1, Fm * Tb, c->cinpad[b + 1]);
+                e2.out16 = view_slot(c, c->H_tc[b + 1], 1, Fm * Tb, c->cinpad[b + 1]);
             } else {
                 e2.act_p = d.final_snake;
-                e2.out16 = view_slot(c->H_fin, 6, Fm * Tb, co);
+                e2.out16 = view_slot(c, c->H_fin, 6, Fm * Tb, co);
             }
             QTTS_TRY(conv_plan(&c->c2[b][j], c->X2[b], SF * Tb, c->N_c[b], d.res_w2[b][j], c->N_c[b],
                                d.res_b2[b][j], e2));
@@ -752,7 +765,7 @@ inline int c2w_step_impl(qtts_c2w* c, const int64_t* codes, int codes_ld, int F,
     const int LAT = d.latent, HID = d.hidden, NH = d.heads, HD = d.head_dim, CD = d.codebook_dim, L = d.layers;
     QTTS_LAUNCH(c2w_rvq_kernel, dim3(nF), dim3(256), 0, st, d.rvq_tables, d.num_codebooks, d.codebook_size, CD, codes,
                 codes_ld, F, slots_in, c->S, (const int32_t*)c->frame, d.window, d.max_frames, c->row_slot,
-                c->row_pos, c->row_kv, c->row_nkeys, c->row_lo, view_slot(c->H_pc, 2, Fm, CD));
+                c->row_pos, c->row_kv, c->row_nkeys, c->row_lo, view_slot(c, c->H_pc, 2, Fm, CD));
     const int32_t* slots = c->row_slot;  // validated slot of each stream
     QTTS_TRY(c2w_im2col(c, c->H_pc, 2, 2 + Fm, F, CD, 3, 1, c->K_pc, slots, n, st));
     QTTS_TRY(gemm_run(c->pre_conv, nF, st));

@@ -87,6 +87,7 @@ enum DeviceErr : int {
     DEV_ERR_SELFTEST_WAIT = 7,  // qtts_selftest_bounded_wait: the wait ran out, as the test intends
     DEV_ERR_ATTN_BOUNDS = 8,    // an attention kernel met a row / slot / index outside its buffers
     DEV_ERR_GRID_BARRIER = 9,   // a persistent kernel's grid barrier ran out of time
+    DEV_ERR_GEMM_BOUNDS = 10,   // a GEMM epilogue access would have left its buffer (skipped)
 };
 
 // Wall-clock limit of every device-side wait (ns).  A correct kernel waits

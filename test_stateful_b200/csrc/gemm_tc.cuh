@@ -46,7 +46,16 @@ namespace qtts {
 struct ActView {
     void* ptr;  // null: not used
     int by_slot, seq_rows, ctx, ld;
+    unsigned long long limit_bytes;  // bytes of the allocation behind ptr (0: not checked)
 };
+
+// Self-check of an epilogue access of `bytes` at element `idx` of a view of `esize`-byte elements:
+// false (and the device error recorded) when it would leave the view's allocation.
+__device__ __forceinline__ bool view_ok(const ActView& v, size_t idx, int esize, int bytes) {
+    if (v.limit_bytes == 0 || idx * (size_t)esize + (size_t)bytes <= v.limit_bytes) return true;
+    record_error(DEV_ERR_GEMM_BOUNDS);
+    return false;
+}
 
 __host__ __device__ __forceinline__ size_t view_index(const ActView& v, int r, int slot, int t, int c) {
     return ((size_t)(v.by_slot ? slot : r) * v.seq_rows + v.ctx + t) * v.ld + c;
@@ -440,9 +449,9 @@ __device__ void gemm_epilogue(const GemmParams& p, float* R, int m0, int per, in
 #pragma unroll
                     for (int u = 0; u < B; ++u) {
                         const int i = i0 + NTL * u;
-                        rv[u] = ok[u] ? *reinterpret_cast<const float4*>(
-                                            res + (size_t)(row_res[i] + ph) * e.res.ld + c0)
-                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+                        const size_t ri = (size_t)(row_res[i] + ph) * e.res.ld + c0;
+                        rv[u] = (ok[u] && view_ok(e.res, ri, 4, 16)) ? *reinterpret_cast<const float4*>(res + ri)
+                                                                       : make_float4(0.f, 0.f, 0.f, 0.f);
                     }
 #pragma unroll
                     for (int u = 0; u < B; ++u) {
@@ -456,7 +465,10 @@ __device__ void gemm_epilogue(const GemmParams& p, float* R, int m0, int per, in
                 for (int u = 0; u < B; ++u) {
                     if (!ok[u]) continue;
                     const int i = i0 + NTL * u;
-                    if (o32) *reinterpret_cast<float4*>(o32 + (size_t)(row_o32[i] + ph) * e.out32.ld + c0) = v[u];
+                    if (o32) {
+                        const size_t oi = (size_t)(row_o32[i] + ph) * e.out32.ld + c0;
+                        if (view_ok(e.out32, oi, 4, 16)) *reinterpret_cast<float4*>(o32 + oi) = v[u];
+                    }
                     if (o16) {
                         float a[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
 #pragma unroll
@@ -473,7 +485,8 @@ __device__ void gemm_epilogue(const GemmParams& p, float* R, int m0, int per, in
                         uint2 pack;
                         pack.x = *reinterpret_cast<const uint32_t*>(&h01);
                         pack.y = *reinterpret_cast<const uint32_t*>(&h23);
-                        *reinterpret_cast<uint2*>(o16 + (size_t)(row_o16[i] + ph) * e.out16.ld + c0) = pack;
+                        const size_t hi16 = (size_t)(row_o16[i] + ph) * e.out16.ld + c0;
+                        if (view_ok(e.out16, hi16, 2, 8)) *reinterpret_cast<uint2*>(o16 + hi16) = pack;
                     }
                 }
             }

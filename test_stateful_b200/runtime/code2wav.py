@@ -26,7 +26,7 @@ Packing (all one-time, at load):
 from __future__ import annotations
 
 import ctypes as C
-from typing import Dict, List
+from typing import Dict, List, Optional
 
 import torch
 
@@ -204,7 +204,7 @@ def expected_state_layout(cfg: Code2WavConfig, max_chunk: int = 1):
 
 
 def warm_state_parts(cfg: Code2WavConfig, packed: Dict[str, torch.Tensor], layout, c2w_kv, conv_states,
-                     transconv_states, frame_idx: int, device) -> List[torch.Tensor]:
+                     transconv_states, frame_idx: int, device, tail_qr: Optional[dict] = None) -> List[torch.Tensor]:
     """A warm decoder state in the reference's layout (``Executor.apply_c2w_warm_state``,
     engine/backend/executor.py:715-757) as this decoder's state parts (``qtts_c2w_state_part``).
 
@@ -219,8 +219,11 @@ def warm_state_parts(cfg: Code2WavConfig, packed: Dict[str, torch.Tensor], layou
       full-rank W, so ``x_prev`` is its least-squares solution, using the packed x(i-1) tap of
       the block's transposed-conv weights (rows (phase, out channel)).
 
-    Raises ``ValueError`` on any shape that does not match this decoder."""
-    dev = torch.device(device)
+    The conversion runs on the host (float64 QR of each tap, cached in ``tail_qr`` per block)
+    and the parts are moved to ``device`` at the end.  Raises ``ValueError`` on any shape that
+    does not match this decoder."""
+    out_dev = torch.device(device)
+    dev = torch.device("cpu")
     parts: List[torch.Tensor] = []
     L, H, D, Wn = cfg.num_layers, cfg.num_heads, cfg.head_dim, cfg.window
     kv = torch.as_tensor(c2w_kv).to(dev, torch.float32)
@@ -254,13 +257,19 @@ def warm_state_parts(cfg: Code2WavConfig, packed: Dict[str, torch.Tensor], layou
         tail = tail.reshape(tail.shape[-2], tail.shape[-1])  # [C_out, s]
         if tuple(tail.shape) != (cout, s) or valid != cin or rows != 1:
             raise ValueError(f"transconv_overlap_{b} shape {tuple(tail.shape)} != [{cout}, {s}]")
-        A = packed[f"blk_tw{b}"][: s * cout, :cin].to(torch.float32)  # tap x(i-1), rows (phase, c)
-        rhs = tail.t().reshape(-1, 1)
-        x_prev = torch.linalg.lstsq(A, rhs).solution[:, 0]
+        qr = tail_qr.get(b) if tail_qr is not None else None
+        if qr is None:  # tap x(i-1), rows (phase, c): A = Q R
+            A = packed[f"blk_tw{b}"][: s * cout, :cin].to("cpu", torch.float64)
+            qr = torch.linalg.qr(A)
+            if tail_qr is not None:
+                tail_qr[b] = qr
+        Q, R = qr
+        rhs = tail.t().reshape(-1, 1).to(torch.float64)
+        x_prev = torch.linalg.solve_triangular(R, Q.t() @ rhs, upper=True)[:, 0]
         part = torch.zeros(1, row_elems, device=dev, dtype=torch.float32)
-        part[0, :cin] = x_prev
+        part[0, :cin] = x_prev.to(torch.float32)
         parts.append(part.to(_STATE_DTYPES[dt]).contiguous())
-    return parts
+    return [t.to(out_dev).contiguous() for t in parts]
 
 
 class DeviceCode2Wav:
@@ -310,6 +319,7 @@ class DeviceCode2Wav:
         _lib.check(lib.qtts_c2w_create(C.byref(d), C.byref(h)), "c2w_create")
         self.handle = h
         self.last_launches = 0
+        self.tail_qr: dict = {}  # warm-state conversion: QR of each block's x(i-1) tap (host, float64)
 
     def set_background(self, on: bool = True) -> None:
         """Mark the decoder as running beside a latency-critical stream (its kernels then launch

@@ -279,7 +279,8 @@ class B200Executor:
         try:
             with torch.cuda.stream(cur):
                 parts = warm_state_parts(self._config.c2w, self._c2w.P, self._c2w.state_layout(), c2w_kv,
-                                         conv_states, transconv_states, int(frame_idx), self._device)
+                                         conv_states, transconv_states, int(frame_idx), self._device,
+                                         tail_qr=self._c2w.tail_qr)
         except ValueError as exc:
             logger.warning("Skipping Code2Wav warm state (slot=%d): %s", slot.slot_id, exc)
             return False

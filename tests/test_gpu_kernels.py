@@ -372,6 +372,21 @@ def test_gemm_opt_in_variants(knob):
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
 
 
+@pytest.mark.skipif(os.environ.get("QTTS_ATTN_ROWS") is not None, reason="already a forced run")
+def test_attention_split_form():
+    """head_dim 128 decode attention runs one CTA per (row, kv head) by default; the split form
+    (paged_attn_tc_kernel + attn_combine_kernel) stays available (QTTS_ATTN_ROWS=0, read once per
+    process): rerun the attention tests in a child process with it."""
+    import subprocess
+    import sys
+
+    env = dict(os.environ, QTTS_ATTN_ROWS="0")
+    r = subprocess.run([sys.executable, "-m", "pytest", "-x", "-q", "-m", "gpu", "-p", "no:cacheprovider", "-k",
+                        "attention and not split_form", os.path.abspath(__file__)], env=env, capture_output=True,
+                       text=True, timeout=900)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
+
+
 # --------------------------------------------------------------------- bounded device waits
 def test_bounded_wait_runs_out_and_returns_a_status():
     """The failure path of every mbarrier wait in the library: a wait on a phase that nothing
