@@ -122,9 +122,14 @@ def bench_prefill_attention(streams: int, chunk: int, past: int, launches: int, 
     t_dec = timed(lambda l: ops.paged_attention(q, kv, l, table, row_slot, row_ctx, max_ctx, out=out, out_lo=out_lo,
                                                 split_blocks=split))
     unique = streams * ctx_end * 2 * 8 * 128 * 2 + R * 16 * 128 * (4 + 4)
-    return {"kernel": "paged_prefill_tc_kernel (8-query tiles)", "streams": streams, "chunk": chunk, "past": past,
+    # causal score + PV multiply-adds of every (query, head, visible key): 2 x 2 x D flops each
+    flops = streams * 16 * 4 * 128 * sum(past + t + 1 for t in range(chunk))
+    umma = os.environ.get("QTTS_PREFILL_UMMA") != "0"
+    kernel = "paged_prefill_umma_kernel (tcgen05, 64-query groups)" if umma else "paged_prefill_tc_kernel (8-query tiles)"
+    return {"kernel": kernel, "streams": streams, "chunk": chunk, "past": past,
             "split_blocks": split or 16, "launch_us": t_pre * 1e6, "unique_bytes": unique,
-            "achieved_unique_gbs": unique / t_pre / 1e9, "prefill_tokens_per_s": R / t_pre,
+            "achieved_unique_gbs": unique / t_pre / 1e9, "causal_tflops": flops / t_pre / 1e12,
+            "prefill_tokens_per_s": R / t_pre,
             "decode_kernel_same_rows_us": t_dec * 1e6, "speedup_vs_decode_rows": t_dec / t_pre}
 
 

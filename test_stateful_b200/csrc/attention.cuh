@@ -862,9 +862,17 @@ __global__ void __launch_bounds__(W * 32) paged_attn_tc_row_kernel(const __grid_
     }
 }
 
-template <int S>
-inline int launch_attention_tc_rows(const AttnParams& p, cudaStream_t st) {
-    constexpr int W = 4;
+// warps per (row, kv head) CTA of the row form (QTTS_ATTN_ROW_WARPS: 4 or 8)
+inline int attn_row_warps() {
+    static const int w = [] {
+        const char* v = getenv("QTTS_ATTN_ROW_WARPS");
+        return (v && atoi(v) == 8) ? 8 : 4;
+    }();
+    return w;
+}
+
+template <int S, int W>
+inline int launch_attention_tc_rows_w(const AttnParams& p, cudaStream_t st) {
     using L = AttnRowLayout<S, W>;
     CUtensorMap map;
     const int rc = make_kv_map(&map, p);
@@ -873,6 +881,11 @@ inline int launch_attention_tc_rows(const AttnParams& p, cudaStream_t st) {
     QTTS_CHECK_CUDA((func_attr_once<paged_attn_tc_row_kernel<S, W>>(L::SMEM)));
     QTTS_LAUNCH(kern, dim3(p.R * p.kv_heads), dim3(W * 32), L::SMEM, st, map, p);
     return QTTS_OK;
+}
+
+template <int S>
+inline int launch_attention_tc_rows(const AttnParams& p, cudaStream_t st) {
+    return attn_row_warps() == 8 ? launch_attention_tc_rows_w<S, 8>(p, st) : launch_attention_tc_rows_w<S, 4>(p, st);
 }
 
 // head_dim 128 decode attention as one CTA per (row, kv head), no split partials or combine
@@ -1361,6 +1374,362 @@ inline int launch_prefill_tc(const AttnParams& p, cudaStream_t st) {
     return QTTS_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Chunked prefill on the tcgen05 tensor pipe (head_dim 128, two query heads per KV head).
+// One CTA per (stream, kv head, group of 64 query rows): the group's 64 queries x 2 heads are
+// the 128 rows of the UMMA M side (row t = head * 64 + query), keys arrive in tiles of 64 (four
+// 16-token blocks, TMA with the 128-B swizzle, a 2-stage ring), and per tile
+//   S[128][64]  = Q · K^T           (TMEM columns 0..63; Q as an fp16 hi/lo pair: two passes)
+//   softmax     one thread per TMEM lane (= row): causal mask (keys < row_ctx), online max in
+//               the log2 domain; O is rescaled in TMEM only when the max grows by more than
+//               2^8 (P = 2^(s - m) stays below 256, exact enough in fp16)
+//   P -> shared memory as an fp16 hi/lo pair (K-major, swizzled), V -> V^T by ldmatrix.trans /
+//   stmatrix (so both PV operands are K-major)
+//   O[128][128] += P · V            (TMEM columns 64..191; two passes, hi and lo)
+// then O / l per row, written as a bf16 hi/lo pair.  No key splits: the group's keys run in one
+// CTA (prefill chunks are at most max_prefill_rows long).  Every wait is bounded.
+// ---------------------------------------------------------------------------
+constexpr int kPfuQ = 64;        // queries per CTA
+constexpr int kPfuKeys = 64;     // keys per tile
+constexpr int kPfuStages = 2;
+
+struct PfuLayout {
+    static constexpr int QH = 0;                      // Q hi: 2 halves [128 rows][64 dims] fp16
+    static constexpr int QL = QH + 2 * 128 * 128;     // Q lo
+    static constexpr int RING = QL + 2 * 128 * 128;   // stages: K half 0/1, V half 0/1 [64 keys][64 dims]
+    static constexpr int STAGE = 4 * 64 * 128;
+    static constexpr int VT = RING + kPfuStages * STAGE;  // V^T [128 dims][64 keys]
+    static constexpr int PH = VT + 128 * 128;         // P hi [128 rows][64 keys]
+    static constexpr int PL = PH + 128 * 128;         // P lo
+    static constexpr int BAR = PL + 128 * 128;
+    static constexpr int SMEM = 1024 + BAR + 64;
+};
+
+// byte offset of (row, col) (col < 64 fp16) in a K-major tile of 128-B rows with the 128-B swizzle
+__device__ __forceinline__ uint32_t sw128_off(int row, int col) {
+    return (uint32_t)(row * 128 + ((((col >> 3) ^ (row & 7)) << 4)) + (col & 7) * 2);
+}
+
+__device__ __forceinline__ void stsm_x4(uint32_t addr, const uint32_t (&r)[4]) {
+    asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(r[0]),
+                 "r"(r[1]), "r"(r[2]), "r"(r[3])
+                 : "memory");
+}
+
+__global__ void __launch_bounds__(128, 1) paged_prefill_umma_kernel(const __grid_constant__ CUtensorMap tmKV,
+                                                                     const AttnParams p) {
+    constexpr int D = 128;
+    using L = PfuLayout;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* kv_full = reinterpret_cast<uint64_t*>(smem + L::BAR);
+    uint64_t* s_done = kv_full + kPfuStages;
+    uint64_t* pv_done = s_done + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 1);
+
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    griddep_wait();
+    griddep_launch();
+    const int SPS = p.rows_per_stream;
+    const int n_streams = p.R / SPS;
+    const int n_groups = (SPS + kPfuQ - 1) / kPfuQ;
+    int rest = blockIdx.x;  // CTA-uniform
+    const int g = rest % p.kv_heads;
+    rest /= p.kv_heads;
+    const int grp = rest % n_groups;
+    const int b = rest / n_groups;
+    if (b >= n_streams) return;
+    const int q0 = grp * kPfuQ;                        // first query of the group within the stream
+    const int nq = min(kPfuQ, SPS - q0);
+    const int h = t >> 6, qi = t & 63;                 // this thread's row
+    const bool row_ok = qi < nq;
+    const int r = b * SPS + q0 + qi;                   // row of the call
+    const int ctx_row = row_ok ? p.row_ctx[r] : 0;
+    const int slot = p.row_slot[b * SPS];
+    // the group's keys: the largest key count of its rows (CTA-uniform through shared memory)
+    __shared__ int s_ctx;
+    if (t == 0) s_ctx = 0;
+    __syncthreads();
+    if (row_ok) atomicMax(&s_ctx, ctx_row);
+    __syncthreads();
+    const int ctx_max = s_ctx;
+    const size_t out_row = (size_t)r * p.num_heads + g * 2 + h;
+    if (ctx_max <= 0 || slot < 0 || (b + 1) * SPS > p.R) {  // CTA-uniform: nothing to attend
+        if (ctx_max > 0 && t == 0) record_error(DEV_ERR_ATTN_BOUNDS);
+        if (row_ok)
+            for (int d = 0; d < D; ++d) {
+                p.out[out_row * D + d] = __float2bfloat16(0.f);
+                if (p.out_lo) p.out_lo[out_row * D + d] = __float2bfloat16(0.f);
+            }
+        return;
+    }
+    const int nbt = (ctx_max + 15) >> 4;               // 16-token blocks the group reads
+    const int ntiles = (ctx_max + kPfuKeys - 1) / kPfuKeys;
+
+    if (t == 0) {
+        for (int s2 = 0; s2 < kPfuStages; ++s2) mbar_init(&kv_full[s2], 1);
+        mbar_init(s_done, 1);
+        mbar_init(pv_done, 1);
+        fence_mbar_init();
+        tma_prefetch_desc(&tmKV);
+    }
+    if (warp == 0) {
+        tmem_alloc(tmem_slot, 256);
+        tmem_relinquish();
+    }
+    // ---- Q rows (x scale_log2) as an fp16 hi/lo pair, swizzled K-major halves
+    {
+        const float4* qp = reinterpret_cast<const float4*>(p.q + out_row * D);
+#pragma unroll 2
+        for (int c = 0; c < 16; ++c) {  // 16-B chunk c: dims 8c .. 8c + 7
+            float4 x0 = make_float4(0.f, 0.f, 0.f, 0.f), x1 = x0;
+            if (row_ok) {
+                x0 = qp[2 * c];
+                x1 = qp[2 * c + 1];
+            }
+            const float sc = p.scale_log2;
+            uint32_t hi[4], lo[4];
+            split_h2(x0.x * sc, x0.y * sc, hi[0], lo[0]);
+            split_h2(x0.z * sc, x0.w * sc, hi[1], lo[1]);
+            split_h2(x1.x * sc, x1.y * sc, hi[2], lo[2]);
+            split_h2(x1.z * sc, x1.w * sc, hi[3], lo[3]);
+            const int half = c >> 3, col = (c & 7) * 8;
+            const uint32_t off = (uint32_t)half * (128 * 128) + sw128_off(t, col);
+            *reinterpret_cast<uint4*>(smem + L::QH + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+            *reinterpret_cast<uint4*>(smem + L::QL + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        }
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+
+    auto issue = [&](int i) {  // thread 0: tile i's four blocks (K and V, both dim halves)
+        const int s2 = i % kPfuStages;
+        uint8_t* st = smem + L::RING + s2 * L::STAGE;
+        mbar_arrive_expect_tx(&kv_full[s2], L::STAGE);
+        for (int j = 0; j < 4; ++j) {
+            int jb = i * 4 + j;
+            if (jb >= nbt) jb = 0;  // past the group's keys: any valid block (its keys are masked)
+            int blk = jb < p.mbps ? p.block_table[(size_t)slot * p.mbps + jb] : -1;
+            if (blk < 0 || blk >= p.num_blocks) {
+                record_error(DEV_ERR_ATTN_WAIT);
+                blk = 0;
+            }
+            const int krow = (((blk * p.num_layers + p.layer) * 2 + 0) * p.kv_heads + g) * 16;
+            const int vrow = krow + p.kv_heads * 16;
+            tma_load_2d(st + 0 * 8192 + j * 2048, &tmKV, &kv_full[s2], 0, krow);
+            tma_load_2d(st + 1 * 8192 + j * 2048, &tmKV, &kv_full[s2], 64, krow);
+            tma_load_2d(st + 2 * 8192 + j * 2048, &tmKV, &kv_full[s2], 0, vrow);
+            tma_load_2d(st + 3 * 8192 + j * 2048, &tmKV, &kv_full[s2], 64, vrow);
+        }
+    };
+    if (t == 0)
+        for (int i = 0; i < ntiles && i < kPfuStages; ++i) issue(i);
+
+    const uint32_t idesc_s = make_idesc_f16(128, kPfuKeys), idesc_o = make_idesc_f16(128, D);
+    float m_ref = -INFINITY, l = 0.f;
+    int issued = ntiles < kPfuStages ? ntiles : kPfuStages;  // thread 0's count (drain after a failure)
+    bool fail = false;  // this thread saw a wait run out; the CTA leaves the loop together
+    int i = 0;
+    for (; i < ntiles; ++i) {
+        const int s2 = i % kPfuStages;
+        const uint32_t st = smem_u32(smem + L::RING + s2 * L::STAGE);
+        const bool loaded = mbar_wait(&kv_full[s2], (uint32_t)(i / kPfuStages) & 1u, DEV_ERR_ATTN_WAIT);
+        fail |= !loaded;
+        tc_fence_after();
+        // ---- S = Q K^T (hi, then lo)
+        if (t == 0 && loaded) {
+#pragma unroll
+            for (int part = 0; part < 2; ++part) {
+                const uint32_t qb = smem_u32(smem + (part ? L::QL : L::QH));
+#pragma unroll
+                for (int hd = 0; hd < 2; ++hd)
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        umma_bf16(tmem, make_sw128_desc(qb + hd * 16384) + 2 * kk,
+                                  make_sw128_desc(st + hd * 8192) + 2 * kk, idesc_s,
+                                  (part | hd | kk) ? 1u : 0u);
+            }
+        }
+        if (t == 0) umma_commit(s_done);  // fires at once when nothing was issued
+        fail |= !mbar_wait(s_done, (uint32_t)i & 1u, DEV_ERR_ATTN_WAIT);
+        __syncwarp();
+        tc_fence_after();
+        // ---- this row's scores, mask, online max
+        float sv[kPfuKeys];
+#pragma unroll
+        for (int c = 0; c < kPfuKeys; c += 16) {
+            float v[16];
+            tmem_ld16(tmem + lane_base + (uint32_t)c, v);
+#pragma unroll
+            for (int k = 0; k < 16; ++k) sv[c + k] = (i * kPfuKeys + c + k < ctx_row) ? v[k] : -INFINITY;
+        }
+        float mt = -INFINITY;
+#pragma unroll
+        for (int k = 0; k < kPfuKeys; ++k) mt = fmaxf(mt, sv[k]);
+        float alpha = 1.f;
+        bool rescale = false;
+        if (mt != -INFINITY) {
+            if (m_ref == -INFINITY) {
+                m_ref = mt;
+            } else if (mt > m_ref + 8.f) {
+                alpha = exp2f(m_ref - mt);
+                l *= alpha;
+                m_ref = mt;
+                rescale = true;
+            }
+        }
+        // the previous tile's PV has finished: O is stable, P and V^T may be rewritten
+        if (i > 0) fail |= !mbar_wait(pv_done, (uint32_t)(i - 1) & 1u, DEV_ERR_ATTN_WAIT);
+        __syncwarp();
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, rescale)) {  // warp-collective TMEM read-modify-write of O
+#pragma unroll 1
+            for (int c = 0; c < D; c += 16) {
+                float v[16];
+                tmem_ld16(tmem + lane_base + 64u + (uint32_t)c, v);
+#pragma unroll
+                for (int k = 0; k < 16; ++k) v[k] *= alpha;
+                tmem_st16(tmem + lane_base + 64u + (uint32_t)c, v);
+            }
+        }
+        // ---- P = 2^(s - m) as an fp16 hi/lo pair, row t of the P tiles
+        float psum = 0.f;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            uint32_t hi[4], lo[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float a = sv[8 * c + 2 * j] == -INFINITY ? 0.f : exp2f(sv[8 * c + 2 * j] - m_ref);
+                const float b2 = sv[8 * c + 2 * j + 1] == -INFINITY ? 0.f : exp2f(sv[8 * c + 2 * j + 1] - m_ref);
+                psum += a + b2;
+                split_h2(a, b2, hi[j], lo[j]);
+            }
+            const uint32_t off = sw128_off(t, 8 * c);
+            *reinterpret_cast<uint4*>(smem + L::PH + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+            *reinterpret_cast<uint4*>(smem + L::PL + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        }
+        l += psum;
+        // ---- V^T [128 dims][64 keys] from the stage's V halves: 8x8 blocks, ldmatrix.trans -> stmatrix
+        {
+            const int mi = lane >> 3, rr = lane & 7;
+#pragma unroll
+            for (int it = 0; it < 8; ++it) {
+                const int bidx = (warp * 8 + it) * 4 + mi;  // 128 blocks: key block kb, dim block db
+                const int kb = bidx & 7, db = bidx >> 3;
+                const uint32_t src = st + 2 * 8192 + (uint32_t)(db >> 3) * 8192 + sw128_off(kb * 8 + rr, (db & 7) * 8);
+                uint32_t v4[4];
+                ldsm_x4_t(src, v4);
+                // register j holds matrix j (block (warp * 8 + it) * 4 + j): V^T's row lane / 4,
+                // keys 2 (lane % 4) and + 1.  Keys past the group's last key read whatever the
+                // pool holds there; they are zeroed so that P = 0 meets a finite V.
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int key = i * kPfuKeys + (((warp * 8 + it) * 4 + j) & 7) * 8 + 2 * (lane & 3);
+                    if (key >= ctx_max) v4[j] = 0u;
+                    else if (key + 1 >= ctx_max) v4[j] &= 0xffffu;
+                }
+                // lane 8 mi + rr addresses row rr of matrix mi, the same block it loaded
+                const uint32_t dst = smem_u32(smem + L::VT) + sw128_off(db * 8 + rr, kb * 8);
+                stsm_x4(dst, v4);
+            }
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        const int any_fail = __syncthreads_or(fail ? 1 : 0);  // CTA-uniform
+        tc_fence_after();
+        if (any_fail) {
+            fail = true;
+            break;
+        }
+        // ---- O += P V (hi, then lo); then refill the stage with tile i + 2
+        if (t == 0) {
+#pragma unroll
+            for (int part = 0; part < 2; ++part) {
+                const uint32_t pb = smem_u32(smem + (part ? L::PL : L::PH));
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    umma_bf16(tmem + 64u, make_sw128_desc(pb) + 2 * kk, make_sw128_desc(smem_u32(smem + L::VT)) + 2 * kk,
+                              idesc_o, (i > 0 || part > 0 || kk > 0) ? 1u : 0u);
+            }
+            umma_commit(pv_done);
+            if (i + kPfuStages < ntiles) {
+                issue(i + kPfuStages);
+                ++issued;
+            }
+        }
+    }
+    // ---- O / l -> out (bf16 hi/lo), after the last PV
+    const bool good = !fail && mbar_wait(pv_done, (uint32_t)(ntiles - 1) & 1u, DEV_ERR_ATTN_WAIT);
+    __syncwarp();
+    tc_fence_after();
+    const float inv = (good && l > 0.f) ? 1.f / l : 0.f;
+#pragma unroll 1
+    for (int c = 0; c < D; c += 16) {
+        float v[16];
+        tmem_ld16(tmem + lane_base + 64u + (uint32_t)c, v);
+        if (!good)
+#pragma unroll
+            for (int k = 0; k < 16; ++k) v[k] = 0.f;
+        if (row_ok) {
+            uint32_t hw[8], lw[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const float a = v[2 * k] * inv, b2 = v[2 * k + 1] * inv;
+                const __nv_bfloat162 hb = __floats2bfloat162_rn(a, b2);
+                const float2 hf = __bfloat1622float2(hb);
+                const __nv_bfloat162 lb = __floats2bfloat162_rn(a - hf.x, b2 - hf.y);
+                hw[k] = *reinterpret_cast<const uint32_t*>(&hb);
+                lw[k] = *reinterpret_cast<const uint32_t*>(&lb);
+            }
+            uint4* oh = reinterpret_cast<uint4*>(p.out + out_row * D + c);
+            oh[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            oh[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+            if (p.out_lo) {
+                uint4* ol = reinterpret_cast<uint4*>(p.out_lo + out_row * D + c);
+                ol[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+                ol[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+            }
+        }
+    }
+    // ---- drain (after a failure) and release TMEM
+    if (t == 0 && fail) {
+        for (int j = issued > kPfuStages ? issued - kPfuStages : 0; j < issued; ++j)
+            mbar_wait(&kv_full[j % kPfuStages], (uint32_t)(j / kPfuStages) & 1u, DEV_ERR_DRAIN);
+        // every UMMA this thread issued has finished before TMEM is released (s_done has
+        // completed i + 1 phases when the loop left at tile i)
+        umma_commit(s_done);
+        mbar_wait(s_done, (uint32_t)(i + 1) & 1u, DEV_ERR_DRAIN);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, 256);
+}
+
+inline int launch_prefill_umma(const AttnParams& p, cudaStream_t st) {
+    CUtensorMap map;
+    const int rc = make_kv_map(&map, p);
+    if (rc) return rc;
+    QTTS_CHECK_CUDA((func_attr_once<paged_prefill_umma_kernel>(PfuLayout::SMEM)));
+    const int n_groups = (p.rows_per_stream + kPfuQ - 1) / kPfuQ;
+    const int ctas = (p.R / p.rows_per_stream) * n_groups * p.kv_heads;
+    QTTS_LAUNCH(paged_prefill_umma_kernel, dim3(ctas), dim3(128), PfuLayout::SMEM, st, map, p);
+    return QTTS_OK;
+}
+
+// Prefill attention on the tcgen05 tensor pipe (head_dim 128, 2 query heads per KV head) unless
+// QTTS_PREFILL_UMMA=0 (the mma.sync query-tile kernel).
+inline bool attn_prefill_umma() {
+    static const bool on = [] {
+        const char* v = getenv("QTTS_PREFILL_UMMA");
+        return !(v && *v == '0');
+    }();
+    return on;
+}
+
 // The engine's prefill steps use the query-tile kernel unless QTTS_PREFILL_TILES=0 (one row per
 // query through the decode kernel).
 inline bool attn_prefill_tiles() {
@@ -1378,6 +1747,9 @@ inline int launch_prefill_attention(const AttnParams& p, cudaStream_t st) {
         set_error("prefill attention: %d rows are not streams of %d tokens", p.R, p.rows_per_stream);
         return QTTS_ERR_INVALID;
     }
+    const bool aligned = ((reinterpret_cast<uintptr_t>(p.q) | reinterpret_cast<uintptr_t>(p.out) |
+                           reinterpret_cast<uintptr_t>(p.out_lo)) & 15) == 0;
+    if (p.num_heads == 2 * p.kv_heads && aligned && attn_prefill_umma()) return launch_prefill_umma(p, st);
     const int rc = launch_prefill_tc<2>(p, st);
     if (rc) return rc;
     if (p.max_splits > 1) QTTS_LAUNCH(attn_combine_kernel<128>, dim3(p.R, p.num_heads), dim3(128), 0, st, p);

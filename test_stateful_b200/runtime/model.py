@@ -56,7 +56,9 @@ class PagedPoolTensors:
         self.block_table = torch.empty(p.max_slots, p.max_blocks_per_seq, **i32)
         self.seq_len = torch.empty(p.max_slots, **i32)
         self.position_offset = torch.empty(p.max_slots, **i32)
-        self.kv = torch.empty(p.num_blocks, t.num_layers, 2, t.kv_heads, p.block_size, t.head_dim,
+        # zero-filled: attention kernels multiply V rows past a sequence's last key by P = 0, so the
+        # pool must never hold a non-finite value (it only ever receives written K/V after this)
+        self.kv = torch.zeros(p.num_blocks, t.num_layers, 2, t.kv_heads, p.block_size, t.head_dim,
                               device=device, dtype=torch.float16)
         self.block_elems = t.num_layers * 2 * t.kv_heads * p.block_size * t.head_dim
         self.state = _lib.PagedState(

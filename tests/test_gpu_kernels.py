@@ -227,6 +227,75 @@ def test_paged_prefill_attention_query_tiles(split):
         torch.testing.assert_close(got[r], dec[r], rtol=1e-3, atol=1e-4)
 
 
+@pytest.mark.skipif(os.environ.get("QTTS_PREFILL_UMMA") == "0", reason="query-tile form reads stale tails")
+def test_paged_prefill_long_chunks_stale_tail():
+    """Chunked prefill past one 64-query group (S = 150: groups of 64, 64 and 22 queries) with
+    pasts that start mid-block and up to 850 keys, against an fp32 torch statement.  Every pool
+    entry the streams do not own, and the tail of each stream's last block past its last key,
+    holds NaN: keys past a row's count must contribute exactly nothing (the tcgen05 form zeroes
+    V past the group's keys before P . V)."""
+    D, Hkv, Hq, L, layer, nb, mbps = 128, 8, 16, 2, 0, 400, 64
+    S = 150
+    pasts = [0, 700, 33, 64]
+    n = len(pasts)
+    g = _gen(35)
+    kv = torch.full((nb, L, 2, Hkv, 16, D), float("nan"), dtype=torch.float16)
+    table = torch.full((n, mbps), -1, dtype=torch.int32)
+    perm = torch.randperm(nb, generator=g)
+    for b, pl in enumerate(pasts):
+        k = -(-(pl + S) // 16)
+        table[b, :k] = perm[b * mbps: b * mbps + k]
+        keys = torch.randn(2, Hkv, k * 16, D, generator=g).to(torch.float16)
+        keys[:, :, pl + S:] = float("nan")
+        kv[table[b, :k].long(), layer] = keys.reshape(2, Hkv, k, 16, D).permute(2, 0, 1, 3, 4)
+    kv = kv.to(DEV)
+    R = n * S
+    q = torch.randn(R, Hq, D, generator=g).to(DEV)
+    row_slot = torch.tensor([b for b in range(n) for _ in range(S)], dtype=torch.int32, device=DEV)
+    ctxs = [pl + t + 1 for pl in pasts for t in range(S)]
+    row_ctx = torch.tensor(ctxs, dtype=torch.int32, device=DEV)
+    max_ctx = mbps * 16
+    splits = -(-(max_ctx // 16) // _lib.ATTN_SPLIT_BLOCKS)
+    ws_o = torch.empty(R * Hq * splits * D, device=DEV)
+    ws_ml = torch.empty(R * Hq * splits * 2, device=DEV)
+    out = torch.empty(R, Hq * D, device=DEV, dtype=torch.bfloat16)
+    out_lo = torch.empty_like(out)
+    tdev = table.to(DEV)
+    rc = _lib.load().qtts_paged_attention_prefill(q.data_ptr(), R, S, Hq, Hkv, D, kv.data_ptr(), layer, L, 16, nb,
+                                                  tdev.data_ptr(), mbps, row_slot.data_ptr(), row_ctx.data_ptr(),
+                                                  max_ctx, 0, ws_o.data_ptr(), ws_ml.data_ptr(), out.data_ptr(),
+                                                  out_lo.data_ptr(), _lib.stream_ptr())
+    _lib.check(rc, "paged_attention_prefill")
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    got = (out.float() + out_lo.float()).cpu()
+    assert torch.isfinite(got).all()
+    kvc, qc = kv.float().cpu(), q.float().cpu()
+    for r, c in enumerate(ctxs):
+        b = r // S
+        blocks = table[b, : -(-c // 16)].long()
+        K = kvc[blocks, layer, 0].permute(1, 0, 2, 3).reshape(Hkv, -1, D)[:, :c].repeat_interleave(2, 0)
+        V = kvc[blocks, layer, 1].permute(1, 0, 2, 3).reshape(Hkv, -1, D)[:, :c].repeat_interleave(2, 0)
+        p = torch.softmax((qc[r].unsqueeze(1) @ K.transpose(1, 2)).squeeze(1) / D ** 0.5, dim=-1)
+        ref = (p.unsqueeze(1) @ V).squeeze(1).reshape(-1)
+        torch.testing.assert_close(got[r], ref, rtol=1e-3, atol=1e-4)
+
+
+@pytest.mark.skipif(os.environ.get("QTTS_PREFILL_UMMA") is not None, reason="already a forced run")
+def test_prefill_query_tile_form():
+    """Chunked prefill with two query heads per KV head runs on the tcgen05 kernel by default;
+    the mma.sync query-tile kernel stays available (QTTS_PREFILL_UMMA=0, read once per
+    process): rerun the prefill tests in a child process with it."""
+    import subprocess
+    import sys
+
+    env = dict(os.environ, QTTS_PREFILL_UMMA="0")
+    r = subprocess.run([sys.executable, "-m", "pytest", "-x", "-q", "-m", "gpu", "-p", "no:cacheprovider", "-k",
+                        "prefill and not tile_form", os.path.abspath(__file__)], env=env, capture_output=True,
+                       text=True, timeout=900)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
+
+
 # --------------------------------------------------------------------- scheduler
 def _pool(num_blocks=16, max_slots=6, mbps=8):
     cfg = EngineConfig(talker=TalkerConfig(num_layers=1, kv_heads=1, head_dim=8),
