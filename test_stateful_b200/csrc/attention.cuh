@@ -1377,21 +1377,27 @@ inline int launch_prefill_tc(const AttnParams& p, cudaStream_t st) {
 // ---------------------------------------------------------------------------
 // Chunked prefill on the tcgen05 tensor pipe (head_dim 128, two query heads per KV head).
 // One CTA per (stream, kv head, group of 64 query rows): the group's 64 queries x 2 heads are
-// the 128 rows of the UMMA M side (row t = head * 64 + query), keys arrive in tiles of 64 (four
-// 16-token blocks, TMA with the 128-B swizzle, a 2-stage ring), and per tile
-//   S[128][64]  = Q · K^T           (TMEM columns 0..63; Q as an fp16 hi/lo pair: two passes)
-//   softmax     one thread per TMEM lane (= row): causal mask (keys < row_ctx), online max in
-//               the log2 domain; O is rescaled in TMEM only when the max grows by more than
-//               2^8 (P = 2^(s - m) stays below 256, exact enough in fp16)
-//   P -> shared memory as an fp16 hi/lo pair (K-major, swizzled), V -> V^T by ldmatrix.trans /
-//   stmatrix (so both PV operands are K-major)
-//   O[128][128] += P · V            (TMEM columns 64..191; two passes, hi and lo)
-// then O / l per row, written as a bf16 hi/lo pair.  No key splits: the group's keys run in one
-// CTA (prefill chunks are at most max_prefill_rows long).  Every wait is bounded.
+// the 128 rows of the UMMA M side (row = head * 64 + query), keys arrive in tiles of 64 (four
+// 16-token blocks, TMA with the 128-B swizzle, a 3-stage ring), and per tile i
+//   S[128][64]  = Q · K^T     TMEM, two buffers (columns 0..63 / 192..255): thread 0 issues
+//                             S(i + 1) before the CTA turns to the softmax of tile i, so the
+//                             tensor pipe works while the CUDA cores do
+//   softmax     8 warps, two threads per row (TMEM lane): each takes 32 keys and 64 columns of
+//               O; causal mask (keys < row_ctx), online max in the log2 domain shared by the
+//               pair through shared memory; O is rescaled in TMEM only when the max grows by
+//               more than 8 (P = 2^(s - m) stays below 256, exact enough as an fp16 pair)
+//   P -> shared memory as an fp16 hi/lo pair (K-major, swizzled); V -> V^T by ldmatrix.trans
+//   / stmatrix (both PV operands K-major), V past the group's keys zeroed
+//   O[128][128] += P · V      TMEM columns 64..191; two passes, hi and lo
+// then O / l per row, written as a bf16 hi/lo pair.  Q is an fp16 hi/lo pair too, so both
+// products keep about 22 bits.  No key splits: the group's keys run in one CTA (prefill chunks
+// are at most max_prefill_rows long).  Every wait is bounded.
 // ---------------------------------------------------------------------------
 constexpr int kPfuQ = 64;        // queries per CTA
 constexpr int kPfuKeys = 64;     // keys per tile
-constexpr int kPfuStages = 2;
+constexpr int kPfuStages = 3;
+constexpr int kPfuSoftmaxWarps = 8;                        // two per TMEM lane quadrant
+constexpr int kPfuThreads = (kPfuSoftmaxWarps + 1) * 32;   // + the control warp
 
 struct PfuLayout {
     static constexpr int QH = 0;                      // Q hi: 2 halves [128 rows][64 dims] fp16
@@ -1401,9 +1407,11 @@ struct PfuLayout {
     static constexpr int VT = RING + kPfuStages * STAGE;  // V^T [128 dims][64 keys]
     static constexpr int PH = VT + 128 * 128;         // P hi [128 rows][64 keys]
     static constexpr int PL = PH + 128 * 128;         // P lo
-    static constexpr int BAR = PL + 128 * 128;
-    static constexpr int SMEM = 1024 + BAR + 64;
+    static constexpr int BAR = PL + 128 * 128;        // kv_full[3], s_full[2], pv_done, drain, tmem slot
+    static constexpr int XCH = BAR + 128;             // [2][128] floats: a row's pair exchange
+    static constexpr int SMEM = 1024 + XCH + 2 * 128 * 4;
 };
+static_assert(PfuLayout::SMEM <= 227 * 1024, "prefill tile exceeds shared memory");
 
 // byte offset of (row, col) (col < 64 fp16) in a K-major tile of 128-B rows with the 128-B swizzle
 __device__ __forceinline__ uint32_t sw128_off(int row, int col) {
@@ -1416,18 +1424,42 @@ __device__ __forceinline__ void stsm_x4(uint32_t addr, const uint32_t (&r)[4]) {
                  : "memory");
 }
 
-__global__ void __launch_bounds__(128, 1) paged_prefill_umma_kernel(const __grid_constant__ CUtensorMap tmKV,
-                                                                     const AttnParams p) {
+// 32 lanes x 32 bits, 32 consecutive columns (one wait)
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// the two warps that share a TMEM lane quadrant (w and w + 4) meet at barrier 1 + w % 4
+__device__ __forceinline__ void pair_sync(int warp) {
+    asm volatile("bar.sync %0, 64;" ::"r"(1 + (warp & 3)) : "memory");
+}
+
+__global__ void __launch_bounds__(kPfuThreads, 1) paged_prefill_umma_kernel(const __grid_constant__ CUtensorMap tmKV,
+                                                                             const AttnParams p) {
     constexpr int D = 128;
     using L = PfuLayout;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* kv_full = reinterpret_cast<uint64_t*>(smem + L::BAR);
-    uint64_t* s_done = kv_full + kPfuStages;
-    uint64_t* pv_done = s_done + 1;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 1);
+    uint64_t* s_full = kv_full + kPfuStages;  // [2]: S buffer b holds its tile's scores
+    uint64_t* pv_done = s_full + 2;
+    uint64_t* drain = pv_done + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    float* xch = reinterpret_cast<float*>(smem + L::XCH);
 
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    const bool ctrl = warp == kPfuSoftmaxWarps;  // the control warp: TMA and UMMA issue
     griddep_wait();
     griddep_launch();
     const int SPS = p.rows_per_stream;
@@ -1441,8 +1473,9 @@ __global__ void __launch_bounds__(128, 1) paged_prefill_umma_kernel(const __grid
     if (b >= n_streams) return;
     const int q0 = grp * kPfuQ;                        // first query of the group within the stream
     const int nq = min(kPfuQ, SPS - q0);
-    const int h = t >> 6, qi = t & 63;                 // this thread's row
-    const bool row_ok = qi < nq;
+    const int row = t & 127, ch = (t >> 7) & 1;        // softmax threads: TMEM lane and half
+    const int h = row >> 6, qi = row & 63;
+    const bool row_ok = !ctrl && qi < nq;
     const int r = b * SPS + q0 + qi;                   // row of the call
     const int ctx_row = row_ok ? p.row_ctx[r] : 0;
     const int slot = p.row_slot[b * SPS];
@@ -1450,14 +1483,14 @@ __global__ void __launch_bounds__(128, 1) paged_prefill_umma_kernel(const __grid
     __shared__ int s_ctx;
     if (t == 0) s_ctx = 0;
     __syncthreads();
-    if (row_ok) atomicMax(&s_ctx, ctx_row);
+    if (row_ok && ch == 0) atomicMax(&s_ctx, ctx_row);
     __syncthreads();
     const int ctx_max = s_ctx;
     const size_t out_row = (size_t)r * p.num_heads + g * 2 + h;
-    if (ctx_max <= 0 || slot < 0 || (b + 1) * SPS > p.R) {  // CTA-uniform: nothing to attend
+    if (ctx_max <= 0 || slot < 0) {  // CTA-uniform: nothing to attend (only after a scheduler error)
         if (ctx_max > 0 && t == 0) record_error(DEV_ERR_ATTN_BOUNDS);
         if (row_ok)
-            for (int d = 0; d < D; ++d) {
+            for (int d = ch * 64; d < ch * 64 + 64; ++d) {
                 p.out[out_row * D + d] = __float2bfloat16(0.f);
                 if (p.out_lo) p.out_lo[out_row * D + d] = __float2bfloat16(0.f);
             }
@@ -1466,35 +1499,77 @@ __global__ void __launch_bounds__(128, 1) paged_prefill_umma_kernel(const __grid
     const int nbt = (ctx_max + 15) >> 4;               // 16-token blocks the group reads
     const int ntiles = (ctx_max + kPfuKeys - 1) / kPfuKeys;
 
+    // block j of tile `tile` (lanes 0..3 of the control warp each fetch one): past the group's
+    // keys any valid block stands in (its keys are masked and its V zeroed)
+    auto tile_block = [&](int tile, int j) -> int {
+        int jb = tile * 4 + j;
+        if (jb >= nbt) jb = 0;
+        int blk = jb < p.mbps ? p.block_table[(size_t)slot * p.mbps + jb] : -1;
+        if (blk < 0 || blk >= p.num_blocks) {
+            record_error(DEV_ERR_ATTN_BOUNDS);
+            blk = 0;  // stay in bounds; the error word reports the bad table entry
+        }
+        return blk;
+    };
+    auto gather = [&](int nb, int (&blk)[4]) {  // control warp, converged: lane j's block to every lane
+#pragma unroll
+        for (int j = 0; j < 4; ++j) blk[j] = __shfl_sync(0xffffffffu, nb, j);
+    };
+    auto issue = [&](int tile, const int (&blk)[4]) {  // the tile's K and V, both dim halves
+        const int s2 = tile % kPfuStages;
+        uint8_t* st = smem + L::RING + s2 * L::STAGE;
+        mbar_arrive_expect_tx(&kv_full[s2], L::STAGE);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int krow = (((blk[j] * p.num_layers + p.layer) * 2 + 0) * p.kv_heads + g) * 16;
+            const int vrow = krow + p.kv_heads * 16;
+            tma_load_2d(st + 0 * 8192 + j * 2048, &tmKV, &kv_full[s2], 0, krow);
+            tma_load_2d(st + 1 * 8192 + j * 2048, &tmKV, &kv_full[s2], 64, krow);
+            tma_load_2d(st + 2 * 8192 + j * 2048, &tmKV, &kv_full[s2], 0, vrow);
+            tma_load_2d(st + 3 * 8192 + j * 2048, &tmKV, &kv_full[s2], 64, vrow);
+        }
+    };
+
+    int issued = 0;   // control lane 0: tiles whose loads were issued
+    int nb_next = 0;  // control lanes 0..3: block ids of the next tile to load
     if (t == 0) {
         for (int s2 = 0; s2 < kPfuStages; ++s2) mbar_init(&kv_full[s2], 1);
-        mbar_init(s_done, 1);
+        mbar_init(&s_full[0], 1);
+        mbar_init(&s_full[1], 1);
         mbar_init(pv_done, 1);
+        mbar_init(drain, 1);
         fence_mbar_init();
-        tma_prefetch_desc(&tmKV);
     }
-    if (warp == 0) {
+    __syncthreads();
+    if (ctrl) {
         tmem_alloc(tmem_slot, 256);
         tmem_relinquish();
-    }
-    // ---- Q rows (x scale_log2) as an fp16 hi/lo pair, swizzled K-major halves
-    {
-        const float4* qp = reinterpret_cast<const float4*>(p.q + out_row * D);
+        if (lane == 0) tma_prefetch_desc(&tmKV);
+        // the first two tiles' loads; tile 2's block ids stay in lanes 0..3
+        for (int tile = 0; tile < 2 && tile < ntiles; ++tile) {
+            int blk[4];
+            gather(lane < 4 ? tile_block(tile, lane) : 0, blk);
+            if (lane == 0) issue(tile, blk);
+        }
+        issued = min(ntiles, 2);
+        nb_next = (lane < 4 && 2 < ntiles) ? tile_block(2, lane) : 0;
+    } else {
+        // ---- Q rows (x scale_log2) as an fp16 hi/lo pair: this thread's half of the dims
+        const float4* qp = reinterpret_cast<const float4*>(p.q + out_row * D + ch * 64);
+        const float sc = p.scale_log2;
 #pragma unroll 2
-        for (int c = 0; c < 16; ++c) {  // 16-B chunk c: dims 8c .. 8c + 7
+        for (int c = 0; c < 8; ++c) {  // 16-B chunk c of the half: dims 64 ch + 8c .. + 7
             float4 x0 = make_float4(0.f, 0.f, 0.f, 0.f), x1 = x0;
             if (row_ok) {
                 x0 = qp[2 * c];
                 x1 = qp[2 * c + 1];
             }
-            const float sc = p.scale_log2;
             uint32_t hi[4], lo[4];
             split_h2(x0.x * sc, x0.y * sc, hi[0], lo[0]);
             split_h2(x0.z * sc, x0.w * sc, hi[1], lo[1]);
             split_h2(x1.x * sc, x1.y * sc, hi[2], lo[2]);
             split_h2(x1.z * sc, x1.w * sc, hi[3], lo[3]);
-            const int half = c >> 3, col = (c & 7) * 8;
-            const uint32_t off = (uint32_t)half * (128 * 128) + sw128_off(t, col);
+            const uint32_t off = (uint32_t)ch * (128 * 128) + sw128_off(row, c * 8);
             *reinterpret_cast<uint4*>(smem + L::QH + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
             *reinterpret_cast<uint4*>(smem + L::QL + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
         }
@@ -1504,137 +1579,146 @@ __global__ void __launch_bounds__(128, 1) paged_prefill_umma_kernel(const __grid
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-
-    auto issue = [&](int i) {  // thread 0: tile i's four blocks (K and V, both dim halves)
-        const int s2 = i % kPfuStages;
-        uint8_t* st = smem + L::RING + s2 * L::STAGE;
-        mbar_arrive_expect_tx(&kv_full[s2], L::STAGE);
-        for (int j = 0; j < 4; ++j) {
-            int jb = i * 4 + j;
-            if (jb >= nbt) jb = 0;  // past the group's keys: any valid block (its keys are masked)
-            int blk = jb < p.mbps ? p.block_table[(size_t)slot * p.mbps + jb] : -1;
-            if (blk < 0 || blk >= p.num_blocks) {
-                record_error(DEV_ERR_ATTN_WAIT);
-                blk = 0;
-            }
-            const int krow = (((blk * p.num_layers + p.layer) * 2 + 0) * p.kv_heads + g) * 16;
-            const int vrow = krow + p.kv_heads * 16;
-            tma_load_2d(st + 0 * 8192 + j * 2048, &tmKV, &kv_full[s2], 0, krow);
-            tma_load_2d(st + 1 * 8192 + j * 2048, &tmKV, &kv_full[s2], 64, krow);
-            tma_load_2d(st + 2 * 8192 + j * 2048, &tmKV, &kv_full[s2], 0, vrow);
-            tma_load_2d(st + 3 * 8192 + j * 2048, &tmKV, &kv_full[s2], 64, vrow);
-        }
-    };
-    if (t == 0)
-        for (int i = 0; i < ntiles && i < kPfuStages; ++i) issue(i);
-
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     const uint32_t idesc_s = make_idesc_f16(128, kPfuKeys), idesc_o = make_idesc_f16(128, D);
-    float m_ref = -INFINITY, l = 0.f;
-    int issued = ntiles < kPfuStages ? ntiles : kPfuStages;  // thread 0's count (drain after a failure)
+
+    // control lane 0: S(tile) = Q K^T into buffer tile & 1, once the tile's K has landed
+    auto issue_s = [&](int tile) -> bool {
+        if (!mbar_wait(&kv_full[tile % kPfuStages], (uint32_t)(tile / kPfuStages) & 1u, DEV_ERR_ATTN_WAIT))
+            return false;
+        tc_fence_after();
+        const uint32_t st = smem_u32(smem + L::RING + (tile % kPfuStages) * L::STAGE);
+        const uint32_t d = tmem + ((tile & 1) ? 192u : 0u);
+#pragma unroll
+        for (int part = 0; part < 2; ++part) {
+            const uint32_t qb = smem_u32(smem + (part ? L::QL : L::QH));
+#pragma unroll
+            for (int hd = 0; hd < 2; ++hd)
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    umma_bf16(d, make_sw128_desc(qb + hd * 16384) + 2 * kk, make_sw128_desc(st + hd * 8192) + 2 * kk,
+                              idesc_s, (part | hd | kk) ? 1u : 0u);
+        }
+        umma_commit(&s_full[tile & 1]);
+        return true;
+    };
+    // control lane 0: O (+)= P V of the tile whose P and V^T are in shared memory
+    auto issue_pv = [&](int tile) {
+#pragma unroll
+        for (int part = 0; part < 2; ++part) {
+            const uint32_t pb = smem_u32(smem + (part ? L::PL : L::PH));
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+                umma_bf16(tmem + 64u, make_sw128_desc(pb) + 2 * kk, make_sw128_desc(smem_u32(smem + L::VT)) + 2 * kk,
+                          idesc_o, (tile > 0 || part > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(pv_done);
+    };
+
     bool fail = false;  // this thread saw a wait run out; the CTA leaves the loop together
+    if (ctrl && lane == 0) fail = !issue_s(0);
+    float m_ref = -INFINITY, l = 0.f;
     int i = 0;
+    // Window i (between two CTA barriers): the softmax warps turn S(i) into P(i) and V(i) into
+    // V^T; the control warp issues PV(i - 1), the loads of tile i + 2 (into the stage tile i - 1
+    // left) and S(i + 1) (into the S buffer tile i - 1 left).
     for (; i < ntiles; ++i) {
-        const int s2 = i % kPfuStages;
-        const uint32_t st = smem_u32(smem + L::RING + s2 * L::STAGE);
-        const bool loaded = mbar_wait(&kv_full[s2], (uint32_t)(i / kPfuStages) & 1u, DEV_ERR_ATTN_WAIT);
-        fail |= !loaded;
-        tc_fence_after();
-        // ---- S = Q K^T (hi, then lo)
-        if (t == 0 && loaded) {
-#pragma unroll
-            for (int part = 0; part < 2; ++part) {
-                const uint32_t qb = smem_u32(smem + (part ? L::QL : L::QH));
-#pragma unroll
-                for (int hd = 0; hd < 2; ++hd)
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        umma_bf16(tmem, make_sw128_desc(qb + hd * 16384) + 2 * kk,
-                                  make_sw128_desc(st + hd * 8192) + 2 * kk, idesc_s,
-                                  (part | hd | kk) ? 1u : 0u);
+        if (ctrl) {
+            if (lane == 0 && !fail && i > 0) issue_pv(i - 1);
+            if (i + 2 < ntiles) {
+                int blk[4];
+                gather(nb_next, blk);
+                nb_next = (lane < 4 && i + 3 < ntiles) ? tile_block(i + 3, lane) : 0;
+                if (lane == 0 && !fail) {
+                    issue(i + 2, blk);
+                    ++issued;
+                }
             }
-        }
-        if (t == 0) umma_commit(s_done);  // fires at once when nothing was issued
-        fail |= !mbar_wait(s_done, (uint32_t)i & 1u, DEV_ERR_ATTN_WAIT);
-        __syncwarp();
-        tc_fence_after();
-        // ---- this row's scores, mask, online max
-        float sv[kPfuKeys];
+            if (lane == 0 && !fail && i + 1 < ntiles) fail = !issue_s(i + 1);
+            __syncwarp();
+        } else {
+            // ---- this thread's 32 scores of tile i
+            fail |= !mbar_wait(&s_full[i & 1], (uint32_t)(i >> 1) & 1u, DEV_ERR_ATTN_WAIT);
+            __syncwarp();
+            tc_fence_after();
+            float sv[32];
+            tmem_ld32(tmem + lane_base + ((i & 1) ? 192u : 0u) + (uint32_t)(ch * 32), sv);
+            const int lim = ctx_row - (i * kPfuKeys + ch * 32);  // keys of the row in this half-tile
+            float mt = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < kPfuKeys; c += 16) {
-            float v[16];
-            tmem_ld16(tmem + lane_base + (uint32_t)c, v);
-#pragma unroll
-            for (int k = 0; k < 16; ++k) sv[c + k] = (i * kPfuKeys + c + k < ctx_row) ? v[k] : -INFINITY;
-        }
-        float mt = -INFINITY;
-#pragma unroll
-        for (int k = 0; k < kPfuKeys; ++k) mt = fmaxf(mt, sv[k]);
-        float alpha = 1.f;
-        bool rescale = false;
-        if (mt != -INFINITY) {
-            if (m_ref == -INFINITY) {
-                m_ref = mt;
-            } else if (mt > m_ref + 8.f) {
-                alpha = exp2f(m_ref - mt);
-                l *= alpha;
-                m_ref = mt;
-                rescale = true;
+            for (int k = 0; k < 32; ++k) {
+                sv[k] = k < lim ? sv[k] : -INFINITY;
+                mt = fmaxf(mt, sv[k]);
             }
-        }
-        // the previous tile's PV has finished: O is stable, P and V^T may be rewritten
-        if (i > 0) fail |= !mbar_wait(pv_done, (uint32_t)(i - 1) & 1u, DEV_ERR_ATTN_WAIT);
-        __syncwarp();
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, rescale)) {  // warp-collective TMEM read-modify-write of O
-#pragma unroll 1
-            for (int c = 0; c < D; c += 16) {
-                float v[16];
-                tmem_ld16(tmem + lane_base + 64u + (uint32_t)c, v);
-#pragma unroll
-                for (int k = 0; k < 16; ++k) v[k] *= alpha;
-                tmem_st16(tmem + lane_base + 64u + (uint32_t)c, v);
+            xch[ch * 128 + row] = mt;
+            pair_sync(warp);
+            mt = fmaxf(mt, xch[(ch ^ 1) * 128 + row]);
+            float alpha = 1.f;
+            bool rescale = false;
+            if (mt != -INFINITY) {
+                if (m_ref == -INFINITY) {
+                    m_ref = mt;
+                } else if (mt > m_ref + 8.f) {
+                    alpha = exp2f(m_ref - mt);
+                    l *= alpha;
+                    m_ref = mt;
+                    rescale = true;
+                }
             }
-        }
-        // ---- P = 2^(s - m) as an fp16 hi/lo pair, row t of the P tiles
-        float psum = 0.f;
+            const float m_use = m_ref == -INFINITY ? 0.f : m_ref;  // a row with no keys yet: P = 0
+            // ---- P = 2^(s - m) of this thread's 32 keys; written after the previous PV finished
+            uint32_t ph[16], pl[16];
+            float psum = 0.f;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-            uint32_t hi[4], lo[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float a = sv[8 * c + 2 * j] == -INFINITY ? 0.f : exp2f(sv[8 * c + 2 * j] - m_ref);
-                const float b2 = sv[8 * c + 2 * j + 1] == -INFINITY ? 0.f : exp2f(sv[8 * c + 2 * j + 1] - m_ref);
+            for (int k = 0; k < 16; ++k) {
+                const float a = exp2f(sv[2 * k] - m_use), b2 = exp2f(sv[2 * k + 1] - m_use);
                 psum += a + b2;
-                split_h2(a, b2, hi[j], lo[j]);
+                split_h2(a, b2, ph[k], pl[k]);
             }
-            const uint32_t off = sw128_off(t, 8 * c);
-            *reinterpret_cast<uint4*>(smem + L::PH + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-            *reinterpret_cast<uint4*>(smem + L::PL + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-        }
-        l += psum;
-        // ---- V^T [128 dims][64 keys] from the stage's V halves: 8x8 blocks, ldmatrix.trans -> stmatrix
-        {
+            l += psum;
+            if (i > 0) fail |= !mbar_wait(pv_done, (uint32_t)(i - 1) & 1u, DEV_ERR_ATTN_WAIT);
+            __syncwarp();
+            tc_fence_after();
+            if (__any_sync(0xffffffffu, rescale)) {  // warp-collective TMEM read-modify-write of O
+#pragma unroll 1
+                for (int c = 0; c < 64; c += 16) {
+                    const uint32_t ta = tmem + lane_base + 64u + (uint32_t)(ch * 64 + c);
+                    float v[16];
+                    tmem_ld16(ta, v);
+#pragma unroll
+                    for (int k = 0; k < 16; ++k) v[k] *= alpha;
+                    tmem_st16(ta, v);
+                }
+            }
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const uint32_t off = sw128_off(row, ch * 32 + 8 * c);
+                *reinterpret_cast<uint4*>(smem + L::PH + off) =
+                    make_uint4(ph[4 * c], ph[4 * c + 1], ph[4 * c + 2], ph[4 * c + 3]);
+                *reinterpret_cast<uint4*>(smem + L::PL + off) =
+                    make_uint4(pl[4 * c], pl[4 * c + 1], pl[4 * c + 2], pl[4 * c + 3]);
+            }
+            // ---- V^T [128 dims][64 keys] from the stage's V halves: 8x8 blocks, ldmatrix.trans -> stmatrix
+            const uint32_t st = smem_u32(smem + L::RING + (i % kPfuStages) * L::STAGE);
             const int mi = lane >> 3, rr = lane & 7;
 #pragma unroll
-            for (int it = 0; it < 8; ++it) {
-                const int bidx = (warp * 8 + it) * 4 + mi;  // 128 blocks: key block kb, dim block db
+            for (int it = 0; it < 4; ++it) {
+                const int bidx = (warp * 4 + it) * 4 + mi;  // 128 blocks: key block kb, dim block db
                 const int kb = bidx & 7, db = bidx >> 3;
                 const uint32_t src = st + 2 * 8192 + (uint32_t)(db >> 3) * 8192 + sw128_off(kb * 8 + rr, (db & 7) * 8);
                 uint32_t v4[4];
                 ldsm_x4_t(src, v4);
-                // register j holds matrix j (block (warp * 8 + it) * 4 + j): V^T's row lane / 4,
+                // register j holds matrix j (block (warp * 4 + it) * 4 + j): V^T's row lane / 4,
                 // keys 2 (lane % 4) and + 1.  Keys past the group's last key read whatever the
                 // pool holds there; they are zeroed so that P = 0 meets a finite V.
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                    const int key = i * kPfuKeys + (((warp * 8 + it) * 4 + j) & 7) * 8 + 2 * (lane & 3);
+                    const int key = i * kPfuKeys + (((warp * 4 + it) * 4 + j) & 7) * 8 + 2 * (lane & 3);
                     if (key >= ctx_max) v4[j] = 0u;
                     else if (key + 1 >= ctx_max) v4[j] &= 0xffffu;
                 }
                 // lane 8 mi + rr addresses row rr of matrix mi, the same block it loaded
-                const uint32_t dst = smem_u32(smem + L::VT) + sw128_off(db * 8 + rr, kb * 8);
-                stsm_x4(dst, v4);
+                stsm_x4(smem_u32(smem + L::VT) + sw128_off(db * 8 + rr, kb * 8), v4);
             }
         }
         fence_proxy_async_smem();
@@ -1645,68 +1729,55 @@ __global__ void __launch_bounds__(128, 1) paged_prefill_umma_kernel(const __grid
             fail = true;
             break;
         }
-        // ---- O += P V (hi, then lo); then refill the stage with tile i + 2
-        if (t == 0) {
-#pragma unroll
-            for (int part = 0; part < 2; ++part) {
-                const uint32_t pb = smem_u32(smem + (part ? L::PL : L::PH));
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    umma_bf16(tmem + 64u, make_sw128_desc(pb) + 2 * kk, make_sw128_desc(smem_u32(smem + L::VT)) + 2 * kk,
-                              idesc_o, (i > 0 || part > 0 || kk > 0) ? 1u : 0u);
-            }
-            umma_commit(pv_done);
-            if (i + kPfuStages < ntiles) {
-                issue(i + kPfuStages);
-                ++issued;
-            }
-        }
     }
-    // ---- O / l -> out (bf16 hi/lo), after the last PV
-    const bool good = !fail && mbar_wait(pv_done, (uint32_t)(ntiles - 1) & 1u, DEV_ERR_ATTN_WAIT);
-    __syncwarp();
-    tc_fence_after();
-    const float inv = (good && l > 0.f) ? 1.f / l : 0.f;
+    if (ctrl && lane == 0 && !fail) issue_pv(ntiles - 1);
+    if (!ctrl) {
+        // ---- O / l -> out (bf16 hi/lo), after the last PV; the pair adds its halves of l
+        const bool good = !fail && mbar_wait(pv_done, (uint32_t)(ntiles - 1) & 1u, DEV_ERR_ATTN_WAIT);
+        __syncwarp();
+        tc_fence_after();
+        xch[ch * 128 + row] = l;
+        pair_sync(warp);
+        const float l_row = l + xch[(ch ^ 1) * 128 + row];
+        const float inv = (good && l_row > 0.f) ? 1.f / l_row : 0.f;
 #pragma unroll 1
-    for (int c = 0; c < D; c += 16) {
-        float v[16];
-        tmem_ld16(tmem + lane_base + 64u + (uint32_t)c, v);
-        if (!good)
+        for (int c = 0; c < 64; c += 16) {
+            float v[16];
+            tmem_ld16(tmem + lane_base + 64u + (uint32_t)(ch * 64 + c), v);
+            if (!good)
 #pragma unroll
-            for (int k = 0; k < 16; ++k) v[k] = 0.f;
-        if (row_ok) {
-            uint32_t hw[8], lw[8];
+                for (int k = 0; k < 16; ++k) v[k] = 0.f;
+            if (row_ok) {
+                uint32_t hw[8], lw[8];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                const float a = v[2 * k] * inv, b2 = v[2 * k + 1] * inv;
-                const __nv_bfloat162 hb = __floats2bfloat162_rn(a, b2);
-                const float2 hf = __bfloat1622float2(hb);
-                const __nv_bfloat162 lb = __floats2bfloat162_rn(a - hf.x, b2 - hf.y);
-                hw[k] = *reinterpret_cast<const uint32_t*>(&hb);
-                lw[k] = *reinterpret_cast<const uint32_t*>(&lb);
-            }
-            uint4* oh = reinterpret_cast<uint4*>(p.out + out_row * D + c);
-            oh[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-            oh[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
-            if (p.out_lo) {
-                uint4* ol = reinterpret_cast<uint4*>(p.out_lo + out_row * D + c);
-                ol[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-                ol[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+                for (int k = 0; k < 8; ++k) {
+                    const float a = v[2 * k] * inv, b2 = v[2 * k + 1] * inv;
+                    const __nv_bfloat162 hb = __floats2bfloat162_rn(a, b2);
+                    const float2 hf = __bfloat1622float2(hb);
+                    const __nv_bfloat162 lb = __floats2bfloat162_rn(a - hf.x, b2 - hf.y);
+                    hw[k] = *reinterpret_cast<const uint32_t*>(&hb);
+                    lw[k] = *reinterpret_cast<const uint32_t*>(&lb);
+                }
+                uint4* oh = reinterpret_cast<uint4*>(p.out + out_row * D + ch * 64 + c);
+                oh[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                oh[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+                if (p.out_lo) {
+                    uint4* ol = reinterpret_cast<uint4*>(p.out_lo + out_row * D + ch * 64 + c);
+                    ol[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+                    ol[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+                }
             }
         }
-    }
-    // ---- drain (after a failure) and release TMEM
-    if (t == 0 && fail) {
+    } else if (lane == 0 && fail) {
+        // after a failure: the loads in flight land and every UMMA finishes before TMEM is released
         for (int j = issued > kPfuStages ? issued - kPfuStages : 0; j < issued; ++j)
             mbar_wait(&kv_full[j % kPfuStages], (uint32_t)(j / kPfuStages) & 1u, DEV_ERR_DRAIN);
-        // every UMMA this thread issued has finished before TMEM is released (s_done has
-        // completed i + 1 phases when the loop left at tile i)
-        umma_commit(s_done);
-        mbar_wait(s_done, (uint32_t)(i + 1) & 1u, DEV_ERR_DRAIN);
+        umma_commit(drain);
+        mbar_wait(drain, 0, DEV_ERR_DRAIN);
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) tmem_dealloc(tmem, 256);
+    if (ctrl) tmem_dealloc(tmem, 256);
 }
 
 inline int launch_prefill_umma(const AttnParams& p, cudaStream_t st) {
@@ -1716,7 +1787,7 @@ inline int launch_prefill_umma(const AttnParams& p, cudaStream_t st) {
     QTTS_CHECK_CUDA((func_attr_once<paged_prefill_umma_kernel>(PfuLayout::SMEM)));
     const int n_groups = (p.rows_per_stream + kPfuQ - 1) / kPfuQ;
     const int ctas = (p.R / p.rows_per_stream) * n_groups * p.kv_heads;
-    QTTS_LAUNCH(paged_prefill_umma_kernel, dim3(ctas), dim3(128), PfuLayout::SMEM, st, map, p);
+    QTTS_LAUNCH(paged_prefill_umma_kernel, dim3(ctas), dim3(kPfuThreads), PfuLayout::SMEM, st, map, p);
     return QTTS_OK;
 }
 
