@@ -1378,36 +1378,36 @@ inline int launch_prefill_tc(const AttnParams& p, cudaStream_t st) {
 // Chunked prefill on the tcgen05 tensor pipe (head_dim 128, two query heads per KV head).
 // One CTA per (stream, kv head, group of 64 query rows): the group's 64 queries x 2 heads are
 // the 128 rows of the UMMA M side (row = head * 64 + query), keys arrive in tiles of 64 (four
-// 16-token blocks, TMA with the 128-B swizzle, a 3-stage ring), and per tile i
-//   S[128][64]  = Q · K^T     TMEM, two buffers (columns 0..63 / 192..255): thread 0 issues
-//                             S(i + 1) before the CTA turns to the softmax of tile i, so the
-//                             tensor pipe works while the CUDA cores do
+// 16-token blocks, TMA with the 128-B swizzle, a 4-stage ring), and per tile i
+//   S[128][64]  = Q · K^T     TMEM, two buffers (columns 0..63 / 192..255); a UMMA warp
+//                             issues S(i + 1) while the softmax warps work on tile i (a TMA
+//                             warp keeps the ring two tiles ahead)
 //   softmax     8 warps, two threads per row (TMEM lane): each takes 32 keys and 64 columns of
 //               O; causal mask (keys < row_ctx), online max in the log2 domain shared by the
 //               pair through shared memory; O is rescaled in TMEM only when the max grows by
 //               more than 8 (P = 2^(s - m) stays below 256, exact enough as an fp16 pair)
-//   P -> shared memory as an fp16 hi/lo pair (K-major, swizzled); V -> V^T by ldmatrix.trans
-//   / stmatrix (both PV operands K-major), V past the group's keys zeroed
-//   O[128][128] += P · V      TMEM columns 64..191; two passes, hi and lo
+//   P -> shared memory as an fp16 hi/lo pair (K-major, swizzled)
+//   O[128][128] += P · V      TMEM columns 64..191; two passes, hi and lo; V is read where TMA
+//                             put it, as an MN-major operand (keys are its K rows, dims its N);
+//                             in the last tile, V rows past the group's keys are zeroed first
 // then O / l per row, written as a bf16 hi/lo pair.  Q is an fp16 hi/lo pair too, so both
 // products keep about 22 bits.  No key splits: the group's keys run in one CTA (prefill chunks
 // are at most max_prefill_rows long).  Every wait is bounded.
 // ---------------------------------------------------------------------------
 constexpr int kPfuQ = 64;        // queries per CTA
 constexpr int kPfuKeys = 64;     // keys per tile
-constexpr int kPfuStages = 3;
+constexpr int kPfuStages = 4;
 constexpr int kPfuSoftmaxWarps = 8;                        // two per TMEM lane quadrant
-constexpr int kPfuThreads = (kPfuSoftmaxWarps + 1) * 32;   // + the control warp
+constexpr int kPfuThreads = (kPfuSoftmaxWarps + 2) * 32;   // + the UMMA warp and the TMA warp
 
 struct PfuLayout {
     static constexpr int QH = 0;                      // Q hi: 2 halves [128 rows][64 dims] fp16
     static constexpr int QL = QH + 2 * 128 * 128;     // Q lo
     static constexpr int RING = QL + 2 * 128 * 128;   // stages: K half 0/1, V half 0/1 [64 keys][64 dims]
     static constexpr int STAGE = 4 * 64 * 128;
-    static constexpr int VT = RING + kPfuStages * STAGE;  // V^T [128 dims][64 keys]
-    static constexpr int PH = VT + 128 * 128;         // P hi [128 rows][64 keys]
+    static constexpr int PH = RING + kPfuStages * STAGE;  // P hi [128 rows][64 keys]
     static constexpr int PL = PH + 128 * 128;         // P lo
-    static constexpr int BAR = PL + 128 * 128;        // kv_full[3], s_full[2], pv_done, drain, tmem slot
+    static constexpr int BAR = PL + 128 * 128;        // kv_full[4], s_full[2], pv_done, drain, tmem slot
     static constexpr int XCH = BAR + 128;             // [2][128] floats: a row's pair exchange
     static constexpr int SMEM = 1024 + XCH + 2 * 128 * 4;
 };
@@ -1440,6 +1440,31 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Shared-memory descriptor of an MN-major operand with the 128-B swizzle: 128-B rows (64
+// fp16 along MN) are the K rows, 8-row groups 1024 B apart (SBO), and the next 64 MN elements
+// start `mn_block_bytes` further on (LBO).
+__device__ __forceinline__ uint64_t make_sw128_mn_desc(uint32_t smem_addr, uint32_t mn_block_bytes) {
+    uint64_t d = 0;
+    d |= (uint64_t)((smem_addr >> 4) & 0x3FFF);
+    d |= (uint64_t)((mn_block_bytes >> 4) & 0x3FFF) << 16;  // LBO: next 64 MN elements
+    d |= (uint64_t)(1024 >> 4) << 32;                       // SBO: next 8 K rows
+    d |= (uint64_t)1 << 46;                                 // descriptor version (Blackwell)
+    d |= (uint64_t)2 << 61;                                 // SWIZZLE_128B
+    return d;
+}
+
+__device__ __forceinline__ float ex2_approx(float x) {  // 2^x; 0 for -inf
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// optional per-window timestamps of the tcgen05 prefill (a profiling build defines PFU_STAMP;
+// role 0 = the UMMA warp, 1 / 2 = a softmax thread of each half)
+#ifndef PFU_STAMP
+#define PFU_STAMP(role, point)
+#endif
+
 // the two warps that share a TMEM lane quadrant (w and w + 4) meet at barrier 1 + w % 4
 __device__ __forceinline__ void pair_sync(int warp) {
     asm volatile("bar.sync %0, 64;" ::"r"(1 + (warp & 3)) : "memory");
@@ -1459,7 +1484,9 @@ __global__ void __launch_bounds__(kPfuThreads, 1) paged_prefill_umma_kernel(cons
     float* xch = reinterpret_cast<float*>(smem + L::XCH);
 
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-    const bool ctrl = warp == kPfuSoftmaxWarps;  // the control warp: TMA and UMMA issue
+    const bool mma_w = warp == kPfuSoftmaxWarps;      // issues the UMMAs (and owns TMEM)
+    const bool tma_w = warp == kPfuSoftmaxWarps + 1;  // issues the KV loads
+    const bool ctrl = mma_w || tma_w;
     griddep_wait();
     griddep_launch();
     const int SPS = p.rows_per_stream;
@@ -1469,8 +1496,11 @@ __global__ void __launch_bounds__(kPfuThreads, 1) paged_prefill_umma_kernel(cons
     const int g = rest % p.kv_heads;
     rest /= p.kv_heads;
     const int grp = rest % n_groups;
-    const int b = rest / n_groups;
-    if (b >= n_streams) return;
+    rest /= n_groups;
+    const int b = rest % n_streams;
+    const int sp = rest / n_streams;  // key split sp of max_splits: a contiguous share of the group's tiles
+    if (sp >= p.max_splits) return;
+    const int nsplit = p.max_splits;
     const int q0 = grp * kPfuQ;                        // first query of the group within the stream
     const int nq = min(kPfuQ, SPS - q0);
     const int row = t & 127, ch = (t >> 7) & 1;        // softmax threads: TMEM lane and half
@@ -1487,51 +1517,65 @@ __global__ void __launch_bounds__(kPfuThreads, 1) paged_prefill_umma_kernel(cons
     __syncthreads();
     const int ctx_max = s_ctx;
     const size_t out_row = (size_t)r * p.num_heads + g * 2 + h;
+    const size_t part_row = (size_t)out_row * nsplit + sp;  // this row's partial (several splits)
     if (ctx_max <= 0 || slot < 0) {  // CTA-uniform: nothing to attend (only after a scheduler error)
-        if (ctx_max > 0 && t == 0) record_error(DEV_ERR_ATTN_BOUNDS);
-        if (row_ok)
+        if (ctx_max > 0 && t == 0 && sp == 0) record_error(DEV_ERR_ATTN_BOUNDS);
+        if (row_ok && nsplit == 1)
             for (int d = ch * 64; d < ch * 64 + 64; ++d) {
                 p.out[out_row * D + d] = __float2bfloat16(0.f);
                 if (p.out_lo) p.out_lo[out_row * D + d] = __float2bfloat16(0.f);
             }
+        if (row_ok && nsplit > 1 && ch == 0) {  // an empty partial: prefill_combine_kernel writes zeros
+            p.ws_ml[part_row * 2 + 0] = -INFINITY;
+            p.ws_ml[part_row * 2 + 1] = 0.f;
+        }
         return;
     }
     const int nbt = (ctx_max + 15) >> 4;               // 16-token blocks the group reads
     const int ntiles = (ctx_max + kPfuKeys - 1) / kPfuKeys;
+    const int t0 = (int)(((long long)sp * ntiles) / nsplit);
+    const int nt = (int)(((long long)(sp + 1) * ntiles) / nsplit) - t0;  // this CTA's tiles: t0 .. t0 + nt - 1
+    if (nt <= 0) {  // CTA-uniform: fewer tiles than splits; this split is empty for every row
+        if (row_ok && ch == 0) {
+            p.ws_ml[part_row * 2 + 0] = -INFINITY;
+            p.ws_ml[part_row * 2 + 1] = 0.f;
+        }
+        return;
+    }
 
-    // block j of tile `tile` (lanes 0..3 of the control warp each fetch one): past the group's
-    // keys any valid block stands in (its keys are masked and its V zeroed)
-    auto tile_block = [&](int tile, int j) -> int {
+    // Block j of tile `tile` as the table holds it (lanes 0..3 of the TMA warp each fetch
+    // one, a window before the block is loaded, so the read's latency is hidden); past the
+    // group's keys any valid block stands in (its keys are masked and its V zeroed).
+    auto tile_block_raw = [&](int tile, int j) -> int {
         int jb = tile * 4 + j;
         if (jb >= nbt) jb = 0;
-        int blk = jb < p.mbps ? p.block_table[(size_t)slot * p.mbps + jb] : -1;
+        return jb < p.mbps ? p.block_table[(size_t)slot * p.mbps + jb] : -1;
+    };
+    auto checked = [&](int blk) -> int {
         if (blk < 0 || blk >= p.num_blocks) {
             record_error(DEV_ERR_ATTN_BOUNDS);
             blk = 0;  // stay in bounds; the error word reports the bad table entry
         }
         return blk;
     };
-    auto gather = [&](int nb, int (&blk)[4]) {  // control warp, converged: lane j's block to every lane
-#pragma unroll
-        for (int j = 0; j < 4; ++j) blk[j] = __shfl_sync(0xffffffffu, nb, j);
-    };
-    auto issue = [&](int tile, const int (&blk)[4]) {  // the tile's K and V, both dim halves
-        const int s2 = tile % kPfuStages;
+    // TMA warp, converged: local tile li's K and V, both dim halves, one box per lane 0..15
+    // (lane = 4 j + 2 kind + half); lanes 0..3 hold the four block ids.
+    auto issue = [&](int li, int nb, bool go) {
+        const int s2 = li % kPfuStages;
         uint8_t* st = smem + L::RING + s2 * L::STAGE;
-        mbar_arrive_expect_tx(&kv_full[s2], L::STAGE);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int krow = (((blk[j] * p.num_layers + p.layer) * 2 + 0) * p.kv_heads + g) * 16;
-            const int vrow = krow + p.kv_heads * 16;
-            tma_load_2d(st + 0 * 8192 + j * 2048, &tmKV, &kv_full[s2], 0, krow);
-            tma_load_2d(st + 1 * 8192 + j * 2048, &tmKV, &kv_full[s2], 64, krow);
-            tma_load_2d(st + 2 * 8192 + j * 2048, &tmKV, &kv_full[s2], 0, vrow);
-            tma_load_2d(st + 3 * 8192 + j * 2048, &tmKV, &kv_full[s2], 64, vrow);
+        const int blk = __shfl_sync(0xffffffffu, nb, (lane >> 2) & 3);
+        if (!go) return;
+        if (lane == 0) mbar_arrive_expect_tx(&kv_full[s2], L::STAGE);
+        __syncwarp();
+        if (lane < 16) {
+            const int j = lane >> 2, kind = (lane >> 1) & 1, half = lane & 1;
+            const int row = (((blk * p.num_layers + p.layer) * 2 + kind) * p.kv_heads + g) * 16;
+            tma_load_2d(st + (kind * 2 + half) * 8192 + j * 2048, &tmKV, &kv_full[s2], half * 64, row);
         }
     };
 
-    int issued = 0;   // control lane 0: tiles whose loads were issued
-    int nb_next = 0;  // control lanes 0..3: block ids of the next tile to load
+    int issued = 0;   // TMA lane 0: tiles whose loads were issued
+    int nb_next = 0;  // TMA lanes 0..3: block ids (as read) of the next tile to load
     if (t == 0) {
         for (int s2 = 0; s2 < kPfuStages; ++s2) mbar_init(&kv_full[s2], 1);
         mbar_init(&s_full[0], 1);
@@ -1541,18 +1585,16 @@ __global__ void __launch_bounds__(kPfuThreads, 1) paged_prefill_umma_kernel(cons
         fence_mbar_init();
     }
     __syncthreads();
-    if (ctrl) {
+    if (mma_w) {
         tmem_alloc(tmem_slot, 256);
         tmem_relinquish();
+    } else if (tma_w) {
         if (lane == 0) tma_prefetch_desc(&tmKV);
-        // the first two tiles' loads; tile 2's block ids stay in lanes 0..3
-        for (int tile = 0; tile < 2 && tile < ntiles; ++tile) {
-            int blk[4];
-            gather(lane < 4 ? tile_block(tile, lane) : 0, blk);
-            if (lane == 0) issue(tile, blk);
-        }
-        issued = min(ntiles, 2);
-        nb_next = (lane < 4 && 2 < ntiles) ? tile_block(2, lane) : 0;
+        // the first two tiles' loads; the third's block ids stay in lanes 0..3
+        for (int li = 0; li < 2 && li < nt; ++li)
+            issue(li, lane < 4 ? checked(tile_block_raw(t0 + li, lane)) : 0, true);
+        issued = min(nt, 2);
+        nb_next = (lane < 4 && 2 < nt) ? tile_block_raw(t0 + 2, lane) : 0;
     } else {
         // ---- Q rows (x scale_log2) as an fp16 hi/lo pair: this thread's half of the dims
         const float4* qp = reinterpret_cast<const float4*>(p.q + out_row * D + ch * 64);
@@ -1580,15 +1622,16 @@ __global__ void __launch_bounds__(kPfuThreads, 1) paged_prefill_umma_kernel(cons
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-    const uint32_t idesc_s = make_idesc_f16(128, kPfuKeys), idesc_o = make_idesc_f16(128, D);
+    // O's B operand (V) is MN-major: bit 16 of the instruction descriptor
+    const uint32_t idesc_s = make_idesc_f16(128, kPfuKeys), idesc_o = make_idesc_f16(128, D) | (1u << 16);
 
-    // control lane 0: S(tile) = Q K^T into buffer tile & 1, once the tile's K has landed
-    auto issue_s = [&](int tile) -> bool {
-        if (!mbar_wait(&kv_full[tile % kPfuStages], (uint32_t)(tile / kPfuStages) & 1u, DEV_ERR_ATTN_WAIT))
+    // UMMA lane 0: S of local tile li = Q K^T into buffer li & 1, once the tile's K has landed
+    auto issue_s = [&](int li) -> bool {
+        if (!mbar_wait(&kv_full[li % kPfuStages], (uint32_t)(li / kPfuStages) & 1u, DEV_ERR_ATTN_WAIT))
             return false;
         tc_fence_after();
-        const uint32_t st = smem_u32(smem + L::RING + (tile % kPfuStages) * L::STAGE);
-        const uint32_t d = tmem + ((tile & 1) ? 192u : 0u);
+        const uint32_t st = smem_u32(smem + L::RING + (li % kPfuStages) * L::STAGE);
+        const uint32_t d = tmem + ((li & 1) ? 192u : 0u);
 #pragma unroll
         for (int part = 0; part < 2; ++part) {
             const uint32_t qb = smem_u32(smem + (part ? L::QL : L::QH));
@@ -1599,67 +1642,76 @@ __global__ void __launch_bounds__(kPfuThreads, 1) paged_prefill_umma_kernel(cons
                     umma_bf16(d, make_sw128_desc(qb + hd * 16384) + 2 * kk, make_sw128_desc(st + hd * 8192) + 2 * kk,
                               idesc_s, (part | hd | kk) ? 1u : 0u);
         }
-        umma_commit(&s_full[tile & 1]);
+        umma_commit(&s_full[li & 1]);
         return true;
     };
-    // control lane 0: O (+)= P V of the tile whose P and V^T are in shared memory
-    auto issue_pv = [&](int tile) {
+    // UMMA lane 0: O (+)= P V of the tile whose P is in shared memory (V in its stage; a
+    // K step of 16 keys is two 8-row groups, 2048 B)
+    auto issue_pv = [&](int li) {
+        const uint32_t vb = smem_u32(smem + L::RING + (li % kPfuStages) * L::STAGE) + 2 * 8192;
 #pragma unroll
         for (int part = 0; part < 2; ++part) {
             const uint32_t pb = smem_u32(smem + (part ? L::PL : L::PH));
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
-                umma_bf16(tmem + 64u, make_sw128_desc(pb) + 2 * kk, make_sw128_desc(smem_u32(smem + L::VT)) + 2 * kk,
-                          idesc_o, (tile > 0 || part > 0 || kk > 0) ? 1u : 0u);
+                umma_bf16(tmem + 64u, make_sw128_desc(pb) + 2 * kk, make_sw128_mn_desc(vb + kk * 2048, 8192), idesc_o,
+                          (li > 0 || part > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(pv_done);
     };
 
     bool fail = false;  // this thread saw a wait run out; the CTA leaves the loop together
-    if (ctrl && lane == 0) fail = !issue_s(0);
+    if (mma_w && lane == 0) fail = !issue_s(0);
     float m_ref = -INFINITY, l = 0.f;
-    int i = 0;
-    // Window i (between two CTA barriers): the softmax warps turn S(i) into P(i) and V(i) into
-    // V^T; the control warp issues PV(i - 1), the loads of tile i + 2 (into the stage tile i - 1
-    // left) and S(i + 1) (into the S buffer tile i - 1 left).
-    for (; i < ntiles; ++i) {
-        if (ctrl) {
-            if (lane == 0 && !fail && i > 0) issue_pv(i - 1);
-            if (i + 2 < ntiles) {
-                int blk[4];
-                gather(nb_next, blk);
-                nb_next = (lane < 4 && i + 3 < ntiles) ? tile_block(i + 3, lane) : 0;
-                if (lane == 0 && !fail) {
-                    issue(i + 2, blk);
-                    ++issued;
-                }
+    int li = 0;
+    // Window li (between two CTA barriers; local tile li = tile t0 + li): the softmax warps turn
+    // S(li) into P(li); the UMMA warp issues PV(li - 1) and S(li + 1) (into the S buffer li - 1
+    // left) back to back; the TMA warp issues the loads of li + 2 (into the stage of li - 2, whose
+    // PV the softmax warps saw finish in window li - 1) and reads the block ids of li + 3.
+    for (; li < nt; ++li) {
+        const int i = t0 + li;  // the tile: keys 64 i .. 64 i + 63
+        if (mma_w) {
+            PFU_STAMP(0, 0);
+            if (lane == 0 && !fail && li > 0) issue_pv(li - 1);
+            PFU_STAMP(0, 1);
+            if (lane == 0 && !fail && li + 1 < nt) fail = !issue_s(li + 1);
+            __syncwarp();
+            PFU_STAMP(0, 2);
+        } else if (tma_w) {
+            if (li + 2 < nt) {
+                issue(li + 2, lane < 4 ? checked(nb_next) : 0, true);
+                if (lane == 0) ++issued;
+                nb_next = (lane < 4 && li + 3 < nt) ? tile_block_raw(i + 3, lane) : 0;
             }
-            if (lane == 0 && !fail && i + 1 < ntiles) fail = !issue_s(i + 1);
             __syncwarp();
         } else {
+            PFU_STAMP(1, 0);
             // ---- this thread's 32 scores of tile i
-            fail |= !mbar_wait(&s_full[i & 1], (uint32_t)(i >> 1) & 1u, DEV_ERR_ATTN_WAIT);
+            fail |= !mbar_wait(&s_full[li & 1], (uint32_t)(li >> 1) & 1u, DEV_ERR_ATTN_WAIT);
             __syncwarp();
             tc_fence_after();
+            PFU_STAMP(1, 1);
             float sv[32];
-            tmem_ld32(tmem + lane_base + ((i & 1) ? 192u : 0u) + (uint32_t)(ch * 32), sv);
+            tmem_ld32(tmem + lane_base + ((li & 1) ? 192u : 0u) + (uint32_t)(ch * 32), sv);
+            PFU_STAMP(1, 2);
             const int lim = ctx_row - (i * kPfuKeys + ch * 32);  // keys of the row in this half-tile
-            float mt = -INFINITY;
+            if (lim < 32)
 #pragma unroll
-            for (int k = 0; k < 32; ++k) {
-                sv[k] = k < lim ? sv[k] : -INFINITY;
-                mt = fmaxf(mt, sv[k]);
-            }
+                for (int k = 0; k < 32; ++k) sv[k] = k < lim ? sv[k] : -INFINITY;
+            float mt = sv[0];
+#pragma unroll
+            for (int k = 1; k < 32; ++k) mt = fmaxf(mt, sv[k]);
             xch[ch * 128 + row] = mt;
             pair_sync(warp);
             mt = fmaxf(mt, xch[(ch ^ 1) * 128 + row]);
+            PFU_STAMP(1, 3);
             float alpha = 1.f;
             bool rescale = false;
             if (mt != -INFINITY) {
                 if (m_ref == -INFINITY) {
                     m_ref = mt;
                 } else if (mt > m_ref + 8.f) {
-                    alpha = exp2f(m_ref - mt);
+                    alpha = ex2_approx(m_ref - mt);
                     l *= alpha;
                     m_ref = mt;
                     rescale = true;
@@ -1671,14 +1723,16 @@ __global__ void __launch_bounds__(kPfuThreads, 1) paged_prefill_umma_kernel(cons
             float psum = 0.f;
 #pragma unroll
             for (int k = 0; k < 16; ++k) {
-                const float a = exp2f(sv[2 * k] - m_use), b2 = exp2f(sv[2 * k + 1] - m_use);
+                const float a = ex2_approx(sv[2 * k] - m_use), b2 = ex2_approx(sv[2 * k + 1] - m_use);
                 psum += a + b2;
                 split_h2(a, b2, ph[k], pl[k]);
             }
             l += psum;
-            if (i > 0) fail |= !mbar_wait(pv_done, (uint32_t)(i - 1) & 1u, DEV_ERR_ATTN_WAIT);
+            PFU_STAMP(1, 4);
+            if (li > 0) fail |= !mbar_wait(pv_done, (uint32_t)(li - 1) & 1u, DEV_ERR_ATTN_WAIT);
             __syncwarp();
             tc_fence_after();
+            PFU_STAMP(1, 5);
             if (__any_sync(0xffffffffu, rescale)) {  // warp-collective TMEM read-modify-write of O
 #pragma unroll 1
                 for (int c = 0; c < 64; c += 16) {
@@ -1698,28 +1752,18 @@ __global__ void __launch_bounds__(kPfuThreads, 1) paged_prefill_umma_kernel(cons
                 *reinterpret_cast<uint4*>(smem + L::PL + off) =
                     make_uint4(pl[4 * c], pl[4 * c + 1], pl[4 * c + 2], pl[4 * c + 3]);
             }
-            // ---- V^T [128 dims][64 keys] from the stage's V halves: 8x8 blocks, ldmatrix.trans -> stmatrix
-            const uint32_t st = smem_u32(smem + L::RING + (i % kPfuStages) * L::STAGE);
-            const int mi = lane >> 3, rr = lane & 7;
-#pragma unroll
-            for (int it = 0; it < 4; ++it) {
-                const int bidx = (warp * 4 + it) * 4 + mi;  // 128 blocks: key block kb, dim block db
-                const int kb = bidx & 7, db = bidx >> 3;
-                const uint32_t src = st + 2 * 8192 + (uint32_t)(db >> 3) * 8192 + sw128_off(kb * 8 + rr, (db & 7) * 8);
-                uint32_t v4[4];
-                ldsm_x4_t(src, v4);
-                // register j holds matrix j (block (warp * 4 + it) * 4 + j): V^T's row lane / 4,
-                // keys 2 (lane % 4) and + 1.  Keys past the group's last key read whatever the
-                // pool holds there; they are zeroed so that P = 0 meets a finite V.
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int key = i * kPfuKeys + (((warp * 4 + it) * 4 + j) & 7) * 8 + 2 * (lane & 3);
-                    if (key >= ctx_max) v4[j] = 0u;
-                    else if (key + 1 >= ctx_max) v4[j] &= 0xffffu;
+            // ---- the last tile's keys past the group's last one read whatever the pool holds
+            // there: their V rows are zeroed so that P = 0 meets a finite V
+            const int first_stale = ctx_max - i * kPfuKeys;
+            if (i == ntiles - 1 && first_stale < kPfuKeys) {
+                fail |= !mbar_wait(&kv_full[li % kPfuStages], (uint32_t)(li / kPfuStages) & 1u, DEV_ERR_ATTN_WAIT);
+                uint8_t* vst = smem + L::RING + (li % kPfuStages) * L::STAGE + 2 * 8192;
+                for (int c = t; c < (kPfuKeys - first_stale) * 16; c += kPfuSoftmaxWarps * 32) {
+                    const int key = first_stale + (c >> 4), half = (c >> 3) & 1, chunk = c & 7;
+                    *reinterpret_cast<uint4*>(vst + half * 8192 + key * 128 + chunk * 16) = make_uint4(0u, 0u, 0u, 0u);
                 }
-                // lane 8 mi + rr addresses row rr of matrix mi, the same block it loaded
-                stsm_x4(smem_u32(smem + L::VT) + sw128_off(db * 8 + rr, kb * 8), v4);
             }
+            PFU_STAMP(1, 6);
         }
         fence_proxy_async_smem();
         tc_fence_before();
@@ -1730,16 +1774,25 @@ __global__ void __launch_bounds__(kPfuThreads, 1) paged_prefill_umma_kernel(cons
             break;
         }
     }
-    if (ctrl && lane == 0 && !fail) issue_pv(ntiles - 1);
+    if (mma_w && lane == 0 && !fail) issue_pv(nt - 1);
     if (!ctrl) {
-        // ---- O / l -> out (bf16 hi/lo), after the last PV; the pair adds its halves of l
-        const bool good = !fail && mbar_wait(pv_done, (uint32_t)(ntiles - 1) & 1u, DEV_ERR_ATTN_WAIT);
+        // ---- after the last PV: O / l -> out (bf16 hi/lo) with one split, else O, the max and
+        // the sum -> this split's partial (max -inf: no keys of the row here); the pair adds its
+        // halves of l
+        const bool good = !fail && mbar_wait(pv_done, (uint32_t)(nt - 1) & 1u, DEV_ERR_ATTN_WAIT);
         __syncwarp();
         tc_fence_after();
         xch[ch * 128 + row] = l;
         pair_sync(warp);
         const float l_row = l + xch[(ch ^ 1) * 128 + row];
-        const float inv = (good && l_row > 0.f) ? 1.f / l_row : 0.f;
+        const bool final_out = nsplit == 1;
+        const bool has_keys = good && m_ref != -INFINITY;
+        const bool partial = !final_out && has_keys;  // its O goes to the workspace
+        const float inv = final_out ? ((good && l_row > 0.f) ? 1.f / l_row : 0.f) : 1.f;
+        if (row_ok && !final_out && ch == 0) {
+            p.ws_ml[part_row * 2 + 0] = has_keys ? m_ref : -INFINITY;
+            p.ws_ml[part_row * 2 + 1] = has_keys ? l_row : 0.f;
+        }
 #pragma unroll 1
         for (int c = 0; c < 64; c += 16) {
             float v[16];
@@ -1747,7 +1800,12 @@ __global__ void __launch_bounds__(kPfuThreads, 1) paged_prefill_umma_kernel(cons
             if (!good)
 #pragma unroll
                 for (int k = 0; k < 16; ++k) v[k] = 0.f;
-            if (row_ok) {
+            if (row_ok && partial) {
+                float4* wo = reinterpret_cast<float4*>(p.ws_o + part_row * D + ch * 64 + c);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) wo[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+            }
+            if (row_ok && final_out) {
                 uint32_t hw[8], lw[8];
 #pragma unroll
                 for (int k = 0; k < 8; ++k) {
@@ -1770,14 +1828,72 @@ __global__ void __launch_bounds__(kPfuThreads, 1) paged_prefill_umma_kernel(cons
         }
     } else if (lane == 0 && fail) {
         // after a failure: the loads in flight land and every UMMA finishes before TMEM is released
-        for (int j = issued > kPfuStages ? issued - kPfuStages : 0; j < issued; ++j)
-            mbar_wait(&kv_full[j % kPfuStages], (uint32_t)(j / kPfuStages) & 1u, DEV_ERR_DRAIN);
-        umma_commit(drain);
-        mbar_wait(drain, 0, DEV_ERR_DRAIN);
+        if (tma_w)
+            for (int j = issued > kPfuStages ? issued - kPfuStages : 0; j < issued; ++j)
+                mbar_wait(&kv_full[j % kPfuStages], (uint32_t)(j / kPfuStages) & 1u, DEV_ERR_DRAIN);
+        if (mma_w) {
+            umma_commit(drain);
+            mbar_wait(drain, 0, DEV_ERR_DRAIN);
+        }
     }
     tc_fence_before();
     __syncthreads();
-    if (ctrl) tmem_dealloc(tmem, 256);
+    if (mma_w) tmem_dealloc(tmem, 256);
+}
+
+
+// Folds the key splits of paged_prefill_umma_kernel: one warp per (row, q head), lane d4 owns
+// dims 4 d4 .. 4 d4 + 3; a partial whose max is -inf holds no keys and is skipped.
+__global__ void __launch_bounds__(128) prefill_combine_kernel(const AttnParams p) {
+    constexpr int D = 128;
+    griddep_wait();
+    griddep_launch();
+    const int pair = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (pair >= p.R * p.num_heads) return;
+    const int k = p.max_splits;
+    const float* ml = p.ws_ml + (size_t)pair * k * 2;
+    float M = -INFINITY;
+    for (int s2 = 0; s2 < k; ++s2) M = fmaxf(M, ml[2 * s2]);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float lsum = 0.f;
+    if (M != -INFINITY)
+        for (int s2 = 0; s2 < k; ++s2) {
+            const float ms = ml[2 * s2];
+            if (ms == -INFINITY) continue;
+            const float f = exp2f(ms - M);
+            const float4 o = reinterpret_cast<const float4*>(p.ws_o + ((size_t)pair * k + s2) * D)[lane];
+            acc.x += o.x * f;
+            acc.y += o.y * f;
+            acc.z += o.z * f;
+            acc.w += o.w * f;
+            lsum += ml[2 * s2 + 1] * f;
+        }
+    const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+    const float v[4] = {acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv};
+    uint32_t hw[2], lw[2];
+#pragma unroll
+    for (int k2 = 0; k2 < 2; ++k2) {
+        const __nv_bfloat162 hb = __floats2bfloat162_rn(v[2 * k2], v[2 * k2 + 1]);
+        const float2 hf = __bfloat1622float2(hb);
+        const __nv_bfloat162 lb = __floats2bfloat162_rn(v[2 * k2] - hf.x, v[2 * k2 + 1] - hf.y);
+        hw[k2] = *reinterpret_cast<const uint32_t*>(&hb);
+        lw[k2] = *reinterpret_cast<const uint32_t*>(&lb);
+    }
+    reinterpret_cast<uint2*>(p.out + (size_t)pair * D)[lane] = make_uint2(hw[0], hw[1]);
+    if (p.out_lo) reinterpret_cast<uint2*>(p.out_lo + (size_t)pair * D)[lane] = make_uint2(lw[0], lw[1]);
+}
+
+// Key splits of the tcgen05 prefill: with fewer (stream, group, kv head) CTAs than half the SMs,
+// each group's tiles are shared by up to floor(SMs / CTAs) CTAs (at most the workspace's
+// max_splits and kPfuMaxSplits; QTTS_PREFILL_SPLITS caps it, 1 = never split).
+constexpr int kPfuMaxSplits = 16;
+inline int prefill_umma_split_cap() {
+    static const int c = [] {
+        const char* v = getenv("QTTS_PREFILL_SPLITS");
+        const int x = (v && *v) ? atoi(v) : kPfuMaxSplits;
+        return (x >= 1 && x <= kPfuMaxSplits) ? x : kPfuMaxSplits;
+    }();
+    return c;
 }
 
 inline int launch_prefill_umma(const AttnParams& p, cudaStream_t st) {
@@ -1786,8 +1902,16 @@ inline int launch_prefill_umma(const AttnParams& p, cudaStream_t st) {
     if (rc) return rc;
     QTTS_CHECK_CUDA((func_attr_once<paged_prefill_umma_kernel>(PfuLayout::SMEM)));
     const int n_groups = (p.rows_per_stream + kPfuQ - 1) / kPfuQ;
-    const int ctas = (p.R / p.rows_per_stream) * n_groups * p.kv_heads;
-    QTTS_LAUNCH(paged_prefill_umma_kernel, dim3(ctas), dim3(kPfuThreads), PfuLayout::SMEM, st, map, p);
+    const int base = (p.R / p.rows_per_stream) * n_groups * p.kv_heads;
+    const int sms = num_sms();
+    int k = 1;
+    const bool ws_ok = p.ws_o && p.ws_ml && (reinterpret_cast<uintptr_t>(p.ws_o) & 15) == 0;
+    if (ws_ok && 2 * base <= sms) k = min(min(sms / base, p.max_splits), prefill_umma_split_cap());
+    AttnParams q = p;
+    q.max_splits = k > 1 ? k : 1;  // the workspace stride: k partials per (row, q head)
+    QTTS_LAUNCH(paged_prefill_umma_kernel, dim3(base * q.max_splits), dim3(kPfuThreads), PfuLayout::SMEM, st, map, q);
+    if (q.max_splits > 1)
+        QTTS_LAUNCH(prefill_combine_kernel, dim3(ceil_div(q.R * q.num_heads, 4)), dim3(128), 0, st, q);
     return QTTS_OK;
 }
 

@@ -228,15 +228,16 @@ def test_paged_prefill_attention_query_tiles(split):
 
 
 @pytest.mark.skipif(os.environ.get("QTTS_PREFILL_UMMA") == "0", reason="query-tile form reads stale tails")
-def test_paged_prefill_long_chunks_stale_tail():
+@pytest.mark.parametrize("pasts", [[0, 700, 33, 64], [700]], ids=["4streams", "1stream_splits"])
+def test_paged_prefill_long_chunks_stale_tail(pasts):
     """Chunked prefill past one 64-query group (S = 150: groups of 64, 64 and 22 queries) with
     pasts that start mid-block and up to 850 keys, against an fp32 torch statement.  Every pool
     entry the streams do not own, and the tail of each stream's last block past its last key,
     holds NaN: keys past a row's count must contribute exactly nothing (the tcgen05 form zeroes
-    V past the group's keys before P . V)."""
+    V past the group's keys before P . V).  One stream gives 24 (group, kv head) CTAs, so the
+    tcgen05 form splits each group's keys over several CTAs and folds them in a second kernel."""
     D, Hkv, Hq, L, layer, nb, mbps = 128, 8, 16, 2, 0, 400, 64
     S = 150
-    pasts = [0, 700, 33, 64]
     n = len(pasts)
     g = _gen(35)
     kv = torch.full((nb, L, 2, Hkv, 16, D), float("nan"), dtype=torch.float16)
@@ -291,8 +292,24 @@ def test_prefill_query_tile_form():
 
     env = dict(os.environ, QTTS_PREFILL_UMMA="0")
     r = subprocess.run([sys.executable, "-m", "pytest", "-x", "-q", "-m", "gpu", "-p", "no:cacheprovider", "-k",
-                        "prefill and not tile_form", os.path.abspath(__file__)], env=env, capture_output=True,
-                       text=True, timeout=900)
+                        "prefill and not tile_form and not without_splits", os.path.abspath(__file__)], env=env,
+                       capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
+
+
+@pytest.mark.skipif(os.environ.get("QTTS_PREFILL_UMMA") is not None or os.environ.get("QTTS_PREFILL_SPLITS")
+                    is not None, reason="already a forced run")
+def test_prefill_umma_without_splits():
+    """The tcgen05 prefill splits a group's keys over several CTAs when the grid is small
+    (QTTS_PREFILL_SPLITS caps the count, read once per process): rerun the prefill tests in a
+    child process with splitting off, so both the split and the one-CTA forms are covered."""
+    import subprocess
+    import sys
+
+    env = dict(os.environ, QTTS_PREFILL_SPLITS="1")
+    r = subprocess.run([sys.executable, "-m", "pytest", "-x", "-q", "-m", "gpu", "-p", "no:cacheprovider", "-k",
+                        "prefill and not tile_form and not without_splits", os.path.abspath(__file__)], env=env,
+                       capture_output=True, text=True, timeout=900)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
 
 
