@@ -70,7 +70,9 @@ def bench_attention(rows: int, ctx_mean: int, launches: int, layers: int = 4, se
         s.synchronize()
     sec = e0.elapsed_time(e1) / 1e3 / launches
     algo = int(ctx.sum()) * 2 * 8 * 128 * 2 + rows * 16 * 128 * (4 + 4)
-    return {"kernel": "paged_attn_tc_kernel", "split_blocks": split or 16, "rows": rows, "ctx_sum": int(ctx.sum()), "launch_us": sec * 1e6,
+    rows_form = os.environ.get("QTTS_ATTN_ROWS") != "0"
+    kernel = "paged_attn_tc_row_kernel (CTA per row x kv head)" if rows_form else "paged_attn_tc_kernel + combine"
+    return {"kernel": kernel, "split_blocks": split or 16, "rows": rows, "ctx_sum": int(ctx.sum()), "launch_us": sec * 1e6,
             "algorithmic_bytes": algo, "achieved_gbs": algo / sec / 1e9}
 
 
