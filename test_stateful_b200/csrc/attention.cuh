@@ -695,10 +695,14 @@ __global__ void __launch_bounds__(W * 32) paged_attn_tc_row_kernel(const __grid_
     }
     __syncwarp();
 
-    auto issue = [&](int i) {
+    // the table entry of this warp's block i (lane 0 reads the next one while a block is worked
+    // on, so the read's latency stays off the refill)
+    auto raw_block = [&](int i) -> int {
         const int jb = warp + W * i;
+        return jb < p.mbps ? p.block_table[(size_t)slot * p.mbps + jb] : -1;
+    };
+    auto issue = [&](int i, int blk) {
         const int s2 = i % S;
-        int blk = jb < p.mbps ? p.block_table[(size_t)slot * p.mbps + jb] : -1;
         if (blk < 0 || blk >= p.num_blocks) {
             record_error(DEV_ERR_ATTN_WAIT);
             blk = 0;  // stay in bounds; the error word reports the bad table entry
@@ -714,9 +718,11 @@ __global__ void __launch_bounds__(W * 32) paged_attn_tc_row_kernel(const __grid_
     };
 
     int issued = 0;
+    int next_raw = -1;  // lane 0: table entry of block `issued`
     if (lane == 0) {
-        for (int i = 0; i < n_mine && i < S; ++i) issue(i);
+        for (int i = 0; i < n_mine && i < S; ++i) issue(i, raw_block(i));
         issued = min(n_mine, S);
+        if (issued < n_mine) next_raw = raw_block(issued);
     }
     issued = __shfl_sync(0xffffffffu, issued, 0);
 
@@ -741,14 +747,19 @@ __global__ void __launch_bounds__(W * 32) paged_attn_tc_row_kernel(const __grid_
         const uint32_t vb = kb + 2 * kTcBox;
         const int jb = warp + W * i;
 
-        float sc[4] = {0.f, 0.f, 0.f, 0.f};
+        // four independent accumulator chains (hi / lo x even / odd k-slices), summed at the end:
+        // the 16 MMAs of a block would otherwise wait on one another
+        float sc4[4][4] = {};
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
             uint32_t a[4];
             ldsm_x4(tc_sw128(kb, k_tok, 16 * ks + k_dim), a);
-            mma_16816(sc, a, qh[ks][0], qh[ks][1]);
-            mma_16816(sc, a, ql[ks][0], ql[ks][1]);
+            mma_16816(sc4[ks & 1], a, qh[ks][0], qh[ks][1]);
+            mma_16816(sc4[2 + (ks & 1)], a, ql[ks][0], ql[ks][1]);
         }
+        float sc[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sc[e] = (sc4[0][e] + sc4[1][e]) + (sc4[2][e] + sc4[3][e]);
         const int tA = jb * 16 + gq, tB = tA + 8;
         const float s00 = tA < ctx ? sc[0] : -INFINITY, s01 = tA < ctx ? sc[1] : -INFINITY;
         const float s10 = tB < ctx ? sc[2] : -INFINITY, s11 = tB < ctx ? sc[3] : -INFINITY;
@@ -808,8 +819,9 @@ __global__ void __launch_bounds__(W * 32) paged_attn_tc_row_kernel(const __grid_
         __syncwarp();
         if (lane == 0 && i + S < n_mine) {
             fence_proxy_async_smem();
-            issue(i + S);
+            issue(i + S, next_raw);
             ++issued;
+            if (issued < n_mine) next_raw = raw_block(issued);
         }
         issued = __shfl_sync(0xffffffffu, issued, 0);
     }
