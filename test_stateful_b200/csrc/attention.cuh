@@ -476,15 +476,18 @@ __global__ void __launch_bounds__(128) paged_attn_tc_kernel(const __grid_constan
         const uint32_t vb = kb + 2 * kTcBox;
         const int jb = b_start + i;
 
-        // ---- S^T = K Q^T
-        float sc[4] = {0.f, 0.f, 0.f, 0.f};
+        // ---- S^T = K Q^T, four independent accumulator chains (hi / lo x even / odd k-slices)
+        float sc4[4][4] = {};
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
             uint32_t a[4];
             ldsm_x4(tc_sw128(kb, k_tok, 16 * ks + k_dim), a);
-            mma_16816(sc, a, qh[ks][0], qh[ks][1]);
-            mma_16816(sc, a, ql[ks][0], ql[ks][1]);
+            mma_16816(sc4[ks & 1], a, qh[ks][0], qh[ks][1]);
+            mma_16816(sc4[2 + (ks & 1)], a, ql[ks][0], ql[ks][1]);
         }
+        float sc[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sc[e] = (sc4[0][e] + sc4[1][e]) + (sc4[2][e] + sc4[3][e]);
         // lanes with qq == 0: sc[0] = (tok gq, head 0), sc[1] = (tok gq, head 1), sc[2], sc[3] = tok gq + 8
         const int tA = jb * 16 + gq, tB = tA + 8;
         const float s00 = tA < ctx ? sc[0] : -INFINITY, s01 = tA < ctx ? sc[1] : -INFINITY;
@@ -874,11 +877,14 @@ __global__ void __launch_bounds__(W * 32) paged_attn_tc_row_kernel(const __grid_
     }
 }
 
-// warps per (row, kv head) CTA of the row form (QTTS_ATTN_ROW_WARPS: 4 or 8)
+// warps per (row, kv head) CTA of the row form (QTTS_ATTN_ROW_WARPS: 2, 3, 4 or 8).  Three
+// with the default 2-stage rings (52 KB of shared memory) keep 4 CTAs on an SM, so the 512 CTAs
+// of a 64-row step fit in one wave; four (69 KB) fit only 3 per SM.
 inline int attn_row_warps() {
     static const int w = [] {
         const char* v = getenv("QTTS_ATTN_ROW_WARPS");
-        return (v && atoi(v) == 8) ? 8 : 4;
+        const int x = v ? atoi(v) : 3;
+        return (x == 2 || x == 4 || x == 8) ? x : 3;
     }();
     return w;
 }
@@ -897,7 +903,12 @@ inline int launch_attention_tc_rows_w(const AttnParams& p, cudaStream_t st) {
 
 template <int S>
 inline int launch_attention_tc_rows(const AttnParams& p, cudaStream_t st) {
-    return attn_row_warps() == 8 ? launch_attention_tc_rows_w<S, 8>(p, st) : launch_attention_tc_rows_w<S, 4>(p, st);
+    switch (attn_row_warps()) {
+        case 2: return launch_attention_tc_rows_w<S, 2>(p, st);
+        case 4: return launch_attention_tc_rows_w<S, 4>(p, st);
+        case 8: return launch_attention_tc_rows_w<S, 8>(p, st);
+        default: return launch_attention_tc_rows_w<S, 3>(p, st);
+    }
 }
 
 // head_dim 128 decode attention as one CTA per (row, kv head), no split partials or combine
@@ -1246,17 +1257,21 @@ __global__ void __launch_bounds__(128) paged_prefill_tc_kernel(const __grid_cons
         const uint32_t vb = kb + 2 * kTcBox;
         const int jb = b_start + i;
 
-        // ---- S = Q K^T: two 8-key n-tiles
-        float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        // ---- S = Q K^T: two 8-key n-tiles, hi and lo in separate accumulator chains
+        float sc[2][4] = {}, sl[2][4] = {};
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
             uint32_t kf[4];
             ldsm_x4(tc_sw128(kb, kb_key, 16 * ks + kb_dim), kf);
             mma_16816(sc[0], qh[ks], kf[0], kf[1]);
-            mma_16816(sc[0], ql[ks], kf[0], kf[1]);
+            mma_16816(sl[0], ql[ks], kf[0], kf[1]);
             mma_16816(sc[1], qh[ks], kf[2], kf[3]);
-            mma_16816(sc[1], ql[ks], kf[2], kf[3]);
+            mma_16816(sl[1], ql[ks], kf[2], kf[3]);
         }
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) sc[nt][e] += sl[nt][e];
         // sc[nt][0,1] = (head 0, keys 16 jb + 8 nt + 2 qq, +1), sc[nt][2,3] = head 1, same keys
         float bm0 = -INFINITY, bm1 = -INFINITY;
 #pragma unroll
