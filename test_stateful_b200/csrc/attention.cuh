@@ -46,6 +46,9 @@ struct AttnParams {
                       // stream, so a kernel may read them before waiting on its predecessor
     int rows_per_stream;  // chunked prefill: rows come as R / rows_per_stream streams of this many
                           // consecutive query tokens (0 or 1: independent rows)
+    int meta_settled;  // decode rows whose row_slot / row_ctx / block_table and every key but each
+                       // row's newest were written at least two launches earlier: the row kernel
+                       // reads them and starts its first loads before waiting on its predecessor
 };
 
 // Ring depth per warp (QTTS_ATTN_STAGES, default below): 3 stages x 8 KB x 4
@@ -652,16 +655,23 @@ __global__ void __launch_bounds__(W * 32) paged_attn_tc_row_kernel(const __grid_
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gq = lane >> 2, qq = lane & 3;  // mma fragment coordinates
-    griddep_wait();
-    griddep_launch();
+    const bool early = p.meta_settled != 0;  // metadata and past keys may be read before the wait
+    if (!early) {
+        griddep_wait();
+        griddep_launch();
+    }
     const int g = blockIdx.x % p.kv_heads;  // CTA-uniform
     const int r = blockIdx.x / p.kv_heads;
     if (r >= p.R) return;
-    const int ctx = p.row_ctx[r];
+    const int ctx = __ldcg(p.row_ctx + r);
     const int nbt = (ctx + 15) >> 4;
     const size_t hrow0 = (size_t)r * p.num_heads + g * 2;
-    const int slot = p.row_slot[r];
+    const int slot = __ldcg(p.row_slot + r);
     if (nbt <= 0 || slot < 0) {  // CTA-uniform: a row with no keys (only after a scheduler error)
+        if (early) {
+            griddep_wait();
+            griddep_launch();
+        }
         for (int i = threadIdx.x; i < 2 * D; i += W * 32) {
             p.out[hrow0 * D + i] = __float2bfloat16(0.f);
             if (p.out_lo) p.out_lo[hrow0 * D + i] = __float2bfloat16(0.f);
@@ -669,6 +679,59 @@ __global__ void __launch_bounds__(W * 32) paged_attn_tc_row_kernel(const __grid_
         return;
     }
     const int n_mine = warp < nbt ? (nbt - warp + W - 1) / W : 0;  // blocks warp, warp + W, ...
+
+    uint8_t* wbuf = smem + warp * S * kTcStage;
+    uint64_t* wbar = bars + warp * S;
+    if (lane == 0) {
+        for (int s2 = 0; s2 < S; ++s2) mbar_init(&wbar[s2], 1);
+        tma_prefetch_desc(&tmKV);
+        fence_mbar_init();
+    }
+    __syncwarp();
+
+    // the table entry of this warp's block i (lane 0 reads the next one while a block is worked
+    // on, so the read's latency stays off the refill)
+    auto raw_block = [&](int i) -> int {
+        const int jb = warp + W * i;
+        return jb < p.mbps ? __ldcg(p.block_table + (size_t)slot * p.mbps + jb) : -1;
+    };
+    auto issue = [&](int i, int blk) {
+        const int s2 = i % S;
+        if (blk < 0 || blk >= p.num_blocks) {
+            record_error(DEV_ERR_ATTN_WAIT);
+            blk = 0;  // stay in bounds; the error word reports the bad table entry
+        }
+        const int krow = (((blk * p.num_layers + p.layer) * 2 + 0) * p.kv_heads + g) * 16;
+        const int vrow = krow + p.kv_heads * 16;
+        uint8_t* dst = wbuf + s2 * kTcStage;
+        mbar_arrive_expect_tx(&wbar[s2], kTcStage);
+        tma_load_2d(dst, &tmKV, &wbar[s2], 0, krow);
+        tma_load_2d(dst + kTcBox, &tmKV, &wbar[s2], 64, krow);
+        tma_load_2d(dst + 2 * kTcBox, &tmKV, &wbar[s2], 0, vrow);
+        tma_load_2d(dst + 3 * kTcBox, &tmKV, &wbar[s2], 64, vrow);
+    };
+
+    // the first S loads; with settled metadata they go out before the wait on the preceding
+    // kernel (the QKV projection), except the block holding the row's newest key, which that
+    // kernel writes
+    int issued = 0;
+    int next_raw = -1;  // lane 0: table entry of block `issued`
+    int deferred = -1;  // lane 0: the first-S block that waits for the preceding kernel
+    if (lane == 0) {
+        const int newest = (ctx - 1) >> 4;
+        for (int i = 0; i < n_mine && i < S; ++i) {
+            if (early && warp + W * i == newest) deferred = i;
+            else issue(i, raw_block(i));
+        }
+        issued = min(n_mine, S);
+        if (issued < n_mine) next_raw = raw_block(issued);
+    }
+    issued = __shfl_sync(0xffffffffu, issued, 0);
+    if (early) {
+        griddep_wait();
+        griddep_launch();
+        if (lane == 0 && deferred >= 0) issue(deferred, raw_block(deferred));
+    }
 
     // Q^T fragments (B operand): lane (gq, qq) holds head gq's dims 16s + 2qq (+1) and +8 (+9)
     uint32_t qh[8][2], ql[8][2];
@@ -688,46 +751,6 @@ __global__ void __launch_bounds__(W * 32) paged_attn_tc_row_kernel(const __grid_
             split_h2(v[2], v[3], qh[s2][1], ql[s2][1]);
         }
     }
-
-    uint8_t* wbuf = smem + warp * S * kTcStage;
-    uint64_t* wbar = bars + warp * S;
-    if (lane == 0) {
-        for (int s2 = 0; s2 < S; ++s2) mbar_init(&wbar[s2], 1);
-        tma_prefetch_desc(&tmKV);
-        fence_mbar_init();
-    }
-    __syncwarp();
-
-    // the table entry of this warp's block i (lane 0 reads the next one while a block is worked
-    // on, so the read's latency stays off the refill)
-    auto raw_block = [&](int i) -> int {
-        const int jb = warp + W * i;
-        return jb < p.mbps ? p.block_table[(size_t)slot * p.mbps + jb] : -1;
-    };
-    auto issue = [&](int i, int blk) {
-        const int s2 = i % S;
-        if (blk < 0 || blk >= p.num_blocks) {
-            record_error(DEV_ERR_ATTN_WAIT);
-            blk = 0;  // stay in bounds; the error word reports the bad table entry
-        }
-        const int krow = (((blk * p.num_layers + p.layer) * 2 + 0) * p.kv_heads + g) * 16;
-        const int vrow = krow + p.kv_heads * 16;
-        uint8_t* dst = wbuf + s2 * kTcStage;
-        mbar_arrive_expect_tx(&wbar[s2], kTcStage);
-        tma_load_2d(dst, &tmKV, &wbar[s2], 0, krow);
-        tma_load_2d(dst + kTcBox, &tmKV, &wbar[s2], 64, krow);
-        tma_load_2d(dst + 2 * kTcBox, &tmKV, &wbar[s2], 0, vrow);
-        tma_load_2d(dst + 3 * kTcBox, &tmKV, &wbar[s2], 64, vrow);
-    };
-
-    int issued = 0;
-    int next_raw = -1;  // lane 0: table entry of block `issued`
-    if (lane == 0) {
-        for (int i = 0; i < n_mine && i < S; ++i) issue(i, raw_block(i));
-        issued = min(n_mine, S);
-        if (issued < n_mine) next_raw = raw_block(issued);
-    }
-    issued = __shfl_sync(0xffffffffu, issued, 0);
 
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
     float o[8][4];
@@ -1976,6 +1999,16 @@ inline int launch_prefill_attention(const AttnParams& p, cudaStream_t st) {
     if (rc) return rc;
     if (p.max_splits > 1) QTTS_LAUNCH(attn_combine_kernel<128>, dim3(p.R, p.num_heads), dim3(128), 0, st, p);
     return QTTS_OK;
+}
+
+// The engine's decode steps let the row kernel read its metadata and start its first loads
+// before the wait on the preceding launch (AttnParams::meta_settled) unless QTTS_ATTN_EARLY=0.
+inline bool attn_early() {
+    static const bool on = [] {
+        const char* v = getenv("QTTS_ATTN_EARLY");
+        return !(v && *v == '0');
+    }();
+    return on;
 }
 
 // head_dim 128 runs on the tensor pipe unless QTTS_ATTN_TC=0

@@ -507,6 +507,10 @@ inline int engine_step_impl(qtts_engine* e, const qtts_step_io& io, cudaStream_t
     ap.out_lo = e->attn_lo;
     ap.R = R;
     ap.rows_per_stream = nn;
+    // decode steps: the scheduler wrote the rows' metadata (and any copied blocks) at least two
+    // launches before each layer's attention; only each row's newest key comes from the QKV
+    // projection right before it
+    ap.meta_settled = (nn == 1 && attn_early()) ? 1 : 0;
 
     // ---- talker layers
     for (int l = 0; l < d.layers; ++l) {
