@@ -180,9 +180,13 @@ int qtts_paged_attention(const void* q, int R, int num_heads, int kv_heads, int 
 /* Chunked-prefill form of qtts_paged_attention (head_dim 128): the R rows are R / rows_per_stream
  * streams of rows_per_stream consecutive query tokens (row_slot equal within a stream, row_ctx
  * each token's visible keys: its stream's earlier KV plus the chunk up to itself — the causal
- * mask of talker_unified_modules.py:282-294).  Tiles of 8 queries share every KV block they
- * read, instead of each row reading its whole context.  Same output and scratch as
- * qtts_paged_attention (executor.py:759-877 runs this attention inside its fused prefill). */
+ * mask of talker_unified_modules.py:282-294).  With two query heads per KV head, groups of 64
+ * queries x 2 heads run as 128-row tcgen05 tiles that read every KV block once; when those tiles
+ * are few, a group's keys are split over several CTAs whose partials go to ws_o / ws_ml (up to
+ * the max_splits the scratch sizes allow) and are folded by a second kernel.  Other head layouts
+ * use 8-query mma.sync tiles.  Same output and scratch as qtts_paged_attention (executor.py:
+ * 759-877 runs this attention inside its fused prefill).  q, out and out_lo must be 16-byte
+ * aligned for the tcgen05 form (otherwise the 8-query tiles run). */
 int qtts_paged_attention_prefill(const void* q, int R, int rows_per_stream, int num_heads, int kv_heads,
                                  int head_dim, const void* kv_pool, int layer, int num_layers, int block_size,
                                  int num_blocks, const int32_t* block_table, int max_blocks_per_seq,
