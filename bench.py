@@ -145,7 +145,7 @@ def build_workload(device):
     from test_stateful_b200.config import EngineConfig
     from test_stateful_b200.runtime.executor import B200Executor
 
-    steps_total = ARGS.warmup + ARGS.steps + ARGS.e2e_steps + 2
+    steps_total = ARGS.warmup + ARGS.steps + E2E_WARMUP + ARGS.e2e_steps + 2
     max_seq = 512 + steps_total + 16
     ex = B200Executor(device_id=device.index or 0, max_batch_size=STREAMS + 1, max_seq_len=max_seq,
                       model_config=EngineConfig(), do_sample=True, temperature=0.9, repetition_penalty=1.05,
@@ -166,6 +166,7 @@ def build_workload(device):
 # 96-token prefix every row shares is read from DRAM once), GEMM 26 023 022 + 570 bytes per
 # launch for 27 262 976 algorithmic bytes (its activations stay in L2).  Traffic scales with the
 # unique blocks read (attention) and the weight bytes (GEMM).
+E2E_WARMUP = 3  # untimed steps through the executor call before the e2e timing
 ATTN_TRAFFIC_PER_UNIQUE = (44404792 + 1986) / 43307008
 GEMM_TRAFFIC_RATIO = (26023022 + 570) / 27262976
 
@@ -483,20 +484,29 @@ def run_b200(rank, world, local):
         torch.distributed.barrier()
     # one step of lookahead, as a serving loop runs it: step k + 1 is launched (its text
     # input copied from pinned host memory first) before step k's codes and audio are read
+    def e2e_loop(steps):
+        pending = None
+        for _ in range(steps):
+            with torch.cuda.stream(stream):
+                staged.copy_(t_host, non_blocking=True)
+                ex.text_add.index_copy_(0, idx, staged)
+            fut = ex.launch_decode_step(slots)
+            ex.advance(slots)  # the loop's per-slot counters, before the next launch
+            if pending is not None:
+                out = pending.wait()
+                _ = out.full_codec, out.audio_chunks
+            pending = fut
+        out = pending.wait()
+        _ = out.full_codec, out.audio_chunks
+
+    # untimed warm-up of this path (its first use loads the copy and index kernels' modules,
+    # ~20 ms once, which would otherwise be charged to the timed steps)
+    e2e_loop(E2E_WARMUP)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        torch.distributed.barrier()
     t0 = time.perf_counter()
-    pending = None
-    for _ in range(ARGS.e2e_steps):
-        with torch.cuda.stream(stream):
-            staged.copy_(t_host, non_blocking=True)
-            ex.text_add.index_copy_(0, idx, staged)
-        fut = ex.launch_decode_step(slots)
-        ex.advance(slots)  # the loop's per-slot counters, before the next launch
-        if pending is not None:
-            out = pending.wait()
-            _ = out.full_codec, out.audio_chunks
-        pending = fut
-    out = pending.wait()
-    _ = out.full_codec, out.audio_chunks
+    e2e_loop(ARGS.e2e_steps)
     torch.cuda.synchronize(dev)
     e2e_sec = time.perf_counter() - t0
     if world > 1:
@@ -534,7 +544,8 @@ def run_b200(rank, world, local):
         "roofline_attention": roof_attn,
         "cpu_baseline": cpu,
         "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "steps": ARGS.e2e_steps, "path": "B200Executor.launch_decode_step -> GPUFuture.wait",
+                "steps": ARGS.e2e_steps, "warmup": E2E_WARMUP,
+                "path": "B200Executor.launch_decode_step -> GPUFuture.wait",
                 "lookahead": "step k+1 launched before step k's results are read"},
         "clocks": clk,
     }

@@ -27,10 +27,13 @@ import torch  # noqa: E402
 from test_stateful_b200 import _lib, ops  # noqa: E402
 
 
-def bench_attention(rows: int, ctx_mean: int, launches: int, layers: int = 4, seed: int = 0, split: int = 0):
+def bench_attention(rows: int, ctx_mean: int, launches: int, layers: int = 4, seed: int = 0, split: int = 0,
+                    spread: float = 0.5):
+    """Decode attention over `rows` rows with contexts U[mean (1 - spread), mean (1 + spread)]
+    (spread 0: every row at the mean)."""
     dev = "cuda"
     g = torch.Generator().manual_seed(seed)
-    lo, hi = max(1, ctx_mean // 2), ctx_mean * 3 // 2
+    lo, hi = max(1, int(ctx_mean * (1 - spread))), max(1, int(ctx_mean * (1 + spread)))
     ctx = torch.randint(lo, hi + 1, (rows,), generator=g)
     nblk = [-(-int(c) // 16) for c in ctx]
     mbps = max(nblk)
@@ -224,6 +227,7 @@ def main():
     ap.add_argument("--past", type=int, default=384, help="prefill-attention: positions before the chunk")
     ap.add_argument("--rows", type=int, default=64)
     ap.add_argument("--ctx-mean", type=int, default=520)
+    ap.add_argument("--ctx-spread", type=float, default=0.5, help="attention: contexts U[mean(1-s), mean(1+s)]")
     ap.add_argument("--n", type=int, default=12288)
     ap.add_argument("--k", type=int, default=2048)
     ap.add_argument("--m", type=int, default=64)
@@ -233,7 +237,7 @@ def main():
     ap.add_argument("--plain", action="store_true", help="gemm: plain bf16 activations (no lo operand)")
     a = ap.parse_args()
     if a.what == "attention":
-        r = bench_attention(a.rows, a.ctx_mean, a.launches, split=a.split)
+        r = bench_attention(a.rows, a.ctx_mean, a.launches, split=a.split, spread=a.ctx_spread)
     elif a.what == "prefill-attention":
         r = bench_prefill_attention(a.streams, a.prefill_chunk, a.past, a.launches, split=a.split)
     elif a.what == "code2wav":
