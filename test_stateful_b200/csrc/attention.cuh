@@ -1892,6 +1892,464 @@ __global__ void __launch_bounds__(kPfuThreads, 1) paged_prefill_umma_kernel(cons
 }
 
 
+// ---------------------------------------------------------------------------
+// The same attention with 128-key tiles and both UMMA A operands in TMEM: Q (fp16 hi/lo, 128
+// columns) for S = Q K^T, P (fp16 hi/lo, 128 columns) for O += P V, so a 128-key tile takes
+// 16 + 16 UMMAs of N = 128 instead of 2 x (16 of N = 64 + 8 of N = 128), and shared memory
+// holds only the KV rings: K in 3 slots (its tile is loaded two windows ahead, as soon as the
+// S that read the slot is done), V in 2 (loaded one window ahead, once the PV that read the
+// slot is done). TMEM columns: Q hi 0..63, Q lo 64..127, S 128..255, P hi 256..319, P lo
+// 320..383, O 384..511. Per window li: the softmax warps read S(li) and release it (s_free),
+// the UMMA warp then issues S(li + 1) while they compute P(li), which they store to TMEM once
+// PV(li - 1) is done; after the window's barrier the UMMA warp issues PV(li).
+// ---------------------------------------------------------------------------
+constexpr int kPf2Keys = 128;
+constexpr int kPf2KSlots = 3, kPf2VSlots = 2;
+
+struct Pf2Layout {
+    static constexpr int SLOT = 2 * 128 * 128;                // 128 keys x 2 dim halves x 128 B
+    static constexpr int KRING = 0;
+    static constexpr int VRING = KRING + kPf2KSlots * SLOT;
+    static constexpr int BAR = VRING + kPf2VSlots * SLOT;     // k_full[3], v_full[2], s_full, s_free, pv_done, drain, slot
+    static constexpr int XCH = BAR + 128;
+    static constexpr int SMEM = 1024 + XCH + 2 * 128 * 4;
+};
+static_assert(Pf2Layout::SMEM <= 227 * 1024, "prefill tile exceeds shared memory");
+
+// D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::f16 (A: M rows = TMEM lanes, two 16-bit
+// elements per 32-bit column along K)
+__device__ __forceinline__ void umma_ts_f16(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// 32 lanes x 32 bits, 16 consecutive columns of packed words (waits for the store)
+__device__ __forceinline__ void tmem_st16_u(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(kPfuThreads, 1) paged_prefill_umma128_kernel(const __grid_constant__ CUtensorMap tmKV,
+                                                                                const AttnParams p) {
+    constexpr int D = 128;
+    using L = Pf2Layout;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* k_full = reinterpret_cast<uint64_t*>(smem + L::BAR);
+    uint64_t* v_full = k_full + kPf2KSlots;
+    uint64_t* s_full = v_full + kPf2VSlots;  // S(li) is in TMEM
+    uint64_t* s_free = s_full + 1;           // the softmax threads have read S(li)
+    uint64_t* pv_done = s_free + 1;
+    uint64_t* drain = pv_done + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    float* xch = reinterpret_cast<float*>(smem + L::XCH);
+    constexpr uint32_t kQ = 0, kS = 128, kP = 256, kO = 384;  // TMEM columns
+
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    const bool mma_w = warp == kPfuSoftmaxWarps;      // issues the UMMAs (and owns TMEM)
+    const bool tma_w = warp == kPfuSoftmaxWarps + 1;  // issues the KV loads
+    const bool ctrl = mma_w || tma_w;
+    griddep_wait();
+    griddep_launch();
+    const int SPS = p.rows_per_stream;
+    const int n_streams = p.R / SPS;
+    const int n_groups = (SPS + kPfuQ - 1) / kPfuQ;
+    int rest = blockIdx.x;  // CTA-uniform
+    const int g = rest % p.kv_heads;
+    rest /= p.kv_heads;
+    const int grp = rest % n_groups;
+    rest /= n_groups;
+    const int b = rest % n_streams;
+    const int sp = rest / n_streams;  // key split sp of max_splits: a contiguous share of the group's tiles
+    if (sp >= p.max_splits) return;
+    const int nsplit = p.max_splits;
+    const int q0 = grp * kPfuQ;
+    const int nq = min(kPfuQ, SPS - q0);
+    const int row = t & 127, ch = (t >> 7) & 1;  // softmax threads: TMEM lane and half
+    const int h = row >> 6, qi = row & 63;
+    const bool row_ok = !ctrl && qi < nq;
+    const int r = b * SPS + q0 + qi;
+    const int ctx_row = row_ok ? p.row_ctx[r] : 0;
+    const int slot = p.row_slot[b * SPS];
+    __shared__ int s_ctx;
+    if (t == 0) s_ctx = 0;
+    __syncthreads();
+    if (row_ok && ch == 0) atomicMax(&s_ctx, ctx_row);
+    __syncthreads();
+    const int ctx_max = s_ctx;
+    const size_t out_row = (size_t)r * p.num_heads + g * 2 + h;
+    const size_t part_row = (size_t)out_row * nsplit + sp;
+    if (ctx_max <= 0 || slot < 0) {  // CTA-uniform: nothing to attend (only after a scheduler error)
+        if (ctx_max > 0 && t == 0 && sp == 0) record_error(DEV_ERR_ATTN_BOUNDS);
+        if (row_ok && nsplit == 1)
+            for (int d = ch * 64; d < ch * 64 + 64; ++d) {
+                p.out[out_row * D + d] = __float2bfloat16(0.f);
+                if (p.out_lo) p.out_lo[out_row * D + d] = __float2bfloat16(0.f);
+            }
+        if (row_ok && nsplit > 1 && ch == 0) {
+            p.ws_ml[part_row * 2 + 0] = -INFINITY;
+            p.ws_ml[part_row * 2 + 1] = 0.f;
+        }
+        return;
+    }
+    const int nbt = (ctx_max + 15) >> 4;
+    const int ntiles = (ctx_max + kPf2Keys - 1) / kPf2Keys;
+    const int t0 = (int)(((long long)sp * ntiles) / nsplit);
+    const int nt = (int)(((long long)(sp + 1) * ntiles) / nsplit) - t0;
+    if (nt <= 0) {
+        if (row_ok && ch == 0) {
+            p.ws_ml[part_row * 2 + 0] = -INFINITY;
+            p.ws_ml[part_row * 2 + 1] = 0.f;
+        }
+        return;
+    }
+
+    // block j (0..7) of tile `tile` as the table holds it; past the group's keys any valid
+    // block stands in (its keys are masked, its V zeroed)
+    auto tile_block_raw = [&](int tile, int j) -> int {
+        int jb = tile * 8 + j;
+        if (jb >= nbt) jb = 0;
+        return jb < p.mbps ? p.block_table[(size_t)slot * p.mbps + jb] : -1;
+    };
+    auto checked = [&](int blk) -> int {
+        if (blk < 0 || blk >= p.num_blocks) {
+            record_error(DEV_ERR_ATTN_BOUNDS);
+            blk = 0;
+        }
+        return blk;
+    };
+    // TMA warp, converged: K (kind 0) or V (kind 1) of local tile li into its slot, one box per
+    // lane 0..15 (lane = 2 j + half); lanes 0..7 hold the eight block ids
+    auto issue_kv = [&](int kind, int li, int nb) {
+        const int nslots = kind ? kPf2VSlots : kPf2KSlots;
+        const int s2 = li % nslots;
+        uint64_t* bar = kind ? &v_full[s2] : &k_full[s2];
+        uint8_t* dst = smem + (kind ? L::VRING : L::KRING) + s2 * L::SLOT;
+        const int blk = __shfl_sync(0xffffffffu, nb, (lane >> 1) & 7);
+        if (lane == 0) mbar_arrive_expect_tx(bar, L::SLOT);
+        __syncwarp();
+        if (lane < 16) {
+            const int j = lane >> 1, half = lane & 1;
+            const int krow = (((blk * p.num_layers + p.layer) * 2 + kind) * p.kv_heads + g) * 16;
+            tma_load_2d(dst + half * (128 * 128) + j * 2048, &tmKV, bar, half * 64, krow);
+        }
+    };
+
+    int k_issued = 0, v_issued = 0;  // TMA lane 0
+    int id_v = 0, id_k = 0;          // TMA lanes 0..7: checked ids of the next V tile, raw ids of the next K tile
+    if (t == 0) {
+        for (int s2 = 0; s2 < kPf2KSlots; ++s2) mbar_init(&k_full[s2], 1);
+        for (int s2 = 0; s2 < kPf2VSlots; ++s2) mbar_init(&v_full[s2], 1);
+        mbar_init(s_full, 1);
+        mbar_init(s_free, kPfuSoftmaxWarps * 32);
+        mbar_init(pv_done, 1);
+        mbar_init(drain, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (mma_w) {
+        tmem_alloc(tmem_slot, 512);
+        tmem_relinquish();
+    } else if (tma_w) {
+        if (lane == 0) tma_prefetch_desc(&tmKV);
+        const int id0 = lane < 8 ? checked(tile_block_raw(t0, lane)) : 0;
+        issue_kv(0, 0, id0);
+        issue_kv(1, 0, id0);
+        k_issued = v_issued = 1;
+        if (nt > 1) {
+            const int id1 = lane < 8 ? checked(tile_block_raw(t0 + 1, lane)) : 0;
+            issue_kv(0, 1, id1);
+            k_issued = 2;
+            id_v = id1;
+        }
+        id_k = (lane < 8 && nt > 2) ? tile_block_raw(t0 + 2, lane) : 0;
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    if (!ctrl) {
+        // ---- Q rows (x scale_log2) as an fp16 hi/lo pair into TMEM: dims 64 ch .. 64 ch + 63
+        // are columns 32 ch .. 32 ch + 31 of each (two dims per column, the even one low)
+        const float4* qp = reinterpret_cast<const float4*>(p.q + out_row * D + ch * 64);
+        const float sc = p.scale_log2;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {  // 32 dims -> 16 columns
+            uint32_t hi[16], lo[16];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const float4 x = row_ok ? qp[c * 8 + k] : make_float4(0.f, 0.f, 0.f, 0.f);
+                split_h2(x.x * sc, x.y * sc, hi[2 * k], lo[2 * k]);
+                split_h2(x.z * sc, x.w * sc, hi[2 * k + 1], lo[2 * k + 1]);
+            }
+            tmem_st16_u(tmem + lane_base + kQ + (uint32_t)(ch * 32 + c * 16), hi);
+            tmem_st16_u(tmem + lane_base + kQ + 64u + (uint32_t)(ch * 32 + c * 16), lo);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    // O's B operand (V) is MN-major: bit 16 of the instruction descriptor
+    const uint32_t idesc_s = make_idesc_f16(128, kPf2Keys), idesc_o = make_idesc_f16(128, D) | (1u << 16);
+
+    // UMMA lane 0: S(li) = Q K^T, A = Q from TMEM (k step kk: dims 16 kk .. : columns 8 kk ..)
+    auto issue_s = [&](int li) -> bool {
+        if (!mbar_wait(&k_full[li % kPf2KSlots], (uint32_t)(li / kPf2KSlots) & 1u, DEV_ERR_ATTN_WAIT)) return false;
+        tc_fence_after();
+        const uint32_t kb = smem_u32(smem + L::KRING + (li % kPf2KSlots) * L::SLOT);
+#pragma unroll
+        for (int part = 0; part < 2; ++part)
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+                umma_ts_f16(tmem + kS, tmem + kQ + (uint32_t)(part * 64 + kk * 8),
+                            make_sw128_desc(kb + (kk >> 2) * (128 * 128)) + 2 * (kk & 3), idesc_s,
+                            (part | kk) ? 1u : 0u);
+        umma_commit(s_full);
+        return true;
+    };
+    // UMMA lane 0: O (+)= P V, A = P from TMEM (16 keys per step: 8 columns), B = V MN-major in
+    // its slot (LBO: the second 64 dims 16 KB on, 16 keys = 2048 B)
+    auto issue_pv = [&](int li) -> bool {
+        if (!mbar_wait(&v_full[li % kPf2VSlots], (uint32_t)(li / kPf2VSlots) & 1u, DEV_ERR_ATTN_WAIT)) return false;
+        tc_fence_after();
+        const uint32_t vb = smem_u32(smem + L::VRING + (li % kPf2VSlots) * L::SLOT);
+#pragma unroll
+        for (int part = 0; part < 2; ++part)
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+                umma_ts_f16(tmem + kO, tmem + kP + (uint32_t)(part * 64 + kk * 8),
+                            make_sw128_mn_desc(vb + kk * 2048, 128 * 128), idesc_o,
+                            (li > 0 || part > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(pv_done);
+        return true;
+    };
+
+    bool fail = false;
+    if (mma_w && lane == 0) fail = !issue_s(0);
+    float m_ref = -INFINITY, l = 0.f;
+    int li = 0;
+    for (; li < nt; ++li) {
+        const int i = t0 + li;  // the tile: keys 128 i .. 128 i + 127
+        if (mma_w) {
+            PFU_STAMP(0, 0);
+            if (lane == 0 && !fail && li > 0) fail = !issue_pv(li - 1);
+            PFU_STAMP(0, 1);
+            if (lane == 0 && !fail && li + 1 < nt) {
+                // S(li + 1) overwrites S(li): after the softmax threads have read it
+                fail = !mbar_wait(s_free, (uint32_t)li & 1u, DEV_ERR_ATTN_WAIT);
+                tc_fence_after();
+                PFU_STAMP(0, 2);
+                if (!fail) fail = !issue_s(li + 1);
+            }
+            __syncwarp();
+            PFU_STAMP(0, 3);
+        } else if (tma_w) {
+            const bool dead = __shfl_sync(0xffffffffu, fail, 0);
+            if (li + 2 < nt && !dead) {  // K of li + 2 into the slot S(li - 1) read
+                const int idc = lane < 8 ? checked(id_k) : 0;
+                issue_kv(0, li + 2, idc);
+                if (lane == 0) ++k_issued;
+                id_k = (lane < 8 && li + 3 < nt) ? tile_block_raw(i + 3, lane) : 0;
+                if (li + 1 < nt) {
+                    // V of li + 1 into the slot PV(li - 1) reads: once that PV is done
+                    if (li > 0 && lane == 0) fail = !mbar_wait(pv_done, (uint32_t)(li - 1) & 1u, DEV_ERR_ATTN_WAIT);
+                    if (!__shfl_sync(0xffffffffu, fail, 0)) {
+                        issue_kv(1, li + 1, id_v);
+                        if (lane == 0) ++v_issued;
+                    }
+                }
+                id_v = idc;
+            } else if (li + 1 < nt && !dead) {
+                if (li > 0 && lane == 0) fail = !mbar_wait(pv_done, (uint32_t)(li - 1) & 1u, DEV_ERR_ATTN_WAIT);
+                if (!__shfl_sync(0xffffffffu, fail, 0)) {
+                    issue_kv(1, li + 1, id_v);
+                    if (lane == 0) ++v_issued;
+                }
+            }
+            __syncwarp();
+        } else {
+            PFU_STAMP(1, 0);
+            // ---- this thread's 64 scores of tile i: columns 64 ch .. 64 ch + 63 of S
+            fail |= !mbar_wait(s_full, (uint32_t)li & 1u, DEV_ERR_ATTN_WAIT);
+            __syncwarp();
+            tc_fence_after();
+            PFU_STAMP(1, 1);
+            float sv[64];
+            {
+                float a32[32];
+                tmem_ld32(tmem + lane_base + kS + (uint32_t)(ch * 64), a32);
+#pragma unroll
+                for (int k = 0; k < 32; ++k) sv[k] = a32[k];
+                tmem_ld32(tmem + lane_base + kS + (uint32_t)(ch * 64 + 32), a32);
+#pragma unroll
+                for (int k = 0; k < 32; ++k) sv[32 + k] = a32[k];
+            }
+            tc_fence_before();
+            mbar_arrive(s_free);  // S may be overwritten: the UMMA warp issues S(li + 1)
+            PFU_STAMP(1, 2);
+            const int lim = ctx_row - (i * kPf2Keys + ch * 64);  // keys of the row in this half-tile
+            if (lim < 64)
+#pragma unroll
+                for (int k = 0; k < 64; ++k) sv[k] = k < lim ? sv[k] : -INFINITY;
+            float mt = sv[0];
+#pragma unroll
+            for (int k = 1; k < 64; ++k) mt = fmaxf(mt, sv[k]);
+            xch[ch * 128 + row] = mt;
+            pair_sync(warp);
+            mt = fmaxf(mt, xch[(ch ^ 1) * 128 + row]);
+            PFU_STAMP(1, 3);
+            float alpha = 1.f;
+            bool rescale = false;
+            if (mt != -INFINITY) {
+                if (m_ref == -INFINITY) {
+                    m_ref = mt;
+                } else if (mt > m_ref + 8.f) {
+                    alpha = ex2_approx(m_ref - mt);
+                    l *= alpha;
+                    m_ref = mt;
+                    rescale = true;
+                }
+            }
+            const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
+            // ---- P = 2^(s - m), an fp16 hi/lo pair per key, two keys per column (even one low);
+            // the first 32 keys' words are formed while PV(li - 1) still reads P(li - 1)
+            float psum = 0.f;
+            uint32_t wh[16], wl[16];
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+                const float a = ex2_approx(sv[2 * k] - m_use), b2 = ex2_approx(sv[2 * k + 1] - m_use);
+                psum += a + b2;
+                split_h2(a, b2, wh[k], wl[k]);
+            }
+            // P(li) replaces P(li - 1) in TMEM and O is rescaled: both once PV(li - 1) is done
+            if (li > 0) fail |= !mbar_wait(pv_done, (uint32_t)(li - 1) & 1u, DEV_ERR_ATTN_WAIT);
+            __syncwarp();
+            tc_fence_after();
+            PFU_STAMP(1, 4);
+            if (__any_sync(0xffffffffu, rescale)) {  // warp-collective TMEM read-modify-write of O
+#pragma unroll 1
+                for (int c = 0; c < 64; c += 16) {
+                    const uint32_t ta = tmem + lane_base + kO + (uint32_t)(ch * 64 + c);
+                    float v[16];
+                    tmem_ld16(ta, v);
+#pragma unroll
+                    for (int k = 0; k < 16; ++k) v[k] *= alpha;
+                    tmem_st16(ta, v);
+                }
+            }
+            tmem_st16_u(tmem + lane_base + kP + (uint32_t)(ch * 32), wh);
+            tmem_st16_u(tmem + lane_base + kP + 64u + (uint32_t)(ch * 32), wl);
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+                const float a = ex2_approx(sv[32 + 2 * k] - m_use), b2 = ex2_approx(sv[33 + 2 * k] - m_use);
+                psum += a + b2;
+                split_h2(a, b2, wh[k], wl[k]);
+            }
+            tmem_st16_u(tmem + lane_base + kP + (uint32_t)(ch * 32 + 16), wh);
+            tmem_st16_u(tmem + lane_base + kP + 64u + (uint32_t)(ch * 32 + 16), wl);
+            l += psum;
+            PFU_STAMP(1, 5);
+            // ---- the last tile's keys past the group's last one: V rows zeroed (P = 0 meets a
+            // finite V)
+            const int first_stale = ctx_max - i * kPf2Keys;
+            if (i == ntiles - 1 && first_stale < kPf2Keys) {
+                fail |= !mbar_wait(&v_full[li % kPf2VSlots], (uint32_t)(li / kPf2VSlots) & 1u, DEV_ERR_ATTN_WAIT);
+                uint8_t* vst = smem + L::VRING + (li % kPf2VSlots) * L::SLOT;
+                for (int c = t; c < (kPf2Keys - first_stale) * 16; c += kPfuSoftmaxWarps * 32) {
+                    const int key = first_stale + (c >> 4), half = (c >> 3) & 1, chunk = c & 7;
+                    *reinterpret_cast<uint4*>(vst + half * (128 * 128) + key * 128 + chunk * 16) =
+                        make_uint4(0u, 0u, 0u, 0u);
+                }
+            }
+            PFU_STAMP(1, 6);
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        const int any_fail = __syncthreads_or(fail ? 1 : 0);
+        tc_fence_after();
+        if (any_fail) {
+            fail = true;
+            break;
+        }
+    }
+    if (mma_w && lane == 0 && !fail) fail = !issue_pv(nt - 1);
+    if (!ctrl) {
+        const bool good = !fail && mbar_wait(pv_done, (uint32_t)(nt - 1) & 1u, DEV_ERR_ATTN_WAIT);
+        __syncwarp();
+        tc_fence_after();
+        xch[ch * 128 + row] = l;
+        pair_sync(warp);
+        const float l_row = l + xch[(ch ^ 1) * 128 + row];
+        const bool final_out = nsplit == 1;
+        const bool has_keys = good && m_ref != -INFINITY;
+        const bool partial = !final_out && has_keys;
+        const float inv = final_out ? ((good && l_row > 0.f) ? 1.f / l_row : 0.f) : 1.f;
+        if (row_ok && !final_out && ch == 0) {
+            p.ws_ml[part_row * 2 + 0] = has_keys ? m_ref : -INFINITY;
+            p.ws_ml[part_row * 2 + 1] = has_keys ? l_row : 0.f;
+        }
+#pragma unroll 1
+        for (int c = 0; c < 64; c += 16) {
+            float v[16];
+            tmem_ld16(tmem + lane_base + kO + (uint32_t)(ch * 64 + c), v);
+            if (!good)
+#pragma unroll
+                for (int k = 0; k < 16; ++k) v[k] = 0.f;
+            if (row_ok && partial) {
+                float4* wo = reinterpret_cast<float4*>(p.ws_o + part_row * D + ch * 64 + c);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) wo[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+            }
+            if (row_ok && final_out) {
+                uint32_t hw[8], lw[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const float a = v[2 * k] * inv, b2 = v[2 * k + 1] * inv;
+                    const __nv_bfloat162 hb = __floats2bfloat162_rn(a, b2);
+                    const float2 hf = __bfloat1622float2(hb);
+                    const __nv_bfloat162 lb = __floats2bfloat162_rn(a - hf.x, b2 - hf.y);
+                    hw[k] = *reinterpret_cast<const uint32_t*>(&hb);
+                    lw[k] = *reinterpret_cast<const uint32_t*>(&lb);
+                }
+                uint4* oh = reinterpret_cast<uint4*>(p.out + out_row * D + ch * 64 + c);
+                oh[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                oh[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+                if (p.out_lo) {
+                    uint4* ol = reinterpret_cast<uint4*>(p.out_lo + out_row * D + ch * 64 + c);
+                    ol[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+                    ol[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+                }
+            }
+        }
+    } else if (lane == 0 && fail) {
+        // after a failure: the loads in flight land and every UMMA finishes before TMEM is released
+        if (tma_w) {
+            for (int j = k_issued > kPf2KSlots ? k_issued - kPf2KSlots : 0; j < k_issued; ++j)
+                mbar_wait(&k_full[j % kPf2KSlots], (uint32_t)(j / kPf2KSlots) & 1u, DEV_ERR_DRAIN);
+            for (int j = v_issued > kPf2VSlots ? v_issued - kPf2VSlots : 0; j < v_issued; ++j)
+                mbar_wait(&v_full[j % kPf2VSlots], (uint32_t)(j / kPf2VSlots) & 1u, DEV_ERR_DRAIN);
+        }
+        if (mma_w) {
+            umma_commit(drain);
+            mbar_wait(drain, 0, DEV_ERR_DRAIN);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (mma_w) tmem_dealloc(tmem, 512);
+}
+
 // Folds the key splits of paged_prefill_umma_kernel: one warp per (row, q head), lane d4 owns
 // dims 4 d4 .. 4 d4 + 3; a partial whose max is -inf holds no keys and is skipped.
 __global__ void __launch_bounds__(128) prefill_combine_kernel(const AttnParams p) {
@@ -1946,11 +2404,24 @@ inline int prefill_umma_split_cap() {
     return c;
 }
 
+// QTTS_PREFILL_UMMA: 1 = 64-key tiles (Q and P in shared memory), 2 = 128-key tiles with Q and P
+// in TMEM, unset = 2 for chunks of 128 rows or more per stream (long chunks, whose pasts tend to
+// be long too, gain from the wider tiles; short chunks lose to their partial last tile)
+inline int attn_prefill_umma_form(int rows_per_stream) {
+    static const int f = [] {
+        const char* v = getenv("QTTS_PREFILL_UMMA");
+        return (v && (*v == '1' || *v == '2')) ? (*v - '0') : 0;
+    }();
+    return f ? f : (rows_per_stream >= 128 ? 2 : 1);
+}
+
 inline int launch_prefill_umma(const AttnParams& p, cudaStream_t st) {
     CUtensorMap map;
     const int rc = make_kv_map(&map, p);
     if (rc) return rc;
-    QTTS_CHECK_CUDA((func_attr_once<paged_prefill_umma_kernel>(PfuLayout::SMEM)));
+    const bool wide = attn_prefill_umma_form(p.rows_per_stream) == 2;
+    if (wide) QTTS_CHECK_CUDA((func_attr_once<paged_prefill_umma128_kernel>(Pf2Layout::SMEM)));
+    else QTTS_CHECK_CUDA((func_attr_once<paged_prefill_umma_kernel>(PfuLayout::SMEM)));
     const int n_groups = (p.rows_per_stream + kPfuQ - 1) / kPfuQ;
     const int base = (p.R / p.rows_per_stream) * n_groups * p.kv_heads;
     const int sms = num_sms();
@@ -1959,14 +2430,19 @@ inline int launch_prefill_umma(const AttnParams& p, cudaStream_t st) {
     if (ws_ok && 2 * base <= sms) k = min(min(sms / base, p.max_splits), prefill_umma_split_cap());
     AttnParams q = p;
     q.max_splits = k > 1 ? k : 1;  // the workspace stride: k partials per (row, q head)
-    QTTS_LAUNCH(paged_prefill_umma_kernel, dim3(base * q.max_splits), dim3(kPfuThreads), PfuLayout::SMEM, st, map, q);
+    if (wide)
+        QTTS_LAUNCH(paged_prefill_umma128_kernel, dim3(base * q.max_splits), dim3(kPfuThreads), Pf2Layout::SMEM, st,
+                    map, q);
+    else
+        QTTS_LAUNCH(paged_prefill_umma_kernel, dim3(base * q.max_splits), dim3(kPfuThreads), PfuLayout::SMEM, st,
+                    map, q);
     if (q.max_splits > 1)
         QTTS_LAUNCH(prefill_combine_kernel, dim3(ceil_div(q.R * q.num_heads, 4)), dim3(128), 0, st, q);
     return QTTS_OK;
 }
 
 // Prefill attention on the tcgen05 tensor pipe (head_dim 128, 2 query heads per KV head) unless
-// QTTS_PREFILL_UMMA=0 (the mma.sync query-tile kernel).
+// QTTS_PREFILL_UMMA=0 (the mma.sync query-tile kernel); 1 / 2 pick its form (above).
 inline bool attn_prefill_umma() {
     static const bool on = [] {
         const char* v = getenv("QTTS_PREFILL_UMMA");

@@ -292,8 +292,25 @@ def test_prefill_query_tile_form():
 
     env = dict(os.environ, QTTS_PREFILL_UMMA="0")
     r = subprocess.run([sys.executable, "-m", "pytest", "-x", "-q", "-m", "gpu", "-p", "no:cacheprovider", "-k",
-                        "prefill and not tile_form and not without_splits", os.path.abspath(__file__)], env=env,
+                        "prefill and not tile_form and not without_splits and not umma_forms", os.path.abspath(__file__)], env=env,
                        capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
+
+
+@pytest.mark.skipif(os.environ.get("QTTS_PREFILL_UMMA") is not None, reason="already a forced run")
+@pytest.mark.parametrize("form", ["1", "2"])
+def test_prefill_umma_forms(form):
+    """The tcgen05 prefill has two forms — 64-key tiles with Q and P in shared memory (1) and
+    128-key tiles with Q and P as TMEM operands (2) — picked by chunk length unless
+    QTTS_PREFILL_UMMA forces one (read once per process): rerun the prefill kernel tests in a
+    child process with each forced, so both see every case."""
+    import subprocess
+    import sys
+
+    env = dict(os.environ, QTTS_PREFILL_UMMA=form)
+    r = subprocess.run([sys.executable, "-m", "pytest", "-x", "-q", "-m", "gpu", "-p", "no:cacheprovider", "-k",
+                        "paged_prefill", os.path.abspath(__file__)], env=env, capture_output=True, text=True,
+                       timeout=900)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
 
 
@@ -308,7 +325,7 @@ def test_prefill_umma_without_splits():
 
     env = dict(os.environ, QTTS_PREFILL_SPLITS="1")
     r = subprocess.run([sys.executable, "-m", "pytest", "-x", "-q", "-m", "gpu", "-p", "no:cacheprovider", "-k",
-                        "prefill and not tile_form and not without_splits", os.path.abspath(__file__)], env=env,
+                        "prefill and not tile_form and not without_splits and not umma_forms", os.path.abspath(__file__)], env=env,
                        capture_output=True, text=True, timeout=900)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
 
